@@ -1,0 +1,318 @@
+#!/usr/bin/env python3
+"""Benchmark of the quantized matvec hot path.
+
+Workload: one Q4_K x Q8_K matvec, weight 17408 x 5120 in GGUF Q4_K layout
+(fp16 d/dmin ~ |N(0,0.01)|, uniform 6-bit scales/mins and 4-bit quants),
+activation 5120 fp32 ~ N(0,1) quantized to Q8_K, output 17408 fp32 - seeded
+synthetic data (no checkpoint is available offline).  A step is one matvec.
+
+  value   algorithmic bytes / device time per step, inputs resident in HBM,
+          summed over ranks (each rank runs its own matvecs: weak scaling).
+          Weights rotate over COPIES distinct device copies (> L2) so every
+          step streams from HBM.
+  e2e     the same metric through the C ABI with host buffers: per step the
+          fp32 activation is copied host->device from pinned memory, quantized
+          to Q8_K, multiplied, and the fp32 output is read back to the host.
+  roofline / cpu_baseline   see the JSON keys.
+
+`--impl reference` times the upstream engine's own CPU kernel
+(q38_tensor_gemv_q8_k built from its sources into oracle/_ref/, or the
+oracle restatement when that library is absent) on this host's cores.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "qwen3.8-27b-in-c_b200", "python"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "decode tok/s (Q4_K_M, bs1, MTP on/off); quant matvec HBM GB/s vs 8 TB/s peak"
+UNIT = "GB/s"
+Q4_K = 12
+ROWS, WIDTH = 17408, 5120
+ROW_BYTES = WIDTH // 256 * 144
+W_BYTES = ROWS * ROW_BYTES                      # 50,135,040
+X_BYTES = WIDTH // 256 * 292                    # Q8_K activation, 5,840
+Y_BYTES = ROWS * 4                              # 69,632
+STEP_BYTES = W_BYTES + X_BYTES + Y_BYTES        # algorithmic bytes per matvec
+COPIES = 8                                      # 401 MB of weights > 126 MB L2
+NOMINAL_HBM_GBS = 8000.0
+WORKLOAD = "config0: Q4_K 17408x5120 x Q8_K matvec, bs1"
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as handle:
+            data = json.load(handle)
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def read_traffic():
+    """DRAM bytes per launch from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "q4k_gemv_17408x5120.md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("dram_bytes_per_launch:"):
+            return int(line.split(":")[1].strip().replace(",", ""))
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        0x0000000000000002: "applications_clocks_setting",
+        0x0000000000000004: "sw_power_cap",
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000080: "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, device_index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nvml.nvmlDeviceGetClockInfo(self._handle, self._nvml.NVML_CLOCK_SM))
+                mask = self._nvml.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                for bit, name in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self):
+        if self._nvml:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+def cpu_reference_gemv(seconds=3.0, min_calls=20):
+    """Time the upstream CPU kernel on this host (all cores, OpenMP)."""
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    from q38b200 import synth
+    weights = synth.quant_tensor(Q4_K, ROWS, WIDTH, seed=0)
+    x = synth.activations(1, WIDTH, seed=1)
+    copies = [weights] + [weights.copy() for _ in range(COPIES - 1)]
+    if O.reference_available():
+        impl, kind = O.Reference(), "reference"
+        threads = int(os.environ["OMP_NUM_THREADS"])
+    else:
+        impl, kind = O.Oracle(), "port"
+        threads = 1
+    q8k = impl.quantize_q8_k(x)
+    times = []
+    start = time.perf_counter()
+    i = 0
+    while (time.perf_counter() - start < seconds or len(times) < min_calls) and len(times) < 10000:
+        w = copies[i % COPIES]
+        t0 = time.perf_counter()
+        impl.gemm_q8_k(Q4_K, w, ROWS, WIDTH, q8k)
+        times.append(time.perf_counter() - t0)
+        i += 1
+        if kind == "port" and time.perf_counter() - start > seconds:
+            break
+    med = statistics.median(times)
+    return {"value": STEP_BYTES / med / 1e9, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{len(times)} full 17408x5120 Q4_K matvecs rotating {COPIES} weight copies; "
+                      f"median {med * 1e3:.3f} ms"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    base = cpu_reference_gemv(seconds=max(2.0, 0.02 * args.steps))
+    line = {"metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "impl": "reference", "dtype": "int8xint8->int32,f32",
+            "data": "synthetic", "scaling": "weak",
+            "config": {"workload": WORKLOAD, "l2": f"rotating {COPIES} weight copies"},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "vs_baseline": None}
+    print(json.dumps(line), flush=True)
+
+
+def capture(fn, count):
+    import torch
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(count):
+            fn(i)
+    return g
+
+
+def run_ours(args, rank, world, dist):
+    import torch
+    import q38b200 as q38
+    from q38b200 import synth
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    weights = synth.quant_tensor(Q4_K, ROWS, WIDTH, seed=0)
+    x_host = synth.activations(1, WIDTH, seed=1)
+    tensors = [q38.DeviceTensor(Q4_K, WIDTH, ROWS, weights) for _ in range(COPIES)]
+    x_dev = torch.from_numpy(x_host).cuda()
+    act = q38.quantize_q8_k(x_dev)
+    out = torch.empty((1, ROWS), dtype=torch.float32, device="cuda")
+
+    def step(i):
+        q38.gemm_q8_k(tensors[i % COPIES], act, 1, out=out)
+
+    # Uncaptured first call: sets kernel attributes and caches the plan.
+    step(0)
+    torch.cuda.synchronize()
+    chunk = 64
+    full_graph = capture(step, chunk)
+    rem = args.steps % chunk
+    rem_graph = capture(step, rem) if rem else None
+    warm_graph = capture(step, args.warmup)
+
+    warm_graph.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for _ in range(args.steps // chunk):
+            full_graph.replay()
+        if rem_graph:
+            rem_graph.replay()
+        end.record()
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    elapsed_ms = start.elapsed_time(end)
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    ms_per_step = max_ms / args.steps
+    value = STEP_BYTES * args.steps * world / (max_ms / 1e3) / 1e9
+    per_gpu = STEP_BYTES / (ms_per_step / 1e3) / 1e9
+
+    # End-to-end through the C ABI with host buffers.
+    x_pinned = torch.from_numpy(x_host).pin_memory()
+    y_pinned = torch.empty((1, ROWS), dtype=torch.float32).pin_memory()
+    e2e_steps = min(args.steps, 2000)
+
+    def e2e_step(i):
+        x_dev.copy_(x_pinned, non_blocking=True)
+        q38.quantize_q8_k(x_dev, out=act)
+        q38.gemm_q8_k(tensors[i % COPIES], act, 1, out=out)
+        y_pinned.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for i in range(max(3, args.warmup)):
+        e2e_step(i)
+    if dist:
+        dist.barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e2.record()
+    torch.cuda.synchronize()
+    t2 = torch.tensor([s2.elapsed_time(e2)], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_value = STEP_BYTES * e2e_steps * world / (float(t2.item()) / 1e3) / 1e9
+
+    status = q38.device_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status}: a kernel abandoned a bounded wait")
+
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peaks()
+    cpu = cpu_reference_gemv(seconds=3.0) if world == 1 else None
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8xint8->int32,f32", "data": "synthetic (seeded)",
+        "config": {"workload": WORKLOAD, "rows": ROWS, "width": WIDTH, "batch": 1,
+                   "algorithmic_bytes_per_step": STEP_BYTES,
+                   "l2": f"inputs larger than L2: {COPIES} rotating weight copies ({COPIES * W_BYTES / 1e6:.0f} MB)",
+                   "parallelism": f"replica per GPU x{world}"},
+        "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
+                     "peak_source": peak_kind, "frac_of_nominal_8tbs": per_gpu / NOMINAL_HBM_GBS,
+                     "traffic": read_traffic(), "timing": "CUDA events over graph-replayed launches"},
+        "e2e": {"value": e2e_value, "unit": UNIT, "steps": e2e_steps,
+                "h2d_bytes_per_step": WIDTH * 4, "d2h_bytes_per_step": ROWS * 4},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20000)
+    parser.add_argument("--warmup", type=int, default=20)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    args = parser.parse_args()
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    dist = None
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as torch_dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        torch_dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist = torch_dist
+    try:
+        run_ours(args, rank, world, dist)
+    finally:
+        if dist:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,118 @@
+/* q38cuda.h - C ABI of the B200 (sm_100a) quantized-kernel library.
+ *
+ * Drop-in device counterpart of the upstream engine's kernel API
+ * (include/qwen38/qwen38_quant.h).  Every entry point takes plain pointers,
+ * sizes and a CUDA stream passed as `void *` (a cudaStream_t; NULL = legacy
+ * default stream), never a framework type.
+ *
+ * Conventions shared with the upstream API:
+ *   - matrices use GGUF order: shape[0] is the input width K, shape[1] the
+ *     number of output rows N (qwen38_quant.h:33);
+ *   - GEMM outputs are batch-major, out[token * N + row] (qwen38_quant.h:44-46);
+ *   - return 1 on success and 0 on bad arguments, shape or unsupported type
+ *     (qwen38_quant.c:2837-2857).  The reason for a 0 is available from
+ *     q38cu_last_error().
+ * Differences forced by the device:
+ *   - all buffers are device pointers owned by the caller;
+ *   - calls are asynchronous on `stream`; a kernel that gives up a bounded
+ *     wait records a code readable with q38cu_device_status();
+ *   - tensor data must start on a 16-byte boundary and its allocation must
+ *     extend to the next multiple of 16 bytes past nbytes (weights are moved
+ *     with 16-byte bulk copies); q38cu_tensor_upload() guarantees both.
+ */
+#ifndef Q38CUDA_H
+#define Q38CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Q38CU_Q8_K_BLOCK_SIZE 256
+
+/* Same layout as the upstream Q38Q8KBlock (qwen38_quant.h:14-18): 292 bytes. */
+typedef struct {
+    float scale;
+    int8_t quants[Q38CU_Q8_K_BLOCK_SIZE];
+    int16_t sums[Q38CU_Q8_K_BLOCK_SIZE / 16];
+} Q38CuQ8KBlock;
+
+/* Device view of a GGUF tensor.  Mirrors the fields of the upstream
+ * Q38GGUFTensor (qwen38_gguf.h:186-195) that the kernels read: `data` is the
+ * device copy of the tensor's GGUF bytes. */
+typedef struct {
+    uint32_t type;      /* GGML type id (GGUF value) */
+    uint32_t n_dims;    /* 2 for matrices, 1 for vectors */
+    uint64_t shape[2];  /* shape[0] = K (input width), shape[1] = N (rows) */
+    uint64_t nbytes;    /* bytes of GGUF data */
+    const void *data;   /* device pointer, 16-byte aligned */
+} Q38CuTensor;
+
+/* fp16 bits -> float (replaces q38_f16_to_f32, qwen38_quant.h:20). Host only. */
+float q38cu_f16_to_f32(uint16_t value);
+
+/* Quantize `length` fp32 values (a multiple of 256) into length/256 Q8_K
+ * blocks, bit-exact with q38_quantize_q8_k (qwen38_quant.h:24-25,
+ * qwen38_quant.c:50-88). */
+int q38cu_quantize_q8_k(Q38CuQ8KBlock *output, const float *input, uint64_t length,
+                        void *stream);
+
+/* Integer GEMV against a Q8_K activation row (replaces q38_tensor_gemv_q8_k,
+ * qwen38_quant.h:37-39). */
+int q38cu_tensor_gemv_q8_k(float *output, const Q38CuQ8KBlock *input, uint64_t input_length,
+                           const Q38CuTensor *tensor, void *stream);
+
+/* Batch-major integer GEMM, output [batch][N] (replaces q38_tensor_gemm_q8_k,
+ * qwen38_quant.h:47-49).  Each weight superblock is read from HBM once for
+ * all batch_size tokens. */
+int q38cu_tensor_gemm_q8_k(float *output, const Q38CuQ8KBlock *input, uint32_t batch_size,
+                           uint64_t input_length, const Q38CuTensor *tensor, void *stream);
+
+/* Parity probe: the same GEMM kernel additionally stores, for every
+ * (token, row, superblock), the two integer sums the upstream code folds into
+ * its float result: w = the scaled quant dot, x = the min term (Q2_K, Q4_K,
+ * Q5_K) or the delta correction (IQ1_S, IQ1_M), else 0.  Arrays are
+ * [batch][N][K/256].  No upstream counterpart (the upstream kernels keep these
+ * sums in registers); used to prove the sums bit-exact. */
+int q38cu_tensor_gemm_q8_k_sums(float *output, int32_t *w_out, int32_t *x_out,
+                                const Q38CuQ8KBlock *input, uint32_t batch_size,
+                                uint64_t input_length, const Q38CuTensor *tensor, void *stream);
+
+/* Float-activation GEMV/GEMM (replaces q38_tensor_gemv_f32 and
+ * q38_tensor_gemm_f32, qwen38_quant.h:33-35, 44-46).  Types: F32, F16, BF16,
+ * Q8_0 (the Q8_0 tensors of the Q4_K_M mix only take this path), Q2_K..Q6_K,
+ * IQ4_NL. */
+int q38cu_tensor_gemv_f32(float *output, const float *input, const Q38CuTensor *tensor,
+                          void *stream);
+int q38cu_tensor_gemm_f32(float *output, const float *input, uint32_t batch_size,
+                          uint64_t input_length, const Q38CuTensor *tensor, void *stream);
+
+/* Dequantize one row (replaces q38_tensor_row_f32, qwen38_quant.h:28-29);
+ * bit-exact with the upstream basis-vector evaluation for finite weights. */
+int q38cu_tensor_row_f32(float *output, const Q38CuTensor *tensor, uint64_t row, void *stream);
+
+/* Allocate device memory for a tensor (16-byte aligned, padded) and copy
+ * `host_data` (GGUF bytes, may be NULL to only allocate) into it.  The
+ * library counterpart of binding an mmapped tensor (qwen38_gguf.h:186-195). */
+int q38cu_tensor_upload(Q38CuTensor *tensor, uint32_t type, uint64_t width, uint64_t rows,
+                        const void *host_data, void *stream);
+void q38cu_tensor_free(Q38CuTensor *tensor);
+
+/* Bytes per GGUF block / elements per block (replaces q38_ggml_block_bytes and
+ * q38_ggml_block_elements, qwen38_gguf.h:228-229). */
+uint32_t q38cu_block_bytes(uint32_t type);
+uint32_t q38cu_block_elements(uint32_t type);
+
+/* Diagnostics: the message behind the last 0 return on this host thread, and
+ * the device status word (0 = ok, else a bounded wait gave up) which is read
+ * after synchronizing `stream` and then cleared. */
+const char *q38cu_last_error(void);
+int q38cu_device_status(void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

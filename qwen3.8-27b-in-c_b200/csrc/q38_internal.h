@@ -1,0 +1,45 @@
+// q38_internal.h - host-side interfaces between the C ABI (q38_api.cu) and
+// the kernel launchers (q38_kernels.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace q38 {
+
+// How one weight-streaming GEMM launch walks a tensor.
+struct GemmPlan {
+    uint64_t row_bytes;   // GGUF bytes of one weight row
+    int rows;             // N
+    int nb;               // 256-element superblocks per row (K / 256)
+    int rows_per_pass;    // rows decoded concurrently by one CTA (one superblock per thread)
+    int rows_per_stage;   // rows moved per bulk copy (a multiple of rows_per_pass)
+    int units;            // ceil(rows / rows_per_stage)
+    int stages;           // bulk-copy pipeline depth
+    uint32_t stage_bytes; // shared memory reserved per stage
+    int threads;          // CTA size
+    int max_ctas_per_sm;  // 0 = as many as fit
+};
+
+struct LaunchGemm {
+    const void *weights;
+    const void *act;
+    int batch;
+    float *out;
+    int32_t *dbg_w;  // optional per-superblock integer sums
+    int32_t *dbg_x;
+};
+
+int device_sm_count();
+int superblock_bytes(int type);
+size_t gemm_smem_for(int type, const GemmPlan &plan, int batch);
+cudaError_t launch_q8k_gemm(int type, const GemmPlan &plan, const LaunchGemm &l, cudaStream_t s);
+cudaError_t launch_quantize_q8k(void *out, const float *in, uint64_t blocks, cudaStream_t s);
+cudaError_t launch_f32_gemm(float *out, const float *x, int batch, uint64_t width, const void *w, uint64_t rows,
+                            int type, int be, int bb, cudaStream_t s);
+cudaError_t launch_row_f32(float *out, const void *w, uint64_t width, uint64_t row, int type, int be, int bb,
+                           cudaStream_t s);
+cudaError_t read_and_clear_status(int *status, cudaStream_t s);
+
+}  // namespace q38

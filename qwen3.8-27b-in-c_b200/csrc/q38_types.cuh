@@ -1,0 +1,426 @@
+// q38_types.cuh - per-format superblock decoders for the Q8_K integer path.
+//
+// A decoder works on one 256-element superblock of one weight row that sits
+// in shared memory, against MT Q8_K activation blocks held in registers (one
+// per token).  For each token it produces the two integer sums the upstream
+// kernels form (w, x) and the superblock's float contribution v, using the
+// same per-block formula as the upstream scalar code (src/qwen38/
+// qwen38_quant.c, cited per type).  Activation words are indexed with
+// compile-time constants only, so they stay in registers.
+#pragma once
+
+#include "q38_device.cuh"
+
+namespace q38 {
+
+enum : int {
+    kF32 = 0, kF16 = 1, kQ8_0 = 8, kQ2_K = 10, kQ3_K = 11, kQ4_K = 12, kQ5_K = 13, kQ6_K = 14,
+    kIQ2_XXS = 16, kIQ2_XS = 17, kIQ3_XXS = 18, kIQ1_S = 19, kIQ4_NL = 20, kIQ3_S = 21,
+    kIQ2_S = 22, kIQ4_XS = 23, kIQ1_M = 29, kBF16 = 30
+};
+
+// Device copy of an upstream Q38Q8KBlock (292 bytes, 4-byte aligned).
+struct Q8KBlock {
+    float scale;
+    int8_t quants[256];
+    int16_t sums[16];
+};
+
+// Activation block in registers: 64 words of int8 quants plus the block scale.
+struct ActBase {
+    uint32_t q[64];
+    float xs;
+};
+
+__device__ __forceinline__ void load_act_base(ActBase &a, const Q8KBlock *g)
+{
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(g->quants);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) a.q[i] = __ldg(w + i);
+    a.xs = __ldg(&g->scale);
+}
+
+__device__ __forceinline__ void zero_act_base(ActBase &a)
+{
+#pragma unroll
+    for (int i = 0; i < 64; ++i) a.q[i] = 0u;
+    a.xs = 0.0f;
+}
+
+// Sixteen int16 bsums of a Q8_K block.
+__device__ __forceinline__ int bsum(const Q8KBlock *g, int k) { return __ldg(&g->sums[k]); }
+
+__device__ __forceinline__ uint32_t pack16(int lo, int hi)
+{
+    return (static_cast<uint32_t>(lo) & 0xFFFFu) | (static_cast<uint32_t>(hi) << 16);
+}
+
+// ===========================================================================
+// Q4_K (144 B: fp16 d, fp16 dmin, 12 B packed 6-bit scales/mins, 128 B quants)
+// qwen38_quant.c:1546-1634 (integer path), :131-143 (scale unpack).
+// ===========================================================================
+struct ActQ4K : ActBase {
+    uint32_t pm[4];  // int16 pairs: bsum[2j] + bsum[2j+1] for sub-blocks j = 0..7
+};
+
+struct DecQ4K {
+    static constexpr int kBytes = 144;
+    static constexpr int kAlign = 16;
+    using Act = ActQ4K;
+    __device__ static void load(Act &a, const Q8KBlock *g)
+    {
+        load_act_base(a, g);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            a.pm[j] = pack16(bsum(g, 4 * j) + bsum(g, 4 * j + 1), bsum(g, 4 * j + 2) + bsum(g, 4 * j + 3));
+    }
+    __device__ static void zero(Act &a)
+    {
+        zero_act_base(a);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) a.pm[j] = 0u;
+    }
+    template <int MT>
+    __device__ static void block(const uint8_t *blk, const Act (&a)[MT], int (&w)[MT], int (&x)[MT],
+                                 float (&v)[MT])
+    {
+        const uint4 *p = reinterpret_cast<const uint4 *>(blk);
+        const uint4 h = p[0];
+        const uint32_t s0 = h.y, s1 = h.z, s2 = h.w;
+        const uint32_t sc_lo = s0 & 0x3F3F3F3Fu;
+        const uint32_t m_lo = s1 & 0x3F3F3F3Fu;
+        const uint32_t sc_hi = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
+        const uint32_t m_hi = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
+        int wl[MT], wh[MT];
+#pragma unroll
+        for (int t = 0; t < MT; ++t) wl[t] = wh[t] = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint4 qa = p[1 + 2 * c], qb = p[2 + 2 * c];
+            const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+            const uint32_t scw = c < 2 ? sc_lo : sc_hi;
+            const int sc0 = static_cast<int>(byte_of(scw, (2 * c) & 3));
+            const int sc1 = static_cast<int>(byte_of(scw, (2 * c + 1) & 3));
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+                int dl = 0, dh = 0;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    dl = dp4a_ss(q[i] & 0x0F0F0F0Fu, a[t].q[c * 16 + i], dl);
+                    // high nibbles kept in place: unsigned bytes 16*q
+                    dh = dp4a_us(q[i] & 0xF0F0F0F0u, a[t].q[c * 16 + 8 + i], dh);
+                }
+                wl[t] += sc0 * dl;
+                wh[t] += sc1 * dh;
+            }
+        }
+        const float d = f16_bits_to_f32(h.x & 0xFFFFu);
+        const float dmin = f16_bits_to_f32(h.x >> 16);
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+            w[t] = wl[t] + (wh[t] >> 4);  // wh is an exact multiple of 16
+            int m = dp2a_lo_ss(a[t].pm[0], m_lo, 0);
+            m = dp2a_hi_ss(a[t].pm[1], m_lo, m);
+            m = dp2a_lo_ss(a[t].pm[2], m_hi, m);
+            m = dp2a_hi_ss(a[t].pm[3], m_hi, m);
+            x[t] = m;
+            const float dd = __fmul_rn(d, a[t].xs), dm = __fmul_rn(dmin, a[t].xs);
+            v[t] = __fsub_rn(__fmul_rn(dd, static_cast<float>(w[t])), __fmul_rn(dm, static_cast<float>(m)));
+        }
+    }
+};
+
+// ===========================================================================
+// Q6_K (210 B: 128 B low nibbles, 64 B high 2-bit pairs, 16 int8 scales, fp16 d)
+// qwen38_quant.c:1727-1833 (the AVX2 form: unsigned q, minus 32*sum(sc*bsum)).
+// ===========================================================================
+struct ActQ6K : ActBase {
+    uint32_t bs[8];  // int16 pairs of the 16 bsums
+};
+
+struct DecQ6K {
+    static constexpr int kBytes = 210;
+    static constexpr int kAlign = 2;
+    using Act = ActQ6K;
+    __device__ static void load(Act &a, const Q8KBlock *g)
+    {
+        load_act_base(a, g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a.bs[j] = pack16(bsum(g, 2 * j), bsum(g, 2 * j + 1));
+    }
+    __device__ static void zero(Act &a)
+    {
+        zero_act_base(a);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a.bs[j] = 0u;
+    }
+    template <int MT>
+    __device__ static void block(const uint8_t *blk, const Act (&a)[MT], int (&w)[MT], int (&x)[MT],
+                                 float (&v)[MT])
+    {
+        uint32_t tail[5];  // bytes 192..211: 16 int8 scales, fp16 d (+2 past the end)
+        lds_words<5>(blk + 192, tail);
+        int acc[MT];
+#pragma unroll
+        for (int t = 0; t < MT; ++t) acc[t] = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint32_t ql[16], qh[8];
+            lds_words<16>(blk + 64 * h, ql);
+            lds_words<8>(blk + 128 + 32 * h, qh);
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) {
+                const int s = 4 * h + qq;
+                uint32_t val[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t lw = ql[(qq & 1) * 8 + i];
+                    const uint32_t nib = qq < 2 ? (lw & 0x0F0F0F0Fu) : ((lw >> 4) & 0x0F0F0F0Fu);
+                    val[i] = nib | (((qh[i] >> (2 * qq)) & 0x03030303u) << 4);
+                }
+                const int g0 = 8 * h + 2 * qq;
+                const int sc0 = sbyte_of(tail[g0 / 4], g0 & 3);
+                const int sc1 = sbyte_of(tail[(g0 + 1) / 4], (g0 + 1) & 3);
+#pragma unroll
+                for (int t = 0; t < MT; ++t) {
+                    int da = 0, db = 0;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) da = dp4a_us(val[i], a[t].q[s * 8 + i], da);
+#pragma unroll
+                    for (int i = 4; i < 8; ++i) db = dp4a_us(val[i], a[t].q[s * 8 + i], db);
+                    acc[t] += sc0 * da + sc1 * db;
+                }
+            }
+        }
+        const float d = f16_bits_to_f32(tail[4] & 0xFFFFu);
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+            int off = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                off = dp2a_lo_ss(a[t].bs[2 * j], tail[j], off);
+                off = dp2a_hi_ss(a[t].bs[2 * j + 1], tail[j], off);
+            }
+            w[t] = acc[t] - 32 * off;
+            x[t] = 0;
+            v[t] = __fmul_rn(__fmul_rn(d, a[t].xs), static_cast<float>(w[t]));
+        }
+    }
+};
+
+// ===========================================================================
+// IQ2_S (82 B: fp16 d, 32 B grid index low bytes, 32 B signs, 8 B index high
+// bits, 8 B 4-bit scales).  qwen38_quant.c:664-756.  `grid` is the 1024-entry
+// magnitude table expanded into shared memory (8 bytes per entry).
+// ===========================================================================
+struct DecIQ2S {
+    static constexpr int kBytes = 82;
+    static constexpr int kAlign = 2;
+    using Act = ActBase;
+    __device__ static void load(Act &a, const Q8KBlock *g) { load_act_base(a, g); }
+    __device__ static void zero(Act &a) { zero_act_base(a); }
+    template <int MT>
+    __device__ static void block(const uint8_t *blk, const Act (&a)[MT], int (&w)[MT], int (&x)[MT],
+                                 float (&v)[MT], const uint2 *grid)
+    {
+        uint32_t raw[21];  // bytes 0..83
+        lds_words<21>(blk, raw);
+        // byte k of the block
+#define Q38_B(k) byte_of(raw[(k) >> 2], (k) & 3)
+        int acc[MT];
+#pragma unroll
+        for (int t = 0; t < MT; ++t) acc[t] = 0;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const uint32_t qh = Q38_B(66 + g);
+            const uint32_t scb = Q38_B(74 + g);
+            const int s0 = 1 + 2 * static_cast<int>(scb & 15u);
+            const int s1 = 1 + 2 * static_cast<int>(scb >> 4);
+            int part[MT][2];
+#pragma unroll
+            for (int t = 0; t < MT; ++t) part[t][0] = part[t][1] = 0;
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const uint32_t gi = Q38_B(2 + 4 * g + s) | ((qh << (8 - 2 * s)) & 0x300u);
+                const uint2 e = grid[gi];
+                const uint32_t sg = Q38_B(34 + 4 * g + s);
+                const uint32_t lo = apply_signs(e.x, sign_mask4(sg & 15u));
+                const uint32_t hi = apply_signs(e.y, sign_mask4(sg >> 4));
+#pragma unroll
+                for (int t = 0; t < MT; ++t) {
+                    int d = dp4a_ss(lo, a[t].q[8 * g + 2 * s], part[t][s / 2]);
+                    part[t][s / 2] = dp4a_ss(hi, a[t].q[8 * g + 2 * s + 1], d);
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < MT; ++t) acc[t] += s0 * part[t][0] + s1 * part[t][1];
+        }
+#undef Q38_B
+        const float d = __fmul_rn(0.125f, f16_bits_to_f32(raw[0] & 0xFFFFu));
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+            w[t] = acc[t];
+            x[t] = 0;
+            v[t] = __fmul_rn(__fmul_rn(d, a[t].xs), static_cast<float>(acc[t]));
+        }
+    }
+};
+
+// ===========================================================================
+// IQ1_S (50 B: fp16 d, 32 B grid index low bytes, 8 x u16 {3-bit index highs,
+// 3-bit scale, delta sign}).  qwen38_quant.c:1177-1253.  `grid` is the
+// 2048-entry {-1,0,1} table expanded into shared memory.
+// ===========================================================================
+struct ActIQ1S : ActBase {
+    int gs[8];  // bsum[2g] + bsum[2g+1]
+};
+
+struct DecIQ1S {
+    static constexpr int kBytes = 50;
+    static constexpr int kAlign = 2;
+    using Act = ActIQ1S;
+    __device__ static void load(Act &a, const Q8KBlock *g)
+    {
+        load_act_base(a, g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a.gs[j] = bsum(g, 2 * j) + bsum(g, 2 * j + 1);
+    }
+    __device__ static void zero(Act &a)
+    {
+        zero_act_base(a);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a.gs[j] = 0;
+    }
+    template <int MT>
+    __device__ static void block(const uint8_t *blk, const Act (&a)[MT], int (&w)[MT], int (&x)[MT],
+                                 float (&v)[MT], const uint2 *grid)
+    {
+        uint32_t raw[13];  // bytes 0..51
+        lds_words<13>(blk, raw);
+#define Q38_B(k) byte_of(raw[(k) >> 2], (k) & 3)
+        int acc[MT], cor[MT];
+#pragma unroll
+        for (int t = 0; t < MT; ++t) acc[t] = cor[t] = 0;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const uint32_t qh = Q38_B(34 + 2 * g) | (Q38_B(35 + 2 * g) << 8);
+            const int scale = 1 + 2 * static_cast<int>((qh >> 12) & 7u);
+            const int sd = (qh & 0x8000u) ? -scale : scale;
+            int dot[MT];
+#pragma unroll
+            for (int t = 0; t < MT; ++t) dot[t] = 0;
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const uint32_t gi = Q38_B(2 + 4 * g + s) | (((qh >> (3 * s)) & 7u) << 8);
+                const uint2 e = grid[gi];
+#pragma unroll
+                for (int t = 0; t < MT; ++t) {
+                    dot[t] = dp4a_ss(e.x, a[t].q[8 * g + 2 * s], dot[t]);
+                    dot[t] = dp4a_ss(e.y, a[t].q[8 * g + 2 * s + 1], dot[t]);
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+                acc[t] += scale * dot[t];
+                cor[t] += sd * a[t].gs[g];
+            }
+        }
+#undef Q38_B
+        const float d = f16_bits_to_f32(raw[0] & 0xFFFFu);
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+            w[t] = acc[t];
+            x[t] = cor[t];
+            const float dd = __fmul_rn(d, a[t].xs);
+            v[t] = __fmul_rn(dd, __fadd_rn(static_cast<float>(acc[t]),
+                                           __fmul_rn(0.125f, static_cast<float>(cor[t]))));
+        }
+    }
+};
+
+// ===========================================================================
+// IQ1_M (56 B: 32 B grid index low bytes, 16 B {3-bit index highs, delta
+// signs}, 8 B {3-bit scales, fp16 super-scale in the top nibbles}).
+// qwen38_quant.c:1388-1544.  The correction uses 8-element activation sums.
+// ===========================================================================
+struct ActIQ1M : ActBase {
+    uint32_t s8[16];  // int16 pairs of the 32 eight-element quant sums
+};
+
+struct DecIQ1M {
+    static constexpr int kBytes = 56;
+    static constexpr int kAlign = 8;
+    using Act = ActIQ1M;
+    __device__ static void load(Act &a, const Q8KBlock *g)
+    {
+        load_act_base(a, g);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int lo = dp4a_ss(a.q[4 * j], 0x01010101u, dp4a_ss(a.q[4 * j + 1], 0x01010101u, 0));
+            const int hi = dp4a_ss(a.q[4 * j + 2], 0x01010101u, dp4a_ss(a.q[4 * j + 3], 0x01010101u, 0));
+            a.s8[j] = pack16(lo, hi);
+        }
+    }
+    __device__ static void zero(Act &a)
+    {
+        zero_act_base(a);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) a.s8[j] = 0u;
+    }
+    template <int MT>
+    __device__ static void block(const uint8_t *blk, const Act (&a)[MT], int (&w)[MT], int (&x)[MT],
+                                 float (&v)[MT], const uint2 *grid)
+    {
+        const uint2 *p = reinterpret_cast<const uint2 *>(blk);
+        uint32_t raw[14];
+#pragma unroll
+        for (int i = 0; i < 7; ++i) {
+            const uint2 u = p[i];
+            raw[2 * i] = u.x;
+            raw[2 * i + 1] = u.y;
+        }
+#define Q38_B(k) byte_of(raw[(k) >> 2], (k) & 3)
+        int acc[MT], cor[MT];
+#pragma unroll
+        for (int t = 0; t < MT; ++t) acc[t] = cor[t] = 0;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const uint32_t scw = (g < 4 ? raw[12] : raw[13]) >> (16 * ((g / 2) & 1));
+            const int shift = 6 * (g % 2);
+            const int sc[2] = {1 + 2 * static_cast<int>((scw >> shift) & 7u),
+                               1 + 2 * static_cast<int>((scw >> (shift + 3)) & 7u)};
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const uint32_t hb = Q38_B(32 + 2 * g + s / 2);
+                const uint32_t gi = Q38_B(4 * g + s) | ((hb << (8 - 4 * (s % 2))) & 0x700u);
+                const bool neg = (hb & (s % 2 ? 0x80u : 0x08u)) != 0;
+                const int scl = sc[s / 2];
+                const uint2 e = grid[gi];
+#pragma unroll
+                for (int t = 0; t < MT; ++t) {
+                    int d = dp4a_ss(e.x, a[t].q[8 * g + 2 * s], 0);
+                    d = dp4a_ss(e.y, a[t].q[8 * g + 2 * s + 1], d);
+                    acc[t] += scl * d;
+                    const uint32_t pair = a[t].s8[(4 * g + s) >> 1];
+                    const int sec = ((4 * g + s) & 1) ? static_cast<int>(static_cast<int16_t>(pair >> 16))
+                                                      : static_cast<int>(static_cast<int16_t>(pair & 0xFFFFu));
+                    cor[t] += neg ? -scl * sec : scl * sec;
+                }
+            }
+        }
+#undef Q38_B
+        const uint32_t sb = ((raw[12] & 0xFFFFu) >> 12) | (((raw[12] >> 16) >> 8) & 0x00F0u) |
+                            (((raw[13] & 0xFFFFu) >> 4) & 0x0F00u) | ((raw[13] >> 16) & 0xF000u);
+        const float d = f16_bits_to_f32(sb);
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+            w[t] = acc[t];
+            x[t] = cor[t];
+            const float dd = __fmul_rn(d, a[t].xs);
+            v[t] = __fmul_rn(dd, __fadd_rn(static_cast<float>(acc[t]),
+                                           __fmul_rn(0.125f, static_cast<float>(cor[t]))));
+        }
+    }
+};
+
+}  // namespace q38

@@ -1,0 +1,67 @@
+"""CPU tests of the C ABI: the library loads without a GPU, exports every
+symbol include/q38cuda.h declares, and rejects bad arguments with the
+upstream return convention (0) before touching the device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "q38cuda.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(q38cu_\w+)\s*\(", text)))
+
+
+def test_library_exports_header(q38):
+    lib = q38.lib()
+    names = declared_functions()
+    assert len(names) >= 14
+    for name in names:
+        assert hasattr(lib, name), name
+
+
+def test_host_helpers(q38):
+    lib = q38.lib()
+    assert lib.q38cu_f16_to_f32(0x3C00) == 1.0
+    assert lib.q38cu_f16_to_f32(0x0001) == 2.0 ** -24
+    assert lib.q38cu_f16_to_f32(0xC000) == -2.0
+    # GGUF block geometry (upstream src/io/qwen38_gguf.c:130-185)
+    expect = {12: (256, 144), 14: (256, 210), 8: (32, 34), 19: (256, 50), 29: (256, 56), 22: (256, 82),
+              0: (1, 4), 1: (1, 2), 20: (32, 18)}
+    for t, (e, b) in expect.items():
+        assert lib.q38cu_block_elements(t) == e and lib.q38cu_block_bytes(t) == b
+    assert lib.q38cu_block_bytes(2) == 0  # Q4_0 is not part of this engine's formats
+
+
+def test_rejects_bad_arguments_without_device(q38):
+    lib = q38.lib()
+    null = ctypes.c_void_p()
+    assert lib.q38cu_quantize_q8_k(null, null, 256, null) == 0
+    assert "required" in q38.last_error()
+    t = q38.CuTensor()
+    t.type, t.n_dims, t.shape[0], t.shape[1], t.nbytes = 12, 2, 512, 4, 4 * 288
+    t.data = 16
+    buf = ctypes.c_void_p(64)
+    # width mismatch
+    assert lib.q38cu_tensor_gemv_q8_k(buf, buf, 256, ctypes.byref(t), null) == 0
+    assert "shape[0]" in q38.last_error()
+    # misaligned data
+    t.data = 18
+    assert lib.q38cu_tensor_gemv_q8_k(buf, buf, 512, ctypes.byref(t), null) == 0
+    assert "aligned" in q38.last_error()
+    # too few bytes
+    t.data, t.nbytes = 16, 100
+    assert lib.q38cu_tensor_gemv_q8_k(buf, buf, 512, ctypes.byref(t), null) == 0
+    # float-path type on the integer path
+    t.type, t.nbytes = 8, 10 ** 6
+    assert lib.q38cu_tensor_gemv_q8_k(buf, buf, 512, ctypes.byref(t), null) == 0
+    assert "Q8_K" in q38.last_error()
+    # zero batch
+    t.type = 12
+    assert lib.q38cu_tensor_gemm_q8_k(buf, buf, 0, 512, ctypes.byref(t), null) == 0

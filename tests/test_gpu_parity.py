@@ -1,0 +1,168 @@
+"""GPU parity tests: the sm_100a kernels behind the C ABI against the CPU
+oracle and the golden fixtures produced by the upstream engine.
+
+Bars (from the project's target): the Q8_K quantizer, per-superblock integer
+sums and row dequantization are bit-exact; GEMV/GEMM fp32 outputs agree with
+the oracle within REL = 1e-3 relative (the upstream AVX2 kernels and this
+kernel add the same per-superblock floats in different orders; the observed
+differences are ~1e-7 relative); a batched GEMM row is bit-identical to the
+single-token GEMV of the same token (tests/unit/test_qwen38_quant.c:637-684).
+"""
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import GOLDEN
+from q38b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+REL = 1e-3
+DEVICE_Q8K = (O.Q4_K, O.Q6_K, O.IQ2_S, O.IQ1_S, O.IQ1_M)
+NAME = O.TYPE_NAMES
+
+
+def to_dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def q8k_dev(q8k):
+    return to_dev(np.ascontiguousarray(q8k).view(np.uint8).reshape(-1))
+
+
+def assert_close(gpu, ref, rel=REL):
+    gpu = np.asarray(gpu, np.float64)
+    ref = np.asarray(ref, np.float64)
+    floor = 1e-2 * np.sqrt(np.mean(ref * ref)) + 1e-30
+    bad = np.abs(gpu - ref) > rel * np.maximum(np.abs(ref), floor)
+    assert not bad.any(), f"{bad.sum()} mismatches; worst {np.max(np.abs(gpu - ref) / np.maximum(np.abs(ref), floor))}"
+
+
+def test_quantize_random_bitexact(q38, oracle):
+    for m, k in ((1, 5120), (3, 17408), (2, 256), (4, 6144)):
+        x = synth.activations(m, k, seed=m * 7 + k)
+        x[0, :256] *= 1e-20  # tiny block
+        x[-1, -256:] = 0.0   # zero block
+        got = q38.quantize_q8_k(to_dev(x)).cpu().numpy()
+        assert np.array_equal(got.reshape(-1), oracle.quantize_q8_k(x).view(np.uint8).reshape(-1))
+
+
+def test_quantize_golden_edges(q38):
+    g = np.load(os.path.join(GOLDEN, "quantize_edges.npz"))
+    got = q38.quantize_q8_k(to_dev(g["x"])).cpu().numpy()
+    assert np.array_equal(got.reshape(g["q8k"].shape), g["q8k"])
+
+
+@pytest.mark.parametrize("qtype", DEVICE_Q8K, ids=lambda t: NAME[t])
+def test_gemm_golden(q38, qtype):
+    g = np.load(os.path.join(GOLDEN, f"q8k_{NAME[qtype]}.npz"))
+    rows, width = g["weights"].shape[0], g["x"].shape[1]
+    batch = g["x"].shape[0]
+    t = q38.DeviceTensor(qtype, width, rows, g["weights"])
+    act = to_dev(g["q8k"].reshape(-1))
+    out, w, x = q38.gemm_q8_k_sums(t, act, batch)
+    out, w, x = out.cpu().numpy(), w.cpu().numpy().astype(np.int64), x.cpu().numpy().astype(np.int64)
+    assert_close(out, g["out"])
+    if qtype == O.IQ1_M:
+        assert np.array_equal(8 * w + x, g["block_w"])
+    else:
+        assert np.array_equal(w, g["block_w"]) and np.array_equal(x, g["block_x"])
+    for tok in range(batch):
+        single = q38.gemm_q8_k(t, act[tok * (width // 256) * 292:(tok + 1) * (width // 256) * 292], 1)
+        assert_close(single.cpu().numpy()[0], g["gemv"][tok])
+
+
+SHAPES = [(17, 256), (64, 512), (333, 5120), (37, 17408), (5, 6144), (129, 10240), (1, 5120)]
+
+
+@pytest.mark.parametrize("qtype", DEVICE_Q8K, ids=lambda t: NAME[t])
+@pytest.mark.parametrize("rows,width", SHAPES)
+def test_gemm_random_vs_oracle(q38, oracle, qtype, rows, width):
+    weights = synth.quant_tensor(qtype, rows, width, seed=rows * 31 + width + qtype)
+    t = q38.DeviceTensor(qtype, width, rows, weights)
+    for batch in (1, 2, 3, 8):
+        q8k = oracle.quantize_q8_k(synth.activations(batch, width, seed=batch + rows))
+        out, w, x = q38.gemm_q8_k_sums(t, q8k_dev(q8k), batch)
+        ref_out = oracle.gemm_q8_k(qtype, weights, rows, width, q8k)
+        ref_w, ref_x = oracle.gemm_q8_k_sums(qtype, weights, rows, width, q8k)
+        assert np.array_equal(w.cpu().numpy(), ref_w), f"w sums differ (batch {batch})"
+        assert np.array_equal(x.cpu().numpy(), ref_x), f"x sums differ (batch {batch})"
+        assert_close(out.cpu().numpy(), ref_out)
+
+
+@pytest.mark.parametrize("qtype", DEVICE_Q8K, ids=lambda t: NAME[t])
+def test_batch_bit_exact_with_gemv(q38, oracle, qtype):
+    rows, width = 96, 5120
+    weights = synth.quant_tensor(qtype, rows, width, seed=qtype)
+    t = q38.DeviceTensor(qtype, width, rows, weights)
+    q8k = oracle.quantize_q8_k(synth.activations(8, width, seed=99))
+    act = q8k_dev(q8k)
+    per_token = width // 256 * 292
+    single = np.stack([q38.gemm_q8_k(t, act[i * per_token:(i + 1) * per_token], 1).cpu().numpy()[0]
+                       for i in range(8)])
+    for batch in range(1, 9):
+        out = q38.gemm_q8_k(t, act[:batch * per_token], batch).cpu().numpy()
+        assert np.array_equal(out, single[:batch]), f"batch {batch}"
+
+
+def test_q4k_full_size(q38, oracle):
+    """BASELINE config 0 shape: 17408 x 5120 Q4_K, fp32 N(0,1) activation."""
+    rows, width = 17408, 5120
+    weights = synth.quant_tensor(O.Q4_K, rows, width, seed=0)
+    x = synth.activations(1, width, seed=1)
+    t = q38.DeviceTensor(O.Q4_K, width, rows, weights)
+    act = q38.quantize_q8_k(to_dev(x))
+    q8k = oracle.quantize_q8_k(x)
+    assert np.array_equal(act.cpu().numpy().reshape(-1), q8k.view(np.uint8).reshape(-1))
+    out = q38.gemm_q8_k(t, act, 1).cpu().numpy()
+    assert_close(out, oracle.gemm_q8_k(O.Q4_K, weights, rows, width, q8k))
+
+
+F32_TYPES = (O.Q8_0, O.F32, O.F16, O.Q4_K, O.Q6_K, O.Q2_K, O.Q3_K, O.Q5_K, O.IQ4_NL)
+
+
+@pytest.mark.parametrize("qtype", F32_TYPES, ids=lambda t: NAME[t])
+def test_float_path_golden(q38, qtype):
+    g = np.load(os.path.join(GOLDEN, f"f32_{NAME[qtype]}.npz"))
+    rows, width = g["weights"].shape[0], g["x"].shape[1]
+    t = q38.DeviceTensor(qtype, width, rows, g["weights"])
+    out = q38.gemm_f32(t, to_dev(g["x"])).cpu().numpy()
+    assert_close(out, g["out"])
+    for r in range(rows):
+        assert np.array_equal(q38.row_f32(t, r).cpu().numpy(), g["rows"][r])
+
+
+def test_q8_0_alpha_beta_shape(q38, oracle):
+    """ssm_alpha / ssm_beta: Q8_0 48 x 5120 through the float path."""
+    weights = synth.quant_tensor(O.Q8_0, 48, 5120, seed=5)
+    x = synth.activations(4, 5120, seed=6)
+    t = q38.DeviceTensor(O.Q8_0, 5120, 48, weights)
+    out = q38.gemm_f32(t, to_dev(x)).cpu().numpy()
+    assert_close(out, oracle.gemm_f32(O.Q8_0, weights, 48, 5120, x))
+
+
+def test_embedding_row_full_size(q38, oracle):
+    """token_embd row dequant (Q4_K 248320 x 5120 in the mix; a slice here)."""
+    rows, width = 64, 5120
+    weights = synth.quant_tensor(O.Q4_K, rows, width, seed=8)
+    t = q38.DeviceTensor(O.Q4_K, width, rows, weights)
+    for r in (0, 31, 63):
+        assert np.array_equal(q38.row_f32(t, r).cpu().numpy(), oracle.row_f32(O.Q4_K, weights, rows, width, r))
+
+
+def test_device_status_clean(q38):
+    assert q38.device_status() == 0
+
+
+def test_error_paths(q38):
+    t = q38.DeviceTensor(O.Q4_K, 512, 4, synth.quant_tensor(O.Q4_K, 4, 512, seed=1))
+    import torch
+    act = torch.zeros(2 * 292, dtype=torch.uint8, device="cuda")
+    with pytest.raises(q38.Q38CudaError):
+        q38.gemm_q8_k(t, act, 0)
+    t2 = q38.DeviceTensor(O.Q5_K, 512, 4, synth.quant_tensor(O.Q5_K, 4, 512, seed=1))
+    with pytest.raises(q38.Q38CudaError, match="not yet implemented"):
+        q38.gemm_q8_k(t2, act, 1)

@@ -39,15 +39,31 @@ typedef struct {
     int16_t sums[Q38CU_Q8_K_BLOCK_SIZE / 16];
 } Q38CuQ8KBlock;
 
+/* Tensor data layouts on the device. */
+#define Q38CU_LAYOUT_GGUF 0u   /* the GGUF bytes as in the file (row-major blocks) */
+#define Q38CU_LAYOUT_TILED 1u  /* the same blocks regrouped for streaming: rows in tiles of
+                                  tile_rows, block (r, b) at
+                                  (((r / T) * nb + b) * T + r % T) * B with T = tile_rows,
+                                  rows padded with zero blocks to whole tiles */
+
 /* Device view of a GGUF tensor.  Mirrors the fields of the upstream
  * Q38GGUFTensor (qwen38_gguf.h:186-195) that the kernels read: `data` is the
- * device copy of the tensor's GGUF bytes. */
+ * device copy of the tensor's GGUF bytes, optionally in the streaming layout
+ * (the upstream `iq1_s_repack` side view, qwen38_gguf.h:194, is the precedent
+ * for a load-time repack hanging off the tensor).  Tensors in the tiled layout
+ * carry `scratch`: per-tensor device memory for the partial sums of row tiles
+ * that several CTAs share (zeroed counters at the start); calls that use the
+ * same tensor concurrently on two streams race. */
 typedef struct {
     uint32_t type;      /* GGML type id (GGUF value) */
     uint32_t n_dims;    /* 2 for matrices, 1 for vectors */
     uint64_t shape[2];  /* shape[0] = K (input width), shape[1] = N (rows) */
-    uint64_t nbytes;    /* bytes of GGUF data */
+    uint64_t nbytes;    /* bytes of device data (padded rows included) */
     const void *data;   /* device pointer, 16-byte aligned */
+    uint32_t layout;    /* Q38CU_LAYOUT_* */
+    uint32_t tile_rows; /* tiled layout: rows per tile (a multiple of 8); else 0 */
+    void *scratch;      /* tiled layout only: device scratch */
+    uint64_t scratch_bytes;
 } Q38CuTensor;
 
 /* fp16 bits -> float (replaces q38_f16_to_f32, qwen38_quant.h:20). Host only. */
@@ -93,11 +109,17 @@ int q38cu_tensor_gemm_f32(float *output, const float *input, uint32_t batch_size
  * bit-exact with the upstream basis-vector evaluation for finite weights. */
 int q38cu_tensor_row_f32(float *output, const Q38CuTensor *tensor, uint64_t row, void *stream);
 
-/* Allocate device memory for a tensor (16-byte aligned, padded) and copy
- * `host_data` (GGUF bytes, may be NULL to only allocate) into it.  The
- * library counterpart of binding an mmapped tensor (qwen38_gguf.h:186-195). */
+/* Allocate device memory for a tensor (16-byte aligned, padded), copy
+ * `host_data` (GGUF bytes, may be NULL to only allocate) into it in the given
+ * layout and, for the tiled layout, choose its tile height for this device and
+ * allocate its scratch.  The
+ * library counterpart of binding an mmapped tensor (qwen38_gguf.h:186-195,
+ * qwen38_model.c:1370-1406). */
 int q38cu_tensor_upload(Q38CuTensor *tensor, uint32_t type, uint64_t width, uint64_t rows,
-                        const void *host_data, void *stream);
+                        const void *host_data, uint32_t layout, void *stream);
+/* Build a tiled copy (plus scratch) of a GGUF-layout device tensor
+ * (counterpart of q38_prepare_iq1_s_repacks, qwen38_quant.h:53-56). */
+int q38cu_tensor_repack(Q38CuTensor *dst, const Q38CuTensor *src, void *stream);
 void q38cu_tensor_free(Q38CuTensor *tensor);
 
 /* Bytes per GGUF block / elements per block (replaces q38_ggml_block_bytes and

@@ -131,6 +131,13 @@ q38::GemmPlan make_plan(uint32_t type, uint64_t width, uint64_t rows, int batch)
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+uint64_t rows_padded(uint64_t rows, uint32_t tile_rows)
+{
+    return (rows + tile_rows - 1) / tile_rows * tile_rows;
+}
+
+bool superblock_layout_type(uint32_t type) { return geometry(type).elements == 256; }
+
 int check_matrix(const Q38CuTensor *t, uint64_t input_length)
 {
     if (!t) return fail("tensor is NULL%s");
@@ -141,8 +148,61 @@ int check_matrix(const Q38CuTensor *t, uint64_t input_length)
     const Geometry g = geometry(t->type);
     if (!g.elements || input_length % g.elements) return fail("unsupported type or width%s");
     if (t->shape[1] == 0 || t->shape[1] > 0x7fffffffull) return fail("bad row count%s");
-    const uint64_t need = input_length / g.elements * g.bytes * t->shape[1];
+    if (t->layout != Q38CU_LAYOUT_GGUF && t->layout != Q38CU_LAYOUT_TILED)
+        return fail("unknown tensor layout%s");
+    if (t->layout == Q38CU_LAYOUT_TILED && !superblock_layout_type(t->type))
+        return fail("tiled layout needs a 256-element block type%s");
+    if (t->layout == Q38CU_LAYOUT_TILED && (t->tile_rows == 0 || t->tile_rows % 8 || t->tile_rows > 256))
+        return fail("tiled layout needs tile_rows a multiple of 8 in 8..256%s");
+    const uint64_t rows = t->layout == Q38CU_LAYOUT_GGUF ? t->shape[1] : rows_padded(t->shape[1], t->tile_rows);
+    const uint64_t need = input_length / g.elements * g.bytes * rows;
     if (t->nbytes < need) return fail("tensor nbytes smaller than shape requires%s");
+    return 1;
+}
+
+uint32_t layout_tile_rows(const Q38CuTensor *t) { return t->layout == Q38CU_LAYOUT_TILED ? t->tile_rows : 0; }
+
+int stream_gemm(float *output, int32_t *w_out, int32_t *x_out, const Q38CuQ8KBlock *input, uint32_t batch,
+                uint64_t input_length, const Q38CuTensor *tensor, cudaStream_t stream)
+{
+    const int rows = static_cast<int>(tensor->shape[1]);
+    const int width = static_cast<int>(input_length);
+    const int nb = width / 256;
+    for (uint32_t tok0 = 0; tok0 < batch;) {
+        q38::StreamPlan plan;
+        cudaError_t e = q38::stream_plan(static_cast<int>(tensor->type), rows, width,
+                                         static_cast<int>(tensor->tile_rows), static_cast<int>(batch - tok0), &plan);
+        if (e != cudaSuccess) return fail_cuda("stream plan", e);
+        if (!tensor->scratch || tensor->scratch_bytes < plan.scratch_bytes)
+            return fail("tensor scratch missing or too small (prepare it with q38cu_tensor_upload/repack)%s");
+        const int tokens = plan.token_group;
+        q38::StreamLaunch l;
+        l.weights = tensor->data;
+        l.act = input + static_cast<size_t>(tok0) * nb;
+        l.tokens = tokens;
+        l.out = output + static_cast<size_t>(tok0) * rows;
+        l.scratch = tensor->scratch;
+        l.dbg_w = w_out ? w_out + static_cast<size_t>(tok0) * rows * nb : nullptr;
+        l.dbg_x = x_out ? x_out + static_cast<size_t>(tok0) * rows * nb : nullptr;
+        e = q38::launch_stream_gemm(static_cast<int>(tensor->type), plan, l, stream);
+        if (e != cudaSuccess) return fail_cuda("stream gemm launch", e);
+        tok0 += static_cast<uint32_t>(tokens);
+    }
+    return 1;
+}
+
+// Scratch a tiled tensor needs for any batch size.
+int stream_scratch_bytes(uint32_t type, uint64_t width, uint64_t rows, uint32_t tile_rows, uint64_t *bytes)
+{
+    uint64_t need = 0;
+    for (int tokens = 1; tokens <= 8; ++tokens) {
+        q38::StreamPlan plan;
+        const cudaError_t e = q38::stream_plan(static_cast<int>(type), static_cast<int>(rows),
+                                               static_cast<int>(width), static_cast<int>(tile_rows), tokens, &plan);
+        if (e != cudaSuccess) return fail_cuda("stream plan", e);
+        need = std::max(need, plan.scratch_bytes);
+    }
+    *bytes = need;
     return 1;
 }
 
@@ -156,6 +216,8 @@ int gemm_q8k(float *output, int32_t *w_out, int32_t *x_out, const Q38CuQ8KBlock 
     if (!q38::superblock_bytes(static_cast<int>(tensor->type)))
         return fail("type not yet implemented on the device%s");
     if (input_length / 256 > 256) return fail("input length above 65536 is not supported%s");
+    if (tensor->layout == Q38CU_LAYOUT_TILED)
+        return stream_gemm(output, w_out, x_out, input, batch, input_length, tensor, static_cast<cudaStream_t>(stream));
     const q38::GemmPlan plan = make_plan(tensor->type, input_length, tensor->shape[1], static_cast<int>(batch));
     q38::LaunchGemm l{tensor->data, input, static_cast<int>(batch), output, w_out, x_out};
     const cudaError_t e =
@@ -215,13 +277,14 @@ const char *q38cu_last_error(void) { return g_error; }
 
 int q38cu_device_status(void *stream)
 {
-    int status = 0;
-    const cudaError_t e = q38::read_and_clear_status(&status, static_cast<cudaStream_t>(stream));
+    int status = 0, stream_status = 0;
+    cudaError_t e = q38::read_and_clear_status(&status, static_cast<cudaStream_t>(stream));
+    if (e == cudaSuccess) e = q38::read_and_clear_stream_status(&stream_status);
     if (e != cudaSuccess) {
         fail_cuda("device status", e);
         return -1;
     }
-    return status;
+    return status ? status : stream_status;
 }
 
 int q38cu_quantize_q8_k(Q38CuQ8KBlock *output, const float *input, uint64_t length, void *stream)
@@ -262,7 +325,8 @@ int q38cu_tensor_gemm_f32(float *output, const float *input, uint32_t batch_size
     if (!float_path_type(tensor->type)) return fail("type has no float-path kernel%s");
     const Geometry g = geometry(tensor->type);
     const cudaError_t e = q38::launch_f32_gemm(output, input, static_cast<int>(batch_size), input_length,
-                                               tensor->data, tensor->shape[1], static_cast<int>(tensor->type),
+                                               tensor->data, tensor->shape[1], layout_tile_rows(tensor),
+                                               static_cast<int>(tensor->type),
                                                static_cast<int>(g.elements), static_cast<int>(g.bytes),
                                                static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? 1 : fail_cuda("f32 gemm launch", e);
@@ -281,44 +345,99 @@ int q38cu_tensor_row_f32(float *output, const Q38CuTensor *tensor, uint64_t row,
     if (row >= tensor->shape[1]) return fail("row out of range%s");
     if (!float_path_type(tensor->type)) return fail("type has no row decoder%s");
     const Geometry g = geometry(tensor->type);
-    const cudaError_t e = q38::launch_row_f32(output, tensor->data, tensor->shape[0], row,
+    const cudaError_t e = q38::launch_row_f32(output, tensor->data, tensor->shape[0], layout_tile_rows(tensor), row,
                                               static_cast<int>(tensor->type), static_cast<int>(g.elements),
                                               static_cast<int>(g.bytes), static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? 1 : fail_cuda("row launch", e);
 }
 
 int q38cu_tensor_upload(Q38CuTensor *tensor, uint32_t type, uint64_t width, uint64_t rows, const void *host_data,
-                        void *stream)
+                        uint32_t layout, void *stream)
 {
     if (!tensor) return fail("tensor is NULL%s");
     const Geometry g = geometry(type);
     if (!g.elements || !width || width % g.elements || !rows) return fail("unsupported type or shape%s");
-    const uint64_t nbytes = width / g.elements * g.bytes * rows;
+    if (layout != Q38CU_LAYOUT_GGUF && layout != Q38CU_LAYOUT_TILED) return fail("unknown layout%s");
+    if (layout == Q38CU_LAYOUT_TILED && !superblock_layout_type(type))
+        return fail("tiled layout needs a 256-element block type%s");
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    Q38CuTensor src{};
+    src.type = type;
+    src.n_dims = 2;
+    src.shape[0] = width;
+    src.shape[1] = rows;
+    src.nbytes = width / g.elements * g.bytes * rows;
+    src.layout = Q38CU_LAYOUT_GGUF;
     void *dev = nullptr;
-    cudaError_t e = cudaMalloc(&dev, (nbytes + 15) / 16 * 16 + 256);
+    cudaError_t e = cudaMalloc(&dev, (src.nbytes + 15) / 16 * 16 + 256);
     if (e != cudaSuccess) return fail_cuda("cudaMalloc", e);
     if (host_data) {
-        e = cudaMemcpyAsync(dev, host_data, nbytes, cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream));
-        if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+        e = cudaMemcpyAsync(dev, host_data, src.nbytes, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) {
             cudaFree(dev);
             return fail_cuda("upload copy", e);
         }
     }
-    tensor->type = type;
-    tensor->n_dims = 2;
-    tensor->shape[0] = width;
-    tensor->shape[1] = rows;
-    tensor->nbytes = nbytes;
-    tensor->data = dev;
+    src.data = dev;
+    if (layout == Q38CU_LAYOUT_GGUF) {
+        *tensor = src;
+        return 1;
+    }
+    const int ok = q38cu_tensor_repack(tensor, &src, stream);
+    cudaStreamSynchronize(s);
+    cudaFree(dev);
+    return ok;
+}
+
+int q38cu_tensor_repack(Q38CuTensor *dst, const Q38CuTensor *src, void *stream)
+{
+    if (!dst || !src) return fail("dst and src are required%s");
+    if (!check_matrix(src, src->shape[0])) return 0;
+    if (src->layout != Q38CU_LAYOUT_GGUF) return fail("source must be in the GGUF layout%s");
+    if (!superblock_layout_type(src->type)) return fail("tiled layout needs a 256-element block type%s");
+    if (!q38::superblock_bytes(static_cast<int>(src->type))) return fail("type not yet implemented on the device%s");
+    const Geometry g = geometry(src->type);
+    const uint64_t nb = src->shape[0] / 256, rows = src->shape[1];
+    const uint32_t tile_rows = static_cast<uint32_t>(q38::stream_tile_rows(static_cast<int>(rows)));
+    const uint64_t nbytes = nb * g.bytes * rows_padded(rows, tile_rows);
+    uint64_t scratch_bytes = 0;
+    if (!stream_scratch_bytes(src->type, src->shape[0], rows, tile_rows, &scratch_bytes)) return 0;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void *data = nullptr, *scratch = nullptr;
+    cudaError_t e = cudaMalloc(&data, nbytes + 256);
+    if (e == cudaSuccess) e = cudaMalloc(&scratch, scratch_bytes);
+    if (e == cudaSuccess) e = cudaMemsetAsync(data, 0, nbytes + 256, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(scratch, 0, scratch_bytes, s);
+    if (e == cudaSuccess) e = q38::launch_repack_tiled(data, src->data, rows, nb, tile_rows, g.bytes, s);
+    if (e != cudaSuccess) {
+        cudaFree(data);
+        cudaFree(scratch);
+        return fail_cuda("repack", e);
+    }
+    Q38CuTensor t{};
+    t.type = src->type;
+    t.n_dims = 2;
+    t.shape[0] = src->shape[0];
+    t.shape[1] = rows;
+    t.nbytes = nbytes;
+    t.data = data;
+    t.layout = Q38CU_LAYOUT_TILED;
+    t.tile_rows = tile_rows;
+    t.scratch = scratch;
+    t.scratch_bytes = scratch_bytes;
+    *dst = t;
     return 1;
 }
 
 void q38cu_tensor_free(Q38CuTensor *tensor)
 {
-    if (!tensor || !tensor->data) return;
-    cudaFree(const_cast<void *>(tensor->data));
+    if (!tensor) return;
+    if (tensor->data) cudaFree(const_cast<void *>(tensor->data));
+    if (tensor->scratch) cudaFree(tensor->scratch);
     tensor->data = nullptr;
+    tensor->scratch = nullptr;
+    tensor->scratch_bytes = 0;
 }
 
 }  // extern "C"

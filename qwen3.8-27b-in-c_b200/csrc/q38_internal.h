@@ -31,15 +31,46 @@ struct LaunchGemm {
     int32_t *dbg_x;
 };
 
+// Tiled-layout streaming GEMM (q38_stream.cu).
+struct StreamPlan {
+    int rows, rows_pad, nb, block_bytes;
+    int tile_rows, tiles, groups, chunk;
+    int mt, token_group;  // kernel token capacity / tokens handled per launch
+    int stages;
+    uint32_t stage_bytes;
+    int threads, grid;
+    long long units;
+    int max_slots;
+    uint64_t counter_bytes, scratch_bytes;
+};
+
+struct StreamLaunch {
+    const void *weights;  // tiled-layout bytes
+    const void *act;      // Q8_K blocks of this launch's tokens
+    int tokens;
+    float *out;           // rows of this launch's first token
+    void *scratch;
+    int32_t *dbg_w;
+    int32_t *dbg_x;
+};
+
+int stream_tile_rows(int rows);
+cudaError_t stream_plan(int type, int rows, int width, int tile_rows, int tokens, StreamPlan *p);
+cudaError_t launch_stream_gemm(int type, const StreamPlan &p, const StreamLaunch &l, cudaStream_t s);
+cudaError_t launch_repack_tiled(void *dst, const void *src, uint64_t rows, uint64_t nb, uint32_t tile_rows,
+                                uint32_t block_bytes, cudaStream_t s);
+
 int device_sm_count();
 int superblock_bytes(int type);
 size_t gemm_smem_for(int type, const GemmPlan &plan, int batch);
 cudaError_t launch_q8k_gemm(int type, const GemmPlan &plan, const LaunchGemm &l, cudaStream_t s);
 cudaError_t launch_quantize_q8k(void *out, const float *in, uint64_t blocks, cudaStream_t s);
+// `tile_rows` != 0 selects the tiled layout for block addressing.
 cudaError_t launch_f32_gemm(float *out, const float *x, int batch, uint64_t width, const void *w, uint64_t rows,
-                            int type, int be, int bb, cudaStream_t s);
-cudaError_t launch_row_f32(float *out, const void *w, uint64_t width, uint64_t row, int type, int be, int bb,
-                           cudaStream_t s);
+                            uint32_t tile_rows, int type, int be, int bb, cudaStream_t s);
+cudaError_t launch_row_f32(float *out, const void *w, uint64_t width, uint32_t tile_rows, uint64_t row, int type,
+                           int be, int bb, cudaStream_t s);
 cudaError_t read_and_clear_status(int *status, cudaStream_t s);
+cudaError_t read_and_clear_stream_status(int *status);
 
 }  // namespace q38

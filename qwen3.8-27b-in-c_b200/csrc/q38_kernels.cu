@@ -22,19 +22,14 @@
 #include <mutex>
 
 #include "../../include/q38cuda.h"
-#define Q38_CODEBOOKS_MACROS_ONLY
-#include "q38_codebooks.h"
 #include "q38_device.cuh"
+#include "q38_grid.cuh"
 #include "q38_internal.h"
 #include "q38_types.cuh"
 
 namespace q38 {
 
 __device__ int g_status;  // device status word (see q38cu_device_status)
-
-// Compact codebooks (see gen_codebooks.py), expanded per CTA into shared memory.
-__device__ const uint32_t d_iq1s_nib[2048] = Q38_IQ1S_GRID_NIB_INIT;
-__device__ const uint32_t d_iq2s_nib[1024] = Q38_IQ2S_GRID_NIB_INIT;
 
 constexpr int kMaxStages = 4;
 
@@ -56,46 +51,6 @@ struct GemmArgs {
     uint32_t stage_bytes;  // bytes reserved per stage (>= data + 32 slack)
 };
 
-template <typename Dec>
-struct NeedsGrid { static constexpr int kEntries = 0; };
-template <> struct NeedsGrid<DecIQ1S> { static constexpr int kEntries = 2048; };
-template <> struct NeedsGrid<DecIQ1M> { static constexpr int kEntries = 2048; };
-template <> struct NeedsGrid<DecIQ2S> { static constexpr int kEntries = 1024; };
-
-template <typename Dec, int MT>
-__device__ __forceinline__ void run_block(const uint8_t *blk, const typename Dec::Act (&a)[MT], int (&w)[MT],
-                                          int (&x)[MT], float (&v)[MT], const uint2 *grid)
-{
-    if constexpr (NeedsGrid<Dec>::kEntries > 0)
-        Dec::template block<MT>(blk, a, w, x, v, grid);
-    else
-        Dec::template block<MT>(blk, a, w, x, v);
-}
-
-template <typename Dec>
-__device__ void build_grid(uint2 *grid)
-{
-    if constexpr (NeedsGrid<Dec>::kEntries == 2048) {
-        for (int i = threadIdx.x; i < 2048; i += blockDim.x) {
-            const uint32_t e = d_iq1s_nib[i];
-            // nibble = value + 1  ->  signed byte value
-            const uint32_t lo = e & 0x0F0F0F0Fu, hi = (e >> 4) & 0x0F0F0F0Fu;
-            const uint32_t lo_v = ((lo | 0x80808080u) - 0x01010101u) ^ 0x80808080u;
-            const uint32_t hi_v = ((hi | 0x80808080u) - 0x01010101u) ^ 0x80808080u;
-            grid[i] = make_uint2(lo_v, hi_v);
-        }
-    } else if constexpr (NeedsGrid<Dec>::kEntries == 1024) {
-        for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
-            const uint32_t e = d_iq2s_nib[i];
-            // nibble = index into {8, 25, 43}: 8 + 17c + (c >> 1) per byte
-            const uint32_t lo = e & 0x0F0F0F0Fu, hi = (e >> 4) & 0x0F0F0F0Fu;
-            const uint32_t lo_v = lo * 17u + 0x08080808u + ((lo >> 1) & 0x01010101u);
-            const uint32_t hi_v = hi * 17u + 0x08080808u + ((hi >> 1) & 0x01010101u);
-            grid[i] = make_uint2(lo_v, hi_v);
-        }
-    }
-}
-
 // Issue the bulk copy of unit `unit` into stage `s`.  Returns the byte offset
 // of the unit's first row inside the stage.
 __device__ __forceinline__ void issue_unit(const GemmArgs &g, uint8_t *stage, uint64_t *bar, int unit)
@@ -116,7 +71,6 @@ template <int MT> struct MaxThreads { static constexpr int kValue = MT == 1 ? 38
 template <typename Dec, int MT, bool kDbg>
 __global__ void __launch_bounds__(MaxThreads<MT>::kValue) q8k_gemm_kernel(GemmArgs g)
 {
-    using Act = typename Dec::Act;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *stages = smem;
     float *red = reinterpret_cast<float *>(smem + static_cast<size_t>(g.stages) * g.stage_bytes);
@@ -188,7 +142,7 @@ __global__ void __launch_bounds__(MaxThreads<MT>::kValue) q8k_gemm_kernel(GemmAr
                                              static_cast<size_t>(my_col) * Dec::kBytes;
                         int w[MT], x[MT];
                         float v[MT];
-                        run_block<Dec, MT>(blk, a, w, x, v, grid);
+                        run_block<Dec, MT>(blk, RegActs<MT>{a}, w, x, v, grid);
 #pragma unroll
                         for (int t = 0; t < MT; ++t) {
                             red[(r * g.nb + my_col) * MT + t] = v[t];
@@ -380,8 +334,18 @@ __device__ float element_weight(int type, const uint8_t *b, int i)
 
 // One warp per (row, token).  Lanes take blocks lane, lane+32, ... and the
 // partials are reduced with shuffles (fixed order).
+// Address of block `blk` of row `row`: GGUF row-major, or the tiled layout
+// when tile_rows != 0.
+__device__ __forceinline__ const uint8_t *block_at(const uint8_t *w, uint64_t row, uint64_t blk, uint64_t nblocks,
+                                                   uint32_t tile_rows, int bb)
+{
+    if (!tile_rows) return w + (row * nblocks + blk) * bb;
+    const uint64_t t = row / tile_rows, r = row - t * tile_rows;
+    return w + ((t * nblocks + blk) * tile_rows + r) * bb;
+}
+
 __global__ void f32_gemm_kernel(float *out, const float *x, int batch, uint64_t width, const uint8_t *w,
-                                uint64_t rows, int type, int be, int bb)
+                                uint64_t rows, uint32_t tile_rows, int type, int be, int bb)
 {
     const uint64_t gw = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -389,11 +353,10 @@ __global__ void f32_gemm_kernel(float *out, const float *x, int batch, uint64_t 
     const uint64_t row = gw % rows;
     const int tok = static_cast<int>(gw / rows);
     const uint64_t nblocks = width / be;
-    const uint8_t *r = w + row * nblocks * bb;
     const float *xx = x + static_cast<uint64_t>(tok) * width;
     float total = 0.0f;
     for (uint64_t blk = lane; blk < nblocks; blk += 32) {
-        const uint8_t *b = r + blk * bb;
+        const uint8_t *b = block_at(w, row, blk, nblocks, tile_rows, bb);
         for (int i = 0; i < be; ++i) total = fmaf(element_weight(type, b, i), __ldg(xx + blk * be + i), total);
     }
 #pragma unroll
@@ -403,13 +366,13 @@ __global__ void f32_gemm_kernel(float *out, const float *x, int batch, uint64_t 
 
 // Element i of row `row`.  The upstream evaluates fma(w, 1, 0) against a
 // basis vector, which equals w for finite w except that -0 becomes +0.
-__global__ void row_f32_kernel(float *out, const uint8_t *w, uint64_t width, uint64_t row, int type, int be,
-                               int bb)
+__global__ void row_f32_kernel(float *out, const uint8_t *w, uint64_t width, uint32_t tile_rows, uint64_t row,
+                               int type, int be, int bb)
 {
     const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= width) return;
     const uint64_t nblocks = width / be;
-    const uint8_t *b = w + (row * nblocks + i / be) * bb;
+    const uint8_t *b = block_at(w, row, i / be, nblocks, tile_rows, bb);
     const float v = element_weight(type, b, static_cast<int>(i % be));
     out[i] = type == kF32 || type == kF16 || type == kBF16 ? v : __fadd_rn(v, 0.0f);
 }
@@ -435,8 +398,17 @@ static cudaError_t cached_occupancy(const void *kernel, int threads, size_t smem
             return cudaSuccess;
         }
     }
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
+    // Opt in to the device's full dynamic shared memory once per kernel, so a
+    // later (smaller) configuration never lowers the limit a cached one uses.
+    bool opted = false;
+    for (int i = 0; i < used; ++i) opted |= cache[i].kernel == kernel && cache[i].device == dev;
+    if (!opted) {
+        int optin = 0;
+        e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+        if (e != cudaSuccess) return e;
+    }
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, kernel, threads, smem);
     if (e != cudaSuccess) return e;
     if (used < 256) cache[used++] = Entry{kernel, dev, threads, smem, *per_sm};
@@ -540,20 +512,21 @@ cudaError_t launch_quantize_q8k(void *out, const float *in, uint64_t blocks, cud
 }
 
 cudaError_t launch_f32_gemm(float *out, const float *x, int batch, uint64_t width, const void *w, uint64_t rows,
-                            int type, int be, int bb, cudaStream_t s)
+                            uint32_t tile_rows, int type, int be, int bb, cudaStream_t s)
 {
     const uint64_t warps = rows * static_cast<uint64_t>(batch);
     if (warps == 0) return cudaSuccess;
     const unsigned grid = static_cast<unsigned>((warps * 32 + 255) / 256);
-    f32_gemm_kernel<<<grid, 256, 0, s>>>(out, x, batch, width, static_cast<const uint8_t *>(w), rows, type, be, bb);
+    f32_gemm_kernel<<<grid, 256, 0, s>>>(out, x, batch, width, static_cast<const uint8_t *>(w), rows, tile_rows, type,
+                                         be, bb);
     return cudaGetLastError();
 }
 
-cudaError_t launch_row_f32(float *out, const void *w, uint64_t width, uint64_t row, int type, int be, int bb,
-                           cudaStream_t s)
+cudaError_t launch_row_f32(float *out, const void *w, uint64_t width, uint32_t tile_rows, uint64_t row, int type,
+                           int be, int bb, cudaStream_t s)
 {
     const unsigned grid = static_cast<unsigned>((width + 255) / 256);
-    row_f32_kernel<<<grid, 256, 0, s>>>(out, static_cast<const uint8_t *>(w), width, row, type, be, bb);
+    row_f32_kernel<<<grid, 256, 0, s>>>(out, static_cast<const uint8_t *>(w), width, tile_rows, row, type, be, bb);
     return cudaGetLastError();
 }
 

@@ -1,0 +1,622 @@
+// q38_stream.cu - weight-streaming GEMV/GEMM over a tiled device repack.
+//
+// Layout (Q38CU_LAYOUT_TILED).  Rows are cut into tiles of T rows (T a
+// multiple of 8, chosen from the row count and the SM count); the blocks are
+// stored tile by tile, column by column: superblock (row r, column b) sits at
+// (((r / T) * nb + b) * T + r % T) * B.  Rows are padded with zero blocks to a
+// whole number of tiles.  A "unit" (one column of one tile, T*B bytes) is a
+// multiple of 16 bytes, and consecutive units of a tile are adjacent, so any
+// run of units moves with one 1-D TMA bulk copy.  The bytes are the GGUF
+// bytes, only permuted (the upstream engine's IQ1_S repack,
+// src/qwen38/qwen38_quant.c:1255-1377, is the precedent for a load-time view).
+//
+// Kernel.  Units in memory order are split into G contiguous ranges, one per
+// CTA; when the tiles fit on the GPU at once each CTA owns exactly one tile.
+// Inside a CTA:
+//   * warp (consumers / 32) is the producer: one lane cuts the CTA's range into
+//     chunks of up to C units that do not cross a tile, and issues each chunk
+//     as one cp.async.bulk into the ring of its consumer group (chunk q goes to
+//     group q % J; each group's ring has S stages and one in-order consumer);
+//   * J consumer groups, each a whole number of warps covering the T rows:
+//     thread rt of a group owns row rt of the tile and, for every column of
+//     the group's chunks, decodes its row's superblock against that Q8_K
+//     activation column (staged once in shared memory; all threads read the
+//     same column - a broadcast).  The superblock's integer sums form inside
+//     one thread; its float contribution is added to the thread's row sum.
+// At the end of a tile (or of the CTA's range) the groups' row sums are added
+// in group order; a tile shared between CTAs is finished by the last CTA to
+// deposit its sums (per-tile counter, deposits added in CTA order).  T, J, C
+// and G depend only on the tensor's shape (the ring depth S does not change
+// the arithmetic), so a row's float sum is associated the same way for any
+// batch size: a batched row is bit-identical
+// to the single-token GEMV (the upstream property,
+// tests/unit/test_qwen38_quant.c:637-684).  Kernels launch with programmatic
+// dependent launch: weight prefetch starts while the previous kernel of the
+// stream finishes; activations, deposits, counters and outputs are touched only
+// after griddepcontrol.wait.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <mutex>
+
+#include "../../include/q38cuda.h"
+#include "q38_device.cuh"
+#include "q38_grid.cuh"
+#include "q38_internal.h"
+#include "q38_types.cuh"
+
+namespace q38 {
+
+__device__ int g_stream_status;  // status word of this file's kernels
+
+constexpr int kStreamMaxStages = 32;            // stages of all groups together
+constexpr size_t kChunkBudget = 112 * 1024;     // one ring pass of all groups (sets the chunk)
+constexpr size_t kActBudget = 64 * 1024;        // shared memory for activation columns
+constexpr int kMaxConsumers = 256;              // CTA bound for 8 tokens: 288 threads
+constexpr size_t kOverlapSmem = 112 * 1024;     // short launches: two CTAs fit an SM
+constexpr size_t kLongLaunchBytes = 2u << 20;   // per-CTA bytes above which a launch is long
+
+struct StreamArgs {
+    const uint8_t *weights;
+    int block_bytes;   // B
+    int rows;          // N
+    int nb;
+    int tile_rows;     // T
+    int tiles;
+    int units;         // tiles * nb
+    int groups;        // J
+    int stages;        // S, per group
+    int chunk;         // C, units per copy
+    uint32_t stage_bytes;
+    const Q8KBlock *act;  // [tokens][nb]
+    int tokens;
+    float *out;           // out[tok * rows + row]
+    float *partials;
+    int *counters;
+    int max_slots;
+    int32_t *dbg_w;       // optional [tokens][rows][nb]
+    int32_t *dbg_x;
+};
+
+__host__ __device__ __forceinline__ int cta_of_unit(long long u, long long units, int grid)
+{
+    // inverse of first_unit(c) = floor(units * c / grid)
+    return static_cast<int>(((u + 1) * grid - 1) / units);
+}
+
+__device__ __forceinline__ void consumer_barrier(int consumers)
+{
+    asm volatile("bar.sync 1, %0;" ::"r"(consumers) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Chunk walker shared by the producer and the consumers: the CTA's range of
+// units [u0, u1) cut at tile ends and every C units.
+struct ChunkWalk {
+    int u, u_end, nb, chunk;
+    int t, b;  // tile and column of `u`
+    __device__ void init(int u0, int u1, int nb_, int chunk_)
+    {
+        u = u0;
+        u_end = u1;
+        nb = nb_;
+        chunk = chunk_;
+        t = u0 / nb_;
+        b = u0 - t * nb_;
+    }
+    __device__ bool done() const { return u >= u_end; }
+    __device__ int len() const { return min(chunk, min(nb - b, u_end - u)); }
+    __device__ void next(int n)
+    {
+        u += n;
+        b += n;
+        if (b == nb) { b = 0; ++t; }
+    }
+};
+
+// CTA size bound: 416 threads (157 registers) for up to 2 tokens, 288 threads
+// (227 registers) for 4 and 8.
+template <int MT> struct StreamThreads { static constexpr int kValue = MT <= 2 ? 416 : 288; };
+
+template <typename Dec, int MT, bool kDbg>
+__device__ __forceinline__ void decode_column(const StreamArgs &g, const uint8_t *blk, const Act *acts, int b,
+                                              int row, float (&acc)[MT], const uint2 *grid)
+{
+    SmemActs<MT> a;
+#pragma unroll
+    for (int tok = 0; tok < MT; ++tok) a.p[tok] = acts + tok * g.nb + b;
+    int w[MT], x[MT];
+    float val[MT];
+    run_block<Dec, MT>(blk, a, w, x, val, grid);
+#pragma unroll
+    for (int tok = 0; tok < MT; ++tok) acc[tok] += val[tok];
+    if constexpr (kDbg) {
+        if (row < g.rows) {
+#pragma unroll
+            for (int tok = 0; tok < MT; ++tok) {
+                if (tok < g.tokens) {
+                    const size_t o = (static_cast<size_t>(tok) * g.rows + row) * g.nb + b;
+                    g.dbg_w[o] = w[tok];
+                    g.dbg_x[o] = x[tok];
+                }
+            }
+        }
+    }
+}
+
+template <typename Dec, int MT, bool kDbg>
+__global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kernel(StreamArgs g)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int consumers = static_cast<int>(blockDim.x) - 32;
+    const int n_stages = g.groups * g.stages;
+    uint8_t *stage_mem = smem;
+    Act *acts = reinterpret_cast<Act *>(smem + static_cast<size_t>(n_stages) * g.stage_bytes);
+    uint2 *grid = reinterpret_cast<uint2 *>(acts + MT * g.nb);
+    float *red = reinterpret_cast<float *>(grid + NeedsGrid<Dec>::kEntries);  // [groups][MT][row threads]
+    uint64_t *full = reinterpret_cast<uint64_t *>(red + consumers * MT);
+    uint64_t *empty = full + kStreamMaxStages;
+    volatile int *issued = reinterpret_cast<volatile int *>(empty + kStreamMaxStages);
+    volatile int *last_flag = issued + 1;
+
+    const int tid = threadIdx.x;
+    const int G = gridDim.x, c = blockIdx.x;
+    const int u0 = static_cast<int>(static_cast<long long>(g.units) * c / G);
+    const int u1 = static_cast<int>(static_cast<long long>(g.units) * (c + 1) / G);
+    const int row_threads = consumers / g.groups;
+
+    if (tid == 0) {
+        for (int s = 0; s < n_stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], row_threads / 32);  // the owning group's warps free a stage
+        }
+        *issued = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    // Let the next kernel in the stream start its prologue (weight prefetch)
+    // while this grid drains; it waits for our completion before it touches
+    // anything we write.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    if (tid >= consumers) {
+        // ---------------- producer warp ----------------
+        if (tid == consumers) {
+            ChunkWalk w;
+            w.init(u0, u1, g.nb, g.chunk);
+            int q = 0, grp = 0, slot = 0, wrap = 0;
+            const size_t unit_bytes = static_cast<size_t>(g.tile_rows) * g.block_bytes;
+            for (; !w.done(); ++q) {
+                const int n = w.len();
+                const int s = grp * g.stages + slot;
+                if (wrap > 0) {
+                    if (!mbar_wait_bounded(&empty[s], static_cast<uint32_t>(wrap - 1) & 1u, &g_stream_status)) break;
+                    fence_proxy_async_shared();
+                }
+                const uint32_t bytes = static_cast<uint32_t>(n * unit_bytes);
+                mbar_arrive_expect_tx(&full[s], bytes);
+                bulk_copy_g2s(stage_mem + static_cast<size_t>(s) * g.stage_bytes,
+                              g.weights + static_cast<size_t>(w.u) * unit_bytes, bytes, &full[s]);
+                *issued = q + 1;
+                w.next(n);
+                if (++grp == g.groups) {
+                    grp = 0;
+                    if (++slot == g.stages) { slot = 0; ++wrap; }
+                }
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumer warps ----------------
+    const int lane = tid & 31;
+    if constexpr (NeedsGrid<Dec>::kEntries > 0) {
+        // Codebook expansion (constant tables only) may precede the grid dependency.
+        for (int i = tid; i < NeedsGrid<Dec>::kEntries; i += consumers) {
+            if constexpr (NeedsGrid<Dec>::kEntries == 2048) {
+                const uint32_t e = d_iq1s_nib[i];
+                const uint32_t lo = e & 0x0F0F0F0Fu, hi = (e >> 4) & 0x0F0F0F0Fu;
+                grid[i] = make_uint2(((lo | 0x80808080u) - 0x01010101u) ^ 0x80808080u,
+                                     ((hi | 0x80808080u) - 0x01010101u) ^ 0x80808080u);
+            } else {
+                const uint32_t e = d_iq2s_nib[i];
+                const uint32_t lo = e & 0x0F0F0F0Fu, hi = (e >> 4) & 0x0F0F0F0Fu;
+                grid[i] = make_uint2(lo * 17u + 0x08080808u + ((lo >> 1) & 0x01010101u),
+                                     hi * 17u + 0x08080808u + ((hi >> 1) & 0x01010101u));
+            }
+        }
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    // Activation columns -> shared memory in one round trip: quants, raw bsums
+    // (into aux[8..15]) and scale; tokens beyond g.tokens are zero.  The
+    // per-format sums are then derived from shared memory only.
+    const int slots = MT * g.nb;
+    for (int i = tid; i < slots * 72; i += consumers) {
+        const int slot = i / 72, w = i - slot * 72;
+        const int tok = slot / g.nb, col = slot - tok * g.nb;
+        uint32_t v = 0u;
+        if (tok < g.tokens)
+            v = __ldg(reinterpret_cast<const uint32_t *>(g.act + static_cast<size_t>(tok) * g.nb + col) + 1 + w);
+        if (w < 64) acts[slot].q[w] = v;          // words 1..64: quants
+        else acts[slot].aux[8 + (w - 64)] = v;    // words 65..72: bsums
+    }
+    for (int slot = tid; slot < slots; slot += consumers) {
+        const int tok = slot / g.nb, col = slot - tok * g.nb;
+        acts[slot].xs = tok < g.tokens ? __ldg(&g.act[static_cast<size_t>(tok) * g.nb + col].scale) : 0.0f;
+    }
+    consumer_barrier(consumers);
+    for (int slot = tid; slot < slots; slot += consumers) Dec::aux_from_raw(acts[slot]);
+    consumer_barrier(consumers);
+
+    const int grp = tid / row_threads, rt = tid - grp * row_threads;
+    const bool mine_row = rt < g.tile_rows;
+    const size_t unit_bytes = static_cast<size_t>(g.tile_rows) * g.block_bytes;
+    bool failed = false;
+    int slot = 0, wrap = 0;  // this group's ring position
+    ChunkWalk w;
+    w.init(u0, u1, g.nb, g.chunk);
+    int q = 0;  // CTA chunk index
+    while (!w.done()) {
+        // One tile segment: the chunks of tile w.t inside [u0, u1).
+        const int t = w.t;
+        const bool seg_whole = w.b == 0 && (t + 1) * g.nb <= u1;
+        const int row = t * g.tile_rows + rt;
+        float acc[MT];
+#pragma unroll
+        for (int tok = 0; tok < MT; ++tok) acc[tok] = 0.0f;
+        do {
+            const int n = w.len();
+            if (q % g.groups == grp) {
+                const int s = grp * g.stages + slot;
+                if (!failed) failed = !mbar_wait_bounded(&full[s], static_cast<uint32_t>(wrap) & 1u, &g_stream_status);
+                if (!failed && mine_row) {
+                    const uint8_t *base = stage_mem + static_cast<size_t>(s) * g.stage_bytes +
+                                          static_cast<size_t>(rt) * g.block_bytes;
+                    int k = 0;
+                    if constexpr (MT <= 2 && !kDbg) {
+                        // two columns in flight: independent decode chains,
+                        // the earlier column still added first
+                        for (; k + 1 < n; k += 2) {
+                            float a0[MT], a1[MT];
+#pragma unroll
+                            for (int tok = 0; tok < MT; ++tok) a0[tok] = a1[tok] = 0.0f;
+                            decode_column<Dec, MT, kDbg>(g, base + k * unit_bytes, acts, w.b + k, row, a0, grid);
+                            decode_column<Dec, MT, kDbg>(g, base + (k + 1) * unit_bytes, acts, w.b + k + 1, row, a1,
+                                                         grid);
+#pragma unroll
+                            for (int tok = 0; tok < MT; ++tok) {
+                                acc[tok] += a0[tok];
+                                acc[tok] += a1[tok];
+                            }
+                        }
+                    }
+                    for (; k < n; ++k) {
+                        float a0[MT];
+#pragma unroll
+                        for (int tok = 0; tok < MT; ++tok) a0[tok] = 0.0f;
+                        decode_column<Dec, MT, kDbg>(g, base + k * unit_bytes, acts, w.b + k, row, a0, grid);
+#pragma unroll
+                        for (int tok = 0; tok < MT; ++tok) acc[tok] += a0[tok];
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+                if (++slot == g.stages) { slot = 0; ++wrap; }
+            }
+            ++q;
+            w.next(n);
+        } while (!w.done() && w.t == t);
+
+        // Combine the groups' row sums in group order.
+#pragma unroll
+        for (int tok = 0; tok < MT; ++tok) red[(grp * MT + tok) * row_threads + rt] = acc[tok];
+        consumer_barrier(consumers);
+        float total[MT];
+#pragma unroll
+        for (int tok = 0; tok < MT; ++tok) {
+            float sum = 0.0f;
+            if (grp == 0)
+                for (int k = 0; k < g.groups; ++k) sum += red[(k * MT + tok) * row_threads + rt];
+            total[tok] = sum;
+        }
+        if (seg_whole) {
+            if (grp == 0 && !failed && mine_row && row < g.rows) {
+#pragma unroll
+                for (int tok = 0; tok < MT; ++tok)
+                    if (tok < g.tokens) g.out[static_cast<size_t>(tok) * g.rows + row] = total[tok];
+            }
+        } else {
+            // The tile is shared with other CTAs: deposit this segment's sums;
+            // the last CTA to arrive adds all deposits in CTA order.
+            const long long tu = static_cast<long long>(t) * g.nb;
+            const int cf = cta_of_unit(tu, g.units, G);
+            const int cl = cta_of_unit(tu + g.nb - 1, g.units, G);
+            const int n_dep = cl - cf + 1, dep = c - cf;
+            if (grp == 0 && mine_row) {
+                float *mine = g.partials + (static_cast<size_t>(t) * g.max_slots + dep) * MT * g.tile_rows;
+#pragma unroll
+                for (int tok = 0; tok < MT; ++tok) __stcg(mine + tok * g.tile_rows + rt, total[tok]);
+            }
+            __threadfence();
+            consumer_barrier(consumers);
+            if (tid == 0) *last_flag = !failed && atomicAdd(&g.counters[t], 1) == n_dep - 1;
+            consumer_barrier(consumers);
+            if (*last_flag && grp == 0 && mine_row) {
+                __threadfence();
+                const float *base = g.partials + static_cast<size_t>(t) * g.max_slots * MT * g.tile_rows;
+#pragma unroll
+                for (int tok = 0; tok < MT; ++tok) {
+                    if (tok >= g.tokens) break;
+                    float sum = 0.0f;
+                    for (int k = 0; k < n_dep; ++k)
+                        sum += __ldcg(base + (static_cast<size_t>(k) * MT + tok) * g.tile_rows + rt);
+                    if (row < g.rows) g.out[static_cast<size_t>(tok) * g.rows + row] = sum;
+                }
+            }
+            if (*last_flag && tid == 0) atomicExch(&g.counters[t], 0);
+        }
+        consumer_barrier(consumers);  // `red` and the flag are reused by the next segment
+    }
+    if (failed && tid == 0) {
+        // Drain the bulk copies still in flight before shared memory goes away:
+        // the last copy issued into each stage completes after all earlier ones,
+        // and the last (groups * stages) chunks cover every stage's last copy.
+        const int n_issued = *issued;
+        const int from = n_issued - n_stages;
+        for (int j = from < 0 ? 0 : from; j < n_issued; ++j) {
+            const int k = j / g.groups;
+            const int st = (j % g.groups) * g.stages + k % g.stages;
+            mbar_wait_bounded(&full[st], static_cast<uint32_t>(k / g.stages) & 1u, nullptr);
+        }
+    }
+}
+
+// GGUF row-major -> tiled layout (padding rows stay zero).
+__global__ void repack_tiled_kernel(uint8_t *dst, const uint8_t *src, uint64_t rows, uint64_t nb, uint32_t tile_rows,
+                                    uint32_t block_bytes)
+{
+    const uint64_t total = rows * nb * block_bytes;
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint64_t blk = i / block_bytes, k = i - blk * block_bytes;
+        const uint64_t r = blk / nb, b = blk - r * nb;
+        const uint64_t t = r / tile_rows, rr = r - t * tile_rows;
+        dst[((t * nb + b) * tile_rows + rr) * block_bytes + k] = src[i];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+namespace {
+
+// Tuning overrides read from the environment (for sweeps; unset = the
+// built-in plan).
+int env_knob(const char *name, int fallback)
+{
+    const char *v = std::getenv(name);
+    return v && *v ? std::atoi(v) : fallback;
+}
+
+template <typename Dec>
+size_t stream_smem(const StreamPlan &p)
+{
+    return static_cast<size_t>(p.groups) * p.stages * p.stage_bytes + static_cast<size_t>(p.mt) * p.nb * sizeof(Act) +
+           static_cast<size_t>(NeedsGrid<Dec>::kEntries) * 8 + static_cast<size_t>(p.threads - 32) * p.mt * 4 +
+           2 * kStreamMaxStages * 8 + 16;
+}
+
+template <typename Dec, int MT, bool kDbg>
+const void *stream_kernel_ptr()
+{
+    return reinterpret_cast<const void *>(stream_gemm_kernel<Dec, MT, kDbg>);
+}
+
+template <typename Dec>
+const void *select_kernel(int mt, bool dbg)
+{
+    switch (mt) {
+    case 1: return dbg ? stream_kernel_ptr<Dec, 1, true>() : stream_kernel_ptr<Dec, 1, false>();
+    case 2: return dbg ? stream_kernel_ptr<Dec, 2, true>() : stream_kernel_ptr<Dec, 2, false>();
+    case 4: return dbg ? stream_kernel_ptr<Dec, 4, true>() : stream_kernel_ptr<Dec, 4, false>();
+    default: return dbg ? stream_kernel_ptr<Dec, 8, true>() : stream_kernel_ptr<Dec, 8, false>();
+    }
+}
+
+// Opt a kernel in to the device's full dynamic shared memory, once per device.
+cudaError_t opt_in(const void *kernel)
+{
+    struct Entry { const void *kernel; int device; };
+    static Entry done[256];
+    static int used = 0;
+    static std::mutex lock;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> guard(lock);
+    for (int i = 0; i < used; ++i)
+        if (done[i].kernel == kernel && done[i].device == dev) return cudaSuccess;
+    int optin = 0;
+    e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+    if (e == cudaSuccess && used < 256) done[used++] = Entry{kernel, dev};
+    return e;
+}
+
+template <typename Dec>
+cudaError_t plan_t(int rows, int width, int tile_rows, int tokens, StreamPlan *p)
+{
+    StreamPlan q{};
+    q.rows = rows;
+    q.nb = width / 256;
+    q.block_bytes = Dec::kBytes;
+    q.tile_rows = tile_rows;
+    q.tiles = (rows + tile_rows - 1) / tile_rows;
+    q.rows_pad = q.tiles * tile_rows;
+    q.units = static_cast<long long>(q.tiles) * q.nb;
+    if (q.units >= (1LL << 31)) return cudaErrorInvalidValue;
+    // tokens per launch: the activation columns of a launch fit kActBudget
+    int tg = 8;
+    while (tg > 1 && static_cast<size_t>(tg) * q.nb * sizeof(Act) > kActBudget) tg >>= 1;
+    q.token_group = std::min(tg, tokens);
+    q.mt = 1;
+    while (q.mt < q.token_group) q.mt <<= 1;
+    // Shape-only structure (identical for every token count):
+    const int sms = device_sm_count();
+    const int row_threads = (tile_rows + 31) / 32 * 32;
+    q.groups = std::max(1, std::min(q.nb, kMaxConsumers / row_threads));
+    const int env_groups = env_knob("Q38CU_STREAM_GROUPS", 0);
+    if (env_groups > 0) q.groups = std::max(1, std::min({q.nb, env_groups, kMaxConsumers / row_threads}));
+    const size_t unit_bytes = static_cast<size_t>(tile_rows) * q.block_bytes;
+    // Chunk (units per bulk copy; decides which columns each group sums, so
+    // shape-only): the groups' stages of one ring pass share kChunkBudget.
+    q.chunk = static_cast<int>(std::max<size_t>(1, kChunkBudget / (unit_bytes * q.groups)));
+    const int env_chunk = env_knob("Q38CU_STREAM_CHUNK", 0);
+    if (env_chunk > 0) q.chunk = env_chunk;
+    q.chunk = std::max(1, std::min(q.chunk, q.nb));
+    q.stage_bytes = static_cast<uint32_t>((q.chunk * unit_bytes + 16 + 15) / 16 * 16);  // +16: decoder over-read
+    q.threads = q.groups * row_threads + 32;
+    q.grid = q.tiles <= sms ? q.tiles : sms;
+    const int env_grid = env_knob("Q38CU_STREAM_GRID", 0);
+    if (env_grid > 0) q.grid = static_cast<int>(std::min<long long>(q.units, env_grid));
+    // Ring depth (no effect on the arithmetic).  A short launch keeps its CTA
+    // under half of an SM's shared memory, so the next launch of the stream
+    // (programmatic dependent launch) can be resident beside it and prefetch
+    // its weights while this one finishes; a long launch takes what it can.
+    int optin = 0, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (optin <= 0) optin = 227 * 1024;
+    const size_t cta_bytes = static_cast<size_t>((q.units + q.grid - 1) / q.grid) * unit_bytes;
+    size_t budget = static_cast<size_t>(optin);
+    const int env_budget = env_knob("Q38CU_STREAM_SMEM_KB", 0);
+    if (env_budget > 0) budget = std::min(budget, static_cast<size_t>(env_budget) * 1024);
+    else if (cta_bytes < kLongLaunchBytes) budget = std::min(budget, kOverlapSmem);
+    StreamPlan no_stages = q;
+    no_stages.stages = 0;
+    const size_t fixed = stream_smem<Dec>(no_stages);
+    const size_t ring_pass = static_cast<size_t>(q.groups) * q.stage_bytes;
+    if (fixed + 2 * ring_pass > budget && env_budget <= 0) budget = static_cast<size_t>(optin);  // too tight to share
+    if (fixed >= budget) return cudaErrorInvalidConfiguration;
+    q.stages = static_cast<int>(std::min<size_t>(kStreamMaxStages / q.groups, (budget - fixed) / ring_pass));
+    const int env_stages = env_knob("Q38CU_STREAM_STAGES", 0);
+    if (env_stages > 0) q.stages = std::min(q.stages, env_stages);
+    if (q.stages < 1) return cudaErrorInvalidConfiguration;
+    // deposits per shared tile
+    int max_slots = 1;
+    for (int t = 0; t < q.tiles; ++t) {
+        const long long tu = static_cast<long long>(t) * q.nb;
+        const int n = cta_of_unit(tu + q.nb - 1, q.units, q.grid) - cta_of_unit(tu, q.units, q.grid) + 1;
+        max_slots = std::max(max_slots, n);
+    }
+    q.max_slots = max_slots;
+    // scratch = [tile counters, fixed position for the tensor][deposits]
+    q.counter_bytes = (static_cast<uint64_t>(q.tiles) * sizeof(int) + 255) / 256 * 256;
+    q.scratch_bytes = q.counter_bytes + static_cast<uint64_t>(q.tiles) * max_slots * q.mt * tile_rows * sizeof(float);
+    *p = q;
+    return cudaSuccess;
+}
+
+template <typename Dec>
+cudaError_t launch_t(const StreamPlan &p, const StreamLaunch &l, cudaStream_t stream)
+{
+    StreamArgs g;
+    g.weights = static_cast<const uint8_t *>(l.weights);
+    g.block_bytes = p.block_bytes;
+    g.rows = p.rows;
+    g.nb = p.nb;
+    g.tile_rows = p.tile_rows;
+    g.tiles = p.tiles;
+    g.units = static_cast<int>(p.units);
+    g.groups = p.groups;
+    g.stages = p.stages;
+    g.chunk = p.chunk;
+    g.stage_bytes = p.stage_bytes;
+    g.act = static_cast<const Q8KBlock *>(l.act);
+    g.tokens = l.tokens;
+    g.out = l.out;
+    g.counters = static_cast<int *>(l.scratch);
+    g.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(l.scratch) + p.counter_bytes);
+    g.max_slots = p.max_slots;
+    g.dbg_w = l.dbg_w;
+    g.dbg_x = l.dbg_x;
+    const void *kernel = select_kernel<Dec>(p.mt, l.dbg_w != nullptr);
+    cudaError_t e = opt_in(kernel);
+    if (e != cudaSuccess) return e;
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid);
+    cfg.blockDim = dim3(p.threads);
+    cfg.dynamicSmemBytes = stream_smem<Dec>(p);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = env_knob("Q38CU_NO_PDL", 0) ? 0 : 1;
+    void *args[] = {&g};
+    return cudaLaunchKernelExC(&cfg, kernel, args);
+}
+
+}  // namespace
+
+int stream_tile_rows(int rows)
+{
+    const int env_tile = env_knob("Q38CU_STREAM_TILE", 0);
+    if (env_tile > 0) return std::max(8, std::min(256, env_tile / 8 * 8));
+    // the smallest multiple of 8 that gives at most one tile per SM
+    const int sms = device_sm_count();
+    const int per_sm = (rows + sms - 1) / sms;
+    return std::max(8, std::min(256, (per_sm + 7) / 8 * 8));
+}
+
+cudaError_t stream_plan(int type, int rows, int width, int tile_rows, int tokens, StreamPlan *p)
+{
+    switch (type) {
+    case kQ4_K: return plan_t<DecQ4K>(rows, width, tile_rows, tokens, p);
+    case kQ6_K: return plan_t<DecQ6K>(rows, width, tile_rows, tokens, p);
+    case kIQ2_S: return plan_t<DecIQ2S>(rows, width, tile_rows, tokens, p);
+    case kIQ1_S: return plan_t<DecIQ1S>(rows, width, tile_rows, tokens, p);
+    case kIQ1_M: return plan_t<DecIQ1M>(rows, width, tile_rows, tokens, p);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_stream_gemm(int type, const StreamPlan &p, const StreamLaunch &l, cudaStream_t s)
+{
+    switch (type) {
+    case kQ4_K: return launch_t<DecQ4K>(p, l, s);
+    case kQ6_K: return launch_t<DecQ6K>(p, l, s);
+    case kIQ2_S: return launch_t<DecIQ2S>(p, l, s);
+    case kIQ1_S: return launch_t<DecIQ1S>(p, l, s);
+    case kIQ1_M: return launch_t<DecIQ1M>(p, l, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t read_and_clear_stream_status(int *status)
+{
+    cudaError_t e = cudaMemcpyFromSymbol(status, g_stream_status, sizeof(int));
+    if (e != cudaSuccess) return e;
+    const int zero = 0;
+    return cudaMemcpyToSymbol(g_stream_status, &zero, sizeof(int));
+}
+
+cudaError_t launch_repack_tiled(void *dst, const void *src, uint64_t rows, uint64_t nb, uint32_t tile_rows,
+                                uint32_t block_bytes, cudaStream_t s)
+{
+    const uint64_t total = rows * nb * block_bytes;
+    if (!total) return cudaSuccess;
+    const unsigned grid = static_cast<unsigned>(std::min<uint64_t>((total + 255) / 256, 65535ull * 16));
+    repack_tiled_kernel<<<grid, 256, 0, s>>>(static_cast<uint8_t *>(dst), static_cast<const uint8_t *>(src), rows, nb,
+                                             tile_rows, block_bytes);
+    return cudaGetLastError();
+}
+
+}  // namespace q38

@@ -26,13 +26,19 @@ struct Q8KBlock {
     int16_t sums[16];
 };
 
-// Activation block in registers: 64 words of int8 quants plus the block scale.
-struct ActBase {
+// Activation block: 64 words of int8 quants, up to 16 words of per-format
+// precomputed sums ("aux", see each decoder's load) and the block scale.  The
+// same layout is used in registers (one block per thread) and in shared memory
+// (one block per column, read by every thread of a CTA).
+struct Act {
     uint32_t q[64];
+    uint32_t aux[16];
     float xs;
+    uint32_t pad[3];
 };
+static_assert(sizeof(Act) == 336, "shared-memory activation slot is 336 bytes");
 
-__device__ __forceinline__ void load_act_base(ActBase &a, const Q8KBlock *g)
+__device__ __forceinline__ void load_act_base(Act &a, const Q8KBlock *g)
 {
     const uint32_t *w = reinterpret_cast<const uint32_t *>(g->quants);
 #pragma unroll
@@ -40,15 +46,51 @@ __device__ __forceinline__ void load_act_base(ActBase &a, const Q8KBlock *g)
     a.xs = __ldg(&g->scale);
 }
 
-__device__ __forceinline__ void zero_act_base(ActBase &a)
+__device__ __forceinline__ void zero_act(Act &a)
 {
 #pragma unroll
     for (int i = 0; i < 64; ++i) a.q[i] = 0u;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) a.aux[i] = 0u;
     a.xs = 0.0f;
 }
 
+// Accessors over MT activation blocks: registers (RegActs) or shared memory
+// (SmemActs, one pointer per token).  Indices are compile-time constants.
+template <int MT>
+struct RegActs {
+    const Act (&a)[MT];
+    __device__ __forceinline__ uint4 q4(int t, int j) const
+    {
+        return make_uint4(a[t].q[4 * j], a[t].q[4 * j + 1], a[t].q[4 * j + 2], a[t].q[4 * j + 3]);
+    }
+    __device__ __forceinline__ uint4 aux4(int t, int j) const
+    {
+        return make_uint4(a[t].aux[4 * j], a[t].aux[4 * j + 1], a[t].aux[4 * j + 2], a[t].aux[4 * j + 3]);
+    }
+    __device__ __forceinline__ uint32_t q(int t, int i) const { return a[t].q[i]; }
+    __device__ __forceinline__ uint32_t aux(int t, int i) const { return a[t].aux[i]; }
+    __device__ __forceinline__ float xs(int t) const { return a[t].xs; }
+};
+
+template <int MT>
+struct SmemActs {
+    const Act *p[MT];  // 16-byte aligned slots in shared memory
+    __device__ __forceinline__ uint4 q4(int t, int j) const { return reinterpret_cast<const uint4 *>(p[t]->q)[j]; }
+    __device__ __forceinline__ uint4 aux4(int t, int j) const
+    {
+        return reinterpret_cast<const uint4 *>(p[t]->aux)[j];
+    }
+    __device__ __forceinline__ uint32_t q(int t, int i) const { return p[t]->q[i]; }
+    __device__ __forceinline__ uint32_t aux(int t, int i) const { return p[t]->aux[i]; }
+    __device__ __forceinline__ float xs(int t) const { return p[t]->xs; }
+};
+
 // Sixteen int16 bsums of a Q8_K block.
 __device__ __forceinline__ int bsum(const Q8KBlock *g, int k) { return __ldg(&g->sums[k]); }
+
+__device__ __forceinline__ int lo16(uint32_t p) { return static_cast<int>(static_cast<int16_t>(p & 0xFFFFu)); }
+__device__ __forceinline__ int hi16(uint32_t p) { return static_cast<int>(static_cast<int16_t>(p >> 16)); }
 
 __device__ __forceinline__ uint32_t pack16(int lo, int hi)
 {
@@ -59,30 +101,30 @@ __device__ __forceinline__ uint32_t pack16(int lo, int hi)
 // Q4_K (144 B: fp16 d, fp16 dmin, 12 B packed 6-bit scales/mins, 128 B quants)
 // qwen38_quant.c:1546-1634 (integer path), :131-143 (scale unpack).
 // ===========================================================================
-struct ActQ4K : ActBase {
-    uint32_t pm[4];  // int16 pairs: bsum[2j] + bsum[2j+1] for sub-blocks j = 0..7
-};
-
 struct DecQ4K {
     static constexpr int kBytes = 144;
     static constexpr int kAlign = 16;
-    using Act = ActQ4K;
-    __device__ static void load(Act &a, const Q8KBlock *g)
+    // aux[j] = int16 pair (bsum[4j] + bsum[4j+1], bsum[4j+2] + bsum[4j+3]): the
+    // activation sums of sub-blocks 2j and 2j+1, weighted by the 6-bit mins.
+    __device__ static void aux(Act &a, const Q8KBlock *g)
     {
-        load_act_base(a, g);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-            a.pm[j] = pack16(bsum(g, 4 * j) + bsum(g, 4 * j + 1), bsum(g, 4 * j + 2) + bsum(g, 4 * j + 3));
+            a.aux[j] = pack16(bsum(g, 4 * j) + bsum(g, 4 * j + 1), bsum(g, 4 * j + 2) + bsum(g, 4 * j + 3));
     }
-    __device__ static void zero(Act &a)
+    // Same, from the raw bsums staged in aux[8..15] (int16 pairs).
+    __device__ static void aux_from_raw(Act &a)
     {
-        zero_act_base(a);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) a.pm[j] = 0u;
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t p0 = a.aux[8 + 2 * j], p1 = a.aux[9 + 2 * j];
+            a.aux[j] = pack16(lo16(p0) + hi16(p0), lo16(p1) + hi16(p1));
+        }
     }
-    template <int MT>
-    __device__ static void block(const uint8_t *blk, const Act (&a)[MT], int (&w)[MT], int (&x)[MT],
-                                 float (&v)[MT])
+    __device__ static void load(Act &a, const Q8KBlock *g) { load_act_base(a, g); aux(a, g); }
+    __device__ static void zero(Act &a) { zero_act(a); }
+    template <int MT, class A>
+    __device__ static void block(const uint8_t *blk, const A &a, int (&w)[MT], int (&x)[MT], float (&v)[MT])
     {
         const uint4 *p = reinterpret_cast<const uint4 *>(blk);
         const uint4 h = p[0];
@@ -103,15 +145,22 @@ struct DecQ4K {
             const int sc1 = static_cast<int>(byte_of(scw, (2 * c + 1) & 3));
 #pragma unroll
             for (int t = 0; t < MT; ++t) {
-                int dl = 0, dh = 0;
+                const uint4 x0 = a.q4(t, 4 * c), x1 = a.q4(t, 4 * c + 1);
+                const uint4 x2 = a.q4(t, 4 * c + 2), x3 = a.q4(t, 4 * c + 3);
+                const uint32_t xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                const uint32_t xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+                // two independent chains per half for instruction-level parallelism
+                int dl0 = 0, dl1 = 0, dh0 = 0, dh1 = 0;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    dl = dp4a_ss(q[i] & 0x0F0F0F0Fu, a[t].q[c * 16 + i], dl);
+                for (int i = 0; i < 8; i += 2) {
+                    dl0 = dp4a_ss(q[i] & 0x0F0F0F0Fu, xl[i], dl0);
+                    dl1 = dp4a_ss(q[i + 1] & 0x0F0F0F0Fu, xl[i + 1], dl1);
                     // high nibbles kept in place: unsigned bytes 16*q
-                    dh = dp4a_us(q[i] & 0xF0F0F0F0u, a[t].q[c * 16 + 8 + i], dh);
+                    dh0 = dp4a_us(q[i] & 0xF0F0F0F0u, xh[i], dh0);
+                    dh1 = dp4a_us(q[i + 1] & 0xF0F0F0F0u, xh[i + 1], dh1);
                 }
-                wl[t] += sc0 * dl;
-                wh[t] += sc1 * dh;
+                wl[t] += sc0 * (dl0 + dl1);
+                wh[t] += sc1 * (dh0 + dh1);
             }
         }
         const float d = f16_bits_to_f32(h.x & 0xFFFFu);
@@ -119,12 +168,13 @@ struct DecQ4K {
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
             w[t] = wl[t] + (wh[t] >> 4);  // wh is an exact multiple of 16
-            int m = dp2a_lo_ss(a[t].pm[0], m_lo, 0);
-            m = dp2a_hi_ss(a[t].pm[1], m_lo, m);
-            m = dp2a_lo_ss(a[t].pm[2], m_hi, m);
-            m = dp2a_hi_ss(a[t].pm[3], m_hi, m);
+            const uint4 pm = a.aux4(t, 0);
+            int m = dp2a_lo_ss(pm.x, m_lo, 0);
+            m = dp2a_hi_ss(pm.y, m_lo, m);
+            m = dp2a_lo_ss(pm.z, m_hi, m);
+            m = dp2a_hi_ss(pm.w, m_hi, m);
             x[t] = m;
-            const float dd = __fmul_rn(d, a[t].xs), dm = __fmul_rn(dmin, a[t].xs);
+            const float dd = __fmul_rn(d, a.xs(t)), dm = __fmul_rn(dmin, a.xs(t));
             v[t] = __fsub_rn(__fmul_rn(dd, static_cast<float>(w[t])), __fmul_rn(dm, static_cast<float>(m)));
         }
     }
@@ -134,29 +184,24 @@ struct DecQ4K {
 // Q6_K (210 B: 128 B low nibbles, 64 B high 2-bit pairs, 16 int8 scales, fp16 d)
 // qwen38_quant.c:1727-1833 (the AVX2 form: unsigned q, minus 32*sum(sc*bsum)).
 // ===========================================================================
-struct ActQ6K : ActBase {
-    uint32_t bs[8];  // int16 pairs of the 16 bsums
-};
-
 struct DecQ6K {
     static constexpr int kBytes = 210;
     static constexpr int kAlign = 2;
-    using Act = ActQ6K;
-    __device__ static void load(Act &a, const Q8KBlock *g)
+    // aux[j] = int16 pair (bsum[2j], bsum[2j+1]).
+    __device__ static void aux(Act &a, const Q8KBlock *g)
     {
-        load_act_base(a, g);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) a.bs[j] = pack16(bsum(g, 2 * j), bsum(g, 2 * j + 1));
+        for (int j = 0; j < 8; ++j) a.aux[j] = pack16(bsum(g, 2 * j), bsum(g, 2 * j + 1));
     }
-    __device__ static void zero(Act &a)
+    __device__ static void aux_from_raw(Act &a)
     {
-        zero_act_base(a);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) a.bs[j] = 0u;
+        for (int j = 0; j < 8; ++j) a.aux[j] = a.aux[8 + j];
     }
-    template <int MT>
-    __device__ static void block(const uint8_t *blk, const Act (&a)[MT], int (&w)[MT], int (&x)[MT],
-                                 float (&v)[MT])
+    __device__ static void load(Act &a, const Q8KBlock *g) { load_act_base(a, g); aux(a, g); }
+    __device__ static void zero(Act &a) { zero_act(a); }
+    template <int MT, class A>
+    __device__ static void block(const uint8_t *blk, const A &a, int (&w)[MT], int (&x)[MT], float (&v)[MT])
     {
         uint32_t tail[5];  // bytes 192..211: 16 int8 scales, fp16 d (+2 past the end)
         lds_words<5>(blk + 192, tail);
@@ -183,11 +228,11 @@ struct DecQ6K {
                 const int sc1 = sbyte_of(tail[(g0 + 1) / 4], (g0 + 1) & 3);
 #pragma unroll
                 for (int t = 0; t < MT; ++t) {
-                    int da = 0, db = 0;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) da = dp4a_us(val[i], a[t].q[s * 8 + i], da);
-#pragma unroll
-                    for (int i = 4; i < 8; ++i) db = dp4a_us(val[i], a[t].q[s * 8 + i], db);
+                    const uint4 x0 = a.q4(t, 2 * s), x1 = a.q4(t, 2 * s + 1);
+                    const int da = dp4a_us(val[0], x0.x, 0) + dp4a_us(val[1], x0.y, 0) +
+                                   (dp4a_us(val[2], x0.z, 0) + dp4a_us(val[3], x0.w, 0));
+                    const int db = dp4a_us(val[4], x1.x, 0) + dp4a_us(val[5], x1.y, 0) +
+                                   (dp4a_us(val[6], x1.z, 0) + dp4a_us(val[7], x1.w, 0));
                     acc[t] += sc0 * da + sc1 * db;
                 }
             }
@@ -195,15 +240,17 @@ struct DecQ6K {
         const float d = f16_bits_to_f32(tail[4] & 0xFFFFu);
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
+            const uint4 b0 = a.aux4(t, 0), b1 = a.aux4(t, 1);
+            const uint32_t bs[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
             int off = 0;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                off = dp2a_lo_ss(a[t].bs[2 * j], tail[j], off);
-                off = dp2a_hi_ss(a[t].bs[2 * j + 1], tail[j], off);
+                off = dp2a_lo_ss(bs[2 * j], tail[j], off);
+                off = dp2a_hi_ss(bs[2 * j + 1], tail[j], off);
             }
             w[t] = acc[t] - 32 * off;
             x[t] = 0;
-            v[t] = __fmul_rn(__fmul_rn(d, a[t].xs), static_cast<float>(w[t]));
+            v[t] = __fmul_rn(__fmul_rn(d, a.xs(t)), static_cast<float>(w[t]));
         }
     }
 };
@@ -216,12 +263,13 @@ struct DecQ6K {
 struct DecIQ2S {
     static constexpr int kBytes = 82;
     static constexpr int kAlign = 2;
-    using Act = ActBase;
+    __device__ static void aux(Act &, const Q8KBlock *) {}
+    __device__ static void aux_from_raw(Act &) {}
     __device__ static void load(Act &a, const Q8KBlock *g) { load_act_base(a, g); }
-    __device__ static void zero(Act &a) { zero_act_base(a); }
-    template <int MT>
-    __device__ static void block(const uint8_t *blk, const Act (&a)[MT], int (&w)[MT], int (&x)[MT],
-                                 float (&v)[MT], const uint2 *grid)
+    __device__ static void zero(Act &a) { zero_act(a); }
+    template <int MT, class A>
+    __device__ static void block(const uint8_t *blk, const A &a, int (&w)[MT], int (&x)[MT], float (&v)[MT],
+                                 const uint2 *grid)
     {
         uint32_t raw[21];  // bytes 0..83
         lds_words<21>(blk, raw);
@@ -248,8 +296,8 @@ struct DecIQ2S {
                 const uint32_t hi = apply_signs(e.y, sign_mask4(sg >> 4));
 #pragma unroll
                 for (int t = 0; t < MT; ++t) {
-                    int d = dp4a_ss(lo, a[t].q[8 * g + 2 * s], part[t][s / 2]);
-                    part[t][s / 2] = dp4a_ss(hi, a[t].q[8 * g + 2 * s + 1], d);
+                    int d = dp4a_ss(lo, a.q(t, 8 * g + 2 * s), part[t][s / 2]);
+                    part[t][s / 2] = dp4a_ss(hi, a.q(t, 8 * g + 2 * s + 1), d);
                 }
             }
 #pragma unroll
@@ -261,7 +309,7 @@ struct DecIQ2S {
         for (int t = 0; t < MT; ++t) {
             w[t] = acc[t];
             x[t] = 0;
-            v[t] = __fmul_rn(__fmul_rn(d, a[t].xs), static_cast<float>(acc[t]));
+            v[t] = __fmul_rn(__fmul_rn(d, a.xs(t)), static_cast<float>(acc[t]));
         }
     }
 };
@@ -271,29 +319,28 @@ struct DecIQ2S {
 // 3-bit scale, delta sign}).  qwen38_quant.c:1177-1253.  `grid` is the
 // 2048-entry {-1,0,1} table expanded into shared memory.
 // ===========================================================================
-struct ActIQ1S : ActBase {
-    int gs[8];  // bsum[2g] + bsum[2g+1]
-};
-
 struct DecIQ1S {
     static constexpr int kBytes = 50;
     static constexpr int kAlign = 2;
-    using Act = ActIQ1S;
-    __device__ static void load(Act &a, const Q8KBlock *g)
+    // aux[g] = bsum[2g] + bsum[2g+1] (the 32-element group sums).
+    __device__ static void aux(Act &a, const Q8KBlock *g)
     {
-        load_act_base(a, g);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) a.gs[j] = bsum(g, 2 * j) + bsum(g, 2 * j + 1);
+        for (int j = 0; j < 8; ++j) a.aux[j] = static_cast<uint32_t>(bsum(g, 2 * j) + bsum(g, 2 * j + 1));
     }
-    __device__ static void zero(Act &a)
+    __device__ static void aux_from_raw(Act &a)
     {
-        zero_act_base(a);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) a.gs[j] = 0;
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t p = a.aux[8 + j];
+            a.aux[j] = static_cast<uint32_t>(lo16(p) + hi16(p));
+        }
     }
-    template <int MT>
-    __device__ static void block(const uint8_t *blk, const Act (&a)[MT], int (&w)[MT], int (&x)[MT],
-                                 float (&v)[MT], const uint2 *grid)
+    __device__ static void load(Act &a, const Q8KBlock *g) { load_act_base(a, g); aux(a, g); }
+    __device__ static void zero(Act &a) { zero_act(a); }
+    template <int MT, class A>
+    __device__ static void block(const uint8_t *blk, const A &a, int (&w)[MT], int (&x)[MT], float (&v)[MT],
+                                 const uint2 *grid)
     {
         uint32_t raw[13];  // bytes 0..51
         lds_words<13>(blk, raw);
@@ -315,14 +362,14 @@ struct DecIQ1S {
                 const uint2 e = grid[gi];
 #pragma unroll
                 for (int t = 0; t < MT; ++t) {
-                    dot[t] = dp4a_ss(e.x, a[t].q[8 * g + 2 * s], dot[t]);
-                    dot[t] = dp4a_ss(e.y, a[t].q[8 * g + 2 * s + 1], dot[t]);
+                    dot[t] = dp4a_ss(e.x, a.q(t, 8 * g + 2 * s), dot[t]);
+                    dot[t] = dp4a_ss(e.y, a.q(t, 8 * g + 2 * s + 1), dot[t]);
                 }
             }
 #pragma unroll
             for (int t = 0; t < MT; ++t) {
                 acc[t] += scale * dot[t];
-                cor[t] += sd * a[t].gs[g];
+                cor[t] += sd * static_cast<int>(a.aux(t, g));
             }
         }
 #undef Q38_B
@@ -331,7 +378,7 @@ struct DecIQ1S {
         for (int t = 0; t < MT; ++t) {
             w[t] = acc[t];
             x[t] = cor[t];
-            const float dd = __fmul_rn(d, a[t].xs);
+            const float dd = __fmul_rn(d, a.xs(t));
             v[t] = __fmul_rn(dd, __fadd_rn(static_cast<float>(acc[t]),
                                            __fmul_rn(0.125f, static_cast<float>(cor[t]))));
         }
@@ -343,33 +390,26 @@ struct DecIQ1S {
 // signs}, 8 B {3-bit scales, fp16 super-scale in the top nibbles}).
 // qwen38_quant.c:1388-1544.  The correction uses 8-element activation sums.
 // ===========================================================================
-struct ActIQ1M : ActBase {
-    uint32_t s8[16];  // int16 pairs of the 32 eight-element quant sums
-};
-
 struct DecIQ1M {
     static constexpr int kBytes = 56;
     static constexpr int kAlign = 8;
-    using Act = ActIQ1M;
-    __device__ static void load(Act &a, const Q8KBlock *g)
+    // aux[j] = int16 pair of the eight-element quant sums of sections 2j, 2j+1
+    // (computed from the quants, which must already be in `a`).
+    __device__ static void aux(Act &a, const Q8KBlock *)
     {
-        load_act_base(a, g);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
             const int lo = dp4a_ss(a.q[4 * j], 0x01010101u, dp4a_ss(a.q[4 * j + 1], 0x01010101u, 0));
             const int hi = dp4a_ss(a.q[4 * j + 2], 0x01010101u, dp4a_ss(a.q[4 * j + 3], 0x01010101u, 0));
-            a.s8[j] = pack16(lo, hi);
+            a.aux[j] = pack16(lo, hi);
         }
     }
-    __device__ static void zero(Act &a)
-    {
-        zero_act_base(a);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) a.s8[j] = 0u;
-    }
-    template <int MT>
-    __device__ static void block(const uint8_t *blk, const Act (&a)[MT], int (&w)[MT], int (&x)[MT],
-                                 float (&v)[MT], const uint2 *grid)
+    __device__ static void aux_from_raw(Act &a) { aux(a, nullptr); }
+    __device__ static void load(Act &a, const Q8KBlock *g) { load_act_base(a, g); aux(a, g); }
+    __device__ static void zero(Act &a) { zero_act(a); }
+    template <int MT, class A>
+    __device__ static void block(const uint8_t *blk, const A &a, int (&w)[MT], int (&x)[MT], float (&v)[MT],
+                                 const uint2 *grid)
     {
         const uint2 *p = reinterpret_cast<const uint2 *>(blk);
         uint32_t raw[14];
@@ -398,10 +438,10 @@ struct DecIQ1M {
                 const uint2 e = grid[gi];
 #pragma unroll
                 for (int t = 0; t < MT; ++t) {
-                    int d = dp4a_ss(e.x, a[t].q[8 * g + 2 * s], 0);
-                    d = dp4a_ss(e.y, a[t].q[8 * g + 2 * s + 1], d);
+                    int d = dp4a_ss(e.x, a.q(t, 8 * g + 2 * s), 0);
+                    d = dp4a_ss(e.y, a.q(t, 8 * g + 2 * s + 1), d);
                     acc[t] += scl * d;
-                    const uint32_t pair = a[t].s8[(4 * g + s) >> 1];
+                    const uint32_t pair = a.aux(t, (4 * g + s) >> 1);
                     const int sec = ((4 * g + s) & 1) ? static_cast<int>(static_cast<int16_t>(pair >> 16))
                                                       : static_cast<int>(static_cast<int16_t>(pair & 0xFFFFu));
                     cor[t] += neg ? -scl * sec : scl * sec;
@@ -416,7 +456,7 @@ struct DecIQ1M {
         for (int t = 0; t < MT; ++t) {
             w[t] = acc[t];
             x[t] = cor[t];
-            const float dd = __fmul_rn(d, a[t].xs);
+            const float dd = __fmul_rn(d, a.xs(t));
             v[t] = __fmul_rn(dd, __fadd_rn(static_cast<float>(acc[t]),
                                            __fmul_rn(0.125f, static_cast<float>(cor[t]))));
         }

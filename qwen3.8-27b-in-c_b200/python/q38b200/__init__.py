@@ -19,11 +19,16 @@ LIB_PATH = os.path.normpath(os.path.join(_HERE, "..", "..", "lib", "libq38cuda.s
 Q8K_BYTES = 292
 
 
+LAYOUT_GGUF = 0
+LAYOUT_TILED = 1
+
+
 class CuTensor(ctypes.Structure):
     """Q38CuTensor (include/q38cuda.h)."""
     _fields_ = [("type", ctypes.c_uint32), ("n_dims", ctypes.c_uint32),
                 ("shape", ctypes.c_uint64 * 2), ("nbytes", ctypes.c_uint64),
-                ("data", ctypes.c_void_p)]
+                ("data", ctypes.c_void_p), ("layout", ctypes.c_uint32), ("tile_rows", ctypes.c_uint32),
+                ("scratch", ctypes.c_void_p), ("scratch_bytes", ctypes.c_uint64)]
 
 
 class Q38CudaError(RuntimeError):
@@ -46,7 +51,8 @@ def _load(path=LIB_PATH):
         "q38cu_tensor_gemv_f32": ([vp, vp, tp, vp], ctypes.c_int),
         "q38cu_tensor_gemm_f32": ([vp, vp, u32, u64, tp, vp], ctypes.c_int),
         "q38cu_tensor_row_f32": ([vp, tp, u64, vp], ctypes.c_int),
-        "q38cu_tensor_upload": ([tp, u32, u64, u64, vp, vp], ctypes.c_int),
+        "q38cu_tensor_upload": ([tp, u32, u64, u64, vp, u32, vp], ctypes.c_int),
+        "q38cu_tensor_repack": ([tp, tp, vp], ctypes.c_int),
         "q38cu_tensor_free": ([tp], None),
         "q38cu_block_bytes": ([u32], u32),
         "q38cu_block_elements": ([u32], u32),
@@ -92,15 +98,15 @@ def _ptr(t):
 class DeviceTensor:
     """A GGUF tensor resident in device memory (16-byte aligned, padded)."""
 
-    def __init__(self, qtype, width, rows, host_bytes=None):
+    def __init__(self, qtype, width, rows, host_bytes=None, layout=LAYOUT_GGUF):
         self.desc = CuTensor()
         buf = None
         if host_bytes is not None:
             buf = np.ascontiguousarray(host_bytes, dtype=np.uint8)
         src = ctypes.c_void_p(buf.ctypes.data) if buf is not None else None
-        _check(lib().q38cu_tensor_upload(ctypes.byref(self.desc), qtype, width, rows, src, _stream()),
+        _check(lib().q38cu_tensor_upload(ctypes.byref(self.desc), qtype, width, rows, src, layout, _stream()),
                "q38cu_tensor_upload")
-        self.qtype, self.width, self.rows = qtype, width, rows
+        self.qtype, self.width, self.rows, self.layout = qtype, width, rows, layout
 
     @property
     def nbytes(self):

@@ -65,3 +65,14 @@ def test_rejects_bad_arguments_without_device(q38):
     # zero batch
     t.type = 12
     assert lib.q38cu_tensor_gemm_q8_k(buf, buf, 0, 512, ctypes.byref(t), null) == 0
+
+
+def test_stream_unit_ownership_formula():
+    """The streaming kernel gives CTA c the units [floor(U c / G), floor(U (c+1) / G))
+    and finds a unit's owner with ((u + 1) G - 1) // U (q38_stream.cu)."""
+    for units in (1, 2, 7, 20, 136, 1360, 19400):
+        for grid in range(1, min(units, 300) + 1):
+            owner = [((u + 1) * grid - 1) // units for u in range(units)]
+            for c in range(grid):
+                for u in range(units * c // grid, units * (c + 1) // grid):
+                    assert owner[u] == c

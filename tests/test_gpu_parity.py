@@ -22,6 +22,10 @@ pytestmark = pytest.mark.gpu
 REL = 1e-3
 DEVICE_Q8K = (O.Q4_K, O.Q6_K, O.IQ2_S, O.IQ1_S, O.IQ1_M)
 NAME = O.TYPE_NAMES
+# GGUF row-major layout (row-streaming kernel) and the tiled streaming
+# layout (the fast path).
+LAYOUTS = (0, 1)
+LAYOUT_IDS = ("gguf", "tiled")
 
 
 def to_dev(a):
@@ -38,7 +42,8 @@ def assert_close(gpu, ref, rel=REL):
     ref = np.asarray(ref, np.float64)
     floor = 1e-2 * np.sqrt(np.mean(ref * ref)) + 1e-30
     bad = np.abs(gpu - ref) > rel * np.maximum(np.abs(ref), floor)
-    assert not bad.any(), f"{bad.sum()} mismatches; worst {np.max(np.abs(gpu - ref) / np.maximum(np.abs(ref), floor))}"
+    assert not bad.any(), (f"{bad.sum()} mismatches at {np.argwhere(bad)[:8].tolist()}; "
+                           f"worst {np.max(np.abs(gpu - ref) / np.maximum(np.abs(ref), floor))}")
 
 
 def test_quantize_random_bitexact(q38, oracle):
@@ -56,12 +61,13 @@ def test_quantize_golden_edges(q38):
     assert np.array_equal(got.reshape(g["q8k"].shape), g["q8k"])
 
 
+@pytest.mark.parametrize("layout", LAYOUTS, ids=LAYOUT_IDS)
 @pytest.mark.parametrize("qtype", DEVICE_Q8K, ids=lambda t: NAME[t])
-def test_gemm_golden(q38, qtype):
+def test_gemm_golden(q38, qtype, layout):
     g = np.load(os.path.join(GOLDEN, f"q8k_{NAME[qtype]}.npz"))
     rows, width = g["weights"].shape[0], g["x"].shape[1]
     batch = g["x"].shape[0]
-    t = q38.DeviceTensor(qtype, width, rows, g["weights"])
+    t = q38.DeviceTensor(qtype, width, rows, g["weights"], layout=layout)
     act = to_dev(g["q8k"].reshape(-1))
     out, w, x = q38.gemm_q8_k_sums(t, act, batch)
     out, w, x = out.cpu().numpy(), w.cpu().numpy().astype(np.int64), x.cpu().numpy().astype(np.int64)
@@ -78,12 +84,13 @@ def test_gemm_golden(q38, qtype):
 SHAPES = [(17, 256), (64, 512), (333, 5120), (37, 17408), (5, 6144), (129, 10240), (1, 5120)]
 
 
+@pytest.mark.parametrize("layout", LAYOUTS, ids=LAYOUT_IDS)
 @pytest.mark.parametrize("qtype", DEVICE_Q8K, ids=lambda t: NAME[t])
 @pytest.mark.parametrize("rows,width", SHAPES)
-def test_gemm_random_vs_oracle(q38, oracle, qtype, rows, width):
+def test_gemm_random_vs_oracle(q38, oracle, qtype, rows, width, layout):
     weights = synth.quant_tensor(qtype, rows, width, seed=rows * 31 + width + qtype)
-    t = q38.DeviceTensor(qtype, width, rows, weights)
-    for batch in (1, 2, 3, 8):
+    t = q38.DeviceTensor(qtype, width, rows, weights, layout=layout)
+    for batch in (1, 2, 3, 8, 11):
         q8k = oracle.quantize_q8_k(synth.activations(batch, width, seed=batch + rows))
         out, w, x = q38.gemm_q8_k_sums(t, q8k_dev(q8k), batch)
         ref_out = oracle.gemm_q8_k(qtype, weights, rows, width, q8k)
@@ -91,13 +98,17 @@ def test_gemm_random_vs_oracle(q38, oracle, qtype, rows, width):
         assert np.array_equal(w.cpu().numpy(), ref_w), f"w sums differ (batch {batch})"
         assert np.array_equal(x.cpu().numpy(), ref_x), f"x sums differ (batch {batch})"
         assert_close(out.cpu().numpy(), ref_out)
+        # the plain entry point (no sums) must agree bit for bit with the probe
+        plain = q38.gemm_q8_k(t, q8k_dev(q8k), batch).cpu().numpy()
+        assert np.array_equal(plain, out.cpu().numpy()), f"plain vs sums path (batch {batch})"
 
 
+@pytest.mark.parametrize("layout", LAYOUTS, ids=LAYOUT_IDS)
 @pytest.mark.parametrize("qtype", DEVICE_Q8K, ids=lambda t: NAME[t])
-def test_batch_bit_exact_with_gemv(q38, oracle, qtype):
+def test_batch_bit_exact_with_gemv(q38, oracle, qtype, layout):
     rows, width = 96, 5120
     weights = synth.quant_tensor(qtype, rows, width, seed=qtype)
-    t = q38.DeviceTensor(qtype, width, rows, weights)
+    t = q38.DeviceTensor(qtype, width, rows, weights, layout=layout)
     q8k = oracle.quantize_q8_k(synth.activations(8, width, seed=99))
     act = q8k_dev(q8k)
     per_token = width // 256 * 292
@@ -108,12 +119,13 @@ def test_batch_bit_exact_with_gemv(q38, oracle, qtype):
         assert np.array_equal(out, single[:batch]), f"batch {batch}"
 
 
-def test_q4k_full_size(q38, oracle):
-    """BASELINE config 0 shape: 17408 x 5120 Q4_K, fp32 N(0,1) activation."""
-    rows, width = 17408, 5120
+@pytest.mark.parametrize("layout", LAYOUTS, ids=LAYOUT_IDS)
+@pytest.mark.parametrize("rows,width", [(17408, 5120), (5120, 17408)])
+def test_q4k_full_size(q38, oracle, rows, width, layout):
+    """BASELINE config 0 shapes: 17408 x 5120 and 5120 x 17408 Q4_K, fp32 N(0,1) activation."""
     weights = synth.quant_tensor(O.Q4_K, rows, width, seed=0)
     x = synth.activations(1, width, seed=1)
-    t = q38.DeviceTensor(O.Q4_K, width, rows, weights)
+    t = q38.DeviceTensor(O.Q4_K, width, rows, weights, layout=layout)
     act = q38.quantize_q8_k(to_dev(x))
     q8k = oracle.quantize_q8_k(x)
     assert np.array_equal(act.cpu().numpy().reshape(-1), q8k.view(np.uint8).reshape(-1))
@@ -144,11 +156,12 @@ def test_q8_0_alpha_beta_shape(q38, oracle):
     assert_close(out, oracle.gemm_f32(O.Q8_0, weights, 48, 5120, x))
 
 
-def test_embedding_row_full_size(q38, oracle):
+@pytest.mark.parametrize("layout", LAYOUTS, ids=LAYOUT_IDS)
+def test_embedding_row_full_size(q38, oracle, layout):
     """token_embd row dequant (Q4_K 248320 x 5120 in the mix; a slice here)."""
     rows, width = 64, 5120
     weights = synth.quant_tensor(O.Q4_K, rows, width, seed=8)
-    t = q38.DeviceTensor(O.Q4_K, width, rows, weights)
+    t = q38.DeviceTensor(O.Q4_K, width, rows, weights, layout=layout)
     for r in (0, 31, 63):
         assert np.array_equal(q38.row_f32(t, r).cpu().numpy(), oracle.row_f32(O.Q4_K, weights, rows, width, r))
 
@@ -166,3 +179,19 @@ def test_error_paths(q38):
     t2 = q38.DeviceTensor(O.Q5_K, 512, 4, synth.quant_tensor(O.Q5_K, 4, 512, seed=1))
     with pytest.raises(q38.Q38CudaError, match="not yet implemented"):
         q38.gemm_q8_k(t2, act, 1)
+
+
+def test_repeated_launches_reuse_scratch(q38, oracle):
+    """Split row tiles leave their counters at zero: many back-to-back launches
+    (the decode pattern) give identical results."""
+    rows, width = 5120, 17408
+    weights = synth.quant_tensor(O.Q6_K, rows, width, seed=12)
+    t = q38.DeviceTensor(O.Q6_K, width, rows, weights, layout=1)
+    q8k = oracle.quantize_q8_k(synth.activations(2, width, seed=13))
+    act = q8k_dev(q8k)
+    first = q38.gemm_q8_k(t, act, 2).cpu().numpy()
+    for _ in range(20):
+        again = q38.gemm_q8_k(t, act, 2).cpu().numpy()
+        assert np.array_equal(first, again)
+    assert_close(first, oracle.gemm_q8_k(O.Q6_K, weights, rows, width, q8k))
+    assert q38.device_status() == 0

@@ -127,6 +127,29 @@ void q38cu_tensor_free(Q38CuTensor *tensor);
 uint32_t q38cu_block_bytes(uint32_t type);
 uint32_t q38cu_block_elements(uint32_t type);
 
+/* GEMM over a tiled tensor that allocates no device memory.  No counterpart
+ * in the upstream engine (its CPU kernels need no scratch).
+ *
+ * For callers that cannot call cudaMalloc: an engine that hands out device
+ * memory only from a pre-planned arena (cudaMalloc/cudaFree synchronize the
+ * whole device, which a serving loop cannot afford), or code handed a tiled
+ * tensor whose weights were placed without the scratch buffer
+ * q38cu_tensor_upload/q38cu_tensor_repack would allocate.  Same arguments,
+ * result and bit-exactness as q38cu_tensor_gemm_q8_k for a tensor in the tiled
+ * layout (tensor->scratch is ignored and may be NULL).
+ *
+ * Its scratch is one file-scope device array of Q38CU_NOALLOC_SCRATCH_BYTES,
+ * which every GPU that loads the library holds until the process exits.  The
+ * first call on a device looks up that array's device address (set-up, once
+ * per device); make that first call before any stream capture.  Shapes whose
+ * scratch exceeds the maximum are rejected (return 0, reason in
+ * q38cu_last_error).  All calls share the one array and each clears its tile
+ * counters first, so calls whose kernels overlap on the GPU (two streams, or
+ * two host threads on one device) race; serialize them. */
+#define Q38CU_NOALLOC_SCRATCH_BYTES (16u << 20)
+int q38cu_tensor_gemm_q8_k_noalloc(float *output, const Q38CuQ8KBlock *input, uint32_t batch_size,
+                                   uint64_t input_length, const Q38CuTensor *tensor, void *stream);
+
 /* Diagnostics: the message behind the last 0 return on this host thread, and
  * the device status word (0 = ok, else a bounded wait gave up) which is read
  * after synchronizing `stream` and then cleared. */

@@ -229,6 +229,8 @@ int gemm_q8k(float *output, int32_t *w_out, int32_t *x_out, const Q38CuQ8KBlock 
 
 namespace q38 {
 
+void set_last_error(const char *message) { std::snprintf(g_error, sizeof(g_error), "%s", message); }
+
 int device_sm_count()
 {
     static int counts[64] = {0};

@@ -61,6 +61,8 @@ cudaError_t launch_repack_tiled(void *dst, const void *src, uint64_t rows, uint6
                                 uint32_t block_bytes, cudaStream_t s);
 
 int device_sm_count();
+// Message returned by q38cu_last_error() on this host thread.
+void set_last_error(const char *message);
 int superblock_bytes(int type);
 size_t gemm_smem_for(int type, const GemmPlan &plan, int batch);
 cudaError_t launch_q8k_gemm(int type, const GemmPlan &plan, const LaunchGemm &l, cudaStream_t s);

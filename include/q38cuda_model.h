@@ -1,0 +1,65 @@
+/* q38cuda_model.h - the device-resident model behind the upstream model API.
+ *
+ * The q38_model_* entry points have the names, signatures, argument meaning
+ * and error behaviour of include/qwen38/qwen38_model.h (upstream), so the
+ * upstream CLI and probes link against libq38cuda.so in place of
+ * src/qwen38/qwen38_model.c and keep their loader, tokenizer and sampler:
+ *
+ *   Q38Model *q38_model_open_gguf     qwen38_model.h:12   (qwen38_model.c:1370-1414)
+ *   q38_model_attach_mtp_gguf          qwen38_model.h:13   (qwen38_model.c:1416-1434)
+ *   q38_model_close / q38_model_reset  qwen38_model.h:14-15
+ *   q38_model_forward_token            qwen38_model.h:19-20 (qwen38_model.c:1494-1517)
+ *   q38_model_prefill                  qwen38_model.h:24-25 (qwen38_model.c:1519-1560)
+ *   q38_model_enable_mtp / _mtp_forward qwen38_model.h:29-31 (qwen38_model.c:1562-1612)
+ *   q38_model_speculative_greedy       qwen38_model.h:37-42 (qwen38_model.c:1614-1714)
+ *   q38_model_forward_token_layers     qwen38_model.h:46-47 (qwen38_model.c:1476-1492)
+ *   q38_model_vocab_size / _position / _context_length  qwen38_model.h:49-51
+ *
+ * Differences a caller can see: the model lives on the CUDA device that is
+ * current when q38_model_open_gguf is called; logits pointers are pinned host
+ * buffers owned by the model (replaced by the next call, as upstream).
+ * Failures return 0 / NULL, print a diagnostic on stderr as upstream does, and
+ * leave the reason in q38cu_last_error().
+ */
+#ifndef Q38CUDA_MODEL_H
+#define Q38CUDA_MODEL_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct Q38Model Q38Model;
+
+Q38Model *q38_model_open_gguf(const char *path, uint32_t context_length);
+int q38_model_attach_mtp_gguf(Q38Model *model, const char *path);
+void q38_model_close(Q38Model *model);
+void q38_model_reset(Q38Model *model);
+int q38_model_forward_token(Q38Model *model, uint32_t token_id, const float **logits);
+int q38_model_prefill(Q38Model *model, const uint32_t *tokens, uint32_t token_count, const float **logits);
+int q38_model_enable_mtp(Q38Model *model);
+int q38_model_mtp_forward(Q38Model *model, uint32_t token_id, const float **logits);
+int q38_model_speculative_greedy(Q38Model *model, uint32_t token_id, uint32_t stop_token, uint32_t draft_count,
+                                 uint32_t *accepted_tokens, uint32_t *accepted_count, const float **next_logits);
+int q38_model_forward_token_layers(Q38Model *model, uint32_t token_id, uint32_t layer_count, float *hidden_out);
+uint32_t q38_model_vocab_size(const Q38Model *model);
+uint32_t q38_model_position(const Q38Model *model);
+uint32_t q38_model_context_length(const Q38Model *model);
+
+/* Greedy decoding without logits on the host (no upstream counterpart; the
+ * upstream loop is q38_model_forward_token + q38_sampler argmax,
+ * src/cli/qwen38_main.c:545-578).  Evaluates token_id at the current position,
+ * then feeds each step's argmax back as the next input on the device, for
+ * `count` steps; tokens_out[i] is the argmax of step i.  The position advances
+ * by `count`; the last token is pending, as after the upstream loop. */
+int q38cu_model_generate_greedy(Q38Model *model, uint32_t token_id, uint32_t count, uint32_t *tokens_out);
+
+/* The cudaStream_t the model runs on (for event timing by a caller). */
+void *q38cu_model_stream(Q38Model *model);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

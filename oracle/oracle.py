@@ -20,6 +20,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_LIB = os.path.join(HERE, "_build", "libq38oracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libq38ref.so")
+REF_PORTABLE_LIB = os.path.join(HERE, "_ref", "libq38ref_portable.so")
 
 # GGML type ids (GGUF values).
 F32, F16, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K = 0, 1, 8, 10, 11, 12, 13, 14
@@ -202,3 +203,98 @@ class Reference:
 
 def reference_available():
     return os.path.exists(REF_LIB)
+
+
+class ReferenceModel:
+    """The upstream Q38Model (qwen38_model.c compiled from its sources): the
+    model-level oracle.  Same method names as q38b200.model.Model."""
+
+    VOCAB = 248320
+
+    def __init__(self, path, context_length=4096, lib_path=REF_LIB):
+        if not os.path.exists(lib_path):
+            raise FileNotFoundError(f"{lib_path} missing (built only where the upstream tree exists)")
+        lib = ctypes.CDLL(lib_path)
+        vp, u32 = ctypes.c_void_p, ctypes.c_uint32
+        fpp = ctypes.POINTER(ctypes.POINTER(ctypes.c_float))
+        u32p = ctypes.POINTER(ctypes.c_uint32)
+        sig = {
+            "q38_model_open_gguf": ([ctypes.c_char_p, u32], vp),
+            "q38_model_close": ([vp], None),
+            "q38_model_reset": ([vp], None),
+            "q38_model_forward_token": ([vp, u32, fpp], ctypes.c_int),
+            "q38_model_prefill": ([vp, u32p, u32, fpp], ctypes.c_int),
+            "q38_model_enable_mtp": ([vp], ctypes.c_int),
+            "q38_model_mtp_forward": ([vp, u32, fpp], ctypes.c_int),
+            "q38_model_speculative_greedy": ([vp, u32, u32, u32, u32p, u32p, fpp], ctypes.c_int),
+            "q38_model_forward_token_layers": ([vp, u32, u32, vp], ctypes.c_int),
+            "q38_model_position": ([vp], u32),
+        }
+        for name, (args, res) in sig.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = res
+        self.lib = lib
+        self.handle = lib.q38_model_open_gguf(str(path).encode(), context_length)
+        assert self.handle, "upstream q38_model_open_gguf failed"
+
+    def close(self):
+        if self.handle:
+            self.lib.q38_model_close(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+    def _logits(self, p):
+        return np.ctypeslib.as_array(p, shape=(self.VOCAB,)).copy()
+
+    def reset(self):
+        self.lib.q38_model_reset(self.handle)
+
+    def forward_token(self, token):
+        p = ctypes.POINTER(ctypes.c_float)()
+        assert self.lib.q38_model_forward_token(self.handle, token, ctypes.byref(p)) == 1
+        return self._logits(p)
+
+    def forward_token_layers(self, token, layers):
+        out = np.zeros(5120, np.float32)
+        assert self.lib.q38_model_forward_token_layers(self.handle, token, layers, _ptr(out)) == 1
+        return out
+
+    def prefill(self, tokens):
+        ids = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = ctypes.POINTER(ctypes.c_float)()
+        assert self.lib.q38_model_prefill(self.handle, ids.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)),
+                                          ids.size, ctypes.byref(p)) == 1
+        return self._logits(p)
+
+    def enable_mtp(self):
+        assert self.lib.q38_model_enable_mtp(self.handle) == 1
+
+    def mtp_forward(self, token):
+        p = ctypes.POINTER(ctypes.c_float)()
+        assert self.lib.q38_model_mtp_forward(self.handle, token, ctypes.byref(p)) == 1
+        return self._logits(p)
+
+    def speculative_greedy(self, token, stop_token, draft_count):
+        accepted = np.zeros(max(draft_count, 1), np.uint32)
+        count = ctypes.c_uint32(0)
+        p = ctypes.POINTER(ctypes.c_float)()
+        assert self.lib.q38_model_speculative_greedy(
+            self.handle, token, stop_token, draft_count,
+            accepted.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)), ctypes.byref(count), ctypes.byref(p)) == 1
+        return accepted[:count.value].tolist(), self._logits(p)
+
+    def generate_greedy(self, token, count):
+        """The upstream greedy loop: forward_token, then argmax (q38_argmax:
+        the first index of the maximum) as the next input."""
+        out = []
+        for _ in range(count):
+            token = int(np.argmax(self.forward_token(token)))
+            out.append(token)
+        return out
+
+    @property
+    def position(self):
+        return self.lib.q38_model_position(self.handle)

@@ -9,7 +9,18 @@
 namespace q38 {
 
 // Status codes written to the device status word.
-enum : int { kStatusOk = 0, kStatusWaitTimeout = 1 };
+enum : int { kStatusOk = 0, kStatusWaitTimeout = 1, kStatusBadToken = 2 };
+
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute may start before its predecessor finishes;
+// it must call pdl_wait() before touching anything the predecessor reads or
+// writes.  pdl_launch_dependents() lets the next kernel start its prologue.
+// Both are no-ops for kernels launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // Wall-clock bound for any spin on an mbarrier (ns).  A bulk copy completes
 // in microseconds; hitting this means the copy was lost.

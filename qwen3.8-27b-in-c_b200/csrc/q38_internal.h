@@ -52,6 +52,8 @@ struct StreamLaunch {
     void *scratch;
     int32_t *dbg_w;
     int32_t *dbg_x;
+    int out_ld = 0;       // output row stride between tokens (0: rows)
+    int accumulate = 0;   // 1: add the result to the output rows
 };
 
 int stream_tile_rows(int rows);
@@ -70,8 +72,14 @@ cudaError_t launch_quantize_q8k(void *out, const float *in, uint64_t blocks, cud
 // `tile_rows` != 0 selects the tiled layout for block addressing.
 cudaError_t launch_f32_gemm(float *out, const float *x, int batch, uint64_t width, const void *w, uint64_t rows,
                             uint32_t tile_rows, int type, int be, int bb, cudaStream_t s);
+// PDL launch with strides: out[tok * out_ld + row] (+)= row . x[tok * x_ld ..]
+cudaError_t launch_f32_gemm_ex(float *out, uint64_t out_ld, int accumulate, const float *x, uint64_t x_ld, int batch,
+                               uint64_t width, const void *w, uint64_t rows, uint32_t tile_rows, int type, int be,
+                               int bb, cudaStream_t s);
 cudaError_t launch_row_f32(float *out, const void *w, uint64_t width, uint32_t tile_rows, uint64_t row, int type,
                            int be, int bb, cudaStream_t s);
+cudaError_t launch_row_f32_indexed(float *out, const void *w, uint64_t width, uint32_t tile_rows, uint64_t rows,
+                                   const uint32_t *row_index, int count, int type, int be, int bb, cudaStream_t s);
 cudaError_t read_and_clear_status(int *status, cudaStream_t s);
 cudaError_t read_and_clear_stream_status(int *status);
 

@@ -344,16 +344,20 @@ __device__ __forceinline__ const uint8_t *block_at(const uint8_t *w, uint64_t ro
     return w + ((t * nblocks + blk) * tile_rows + r) * bb;
 }
 
+// out[tok * out_ld + row] (+)= row . x[tok * x_ld ..]; one warp per (token, row).
 __global__ void f32_gemm_kernel(float *out, const float *x, int batch, uint64_t width, const uint8_t *w,
-                                uint64_t rows, uint32_t tile_rows, int type, int be, int bb)
+                                uint64_t rows, uint32_t tile_rows, int type, int be, int bb, uint64_t x_ld,
+                                uint64_t out_ld, int accumulate)
 {
+    pdl_wait();
+    pdl_launch_dependents();
     const uint64_t gw = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (gw >= rows * static_cast<uint64_t>(batch)) return;
     const uint64_t row = gw % rows;
     const int tok = static_cast<int>(gw / rows);
     const uint64_t nblocks = width / be;
-    const float *xx = x + static_cast<uint64_t>(tok) * width;
+    const float *xx = x + static_cast<uint64_t>(tok) * x_ld;
     float total = 0.0f;
     for (uint64_t blk = lane; blk < nblocks; blk += 32) {
         const uint8_t *b = block_at(w, row, blk, nblocks, tile_rows, bb);
@@ -361,7 +365,10 @@ __global__ void f32_gemm_kernel(float *out, const float *x, int batch, uint64_t 
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) total += __shfl_xor_sync(0xffffffffu, total, off);
-    if (lane == 0) out[static_cast<uint64_t>(tok) * rows + row] = total;
+    if (lane == 0) {
+        float *dst = out + static_cast<uint64_t>(tok) * out_ld + row;
+        *dst = accumulate ? __fadd_rn(*dst, total) : total;
+    }
 }
 
 // Element i of row `row`.  The upstream evaluates fma(w, 1, 0) against a
@@ -375,6 +382,29 @@ __global__ void row_f32_kernel(float *out, const uint8_t *w, uint64_t width, uin
     const uint8_t *b = block_at(w, row, i / be, nblocks, tile_rows, bb);
     const float v = element_weight(type, b, static_cast<int>(i % be));
     out[i] = type == kF32 || type == kF16 || type == kBF16 ? v : __fadd_rn(v, 0.0f);
+}
+
+// Rows selected by token ids held in device memory (the model's embedding
+// lookup inside a captured decode step): output row y is row row_index[y].
+// An id outside the tensor yields NaN and the kStatusBadToken status.
+__global__ void row_f32_indexed_kernel(float *out, const uint8_t *w, uint64_t width, uint32_t tile_rows,
+                                       uint64_t rows, const uint32_t *row_index, int type, int be, int bb)
+{
+    pdl_wait();
+    pdl_launch_dependents();
+    const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= width) return;
+    const uint64_t row = row_index[blockIdx.y];
+    float *o = out + static_cast<uint64_t>(blockIdx.y) * width;
+    if (row >= rows) {
+        o[i] = __int_as_float(0x7fc00000);
+        if (i == 0) atomicExch(&g_status, kStatusBadToken);
+        return;
+    }
+    const uint64_t nblocks = width / be;
+    const uint8_t *b = block_at(w, row, i / be, nblocks, tile_rows, bb);
+    const float v = element_weight(type, b, static_cast<int>(i % be));
+    o[i] = type == kF32 || type == kF16 || type == kBF16 ? v : __fadd_rn(v, 0.0f);
 }
 
 // ---------------------------------------------------------------------------
@@ -518,8 +548,27 @@ cudaError_t launch_f32_gemm(float *out, const float *x, int batch, uint64_t widt
     if (warps == 0) return cudaSuccess;
     const unsigned grid = static_cast<unsigned>((warps * 32 + 255) / 256);
     f32_gemm_kernel<<<grid, 256, 0, s>>>(out, x, batch, width, static_cast<const uint8_t *>(w), rows, tile_rows, type,
-                                         be, bb);
+                                         be, bb, width, rows, 0);
     return cudaGetLastError();
+}
+
+cudaError_t launch_f32_gemm_ex(float *out, uint64_t out_ld, int accumulate, const float *x, uint64_t x_ld, int batch,
+                               uint64_t width, const void *w, uint64_t rows, uint32_t tile_rows, int type, int be,
+                               int bb, cudaStream_t s)
+{
+    const uint64_t warps = rows * static_cast<uint64_t>(batch);
+    if (warps == 0) return cudaSuccess;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((warps * 32 + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, f32_gemm_kernel, out, x, batch, width, static_cast<const uint8_t *>(w), rows,
+                              tile_rows, type, be, bb, x_ld, out_ld, accumulate);
 }
 
 cudaError_t launch_row_f32(float *out, const void *w, uint64_t width, uint32_t tile_rows, uint64_t row, int type,
@@ -528,6 +577,22 @@ cudaError_t launch_row_f32(float *out, const void *w, uint64_t width, uint32_t t
     const unsigned grid = static_cast<unsigned>((width + 255) / 256);
     row_f32_kernel<<<grid, 256, 0, s>>>(out, static_cast<const uint8_t *>(w), width, tile_rows, row, type, be, bb);
     return cudaGetLastError();
+}
+
+cudaError_t launch_row_f32_indexed(float *out, const void *w, uint64_t width, uint32_t tile_rows, uint64_t rows,
+                                   const uint32_t *row_index, int count, int type, int be, int bb, cudaStream_t s)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((width + 255) / 256), static_cast<unsigned>(count));
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, row_f32_indexed_kernel, out, static_cast<const uint8_t *>(w), width, tile_rows,
+                              rows, row_index, type, be, bb);
 }
 
 cudaError_t read_and_clear_status(int *status, cudaStream_t s)

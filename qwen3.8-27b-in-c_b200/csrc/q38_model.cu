@@ -1,0 +1,993 @@
+// q38_model.cu - the device-resident Qwen3.8-27B model behind the upstream
+// model API (include/qwen38/qwen38_model.h, implemented upstream in
+// src/qwen38/qwen38_model.c).
+//
+// Weights, recurrent state, KV cache and activations live in HBM; a token step
+// is one stream of kernels (weight-streaming GEMVs and the fused kernels of
+// q38_model_kernels.cu) that reads the token id and the position from a small
+// device control block, so the whole step is captured once as a CUDA graph
+// and replayed for every token.  Greedy decoding feeds the argmax back into
+// the control block on the device; no logits cross PCIe unless the caller
+// asks for them.
+//
+// Projections that share an input are merged when their types allow it
+// (attn_qkv | attn_gate, attn_q | attn_k, ffn_gate | ffn_up, ssm_beta |
+// ssm_alpha): their rows are concatenated into one tiled tensor, so one launch
+// streams them all.  Results are unchanged by the merge: every output row is
+// computed by the same per-row arithmetic.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/q38cuda.h"
+#include "../../include/q38cuda_model.h"
+#include "q38_gguf_file.h"
+#include "q38_internal.h"
+#include "q38_model_internal.h"
+
+namespace {
+
+constexpr int kHidden = 5120, kFfn = 17408, kLayers = 64, kTotalLayers = 65;
+constexpr int kRecurrent = 48, kFull = 17;
+constexpr int kLinQkv = 10240, kLinV = 6144, kLinHeads = 48, kLinDim = 128;
+constexpr int kAttnQg = 12288, kAttnQ = 6144, kAttnKv = 1024, kAttnDim = 256;
+constexpr int kVocab = 248320;
+constexpr int kMaxTokens = 8;    // tokens per launch of the batch kernels
+constexpr int kMaxDrafts = 64;   // speculative drafts per call
+constexpr int kConvRing = 16;
+
+enum : uint32_t { kF32 = 0, kF16 = 1, kQ8_0 = 8, kBF16 = 30 };
+
+bool q8k_type(uint32_t t)  // upstream q38_matrix_type_q8_k (qwen38_model.c:172-182)
+{
+    return t == 10 || t == 11 || t == 12 || t == 13 || t == 14 || t == 16 || t == 17 || t == 18 || t == 20 ||
+           t == 21 || t == 22 || t == 23 || t == 19 || t == 29;
+}
+bool float_type(uint32_t t) { return t == kF32 || t == kF16 || t == kBF16 || t == kQ8_0; }
+
+int fail(const char *fmt, const std::string &detail = std::string())
+{
+    char buffer[512];
+    std::snprintf(buffer, sizeof(buffer), fmt, detail.c_str());
+    q38::set_last_error(buffer);
+    std::fprintf(stderr, "qwen38: %s\n", buffer);
+    return 0;
+}
+
+bool cuda_ok(cudaError_t e, const char *what)
+{
+    if (e == cudaSuccess) return true;
+    fail("%s", std::string(what) + ": " + cudaGetErrorString(e));
+    return false;
+}
+
+// One projection: one or more weight tensors whose output rows are placed
+// side by side.  A part is either a tiled tensor on the Q8_K integer path or
+// a GGUF-layout tensor on the float path (upstream q38_project,
+// qwen38_model.c:599-606).
+struct Part {
+    Q38CuTensor t{};
+    bool int_path = false;
+    int rows = 0, offset = 0;
+};
+
+struct Proj {
+    std::vector<Part> parts;
+    int rows = 0, width = 0;
+};
+
+struct Layer {
+    bool full = false;
+    int index = 0;  // recurrent index (DeltaNet) or full-attention index
+    float *attn_norm = nullptr, *post_norm = nullptr;
+    Proj in_proj;  // DeltaNet: qkv | z     full: q | k | v
+    Proj ba;       // DeltaNet: beta | alpha
+    Proj out;      // ssm_out / attn_output
+    Proj gate_up;  // ffn_gate | ffn_up
+    Proj down;
+    float *conv_w = nullptr, *dt = nullptr, *a = nullptr, *ssm_norm = nullptr;
+    float *q_norm = nullptr, *k_norm = nullptr;
+};
+
+template <typename T>
+bool dalloc(T **p, size_t count, std::vector<void *> &owned)
+{
+    void *q = nullptr;
+    if (!cuda_ok(cudaMalloc(&q, std::max<size_t>(count * sizeof(T), 16)), "cudaMalloc")) return false;
+    owned.push_back(q);
+    *p = static_cast<T *>(q);
+    return cuda_ok(cudaMemset(q, 0, std::max<size_t>(count * sizeof(T), 16)), "cudaMemset");
+}
+
+}  // namespace
+
+struct Q38Model {
+    q38::GGUFFile gguf, mtp_gguf;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    uint32_t context_length = 0, position = 0, mtp_position = 0;
+    bool mtp_loaded = false, mtp_enabled = false;
+    int attn_splits = 6;
+    float theta_scale = 0.0f;
+
+    Q38CuTensor embedding{}, mtp_embedding{};  // GGUF layout, row lookups
+    Proj output, mtp_output;                   // LM heads
+    float *output_norm = nullptr;
+    Layer layers[kTotalLayers];
+    Proj eh_proj;
+    float *enorm = nullptr, *hnorm = nullptr, *shared_head_norm = nullptr;
+
+    // state
+    float *conv_ring = nullptr, *delta_state = nullptr, *k_cache = nullptr, *v_cache = nullptr;
+    float *ck_conv_ring = nullptr, *ck_delta_state = nullptr, *mtp_hidden = nullptr, *ck_mtp_hidden = nullptr;
+    float *target_norm = nullptr;  // [kMaxDrafts][kHidden]: output-normed hidden of verified tokens
+    uint32_t ck_position = 0, ck_mtp_position = 0;
+
+    // activations, [kMaxTokens] rows each
+    float *hidden = nullptr, *normf = nullptr, *wide = nullptr, *ba = nullptr, *act_f = nullptr, *logits = nullptr;
+    void *q8 = nullptr;
+    int wide_ld = 0, ba_ld = 0;
+    int *ctl = nullptr;  // [0] token, [1] position, [2] history count
+    uint32_t *ids = nullptr, *argmax_out = nullptr, *history = nullptr;
+    float *attn_partials = nullptr, *argmax_part_v = nullptr;
+    int *attn_counters = nullptr, *argmax_part_i = nullptr, *argmax_counters = nullptr;
+
+    // host staging
+    float *host_logits = nullptr;
+    int *host_ctl = nullptr;
+    uint32_t *host_ids = nullptr;
+
+    cudaGraphExec_t decode_graph = nullptr;
+    std::vector<void *> owned;
+    std::vector<Q38CuTensor> tensors;  // every uploaded tensor, freed at close
+    void *staging = nullptr;
+    size_t staging_bytes = 0;
+};
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// loading
+// ---------------------------------------------------------------------------
+const q38::GGUFTensorInfo *find_layer(const q38::GGUFFile &f, int layer, const char *suffix)
+{
+    char name[128];
+    std::snprintf(name, sizeof(name), "blk.%d.%s", layer, suffix);
+    const q38::GGUFTensorInfo *t = f.find_tensor(name);
+    if (!t) fail("missing tensor %s", name);
+    return t;
+}
+
+// upstream q38_expect_tensor (qwen38_model.c:184-205)
+bool expect(const q38::GGUFTensorInfo *t, uint64_t width, uint64_t rows, bool f32_only)
+{
+    if (!t) return false;
+    const uint32_t dims = rows ? 2u : 1u;
+    const bool shape_ok = t->n_dims == dims && t->shape[0] == width && (!rows || t->shape[1] == rows);
+    const bool type_ok = f32_only ? t->type == kF32 : (float_type(t->type) || q8k_type(t->type));
+    if (shape_ok && type_ok) return true;
+    return fail("incompatible tensor %s", t->name);
+}
+
+bool ensure_staging(Q38Model *m, size_t bytes)
+{
+    if (m->staging_bytes >= bytes) return true;
+    if (m->staging) cudaFree(m->staging);
+    m->staging = nullptr;
+    m->staging_bytes = 0;
+    if (!cuda_ok(cudaMalloc(&m->staging, bytes), "cudaMalloc staging")) return false;
+    m->staging_bytes = bytes;
+    return true;
+}
+
+// Upload a group of tensors that share the input width.  Consecutive members
+// of one type on the Q8_K integer path are concatenated into one tiled tensor;
+// float-path members of one type into one GGUF-layout tensor.
+bool upload_proj(Q38Model *m, Proj *p, const std::vector<const q38::GGUFTensorInfo *> &members)
+{
+    p->parts.clear();
+    p->rows = 0;
+    p->width = static_cast<int>(members[0]->shape[0]);
+    size_t i = 0;
+    while (i < members.size()) {
+        size_t j = i + 1;
+        while (j < members.size() && members[j]->type == members[i]->type) ++j;
+        const uint32_t type = members[i]->type;
+        const bool int_path = q8k_type(type);
+        if (int_path && !q38::superblock_bytes(static_cast<int>(type)))
+            return fail("tensor %s: this quantization type has no device kernel yet", members[i]->name);
+        uint64_t rows = 0, bytes = 0;
+        for (size_t k = i; k < j; ++k) {
+            rows += members[k]->shape[1];
+            bytes += members[k]->nbytes;
+        }
+        if (!ensure_staging(m, bytes + 256)) return false;
+        uint64_t at = 0;
+        for (size_t k = i; k < j; ++k) {
+            if (!cuda_ok(cudaMemcpy(static_cast<uint8_t *>(m->staging) + at, members[k]->data, members[k]->nbytes,
+                                    cudaMemcpyHostToDevice),
+                         "weight upload"))
+                return false;
+            at += members[k]->nbytes;
+        }
+        Q38CuTensor src{};
+        src.type = type;
+        src.n_dims = 2;
+        src.shape[0] = members[i]->shape[0];
+        src.shape[1] = rows;
+        src.nbytes = bytes;
+        src.data = m->staging;
+        src.layout = Q38CU_LAYOUT_GGUF;
+        Part part;
+        part.int_path = int_path;
+        part.rows = static_cast<int>(rows);
+        part.offset = p->rows;
+        if (int_path) {
+            if (!q38cu_tensor_repack(&part.t, &src, m->stream)) return fail("%s", q38cu_last_error());
+        } else {
+            void *dev = nullptr;
+            if (!cuda_ok(cudaMalloc(&dev, bytes + 256), "cudaMalloc")) return false;
+            if (!cuda_ok(cudaMemcpyAsync(dev, m->staging, bytes, cudaMemcpyDeviceToDevice, m->stream), "copy"))
+                return false;
+            part.t = src;
+            part.t.data = dev;
+        }
+        if (!cuda_ok(cudaStreamSynchronize(m->stream), "upload")) return false;
+        m->tensors.push_back(part.t);
+        p->parts.push_back(part);
+        p->rows += part.rows;
+        i = j;
+    }
+    return true;
+}
+
+bool upload_vec(Q38Model *m, float **dst, const q38::GGUFTensorInfo *t)
+{
+    if (!dalloc(dst, t->nbytes / 4, m->owned)) return false;
+    return cuda_ok(cudaMemcpy(*dst, t->data, t->nbytes, cudaMemcpyHostToDevice), "vector upload");
+}
+
+bool load_layer(Q38Model *m, const q38::GGUFFile &f, int l)
+{
+    Layer &L = m->layers[l];
+    L.full = (l + 1) % 4 == 0 || l == kLayers;
+    L.index = L.full ? l / 4 : l - (l + 1) / 4;
+    auto T = [&](const char *s) { return find_layer(f, l, s); };
+    const auto *attn_norm = T("attn_norm.weight"), *post_norm = T("post_attention_norm.weight");
+    const auto *gate = T("ffn_gate.weight"), *up = T("ffn_up.weight"), *down = T("ffn_down.weight");
+    bool ok = expect(attn_norm, kHidden, 0, true) && expect(post_norm, kHidden, 0, true) &&
+              expect(gate, kHidden, kFfn, false) && expect(up, kHidden, kFfn, false) &&
+              expect(down, kFfn, kHidden, false);
+    if (!ok) return false;
+    if (L.full) {
+        const auto *q = T("attn_q.weight"), *k = T("attn_k.weight"), *v = T("attn_v.weight");
+        const auto *o = T("attn_output.weight"), *qn = T("attn_q_norm.weight"), *kn = T("attn_k_norm.weight");
+        ok = expect(q, kHidden, kAttnQg, false) && expect(k, kHidden, kAttnKv, false) &&
+             expect(v, kHidden, kAttnKv, false) && expect(o, kAttnQ, kHidden, false) &&
+             expect(qn, kAttnDim, 0, true) && expect(kn, kAttnDim, 0, true);
+        if (!ok || !upload_proj(m, &L.in_proj, {q, k, v}) || !upload_proj(m, &L.out, {o}) ||
+            !upload_vec(m, &L.q_norm, qn) || !upload_vec(m, &L.k_norm, kn))
+            return false;
+    } else {
+        const auto *qkv = T("attn_qkv.weight"), *z = T("attn_gate.weight"), *al = T("ssm_alpha.weight");
+        const auto *be = T("ssm_beta.weight"), *conv = T("ssm_conv1d.weight"), *dt = T("ssm_dt.bias");
+        const auto *a = T("ssm_a"), *nrm = T("ssm_norm.weight"), *o = T("ssm_out.weight");
+        ok = expect(qkv, kHidden, kLinQkv, false) && expect(z, kHidden, kLinV, false) &&
+             expect(al, kHidden, kLinHeads, false) && expect(be, kHidden, kLinHeads, false) &&
+             expect(conv, 4, kLinQkv, true) && expect(dt, kLinHeads, 0, true) && expect(a, kLinHeads, 0, true) &&
+             expect(nrm, kLinDim, 0, true) && expect(o, kLinV, kHidden, false);
+        if (!ok || !upload_proj(m, &L.in_proj, {qkv, z}) || !upload_proj(m, &L.ba, {be, al}) ||
+            !upload_proj(m, &L.out, {o}) || !upload_vec(m, &L.conv_w, conv) || !upload_vec(m, &L.dt, dt) ||
+            !upload_vec(m, &L.a, a) || !upload_vec(m, &L.ssm_norm, nrm))
+            return false;
+    }
+    return upload_vec(m, &L.attn_norm, attn_norm) && upload_vec(m, &L.post_norm, post_norm) &&
+           upload_proj(m, &L.gate_up, {gate, up}) && upload_proj(m, &L.down, {down});
+}
+
+bool meta_is_qwen38(const q38::GGUFFile &f, uint32_t *blocks, uint32_t *nextn)
+{
+    auto u32 = [&](const char *k, uint32_t v) {
+        uint32_t x = 0;
+        return f.meta_u32(k, &x) && x == v;
+    };
+    return f.meta_u32("qwen35.block_count", blocks) && f.meta_u32("qwen35.nextn_predict_layers", nextn) &&
+           ((*blocks == kLayers && *nextn == 0) || (*blocks == kTotalLayers && *nextn == 1)) &&
+           f.meta_string_is("general.architecture", "qwen35") && u32("qwen35.embedding_length", kHidden) &&
+           u32("qwen35.feed_forward_length", kFfn) && u32("qwen35.attention.head_count", 24) &&
+           u32("qwen35.attention.head_count_kv", 4) && u32("qwen35.full_attention_interval", 4) &&
+           u32("qwen35.ssm.state_size", kLinDim) && u32("qwen35.ssm.group_count", 16) &&
+           u32("qwen35.ssm.time_step_rank", kLinHeads) && u32("qwen35.ssm.inner_size", kLinV);
+}
+
+bool upload_embedding(Q38Model *m, Q38CuTensor *dst, const q38::GGUFTensorInfo *t)
+{
+    if (!q38cu_tensor_upload(dst, t->type, t->shape[0], t->shape[1], t->data, Q38CU_LAYOUT_GGUF, m->stream))
+        return fail("%s", q38cu_last_error());
+    m->tensors.push_back(*dst);
+    return true;
+}
+
+bool load_mtp(Q38Model *m, const q38::GGUFFile &f)
+{
+    const auto *emb = f.find_tensor("token_embd.weight"), *out = f.find_tensor("output.weight");
+    const auto *eh = find_layer(f, kLayers, "nextn.eh_proj.weight");
+    const auto *en = find_layer(f, kLayers, "nextn.enorm.weight");
+    const auto *hn = find_layer(f, kLayers, "nextn.hnorm.weight");
+    const auto *sh = find_layer(f, kLayers, "nextn.shared_head_norm.weight");
+    if (!emb || !out || !expect(emb, kHidden, kVocab, false) || !expect(out, kHidden, kVocab, false) ||
+        !expect(eh, 2u * kHidden, kHidden, false) || !expect(en, kHidden, 0, true) || !expect(hn, kHidden, 0, true) ||
+        !expect(sh, kHidden, 0, true))
+        return false;
+    if (&f == &m->gguf) {
+        m->mtp_embedding = m->embedding;  // same tensors as the target model's
+        m->mtp_output = m->output;
+    } else if (!upload_embedding(m, &m->mtp_embedding, emb) || !upload_proj(m, &m->mtp_output, {out})) {
+        return false;
+    }
+    if (!load_layer(m, f, kLayers) || !upload_proj(m, &m->eh_proj, {eh}) || !upload_vec(m, &m->enorm, en) ||
+        !upload_vec(m, &m->hnorm, hn) || !upload_vec(m, &m->shared_head_norm, sh))
+        return false;
+    m->mtp_loaded = true;
+    return true;
+}
+
+bool alloc_runtime(Q38Model *m)
+{
+    auto &o = m->owned;
+    const size_t ctx = m->context_length;
+    m->wide_ld = std::max({kLinQkv + kLinV, kAttnQg + 2 * kAttnKv, 2 * kFfn});
+    m->ba_ld = 2 * kLinHeads;
+    m->attn_splits = std::max(6, static_cast<int>((ctx + q38::kAttnMaxChunk - 1) / q38::kAttnMaxChunk));
+    const size_t q8_blocks = kMaxTokens * static_cast<size_t>(kFfn / 256);
+    return dalloc(&m->conv_ring, static_cast<size_t>(kRecurrent) * kLinQkv * kConvRing, o) &&
+           dalloc(&m->delta_state, static_cast<size_t>(kRecurrent) * kLinHeads * kLinDim * kLinDim, o) &&
+           dalloc(&m->k_cache, kFull * ctx * kAttnKv, o) && dalloc(&m->v_cache, kFull * ctx * kAttnKv, o) &&
+           dalloc(&m->mtp_hidden, kHidden, o) && dalloc(&m->hidden, kMaxTokens * kHidden, o) &&
+           dalloc(&m->normf, kMaxTokens * 2 * kHidden, o) &&
+           dalloc(&m->wide, kMaxTokens * static_cast<size_t>(m->wide_ld), o) &&
+           dalloc(&m->ba, kMaxTokens * m->ba_ld, o) && dalloc(&m->act_f, kMaxTokens * kFfn, o) &&
+           dalloc(&m->logits, kMaxTokens * static_cast<size_t>(kVocab), o) &&
+           dalloc(reinterpret_cast<uint8_t **>(&m->q8), q8_blocks * sizeof(Q38CuQ8KBlock), o) &&
+           dalloc(&m->target_norm, kMaxDrafts * static_cast<size_t>(kHidden), o) &&
+           dalloc(&m->ctl, 4, o) && dalloc(&m->ids, kMaxTokens, o) && dalloc(&m->argmax_out, kMaxDrafts, o) &&
+           dalloc(&m->history, ctx + 1, o) &&
+           dalloc(&m->attn_partials, kMaxTokens * 24 * static_cast<size_t>(m->attn_splits) * (kAttnDim + 2), o) &&
+           dalloc(&m->attn_counters, kMaxTokens * 24, o) &&
+           dalloc(&m->argmax_part_v, kMaxTokens * q38::kArgmaxCtas, o) &&
+           dalloc(&m->argmax_part_i, kMaxTokens * q38::kArgmaxCtas, o) &&
+           dalloc(&m->argmax_counters, kMaxTokens, o) &&
+           cuda_ok(cudaMallocHost(&m->host_logits, kMaxTokens * static_cast<size_t>(kVocab) * sizeof(float)),
+                   "cudaMallocHost") &&
+           cuda_ok(cudaMallocHost(&m->host_ctl, 4 * sizeof(int)), "cudaMallocHost") &&
+           cuda_ok(cudaMallocHost(&m->host_ids, kMaxTokens * sizeof(uint32_t)), "cudaMallocHost");
+}
+
+// ---------------------------------------------------------------------------
+// the token step
+// ---------------------------------------------------------------------------
+// Stream GEMM with an output stride and optional accumulation.
+bool stream_project(const Part &p, const void *q8, int tokens, float *out, int out_ld, int accumulate,
+                    cudaStream_t s)
+{
+    const int width = static_cast<int>(p.t.shape[0]), nb = width / 256;
+    for (int tok0 = 0; tok0 < tokens;) {
+        q38::StreamPlan plan;
+        cudaError_t e = q38::stream_plan(static_cast<int>(p.t.type), p.rows, width, static_cast<int>(p.t.tile_rows),
+                                         tokens - tok0, &plan);
+        if (!cuda_ok(e, "stream plan")) return false;
+        q38::StreamLaunch l;
+        l.weights = p.t.data;
+        l.act = static_cast<const Q38CuQ8KBlock *>(q8) + static_cast<size_t>(tok0) * nb;
+        l.tokens = plan.token_group;
+        l.out = out + static_cast<size_t>(tok0) * out_ld;
+        l.scratch = p.t.scratch;
+        l.dbg_w = nullptr;
+        l.dbg_x = nullptr;
+        l.out_ld = out_ld;
+        l.accumulate = accumulate;
+        if (!cuda_ok(q38::launch_stream_gemm(static_cast<int>(p.t.type), plan, l, s), "stream gemm launch"))
+            return false;
+        tok0 += plan.token_group;
+    }
+    return true;
+}
+
+// out[tok * out_ld + part.offset + row] (+)= projection of this token's input
+bool project(const Proj &p, const void *q8, const float *fin, int fin_ld, int tokens, float *out, int out_ld,
+             int accumulate, cudaStream_t s)
+{
+    for (const Part &part : p.parts) {
+        if (part.int_path) {
+            if (!stream_project(part, q8, tokens, out + part.offset, out_ld, accumulate, s)) return false;
+        } else {
+            const uint32_t be = q38cu_block_elements(part.t.type), bb = q38cu_block_bytes(part.t.type);
+            if (!cuda_ok(q38::launch_f32_gemm_ex(out + part.offset, out_ld, accumulate, fin, fin_ld, tokens,
+                                                 part.t.shape[0], part.t.data, part.rows, 0,
+                                                 static_cast<int>(part.t.type), static_cast<int>(be),
+                                                 static_cast<int>(bb), s),
+                         "f32 gemm launch"))
+                return false;
+        }
+    }
+    return true;
+}
+
+bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
+{
+    (void)base_hint;
+    const Layer &L = m->layers[l];
+    const cudaStream_t s = m->stream;
+    if (!cuda_ok(q38::launch_rmsnorm_quant(m->hidden, kHidden, L.attn_norm, kHidden, tokens, m->normf, kHidden,
+                                           m->q8, s),
+                 "rmsnorm"))
+        return false;
+    if (!project(L.in_proj, m->q8, m->normf, kHidden, tokens, m->wide, m->wide_ld, 0, s)) return false;
+    if (L.full) {
+        q38::AttnArgs a{};
+        a.qkv = m->wide;
+        a.qkv_ld = m->wide_ld;
+        a.k_off = kAttnQg;
+        a.v_off = kAttnQg + kAttnKv;
+        a.q_norm = L.q_norm;
+        a.k_norm = L.k_norm;
+        a.k_cache = m->k_cache + static_cast<size_t>(L.index) * m->context_length * kAttnKv;
+        a.v_cache = m->v_cache + static_cast<size_t>(L.index) * m->context_length * kAttnKv;
+        a.ctl = m->ctl;
+        a.theta_scale = m->theta_scale;
+        a.tokens = tokens;
+        a.splits = m->attn_splits;
+        a.partials = m->attn_partials;
+        a.counters = m->attn_counters;
+        a.out_f = m->act_f;
+        a.out_q = m->q8;
+        if (!cuda_ok(q38::launch_attention(a, s), "attention")) return false;
+        if (!project(L.out, m->q8, m->act_f, kAttnQ, tokens, m->hidden, kHidden, 1, s)) return false;
+    } else {
+        if (!project(L.ba, m->q8, m->normf, kHidden, tokens, m->ba, m->ba_ld, 0, s)) return false;
+        q38::DeltaArgs d{};
+        d.qkvz = m->wide;
+        d.qkvz_ld = m->wide_ld;
+        d.z_off = kLinQkv;
+        d.beta = m->ba;
+        d.alpha = m->ba + kLinHeads;
+        d.ba_ld = m->ba_ld;
+        d.conv_w = L.conv_w;
+        d.conv_ring = m->conv_ring + static_cast<size_t>(L.index) * kLinQkv * kConvRing;
+        d.dt = L.dt;
+        d.a = L.a;
+        d.norm_w = L.ssm_norm;
+        d.state = m->delta_state + static_cast<size_t>(L.index) * kLinHeads * kLinDim * kLinDim;
+        d.ctl = m->ctl;
+        d.tokens = tokens;
+        d.out_f = m->act_f;
+        d.out_q = m->q8;
+        if (!cuda_ok(q38::launch_deltanet(d, s), "deltanet")) return false;
+        if (!project(L.out, m->q8, m->act_f, kLinV, tokens, m->hidden, kHidden, 1, s)) return false;
+    }
+    if (!cuda_ok(q38::launch_rmsnorm_quant(m->hidden, kHidden, L.post_norm, kHidden, tokens, m->normf, kHidden,
+                                           m->q8, s),
+                 "rmsnorm"))
+        return false;
+    if (!project(L.gate_up, m->q8, m->normf, kHidden, tokens, m->wide, m->wide_ld, 0, s)) return false;
+    if (!cuda_ok(q38::launch_swiglu_quant(m->wide, m->wide + kFfn, m->wide_ld, kFfn, tokens, m->act_f, m->q8, s),
+                 "swiglu"))
+        return false;
+    return project(L.down, m->q8, m->act_f, kFfn, tokens, m->hidden, kHidden, 1, s);
+}
+
+// Embedding rows of `tokens` ids held in device memory.
+bool enqueue_embed(Q38Model *m, const Q38CuTensor &emb, const uint32_t *d_ids, int tokens, float *out)
+{
+    const uint32_t be = q38cu_block_elements(emb.type), bb = q38cu_block_bytes(emb.type);
+    return cuda_ok(q38::launch_row_f32_indexed(out, emb.data, kHidden, 0, emb.shape[1], d_ids, tokens,
+                                               static_cast<int>(emb.type), static_cast<int>(be),
+                                               static_cast<int>(bb), m->stream),
+                   "embedding");
+}
+
+// Final norm + LM head + greedy argmax.  The normed hidden rows go to
+// `norm_out` (the MTP head's input); argmax results to argmax_out + out_at;
+// with `feed` the last token's argmax also feeds the control block.
+bool enqueue_head(Q38Model *m, const float *norm_w, const Proj &head, int tokens, float *norm_out, int out_at,
+                  bool feed, int advance)
+{
+    const cudaStream_t s = m->stream;
+    if (!cuda_ok(q38::launch_rmsnorm_quant(m->hidden, kHidden, norm_w, kHidden, tokens, norm_out, kHidden, m->q8, s),
+                 "rmsnorm"))
+        return false;
+    if (!project(head, m->q8, norm_out, kHidden, tokens, m->logits, kVocab, 0, s)) return false;
+    q38::ArgmaxArgs a{};
+    a.logits = m->logits;
+    a.ld = kVocab;
+    a.n = kVocab;
+    a.part_v = m->argmax_part_v;
+    a.part_i = m->argmax_part_i;
+    a.counters = m->argmax_counters;
+    a.out = m->argmax_out + out_at;
+    a.ctl = feed ? m->ctl : nullptr;
+    a.advance = advance;
+    a.history = m->history;
+    a.history_len = static_cast<int>(m->context_length);
+    return cuda_ok(q38::launch_argmax(a, tokens, s), "argmax");
+}
+
+// One decode step of the target model for the token in ctl[0] at ctl[1].
+bool enqueue_decode_step(Q38Model *m)
+{
+    if (!enqueue_embed(m, m->embedding, reinterpret_cast<const uint32_t *>(m->ctl), 1, m->hidden)) return false;
+    for (int l = 0; l < kLayers; ++l)
+        if (!enqueue_layer(m, l, 1, 0)) return false;
+    // the normed hidden is also the MTP head's next input (qwen38_model.c:1507-1509)
+    return enqueue_head(m, m->output_norm, m->output, 1, m->mtp_hidden, 0, true, 1);
+}
+
+bool set_ctl(Q38Model *m, uint32_t token, uint32_t position);
+
+// MTP head over `n` tokens whose ids are in d_ids (qwen38_model.c:1268-1294
+// for a batch, 1588-1612 for one token): its input is
+// [RMSNorm(embedding, enorm) | RMSNorm(previous normed hidden, hnorm)], the
+// previous hidden being the MTP state for the first token and the target's
+// normed hidden of the token before for the others (rows of `prev_rows`).
+// Leaves the MTP layer's output in m->hidden.
+bool enqueue_mtp_body(Q38Model *m, const uint32_t *d_ids, int n, const float *prev_rows)
+{
+    const cudaStream_t s = m->stream;
+    const int w2 = 2 * kHidden, nb2 = w2 / 256, nb = kHidden / 256;
+    Q38CuQ8KBlock *q8 = static_cast<Q38CuQ8KBlock *>(m->q8);
+    if (!enqueue_embed(m, m->mtp_embedding, d_ids, n, m->hidden)) return false;
+    bool ok = cuda_ok(q38::launch_rmsnorm_quant(m->hidden, kHidden, m->enorm, kHidden, n, m->normf, w2, q8, s, nb2),
+                      "rmsnorm") &&
+              cuda_ok(q38::launch_rmsnorm_quant(m->mtp_hidden, kHidden, m->hnorm, kHidden, 1, m->normf + kHidden, w2,
+                                                q8 + nb, s, nb2),
+                      "rmsnorm");
+    if (ok && n > 1)
+        ok = cuda_ok(q38::launch_rmsnorm_quant(prev_rows, kHidden, m->hnorm, kHidden, n - 1, m->normf + w2 + kHidden,
+                                               w2, q8 + nb2 + nb, s, nb2),
+                     "rmsnorm");
+    return ok && project(m->eh_proj, m->q8, m->normf, w2, n, m->hidden, kHidden, 0, s) &&
+           enqueue_layer(m, kLayers, n, 0);
+}
+
+// MTP catch-up of n verified tokens (ids in d_ids, normed target hidden rows
+// in target_rows): advances the MTP layer's KV cache and leaves the MTP state
+// at the last token's normed hidden.
+bool enqueue_mtp_catchup(Q38Model *m, const uint32_t *d_ids, int n, const float *target_rows)
+{
+    return enqueue_mtp_body(m, d_ids, n, target_rows) &&
+           cuda_ok(cudaMemcpyAsync(m->mtp_hidden, target_rows + static_cast<size_t>(n - 1) * kHidden,
+                                   kHidden * sizeof(float), cudaMemcpyDeviceToDevice, m->stream),
+                   "copy");
+}
+
+bool upload_ids(Q38Model *m, const uint32_t *tokens, int n, uint32_t position)
+{
+    std::memcpy(m->host_ids, tokens, n * sizeof(uint32_t));
+    return set_ctl(m, tokens[0], position) &&
+           cuda_ok(cudaMemcpyAsync(m->ids, m->host_ids, n * sizeof(uint32_t), cudaMemcpyHostToDevice, m->stream),
+                   "ids upload");
+}
+
+bool check_status(Q38Model *m);
+
+// Target model over `count` tokens from the current position, in chunks of
+// kMaxTokens (upstream q38_batch_target_eval, qwen38_model.c:1241-1266):
+// argmax of every token to argmax_host, logits of the last token to the host
+// buffer, normed hidden rows to m->target_norm.  count <= kMaxDrafts.
+bool target_eval(Q38Model *m, const uint32_t *tokens, uint32_t count, uint32_t *argmax_host)
+{
+    const uint32_t base = m->position;
+    int last_n = 0;
+    for (uint32_t c0 = 0; c0 < count; c0 += kMaxTokens) {
+        const int n = static_cast<int>(std::min<uint32_t>(kMaxTokens, count - c0));
+        bool ok = upload_ids(m, tokens + c0, n, base + c0) && enqueue_embed(m, m->embedding, m->ids, n, m->hidden);
+        for (int l = 0; ok && l < kLayers; ++l) ok = enqueue_layer(m, l, n, 0);
+        ok = ok && enqueue_head(m, m->output_norm, m->output, n, m->target_norm + static_cast<size_t>(c0) * kHidden,
+                                static_cast<int>(c0), false, 0);
+        if (!ok || !check_status(m)) return false;
+        last_n = n;
+    }
+    const bool ok =
+        cuda_ok(cudaMemcpyAsync(argmax_host, m->argmax_out, count * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                m->stream),
+                "argmax copy") &&
+        cuda_ok(cudaMemcpyAsync(m->host_logits, m->logits + static_cast<size_t>(last_n - 1) * kVocab,
+                                static_cast<size_t>(kVocab) * sizeof(float), cudaMemcpyDeviceToHost, m->stream),
+                "logits copy") &&
+        check_status(m);
+    if (ok) m->position = base + count;
+    return ok;
+}
+
+// MTP catch-up over `count` tokens starting at MTP position `base`, in chunks
+// (the target rows are m->target_norm, as target_eval left them).
+bool mtp_catchup(Q38Model *m, const uint32_t *tokens, uint32_t count, uint32_t base)
+{
+    for (uint32_t c0 = 0; c0 < count; c0 += kMaxTokens) {
+        const int n = static_cast<int>(std::min<uint32_t>(kMaxTokens, count - c0));
+        if (!upload_ids(m, tokens + c0, n, base + c0) ||
+            !enqueue_mtp_catchup(m, m->ids, n, m->target_norm + static_cast<size_t>(c0) * kHidden) ||
+            !check_status(m))
+            return false;
+    }
+    m->mtp_position = base + count;
+    return true;
+}
+
+// One MTP draft step for `token` at the MTP position; its argmax is left in
+// argmax_out[0] and its logits in m->logits.
+bool mtp_step(Q38Model *m, uint32_t token)
+{
+    if (!set_ctl(m, token, m->mtp_position) ||
+        !enqueue_mtp_body(m, reinterpret_cast<const uint32_t *>(m->ctl), 1, nullptr) ||
+        !enqueue_head(m, m->shared_head_norm, m->mtp_output, 1, m->mtp_hidden, 0, false, 0))
+        return false;
+    ++m->mtp_position;
+    return true;
+}
+
+size_t conv_ring_bytes() { return static_cast<size_t>(kRecurrent) * kLinQkv * kConvRing * sizeof(float); }
+size_t delta_state_bytes() { return static_cast<size_t>(kRecurrent) * kLinHeads * kLinDim * kLinDim * sizeof(float); }
+
+// qwen38_model.c:1200-1226
+bool checkpoint_state(Q38Model *m)
+{
+    const cudaStream_t s = m->stream;
+    m->ck_position = m->position;
+    m->ck_mtp_position = m->mtp_position;
+    return cuda_ok(cudaMemcpyAsync(m->ck_conv_ring, m->conv_ring, conv_ring_bytes(), cudaMemcpyDeviceToDevice, s),
+                   "checkpoint") &&
+           cuda_ok(cudaMemcpyAsync(m->ck_delta_state, m->delta_state, delta_state_bytes(), cudaMemcpyDeviceToDevice,
+                                   s),
+                   "checkpoint") &&
+           cuda_ok(cudaMemcpyAsync(m->ck_mtp_hidden, m->mtp_hidden, kHidden * sizeof(float), cudaMemcpyDeviceToDevice,
+                                   s),
+                   "checkpoint");
+}
+
+bool restore_target_state(Q38Model *m)
+{
+    const cudaStream_t s = m->stream;
+    m->position = m->ck_position;
+    return cuda_ok(cudaMemcpyAsync(m->conv_ring, m->ck_conv_ring, conv_ring_bytes(), cudaMemcpyDeviceToDevice, s),
+                   "restore") &&
+           cuda_ok(cudaMemcpyAsync(m->delta_state, m->ck_delta_state, delta_state_bytes(), cudaMemcpyDeviceToDevice,
+                                   s),
+                   "restore");
+}
+
+bool restore_mtp_state(Q38Model *m)
+{
+    m->mtp_position = m->ck_mtp_position;
+    return cuda_ok(cudaMemcpyAsync(m->mtp_hidden, m->ck_mtp_hidden, kHidden * sizeof(float), cudaMemcpyDeviceToDevice,
+                                   m->stream),
+                   "restore");
+}
+
+bool set_ctl(Q38Model *m, uint32_t token, uint32_t position)
+{
+    m->host_ctl[0] = static_cast<int>(token);
+    m->host_ctl[1] = static_cast<int>(position);
+    return cuda_ok(cudaMemcpyAsync(m->ctl, m->host_ctl, 2 * sizeof(int), cudaMemcpyHostToDevice, m->stream),
+                   "control upload");
+}
+
+bool build_decode_graph(Q38Model *m)
+{
+    if (m->decode_graph) return true;
+    cudaGraph_t graph = nullptr;
+    if (!cuda_ok(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "begin capture")) return false;
+    const bool ok = enqueue_decode_step(m);
+    const cudaError_t e = cudaStreamEndCapture(m->stream, &graph);
+    if (!ok || !cuda_ok(e, "end capture")) {
+        if (graph) cudaGraphDestroy(graph);
+        return false;
+    }
+    const cudaError_t ei = cudaGraphInstantiate(&m->decode_graph, graph, 0);
+    cudaGraphDestroy(graph);
+    return cuda_ok(ei, "graph instantiate");
+}
+
+bool check_status(Q38Model *m)
+{
+    if (!cuda_ok(cudaStreamSynchronize(m->stream), "step")) return false;
+    int a = 0, b = 0, c = 0;
+    if (!cuda_ok(q38::read_and_clear_model_status(&a), "status") ||
+        !cuda_ok(q38::read_and_clear_stream_status(&b), "status") ||
+        !cuda_ok(q38::read_and_clear_status(&c, m->stream), "status"))
+        return false;
+    if (a | b | c) return fail("a kernel reported status %s", std::to_string(a | b | c));
+    return true;
+}
+
+bool use_device(const Q38Model *m) { return cuda_ok(cudaSetDevice(m->device), "cudaSetDevice"); }
+
+}  // namespace
+
+extern "C" {
+
+Q38Model *q38_model_open_gguf(const char *path, uint32_t context_length)
+{
+    if (!path || context_length == 0) return nullptr;
+    Q38Model *m = new Q38Model();
+    m->context_length = context_length;
+    // the RoPE frequency step, evaluated by the host libm as upstream does
+    // (qwen38_model.c:699)
+    m->theta_scale = powf(10000000.0f, -2.0f / 64.0f);
+    uint32_t blocks = 0, nextn = 0;
+    bool ok = cuda_ok(cudaGetDevice(&m->device), "cudaGetDevice") &&
+              cuda_ok(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    if (ok && !m->gguf.open(path)) ok = fail("%s", m->gguf.error());
+    if (ok && !meta_is_qwen38(m->gguf, &blocks, &nextn)) ok = fail("checkpoint metadata is not Qwen3.8-27B%s");
+    if (ok) {
+        const auto *emb = m->gguf.find_tensor("token_embd.weight"), *on = m->gguf.find_tensor("output_norm.weight");
+        const auto *out = m->gguf.find_tensor("output.weight");
+        ok = emb && on && out && expect(emb, kHidden, kVocab, false) && expect(on, kHidden, 0, true) &&
+             expect(out, kHidden, kVocab, false);
+        if (!ok && !(emb && on && out)) fail("missing token_embd, output_norm or output tensor%s");
+        ok = ok && upload_embedding(m, &m->embedding, emb) && upload_vec(m, &m->output_norm, on) &&
+             upload_proj(m, &m->output, {out});
+    }
+    for (int l = 0; ok && l < kLayers; ++l) ok = load_layer(m, m->gguf, l);
+    if (ok && blocks == kTotalLayers && nextn == 1) ok = load_mtp(m, m->gguf);
+    ok = ok && alloc_runtime(m);
+    if (m->staging) {
+        cudaFree(m->staging);
+        m->staging = nullptr;
+        m->staging_bytes = 0;
+    }
+    if (!ok) {
+        q38_model_close(m);
+        return nullptr;
+    }
+    return m;
+}
+
+void q38_model_close(Q38Model *m)
+{
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->decode_graph) cudaGraphExecDestroy(m->decode_graph);
+    // tensors shared between the target and the MTP head are listed once
+    for (auto &t : m->tensors) q38cu_tensor_free(&t);
+    for (void *p : m->owned) cudaFree(p);
+    if (m->staging) cudaFree(m->staging);
+    if (m->host_logits) cudaFreeHost(m->host_logits);
+    if (m->host_ctl) cudaFreeHost(m->host_ctl);
+    if (m->host_ids) cudaFreeHost(m->host_ids);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+void q38_model_reset(Q38Model *m)
+{
+    if (!m || !use_device(m)) return;
+    const size_t ctx = m->context_length;
+    cudaMemsetAsync(m->conv_ring, 0, static_cast<size_t>(kRecurrent) * kLinQkv * kConvRing * 4, m->stream);
+    cudaMemsetAsync(m->delta_state, 0, static_cast<size_t>(kRecurrent) * kLinHeads * kLinDim * kLinDim * 4, m->stream);
+    cudaMemsetAsync(m->k_cache, 0, kFull * ctx * kAttnKv * 4, m->stream);
+    cudaMemsetAsync(m->v_cache, 0, kFull * ctx * kAttnKv * 4, m->stream);
+    cudaMemsetAsync(m->mtp_hidden, 0, kHidden * 4, m->stream);
+    cudaMemsetAsync(m->ctl, 0, 4 * sizeof(int), m->stream);
+    cudaStreamSynchronize(m->stream);
+    m->position = 0;
+    m->mtp_position = 0;
+}
+
+int q38_model_forward_token(Q38Model *m, uint32_t token_id, const float **logits)
+{
+    if (!m || !logits || token_id >= kVocab || m->position >= m->context_length) return 0;
+    if (!use_device(m) || !build_decode_graph(m)) return 0;
+    if (!set_ctl(m, token_id, m->position)) return 0;
+    if (!cuda_ok(cudaGraphLaunch(m->decode_graph, m->stream), "graph launch")) return 0;
+    if (!cuda_ok(cudaMemcpyAsync(m->host_logits, m->logits, static_cast<size_t>(kVocab) * sizeof(float),
+                                 cudaMemcpyDeviceToHost, m->stream),
+                 "logits copy"))
+        return 0;
+    if (!check_status(m)) return 0;
+    ++m->position;
+    *logits = m->host_logits;
+    return 1;
+}
+
+int q38_model_forward_token_layers(Q38Model *m, uint32_t token_id, uint32_t layer_count, float *hidden_out)
+{
+    if (!m || !hidden_out || token_id >= kVocab || layer_count > kLayers || m->position >= m->context_length)
+        return 0;
+    if (!use_device(m) || !set_ctl(m, token_id, m->position)) return 0;
+    bool ok = enqueue_embed(m, m->embedding, reinterpret_cast<const uint32_t *>(m->ctl), 1, m->hidden);
+    for (uint32_t l = 0; ok && l < layer_count; ++l) ok = enqueue_layer(m, static_cast<int>(l), 1, 0);
+    ok = ok && cuda_ok(cudaMemcpyAsync(hidden_out, m->hidden, kHidden * sizeof(float), cudaMemcpyDeviceToHost,
+                                       m->stream),
+                       "hidden copy");
+    if (!ok || !check_status(m)) return 0;
+    ++m->position;
+    return 1;
+}
+
+int q38_model_prefill(Q38Model *m, const uint32_t *tokens, uint32_t token_count, const float **logits)
+{
+    if (!m || !tokens || !token_count || !logits || token_count > m->context_length - m->position) return 0;
+    for (uint32_t i = 0; i < token_count; ++i)
+        if (tokens[i] >= kVocab) return 0;
+    if (!use_device(m)) return 0;
+    // Chunks of kMaxTokens tokens go through all layers in turn; the result is
+    // the upstream layer-major batch's (qwen38_model.c:1519-1560), since every
+    // token only depends on the tokens before it.
+    const uint32_t base = m->position;
+    const int nb = kHidden / 256;
+    for (uint32_t done = 0; done < token_count;) {
+        const int n = static_cast<int>(std::min<uint32_t>(kMaxTokens, token_count - done));
+        const bool last = done + n == token_count;
+        bool ok = upload_ids(m, tokens + done, n, base + done) && enqueue_embed(m, m->embedding, m->ids, n, m->hidden);
+        for (int l = 0; ok && l < kLayers; ++l) ok = enqueue_layer(m, l, n, 0);
+        if (ok && (last || m->mtp_enabled))
+            ok = cuda_ok(q38::launch_rmsnorm_quant(m->hidden, kHidden, m->output_norm, kHidden, n, m->target_norm,
+                                                   kHidden, m->q8, m->stream),
+                         "rmsnorm");
+        if (ok && last) {
+            // logits of the last token only
+            const Q38CuQ8KBlock *q8 = static_cast<const Q38CuQ8KBlock *>(m->q8) + static_cast<size_t>(n - 1) * nb;
+            ok = project(m->output, q8, m->target_norm + static_cast<size_t>(n - 1) * kHidden, kHidden, 1, m->logits,
+                         kVocab, 0, m->stream) &&
+                 cuda_ok(cudaMemcpyAsync(m->host_logits, m->logits, static_cast<size_t>(kVocab) * sizeof(float),
+                                         cudaMemcpyDeviceToHost, m->stream),
+                         "logits copy");
+        }
+        if (ok && m->mtp_enabled) ok = enqueue_mtp_catchup(m, m->ids, n, m->target_norm);
+        if (!ok || !check_status(m)) return 0;
+        done += static_cast<uint32_t>(n);
+    }
+    m->position = base + token_count;
+    if (m->mtp_enabled) m->mtp_position = base + token_count;
+    *logits = m->host_logits;
+    return 1;
+}
+
+int q38_model_attach_mtp_gguf(Q38Model *m, const char *path)
+{
+    if (!m || !path || m->position != 0 || m->mtp_position != 0 || m->mtp_enabled || m->mtp_loaded ||
+        m->mtp_gguf.is_open())
+        return 0;
+    if (!use_device(m)) return 0;
+    uint32_t v = 0;
+    bool ok = m->mtp_gguf.open(path);
+    if (!ok) fail("%s", m->mtp_gguf.error());
+    ok = ok && m->mtp_gguf.meta_string_is("general.architecture", "qwen35") &&
+         m->mtp_gguf.meta_u32("qwen35.block_count", &v) && v == kTotalLayers &&
+         m->mtp_gguf.meta_u32("qwen35.nextn_predict_layers", &v) && v == 1 &&
+         m->mtp_gguf.meta_u32("qwen35.embedding_length", &v) && v == kHidden &&
+         m->mtp_gguf.meta_u32("qwen35.feed_forward_length", &v) && v == kFfn;
+    if (!ok) {
+        if (m->mtp_gguf.is_open()) fail("MTP checkpoint metadata is not Qwen3.8-27B%s");
+        m->mtp_gguf.close();
+        return 0;
+    }
+    ok = load_mtp(m, m->mtp_gguf);
+    if (m->staging) {
+        cudaFree(m->staging);
+        m->staging = nullptr;
+        m->staging_bytes = 0;
+    }
+    if (!ok) {
+        m->mtp_loaded = false;
+        m->mtp_gguf.close();
+    }
+    return ok ? 1 : 0;
+}
+
+int q38_model_enable_mtp(Q38Model *m)
+{
+    if (!m || m->position != 0 || m->mtp_position != 0) return 0;
+    if (!m->mtp_loaded) return fail("MTP weights are unavailable; attach the MTP GGUF first%s");
+    if (!use_device(m)) return 0;
+    if (!m->ck_conv_ring &&
+        (!dalloc(reinterpret_cast<uint8_t **>(&m->ck_conv_ring), conv_ring_bytes(), m->owned) ||
+         !dalloc(reinterpret_cast<uint8_t **>(&m->ck_delta_state), delta_state_bytes(), m->owned) ||
+         !dalloc(&m->ck_mtp_hidden, kHidden, m->owned)))
+        return fail("unable to allocate speculative checkpoint%s");
+    m->mtp_enabled = true;
+    return 1;
+}
+
+int q38_model_mtp_forward(Q38Model *m, uint32_t token_id, const float **logits)
+{
+    if (!m || !m->mtp_enabled || !logits || token_id >= kVocab || m->mtp_position >= m->context_length) return 0;
+    if (!use_device(m) || !mtp_step(m, token_id)) return 0;
+    if (!cuda_ok(cudaMemcpyAsync(m->host_logits, m->logits, static_cast<size_t>(kVocab) * sizeof(float),
+                                 cudaMemcpyDeviceToHost, m->stream),
+                 "logits copy") ||
+        !check_status(m)) {
+        --m->mtp_position;
+        return 0;
+    }
+    *logits = m->host_logits;
+    return 1;
+}
+
+int q38_model_speculative_greedy(Q38Model *m, uint32_t token_id, uint32_t stop_token, uint32_t draft_count,
+                                 uint32_t *accepted_tokens, uint32_t *accepted_count, const float **next_logits)
+{
+    if (!m || !m->mtp_enabled || !accepted_tokens || !accepted_count || !next_logits || token_id >= kVocab ||
+        draft_count == 0 || m->position != m->mtp_position || draft_count > m->context_length - m->position)
+        return 0;
+    if (draft_count > kMaxDrafts) return fail("draft_count above %s is not supported", std::to_string(kMaxDrafts));
+    if (!use_device(m) || !checkpoint_state(m)) return 0;
+
+    // drafts from the MTP head, greedy (qwen38_model.c:1636-1650)
+    uint32_t drafts[kMaxDrafts], inputs[kMaxDrafts], target[kMaxDrafts];
+    uint32_t actual = 0, draft_input = token_id;
+    while (actual < draft_count) {
+        uint32_t next = 0;
+        if (!mtp_step(m, draft_input) ||
+            !cuda_ok(cudaMemcpyAsync(&m->host_ids[0], m->argmax_out, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                     m->stream),
+                     "argmax copy") ||
+            !check_status(m)) {
+            restore_mtp_state(m);
+            cudaStreamSynchronize(m->stream);
+            return 0;
+        }
+        next = m->host_ids[0];
+        drafts[actual++] = next;
+        draft_input = next;
+        if (next == stop_token) break;
+    }
+
+    // verify on the target model; replay the consumed prefix on a mismatch
+    inputs[0] = token_id;
+    for (uint32_t i = 1; i < actual; ++i) inputs[i] = drafts[i - 1];
+    bool ok = target_eval(m, inputs, actual, target);
+    uint32_t matched = 0, next = 0;
+    if (ok) {
+        while (matched < actual && target[matched] == drafts[matched]) ++matched;
+        next = matched < actual ? target[matched] : drafts[actual - 1];
+    }
+    const uint32_t consumed = matched < actual ? matched + 1 : actual;
+    if (ok && consumed < actual) ok = restore_target_state(m) && target_eval(m, inputs, consumed, target);
+    if (ok) ok = restore_mtp_state(m) && mtp_catchup(m, inputs, consumed, m->ck_mtp_position);
+    if (!ok) {
+        restore_target_state(m);
+        restore_mtp_state(m);
+        cudaStreamSynchronize(m->stream);
+        return 0;
+    }
+    for (uint32_t i = 0; i < matched; ++i) accepted_tokens[i] = drafts[i];
+    if (matched < actual) accepted_tokens[matched] = next;
+    *accepted_count = consumed;
+    *next_logits = m->host_logits;
+    return 1;
+}
+
+uint32_t q38_model_vocab_size(const Q38Model *m) { return m ? kVocab : 0; }
+uint32_t q38_model_position(const Q38Model *m) { return m ? m->position : 0; }
+uint32_t q38_model_context_length(const Q38Model *m) { return m ? m->context_length : 0; }
+
+int q38cu_model_generate_greedy(Q38Model *m, uint32_t token_id, uint32_t count, uint32_t *tokens_out)
+{
+    if (!m || !tokens_out || token_id >= kVocab || !count || count > m->context_length - m->position) return 0;
+    if (!use_device(m) || !build_decode_graph(m)) return 0;
+    m->host_ctl[2] = 0;
+    if (!set_ctl(m, token_id, m->position) ||
+        !cuda_ok(cudaMemcpyAsync(m->ctl + 2, m->host_ctl + 2, sizeof(int), cudaMemcpyHostToDevice, m->stream),
+                 "control upload"))
+        return 0;
+    for (uint32_t i = 0; i < count; ++i)
+        if (!cuda_ok(cudaGraphLaunch(m->decode_graph, m->stream), "graph launch")) return 0;
+    if (!cuda_ok(cudaMemcpyAsync(tokens_out, m->history, count * sizeof(uint32_t), cudaMemcpyDeviceToHost, m->stream),
+                 "token copy") ||
+        !check_status(m))
+        return 0;
+    m->position += count;
+    return 1;
+}
+
+void *q38cu_model_stream(Q38Model *m) { return m ? m->stream : nullptr; }
+
+}  // extern "C"

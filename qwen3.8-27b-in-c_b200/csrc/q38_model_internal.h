@@ -1,0 +1,73 @@
+// q38_model_internal.h - launch interfaces of the decode-step kernels
+// (q38_model_kernels.cu) used by the device model (q38_model.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace q38 {
+
+// Largest number of positions one attention CTA scores (shared memory bound);
+// the model picks splits >= context / kAttnMaxChunk.
+constexpr int kAttnMaxChunk = 2048;
+constexpr int kArgmaxCtas = 148;
+
+// The device control block every captured step reads: ctl[0] = input token
+// id, ctl[1] = position of the first token of the step, ctl[2] = number of
+// tokens appended to the greedy history.
+struct DeltaArgs {
+    const float *qkvz;  // per token: q | k | v (10240), z at z_off (6144)
+    int qkvz_ld, z_off;
+    const float *beta, *alpha;  // raw projections, per token at stride ba_ld
+    int ba_ld;
+    const float *conv_w;  // [10240][4]
+    float *conv_ring;     // [10240][16]
+    const float *dt, *a;  // [48]
+    const float *norm_w;  // [128]
+    float *state;         // [48][128][128], column-major per head
+    const int *ctl;
+    int tokens;
+    float *out_f;  // optional [tokens][6144]
+    void *out_q;   // [tokens][24] Q8_K
+};
+
+struct AttnArgs {
+    const float *qkv;  // per token: q|gate interleaved per head (12288), k at k_off, v at v_off
+    int qkv_ld, k_off, v_off;
+    const float *q_norm, *k_norm;  // [256]
+    float *k_cache, *v_cache;      // this layer's [context][1024]
+    const int *ctl;
+    float theta_scale;  // powf(1e7, -2 / 64), computed on the host as upstream
+    int tokens, splits;
+    float *partials;  // [tokens * 24 * splits][258]
+    int *counters;    // [tokens * 24], zero between launches
+    float *out_f;     // optional [tokens][6144]
+    void *out_q;      // [tokens][24] Q8_K
+};
+
+struct ArgmaxArgs {
+    const float *logits;
+    int ld, n;
+    float *part_v;  // [tokens][kArgmaxCtas]
+    int *part_i;
+    int *counters;  // [tokens], zero between launches
+    uint32_t *out;  // [tokens]
+    int *ctl;       // optional: fed with the last token's argmax
+    int advance;    // added to ctl[1]
+    uint32_t *history;
+    int history_len;  // appends stop at this many tokens
+};
+
+// RMSNorm of `tokens` rows of n floats, written as floats (out_f, optional)
+// and as Q8_K blocks (out_q, optional; q_ld blocks per token, 0 = n / 256).
+cudaError_t launch_rmsnorm_quant(const float *in, int in_ld, const float *weight, int n, int tokens, float *out_f,
+                                 int out_ld, void *out_q, cudaStream_t s, int q_ld = 0);
+cudaError_t launch_swiglu_quant(const float *gate, const float *up, int ld, int n, int tokens, float *out_f,
+                                void *out_q, cudaStream_t s);
+cudaError_t launch_add(float *out, const float *branch, int n, int tokens, cudaStream_t s);
+cudaError_t launch_deltanet(const DeltaArgs &args, cudaStream_t s);
+cudaError_t launch_attention(const AttnArgs &args, cudaStream_t s);
+cudaError_t launch_argmax(const ArgmaxArgs &args, int tokens, cudaStream_t s);
+cudaError_t read_and_clear_model_status(int *status);
+
+}  // namespace q38

@@ -1,0 +1,657 @@
+// q38_model_kernels.cu - the decode-step kernels around the weight-streaming
+// GEMV: norms and activation quantization, the Gated-DeltaNet mixer, full
+// attention over the KV cache, and greedy argmax.
+//
+// Every kernel here is launched with programmatic dependent launch: it calls
+// pdl_wait() before touching activations or state and lets its successor
+// start early.  Token ids and the position come from device memory (the
+// model's control block) so that one captured CUDA graph serves every step.
+//
+// Float semantics follow the upstream C compiled with -ffp-contract=off
+// (src/qwen38/qwen38_model.c): every product and sum is rounded separately
+// (__fmul_rn / __fadd_rn), except where the upstream itself uses fmaf or its
+// AVX2 FMA kernels.  Reductions run as trees rather than left to right, and
+// expf/logf/cosf/sinf are CUDA's (within 2 ulp of glibc's), so the results
+// agree with the upstream to rounding, not bit for bit.
+#include <cooperative_groups.h>
+#include <cuda_runtime.h>
+
+#include "q38_device.cuh"
+#include "q38_model_internal.h"
+#include "q38_types.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace q38 {
+
+__device__ int g_model_status;
+
+namespace {
+
+constexpr float kRmsEps = 1e-6f;
+
+__device__ __forceinline__ double warp_sum_d(double v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum_f(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float warp_max_f(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Sum of a double over the CTA (all threads get the result).  `red` holds one
+// double per warp; the warps' partials are added in warp order.
+__device__ double block_sum_d(double v, double *red)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    v = warp_sum_d(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    double t = 0.0;
+    for (int w = 0; w < warps; ++w) t += red[w];
+    return t;
+}
+
+__device__ float block_max_f(float v, float *red)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    v = warp_max_f(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = red[0];
+    for (int w = 1; w < warps; ++w) t = fmaxf(t, red[w]);
+    return t;
+}
+
+__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+__device__ __forceinline__ float sigmoid(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))); }
+__device__ __forceinline__ float softplus(float x) { return x > 20.0f ? x : logf(__fadd_rn(1.0f, expf(x))); }
+
+// upstream q38_nearest_int (qwen38_quant.c:42-48)
+__device__ __forceinline__ int nearest_int(float v)
+{
+    const float shifted = __fadd_rn(v, 12582912.0f);
+    return static_cast<int>(__float_as_uint(shifted) & 0x007fffffu) - 0x00400000;
+}
+
+// Largest |v| with the smallest index among equals: the element the upstream
+// quantizer's strict `>` scan keeps (qwen38_quant.c:58-65).
+struct AbsMax {
+    float a;
+    int i;
+    float v;
+};
+
+__device__ __forceinline__ AbsMax better(AbsMax x, AbsMax y)
+{
+    return (y.a > x.a || (y.a == x.a && y.i < x.i)) ? y : x;
+}
+
+__device__ __forceinline__ AbsMax warp_absmax(AbsMax m)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        AbsMax other;
+        other.a = __shfl_xor_sync(0xffffffffu, m.a, o);
+        other.i = __shfl_xor_sync(0xffffffffu, m.i, o);
+        other.v = __shfl_xor_sync(0xffffffffu, m.v, o);
+        m = better(m, other);
+    }
+    return m;
+}
+
+// Q8_K quantization of 256 values held one per thread by a 256-thread CTA
+// (qwen38_quant.c:50-88, bit-exact): thread i owns element i.
+__device__ void quantize_block_256(float v, Q8KBlock *dst, AbsMax *red)
+{
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    AbsMax m{fabsf(v), tid, v};
+    m = warp_absmax(m);
+    __syncthreads();
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    AbsMax best = red[0];
+    for (int w = 1; w < 8; ++w) best = better(best, red[w]);
+    int q = 0;
+    float inverse = 0.0f;
+    if (best.a != 0.0f) {
+        inverse = __fdiv_rn(-127.0f, best.v);
+        q = min(nearest_int(__fmul_rn(inverse, v)), 127);
+    }
+    reinterpret_cast<int8_t *>(dst->quants)[tid] = static_cast<int8_t>(q);
+    int sum = q;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if ((lane & 15) == 0) dst->sums[tid >> 4] = static_cast<int16_t>(sum);
+    if (tid == 0) dst->scale = best.a != 0.0f ? __fdiv_rn(1.0f, inverse) : 0.0f;
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm -> (float, Q8_K).  Grid (n / 256, tokens), 256 threads.
+// qwen38_model.c:426-435 (q38_rmsnorm) followed by q38_quantize_q8_k.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float *in, int in_ld, const float *weight, int n,
+                                                            float *out_f, int out_ld, Q8KBlock *out_q, int q_ld)
+{
+    __shared__ double red_d[8];
+    __shared__ AbsMax red_m[8];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int tok = blockIdx.y;
+    const float *x = in + static_cast<size_t>(tok) * in_ld;
+    double part = 0.0;
+    for (int i = threadIdx.x; i < n; i += 256) {
+        const float v = x[i];
+        part += static_cast<double>(__fmul_rn(v, v));
+    }
+    const double sum = block_sum_d(part, red_d);
+    const float mean = static_cast<float>(sum / static_cast<double>(n));
+    const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps)));
+    const int e = blockIdx.x * 256 + threadIdx.x;
+    const float v = __fmul_rn(__fmul_rn(x[e], scale), weight[e]);
+    if (out_f) out_f[static_cast<size_t>(tok) * out_ld + e] = v;
+    if (out_q) quantize_block_256(v, out_q + static_cast<size_t>(tok) * q_ld + blockIdx.x, red_m);
+}
+
+// ---------------------------------------------------------------------------
+// SwiGLU -> (float, Q8_K).  gate_up[tok] = [gate n | up n] at stride ld.
+// qwen38_model.c:523-541 (scalar q38_swiglu) followed by q38_quantize_q8_k.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) swiglu_quant_kernel(const float *gate, const float *up, int ld, int n,
+                                                           float *out_f, Q8KBlock *out_q)
+{
+    __shared__ AbsMax red_m[8];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int tok = blockIdx.y;
+    const int e = blockIdx.x * 256 + threadIdx.x;
+    const float g = gate[static_cast<size_t>(tok) * ld + e];
+    const float u = up[static_cast<size_t>(tok) * ld + e];
+    const float v = __fmul_rn(silu(g), u);
+    if (out_f) out_f[static_cast<size_t>(tok) * n + e] = v;
+    quantize_block_256(v, out_q + static_cast<size_t>(tok) * (n / 256) + blockIdx.x, red_m);
+}
+
+// ---------------------------------------------------------------------------
+// out[tok][i] += branch[tok][i]  (the residual add, for float-path projections)
+// ---------------------------------------------------------------------------
+__global__ void add_kernel(float *out, const float *branch, int n)
+{
+    pdl_wait();
+    pdl_launch_dependents();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t o = static_cast<size_t>(blockIdx.y) * n + i;
+    if (i < n) out[o] = __fadd_rn(out[o], branch[o]);
+}
+
+// ---------------------------------------------------------------------------
+// Gated-DeltaNet step (qwen38_model.c:715-792), one token after another for
+// `tokens` tokens at positions base .. base + tokens - 1.
+//
+// Grid: 24 clusters of 8 CTAs, 128 threads each.  Cluster c covers value
+// heads 2c and 2c + 1 (= Q8_K block c of the 6144-wide output); CTA rank r
+// covers head 2c + r / 4, value columns [32 (r % 4), 32 (r % 4) + 32).  Each
+// CTA recomputes the causal conv, SiLU and L2 norm of its key head's q and k
+// (key head = value head % 16), keeps its 32 columns of the 128 x 128 state
+// private, and exchanges through distributed shared memory only the per-head
+// sum of squares (the head RMSNorm) and the block's absolute maximum (Q8_K).
+//
+// Conv state is a 16-slot ring per channel: the input of position p lives in
+// slot p % 16.  Taps of positions before `base` come from the ring, taps of
+// this launch's tokens straight from their projections, and each channel's
+// ring is written by one CTA only (q/k channels by the quarter-0 CTA of value
+// heads 0..15).  A launch writes positions >= base and reads positions in
+// [base - 3, base), so with at most 8 tokens the two never share a slot.
+// ---------------------------------------------------------------------------
+constexpr int kDeltaCluster = 8;
+constexpr int kConvRing = 16;
+
+struct __align__(16) DeltaShared {
+    float q[128], k[128];
+    float v[32], o[32];
+    double red[4][2];
+    float beta, decay;
+    double head_part;   // exchanged: this CTA's sum of squares
+    AbsMax block_part;  // exchanged: this CTA's absolute maximum
+};
+
+__device__ __forceinline__ float conv_tap_input(const DeltaArgs &a, int ch, int p, int base)
+{
+    if (p >= base) return a.qkvz[static_cast<size_t>(p - base) * a.qkvz_ld + ch];
+    return a.conv_ring[static_cast<size_t>(ch) * kConvRing + (p & (kConvRing - 1))];
+}
+
+// One conv channel at position pos: ((s0 k0 + s1 k1) + s2 k2) + x k3, then SiLU.
+__device__ __forceinline__ float conv_silu(const DeltaArgs &a, int ch, int pos, int base)
+{
+    const float4 w = *reinterpret_cast<const float4 *>(a.conv_w + static_cast<size_t>(ch) * 4);
+    float v = __fmul_rn(conv_tap_input(a, ch, pos - 3, base), w.x);
+    v = __fadd_rn(v, __fmul_rn(conv_tap_input(a, ch, pos - 2, base), w.y));
+    v = __fadd_rn(v, __fmul_rn(conv_tap_input(a, ch, pos - 1, base), w.z));
+    v = __fadd_rn(v, __fmul_rn(conv_tap_input(a, ch, pos, base), w.w));
+    return silu(v);
+}
+
+__global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
+    deltanet_kernel(DeltaArgs a)
+{
+    __shared__ DeltaShared sh;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int rank = static_cast<int>(cluster.block_rank());
+    const int cidx = blockIdx.x / kDeltaCluster;
+    const int vh = 2 * cidx + rank / 4, quarter = rank & 3, kh = vh % 16;
+    const int col0 = quarter * 32;
+    const bool qk_writer = vh < 16 && quarter == 0;
+
+    pdl_wait();
+    pdl_launch_dependents();
+    const int base = a.ctl[1];
+    float *state = a.state + (static_cast<size_t>(vh) * 128 + col0 + warp * 8) * 128 + lane * 4;
+
+    for (int t = 0; t < a.tokens; ++t) {
+        const int pos = base + t;
+        // state columns of this warp (8 x 128 floats; lane holds 4 of each)
+        float4 s[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s[j] = *reinterpret_cast<const float4 *>(state + j * 128);
+
+        // causal conv + SiLU of q, k (all 128 channels of the key head) and v
+        const int ch_q = kh * 128 + tid, ch_k = 2048 + kh * 128 + tid;
+        const float qv = conv_silu(a, ch_q, pos, base);
+        const float kv = conv_silu(a, ch_k, pos, base);
+        if (tid < 32) sh.v[tid] = conv_silu(a, 4096 + vh * 128 + col0 + tid, pos, base);
+        if (qk_writer) {
+            a.conv_ring[static_cast<size_t>(ch_q) * kConvRing + (pos & (kConvRing - 1))] =
+                a.qkvz[static_cast<size_t>(t) * a.qkvz_ld + ch_q];
+            a.conv_ring[static_cast<size_t>(ch_k) * kConvRing + (pos & (kConvRing - 1))] =
+                a.qkvz[static_cast<size_t>(t) * a.qkvz_ld + ch_k];
+        }
+        if (tid < 32) {
+            const int ch_v = 4096 + vh * 128 + col0 + tid;
+            a.conv_ring[static_cast<size_t>(ch_v) * kConvRing + (pos & (kConvRing - 1))] =
+                a.qkvz[static_cast<size_t>(t) * a.qkvz_ld + ch_v];
+        }
+
+        // L2 norms of q and k (qwen38_model.c:608-614)
+        double pq = warp_sum_d(static_cast<double>(__fmul_rn(qv, qv)));
+        double pk = warp_sum_d(static_cast<double>(__fmul_rn(kv, kv)));
+        if (lane == 0) {
+            sh.red[warp][0] = pq;
+            sh.red[warp][1] = pk;
+        }
+        if (tid == 0) {
+            const size_t bo = static_cast<size_t>(t) * a.ba_ld + vh;
+            const float beta = sigmoid(a.beta[bo]);
+            const float alpha = __fmul_rn(a.a[vh], softplus(__fadd_rn(a.alpha[bo], a.dt[vh])));
+            sh.beta = beta;
+            sh.decay = expf(alpha);
+        }
+        __syncthreads();
+        double sq = 0.0, sk = 0.0;
+        for (int w = 0; w < 4; ++w) {
+            sq += sh.red[w][0];
+            sk += sh.red[w][1];
+        }
+        const float scale_q = __fdiv_rn(1.0f, fmaxf(sqrtf(static_cast<float>(sq)), kRmsEps));
+        const float scale_k = __fdiv_rn(1.0f, fmaxf(sqrtf(static_cast<float>(sk)), kRmsEps));
+        sh.q[tid] = __fmul_rn(qv, scale_q);
+        sh.k[tid] = __fmul_rn(kv, scale_k);
+        __syncthreads();
+
+        // delta rule on this warp's 8 columns (qwen38_model.c:758-781)
+        const float4 k4 = *reinterpret_cast<const float4 *>(&sh.k[lane * 4]);
+        const float4 q4 = *reinterpret_cast<const float4 *>(&sh.q[lane * 4]);
+        const float decay = sh.decay, beta = sh.beta;
+        const float query_scale = __fdiv_rn(1.0f, sqrtf(128.0f));
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float4 x = s[j];
+            x.x = __fmul_rn(x.x, decay);
+            x.y = __fmul_rn(x.y, decay);
+            x.z = __fmul_rn(x.z, decay);
+            x.w = __fmul_rn(x.w, decay);
+            const float pred = warp_sum_f(fmaf(x.w, k4.w, fmaf(x.z, k4.z, fmaf(x.y, k4.y, __fmul_rn(x.x, k4.x)))));
+            const int col = warp * 8 + j;
+            const float delta = __fmul_rn(__fsub_rn(sh.v[col], pred), beta);
+            x.x = fmaf(k4.x, delta, x.x);
+            x.y = fmaf(k4.y, delta, x.y);
+            x.z = fmaf(k4.z, delta, x.z);
+            x.w = fmaf(k4.w, delta, x.w);
+            const float r = warp_sum_f(fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, __fmul_rn(x.x, q4.x)))));
+            *reinterpret_cast<float4 *>(state + j * 128) = x;
+            if (lane == 0) sh.o[col] = __fmul_rn(r, query_scale);
+        }
+        __syncthreads();
+
+        // head RMSNorm across the head's 4 CTAs (qwen38_model.c:783-789)
+        float o = 0.0f;
+        if (tid < 32) {
+            o = sh.o[tid];
+            const double p = warp_sum_d(static_cast<double>(__fmul_rn(o, o)));
+            if (tid == 0) sh.head_part = p;
+        }
+        cluster.sync();
+        if (tid < 32) {
+            double sum = 0.0;
+            for (int r = (rank & ~3); r < (rank & ~3) + 4; ++r) sum += cluster.map_shared_rank(&sh, r)->head_part;
+            const float mean = static_cast<float>(sum / 128.0);
+            const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps)));
+            const int col = col0 + tid;
+            o = __fmul_rn(__fmul_rn(o, scale), a.norm_w[col]);
+            const float z = a.qkvz[static_cast<size_t>(t) * a.qkvz_ld + a.z_off + vh * 128 + col];
+            o = __fmul_rn(o, silu(z));
+            if (a.out_f) a.out_f[static_cast<size_t>(t) * 6144 + vh * 128 + col] = o;
+            const int e = (rank / 4) * 128 + col;  // index inside the Q8_K block
+            AbsMax m = warp_absmax(AbsMax{fabsf(o), e, o});
+            if (tid == 0) sh.block_part = m;
+        }
+        cluster.sync();
+        if (tid < 32) {
+            AbsMax best = cluster.map_shared_rank(&sh, 0)->block_part;
+            for (int r = 1; r < kDeltaCluster; ++r) best = better(best, cluster.map_shared_rank(&sh, r)->block_part);
+            Q8KBlock *dst = static_cast<Q8KBlock *>(a.out_q) + static_cast<size_t>(t) * 24 + cidx;
+            int q = 0;
+            float inverse = 0.0f;
+            if (best.a != 0.0f) {
+                inverse = __fdiv_rn(-127.0f, best.v);
+                q = min(nearest_int(__fmul_rn(inverse, o)), 127);
+            }
+            const int e = (rank / 4) * 128 + col0 + tid;
+            reinterpret_cast<int8_t *>(dst->quants)[e] = static_cast<int8_t>(q);
+            int sum = q;
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            if ((tid & 15) == 0) dst->sums[e >> 4] = static_cast<int16_t>(sum);
+            if (rank == 0 && tid == 0) dst->scale = best.a != 0.0f ? __fdiv_rn(1.0f, inverse) : 0.0f;
+        }
+    }
+    cluster.sync();  // peers may still read this CTA's exchange slots
+}
+
+// ---------------------------------------------------------------------------
+// Full attention (qwen38_model.c:697-713, 816-885) for `tokens` tokens at
+// positions base .. base + tokens - 1.
+//
+// Grid: tokens x 24 heads x `splits` CTAs of 256 threads; thread d owns head
+// dimension d.  CTA (t, h, s) normalizes and rotates its query, scores the
+// positions of split s of [0, base + t], and leaves (max, sum, weighted V) in
+// the scratch; the last CTA of (t, h) to finish merges the splits, applies
+// the sigmoid gate and quantizes the head (one Q8_K block per head).
+// Keys and values of this launch's own tokens are recomputed where needed
+// rather than read back from the cache; CTA (t, 6g, 0) writes token t's key
+// and value rows of KV head g into the cache, which no CTA of the launch reads.
+// ---------------------------------------------------------------------------
+constexpr int kAttnHeads = 24, kAttnDim = 256, kMaxTokens = 8;
+
+struct AttnShared {
+    float q[kAttnDim];
+    float knew[kMaxTokens][kAttnDim];
+    float vnew[kMaxTokens][kAttnDim];
+    float scores[kAttnMaxChunk];
+    double red_d[8];
+    float red_f[8];
+    AbsMax red_m[8];
+    int last;
+};
+
+// Normalize (RMSNorm with `norm`) and rotate (first 64 dims, pairs (j, j + 32))
+// one 256-wide head vector held one element per thread; returns the result.
+__device__ float norm_rope(float x, const float *norm, int pos, float theta_scale, float *tmp, double *red)
+{
+    const int d = threadIdx.x;
+    const double sum = block_sum_d(static_cast<double>(__fmul_rn(x, x)), red);
+    const float mean = static_cast<float>(sum / 256.0);
+    const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps)));
+    const float v = __fmul_rn(__fmul_rn(x, scale), norm[d]);
+    __syncthreads();
+    tmp[d] = v;
+    __syncthreads();
+    if (d >= 64) return v;
+    const int j = d & 31;
+    float theta = static_cast<float>(pos);
+    for (int i = 0; i < j; ++i) theta = __fmul_rn(theta, theta_scale);
+    const float c = cosf(theta), sn = sinf(theta);
+    const float x0 = tmp[j], x1 = tmp[j + 32];
+    return d < 32 ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+}
+
+__global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
+{
+    __shared__ AttnShared sh;
+    const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
+    const int split = blockIdx.x % a.splits;
+    const int th = blockIdx.x / a.splits;
+    const int h = th % kAttnHeads, t = th / kAttnHeads;
+    const int g = h / (kAttnHeads / 4);
+
+    pdl_wait();
+    pdl_launch_dependents();
+    const int base = a.ctl[1];
+    const int pos = base + t, len = pos + 1;
+    const int chunk = (len + a.splits - 1) / a.splits;
+    const int p0 = min(len, split * chunk), p1 = min(len, p0 + chunk);
+    const float *row = a.qkv + static_cast<size_t>(t) * a.qkv_ld;
+
+    // query: RMSNorm + RoPE
+    const float q = norm_rope(row[h * 512 + d], a.q_norm, pos, a.theta_scale, sh.scores, sh.red_d);
+    __syncthreads();
+    sh.q[d] = q;
+
+    // keys/values of this launch's tokens that fall in [p0, p1), and the
+    // cache rows of token t (written by one CTA per KV head)
+    const bool writer = (h % (kAttnHeads / 4)) == 0 && split == 0;
+    for (int tt = 0; tt <= t; ++tt) {
+        const int pp = base + tt;
+        const bool needed = pp >= p0 && pp < p1;
+        if (!needed && !(writer && tt == t)) continue;
+        const float *r2 = a.qkv + static_cast<size_t>(tt) * a.qkv_ld;
+        __syncthreads();
+        const float kx = norm_rope(r2[a.k_off + g * 256 + d], a.k_norm, pp, a.theta_scale, sh.scores, sh.red_d);
+        const float vx = r2[a.v_off + g * 256 + d];
+        sh.knew[tt][d] = kx;
+        sh.vnew[tt][d] = vx;
+        if (writer && tt == t) {
+            a.k_cache[static_cast<size_t>(pp) * 1024 + g * 256 + d] = kx;
+            a.v_cache[static_cast<size_t>(pp) * 1024 + g * 256 + d] = vx;
+        }
+    }
+    __syncthreads();
+
+    // scores of positions [p0, p1): warp w takes p0 + w, p0 + w + 8, ...
+    const float4 qa = *reinterpret_cast<const float4 *>(&sh.q[lane * 4]);
+    const float4 qb = *reinterpret_cast<const float4 *>(&sh.q[128 + lane * 4]);
+    float local_max = -INFINITY;
+    for (int p = p0 + warp; p < p1; p += 8) {
+        const float *k = p < base ? a.k_cache + static_cast<size_t>(p) * 1024 + g * 256 : sh.knew[p - base];
+        const float4 ka = *reinterpret_cast<const float4 *>(k + lane * 4);
+        const float4 kb = *reinterpret_cast<const float4 *>(k + 128 + lane * 4);
+        float part = fmaf(qa.x, ka.x, fmaf(qa.y, ka.y, fmaf(qa.z, ka.z, __fmul_rn(qa.w, ka.w))));
+        part = fmaf(qb.x, kb.x, fmaf(qb.y, kb.y, fmaf(qb.z, kb.z, fmaf(qb.w, kb.w, part))));
+        const float score = __fmul_rn(warp_sum_f(part), 0.0625f);  // 1 / sqrt(256)
+        if (lane == 0) sh.scores[p - p0] = score;
+        local_max = fmaxf(local_max, score);
+    }
+    const float m = block_max_f(local_max, sh.red_f);  // includes the barrier for sh.scores
+    float l_part = 0.0f;
+    for (int i = d; i < p1 - p0; i += 256) {
+        const float e = expf(__fsub_rn(sh.scores[i], m));
+        sh.scores[i] = e;
+        l_part = __fadd_rn(l_part, e);
+    }
+    __syncthreads();
+    const double l = block_sum_d(static_cast<double>(l_part), sh.red_d);
+    float acc = 0.0f;
+    for (int p = p0; p < p1; ++p) {
+        const float v = p < base ? a.v_cache[static_cast<size_t>(p) * 1024 + g * 256 + d] : sh.vnew[p - base][d];
+        acc = fmaf(sh.scores[p - p0], v, acc);
+    }
+
+    // leave this split's partial result; the last CTA of (t, h) merges
+    float *part = a.partials + static_cast<size_t>(blockIdx.x) * (kAttnDim + 2);
+    part[2 + d] = acc;
+    if (d == 0) {
+        part[0] = p1 > p0 ? m : -INFINITY;
+        part[1] = static_cast<float>(l);
+    }
+    __threadfence();
+    __syncthreads();
+    if (d == 0) sh.last = atomicAdd(&a.counters[th], 1) == a.splits - 1;
+    __syncthreads();
+    if (!sh.last) return;
+    __threadfence();
+    const float *parts = a.partials + static_cast<size_t>(th) * a.splits * (kAttnDim + 2);
+    float mx = -INFINITY;
+    for (int s = 0; s < a.splits; ++s) mx = fmaxf(mx, __ldcg(parts + s * (kAttnDim + 2)));
+    float den = 0.0f, num = 0.0f;
+    for (int s = 0; s < a.splits; ++s) {
+        const float ms = __ldcg(parts + s * (kAttnDim + 2));
+        if (ms == -INFINITY) continue;
+        const float w = expf(__fsub_rn(ms, mx));
+        den = fmaf(__ldcg(parts + s * (kAttnDim + 2) + 1), w, den);
+        num = fmaf(__ldcg(parts + s * (kAttnDim + 2) + 2 + d), w, num);
+    }
+    float o = __fdiv_rn(num, den);
+    o = __fmul_rn(o, sigmoid(row[h * 512 + 256 + d]));
+    if (a.out_f) a.out_f[static_cast<size_t>(t) * 6144 + h * 256 + d] = o;
+    quantize_block_256(o, static_cast<Q8KBlock *>(a.out_q) + static_cast<size_t>(t) * 24 + h, sh.red_m);
+    if (d == 0) a.counters[th] = 0;
+}
+
+// ---------------------------------------------------------------------------
+// Greedy argmax over each token's logits (upstream q38_argmax: the first index
+// of the maximum, qwen38_model.c:1228-1239).  Grid (kArgmaxCtas, tokens); the
+// last CTA of a token merges the CTA results in order and, for the last token
+// of the launch, feeds the control block: ctl[0] = token, ctl[1] += tokens,
+// history[ctl[2]++] = token.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) argmax_kernel(ArgmaxArgs a)
+{
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    __shared__ int last;
+    pdl_wait();
+    pdl_launch_dependents();
+    const int tok = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float *x = a.logits + static_cast<size_t>(tok) * a.ld;
+    const int per = (a.n + gridDim.x - 1) / gridDim.x;
+    const int i0 = blockIdx.x * per, i1 = min(a.n, i0 + per);
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = i0 + tid; i < i1; i += 256) {
+        const float v = x[i];
+        if (v > best) { best = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < 8; ++w)
+            if (sv[w] > best || (sv[w] == best && si[w] < bi)) { best = sv[w]; bi = si[w]; }
+        a.part_v[tok * gridDim.x + blockIdx.x] = best;
+        a.part_i[tok * gridDim.x + blockIdx.x] = bi;
+        __threadfence();
+        last = atomicAdd(&a.counters[tok], 1) == static_cast<int>(gridDim.x) - 1;
+    }
+    __syncthreads();
+    if (!last || tid != 0) return;
+    __threadfence();
+    float bv = __ldcg(&a.part_v[tok * gridDim.x]);
+    int bidx = __ldcg(&a.part_i[tok * gridDim.x]);
+    for (unsigned c = 1; c < gridDim.x; ++c) {
+        const float v = __ldcg(&a.part_v[tok * gridDim.x + c]);
+        if (v > bv) { bv = v; bidx = __ldcg(&a.part_i[tok * gridDim.x + c]); }
+    }
+    if (bidx == 0x7fffffff) bidx = 0;  // all NaN / -inf: the upstream scan keeps index 0
+    a.out[tok] = static_cast<uint32_t>(bidx);
+    a.counters[tok] = 0;
+    if (a.ctl && tok == static_cast<int>(gridDim.y) - 1) {
+        a.ctl[0] = bidx;
+        a.ctl[1] += a.advance;
+        if (a.history && a.ctl[2] >= 0 && a.ctl[2] < a.history_len) a.history[a.ctl[2]++] = static_cast<uint32_t>(bidx);
+    }
+}
+
+template <typename Kernel, typename... Args>
+cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, cudaStream_t s, Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+}  // namespace
+
+cudaError_t launch_rmsnorm_quant(const float *in, int in_ld, const float *weight, int n, int tokens, float *out_f,
+                                 int out_ld, void *out_q, cudaStream_t s, int q_ld)
+{
+    if (n % 256) return cudaErrorInvalidValue;
+    return launch_pdl(rmsnorm_quant_kernel, dim3(n / 256, tokens), dim3(256), s, in, in_ld, weight, n, out_f, out_ld,
+                      static_cast<Q8KBlock *>(out_q), q_ld ? q_ld : n / 256);
+}
+
+cudaError_t launch_swiglu_quant(const float *gate, const float *up, int ld, int n, int tokens, float *out_f,
+                                void *out_q, cudaStream_t s)
+{
+    if (n % 256) return cudaErrorInvalidValue;
+    return launch_pdl(swiglu_quant_kernel, dim3(n / 256, tokens), dim3(256), s, gate, up, ld, n, out_f,
+                      static_cast<Q8KBlock *>(out_q));
+}
+
+cudaError_t launch_add(float *out, const float *branch, int n, int tokens, cudaStream_t s)
+{
+    return launch_pdl(add_kernel, dim3((n + 255) / 256, tokens), dim3(256), s, out, branch, n);
+}
+
+cudaError_t launch_deltanet(const DeltaArgs &args, cudaStream_t s)
+{
+    if (args.tokens < 1 || args.tokens > kMaxTokens) return cudaErrorInvalidValue;
+    return launch_pdl(deltanet_kernel, dim3(24 * kDeltaCluster), dim3(128), s, args);
+}
+
+cudaError_t launch_attention(const AttnArgs &args, cudaStream_t s)
+{
+    if (args.tokens < 1 || args.tokens > kMaxTokens || args.splits < 1) return cudaErrorInvalidValue;
+    return launch_pdl(attention_kernel, dim3(args.tokens * kAttnHeads * args.splits), dim3(256), s, args);
+}
+
+cudaError_t launch_argmax(const ArgmaxArgs &args, int tokens, cudaStream_t s)
+{
+    return launch_pdl(argmax_kernel, dim3(kArgmaxCtas, tokens), dim3(256), s, args);
+}
+
+cudaError_t read_and_clear_model_status(int *status)
+{
+    cudaError_t e = cudaMemcpyFromSymbol(status, g_model_status, sizeof(int));
+    if (e != cudaSuccess) return e;
+    const int zero = 0;
+    return cudaMemcpyToSymbol(g_model_status, &zero, sizeof(int));
+}
+
+}  // namespace q38

@@ -71,13 +71,23 @@ struct StreamArgs {
     uint32_t stage_bytes;
     const Q8KBlock *act;  // [tokens][nb]
     int tokens;
-    float *out;           // out[tok * rows + row]
+    float *out;           // out[tok * out_ld + row]
+    int out_ld;
+    int accumulate;       // 1: out += result (the residual add of the caller)
     float *partials;
     int *counters;
     int max_slots;
     int32_t *dbg_w;       // optional [tokens][rows][nb]
     int32_t *dbg_x;
 };
+
+// Final store of one output row; with `accumulate` the value is added to what
+// the row holds (one rounding, as `hidden[i] += branch[i]` upstream).
+__device__ __forceinline__ void store_row(const StreamArgs &g, int tok, int row, float v)
+{
+    float *dst = g.out + static_cast<size_t>(tok) * g.out_ld + row;
+    *dst = g.accumulate ? __fadd_rn(*dst, v) : v;
+}
 
 __host__ __device__ __forceinline__ int cta_of_unit(long long u, long long units, int grid)
 {
@@ -329,7 +339,7 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
             if (grp == 0 && !failed && mine_row && row < g.rows) {
 #pragma unroll
                 for (int tok = 0; tok < MT; ++tok)
-                    if (tok < g.tokens) g.out[static_cast<size_t>(tok) * g.rows + row] = total[tok];
+                    if (tok < g.tokens) store_row(g, tok, row, total[tok]);
             }
         } else {
             // The tile is shared with other CTAs: deposit this segment's sums;
@@ -356,7 +366,7 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
                     float sum = 0.0f;
                     for (int k = 0; k < n_dep; ++k)
                         sum += __ldcg(base + (static_cast<size_t>(k) * MT + tok) * g.tile_rows + rt);
-                    if (row < g.rows) g.out[static_cast<size_t>(tok) * g.rows + row] = sum;
+                    if (row < g.rows) store_row(g, tok, row, sum);
                 }
             }
             if (*last_flag && tid == 0) atomicExch(&g.counters[t], 0);
@@ -541,6 +551,8 @@ cudaError_t launch_t(const StreamPlan &p, const StreamLaunch &l, cudaStream_t st
     g.act = static_cast<const Q8KBlock *>(l.act);
     g.tokens = l.tokens;
     g.out = l.out;
+    g.out_ld = l.out_ld ? l.out_ld : p.rows;
+    g.accumulate = l.accumulate;
     g.counters = static_cast<int *>(l.scratch);
     g.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(l.scratch) + p.counter_bytes);
     g.max_slots = p.max_slots;

@@ -2,7 +2,11 @@
 benchmark configurations (no checkpoint or dataset is available offline).
 
 * K-quants (Q4_K, Q5_K, Q2_K): fp16 d and dmin ~ |N(0, 0.01)|, packed 6-bit
-  scale/min bytes uniform, quant bytes uniform.
+  scale/min bytes uniform, quant bytes uniform.  With centered=True, Q4_K
+  sub-block mins equal their scales and dmin = 7.5 d, so every sub-block is
+  d*sc*(q - 7.5): zero-mean weights, as trained checkpoints have (the uniform
+  draw gives every row a positive mean, and a random model built from it
+  answers every token with the same logits).
 * Q6_K / Q3_K: quant and high-bit bytes uniform, int8 scales uniform, fp16
   d ~ |N(0, 0.01)|.
 * Q8_0: fp16 d ~ |N(0, 0.01)|, int8 quants uniform.
@@ -44,7 +48,24 @@ def half_scales(rng, shape, sigma=0.01):
     return np.abs(rng.normal(0.0, sigma, size=shape)).astype(np.float16).view(np.uint16)
 
 
-def quant_tensor(qtype, rows, width, seed, sigma=0.01):
+def _center_q4_k(rng, data, sigma):
+    """Q4_K blocks with min_j = scale_j and dmin = 7.5 d (packing as
+    ggml-common.h block_q4_K / get_scale_min_k4)."""
+    rows, nblocks = data.shape[:2]
+    d = np.abs(rng.normal(0.0, sigma, size=(rows, nblocks))).astype(np.float16)
+    dmin = (d.astype(np.float32) * 7.5).astype(np.float16)
+    sc = rng.integers(0, 64, size=(rows, nblocks, 8), dtype=np.uint8)
+    packed = np.empty((rows, nblocks, 12), np.uint8)
+    for j in range(4):
+        packed[:, :, j] = sc[:, :, j] | ((sc[:, :, j + 4] >> 4) << 6)
+        packed[:, :, j + 4] = sc[:, :, j] | ((sc[:, :, j + 4] >> 4) << 6)
+        packed[:, :, j + 8] = (sc[:, :, j + 4] & 0xF) | ((sc[:, :, j + 4] & 0xF) << 4)
+    data[:, :, 0:2] = d.view(np.uint8).reshape(rows, nblocks, 2)
+    data[:, :, 2:4] = dmin.view(np.uint8).reshape(rows, nblocks, 2)
+    data[:, :, 4:16] = packed
+
+
+def quant_tensor(qtype, rows, width, seed, sigma=0.01, centered=False):
     """Random GGUF-layout bytes for a [rows x width] matrix of type qtype."""
     rng = np.random.default_rng(seed)
     elements, nbytes = BLOCK[qtype]
@@ -62,6 +83,8 @@ def quant_tensor(qtype, rows, width, seed, sigma=0.01):
             nib = (bits >> (4 * k)) & 0xF
             words[:, :, k] = (words[:, :, k] & 0x0FFF) | (nib << 12)
         data[:, :, 48:56] = words.astype(np.uint16).view(np.uint8).reshape(rows, nblocks, 8)
+    elif centered and qtype == Q4_K:
+        _center_q4_k(rng, data, sigma)
     else:
         for off in _SCALE_OFFSETS[qtype]:
             h = half_scales(rng, (rows, nblocks), sigma)

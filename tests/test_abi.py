@@ -1,6 +1,7 @@
 """CPU tests of the C ABI: the library loads without a GPU, exports every
-symbol include/q38cuda.h declares, and rejects bad arguments with the
-upstream return convention (0) before touching the device."""
+symbol include/q38cuda.h and include/q38cuda_model.h declare, and rejects bad
+arguments with the upstream return convention (0) before touching the
+device."""
 import ctypes
 import os
 import re
@@ -10,12 +11,21 @@ import pytest
 from conftest import ROOT
 
 HEADER = os.path.join(ROOT, "include", "q38cuda.h")
+MODEL_HEADER = os.path.join(ROOT, "include", "q38cuda_model.h")
+# include/qwen38/qwen38_model.h of the upstream engine: the model entry points
+# the device model must provide under the same names.
+UPSTREAM_MODEL_API = [
+    "q38_model_open_gguf", "q38_model_attach_mtp_gguf", "q38_model_close", "q38_model_reset",
+    "q38_model_forward_token", "q38_model_prefill", "q38_model_enable_mtp", "q38_model_mtp_forward",
+    "q38_model_speculative_greedy", "q38_model_forward_token_layers", "q38_model_vocab_size",
+    "q38_model_position", "q38_model_context_length",
+]
 
 
-def declared_functions():
-    text = open(HEADER).read()
+def declared_functions(path=HEADER, prefix="q38cu_"):
+    text = open(path).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(q38cu_\w+)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(" + prefix + r"\w+)\s*\(", text)))
 
 
 def test_library_exports_header(q38):
@@ -24,6 +34,26 @@ def test_library_exports_header(q38):
     assert len(names) >= 14
     for name in names:
         assert hasattr(lib, name), name
+
+
+def test_library_exports_model_api(q38):
+    lib = q38.lib()
+    names = declared_functions(MODEL_HEADER, prefix="q38(?:cu)?_model_")
+    assert set(UPSTREAM_MODEL_API) <= set(names)
+    for name in names:
+        assert hasattr(lib, name), name
+
+
+def test_model_rejects_bad_arguments_without_device(q38):
+    """Argument checks happen before any device work, as upstream
+    (qwen38_model.c:1372, 1497-1498)."""
+    from q38b200 import model as M
+    lib = M._bind()
+    assert not lib.q38_model_open_gguf(None, 16)
+    assert not lib.q38_model_open_gguf(b"model.gguf", 0)
+    assert lib.q38_model_forward_token(None, 1, None) == 0
+    assert lib.q38_model_vocab_size(None) == 0
+    assert lib.q38_model_position(None) == 0
 
 
 def test_host_helpers(q38):

@@ -1,0 +1,220 @@
+"""Model-level parity of the device model (include/q38cuda_model.h) with the
+upstream Q38Model compiled from its sources, on one seeded synthetic GGUF that
+has the upstream loader's exact tensor names, shapes and metadata, the
+Q4_K_M-style type mix and well-conditioned weights (q38b200.gguf, dist
+"conditioned").
+
+Why the full-model bar is relative to the upstream itself.  Every projection
+input is re-quantized to Q8_K, so a one-ulp difference anywhere (a different
+but legal summation order, a libm expf that differs from glibc's in the last
+bit) flips a few int8 activations, and the flips random-walk through the 64
+layers up to the Q8_K noise floor.  The upstream's own native (AVX2) and
+portable C builds drift apart exactly this way (on the real checkpoint RMSE
+0.058 on logits near 25, docs/CORRECTNESS.md of the upstream; on this synthetic
+model their top-1 differs on several tokens).  So:
+
+* every layer is checked with teacher forcing, with its recurrent state and KV
+  cache, over several tokens: the device's own input to layer L goes through
+  the CPU restatement (oracle/model_oracle.py, with the upstream's Q8_K
+  kernels) and must match the device's layer output to rounding (1e-5) except
+  for rare in-layer int8 flips (1e-2);
+* the first layer, whose input is exact, must match the upstream model to 1e-5;
+* over a token sequence the device's logits may not drift from the native
+  upstream build further than the upstream's portable build does (with 50 %
+  slack), and top-1 must agree wherever the native top-2 margin is above 5 %
+  of the top logit;
+* the device's own paths must agree bit for bit: prefill vs token-by-token
+  decode, the device-side greedy loop vs step-by-step argmax, and speculative
+  decoding vs plain greedy decoding.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from q38b200 import gguf
+
+pytestmark = pytest.mark.gpu
+
+COSINE = 0.999
+MARGIN = 0.05
+
+
+@pytest.fixture(scope="module")
+def model_path():
+    return gguf.cached_model_path(seed=1, mtp=True, dist="conditioned")
+
+
+@pytest.fixture(scope="module")
+def portable(model_path):
+    if not __import__("os").path.exists(O.REF_PORTABLE_LIB):
+        pytest.skip("portable upstream build missing")
+    ref = O.ReferenceModel(model_path, 512, lib_path=O.REF_PORTABLE_LIB)
+    yield ref
+    ref.close()
+
+
+@pytest.fixture(scope="module")
+def models(model_path):
+    if not O.reference_available():
+        pytest.skip("upstream reference library not built")
+    from q38b200.model import Model
+    dev = Model(model_path, 512)
+    ref = O.ReferenceModel(model_path, 512)
+    yield dev, ref
+    dev.close()
+    ref.close()
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return np.linalg.norm(a - b) / np.linalg.norm(b)
+
+
+def cosine(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return a @ b / np.linalg.norm(a) / np.linalg.norm(b)
+
+
+def safe_margin(logits):
+    s = np.sort(logits)
+    return (s[-1] - s[-2]) >= MARGIN * abs(s[-1])
+
+
+def check_logits(got, want, what, cos_min=COSINE, top1=True):
+    assert np.all(np.isfinite(got)), what
+    c = cosine(got, want)
+    assert c >= cos_min, f"{what}: cosine {c:.6f}"
+    if top1 and safe_margin(want):
+        assert int(np.argmax(got)) == int(np.argmax(want)), f"{what}: top-1 differs at a safe margin"
+
+
+def test_first_layer_matches_upstream(models):
+    """Layer 0 sees the exact embedding row, so only in-layer rounding separates
+    the two (observed ~7e-7)."""
+    dev, ref = models
+    for token in (777, 3):
+        dev.reset()
+        ref.reset()
+        assert rel(dev.forward_token_layers(token, 1), ref.forward_token_layers(token, 1)) <= 1e-5
+
+
+def test_layers_teacher_forced(models, model_path):
+    """Each layer, with its state, over 3 tokens (positions 0..2)."""
+    import model_oracle as MO
+    dev, _ = models
+    lo = MO.LayerOracle(model_path, O.Reference())
+    tokens = (4321, 17, 99999)
+    errors = []
+    for layer in range(64):
+        dev.reset()
+        inputs = [dev.forward_token_layers(t, layer) for t in tokens]
+        dev.reset()
+        outputs = [dev.forward_token_layers(t, layer + 1) for t in tokens]
+        sl = MO.StatefulLayer(lo, layer)
+        errors += [rel(o, sl.step(i)) for i, o in zip(inputs, outputs)]
+    errors = np.array(errors)
+    assert errors.max() <= 1e-2, f"worst (layer, token) {divmod(int(errors.argmax()), 3)}: {errors.max():.2e}"
+    assert np.mean(errors <= 1e-5) >= 0.9, np.round(errors, 8).tolist()
+
+
+def test_forward_token_drift_within_upstream_builds(models, portable):
+    dev, ref = models
+    for m in (dev, ref, portable):
+        m.reset()
+    dev_err, port_err = [], []
+    for token in (11, 2222, 33333, 5, 200000, 77):
+        want = ref.forward_token(token)
+        got, alt = dev.forward_token(token), portable.forward_token(token)
+        assert np.all(np.isfinite(got))
+        dev_err.append(rel(got, want))
+        port_err.append(rel(alt, want))
+        if safe_margin(want):
+            assert int(np.argmax(got)) == int(np.argmax(want)), f"token {token}: top-1 differs at a safe margin"
+    assert dev.position == ref.position == 6
+    assert np.mean(dev_err) <= 1.5 * np.mean(port_err) + 1e-3, (dev_err, port_err)
+
+
+def test_prefill_matches_decode_bitwise_and_upstream(models):
+    dev, ref = models
+    prompt = np.random.default_rng(5).integers(0, 248320, 11).tolist()  # one chunk of 8, one of 3
+    dev.reset()
+    stepwise = [dev.forward_token(t) for t in prompt][-1]
+    dev.reset()
+    batched = dev.prefill(prompt)
+    assert np.array_equal(batched, stepwise), "prefill and token-by-token decode must agree bit for bit"
+    assert dev.position == 11
+    ref.reset()
+    check_logits(batched, ref.prefill(prompt), "prefill", cos_min=0.9)
+    # decoding continues from the prefilled state
+    check_logits(dev.forward_token(42), ref.forward_token(42), "decode after prefill", cos_min=0.9)
+
+
+def test_greedy_matches_upstream_teacher_forced(models, portable):
+    """Greedy decoding under teacher forcing: the device and the upstream's
+    portable build both read the native build's own greedy sequence.  The
+    device's argmax must agree with the native one at least as often as the
+    portable build's does (less one token), and on the first steps, before
+    any drift has built up."""
+    dev, ref = models
+    for m in (dev, ref, portable):
+        m.reset()
+    token = 1234
+    dev_agree = port_agree = 0
+    steps = 12
+    for step in range(steps):
+        want = ref.forward_token(token)
+        got, alt = dev.forward_token(token), portable.forward_token(token)
+        check_logits(got, want, f"greedy step {step}", cos_min=0.9, top1=False)
+        if step < 2:
+            assert int(np.argmax(got)) == int(np.argmax(want)), f"greedy step {step}"
+        dev_agree += int(np.argmax(got)) == int(np.argmax(want))
+        port_agree += int(np.argmax(alt)) == int(np.argmax(want))
+        token = int(np.argmax(want))
+    assert dev_agree >= port_agree - 1, (dev_agree, port_agree)
+    assert dev_agree >= steps // 2, (dev_agree, port_agree)
+
+
+def test_device_greedy_loop_is_the_argmax_loop(models):
+    dev, _ = models
+    dev.reset()
+    token, want = 99, []
+    for _ in range(10):
+        token = int(np.argmax(dev.forward_token(token)))
+        want.append(token)
+    dev.reset()
+    assert dev.generate_greedy(99, 10) == want
+    assert dev.position == 10
+
+
+def test_mtp_head_after_prefill_matches_upstream(models):
+    """Prefill with MTP enabled runs the MTP catch-up over every prompt token
+    (chunks of 8 and 3 here); the next draft's logits then depend on all of it."""
+    dev, ref = models
+    prompt = np.random.default_rng(9).integers(0, 248320, 11).tolist()
+    for m in (dev, ref):
+        m.reset()
+        m.enable_mtp()
+    check_logits(dev.prefill(prompt), ref.prefill(prompt), "prefill with MTP", cos_min=0.9)
+    check_logits(dev.mtp_forward(prompt[-1]), ref.mtp_forward(prompt[-1]), "MTP draft after prefill", cos_min=0.9)
+
+
+def test_speculative_greedy_preserves_greedy(models):
+    """q38_model_speculative_greedy keeps the target's exact greedy sequence
+    (qwen38_model.h:33-36): drafts, batch verification, rollback, replay of the
+    confirmed prefix and MTP catch-up must not change a single token."""
+    dev, _ = models
+    dev.reset()
+    plain = dev.generate_greedy(7, 12)
+    dev.reset()
+    dev.enable_mtp()
+    token, seq, calls = 7, [], 0
+    while len(seq) < 12:
+        accepted, _ = dev.speculative_greedy(token, 0xFFFFFFFF, 3)
+        assert 1 <= len(accepted) <= 3
+        seq += accepted
+        token = accepted[-1]
+        calls += 1
+    assert seq[:12] == plain
+    assert dev.position == len(seq)

@@ -54,7 +54,16 @@ struct StreamLaunch {
     int32_t *dbg_x;
     int out_ld = 0;       // output row stride between tokens (0: rows)
     int accumulate = 0;   // 1: add the result to the output rows
+    // Activation prologue: kActQ8K reads Q8_K blocks from `act`; the fused
+    // modes form them from floats inside the kernel (see q38_stream.cu).
+    int act_mode = 0;
+    const float *act_x = nullptr;  // RMSNorm: x rows; SwiGLU: gate rows ([tokens][act_ld])
+    const float *act_y = nullptr;  // RMSNorm: norm weight; SwiGLU: up rows
+    int act_ld = 0;
+    float *act_f_out = nullptr;    // optional float copy of the activation [tokens][width]
 };
+
+enum : int { kActQ8K = 0, kActRmsNorm = 1, kActSwiGLU = 2 };
 
 int stream_tile_rows(int rows);
 cudaError_t stream_plan(int type, int rows, int width, int tile_rows, int tokens, StreamPlan *p);

@@ -371,8 +371,22 @@ bool alloc_runtime(Q38Model *m)
 // ---------------------------------------------------------------------------
 // the token step
 // ---------------------------------------------------------------------------
+// The input of a projection: Q8_K blocks already formed (kActQ8K, with the
+// float rows for float-path parts), or floats that the GEMV normalizes /
+// gates and quantizes in its prologue (kActRmsNorm: RMSNorm(x) * y;
+// kActSwiGLU: silu(x) * y).
+struct ActIn {
+    int mode = q38::kActQ8K;
+    const void *q8 = nullptr;   // kActQ8K
+    const float *f = nullptr;   // kActQ8K: float rows for float-path parts
+    int f_ld = 0;
+    const float *x = nullptr, *y = nullptr;  // fused modes
+    int ld = 0;
+    float *f_out = nullptr;     // fused modes: optional float copy of the activation
+};
+
 // Stream GEMM with an output stride and optional accumulation.
-bool stream_project(const Part &p, const void *q8, int tokens, float *out, int out_ld, int accumulate,
+bool stream_project(const Part &p, const ActIn &in, int tokens, float *out, int out_ld, int accumulate,
                     cudaStream_t s)
 {
     const int width = static_cast<int>(p.t.shape[0]), nb = width / 256;
@@ -383,7 +397,7 @@ bool stream_project(const Part &p, const void *q8, int tokens, float *out, int o
         if (!cuda_ok(e, "stream plan")) return false;
         q38::StreamLaunch l;
         l.weights = p.t.data;
-        l.act = static_cast<const Q38CuQ8KBlock *>(q8) + static_cast<size_t>(tok0) * nb;
+        l.act = in.q8 ? static_cast<const Q38CuQ8KBlock *>(in.q8) + static_cast<size_t>(tok0) * nb : nullptr;
         l.tokens = plan.token_group;
         l.out = out + static_cast<size_t>(tok0) * out_ld;
         l.scratch = p.t.scratch;
@@ -391,6 +405,13 @@ bool stream_project(const Part &p, const void *q8, int tokens, float *out, int o
         l.dbg_x = nullptr;
         l.out_ld = out_ld;
         l.accumulate = accumulate;
+        l.act_mode = in.mode;
+        if (in.mode != q38::kActQ8K) {
+            l.act_x = in.x + static_cast<size_t>(tok0) * in.ld;
+            l.act_y = in.mode == q38::kActSwiGLU ? in.y + static_cast<size_t>(tok0) * in.ld : in.y;
+            l.act_ld = in.ld;
+            l.act_f_out = in.f_out ? in.f_out + static_cast<size_t>(tok0) * width : nullptr;
+        }
         if (!cuda_ok(q38::launch_stream_gemm(static_cast<int>(p.t.type), plan, l, s), "stream gemm launch"))
             return false;
         tok0 += plan.token_group;
@@ -398,16 +419,39 @@ bool stream_project(const Part &p, const void *q8, int tokens, float *out, int o
     return true;
 }
 
-// out[tok * out_ld + part.offset + row] (+)= projection of this token's input
-bool project(const Proj &p, const void *q8, const float *fin, int fin_ld, int tokens, float *out, int out_ld,
-             int accumulate, cudaStream_t s)
+bool has_float_part(const Proj &p)
 {
+    for (const Part &part : p.parts)
+        if (!part.int_path) return true;
+    return false;
+}
+
+// out[tok * out_ld + part.offset + row] (+)= projection of this token's input.
+// A fused input that a float-path part cannot take is materialized first
+// (RMSNorm / SwiGLU kernels into the float rows and m->q8).
+bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int out_ld, int accumulate)
+{
+    const cudaStream_t s = m->stream;
+    const int width = p.width;
+    if (in.mode != q38::kActQ8K && has_float_part(p)) {
+        float *f = in.f_out ? in.f_out : m->act_f;
+        const bool ok = in.mode == q38::kActRmsNorm
+                            ? cuda_ok(q38::launch_rmsnorm_quant(in.x, in.ld, in.y, width, tokens, f, width, m->q8, s),
+                                      "rmsnorm")
+                            : cuda_ok(q38::launch_swiglu_quant(in.x, in.y, in.ld, width, tokens, f, m->q8, s),
+                                      "swiglu");
+        if (!ok) return false;
+        in = ActIn();
+        in.q8 = m->q8;
+        in.f = f;
+        in.f_ld = width;
+    }
     for (const Part &part : p.parts) {
         if (part.int_path) {
-            if (!stream_project(part, q8, tokens, out + part.offset, out_ld, accumulate, s)) return false;
+            if (!stream_project(part, in, tokens, out + part.offset, out_ld, accumulate, s)) return false;
         } else {
             const uint32_t be = q38cu_block_elements(part.t.type), bb = q38cu_block_bytes(part.t.type);
-            if (!cuda_ok(q38::launch_f32_gemm_ex(out + part.offset, out_ld, accumulate, fin, fin_ld, tokens,
+            if (!cuda_ok(q38::launch_f32_gemm_ex(out + part.offset, out_ld, accumulate, in.f, in.f_ld, tokens,
                                                  part.t.shape[0], part.t.data, part.rows, 0,
                                                  static_cast<int>(part.t.type), static_cast<int>(be),
                                                  static_cast<int>(bb), s),
@@ -418,16 +462,52 @@ bool project(const Proj &p, const void *q8, const float *fin, int fin_ld, int to
     return true;
 }
 
+ActIn q8_input(const void *q8, const float *f, int f_ld)
+{
+    ActIn in;
+    in.q8 = q8;
+    in.f = f;
+    in.f_ld = f_ld;
+    return in;
+}
+
+ActIn rmsnorm_input(const float *x, int ld, const float *weight, float *f_out = nullptr)
+{
+    ActIn in;
+    in.mode = q38::kActRmsNorm;
+    in.x = x;
+    in.y = weight;
+    in.ld = ld;
+    in.f_out = f_out;
+    return in;
+}
+
+ActIn swiglu_input(const float *gate, const float *up, int ld)
+{
+    ActIn in;
+    in.mode = q38::kActSwiGLU;
+    in.x = gate;
+    in.y = up;
+    in.ld = ld;
+    return in;
+}
+
+// ssm_beta | ssm_alpha as one Q8_0 tensor: the DeltaNet kernel forms both
+// projections itself.
+bool fusable_ba(const Proj &p)
+{
+    return p.parts.size() == 1 && !p.parts[0].int_path && p.parts[0].t.type == kQ8_0 && p.rows == 2 * kLinHeads &&
+           p.width == kHidden;
+}
+
 bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
 {
     (void)base_hint;
     const Layer &L = m->layers[l];
     const cudaStream_t s = m->stream;
-    if (!cuda_ok(q38::launch_rmsnorm_quant(m->hidden, kHidden, L.attn_norm, kHidden, tokens, m->normf, kHidden,
-                                           m->q8, s),
-                 "rmsnorm"))
-        return false;
-    if (!project(L.in_proj, m->q8, m->normf, kHidden, tokens, m->wide, m->wide_ld, 0, s)) return false;
+    const ActIn attn_in = rmsnorm_input(m->hidden, kHidden, L.attn_norm);
+    if (!project(m, L.in_proj, attn_in, tokens, m->wide, m->wide_ld, 0)) return false;
+    const ActIn mixed = q8_input(m->q8, m->act_f, L.full ? kAttnQ : kLinV);
     if (L.full) {
         q38::AttnArgs a{};
         a.qkv = m->wide;
@@ -447,16 +527,22 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         a.out_f = m->act_f;
         a.out_q = m->q8;
         if (!cuda_ok(q38::launch_attention(a, s), "attention")) return false;
-        if (!project(L.out, m->q8, m->act_f, kAttnQ, tokens, m->hidden, kHidden, 1, s)) return false;
     } else {
-        if (!project(L.ba, m->q8, m->normf, kHidden, tokens, m->ba, m->ba_ld, 0, s)) return false;
         q38::DeltaArgs d{};
+        if (fusable_ba(L.ba)) {
+            d.ba_fused = 1;
+            d.ba_w = static_cast<const uint8_t *>(L.ba.parts[0].t.data);
+            d.hidden = m->hidden;
+            d.attn_norm = L.attn_norm;
+        } else {
+            if (!project(m, L.ba, attn_in, tokens, m->ba, m->ba_ld, 0)) return false;
+            d.beta = m->ba;
+            d.alpha = m->ba + kLinHeads;
+            d.ba_ld = m->ba_ld;
+        }
         d.qkvz = m->wide;
         d.qkvz_ld = m->wide_ld;
         d.z_off = kLinQkv;
-        d.beta = m->ba;
-        d.alpha = m->ba + kLinHeads;
-        d.ba_ld = m->ba_ld;
         d.conv_w = L.conv_w;
         d.conv_ring = m->conv_ring + static_cast<size_t>(L.index) * kLinQkv * kConvRing;
         d.dt = L.dt;
@@ -468,17 +554,11 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         d.out_f = m->act_f;
         d.out_q = m->q8;
         if (!cuda_ok(q38::launch_deltanet(d, s), "deltanet")) return false;
-        if (!project(L.out, m->q8, m->act_f, kLinV, tokens, m->hidden, kHidden, 1, s)) return false;
     }
-    if (!cuda_ok(q38::launch_rmsnorm_quant(m->hidden, kHidden, L.post_norm, kHidden, tokens, m->normf, kHidden,
-                                           m->q8, s),
-                 "rmsnorm"))
+    if (!project(m, L.out, mixed, tokens, m->hidden, kHidden, 1)) return false;
+    if (!project(m, L.gate_up, rmsnorm_input(m->hidden, kHidden, L.post_norm), tokens, m->wide, m->wide_ld, 0))
         return false;
-    if (!project(L.gate_up, m->q8, m->normf, kHidden, tokens, m->wide, m->wide_ld, 0, s)) return false;
-    if (!cuda_ok(q38::launch_swiglu_quant(m->wide, m->wide + kFfn, m->wide_ld, kFfn, tokens, m->act_f, m->q8, s),
-                 "swiglu"))
-        return false;
-    return project(L.down, m->q8, m->act_f, kFfn, tokens, m->hidden, kHidden, 1, s);
+    return project(m, L.down, swiglu_input(m->wide, m->wide + kFfn, m->wide_ld), tokens, m->hidden, kHidden, 1);
 }
 
 // Embedding rows of `tokens` ids held in device memory.
@@ -498,10 +578,8 @@ bool enqueue_head(Q38Model *m, const float *norm_w, const Proj &head, int tokens
                   bool feed, int advance)
 {
     const cudaStream_t s = m->stream;
-    if (!cuda_ok(q38::launch_rmsnorm_quant(m->hidden, kHidden, norm_w, kHidden, tokens, norm_out, kHidden, m->q8, s),
-                 "rmsnorm"))
+    if (!project(m, head, rmsnorm_input(m->hidden, kHidden, norm_w, norm_out), tokens, m->logits, kVocab, 0))
         return false;
-    if (!project(head, m->q8, norm_out, kHidden, tokens, m->logits, kVocab, 0, s)) return false;
     q38::ArgmaxArgs a{};
     a.logits = m->logits;
     a.ld = kVocab;
@@ -550,7 +628,7 @@ bool enqueue_mtp_body(Q38Model *m, const uint32_t *d_ids, int n, const float *pr
         ok = cuda_ok(q38::launch_rmsnorm_quant(prev_rows, kHidden, m->hnorm, kHidden, n - 1, m->normf + w2 + kHidden,
                                                w2, q8 + nb2 + nb, s, nb2),
                      "rmsnorm");
-    return ok && project(m->eh_proj, m->q8, m->normf, w2, n, m->hidden, kHidden, 0, s) &&
+    return ok && project(m, m->eh_proj, q8_input(m->q8, m->normf, w2), n, m->hidden, kHidden, 0) &&
            enqueue_layer(m, kLayers, n, 0);
 }
 
@@ -834,8 +912,8 @@ int q38_model_prefill(Q38Model *m, const uint32_t *tokens, uint32_t token_count,
         if (ok && last) {
             // logits of the last token only
             const Q38CuQ8KBlock *q8 = static_cast<const Q38CuQ8KBlock *>(m->q8) + static_cast<size_t>(n - 1) * nb;
-            ok = project(m->output, q8, m->target_norm + static_cast<size_t>(n - 1) * kHidden, kHidden, 1, m->logits,
-                         kVocab, 0, m->stream) &&
+            ok = project(m, m->output, q8_input(q8, m->target_norm + static_cast<size_t>(n - 1) * kHidden, kHidden),
+                         1, m->logits, kVocab, 0) &&
                  cuda_ok(cudaMemcpyAsync(m->host_logits, m->logits, static_cast<size_t>(kVocab) * sizeof(float),
                                          cudaMemcpyDeviceToHost, m->stream),
                          "logits copy");

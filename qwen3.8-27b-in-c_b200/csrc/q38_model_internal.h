@@ -18,8 +18,13 @@ constexpr int kArgmaxCtas = 148;
 struct DeltaArgs {
     const float *qkvz;  // per token: q | k | v (10240), z at z_off (6144)
     int qkvz_ld, z_off;
-    const float *beta, *alpha;  // raw projections, per token at stride ba_ld
+    const float *beta, *alpha;  // raw projections, per token at stride ba_ld (ba_fused == 0)
     int ba_ld;
+    // ba_fused: beta/alpha formed in the kernel from the Q8_0 rows ba_w
+    // ([beta 48 rows | alpha 48 rows], GGUF layout) and RMSNorm(hidden, attn_norm)
+    int ba_fused;
+    const uint8_t *ba_w;
+    const float *hidden, *attn_norm;  // [tokens][5120], [5120]
     const float *conv_w;  // [10240][4]
     float *conv_ring;     // [10240][16]
     const float *dt, *a;  // [48]

@@ -224,6 +224,8 @@ struct __align__(16) DeltaShared {
     float q[128], k[128];
     float v[32], o[32];
     double red[4][2];
+    double ss[4];
+    float ba_part[4];
     float beta, decay;
     double head_part;   // exchanged: this CTA's sum of squares
     AbsMax block_part;  // exchanged: this CTA's absolute maximum
@@ -246,10 +248,78 @@ __device__ __forceinline__ float conv_silu(const DeltaArgs &a, int ch, int pos, 
     return silu(v);
 }
 
+// beta and alpha of value head vh for token t from the Q8_0 rows (upstream
+// q38_dot_q8_0, qwen38_quant.c:496-507: fmaf(d * q, x, acc)) on
+// RMSNorm(hidden, attn_norm) recomputed here into shared memory; threads
+// 0..63 form beta, 64..127 alpha.  Leaves sh.beta / sh.decay (after the
+// caller's barrier).
+__device__ void fused_beta_alpha(const DeltaArgs &a, DeltaShared &sh, float *xs, int t, int vh)
+{
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float4 *h4 = reinterpret_cast<const float4 *>(a.hidden + static_cast<size_t>(t) * 5120);
+    float4 hv[10];
+    double part = 0.0;
+#pragma unroll
+    for (int j = 0; j < 10; ++j) {
+        hv[j] = h4[tid + 128 * j];
+        part += static_cast<double>(__fmul_rn(hv[j].x, hv[j].x));
+        part += static_cast<double>(__fmul_rn(hv[j].y, hv[j].y));
+        part += static_cast<double>(__fmul_rn(hv[j].z, hv[j].z));
+        part += static_cast<double>(__fmul_rn(hv[j].w, hv[j].w));
+    }
+    part = warp_sum_d(part);
+    if (lane == 0) sh.ss[warp] = part;
+    __syncthreads();
+    const double sum = ((sh.ss[0] + sh.ss[1]) + sh.ss[2]) + sh.ss[3];
+    const float mean = static_cast<float>(sum / 5120.0);
+    const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps)));
+    const float4 *w4 = reinterpret_cast<const float4 *>(a.attn_norm);
+#pragma unroll
+    for (int j = 0; j < 10; ++j) {
+        const float4 w = __ldg(w4 + tid + 128 * j);
+        float4 x;
+        x.x = __fmul_rn(__fmul_rn(hv[j].x, scale), w.x);
+        x.y = __fmul_rn(__fmul_rn(hv[j].y, scale), w.y);
+        x.z = __fmul_rn(__fmul_rn(hv[j].z, scale), w.z);
+        x.w = __fmul_rn(__fmul_rn(hv[j].w, scale), w.w);
+        reinterpret_cast<float4 *>(xs)[tid + 128 * j] = x;
+    }
+    __syncthreads();
+    const int which = tid >> 6, k = tid & 63;
+    const uint8_t *row = a.ba_w + static_cast<size_t>(which * 48 + vh) * 5440;
+    float acc = 0.0f;
+    for (int blk = k; blk < 160; blk += 64) {
+        // 34-byte block: fp16 d, 32 int8 quants; 2-byte aligned
+        const unsigned short *b16 = reinterpret_cast<const unsigned short *>(row + blk * 34);
+        unsigned short raw[17];
+#pragma unroll
+        for (int i = 0; i < 17; ++i) raw[i] = __ldg(b16 + i);
+        const float d = __half2float(__ushort_as_half(raw[0]));
+        const float *x = xs + blk * 32;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float q0 = static_cast<float>(static_cast<int8_t>(raw[1 + i] & 0xFF));
+            const float q1 = static_cast<float>(static_cast<int8_t>(raw[1 + i] >> 8));
+            acc = fmaf(__fmul_rn(d, q0), x[2 * i], acc);
+            acc = fmaf(__fmul_rn(d, q1), x[2 * i + 1], acc);
+        }
+    }
+    acc = warp_sum_f(acc);
+    if (lane == 0) sh.ba_part[warp] = acc;
+    __syncthreads();
+    if (tid == 0) {
+        const float beta_raw = __fadd_rn(sh.ba_part[0], sh.ba_part[1]);
+        const float alpha_raw = __fadd_rn(sh.ba_part[2], sh.ba_part[3]);
+        sh.beta = sigmoid(beta_raw);
+        sh.decay = expf(__fmul_rn(a.a[vh], softplus(__fadd_rn(alpha_raw, a.dt[vh]))));
+    }
+}
+
 __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
     deltanet_kernel(DeltaArgs a)
 {
     __shared__ DeltaShared sh;
+    __shared__ __align__(16) float xs[5120];  // RMSNorm(hidden) for the fused beta/alpha rows
     cg::cluster_group cluster = cg::this_cluster();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int rank = static_cast<int>(cluster.block_rank());
@@ -294,13 +364,14 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
             sh.red[warp][0] = pq;
             sh.red[warp][1] = pk;
         }
-        if (tid == 0) {
+        if (!a.ba_fused && tid == 0) {
             const size_t bo = static_cast<size_t>(t) * a.ba_ld + vh;
             const float beta = sigmoid(a.beta[bo]);
             const float alpha = __fmul_rn(a.a[vh], softplus(__fadd_rn(a.alpha[bo], a.dt[vh])));
             sh.beta = beta;
             sh.decay = expf(alpha);
         }
+        if (a.ba_fused) fused_beta_alpha(a, sh, xs, t, vh);
         __syncthreads();
         double sq = 0.0, sk = 0.0;
         for (int w = 0; w < 4; ++w) {

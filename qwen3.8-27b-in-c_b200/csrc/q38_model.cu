@@ -143,6 +143,7 @@ struct Q38Model {
     uint32_t *host_ids = nullptr;
 
     cudaGraphExec_t decode_graph = nullptr;
+    int step_kernels = 0;  // kernel nodes of the decode graph
     std::vector<void *> owned;
     std::vector<Q38CuTensor> tensors;  // every uploaded tensor, freed at close
     void *staging = nullptr;
@@ -766,6 +767,18 @@ bool build_decode_graph(Q38Model *m)
         if (graph) cudaGraphDestroy(graph);
         return false;
     }
+    size_t n_nodes = 0;
+    if (cudaGraphGetNodes(graph, nullptr, &n_nodes) == cudaSuccess && n_nodes) {
+        std::vector<cudaGraphNode_t> nodes(n_nodes);
+        if (cudaGraphGetNodes(graph, nodes.data(), &n_nodes) == cudaSuccess) {
+            m->step_kernels = 0;
+            for (size_t i = 0; i < n_nodes; ++i) {
+                cudaGraphNodeType type;
+                if (cudaGraphNodeGetType(nodes[i], &type) == cudaSuccess && type == cudaGraphNodeTypeKernel)
+                    ++m->step_kernels;
+            }
+        }
+    }
     const cudaError_t ei = cudaGraphInstantiate(&m->decode_graph, graph, 0);
     cudaGraphDestroy(graph);
     return cuda_ok(ei, "graph instantiate");
@@ -1067,5 +1080,11 @@ int q38cu_model_generate_greedy(Q38Model *m, uint32_t token_id, uint32_t count, 
 }
 
 void *q38cu_model_stream(Q38Model *m) { return m ? m->stream : nullptr; }
+
+int q38cu_model_step_kernels(Q38Model *m)
+{
+    if (!m || !use_device(m) || !build_decode_graph(m)) return 0;
+    return m->step_kernels;
+}
 
 }  // extern "C"

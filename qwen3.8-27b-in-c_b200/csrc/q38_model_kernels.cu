@@ -231,88 +231,127 @@ struct __align__(16) DeltaShared {
     AbsMax block_part;  // exchanged: this CTA's absolute maximum
 };
 
-__device__ __forceinline__ float conv_tap_input(const DeltaArgs &a, int ch, int p, int base)
+// The four conv inputs of one channel at position pos (taps pos-3 .. pos-1
+// and the new input) and its kernel, loaded together: a tap before `base`
+// comes from the ring, later ones from this launch's projections, chosen by
+// address so the loads do not wait on one another.
+struct ConvTaps {
+    float t0, t1, t2, x;
+    float4 w;
+};
+
+__device__ __forceinline__ const float *conv_tap_ptr(const DeltaArgs &a, int ch, int p, int base)
 {
-    if (p >= base) return a.qkvz[static_cast<size_t>(p - base) * a.qkvz_ld + ch];
-    return a.conv_ring[static_cast<size_t>(ch) * kConvRing + (p & (kConvRing - 1))];
+    return p >= base ? a.qkvz + static_cast<size_t>(p - base) * a.qkvz_ld + ch
+                     : a.conv_ring + static_cast<size_t>(ch) * kConvRing + (p & (kConvRing - 1));
 }
 
-// One conv channel at position pos: ((s0 k0 + s1 k1) + s2 k2) + x k3, then SiLU.
-__device__ __forceinline__ float conv_silu(const DeltaArgs &a, int ch, int pos, int base)
+__device__ __forceinline__ ConvTaps load_taps(const DeltaArgs &a, int ch, int pos, int base)
 {
-    const float4 w = *reinterpret_cast<const float4 *>(a.conv_w + static_cast<size_t>(ch) * 4);
-    float v = __fmul_rn(conv_tap_input(a, ch, pos - 3, base), w.x);
-    v = __fadd_rn(v, __fmul_rn(conv_tap_input(a, ch, pos - 2, base), w.y));
-    v = __fadd_rn(v, __fmul_rn(conv_tap_input(a, ch, pos - 1, base), w.z));
-    v = __fadd_rn(v, __fmul_rn(conv_tap_input(a, ch, pos, base), w.w));
+    ConvTaps c;
+    c.t0 = *conv_tap_ptr(a, ch, pos - 3, base);
+    c.t1 = *conv_tap_ptr(a, ch, pos - 2, base);
+    c.t2 = *conv_tap_ptr(a, ch, pos - 1, base);
+    c.x = a.qkvz[static_cast<size_t>(pos - base) * a.qkvz_ld + ch];
+    c.w = __ldg(reinterpret_cast<const float4 *>(a.conv_w + static_cast<size_t>(ch) * 4));
+    return c;
+}
+
+// ((s0 k0 + s1 k1) + s2 k2) + x k3, then SiLU (qwen38_model.c:722-737).
+__device__ __forceinline__ float conv_silu(const ConvTaps &c)
+{
+    float v = __fmul_rn(c.t0, c.w.x);
+    v = __fadd_rn(v, __fmul_rn(c.t1, c.w.y));
+    v = __fadd_rn(v, __fmul_rn(c.t2, c.w.z));
+    v = __fadd_rn(v, __fmul_rn(c.x, c.w.w));
     return silu(v);
 }
 
-// beta and alpha of value head vh for token t from the Q8_0 rows (upstream
-// q38_dot_q8_0, qwen38_quant.c:496-507: fmaf(d * q, x, acc)) on
-// RMSNorm(hidden, attn_norm) recomputed here into shared memory; threads
-// 0..63 form beta, 64..127 alpha.  Leaves sh.beta / sh.decay (after the
-// caller's barrier).
-__device__ void fused_beta_alpha(const DeltaArgs &a, DeltaShared &sh, float *xs, int t, int vh)
+// Fused beta/alpha (upstream q38_dot_q8_0, qwen38_quant.c:496-507:
+// fmaf(d * q, x, acc), on RMSNorm(hidden, attn_norm)).  Threads 0..63 form
+// beta, 64..127 alpha; thread k of a row takes Q8_0 blocks k, k + 64, k + 128.
+// Phase 1 loads the hidden row and the norm weights; phase 2 (after the
+// caller's barrier publishes the sum of squares) writes the normed row to
+// shared memory and loads the thread's Q8_0 blocks; phase 3 forms the dots.
+struct BaLoads {
+    float4 h[10], w[10];
+};
+
+__device__ __forceinline__ void ba_load_row(const DeltaArgs &a, int t, BaLoads &l)
 {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x;
     const float4 *h4 = reinterpret_cast<const float4 *>(a.hidden + static_cast<size_t>(t) * 5120);
-    float4 hv[10];
-    double part = 0.0;
-#pragma unroll
-    for (int j = 0; j < 10; ++j) {
-        hv[j] = h4[tid + 128 * j];
-        part += static_cast<double>(__fmul_rn(hv[j].x, hv[j].x));
-        part += static_cast<double>(__fmul_rn(hv[j].y, hv[j].y));
-        part += static_cast<double>(__fmul_rn(hv[j].z, hv[j].z));
-        part += static_cast<double>(__fmul_rn(hv[j].w, hv[j].w));
-    }
-    part = warp_sum_d(part);
-    if (lane == 0) sh.ss[warp] = part;
-    __syncthreads();
-    const double sum = ((sh.ss[0] + sh.ss[1]) + sh.ss[2]) + sh.ss[3];
-    const float mean = static_cast<float>(sum / 5120.0);
-    const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps)));
     const float4 *w4 = reinterpret_cast<const float4 *>(a.attn_norm);
 #pragma unroll
     for (int j = 0; j < 10; ++j) {
-        const float4 w = __ldg(w4 + tid + 128 * j);
+        l.h[j] = h4[tid + 128 * j];
+        l.w[j] = __ldg(w4 + tid + 128 * j);
+    }
+}
+
+__device__ __forceinline__ double ba_sum_squares(const BaLoads &l)
+{
+    double part = 0.0;
+#pragma unroll
+    for (int j = 0; j < 10; ++j) {
+        part += static_cast<double>(__fmul_rn(l.h[j].x, l.h[j].x));
+        part += static_cast<double>(__fmul_rn(l.h[j].y, l.h[j].y));
+        part += static_cast<double>(__fmul_rn(l.h[j].z, l.h[j].z));
+        part += static_cast<double>(__fmul_rn(l.h[j].w, l.h[j].w));
+    }
+    return part;
+}
+
+__device__ __forceinline__ void ba_store_normed(const BaLoads &l, float scale, float *xs)
+{
+    const int tid = threadIdx.x;
+#pragma unroll
+    for (int j = 0; j < 10; ++j) {
         float4 x;
-        x.x = __fmul_rn(__fmul_rn(hv[j].x, scale), w.x);
-        x.y = __fmul_rn(__fmul_rn(hv[j].y, scale), w.y);
-        x.z = __fmul_rn(__fmul_rn(hv[j].z, scale), w.z);
-        x.w = __fmul_rn(__fmul_rn(hv[j].w, scale), w.w);
+        x.x = __fmul_rn(__fmul_rn(l.h[j].x, scale), l.w[j].x);
+        x.y = __fmul_rn(__fmul_rn(l.h[j].y, scale), l.w[j].y);
+        x.z = __fmul_rn(__fmul_rn(l.h[j].z, scale), l.w[j].z);
+        x.w = __fmul_rn(__fmul_rn(l.h[j].w, scale), l.w[j].w);
         reinterpret_cast<float4 *>(xs)[tid + 128 * j] = x;
     }
-    __syncthreads();
-    const int which = tid >> 6, k = tid & 63;
+}
+
+struct BaBlocks {
+    unsigned short raw[3][17];  // fp16 d + 32 int8 quants per 34-byte block
+};
+
+__device__ __forceinline__ void ba_load_blocks(const DeltaArgs &a, int vh, BaBlocks &b)
+{
+    const int tid = threadIdx.x, which = tid >> 6, k = tid & 63;
     const uint8_t *row = a.ba_w + static_cast<size_t>(which * 48 + vh) * 5440;
-    float acc = 0.0f;
-    for (int blk = k; blk < 160; blk += 64) {
-        // 34-byte block: fp16 d, 32 int8 quants; 2-byte aligned
-        const unsigned short *b16 = reinterpret_cast<const unsigned short *>(row + blk * 34);
-        unsigned short raw[17];
 #pragma unroll
-        for (int i = 0; i < 17; ++i) raw[i] = __ldg(b16 + i);
-        const float d = __half2float(__ushort_as_half(raw[0]));
+    for (int n = 0; n < 3; ++n) {
+        const int blk = k + 64 * n;
+        const unsigned short *b16 = reinterpret_cast<const unsigned short *>(row + (blk < 160 ? blk : 0) * 34);
+#pragma unroll
+        for (int i = 0; i < 17; ++i) b.raw[n][i] = blk < 160 ? __ldg(b16 + i) : static_cast<unsigned short>(0);
+    }
+}
+
+__device__ __forceinline__ float ba_dot(const BaBlocks &b, const float *xs)
+{
+    const int k = threadIdx.x & 63;
+    float acc = 0.0f;
+#pragma unroll
+    for (int n = 0; n < 3; ++n) {
+        const int blk = k + 64 * n;
+        if (blk >= 160) break;
+        const float d = __half2float(__ushort_as_half(b.raw[n][0]));
         const float *x = xs + blk * 32;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            const float q0 = static_cast<float>(static_cast<int8_t>(raw[1 + i] & 0xFF));
-            const float q1 = static_cast<float>(static_cast<int8_t>(raw[1 + i] >> 8));
+            const float q0 = static_cast<float>(static_cast<int8_t>(b.raw[n][1 + i] & 0xFF));
+            const float q1 = static_cast<float>(static_cast<int8_t>(b.raw[n][1 + i] >> 8));
             acc = fmaf(__fmul_rn(d, q0), x[2 * i], acc);
             acc = fmaf(__fmul_rn(d, q1), x[2 * i + 1], acc);
         }
     }
-    acc = warp_sum_f(acc);
-    if (lane == 0) sh.ba_part[warp] = acc;
-    __syncthreads();
-    if (tid == 0) {
-        const float beta_raw = __fadd_rn(sh.ba_part[0], sh.ba_part[1]);
-        const float alpha_raw = __fadd_rn(sh.ba_part[2], sh.ba_part[3]);
-        sh.beta = sigmoid(beta_raw);
-        sh.decay = expf(__fmul_rn(a.a[vh], softplus(__fadd_rn(alpha_raw, a.dt[vh]))));
-    }
+    return acc;
 }
 
 __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
@@ -329,49 +368,50 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
     const bool qk_writer = vh < 16 && quarter == 0;
 
     pdl_wait();
-    pdl_launch_dependents();
     const int base = a.ctl[1];
     float *state = a.state + (static_cast<size_t>(vh) * 128 + col0 + warp * 8) * 128 + lane * 4;
 
     for (int t = 0; t < a.tokens; ++t) {
         const int pos = base + t;
-        // state columns of this warp (8 x 128 floats; lane holds 4 of each)
+        // Every independent load of the step first: the warp's state columns
+        // (8 x 128 floats; lane holds 4 of each), the conv inputs of q, k (the
+        // key head's 128 channels) and v (this CTA's 32 channels), and the
+        // hidden row for the fused beta/alpha.
         float4 s[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) s[j] = *reinterpret_cast<const float4 *>(state + j * 128);
-
-        // causal conv + SiLU of q, k (all 128 channels of the key head) and v
         const int ch_q = kh * 128 + tid, ch_k = 2048 + kh * 128 + tid;
-        const float qv = conv_silu(a, ch_q, pos, base);
-        const float kv = conv_silu(a, ch_k, pos, base);
-        if (tid < 32) sh.v[tid] = conv_silu(a, 4096 + vh * 128 + col0 + tid, pos, base);
-        if (qk_writer) {
-            a.conv_ring[static_cast<size_t>(ch_q) * kConvRing + (pos & (kConvRing - 1))] =
-                a.qkvz[static_cast<size_t>(t) * a.qkvz_ld + ch_q];
-            a.conv_ring[static_cast<size_t>(ch_k) * kConvRing + (pos & (kConvRing - 1))] =
-                a.qkvz[static_cast<size_t>(t) * a.qkvz_ld + ch_k];
-        }
-        if (tid < 32) {
-            const int ch_v = 4096 + vh * 128 + col0 + tid;
-            a.conv_ring[static_cast<size_t>(ch_v) * kConvRing + (pos & (kConvRing - 1))] =
-                a.qkvz[static_cast<size_t>(t) * a.qkvz_ld + ch_v];
+        const int ch_v = 4096 + vh * 128 + col0 + (tid & 31);
+        const ConvTaps cq = load_taps(a, ch_q, pos, base);
+        const ConvTaps ck = load_taps(a, ch_k, pos, base);
+        const ConvTaps cv = load_taps(a, ch_v, pos, base);
+        BaLoads bl;
+        if (a.ba_fused) ba_load_row(a, t, bl);
+        float beta_raw = 0.0f, alpha_raw = 0.0f;
+        if (!a.ba_fused && tid == 0) {
+            const size_t bo = static_cast<size_t>(t) * a.ba_ld + vh;
+            beta_raw = a.beta[bo];
+            alpha_raw = a.alpha[bo];
         }
 
-        // L2 norms of q and k (qwen38_model.c:608-614)
-        double pq = warp_sum_d(static_cast<double>(__fmul_rn(qv, qv)));
-        double pk = warp_sum_d(static_cast<double>(__fmul_rn(kv, kv)));
+        // conv ring: this position's inputs, one writer per channel
+        if (qk_writer) {
+            a.conv_ring[static_cast<size_t>(ch_q) * kConvRing + (pos & (kConvRing - 1))] = cq.x;
+            a.conv_ring[static_cast<size_t>(ch_k) * kConvRing + (pos & (kConvRing - 1))] = ck.x;
+        }
+        if (tid < 32) a.conv_ring[static_cast<size_t>(ch_v) * kConvRing + (pos & (kConvRing - 1))] = cv.x;
+
+        // causal conv + SiLU, then the L2 norms of q and k (qwen38_model.c:608-614)
+        const float qv = conv_silu(cq), kv = conv_silu(ck);
+        if (tid < 32) sh.v[tid] = conv_silu(cv);
+        const double pq = warp_sum_d(static_cast<double>(__fmul_rn(qv, qv)));
+        const double pk = warp_sum_d(static_cast<double>(__fmul_rn(kv, kv)));
+        const double ph = a.ba_fused ? warp_sum_d(ba_sum_squares(bl)) : 0.0;
         if (lane == 0) {
             sh.red[warp][0] = pq;
             sh.red[warp][1] = pk;
+            sh.ss[warp] = ph;
         }
-        if (!a.ba_fused && tid == 0) {
-            const size_t bo = static_cast<size_t>(t) * a.ba_ld + vh;
-            const float beta = sigmoid(a.beta[bo]);
-            const float alpha = __fmul_rn(a.a[vh], softplus(__fadd_rn(a.alpha[bo], a.dt[vh])));
-            sh.beta = beta;
-            sh.decay = expf(alpha);
-        }
-        if (a.ba_fused) fused_beta_alpha(a, sh, xs, t, vh);
         __syncthreads();
         double sq = 0.0, sk = 0.0;
         for (int w = 0; w < 4; ++w) {
@@ -382,7 +422,31 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
         const float scale_k = __fdiv_rn(1.0f, fmaxf(sqrtf(static_cast<float>(sk)), kRmsEps));
         sh.q[tid] = __fmul_rn(qv, scale_q);
         sh.k[tid] = __fmul_rn(kv, scale_k);
+
+        // beta and alpha (qwen38_model.c:748-752)
+        if (a.ba_fused) {
+            const double sum = ((sh.ss[0] + sh.ss[1]) + sh.ss[2]) + sh.ss[3];
+            const float mean = static_cast<float>(sum / 5120.0);
+            ba_store_normed(bl, __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps))), xs);
+            BaBlocks bb;
+            ba_load_blocks(a, vh, bb);
+            __syncthreads();  // the normed row is complete
+            const float acc = warp_sum_f(ba_dot(bb, xs));
+            if (lane == 0) sh.ba_part[warp] = acc;
+            __syncthreads();
+            if (tid == 0) {
+                beta_raw = __fadd_rn(sh.ba_part[0], sh.ba_part[1]);
+                alpha_raw = __fadd_rn(sh.ba_part[2], sh.ba_part[3]);
+            }
+        }
+        if (tid == 0) {
+            sh.beta = sigmoid(beta_raw);
+            sh.decay = expf(__fmul_rn(a.a[vh], softplus(__fadd_rn(alpha_raw, a.dt[vh]))));
+        }
         __syncthreads();
+        // the next kernel's weight prefetch may start once this step's loads
+        // are in (earlier, its bulk copies would queue ahead of them)
+        if (t == a.tokens - 1) pdl_launch_dependents();
 
         // delta rule on this warp's 8 columns (qwen38_model.c:758-781)
         const float4 k4 = *reinterpret_cast<const float4 *>(&sh.k[lane * 4]);
@@ -511,7 +575,6 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
     const int g = h / (kAttnHeads / 4);
 
     pdl_wait();
-    pdl_launch_dependents();
     const int base = a.ctl[1];
     const int pos = base + t, len = pos + 1;
     const int chunk = (len + a.splits - 1) / a.splits;
@@ -571,6 +634,9 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
         const float v = p < base ? a.v_cache[static_cast<size_t>(p) * 1024 + g * 256 + d] : sh.vnew[p - base][d];
         acc = fmaf(sh.scores[p - p0], v, acc);
     }
+
+    // the keys and values are read: the next kernel's weight prefetch may start
+    pdl_launch_dependents();
 
     // leave this split's partial result; the last CTA of (t, h) merges
     float *part = a.partials + static_cast<size_t>(blockIdx.x) * (kAttnDim + 2);

@@ -140,76 +140,187 @@ struct ChunkWalk {
 // (227 registers) for 4 and 8.
 template <int MT> struct StreamThreads { static constexpr int kValue = MT <= 2 ? 416 : 288; };
 
-// Activation prologue of the fused modes: the consumer warps form the Q8_K
-// blocks of this launch's input in shared memory themselves (the upstream
-// q38_rmsnorm or q38_swiglu followed by q38_quantize_q8_k), while the
-// producer warp is already streaming weights.  Every CTA computes the same
-// values in the same order; CTA 0 also stores the floats when asked.
+// Activation prologues.  They run after the grid dependency, so their global
+// loads are the latency every launch pays before its first decode: each
+// thread issues all the loads of a batch (ActBatch blocks per warp) before
+// using any of them, instead of one L2 round trip per loop iteration.  The
+// batch is shallower when several tokens share the kernel's registers.
+template <int MT> struct ActBatch { static constexpr int kValue = MT == 1 ? 4 : 2; };
+
+__device__ __forceinline__ void load8(const float *p, float (&v)[8])
+{
+    const float4 a = *reinterpret_cast<const float4 *>(p);
+    const float4 b = *reinterpret_cast<const float4 *>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ void ldg8(const float *p, float (&v)[8])
+{
+    const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4 *>(p + 4));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// Q8_K of one 256-element block held 8 per lane, into an activation slot
+// (raw bsums in aux[8..15], as the Q8_K staging path leaves them).
+__device__ __forceinline__ void store_block(Act &slot, const float (&v)[8])
+{
+    const int lane = threadIdx.x & 31;
+    const WarpQ8K r = act_quantize_warp(v);
+    slot.q[lane * 2] = r.q0;
+    slot.q[lane * 2 + 1] = r.q1;
+    if ((lane & 3) == 0) slot.aux[8 + (lane >> 2)] = r.sums_word;
+    if (lane == 0) slot.xs = r.scale;
+}
+
+__device__ __forceinline__ void store_floats(const StreamArgs &g, int tok, int e, const float (&v)[8])
+{
+    if (g.act_f_out && blockIdx.x == 0) {
+        float *o = g.act_f_out + static_cast<size_t>(tok) * g.nb * 256 + e;
+        *reinterpret_cast<float4 *>(o) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4 *>(o + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+}
+
+// Fused modes: the consumer warps form the Q8_K blocks of this launch's
+// input in shared memory themselves (the upstream q38_rmsnorm or q38_swiglu
+// followed by q38_quantize_q8_k) while the producer warp is already streaming
+// weights.  Warp w owns blocks w, w + warps, ...; lane l holds elements
+// 8l .. 8l + 7 of each.  Every CTA computes the same values in the same order
+// (the order depends only on the shape); CTA 0 also stores the floats when
+// asked.
 template <int MT>
 __device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *red, int consumers)
 {
+    constexpr int kActBatch = ActBatch<MT>::kValue;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, warps = consumers >> 5;
-    const int width = g.nb * 256;
+    const int per_warp = (g.nb + warps - 1) / warps;
     for (int tok = 0; tok < MT; ++tok) {
-        const bool live = tok < g.tokens;
-        const float *x = g.act_x + static_cast<size_t>(tok) * g.act_ld;
-        float scale = 1.0f;
-        if (g.act_mode == kActRmsNorm && live) {
-            double part = 0.0;
-            for (int i = tid; i < width; i += consumers) {
-                const float v = x[i];
-                part += static_cast<double>(__fmul_rn(v, v));
+        Act *slots = acts + tok * g.nb;
+        if (tok >= g.tokens) {
+            for (int b = warp; b < g.nb; b += warps) {
+                slots[b].q[lane * 2] = slots[b].q[lane * 2 + 1] = 0u;
+                if (lane < 8) slots[b].aux[8 + lane] = 0u;
+                if (lane == 0) slots[b].xs = 0.0f;
             }
-            part = act_warp_sum_d(part);
-            if (lane == 0) red[warp] = part;
-            consumer_barrier(consumers);
-            double sum = 0.0;
-            for (int w = 0; w < warps; ++w) sum += red[w];
-            consumer_barrier(consumers);  // red is reused by the next token
-            const float mean = static_cast<float>(sum / static_cast<double>(width));
-            scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps)));
+            continue;
         }
-        for (int b = warp; b < g.nb; b += warps) {
-            Act &slot = acts[tok * g.nb + b];
-            if (!live) {
-                slot.q[lane * 2] = slot.q[lane * 2 + 1] = 0u;
-                if (lane < 8) slot.aux[8 + lane] = 0u;
-                if (lane == 0) slot.xs = 0.0f;
-                continue;
-            }
-            const int e = b * 256 + lane * 8;
-            float v[8];
-            const float4 x0 = *reinterpret_cast<const float4 *>(x + e);
-            const float4 x1 = *reinterpret_cast<const float4 *>(x + e + 4);
-            const float xa[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-            if (g.act_mode == kActRmsNorm) {
-                const float4 w0 = __ldg(reinterpret_cast<const float4 *>(g.act_y + e));
-                const float4 w1 = __ldg(reinterpret_cast<const float4 *>(g.act_y + e + 4));
-                const float wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const float *x = g.act_x + static_cast<size_t>(tok) * g.act_ld;
+        if (g.act_mode == kActSwiGLU) {
+            const float *u = g.act_y + static_cast<size_t>(tok) * g.act_ld;
+            for (int j0 = 0; j0 < per_warp; j0 += kActBatch) {
+                float xv[kActBatch][8], uv[kActBatch][8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(xa[i], scale), wa[i]);
-            } else {
-                const float *u = g.act_y + static_cast<size_t>(tok) * g.act_ld;
-                const float4 u0 = *reinterpret_cast<const float4 *>(u + e);
-                const float4 u1 = *reinterpret_cast<const float4 *>(u + e + 4);
-                const float ua[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+                for (int j = 0; j < kActBatch; ++j) {
+                    const int b = warp + (j0 + j) * warps;
+                    if (b < g.nb) {
+                        load8(x + b * 256 + lane * 8, xv[j]);
+                        load8(u + b * 256 + lane * 8, uv[j]);
+                    }
+                }
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(act_silu(xa[i]), ua[i]);
+                for (int j = 0; j < kActBatch; ++j) {
+                    const int b = warp + (j0 + j) * warps;
+                    if (b >= g.nb) break;
+                    float v[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(act_silu(xv[j][i]), uv[j][i]);
+                    store_floats(g, tok, b * 256 + lane * 8, v);
+                    store_block(slots[b], v);
+                }
             }
-            if (g.act_f_out && blockIdx.x == 0) {
-                float *o = g.act_f_out + static_cast<size_t>(tok) * width + e;
-                *reinterpret_cast<float4 *>(o) = make_float4(v[0], v[1], v[2], v[3]);
-                *reinterpret_cast<float4 *>(o + 4) = make_float4(v[4], v[5], v[6], v[7]);
+            continue;
+        }
+        // RMSNorm: sum of squares (double, per thread in block and element
+        // order, then the warp tree, then warps in order), scale, quantize.
+        float xv[kActBatch][8], wv[kActBatch][8];
+        const bool one_batch = per_warp <= kActBatch;
+        double part = 0.0;
+        for (int j0 = 0; j0 < per_warp; j0 += kActBatch) {
+#pragma unroll
+            for (int j = 0; j < kActBatch; ++j) {
+                const int b = warp + (j0 + j) * warps;
+                if (b < g.nb) {
+                    load8(x + b * 256 + lane * 8, xv[j]);
+                    if (one_batch) ldg8(g.act_y + b * 256 + lane * 8, wv[j]);  // in the same round trip
+                }
             }
-            const WarpQ8K r = act_quantize_warp(v);
-            slot.q[lane * 2] = r.q0;
-            slot.q[lane * 2 + 1] = r.q1;
-            if ((lane & 3) == 0) slot.aux[8 + (lane >> 2)] = r.sums_word;
-            if (lane == 0) slot.xs = r.scale;
+#pragma unroll
+            for (int j = 0; j < kActBatch; ++j) {
+                const int b = warp + (j0 + j) * warps;
+                if (b >= g.nb) break;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) part += static_cast<double>(__fmul_rn(xv[j][i], xv[j][i]));
+            }
+        }
+        part = act_warp_sum_d(part);
+        if (lane == 0) red[warp] = part;
+        consumer_barrier(consumers);
+        double sum = 0.0;
+        for (int w = 0; w < warps; ++w) sum += red[w];
+        consumer_barrier(consumers);  // red is reused by the next token
+        const float mean = static_cast<float>(sum / static_cast<double>(g.nb * 256));
+        const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps)));
+        for (int j0 = 0; j0 < per_warp; j0 += kActBatch) {
+            // a single batch keeps x and the weights in registers from the first pass
+            if (!one_batch) {
+#pragma unroll
+                for (int j = 0; j < kActBatch; ++j) {
+                    const int b = warp + (j0 + j) * warps;
+                    if (b < g.nb) {
+                        load8(x + b * 256 + lane * 8, xv[j]);
+                        ldg8(g.act_y + b * 256 + lane * 8, wv[j]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kActBatch; ++j) {
+                const int b = warp + (j0 + j) * warps;
+                if (b >= g.nb) break;
+                float v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(xv[j][i], scale), wv[j][i]);
+                store_floats(g, tok, b * 256 + lane * 8, v);
+                store_block(slots[b], v);
+            }
         }
     }
 }
 
+// Q8_K staging: the blocks' words (scale, 64 quant words, 8 bsum words) are
+// copied into the activation slots, kBatchWords loads in flight per thread.
+template <int MT>
+__device__ void stage_q8k_activation(const StreamArgs &g, Act *acts, int consumers)
+{
+    constexpr int kWords = 73, kBatchWords = 8;
+    const int tid = threadIdx.x;
+    const int total = MT * g.nb * kWords;
+    for (int i0 = tid; i0 < total; i0 += consumers * kBatchWords) {
+        uint32_t v[kBatchWords];
+#pragma unroll
+        for (int k = 0; k < kBatchWords; ++k) {
+            const int i = i0 + k * consumers;
+            v[k] = 0u;
+            if (i < total) {
+                const int slot = i / kWords, w = i - slot * kWords;
+                const int tok = slot / g.nb, col = slot - tok * g.nb;
+                if (tok < g.tokens)
+                    v[k] = __ldg(reinterpret_cast<const uint32_t *>(g.act + static_cast<size_t>(tok) * g.nb + col) + w);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kBatchWords; ++k) {
+            const int i = i0 + k * consumers;
+            if (i >= total) break;
+            const int slot = i / kWords, w = i - slot * kWords;
+            if (w == 0) acts[slot].xs = __uint_as_float(v[k]);
+            else if (w <= 64) acts[slot].q[w - 1] = v[k];       // quants
+            else acts[slot].aux[8 + (w - 65)] = v[k];           // bsums
+        }
+    }
+}
 template <typename Dec, int MT, bool kDbg>
 __device__ __forceinline__ void decode_column(const StreamArgs &g, const uint8_t *blk, const Act *acts, int b,
                                               int row, float (&acc)[MT], const uint2 *grid)
@@ -266,10 +377,6 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
         fence_mbar_init();
     }
     __syncthreads();
-    // Let the next kernel in the stream start its prologue (weight prefetch)
-    // while this grid drains; it waits for our completion before it touches
-    // anything we write.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (tid >= consumers) {
         // ---------------- producer warp ----------------
@@ -322,28 +429,21 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
 
     const int slots = MT * g.nb;
     if (g.act_mode == kActQ8K) {
-        // Activation columns -> shared memory in one round trip: quants, raw
-        // bsums (into aux[8..15]) and scale; tokens beyond g.tokens are zero.
-        // The per-format sums are then derived from shared memory only.
-        for (int i = tid; i < slots * 72; i += consumers) {
-            const int slot = i / 72, w = i - slot * 72;
-            const int tok = slot / g.nb, col = slot - tok * g.nb;
-            uint32_t v = 0u;
-            if (tok < g.tokens)
-                v = __ldg(reinterpret_cast<const uint32_t *>(g.act + static_cast<size_t>(tok) * g.nb + col) + 1 + w);
-            if (w < 64) acts[slot].q[w] = v;          // words 1..64: quants
-            else acts[slot].aux[8 + (w - 64)] = v;    // words 65..72: bsums
-        }
-        for (int slot = tid; slot < slots; slot += consumers) {
-            const int tok = slot / g.nb, col = slot - tok * g.nb;
-            acts[slot].xs = tok < g.tokens ? __ldg(&g.act[static_cast<size_t>(tok) * g.nb + col].scale) : 0.0f;
-        }
+        // Activation columns -> shared memory: quants, raw bsums (into
+        // aux[8..15]) and scale; tokens beyond g.tokens are zero.  The
+        // per-format sums are then derived from shared memory only.
+        stage_q8k_activation<MT>(g, acts, consumers);
     } else {
         stage_fused_activation<MT>(g, acts, reinterpret_cast<double *>(red), consumers);
     }
     consumer_barrier(consumers);
     for (int slot = tid; slot < slots; slot += consumers) Dec::aux_from_raw(acts[slot]);
     consumer_barrier(consumers);
+    // Only now let the next kernel in the stream launch and start its weight
+    // prefetch: launched earlier, its bulk copies queue ahead of this kernel's
+    // activation loads in the memory system and stall the prologue.  It still
+    // waits for our completion before it touches anything we write.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     const int grp = tid / row_threads, rt = tid - grp * row_threads;
     const bool mine_row = rt < g.tile_rows;

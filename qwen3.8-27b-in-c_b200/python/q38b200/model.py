@@ -40,6 +40,7 @@ def _bind():
         "q38_model_context_length": ([vp], u32),
         "q38cu_model_generate_greedy": ([vp, u32, u32, u32p], ctypes.c_int),
         "q38cu_model_stream": ([vp], vp),
+        "q38cu_model_step_kernels": ([vp], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -135,3 +136,7 @@ class Model:
     @property
     def stream(self):
         return self.lib.q38cu_model_stream(self.handle)
+
+    @property
+    def step_kernels(self):
+        return self.lib.q38cu_model_step_kernels(self.handle)

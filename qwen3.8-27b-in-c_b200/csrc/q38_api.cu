@@ -394,6 +394,19 @@ int q38cu_tensor_upload(Q38CuTensor *tensor, uint32_t type, uint64_t width, uint
 
 int q38cu_tensor_repack(Q38CuTensor *dst, const Q38CuTensor *src, void *stream)
 {
+    return q38::repack_tiled_with(dst, src, 0, stream);
+}
+
+}  // extern "C"
+
+namespace q38 {
+
+// q38cu_tensor_repack with a caller-chosen tile height (0: the default for the
+// row count).
+int repack_tiled_with(void *dst_tensor, const void *src_tensor, uint32_t forced_tile_rows, void *stream)
+{
+    Q38CuTensor *dst = static_cast<Q38CuTensor *>(dst_tensor);
+    const Q38CuTensor *src = static_cast<const Q38CuTensor *>(src_tensor);
     if (!dst || !src) return fail("dst and src are required%s");
     if (!check_matrix(src, src->shape[0])) return 0;
     if (src->layout != Q38CU_LAYOUT_GGUF) return fail("source must be in the GGUF layout%s");
@@ -401,7 +414,9 @@ int q38cu_tensor_repack(Q38CuTensor *dst, const Q38CuTensor *src, void *stream)
     if (!q38::superblock_bytes(static_cast<int>(src->type))) return fail("type not yet implemented on the device%s");
     const Geometry g = geometry(src->type);
     const uint64_t nb = src->shape[0] / 256, rows = src->shape[1];
-    const uint32_t tile_rows = static_cast<uint32_t>(q38::stream_tile_rows(static_cast<int>(rows)));
+    if (forced_tile_rows && (forced_tile_rows % 8 || forced_tile_rows > 256)) return fail("bad tile height%s");
+    const uint32_t tile_rows =
+        forced_tile_rows ? forced_tile_rows : static_cast<uint32_t>(q38::stream_tile_rows(static_cast<int>(rows)));
     const uint64_t nbytes = nb * g.bytes * rows_padded(rows, tile_rows);
     uint64_t scratch_bytes = 0;
     if (!stream_scratch_bytes(src->type, src->shape[0], rows, tile_rows, &scratch_bytes)) return 0;
@@ -431,6 +446,10 @@ int q38cu_tensor_repack(Q38CuTensor *dst, const Q38CuTensor *src, void *stream)
     *dst = t;
     return 1;
 }
+
+}  // namespace q38
+
+extern "C" {
 
 void q38cu_tensor_free(Q38CuTensor *tensor)
 {

@@ -76,6 +76,48 @@ __device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32
         : "memory");
 }
 
+// L2 policy for data read once: evict it before anything else.
+__device__ __forceinline__ uint64_t l2_evict_first_policy()
+{
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+
+// bulk_copy_g2s with an L2 cache-policy hint.
+__device__ __forceinline__ void bulk_copy_g2s_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                                   uint64_t policy)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+            "r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+// Prefetch [src, src + bytes) into L2 (16-byte aligned, a multiple of 16
+// bytes); nothing waits for it.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// This CTA's share of an L2 prefetch of [base, base + bytes): the range is cut
+// into gridDim.x 16-byte-aligned pieces issued in 1 MiB requests.
+__device__ __forceinline__ void prefetch_share_l2(const void *base, long long bytes)
+{
+    if (!base || bytes <= 0) return;
+    const long long n = bytes >> 4;  // 16-byte units
+    const long long g = gridDim.x, c = blockIdx.x;
+    long long lo = n * c / g, hi = n * (c + 1) / g;
+    const char *p = static_cast<const char *>(base);
+    while (lo < hi) {
+        const long long take = hi - lo < 65536 ? hi - lo : 65536;
+        bulk_prefetch_l2(p + (lo << 4), static_cast<uint32_t>(take << 4));
+        lo += take;
+    }
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
 {
     uint32_t done;

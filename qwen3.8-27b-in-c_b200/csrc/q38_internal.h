@@ -61,6 +61,22 @@ struct StreamLaunch {
     const float *act_y = nullptr;  // RMSNorm: norm weight; SwiGLU: up rows
     int act_ld = 0;
     float *act_f_out = nullptr;    // optional float copy of the activation [tokens][width]
+    // Replicas (see q38_stream.cu): inputs read from copy blockIdx % act_reps,
+    // outputs stored out_reps times; strides in bytes.
+    int act_reps = 1;
+    long long act_rep_bytes = 0, act_y_rep_bytes = 0;
+    int out_reps = 1;
+    long long out_rep_bytes = 0;
+    // L2 prefetch of the next kernel's leading weights (16-byte aligned)
+    const void *pf_ptr = nullptr;
+    long long pf_bytes = 0;
+    // SwiGLU epilogue for interleaved (gate, up) rows in 256-row tiles (see
+    // q38_stream.cu): floats to sw_act, Q8_K blocks to sw_q8 (sw_q_reps copies)
+    float *sw_act = nullptr;
+    void *sw_q8 = nullptr;
+    int *sw_counters = nullptr;
+    int sw_q_reps = 1;
+    long long sw_q_rep_bytes = 0;
 };
 
 enum : int { kActQ8K = 0, kActRmsNorm = 1, kActSwiGLU = 2 };
@@ -70,6 +86,8 @@ cudaError_t stream_plan(int type, int rows, int width, int tile_rows, int tokens
 cudaError_t launch_stream_gemm(int type, const StreamPlan &p, const StreamLaunch &l, cudaStream_t s);
 cudaError_t launch_repack_tiled(void *dst, const void *src, uint64_t rows, uint64_t nb, uint32_t tile_rows,
                                 uint32_t block_bytes, cudaStream_t s);
+// q38cu_tensor_repack with a given tile height (a multiple of 8, 8..256).
+int repack_tiled_with(void *dst_tensor, const void *src_tensor, uint32_t tile_rows, void *stream);
 
 int device_sm_count();
 // Message returned by q38cu_last_error() on this host thread.
@@ -87,8 +105,10 @@ cudaError_t launch_f32_gemm_ex(float *out, uint64_t out_ld, int accumulate, cons
                                int bb, cudaStream_t s);
 cudaError_t launch_row_f32(float *out, const void *w, uint64_t width, uint32_t tile_rows, uint64_t row, int type,
                            int be, int bb, cudaStream_t s);
+// Output row y (and its reps - 1 replicas, rep_floats apart) = row row_index[y].
 cudaError_t launch_row_f32_indexed(float *out, const void *w, uint64_t width, uint32_t tile_rows, uint64_t rows,
-                                   const uint32_t *row_index, int count, int type, int be, int bb, cudaStream_t s);
+                                   const uint32_t *row_index, int count, int type, int be, int bb, cudaStream_t s,
+                                   int reps = 1, long long rep_floats = 0);
 cudaError_t read_and_clear_status(int *status, cudaStream_t s);
 cudaError_t read_and_clear_stream_status(int *status);
 

@@ -388,7 +388,8 @@ __global__ void row_f32_kernel(float *out, const uint8_t *w, uint64_t width, uin
 // lookup inside a captured decode step): output row y is row row_index[y].
 // An id outside the tensor yields NaN and the kStatusBadToken status.
 __global__ void row_f32_indexed_kernel(float *out, const uint8_t *w, uint64_t width, uint32_t tile_rows,
-                                       uint64_t rows, const uint32_t *row_index, int type, int be, int bb)
+                                       uint64_t rows, const uint32_t *row_index, int type, int be, int bb,
+                                       int reps, long long rep_floats)
 {
     pdl_wait();
     pdl_launch_dependents();
@@ -396,15 +397,16 @@ __global__ void row_f32_indexed_kernel(float *out, const uint8_t *w, uint64_t wi
     if (i >= width) return;
     const uint64_t row = row_index[blockIdx.y];
     float *o = out + static_cast<uint64_t>(blockIdx.y) * width;
+    float v = __int_as_float(0x7fc00000);
     if (row >= rows) {
-        o[i] = __int_as_float(0x7fc00000);
         if (i == 0) atomicExch(&g_status, kStatusBadToken);
-        return;
+    } else {
+        const uint64_t nblocks = width / be;
+        const uint8_t *b = block_at(w, row, i / be, nblocks, tile_rows, bb);
+        v = element_weight(type, b, static_cast<int>(i % be));
+        if (!(type == kF32 || type == kF16 || type == kBF16)) v = __fadd_rn(v, 0.0f);
     }
-    const uint64_t nblocks = width / be;
-    const uint8_t *b = block_at(w, row, i / be, nblocks, tile_rows, bb);
-    const float v = element_weight(type, b, static_cast<int>(i % be));
-    o[i] = type == kF32 || type == kF16 || type == kBF16 ? v : __fadd_rn(v, 0.0f);
+    for (int k = 0; k < reps; ++k) o[i + k * rep_floats] = v;  // the row and its replicas
 }
 
 // ---------------------------------------------------------------------------
@@ -580,7 +582,8 @@ cudaError_t launch_row_f32(float *out, const void *w, uint64_t width, uint32_t t
 }
 
 cudaError_t launch_row_f32_indexed(float *out, const void *w, uint64_t width, uint32_t tile_rows, uint64_t rows,
-                                   const uint32_t *row_index, int count, int type, int be, int bb, cudaStream_t s)
+                                   const uint32_t *row_index, int count, int type, int be, int bb, cudaStream_t s,
+                                   int reps, long long rep_floats)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>((width + 255) / 256), static_cast<unsigned>(count));
@@ -592,7 +595,7 @@ cudaError_t launch_row_f32_indexed(float *out, const void *w, uint64_t width, ui
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, row_f32_indexed_kernel, out, static_cast<const uint8_t *>(w), width, tile_rows,
-                              rows, row_index, type, be, bb);
+                              rows, row_index, type, be, bb, reps < 1 ? 1 : reps, rep_floats);
 }
 
 cudaError_t read_and_clear_status(int *status, cudaStream_t s)

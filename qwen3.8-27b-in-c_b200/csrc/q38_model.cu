@@ -20,6 +20,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -40,6 +41,12 @@ constexpr int kVocab = 248320;
 constexpr int kMaxTokens = 8;    // tokens per launch of the batch kernels
 constexpr int kMaxDrafts = 64;   // speculative drafts per call
 constexpr int kConvRing = 16;
+// Copies of each freshly written activation (hidden rows, gate/up outputs, the
+// mixers' Q8_K blocks) and of the RMSNorm weights: every GEMV CTA reads its
+// input right after the previous kernel finishes, and 148 CTAs loading the
+// same lines at once queue at the L2 slices that hold them; CTA c reads copy
+// c % kReps instead.  The producers store all copies.
+constexpr int kReps = 8;
 
 enum : uint32_t { kF32 = 0, kF16 = 1, kQ8_0 = 8, kBF16 = 30 };
 
@@ -88,7 +95,8 @@ struct Layer {
     Proj in_proj;  // DeltaNet: qkv | z     full: q | k | v
     Proj ba;       // DeltaNet: beta | alpha
     Proj out;      // ssm_out / attn_output
-    Proj gate_up;  // ffn_gate | ffn_up
+    Proj gate_up;  // ffn_gate | ffn_up (rows interleaved gate 0, up 0, gate 1, ... when swiglu_fused)
+    bool swiglu_fused = false;  // gate_up's epilogue forms silu(gate) * up and its Q8_K blocks
     Proj down;
     float *conv_w = nullptr, *dt = nullptr, *a = nullptr, *ssm_norm = nullptr;
     float *q_norm = nullptr, *k_norm = nullptr;
@@ -136,6 +144,7 @@ struct Q38Model {
     uint32_t *ids = nullptr, *argmax_out = nullptr, *history = nullptr;
     float *attn_partials = nullptr, *argmax_part_v = nullptr;
     int *attn_counters = nullptr, *argmax_part_i = nullptr, *argmax_counters = nullptr;
+    int *swiglu_counters = nullptr;  // one per Q8_K block of the FFN activation
 
     // host staging
     float *host_logits = nullptr;
@@ -247,6 +256,60 @@ bool upload_proj(Q38Model *m, Proj *p, const std::vector<const q38::GGUFTensorIn
     return true;
 }
 
+// A norm weight vector read by GEMV prologues: kReps copies, nbytes apart.
+bool upload_norm(Q38Model *m, float **dst, const q38::GGUFTensorInfo *t)
+{
+    if (!dalloc(dst, t->nbytes / 4 * kReps, m->owned)) return false;
+    for (int k = 0; k < kReps; ++k)
+        if (!cuda_ok(cudaMemcpy(*dst + k * (t->nbytes / 4), t->data, t->nbytes, cudaMemcpyHostToDevice), "upload"))
+            return false;
+    return true;
+}
+
+// ffn_gate | ffn_up.  When both are one Q8_K integer-path type, their rows are
+// interleaved (gate i, up i) and tiled 256 rows high, so each CTA's tile
+// yields 128 SwiGLU outputs and the GEMV epilogue forms the FFN activation
+// and its Q8_K blocks itself (q38_stream.cu); otherwise a plain projection.
+bool upload_gate_up(Q38Model *m, Layer *L, const q38::GGUFTensorInfo *gate, const q38::GGUFTensorInfo *up)
+{
+    const uint64_t rows = gate->shape[1];
+    const bool fusable = gate->type == up->type && q8k_type(gate->type) &&
+                         q38::superblock_bytes(static_cast<int>(gate->type)) && gate->shape[0] == up->shape[0] &&
+                         rows == up->shape[1] && (2 * rows) % 512 == 0 &&
+                         static_cast<int>(2 * rows / 256) <= q38::device_sm_count();
+    L->swiglu_fused = false;
+    if (!fusable) return upload_proj(m, &L->gate_up, {gate, up});
+    const uint64_t row_bytes = gate->nbytes / rows;
+    if (!ensure_staging(m, 2 * gate->nbytes + 256)) return false;
+    uint8_t *st = static_cast<uint8_t *>(m->staging);
+    if (!cuda_ok(cudaMemcpy2D(st, 2 * row_bytes, gate->data, row_bytes, row_bytes, rows, cudaMemcpyHostToDevice),
+                 "gate upload") ||
+        !cuda_ok(cudaMemcpy2D(st + row_bytes, 2 * row_bytes, up->data, row_bytes, row_bytes, rows,
+                              cudaMemcpyHostToDevice),
+                 "up upload"))
+        return false;
+    Q38CuTensor src{};
+    src.type = gate->type;
+    src.n_dims = 2;
+    src.shape[0] = gate->shape[0];
+    src.shape[1] = 2 * rows;
+    src.nbytes = 2 * gate->nbytes;
+    src.data = st;
+    src.layout = Q38CU_LAYOUT_GGUF;
+    Part part;
+    part.int_path = true;
+    part.rows = static_cast<int>(2 * rows);
+    if (!q38::repack_tiled_with(&part.t, &src, 256, m->stream)) return fail("%s", q38cu_last_error());
+    if (!cuda_ok(cudaStreamSynchronize(m->stream), "upload")) return false;
+    m->tensors.push_back(part.t);
+    L->gate_up.parts.clear();
+    L->gate_up.parts.push_back(part);
+    L->gate_up.rows = part.rows;
+    L->gate_up.width = static_cast<int>(gate->shape[0]);
+    L->swiglu_fused = true;
+    return true;
+}
+
 bool upload_vec(Q38Model *m, float **dst, const q38::GGUFTensorInfo *t)
 {
     if (!dalloc(dst, t->nbytes / 4, m->owned)) return false;
@@ -287,8 +350,8 @@ bool load_layer(Q38Model *m, const q38::GGUFFile &f, int l)
             !upload_vec(m, &L.a, a) || !upload_vec(m, &L.ssm_norm, nrm))
             return false;
     }
-    return upload_vec(m, &L.attn_norm, attn_norm) && upload_vec(m, &L.post_norm, post_norm) &&
-           upload_proj(m, &L.gate_up, {gate, up}) && upload_proj(m, &L.down, {down});
+    return upload_norm(m, &L.attn_norm, attn_norm) && upload_norm(m, &L.post_norm, post_norm) &&
+           upload_gate_up(m, &L, gate, up) && upload_proj(m, &L.down, {down});
 }
 
 bool meta_is_qwen38(const q38::GGUFFile &f, uint32_t *blocks, uint32_t *nextn)
@@ -332,7 +395,7 @@ bool load_mtp(Q38Model *m, const q38::GGUFFile &f)
         return false;
     }
     if (!load_layer(m, f, kLayers) || !upload_proj(m, &m->eh_proj, {eh}) || !upload_vec(m, &m->enorm, en) ||
-        !upload_vec(m, &m->hnorm, hn) || !upload_vec(m, &m->shared_head_norm, sh))
+        !upload_vec(m, &m->hnorm, hn) || !upload_norm(m, &m->shared_head_norm, sh))
         return false;
     m->mtp_loaded = true;
     return true;
@@ -349,17 +412,17 @@ bool alloc_runtime(Q38Model *m)
     return dalloc(&m->conv_ring, static_cast<size_t>(kRecurrent) * kLinQkv * kConvRing, o) &&
            dalloc(&m->delta_state, static_cast<size_t>(kRecurrent) * kLinHeads * kLinDim * kLinDim, o) &&
            dalloc(&m->k_cache, kFull * ctx * kAttnKv, o) && dalloc(&m->v_cache, kFull * ctx * kAttnKv, o) &&
-           dalloc(&m->mtp_hidden, kHidden, o) && dalloc(&m->hidden, kMaxTokens * kHidden, o) &&
+           dalloc(&m->mtp_hidden, kHidden, o) && dalloc(&m->hidden, kReps * kMaxTokens * kHidden, o) &&
            dalloc(&m->normf, kMaxTokens * 2 * kHidden, o) &&
-           dalloc(&m->wide, kMaxTokens * static_cast<size_t>(m->wide_ld), o) &&
+           dalloc(&m->wide, kReps * kMaxTokens * static_cast<size_t>(m->wide_ld), o) &&
            dalloc(&m->ba, kMaxTokens * m->ba_ld, o) && dalloc(&m->act_f, kMaxTokens * kFfn, o) &&
            dalloc(&m->logits, kMaxTokens * static_cast<size_t>(kVocab), o) &&
-           dalloc(reinterpret_cast<uint8_t **>(&m->q8), q8_blocks * sizeof(Q38CuQ8KBlock), o) &&
+           dalloc(reinterpret_cast<uint8_t **>(&m->q8), kReps * q8_blocks * sizeof(Q38CuQ8KBlock), o) &&
            dalloc(&m->target_norm, kMaxDrafts * static_cast<size_t>(kHidden), o) &&
            dalloc(&m->ctl, 4, o) && dalloc(&m->ids, kMaxTokens, o) && dalloc(&m->argmax_out, kMaxDrafts, o) &&
            dalloc(&m->history, ctx + 1, o) &&
            dalloc(&m->attn_partials, kMaxTokens * 24 * static_cast<size_t>(m->attn_splits) * (kAttnDim + 2), o) &&
-           dalloc(&m->attn_counters, kMaxTokens * 24, o) &&
+           dalloc(&m->attn_counters, kMaxTokens * 24, o) && dalloc(&m->swiglu_counters, kFfn / 256, o) &&
            dalloc(&m->argmax_part_v, kMaxTokens * q38::kArgmaxCtas, o) &&
            dalloc(&m->argmax_part_i, kMaxTokens * q38::kArgmaxCtas, o) &&
            dalloc(&m->argmax_counters, kMaxTokens, o) &&
@@ -384,11 +447,54 @@ struct ActIn {
     const float *x = nullptr, *y = nullptr;  // fused modes
     int ld = 0;
     float *f_out = nullptr;     // fused modes: optional float copy of the activation
+    int reps = 1;               // copies of q8 / x (and y for SwiGLU), rep_bytes apart
+    long long rep_bytes = 0, y_rep_bytes = 0;  // y_rep_bytes: copies of the RMSNorm weight
 };
 
+// Copies of an output: the producer stores `reps` copies, `bytes` apart.
+struct OutReps {
+    int reps = 1;
+    long long bytes = 0;
+};
+
+// L2 prefetch of the next weight tensor's leading bytes (see q38_stream.cu):
+// at most Q38CU_PREFETCH_MB (default 0: off, the measured best for decode) MiB, 0 disables it.
+struct Prefetch {
+    const void *ptr = nullptr;
+    long long bytes = 0;
+};
+
+Prefetch prefetch_of(const Part *p)
+{
+    static const long long limit = [] {
+        const char *v = std::getenv("Q38CU_PREFETCH_MB");
+        return (v && *v ? std::atoll(v) : 0LL) << 20;
+    }();
+    Prefetch f;
+    if (!p || limit <= 0) return f;
+    f.ptr = p->t.data;
+    f.bytes = std::min<long long>(limit, static_cast<long long>(p->t.nbytes)) & ~15LL;
+    return f;
+}
+
+const Part *first_part(const Proj &p) { return p.parts.empty() ? nullptr : &p.parts[0]; }
+
+long long hidden_rep_bytes() { return static_cast<long long>(kMaxTokens) * kHidden * 4; }
+long long q8_rep_bytes() { return static_cast<long long>(kMaxTokens) * (kFfn / 256) * sizeof(Q38CuQ8KBlock); }
+long long norm_rep_bytes() { return static_cast<long long>(kHidden) * 4; }
+
 // Stream GEMM with an output stride and optional accumulation.
+// The gate_up SwiGLU epilogue's outputs (see upload_gate_up).
+struct SwigluOut {
+    float *act = nullptr;
+    void *q8 = nullptr;
+    int *counters = nullptr;
+    int reps = 1;
+    long long rep_bytes = 0;
+};
+
 bool stream_project(const Part &p, const ActIn &in, int tokens, float *out, int out_ld, int accumulate,
-                    cudaStream_t s)
+                    const OutReps &orep, const Prefetch &pf, cudaStream_t s, const SwigluOut *sw = nullptr)
 {
     const int width = static_cast<int>(p.t.shape[0]), nb = width / 256;
     for (int tok0 = 0; tok0 < tokens;) {
@@ -407,6 +513,23 @@ bool stream_project(const Part &p, const ActIn &in, int tokens, float *out, int 
         l.out_ld = out_ld;
         l.accumulate = accumulate;
         l.act_mode = in.mode;
+        l.act_reps = in.reps;
+        l.act_rep_bytes = in.rep_bytes;
+        l.act_y_rep_bytes = in.y_rep_bytes;
+        l.out_reps = orep.reps;
+        l.out_rep_bytes = orep.bytes;
+        if (tok0 == 0) {
+            l.pf_ptr = pf.ptr;
+            l.pf_bytes = pf.bytes;
+        }
+        if (sw) {
+            const int width_out = p.rows / 2;
+            l.sw_act = sw->act + static_cast<size_t>(tok0) * width_out;
+            l.sw_q8 = static_cast<Q38CuQ8KBlock *>(sw->q8) + static_cast<size_t>(tok0) * (width_out / 256);
+            l.sw_counters = sw->counters;
+            l.sw_q_reps = sw->reps;
+            l.sw_q_rep_bytes = sw->rep_bytes;
+        }
         if (in.mode != q38::kActQ8K) {
             l.act_x = in.x + static_cast<size_t>(tok0) * in.ld;
             l.act_y = in.mode == q38::kActSwiGLU ? in.y + static_cast<size_t>(tok0) * in.ld : in.y;
@@ -430,7 +553,8 @@ bool has_float_part(const Proj &p)
 // out[tok * out_ld + part.offset + row] (+)= projection of this token's input.
 // A fused input that a float-path part cannot take is materialized first
 // (RMSNorm / SwiGLU kernels into the float rows and m->q8).
-bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int out_ld, int accumulate)
+bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int out_ld, int accumulate,
+             const OutReps &orep = OutReps(), const Part *next_after = nullptr)
 {
     const cudaStream_t s = m->stream;
     const int width = p.width;
@@ -447,10 +571,15 @@ bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int o
         in.f = f;
         in.f_ld = width;
     }
-    for (const Part &part : p.parts) {
+    bool float_part = false;
+    for (size_t i = 0; i < p.parts.size(); ++i) {
+        const Part &part = p.parts[i];
+        const Part *next = i + 1 < p.parts.size() ? &p.parts[i + 1] : next_after;
         if (part.int_path) {
-            if (!stream_project(part, in, tokens, out + part.offset, out_ld, accumulate, s)) return false;
+            if (!stream_project(part, in, tokens, out + part.offset, out_ld, accumulate, orep, prefetch_of(next), s))
+                return false;
         } else {
+            float_part = true;
             const uint32_t be = q38cu_block_elements(part.t.type), bb = q38cu_block_bytes(part.t.type);
             if (!cuda_ok(q38::launch_f32_gemm_ex(out + part.offset, out_ld, accumulate, in.f, in.f_ld, tokens,
                                                  part.t.shape[0], part.t.data, part.rows, 0,
@@ -460,38 +589,57 @@ bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int o
                 return false;
         }
     }
+    // float-path parts store one copy: copy the rows to the replicas
+    if (float_part && orep.reps > 1 &&
+        !cuda_ok(q38::launch_replicate(out, static_cast<size_t>(tokens) * out_ld * 4, orep.reps, orep.bytes, s),
+                 "replicate"))
+        return false;
     return true;
 }
 
-ActIn q8_input(const void *q8, const float *f, int f_ld)
+// Q8_K blocks as input; `replicated` when their producer stored kReps copies.
+ActIn q8_input(const void *q8, const float *f, int f_ld, bool replicated = false)
 {
     ActIn in;
     in.q8 = q8;
     in.f = f;
     in.f_ld = f_ld;
+    if (replicated) {
+        in.reps = kReps;
+        in.rep_bytes = q8_rep_bytes();
+    }
     return in;
 }
 
-ActIn rmsnorm_input(const float *x, int ld, const float *weight, float *f_out = nullptr)
+// RMSNorm(hidden rows) * weight, both replicated.
+ActIn rmsnorm_input(const float *hidden, const float *weight, float *f_out = nullptr)
 {
     ActIn in;
     in.mode = q38::kActRmsNorm;
-    in.x = x;
+    in.x = hidden;
     in.y = weight;
-    in.ld = ld;
+    in.ld = kHidden;
     in.f_out = f_out;
+    in.reps = kReps;
+    in.rep_bytes = hidden_rep_bytes();
+    in.y_rep_bytes = norm_rep_bytes();
     return in;
 }
 
-ActIn swiglu_input(const float *gate, const float *up, int ld)
+// silu(gate) * up from the replicated gate/up rows.
+ActIn swiglu_input(const Q38Model *m)
 {
     ActIn in;
     in.mode = q38::kActSwiGLU;
-    in.x = gate;
-    in.y = up;
-    in.ld = ld;
+    in.x = m->wide;
+    in.y = m->wide + kFfn;
+    in.ld = m->wide_ld;
+    in.reps = kReps;
+    in.rep_bytes = static_cast<long long>(kMaxTokens) * m->wide_ld * 4;
     return in;
 }
+
+OutReps hidden_out() { return OutReps{kReps, hidden_rep_bytes()}; }
 
 // ssm_beta | ssm_alpha as one Q8_0 tensor: the DeltaNet kernel forms both
 // projections itself.
@@ -506,9 +654,12 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
     (void)base_hint;
     const Layer &L = m->layers[l];
     const cudaStream_t s = m->stream;
-    const ActIn attn_in = rmsnorm_input(m->hidden, kHidden, L.attn_norm);
-    if (!project(m, L.in_proj, attn_in, tokens, m->wide, m->wide_ld, 0)) return false;
-    const ActIn mixed = q8_input(m->q8, m->act_f, L.full ? kAttnQ : kLinV);
+    const ActIn attn_in = rmsnorm_input(m->hidden, L.attn_norm);
+    // the weight tensor streamed after this layer's ffn_down
+    const Part *after = l + 1 < kLayers ? first_part(m->layers[l + 1].in_proj) : first_part(m->output);
+    const Prefetch mixer_pf = prefetch_of(first_part(L.gate_up));
+    if (!project(m, L.in_proj, attn_in, tokens, m->wide, m->wide_ld, 0, OutReps(), first_part(L.out))) return false;
+    const ActIn mixed = q8_input(m->q8, m->act_f, L.full ? kAttnQ : kLinV, true);
     if (L.full) {
         q38::AttnArgs a{};
         a.qkv = m->wide;
@@ -527,6 +678,10 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         a.counters = m->attn_counters;
         a.out_f = m->act_f;
         a.out_q = m->q8;
+        a.reps = kReps;
+        a.q_rep_bytes = q8_rep_bytes();
+        a.pf_ptr = mixer_pf.ptr;
+        a.pf_bytes = mixer_pf.bytes;
         if (!cuda_ok(q38::launch_attention(a, s), "attention")) return false;
     } else {
         q38::DeltaArgs d{};
@@ -535,6 +690,7 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
             d.ba_w = static_cast<const uint8_t *>(L.ba.parts[0].t.data);
             d.hidden = m->hidden;
             d.attn_norm = L.attn_norm;
+            d.hidden_rep_bytes = hidden_rep_bytes();
         } else {
             if (!project(m, L.ba, attn_in, tokens, m->ba, m->ba_ld, 0)) return false;
             d.beta = m->ba;
@@ -554,12 +710,32 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         d.tokens = tokens;
         d.out_f = m->act_f;
         d.out_q = m->q8;
+        d.reps = kReps;
+        d.q_rep_bytes = q8_rep_bytes();
+        d.pf_ptr = mixer_pf.ptr;
+        d.pf_bytes = mixer_pf.bytes;
         if (!cuda_ok(q38::launch_deltanet(d, s), "deltanet")) return false;
     }
-    if (!project(m, L.out, mixed, tokens, m->hidden, kHidden, 1)) return false;
-    if (!project(m, L.gate_up, rmsnorm_input(m->hidden, kHidden, L.post_norm), tokens, m->wide, m->wide_ld, 0))
+    if (!project(m, L.out, mixed, tokens, m->hidden, kHidden, 1, hidden_out(), first_part(L.gate_up))) return false;
+    if (L.swiglu_fused) {
+        // gate_up's epilogue leaves silu(gate) * up in act_f and its Q8_K blocks in q8
+        SwigluOut sw;
+        sw.act = m->act_f;
+        sw.q8 = m->q8;
+        sw.counters = m->swiglu_counters;
+        sw.reps = kReps;
+        sw.rep_bytes = q8_rep_bytes();
+        if (!stream_project(L.gate_up.parts[0], rmsnorm_input(m->hidden, L.post_norm), tokens, nullptr, 0, 0,
+                            OutReps(), prefetch_of(first_part(L.down)), s, &sw))
+            return false;
+        return project(m, L.down, q8_input(m->q8, m->act_f, kFfn, true), tokens, m->hidden, kHidden, 1,
+                       hidden_out(), after);
+    }
+    const OutReps wide_out{kReps, static_cast<long long>(kMaxTokens) * m->wide_ld * 4};
+    if (!project(m, L.gate_up, rmsnorm_input(m->hidden, L.post_norm), tokens, m->wide, m->wide_ld, 0, wide_out,
+                 first_part(L.down)))
         return false;
-    return project(m, L.down, swiglu_input(m->wide, m->wide + kFfn, m->wide_ld), tokens, m->hidden, kHidden, 1);
+    return project(m, L.down, swiglu_input(m), tokens, m->hidden, kHidden, 1, hidden_out(), after);
 }
 
 // Embedding rows of `tokens` ids held in device memory.
@@ -568,7 +744,8 @@ bool enqueue_embed(Q38Model *m, const Q38CuTensor &emb, const uint32_t *d_ids, i
     const uint32_t be = q38cu_block_elements(emb.type), bb = q38cu_block_bytes(emb.type);
     return cuda_ok(q38::launch_row_f32_indexed(out, emb.data, kHidden, 0, emb.shape[1], d_ids, tokens,
                                                static_cast<int>(emb.type), static_cast<int>(be),
-                                               static_cast<int>(bb), m->stream),
+                                               static_cast<int>(bb), m->stream, kReps,
+                                               hidden_rep_bytes() / 4),
                    "embedding");
 }
 
@@ -579,7 +756,9 @@ bool enqueue_head(Q38Model *m, const float *norm_w, const Proj &head, int tokens
                   bool feed, int advance)
 {
     const cudaStream_t s = m->stream;
-    if (!project(m, head, rmsnorm_input(m->hidden, kHidden, norm_w, norm_out), tokens, m->logits, kVocab, 0))
+    // the next step starts with layer 0's input projection
+    if (!project(m, head, rmsnorm_input(m->hidden, norm_w, norm_out), tokens, m->logits, kVocab, 0, OutReps(),
+                 first_part(m->layers[0].in_proj)))
         return false;
     q38::ArgmaxArgs a{};
     a.logits = m->logits;
@@ -629,7 +808,7 @@ bool enqueue_mtp_body(Q38Model *m, const uint32_t *d_ids, int n, const float *pr
         ok = cuda_ok(q38::launch_rmsnorm_quant(prev_rows, kHidden, m->hnorm, kHidden, n - 1, m->normf + w2 + kHidden,
                                                w2, q8 + nb2 + nb, s, nb2),
                      "rmsnorm");
-    return ok && project(m, m->eh_proj, q8_input(m->q8, m->normf, w2), n, m->hidden, kHidden, 0) &&
+    return ok && project(m, m->eh_proj, q8_input(m->q8, m->normf, w2), n, m->hidden, kHidden, 0, hidden_out()) &&
            enqueue_layer(m, kLayers, n, 0);
 }
 
@@ -821,7 +1000,7 @@ Q38Model *q38_model_open_gguf(const char *path, uint32_t context_length)
         ok = emb && on && out && expect(emb, kHidden, kVocab, false) && expect(on, kHidden, 0, true) &&
              expect(out, kHidden, kVocab, false);
         if (!ok && !(emb && on && out)) fail("missing token_embd, output_norm or output tensor%s");
-        ok = ok && upload_embedding(m, &m->embedding, emb) && upload_vec(m, &m->output_norm, on) &&
+        ok = ok && upload_embedding(m, &m->embedding, emb) && upload_norm(m, &m->output_norm, on) &&
              upload_proj(m, &m->output, {out});
     }
     for (int l = 0; ok && l < kLayers; ++l) ok = load_layer(m, m->gguf, l);

@@ -25,6 +25,10 @@ struct DeltaArgs {
     int ba_fused;
     const uint8_t *ba_w;
     const float *hidden, *attn_norm;  // [tokens][5120], [5120]
+    // replicas: hidden is read from copy blockIdx % reps (hidden_rep_bytes
+    // apart); out_q is written to all reps copies (q_rep_bytes apart)
+    int reps;
+    long long hidden_rep_bytes, q_rep_bytes;
     const float *conv_w;  // [10240][4]
     float *conv_ring;     // [10240][16]
     const float *dt, *a;  // [48]
@@ -34,6 +38,8 @@ struct DeltaArgs {
     int tokens;
     float *out_f;  // optional [tokens][6144]
     void *out_q;   // [tokens][24] Q8_K
+    const void *pf_ptr;   // L2 prefetch of the next kernel's leading weights
+    long long pf_bytes;
 };
 
 struct AttnArgs {
@@ -47,7 +53,11 @@ struct AttnArgs {
     float *partials;  // [tokens * 24 * splits][258]
     int *counters;    // [tokens * 24], zero between launches
     float *out_f;     // optional [tokens][6144]
-    void *out_q;      // [tokens][24] Q8_K
+    void *out_q;      // [tokens][24] Q8_K, written to all reps copies q_rep_bytes apart
+    int reps;
+    long long q_rep_bytes;
+    const void *pf_ptr;   // L2 prefetch of the next kernel's leading weights
+    long long pf_bytes;
 };
 
 struct ArgmaxArgs {
@@ -61,6 +71,8 @@ struct ArgmaxArgs {
     int advance;    // added to ctl[1]
     uint32_t *history;
     int history_len;  // appends stop at this many tokens
+    const void *pf_ptr;   // L2 prefetch of the next kernel's leading weights
+    long long pf_bytes;
 };
 
 // RMSNorm of `tokens` rows of n floats, written as floats (out_f, optional)
@@ -74,5 +86,7 @@ cudaError_t launch_deltanet(const DeltaArgs &args, cudaStream_t s);
 cudaError_t launch_attention(const AttnArgs &args, cudaStream_t s);
 cudaError_t launch_argmax(const ArgmaxArgs &args, int tokens, cudaStream_t s);
 cudaError_t read_and_clear_model_status(int *status);
+// Copies rows [0, bytes) of `base` to its replicas 1 .. reps - 1 (stride bytes apart).
+cudaError_t launch_replicate(void *base, size_t bytes, int reps, long long stride, cudaStream_t s);
 
 }  // namespace q38

@@ -116,7 +116,7 @@ __device__ __forceinline__ AbsMax warp_absmax(AbsMax m)
 
 // Q8_K quantization of 256 values held one per thread by a 256-thread CTA
 // (qwen38_quant.c:50-88, bit-exact): thread i owns element i.
-__device__ void quantize_block_256(float v, Q8KBlock *dst, AbsMax *red)
+__device__ void quantize_block_256(float v, Q8KBlock *dst, AbsMax *red, int reps = 1, long long rep_bytes = 0)
 {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     AbsMax m{fabsf(v), tid, v};
@@ -132,12 +132,15 @@ __device__ void quantize_block_256(float v, Q8KBlock *dst, AbsMax *red)
         inverse = __fdiv_rn(-127.0f, best.v);
         q = min(nearest_int(__fmul_rn(inverse, v)), 127);
     }
-    reinterpret_cast<int8_t *>(dst->quants)[tid] = static_cast<int8_t>(q);
     int sum = q;
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if ((lane & 15) == 0) dst->sums[tid >> 4] = static_cast<int16_t>(sum);
-    if (tid == 0) dst->scale = best.a != 0.0f ? __fdiv_rn(1.0f, inverse) : 0.0f;
+    for (int k = 0; k < (reps > 1 ? reps : 1); ++k) {  // the block and its replicas
+        Q8KBlock *d = reinterpret_cast<Q8KBlock *>(reinterpret_cast<char *>(dst) + k * rep_bytes);
+        reinterpret_cast<int8_t *>(d->quants)[tid] = static_cast<int8_t>(q);
+        if ((lane & 15) == 0) d->sums[tid >> 4] = static_cast<int16_t>(sum);
+        if (tid == 0) d->scale = best.a != 0.0f ? __fdiv_rn(1.0f, inverse) : 0.0f;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -237,7 +240,6 @@ struct __align__(16) DeltaShared {
 // address so the loads do not wait on one another.
 struct ConvTaps {
     float t0, t1, t2, x;
-    float4 w;
 };
 
 __device__ __forceinline__ const float *conv_tap_ptr(const DeltaArgs &a, int ch, int p, int base)
@@ -253,17 +255,21 @@ __device__ __forceinline__ ConvTaps load_taps(const DeltaArgs &a, int ch, int po
     c.t1 = *conv_tap_ptr(a, ch, pos - 2, base);
     c.t2 = *conv_tap_ptr(a, ch, pos - 1, base);
     c.x = a.qkvz[static_cast<size_t>(pos - base) * a.qkvz_ld + ch];
-    c.w = __ldg(reinterpret_cast<const float4 *>(a.conv_w + static_cast<size_t>(ch) * 4));
     return c;
 }
 
-// ((s0 k0 + s1 k1) + s2 k2) + x k3, then SiLU (qwen38_model.c:722-737).
-__device__ __forceinline__ float conv_silu(const ConvTaps &c)
+__device__ __forceinline__ float4 conv_kernel(const DeltaArgs &a, int ch)
 {
-    float v = __fmul_rn(c.t0, c.w.x);
-    v = __fadd_rn(v, __fmul_rn(c.t1, c.w.y));
-    v = __fadd_rn(v, __fmul_rn(c.t2, c.w.z));
-    v = __fadd_rn(v, __fmul_rn(c.x, c.w.w));
+    return __ldg(reinterpret_cast<const float4 *>(a.conv_w + static_cast<size_t>(ch) * 4));
+}
+
+// ((s0 k0 + s1 k1) + s2 k2) + x k3, then SiLU (qwen38_model.c:722-737).
+__device__ __forceinline__ float conv_silu(const ConvTaps &c, const float4 w)
+{
+    float v = __fmul_rn(c.t0, w.x);
+    v = __fadd_rn(v, __fmul_rn(c.t1, w.y));
+    v = __fadd_rn(v, __fmul_rn(c.t2, w.z));
+    v = __fadd_rn(v, __fmul_rn(c.x, w.w));
     return silu(v);
 }
 
@@ -274,19 +280,24 @@ __device__ __forceinline__ float conv_silu(const ConvTaps &c)
 // caller's barrier publishes the sum of squares) writes the normed row to
 // shared memory and loads the thread's Q8_0 blocks; phase 3 forms the dots.
 struct BaLoads {
-    float4 h[10], w[10];
+    float4 h[10], w[10];  // hidden row (per token), norm weights (loaded once, before the grid dependency)
 };
+
+__device__ __forceinline__ void ba_load_weights(const DeltaArgs &a, BaLoads &l)
+{
+    const float4 *w4 = reinterpret_cast<const float4 *>(a.attn_norm);
+#pragma unroll
+    for (int j = 0; j < 10; ++j) l.w[j] = __ldg(w4 + threadIdx.x + 128 * j);
+}
 
 __device__ __forceinline__ void ba_load_row(const DeltaArgs &a, int t, BaLoads &l)
 {
-    const int tid = threadIdx.x;
-    const float4 *h4 = reinterpret_cast<const float4 *>(a.hidden + static_cast<size_t>(t) * 5120);
-    const float4 *w4 = reinterpret_cast<const float4 *>(a.attn_norm);
+    const float *hidden = a.reps > 1 ? reinterpret_cast<const float *>(reinterpret_cast<const char *>(a.hidden) +
+                                                                       (blockIdx.x % a.reps) * a.hidden_rep_bytes)
+                                     : a.hidden;
+    const float4 *h4 = reinterpret_cast<const float4 *>(hidden + static_cast<size_t>(t) * 5120);
 #pragma unroll
-    for (int j = 0; j < 10; ++j) {
-        l.h[j] = h4[tid + 128 * j];
-        l.w[j] = __ldg(w4 + tid + 128 * j);
-    }
+    for (int j = 0; j < 10; ++j) l.h[j] = h4[threadIdx.x + 128 * j];
 }
 
 __device__ __forceinline__ double ba_sum_squares(const BaLoads &l)
@@ -366,6 +377,13 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
     const int vh = 2 * cidx + rank / 4, quarter = rank & 3, kh = vh % 16;
     const int col0 = quarter * 32;
     const bool qk_writer = vh < 16 && quarter == 0;
+    const int ch_q = kh * 128 + tid, ch_k = 2048 + kh * 128 + tid;
+    const int ch_v = 4096 + vh * 128 + col0 + (tid & 31);
+    // weights do not depend on the previous kernel: load them before waiting
+    const float4 wq = conv_kernel(a, ch_q), wk = conv_kernel(a, ch_k), wvv = conv_kernel(a, ch_v);
+    BaLoads bl;
+    if (a.ba_fused) ba_load_weights(a, bl);
+    if (tid == 0) prefetch_share_l2(a.pf_ptr, a.pf_bytes);  // keeps HBM busy through this latency-bound step
 
     pdl_wait();
     const int base = a.ctl[1];
@@ -380,12 +398,9 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
         float4 s[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) s[j] = *reinterpret_cast<const float4 *>(state + j * 128);
-        const int ch_q = kh * 128 + tid, ch_k = 2048 + kh * 128 + tid;
-        const int ch_v = 4096 + vh * 128 + col0 + (tid & 31);
         const ConvTaps cq = load_taps(a, ch_q, pos, base);
         const ConvTaps ck = load_taps(a, ch_k, pos, base);
         const ConvTaps cv = load_taps(a, ch_v, pos, base);
-        BaLoads bl;
         if (a.ba_fused) ba_load_row(a, t, bl);
         float beta_raw = 0.0f, alpha_raw = 0.0f;
         if (!a.ba_fused && tid == 0) {
@@ -402,8 +417,8 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
         if (tid < 32) a.conv_ring[static_cast<size_t>(ch_v) * kConvRing + (pos & (kConvRing - 1))] = cv.x;
 
         // causal conv + SiLU, then the L2 norms of q and k (qwen38_model.c:608-614)
-        const float qv = conv_silu(cq), kv = conv_silu(ck);
-        if (tid < 32) sh.v[tid] = conv_silu(cv);
+        const float qv = conv_silu(cq, wq), kv = conv_silu(ck, wk);
+        if (tid < 32) sh.v[tid] = conv_silu(cv, wvv);
         const double pq = warp_sum_d(static_cast<double>(__fmul_rn(qv, qv)));
         const double pk = warp_sum_d(static_cast<double>(__fmul_rn(kv, kv)));
         const double ph = a.ba_fused ? warp_sum_d(ba_sum_squares(bl)) : 0.0;
@@ -507,12 +522,16 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
                 q = min(nearest_int(__fmul_rn(inverse, o)), 127);
             }
             const int e = (rank / 4) * 128 + col0 + tid;
-            reinterpret_cast<int8_t *>(dst->quants)[e] = static_cast<int8_t>(q);
             int sum = q;
 #pragma unroll
             for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-            if ((tid & 15) == 0) dst->sums[e >> 4] = static_cast<int16_t>(sum);
-            if (rank == 0 && tid == 0) dst->scale = best.a != 0.0f ? __fdiv_rn(1.0f, inverse) : 0.0f;
+            const int reps = a.reps > 1 ? a.reps : 1;
+            for (int k = 0; k < reps; ++k) {
+                Q8KBlock *d = reinterpret_cast<Q8KBlock *>(reinterpret_cast<char *>(dst) + k * a.q_rep_bytes);
+                reinterpret_cast<int8_t *>(d->quants)[e] = static_cast<int8_t>(q);
+                if ((tid & 15) == 0) d->sums[e >> 4] = static_cast<int16_t>(sum);
+                if (rank == 0 && tid == 0) d->scale = best.a != 0.0f ? __fdiv_rn(1.0f, inverse) : 0.0f;
+            }
         }
     }
     cluster.sync();  // peers may still read this CTA's exchange slots
@@ -573,6 +592,7 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
     const int th = blockIdx.x / a.splits;
     const int h = th % kAttnHeads, t = th / kAttnHeads;
     const int g = h / (kAttnHeads / 4);
+    if (d == 0) prefetch_share_l2(a.pf_ptr, a.pf_bytes);  // keeps HBM busy through this latency-bound step
 
     pdl_wait();
     const int base = a.ctl[1];
@@ -665,7 +685,8 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
     float o = __fdiv_rn(num, den);
     o = __fmul_rn(o, sigmoid(row[h * 512 + 256 + d]));
     if (a.out_f) a.out_f[static_cast<size_t>(t) * 6144 + h * 256 + d] = o;
-    quantize_block_256(o, static_cast<Q8KBlock *>(a.out_q) + static_cast<size_t>(t) * 24 + h, sh.red_m);
+    quantize_block_256(o, static_cast<Q8KBlock *>(a.out_q) + static_cast<size_t>(t) * 24 + h, sh.red_m, a.reps,
+                       a.q_rep_bytes);
     if (d == 0) a.counters[th] = 0;
 }
 
@@ -781,6 +802,26 @@ cudaError_t launch_attention(const AttnArgs &args, cudaStream_t s)
 cudaError_t launch_argmax(const ArgmaxArgs &args, int tokens, cudaStream_t s)
 {
     return launch_pdl(argmax_kernel, dim3(kArgmaxCtas, tokens), dim3(256), s, args);
+}
+
+namespace {
+__global__ void replicate_kernel(char *base, size_t words, int reps, long long stride)
+{
+    pdl_wait();
+    pdl_launch_dependents();
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= words) return;
+    const uint32_t v = reinterpret_cast<const uint32_t *>(base)[i];
+    for (int k = 1; k < reps; ++k) reinterpret_cast<uint32_t *>(base + k * stride)[i] = v;
+}
+}  // namespace
+
+cudaError_t launch_replicate(void *base, size_t bytes, int reps, long long stride, cudaStream_t s)
+{
+    if (reps <= 1 || bytes == 0) return cudaSuccess;
+    const size_t words = bytes / 4;
+    return launch_pdl(replicate_kernel, dim3(static_cast<unsigned>((words + 255) / 256)), dim3(256), s,
+                      static_cast<char *>(base), words, reps, stride);
 }
 
 cudaError_t read_and_clear_model_status(int *status)

@@ -81,6 +81,32 @@ struct StreamArgs {
     const float *act_y;   // kActRmsNorm: norm weight [width]; kActSwiGLU: up rows
     int act_ld;
     float *act_f_out;     // optional: CTA 0 stores the float activation [tokens][width]
+    // Replicated inputs: act / act_x (and act_y in SwiGLU mode) exist act_reps
+    // times, act_rep_bytes apart, and so do the RMSNorm weights
+    // (act_y_rep_bytes apart); CTA c reads copy c % act_reps, so fewer CTAs
+    // load the same freshly written lines at the same time.
+    int act_reps;
+    long long act_rep_bytes, act_y_rep_bytes;
+    // Replicated output: each final row value is also stored out_reps - 1
+    // more times, out_rep_bytes apart, for the next kernel's readers.
+    int out_reps;
+    long long out_rep_bytes;
+    // L2 prefetch of the next kernel's leading weights (each CTA its share),
+    // issued once this CTA's ring is full: it keeps HBM busy while this kernel
+    // and the next wait on their activations.
+    const uint8_t *pf_ptr;
+    long long pf_bytes;
+    // SwiGLU epilogue (sw_act != nullptr): rows come in (gate i, up i) pairs,
+    // 2i and 2i + 1, and a tile is 256 rows = 128 outputs = half a Q8_K
+    // block.  Instead of the rows, the kernel stores sw_act[tok][i] =
+    // silu(gate) * up, and the second CTA to finish a Q8_K block quantizes it
+    // into sw_q8[tok][block] (sw_q_reps copies, sw_q_rep_bytes apart).
+    float *sw_act;
+    Q8KBlock *sw_q8;
+    int *sw_counters;  // one per Q8_K block, zero between launches
+    int sw_width;      // outputs per token (rows / 2)
+    int sw_q_reps;
+    long long sw_q_rep_bytes;
     float *partials;
     int *counters;
     int max_slots;
@@ -93,7 +119,17 @@ struct StreamArgs {
 __device__ __forceinline__ void store_row(const StreamArgs &g, int tok, int row, float v)
 {
     float *dst = g.out + static_cast<size_t>(tok) * g.out_ld + row;
-    *dst = g.accumulate ? __fadd_rn(*dst, v) : v;
+    const float r = g.accumulate ? __fadd_rn(*dst, v) : v;
+    *dst = r;
+    for (int k = 1; k < g.out_reps; ++k)
+        *reinterpret_cast<float *>(reinterpret_cast<char *>(dst) + k * g.out_rep_bytes) = r;
+}
+
+template <typename T>
+__device__ __forceinline__ const T *replica(const T *p, long long bytes, int reps)
+{
+    return reps > 1 ? reinterpret_cast<const T *>(reinterpret_cast<const char *>(p) + (blockIdx.x % reps) * bytes)
+                    : p;
 }
 
 __host__ __device__ __forceinline__ int cta_of_unit(long long u, long long units, int grid)
@@ -191,12 +227,34 @@ __device__ __forceinline__ void store_floats(const StreamArgs &g, int tok, int e
 // 8l .. 8l + 7 of each.  Every CTA computes the same values in the same order
 // (the order depends only on the shape); CTA 0 also stores the floats when
 // asked.
+// The RMSNorm weights do not depend on the previous kernel: when a warp's
+// blocks fit one batch they are loaded before the grid dependency resolves.
 template <int MT>
-__device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *red, int consumers)
+__device__ __forceinline__ bool preload_norm_weights(const StreamArgs &g, int consumers,
+                                                     float (&wv)[ActBatch<MT>::kValue][8])
+{
+    constexpr int kActBatch = ActBatch<MT>::kValue;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = consumers >> 5;
+    if (g.act_mode != kActRmsNorm || (g.nb + warps - 1) / warps > kActBatch) return false;
+    const float *w = replica(g.act_y, g.act_y_rep_bytes, g.act_reps);
+#pragma unroll
+    for (int j = 0; j < kActBatch; ++j) {
+        const int b = warp + j * warps;
+        if (b < g.nb) ldg8(w + b * 256 + lane * 8, wv[j]);
+    }
+    return true;
+}
+
+template <int MT>
+__device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *red, int consumers,
+                                       const float (&wpre)[ActBatch<MT>::kValue][8], bool preloaded)
 {
     constexpr int kActBatch = ActBatch<MT>::kValue;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, warps = consumers >> 5;
     const int per_warp = (g.nb + warps - 1) / warps;
+    const float *act_x = replica(g.act_x, g.act_rep_bytes, g.act_reps);
+    const float *act_y = g.act_mode == kActSwiGLU ? replica(g.act_y, g.act_rep_bytes, g.act_reps)
+                                                  : replica(g.act_y, g.act_y_rep_bytes, g.act_reps);
     for (int tok = 0; tok < MT; ++tok) {
         Act *slots = acts + tok * g.nb;
         if (tok >= g.tokens) {
@@ -207,9 +265,9 @@ __device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *r
             }
             continue;
         }
-        const float *x = g.act_x + static_cast<size_t>(tok) * g.act_ld;
+        const float *x = act_x + static_cast<size_t>(tok) * g.act_ld;
         if (g.act_mode == kActSwiGLU) {
-            const float *u = g.act_y + static_cast<size_t>(tok) * g.act_ld;
+            const float *u = act_y + static_cast<size_t>(tok) * g.act_ld;
             for (int j0 = 0; j0 < per_warp; j0 += kActBatch) {
                 float xv[kActBatch][8], uv[kActBatch][8];
 #pragma unroll
@@ -244,7 +302,14 @@ __device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *r
                 const int b = warp + (j0 + j) * warps;
                 if (b < g.nb) {
                     load8(x + b * 256 + lane * 8, xv[j]);
-                    if (one_batch) ldg8(g.act_y + b * 256 + lane * 8, wv[j]);  // in the same round trip
+                    if (one_batch) {
+                        if (preloaded) {
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) wv[j][i] = wpre[j][i];
+                        } else {
+                            ldg8(act_y + b * 256 + lane * 8, wv[j]);  // in the same round trip
+                        }
+                    }
                 }
             }
 #pragma unroll
@@ -271,7 +336,7 @@ __device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *r
                     const int b = warp + (j0 + j) * warps;
                     if (b < g.nb) {
                         load8(x + b * 256 + lane * 8, xv[j]);
-                        ldg8(g.act_y + b * 256 + lane * 8, wv[j]);
+                        ldg8(act_y + b * 256 + lane * 8, wv[j]);
                     }
                 }
             }
@@ -297,6 +362,7 @@ __device__ void stage_q8k_activation(const StreamArgs &g, Act *acts, int consume
     constexpr int kWords = 73, kBatchWords = 8;
     const int tid = threadIdx.x;
     const int total = MT * g.nb * kWords;
+    const Q8KBlock *act = replica(g.act, g.act_rep_bytes, g.act_reps);
     for (int i0 = tid; i0 < total; i0 += consumers * kBatchWords) {
         uint32_t v[kBatchWords];
 #pragma unroll
@@ -307,7 +373,7 @@ __device__ void stage_q8k_activation(const StreamArgs &g, Act *acts, int consume
                 const int slot = i / kWords, w = i - slot * kWords;
                 const int tok = slot / g.nb, col = slot - tok * g.nb;
                 if (tok < g.tokens)
-                    v[k] = __ldg(reinterpret_cast<const uint32_t *>(g.act + static_cast<size_t>(tok) * g.nb + col) + w);
+                    v[k] = __ldg(reinterpret_cast<const uint32_t *>(act + static_cast<size_t>(tok) * g.nb + col) + w);
             }
         }
 #pragma unroll
@@ -321,6 +387,50 @@ __device__ void stage_q8k_activation(const StreamArgs &g, Act *acts, int consume
         }
     }
 }
+// SwiGLU epilogue of a whole 256-row tile t (see StreamArgs::sw_act): adjacent
+// lanes hold gate and up of one output (the upstream q38_swiglu,
+// qwen38_model.c:523-541); the Q8_K block of outputs 256 (t / 2) .. + 255 is
+// quantized (qwen38_quant.c:50-88) by whichever of its two CTAs finishes last.
+template <int MT>
+__device__ void swiglu_epilogue(const StreamArgs &g, int t, int rt, int grp, bool failed, const float (&total)[MT],
+                                int consumers, volatile int *last_flag)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool pair_lead = (rt & 1) == 0;
+    const int i = (t * 256 + rt) >> 1;  // output index
+#pragma unroll
+    for (int tok = 0; tok < MT; ++tok) {
+        const float up = __shfl_xor_sync(0xffffffffu, total[tok], 1);
+        if (grp == 0 && pair_lead && !failed && tok < g.tokens)
+            g.sw_act[static_cast<size_t>(tok) * g.sw_width + i] = __fmul_rn(act_silu(total[tok]), up);
+    }
+    __threadfence();
+    consumer_barrier(consumers);
+    const int block = t >> 1;
+    if (threadIdx.x == 0) *last_flag = !failed && atomicAdd(&g.sw_counters[block], 1) == 1;
+    consumer_barrier(consumers);
+    if (!*last_flag) return;
+    __threadfence();
+    if (warp < MT && warp < g.tokens) {
+        const float *src = g.sw_act + static_cast<size_t>(warp) * g.sw_width + block * 256 + lane * 8;
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = __ldcg(src + k);
+        const WarpQ8K r = act_quantize_warp(v);
+        for (int k = 0; k < g.sw_q_reps; ++k) {
+            Q8KBlock *d = reinterpret_cast<Q8KBlock *>(reinterpret_cast<char *>(
+                              g.sw_q8 + static_cast<size_t>(warp) * (g.sw_width / 256) + block) +
+                          k * g.sw_q_rep_bytes);
+            uint32_t *q = reinterpret_cast<uint32_t *>(d->quants);
+            q[lane * 2] = r.q0;
+            q[lane * 2 + 1] = r.q1;
+            if ((lane & 3) == 0) reinterpret_cast<uint32_t *>(d->sums)[lane >> 2] = r.sums_word;
+            if (lane == 0) d->scale = r.scale;
+        }
+    }
+    if (threadIdx.x == 0) g.sw_counters[block] = 0;
+}
+
 template <typename Dec, int MT, bool kDbg>
 __device__ __forceinline__ void decode_column(const StreamArgs &g, const uint8_t *blk, const Act *acts, int b,
                                               int row, float (&acc)[MT], const uint2 *grid)
@@ -384,18 +494,24 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
             ChunkWalk w;
             w.init(u0, u1, g.nb, g.chunk);
             int q = 0, grp = 0, slot = 0, wrap = 0;
+            bool prefetched = false;
+            const uint64_t stream_policy = l2_evict_first_policy();  // weights are read once per step
             const size_t unit_bytes = static_cast<size_t>(g.tile_rows) * g.block_bytes;
             for (; !w.done(); ++q) {
                 const int n = w.len();
                 const int s = grp * g.stages + slot;
                 if (wrap > 0) {
+                    if (!prefetched) {
+                        prefetch_share_l2(g.pf_ptr, g.pf_bytes);
+                        prefetched = true;
+                    }
                     if (!mbar_wait_bounded(&empty[s], static_cast<uint32_t>(wrap - 1) & 1u, &g_stream_status)) break;
                     fence_proxy_async_shared();
                 }
                 const uint32_t bytes = static_cast<uint32_t>(n * unit_bytes);
                 mbar_arrive_expect_tx(&full[s], bytes);
-                bulk_copy_g2s(stage_mem + static_cast<size_t>(s) * g.stage_bytes,
-                              g.weights + static_cast<size_t>(w.u) * unit_bytes, bytes, &full[s]);
+                bulk_copy_g2s_hint(stage_mem + static_cast<size_t>(s) * g.stage_bytes,
+                                   g.weights + static_cast<size_t>(w.u) * unit_bytes, bytes, &full[s], stream_policy);
                 *issued = q + 1;
                 w.next(n);
                 if (++grp == g.groups) {
@@ -403,6 +519,7 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
                     if (++slot == g.stages) { slot = 0; ++wrap; }
                 }
             }
+            if (!prefetched) prefetch_share_l2(g.pf_ptr, g.pf_bytes);
         }
         return;
     }
@@ -425,6 +542,8 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
             }
         }
     }
+    float wpre[ActBatch<MT>::kValue][8];
+    const bool preloaded = preload_norm_weights<MT>(g, consumers, wpre);
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
     const int slots = MT * g.nb;
@@ -434,7 +553,7 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
         // per-format sums are then derived from shared memory only.
         stage_q8k_activation<MT>(g, acts, consumers);
     } else {
-        stage_fused_activation<MT>(g, acts, reinterpret_cast<double *>(red), consumers);
+        stage_fused_activation<MT>(g, acts, reinterpret_cast<double *>(red), consumers, wpre, preloaded);
     }
     consumer_barrier(consumers);
     for (int slot = tid; slot < slots; slot += consumers) Dec::aux_from_raw(acts[slot]);
@@ -516,7 +635,9 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
                 for (int k = 0; k < g.groups; ++k) sum += red[(k * MT + tok) * row_threads + rt];
             total[tok] = sum;
         }
-        if (seg_whole) {
+        if (seg_whole && g.sw_act) {
+            swiglu_epilogue<MT>(g, t, rt, grp, failed, total, consumers, last_flag);
+        } else if (seg_whole) {
             if (grp == 0 && !failed && mine_row && row < g.rows) {
 #pragma unroll
                 for (int tok = 0; tok < MT; ++tok)
@@ -739,6 +860,20 @@ cudaError_t launch_t(const StreamPlan &p, const StreamLaunch &l, cudaStream_t st
     g.act_y = l.act_y;
     g.act_ld = l.act_ld;
     g.act_f_out = l.act_f_out;
+    g.act_reps = l.act_reps > 1 ? l.act_reps : 1;
+    g.act_rep_bytes = l.act_rep_bytes;
+    g.act_y_rep_bytes = l.act_y_rep_bytes;
+    g.out_reps = l.out_reps > 1 ? l.out_reps : 1;
+    g.out_rep_bytes = l.out_rep_bytes;
+    g.pf_ptr = static_cast<const uint8_t *>(l.pf_ptr);
+    g.pf_bytes = l.pf_bytes;
+    g.sw_act = l.sw_act;
+    g.sw_q8 = static_cast<Q8KBlock *>(l.sw_q8);
+    g.sw_counters = l.sw_counters;
+    g.sw_width = p.rows / 2;
+    g.sw_q_reps = l.sw_q_reps > 1 ? l.sw_q_reps : 1;
+    g.sw_q_rep_bytes = l.sw_q_rep_bytes;
+    if (l.sw_act && (p.tile_rows != 256 || p.tiles > p.grid || p.rows % 512)) return cudaErrorInvalidValue;
     g.counters = static_cast<int *>(l.scratch);
     g.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(l.scratch) + p.counter_bytes);
     g.max_slots = p.max_slots;

@@ -62,6 +62,22 @@ void *q38cu_model_stream(Q38Model *model);
  * decode graph; builds the graph if needed).  0 on failure. */
 int q38cu_model_step_kernels(Q38Model *model);
 
+/* Launch timeline of the decode step (profiling; no upstream counterpart, the
+ * upstream's closest is its QWEN38_TRACE_LAYERS stderr trace).  Active only
+ * when the environment has Q38CU_TRACE=1 at q38_model_open_gguf.  Each kernel
+ * of the captured decode graph keeps one record of eleven %globaltimer stamps
+ * in ns, each the earliest or latest over the kernel's CTAs: earliest start,
+ * earliest return from the grid-dependency wait, latest end; for the
+ * weight-streaming GEMVs also the latest CTA to finish staging its activation
+ * and to finish decoding its weights, the latest start, the latest return from
+ * the wait, the earliest to finish staging, and for an RMSNorm input the
+ * earliest to know its sum of squares, to receive its first activation floats
+ * and to finish quantizing in warp 0 (0 for other kernels, or ~0 when
+ * unused).  Records accumulate over the replays since the last call.  Copies
+ * up to max_records records (11 uint64 each, launch order) and clears them; returns the number
+ * copied, 0 when tracing is off, -1 on error. */
+int q38cu_model_trace(Q38Model *model, uint64_t *records, int max_records);
+
 #ifdef __cplusplus
 }
 #endif

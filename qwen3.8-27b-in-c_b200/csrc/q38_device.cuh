@@ -38,6 +38,33 @@ __device__ __forceinline__ unsigned long long global_timer_ns()
     return t;
 }
 
+// Launch timeline (profiling; a null record disables it).  A record is
+// kTraceFields %globaltimer stamps, each the earliest (min) or latest (max)
+// over the launch's CTAs: [0] min start, [1] min return from the grid-
+// dependency wait, [2] max end, and for the weight-streaming GEMV [3] max
+// activation staged, [4] max weights decoded, [5] max start, [6] max return
+// from the wait, [7] min activation staged, [8] min RMSNorm sum of squares
+// known, [9] min first activation floats arrived in thread 0, [10] min warp 0
+// done quantizing (the last three for a fused RMSNorm input only).  Thread 0 of every CTA marks; the host
+// initializes min fields to ~0 and max fields to 0.
+enum : int {
+    kTraceStart = 0, kTraceReady = 1, kTraceEnd = 2, kTraceStaged = 3, kTraceDecoded = 4,
+    kTraceLastStart = 5, kTraceLastReady = 6, kTraceFirstStaged = 7, kTraceNormed = 8,
+    kTraceXLoaded = 9, kTraceQuantized = 10
+};
+constexpr int kTraceFields = 11;
+__host__ __device__ constexpr bool trace_is_min(int which)
+{
+    return which == kTraceStart || which == kTraceReady || which >= kTraceFirstStaged;
+}
+__device__ __forceinline__ void trace_mark(unsigned long long *rec, int which)
+{
+    if (!rec || threadIdx.x != 0) return;
+    const unsigned long long t = global_timer_ns();
+    if (trace_is_min(which)) atomicMin(rec + which, t);
+    else atomicMax(rec + which, t);
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
 {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)

@@ -35,6 +35,7 @@ struct LaunchGemm {
 struct StreamPlan {
     int rows, rows_pad, nb, block_bytes;
     int tile_rows, tiles, groups, chunk;
+    int parts, group_threads;  // threads per (row, superblock); threads per group
     int mt, token_group;  // kernel token capacity / tokens handled per launch
     int stages;
     uint32_t stage_bytes;
@@ -67,9 +68,13 @@ struct StreamLaunch {
     long long act_rep_bytes = 0, act_y_rep_bytes = 0;
     int out_reps = 1;
     long long out_rep_bytes = 0;
-    // L2 prefetch of the next kernel's leading weights (16-byte aligned)
-    const void *pf_ptr = nullptr;
-    long long pf_bytes = 0;
+    // L2 prefetch, after the last bulk copy, of the first nx_cta_bytes of each
+    // of the next GEMV's CTA ranges (see q38_stream.cu); null = none
+    const void *nx_weights = nullptr;
+    long long nx_units = 0;
+    int nx_grid = 0;
+    int nx_unit_bytes = 0;
+    long long nx_cta_bytes = 0;
     // SwiGLU epilogue for interleaved (gate, up) rows in 256-row tiles (see
     // q38_stream.cu): floats to sw_act, Q8_K blocks to sw_q8 (sw_q_reps copies)
     float *sw_act = nullptr;
@@ -77,6 +82,7 @@ struct StreamLaunch {
     int *sw_counters = nullptr;
     int sw_q_reps = 1;
     long long sw_q_rep_bytes = 0;
+    unsigned long long *trace = nullptr;  // optional launch timeline record (q38_device.cuh)
 };
 
 enum : int { kActQ8K = 0, kActRmsNorm = 1, kActSwiGLU = 2 };

@@ -27,6 +27,7 @@
 
 #include "../../include/q38cuda.h"
 #include "../../include/q38cuda_model.h"
+#include "q38_device.cuh"
 #include "q38_gguf_file.h"
 #include "q38_internal.h"
 #include "q38_model_internal.h"
@@ -153,6 +154,11 @@ struct Q38Model {
 
     cudaGraphExec_t decode_graph = nullptr;
     int step_kernels = 0;  // kernel nodes of the decode graph
+    // Launch timeline of the decode graph (Q38CU_TRACE=1 at open): one record
+    // of q38::kTraceFields timestamps per traced kernel, in launch order.
+    unsigned long long *trace = nullptr;
+    int trace_cap = 0, trace_slots = 0;
+    bool tracing = false;  // set while the decode step is captured
     std::vector<void *> owned;
     std::vector<Q38CuTensor> tensors;  // every uploaded tensor, freed at close
     void *staging = nullptr;
@@ -457,27 +463,64 @@ struct OutReps {
     long long bytes = 0;
 };
 
-// L2 prefetch of the next weight tensor's leading bytes (see q38_stream.cu):
-// at most Q38CU_PREFETCH_MB (default 0: off, the measured best for decode) MiB, 0 disables it.
+// L2 prefetch of the weights streamed next (see q38_stream.cu): a GEMV's
+// producer, once its last bulk copy is issued, prefetches the first
+// Q38CU_PREFETCH_KB (default 256) KiB of each of the next GEMV's CTA ranges;
+// the latency-bound mixer kernels prefetch the first Q38CU_MIXER_PREFETCH_MB
+// (default 32) MiB of the projection that follows them.  0 disables either.
 struct Prefetch {
-    const void *ptr = nullptr;
-    long long bytes = 0;
+    const Part *next = nullptr;
 };
+
+long long env_bytes(const char *name, long long fallback, int shift)
+{
+    const char *v = std::getenv(name);
+    return (v && *v ? std::atoll(v) : fallback) << shift;
+}
 
 Prefetch prefetch_of(const Part *p)
 {
-    static const long long limit = [] {
-        const char *v = std::getenv("Q38CU_PREFETCH_MB");
-        return (v && *v ? std::atoll(v) : 0LL) << 20;
-    }();
     Prefetch f;
-    if (!p || limit <= 0) return f;
-    f.ptr = p->t.data;
-    f.bytes = std::min<long long>(limit, static_cast<long long>(p->t.nbytes)) & ~15LL;
+    f.next = p && p->int_path ? p : nullptr;
     return f;
 }
 
+// The launch fields of a GEMV's prefetch of `pf.next`.
+void set_next_prefetch(q38::StreamLaunch &l, const Prefetch &pf)
+{
+    static const long long per_cta = env_bytes("Q38CU_PREFETCH_KB", 256, 10);
+    if (!pf.next || per_cta <= 0) return;
+    const Part &n = *pf.next;
+    q38::StreamPlan plan;
+    if (q38::stream_plan(static_cast<int>(n.t.type), n.rows, static_cast<int>(n.t.shape[0]),
+                         static_cast<int>(n.t.tile_rows), 1, &plan) != cudaSuccess)
+        return;
+    l.nx_weights = n.t.data;
+    l.nx_units = plan.units;
+    l.nx_grid = plan.grid;
+    l.nx_unit_bytes = plan.tile_rows * plan.block_bytes;
+    l.nx_cta_bytes = per_cta;
+}
+
+// The contiguous prefetch a mixer kernel issues: the leading bytes of `p`.
+void mixer_prefetch(const Part *p, const void **ptr, long long *bytes)
+{
+    static const long long limit = env_bytes("Q38CU_MIXER_PREFETCH_MB", 32, 20);
+    *ptr = nullptr;
+    *bytes = 0;
+    if (!p || limit <= 0) return;
+    *ptr = p->t.data;
+    *bytes = std::min<long long>(limit, static_cast<long long>(p->t.nbytes)) & ~15LL;
+}
+
 const Part *first_part(const Proj &p) { return p.parts.empty() ? nullptr : &p.parts[0]; }
+
+// The timeline record of the next traced launch (null when tracing is off or full).
+unsigned long long *next_trace(Q38Model *m)
+{
+    if (!m->tracing || m->trace_slots >= m->trace_cap) return nullptr;
+    return m->trace + q38::kTraceFields * m->trace_slots++;
+}
 
 long long hidden_rep_bytes() { return static_cast<long long>(kMaxTokens) * kHidden * 4; }
 long long q8_rep_bytes() { return static_cast<long long>(kMaxTokens) * (kFfn / 256) * sizeof(Q38CuQ8KBlock); }
@@ -494,7 +537,8 @@ struct SwigluOut {
 };
 
 bool stream_project(const Part &p, const ActIn &in, int tokens, float *out, int out_ld, int accumulate,
-                    const OutReps &orep, const Prefetch &pf, cudaStream_t s, const SwigluOut *sw = nullptr)
+                    const OutReps &orep, const Prefetch &pf, cudaStream_t s, const SwigluOut *sw = nullptr,
+                    Q38Model *tm = nullptr)
 {
     const int width = static_cast<int>(p.t.shape[0]), nb = width / 256;
     for (int tok0 = 0; tok0 < tokens;) {
@@ -518,10 +562,8 @@ bool stream_project(const Part &p, const ActIn &in, int tokens, float *out, int 
         l.act_y_rep_bytes = in.y_rep_bytes;
         l.out_reps = orep.reps;
         l.out_rep_bytes = orep.bytes;
-        if (tok0 == 0) {
-            l.pf_ptr = pf.ptr;
-            l.pf_bytes = pf.bytes;
-        }
+        if (tok0 + plan.token_group >= tokens) set_next_prefetch(l, pf);
+        if (tm) l.trace = next_trace(tm);
         if (sw) {
             const int width_out = p.rows / 2;
             l.sw_act = sw->act + static_cast<size_t>(tok0) * width_out;
@@ -576,7 +618,8 @@ bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int o
         const Part &part = p.parts[i];
         const Part *next = i + 1 < p.parts.size() ? &p.parts[i + 1] : next_after;
         if (part.int_path) {
-            if (!stream_project(part, in, tokens, out + part.offset, out_ld, accumulate, orep, prefetch_of(next), s))
+            if (!stream_project(part, in, tokens, out + part.offset, out_ld, accumulate, orep, prefetch_of(next), s,
+                                nullptr, m))
                 return false;
         } else {
             float_part = true;
@@ -657,7 +700,9 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
     const ActIn attn_in = rmsnorm_input(m->hidden, L.attn_norm);
     // the weight tensor streamed after this layer's ffn_down
     const Part *after = l + 1 < kLayers ? first_part(m->layers[l + 1].in_proj) : first_part(m->output);
-    const Prefetch mixer_pf = prefetch_of(first_part(L.gate_up));
+    const void *mixer_pf_ptr = nullptr;
+    long long mixer_pf_bytes = 0;
+    mixer_prefetch(first_part(L.out), &mixer_pf_ptr, &mixer_pf_bytes);
     if (!project(m, L.in_proj, attn_in, tokens, m->wide, m->wide_ld, 0, OutReps(), first_part(L.out))) return false;
     const ActIn mixed = q8_input(m->q8, m->act_f, L.full ? kAttnQ : kLinV, true);
     if (L.full) {
@@ -680,8 +725,9 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         a.out_q = m->q8;
         a.reps = kReps;
         a.q_rep_bytes = q8_rep_bytes();
-        a.pf_ptr = mixer_pf.ptr;
-        a.pf_bytes = mixer_pf.bytes;
+        a.pf_ptr = mixer_pf_ptr;
+        a.pf_bytes = mixer_pf_bytes;
+        a.trace = next_trace(m);
         if (!cuda_ok(q38::launch_attention(a, s), "attention")) return false;
     } else {
         q38::DeltaArgs d{};
@@ -712,8 +758,9 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         d.out_q = m->q8;
         d.reps = kReps;
         d.q_rep_bytes = q8_rep_bytes();
-        d.pf_ptr = mixer_pf.ptr;
-        d.pf_bytes = mixer_pf.bytes;
+        d.pf_ptr = mixer_pf_ptr;
+        d.pf_bytes = mixer_pf_bytes;
+        d.trace = next_trace(m);
         if (!cuda_ok(q38::launch_deltanet(d, s), "deltanet")) return false;
     }
     if (!project(m, L.out, mixed, tokens, m->hidden, kHidden, 1, hidden_out(), first_part(L.gate_up))) return false;
@@ -726,7 +773,7 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         sw.reps = kReps;
         sw.rep_bytes = q8_rep_bytes();
         if (!stream_project(L.gate_up.parts[0], rmsnorm_input(m->hidden, L.post_norm), tokens, nullptr, 0, 0,
-                            OutReps(), prefetch_of(first_part(L.down)), s, &sw))
+                            OutReps(), prefetch_of(first_part(L.down)), s, &sw, m))
             return false;
         return project(m, L.down, q8_input(m->q8, m->act_f, kFfn, true), tokens, m->hidden, kHidden, 1,
                        hidden_out(), after);
@@ -772,6 +819,7 @@ bool enqueue_head(Q38Model *m, const float *norm_w, const Proj &head, int tokens
     a.advance = advance;
     a.history = m->history;
     a.history_len = static_cast<int>(m->context_length);
+    a.trace = next_trace(m);
     return cuda_ok(q38::launch_argmax(a, tokens, s), "argmax");
 }
 
@@ -940,7 +988,10 @@ bool build_decode_graph(Q38Model *m)
     if (m->decode_graph) return true;
     cudaGraph_t graph = nullptr;
     if (!cuda_ok(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "begin capture")) return false;
+    m->trace_slots = 0;
+    m->tracing = m->trace != nullptr;
     const bool ok = enqueue_decode_step(m);
+    m->tracing = false;
     const cudaError_t e = cudaStreamEndCapture(m->stream, &graph);
     if (!ok || !cuda_ok(e, "end capture")) {
         if (graph) cudaGraphDestroy(graph);
@@ -1006,6 +1057,14 @@ Q38Model *q38_model_open_gguf(const char *path, uint32_t context_length)
     for (int l = 0; ok && l < kLayers; ++l) ok = load_layer(m, m->gguf, l);
     if (ok && blocks == kTotalLayers && nextn == 1) ok = load_mtp(m, m->gguf);
     ok = ok && alloc_runtime(m);
+    if (ok) {
+        const char *tv = std::getenv("Q38CU_TRACE");
+        if (tv && *tv && *tv != '0') {
+            m->trace_cap = 1024;
+            ok = dalloc(&m->trace, q38::kTraceFields * static_cast<size_t>(m->trace_cap), m->owned) &&
+                 cuda_ok(q38::launch_trace_reset(m->trace, m->trace_cap, m->stream), "trace reset");
+        }
+    }
     if (m->staging) {
         cudaFree(m->staging);
         m->staging = nullptr;
@@ -1259,6 +1318,20 @@ int q38cu_model_generate_greedy(Q38Model *m, uint32_t token_id, uint32_t count, 
 }
 
 void *q38cu_model_stream(Q38Model *m) { return m ? m->stream : nullptr; }
+
+int q38cu_model_trace(Q38Model *m, uint64_t *records, int max_records)
+{
+    if (!m || !records || max_records < 0) return -1;
+    if (!m->trace || !use_device(m)) return 0;
+    const int n = std::min(m->trace_slots, max_records);
+    if (!cuda_ok(cudaStreamSynchronize(m->stream), "trace") ||
+        !cuda_ok(cudaMemcpy(records, m->trace, q38::kTraceFields * sizeof(uint64_t) * n, cudaMemcpyDeviceToHost),
+                 "trace copy") ||
+        !cuda_ok(q38::launch_trace_reset(m->trace, m->trace_cap, m->stream), "trace reset") ||
+        !cuda_ok(cudaStreamSynchronize(m->stream), "trace reset"))
+        return -1;
+    return n;
+}
 
 int q38cu_model_step_kernels(Q38Model *m)
 {

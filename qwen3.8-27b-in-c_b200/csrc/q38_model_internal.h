@@ -40,6 +40,7 @@ struct DeltaArgs {
     void *out_q;   // [tokens][24] Q8_K
     const void *pf_ptr;   // L2 prefetch of the next kernel's leading weights
     long long pf_bytes;
+    unsigned long long *trace;  // optional launch timeline record (q38_device.cuh)
 };
 
 struct AttnArgs {
@@ -58,6 +59,7 @@ struct AttnArgs {
     long long q_rep_bytes;
     const void *pf_ptr;   // L2 prefetch of the next kernel's leading weights
     long long pf_bytes;
+    unsigned long long *trace;  // optional launch timeline record (q38_device.cuh)
 };
 
 struct ArgmaxArgs {
@@ -73,6 +75,7 @@ struct ArgmaxArgs {
     int history_len;  // appends stop at this many tokens
     const void *pf_ptr;   // L2 prefetch of the next kernel's leading weights
     long long pf_bytes;
+    unsigned long long *trace;  // optional launch timeline record (q38_device.cuh)
 };
 
 // RMSNorm of `tokens` rows of n floats, written as floats (out_f, optional)
@@ -86,6 +89,8 @@ cudaError_t launch_deltanet(const DeltaArgs &args, cudaStream_t s);
 cudaError_t launch_attention(const AttnArgs &args, cudaStream_t s);
 cudaError_t launch_argmax(const ArgmaxArgs &args, int tokens, cudaStream_t s);
 cudaError_t read_and_clear_model_status(int *status);
+// Sets `count` timeline records (q38_device.cuh) to their initial values.
+cudaError_t launch_trace_reset(unsigned long long *records, int count, cudaStream_t s);
 // Copies rows [0, bytes) of `base` to its replicas 1 .. reps - 1 (stride bytes apart).
 cudaError_t launch_replicate(void *base, size_t bytes, int reps, long long stride, cudaStream_t s);
 

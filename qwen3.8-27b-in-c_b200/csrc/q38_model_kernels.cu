@@ -370,6 +370,7 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
 {
     __shared__ DeltaShared sh;
     __shared__ __align__(16) float xs[5120];  // RMSNorm(hidden) for the fused beta/alpha rows
+    trace_mark(a.trace, kTraceStart);
     cg::cluster_group cluster = cg::this_cluster();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int rank = static_cast<int>(cluster.block_rank());
@@ -379,25 +380,33 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
     const bool qk_writer = vh < 16 && quarter == 0;
     const int ch_q = kh * 128 + tid, ch_k = 2048 + kh * 128 + tid;
     const int ch_v = 4096 + vh * 128 + col0 + (tid & 31);
-    // weights do not depend on the previous kernel: load them before waiting
+    // Nothing below depends on the previous kernel, so it loads before the
+    // grid-dependency wait: the weights, the control block and the recurrent
+    // state (written only by launches that completed before the previous
+    // kernel passed its own wait; read through L2, past this SM's L1).  The
+    // warp's 8 state columns (128 floats each, 4 per lane) stay in registers
+    // for all tokens of the launch and are stored once at the end.
     const float4 wq = conv_kernel(a, ch_q), wk = conv_kernel(a, ch_k), wvv = conv_kernel(a, ch_v);
     BaLoads bl;
-    if (a.ba_fused) ba_load_weights(a, bl);
+    BaBlocks bb;
+    if (a.ba_fused) {
+        ba_load_weights(a, bl);
+        ba_load_blocks(a, vh, bb);
+    }
+    const int base = __ldcg(a.ctl + 1);
+    float *state = a.state + (static_cast<size_t>(vh) * 128 + col0 + warp * 8) * 128 + lane * 4;
+    float4 s[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j] = __ldcg(reinterpret_cast<const float4 *>(state + j * 128));
     if (tid == 0) prefetch_share_l2(a.pf_ptr, a.pf_bytes);  // keeps HBM busy through this latency-bound step
 
     pdl_wait();
-    const int base = a.ctl[1];
-    float *state = a.state + (static_cast<size_t>(vh) * 128 + col0 + warp * 8) * 128 + lane * 4;
+    trace_mark(a.trace, kTraceReady);
 
     for (int t = 0; t < a.tokens; ++t) {
         const int pos = base + t;
-        // Every independent load of the step first: the warp's state columns
-        // (8 x 128 floats; lane holds 4 of each), the conv inputs of q, k (the
-        // key head's 128 channels) and v (this CTA's 32 channels), and the
-        // hidden row for the fused beta/alpha.
-        float4 s[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s[j] = *reinterpret_cast<const float4 *>(state + j * 128);
+        // The conv inputs of q, k (the key head's 128 channels) and v (this
+        // CTA's 32 channels) and the hidden row for the fused beta/alpha.
         const ConvTaps cq = load_taps(a, ch_q, pos, base);
         const ConvTaps ck = load_taps(a, ch_k, pos, base);
         const ConvTaps cv = load_taps(a, ch_v, pos, base);
@@ -428,6 +437,7 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
             sh.ss[warp] = ph;
         }
         __syncthreads();
+        if (t == 0) trace_mark(a.trace, kTraceXLoaded);  // taps loaded, conv and norms reduced
         double sq = 0.0, sk = 0.0;
         for (int w = 0; w < 4; ++w) {
             sq += sh.red[w][0];
@@ -443,8 +453,6 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
             const double sum = ((sh.ss[0] + sh.ss[1]) + sh.ss[2]) + sh.ss[3];
             const float mean = static_cast<float>(sum / 5120.0);
             ba_store_normed(bl, __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps))), xs);
-            BaBlocks bb;
-            ba_load_blocks(a, vh, bb);
             __syncthreads();  // the normed row is complete
             const float acc = warp_sum_f(ba_dot(bb, xs));
             if (lane == 0) sh.ba_part[warp] = acc;
@@ -459,6 +467,7 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
             sh.decay = expf(__fmul_rn(a.a[vh], softplus(__fadd_rn(alpha_raw, a.dt[vh]))));
         }
         __syncthreads();
+        if (t == 0) trace_mark(a.trace, kTraceStaged);  // beta, decay ready
         // the next kernel's weight prefetch may start once this step's loads
         // are in (earlier, its bulk copies would queue ahead of them)
         if (t == a.tokens - 1) pdl_launch_dependents();
@@ -483,10 +492,11 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
             x.z = fmaf(k4.z, delta, x.z);
             x.w = fmaf(k4.w, delta, x.w);
             const float r = warp_sum_f(fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, __fmul_rn(x.x, q4.x)))));
-            *reinterpret_cast<float4 *>(state + j * 128) = x;
+            s[j] = x;
             if (lane == 0) sh.o[col] = __fmul_rn(r, query_scale);
         }
         __syncthreads();
+        if (t == 0) trace_mark(a.trace, kTraceNormed);  // delta rule done
 
         // head RMSNorm across the head's 4 CTAs (qwen38_model.c:783-789)
         float o = 0.0f;
@@ -496,6 +506,7 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
             if (tid == 0) sh.head_part = p;
         }
         cluster.sync();
+        if (t == 0) trace_mark(a.trace, kTraceQuantized);  // head norm exchanged
         if (tid < 32) {
             double sum = 0.0;
             for (int r = (rank & ~3); r < (rank & ~3) + 4; ++r) sum += cluster.map_shared_rank(&sh, r)->head_part;
@@ -511,6 +522,7 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
             if (tid == 0) sh.block_part = m;
         }
         cluster.sync();
+        if (t == 0) trace_mark(a.trace, kTraceFirstStaged);  // block max exchanged
         if (tid < 32) {
             AbsMax best = cluster.map_shared_rank(&sh, 0)->block_part;
             for (int r = 1; r < kDeltaCluster; ++r) best = better(best, cluster.map_shared_rank(&sh, r)->block_part);
@@ -534,7 +546,10 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
             }
         }
     }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) *reinterpret_cast<float4 *>(state + j * 128) = s[j];
     cluster.sync();  // peers may still read this CTA's exchange slots
+    trace_mark(a.trace, kTraceEnd);
 }
 
 // ---------------------------------------------------------------------------
@@ -587,6 +602,7 @@ __device__ float norm_rope(float x, const float *norm, int pos, float theta_scal
 __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
 {
     __shared__ AttnShared sh;
+    trace_mark(a.trace, kTraceStart);
     const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
     const int split = blockIdx.x % a.splits;
     const int th = blockIdx.x / a.splits;
@@ -595,6 +611,7 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
     if (d == 0) prefetch_share_l2(a.pf_ptr, a.pf_bytes);  // keeps HBM busy through this latency-bound step
 
     pdl_wait();
+    trace_mark(a.trace, kTraceReady);
     const int base = a.ctl[1];
     const int pos = base + t, len = pos + 1;
     const int chunk = (len + a.splits - 1) / a.splits;
@@ -604,6 +621,7 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
     // query: RMSNorm + RoPE
     const float q = norm_rope(row[h * 512 + d], a.q_norm, pos, a.theta_scale, sh.scores, sh.red_d);
     __syncthreads();
+    trace_mark(a.trace, kTraceXLoaded);  // query normalized and rotated
     sh.q[d] = q;
 
     // keys/values of this launch's tokens that fall in [p0, p1), and the
@@ -625,6 +643,7 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
         }
     }
     __syncthreads();
+    trace_mark(a.trace, kTraceNormed);  // this launch's keys and values ready
 
     // scores of positions [p0, p1): warp w takes p0 + w, p0 + w + 8, ...
     const float4 qa = *reinterpret_cast<const float4 *>(&sh.q[lane * 4]);
@@ -641,6 +660,7 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
         local_max = fmaxf(local_max, score);
     }
     const float m = block_max_f(local_max, sh.red_f);  // includes the barrier for sh.scores
+    trace_mark(a.trace, kTraceQuantized);  // scores done
     float l_part = 0.0f;
     for (int i = d; i < p1 - p0; i += 256) {
         const float e = expf(__fsub_rn(sh.scores[i], m));
@@ -649,14 +669,27 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
     }
     __syncthreads();
     const double l = block_sum_d(static_cast<double>(l_part), sh.red_d);
+    // weighted values in position order; the loads of 8 positions are issued
+    // before their products
     float acc = 0.0f;
-    for (int p = p0; p < p1; ++p) {
+    int p = p0;
+    for (; p + 8 <= p1; p += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            v[k] = p + k < base ? a.v_cache[static_cast<size_t>(p + k) * 1024 + g * 256 + d] : sh.vnew[p + k - base][d];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc = fmaf(sh.scores[p + k - p0], v[k], acc);
+    }
+    for (; p < p1; ++p) {
         const float v = p < base ? a.v_cache[static_cast<size_t>(p) * 1024 + g * 256 + d] : sh.vnew[p - base][d];
         acc = fmaf(sh.scores[p - p0], v, acc);
     }
 
     // the keys and values are read: the next kernel's weight prefetch may start
     pdl_launch_dependents();
+    trace_mark(a.trace, kTraceFirstStaged);  // weighted values done
+    trace_mark(a.trace, kTraceStaged);
 
     // leave this split's partial result; the last CTA of (t, h) merges
     float *part = a.partials + static_cast<size_t>(blockIdx.x) * (kAttnDim + 2);
@@ -669,7 +702,10 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
     __syncthreads();
     if (d == 0) sh.last = atomicAdd(&a.counters[th], 1) == a.splits - 1;
     __syncthreads();
-    if (!sh.last) return;
+    if (!sh.last) {
+        trace_mark(a.trace, kTraceEnd);
+        return;
+    }
     __threadfence();
     const float *parts = a.partials + static_cast<size_t>(th) * a.splits * (kAttnDim + 2);
     float mx = -INFINITY;
@@ -688,6 +724,7 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
     quantize_block_256(o, static_cast<Q8KBlock *>(a.out_q) + static_cast<size_t>(t) * 24 + h, sh.red_m, a.reps,
                        a.q_rep_bytes);
     if (d == 0) a.counters[th] = 0;
+    trace_mark(a.trace, kTraceEnd);
 }
 
 // ---------------------------------------------------------------------------
@@ -702,7 +739,9 @@ __global__ void __launch_bounds__(256) argmax_kernel(ArgmaxArgs a)
     __shared__ float sv[8];
     __shared__ int si[8];
     __shared__ int last;
+    trace_mark(a.trace, kTraceStart);
     pdl_wait();
+    trace_mark(a.trace, kTraceReady);
     pdl_launch_dependents();
     const int tok = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float *x = a.logits + static_cast<size_t>(tok) * a.ld;
@@ -731,17 +770,32 @@ __global__ void __launch_bounds__(256) argmax_kernel(ArgmaxArgs a)
         last = atomicAdd(&a.counters[tok], 1) == static_cast<int>(gridDim.x) - 1;
     }
     __syncthreads();
-    if (!last || tid != 0) return;
-    __threadfence();
-    float bv = __ldcg(&a.part_v[tok * gridDim.x]);
-    int bidx = __ldcg(&a.part_i[tok * gridDim.x]);
-    for (unsigned c = 1; c < gridDim.x; ++c) {
-        const float v = __ldcg(&a.part_v[tok * gridDim.x + c]);
-        if (v > bv) { bv = v; bidx = __ldcg(&a.part_i[tok * gridDim.x + c]); }
+    if (!last || warp != 0) {
+        trace_mark(a.trace, kTraceEnd);
+        return;
     }
+    __threadfence();
+    // Warp 0 merges the CTA results: lane l scans CTAs l, l + 32, ... in
+    // order (strict >: the earliest of equal maxima), then the lanes combine
+    // with ties going to the lower index (CTA ranges are in index order).
+    float bv = -INFINITY;
+    int bidx = 0x7fffffff;
+    for (unsigned c = lane; c < gridDim.x; c += 32) {
+        const float v = __ldcg(&a.part_v[tok * gridDim.x + c]);
+        const int i = __ldcg(&a.part_i[tok * gridDim.x + c]);
+        if (v > bv) { bv = v; bidx = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+        if (ov > bv || (ov == bv && oi < bidx)) { bv = ov; bidx = oi; }
+    }
+    if (lane != 0) return;
     if (bidx == 0x7fffffff) bidx = 0;  // all NaN / -inf: the upstream scan keeps index 0
     a.out[tok] = static_cast<uint32_t>(bidx);
     a.counters[tok] = 0;
+    trace_mark(a.trace, kTraceEnd);
     if (a.ctl && tok == static_cast<int>(gridDim.y) - 1) {
         a.ctl[0] = bidx;
         a.ctl[1] += a.advance;
@@ -815,6 +869,23 @@ __global__ void replicate_kernel(char *base, size_t words, int reps, long long s
     for (int k = 1; k < reps; ++k) reinterpret_cast<uint32_t *>(base + k * stride)[i] = v;
 }
 }  // namespace
+
+namespace {
+__global__ void trace_reset_kernel(unsigned long long *rec, int count)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    unsigned long long *r = rec + static_cast<size_t>(kTraceFields) * i;
+    for (int f = 0; f < kTraceFields; ++f) r[f] = trace_is_min(f) ? ~0ull : 0ull;
+}
+}  // namespace
+
+cudaError_t launch_trace_reset(unsigned long long *records, int count, cudaStream_t s)
+{
+    if (count <= 0) return cudaSuccess;
+    trace_reset_kernel<<<(count + 255) / 256, 256, 0, s>>>(records, count);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_replicate(void *base, size_t bytes, int reps, long long stride, cudaStream_t s)
 {

@@ -39,6 +39,7 @@
 #include <algorithm>
 #include <cstdlib>
 #include <mutex>
+#include <type_traits>
 
 #include "../../include/q38cuda.h"
 #include "q38_device.cuh"
@@ -67,6 +68,8 @@ struct StreamArgs {
     int tiles;
     int units;         // tiles * nb
     int groups;        // J
+    int parts;         // L: threads per (row, superblock); 1 = one thread decodes a whole superblock
+    int group_threads; // threads of one group: T * L rounded up to whole warps
     int stages;        // S, per group
     int chunk;         // C, units per copy
     uint32_t stage_bytes;
@@ -91,11 +94,17 @@ struct StreamArgs {
     // more times, out_rep_bytes apart, for the next kernel's readers.
     int out_reps;
     long long out_rep_bytes;
-    // L2 prefetch of the next kernel's leading weights (each CTA its share),
-    // issued once this CTA's ring is full: it keeps HBM busy while this kernel
-    // and the next wait on their activations.
-    const uint8_t *pf_ptr;
-    long long pf_bytes;
+    // L2 prefetch of the next GEMV's weights, issued by the producer after its
+    // last bulk copy: HBM keeps streaming through this kernel's last decode,
+    // its epilogue and the next kernel's activation prologue, and the next
+    // kernel's first ring fills hit L2.  CTA c prefetches the first
+    // nx_cta_bytes of the unit ranges of the next kernel's CTAs c, c + G, ...
+    // (the next kernel has nx_grid CTAs over nx_units units of nx_unit_bytes).
+    const uint8_t *nx_weights;
+    long long nx_units;
+    int nx_grid;
+    int nx_unit_bytes;
+    long long nx_cta_bytes;
     // SwiGLU epilogue (sw_act != nullptr): rows come in (gate i, up i) pairs,
     // 2i and 2i + 1, and a tile is 256 rows = 128 outputs = half a Q8_K
     // block.  Instead of the rows, the kernel stores sw_act[tok][i] =
@@ -112,6 +121,7 @@ struct StreamArgs {
     int max_slots;
     int32_t *dbg_w;       // optional [tokens][rows][nb]
     int32_t *dbg_x;
+    unsigned long long *trace;  // optional launch timeline record
 };
 
 // Final store of one output row; with `accumulate` the value is added to what
@@ -173,15 +183,23 @@ struct ChunkWalk {
 };
 
 // CTA size bound: 416 threads (157 registers) for up to 2 tokens, 288 threads
-// (227 registers) for 4 and 8.
-template <int MT> struct StreamThreads { static constexpr int kValue = MT <= 2 ? 416 : 288; };
+// (227 registers) for 4 and 8; 672 threads (97 registers) for one token with
+// superblocks split across threads.
+template <int MT, int L = 1> struct StreamThreads {
+    static constexpr int kValue = L > 1 ? 672 : (MT <= 2 ? 416 : 288);
+};
+
+// Threads per superblock a decoder supports (block_part / finish).
+template <typename Dec> struct SplitParts { static constexpr int kMax = 1; };
+template <> struct SplitParts<DecQ4K> { static constexpr int kMax = 4; };
+template <> struct SplitParts<DecQ6K> { static constexpr int kMax = 4; };
 
 // Activation prologues.  They run after the grid dependency, so their global
 // loads are the latency every launch pays before its first decode: each
 // thread issues all the loads of a batch (ActBatch blocks per warp) before
 // using any of them, instead of one L2 round trip per loop iteration.  The
 // batch is shallower when several tokens share the kernel's registers.
-template <int MT> struct ActBatch { static constexpr int kValue = MT == 1 ? 4 : 2; };
+template <int MT, int L = 1> struct ActBatch { static constexpr int kValue = L > 1 ? 1 : (MT == 1 ? 4 : 2); };
 
 __device__ __forceinline__ void load8(const float *p, float (&v)[8])
 {
@@ -200,15 +218,24 @@ __device__ __forceinline__ void ldg8(const float *p, float (&v)[8])
 }
 
 // Q8_K of one 256-element block held 8 per lane, into an activation slot
-// (raw bsums in aux[8..15], as the Q8_K staging path leaves them).
-__device__ __forceinline__ void store_block(Act &slot, const float (&v)[8])
+// (raw bsums in aux[8..15], as the Q8_K staging path leaves them).  One
+// out-of-line copy serves every kernel of this file: the prologue runs once
+// per launch, so its code is fetched cold unless the launches share it.
+__device__ __noinline__ void quantize_to_slot(Act *slot, float v0, float v1, float v2, float v3, float v4,
+                                              float v5, float v6, float v7)
 {
     const int lane = threadIdx.x & 31;
+    const float v[8] = {v0, v1, v2, v3, v4, v5, v6, v7};
     const WarpQ8K r = act_quantize_warp(v);
-    slot.q[lane * 2] = r.q0;
-    slot.q[lane * 2 + 1] = r.q1;
-    if ((lane & 3) == 0) slot.aux[8 + (lane >> 2)] = r.sums_word;
-    if (lane == 0) slot.xs = r.scale;
+    slot->q[lane * 2] = r.q0;
+    slot->q[lane * 2 + 1] = r.q1;
+    if ((lane & 3) == 0) slot->aux[8 + (lane >> 2)] = r.sums_word;
+    if (lane == 0) slot->xs = r.scale;
+}
+
+__device__ __forceinline__ void store_block(Act &slot, const float (&v)[8])
+{
+    quantize_to_slot(&slot, v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7]);
 }
 
 __device__ __forceinline__ void store_floats(const StreamArgs &g, int tok, int e, const float (&v)[8])
@@ -229,11 +256,11 @@ __device__ __forceinline__ void store_floats(const StreamArgs &g, int tok, int e
 // asked.
 // The RMSNorm weights do not depend on the previous kernel: when a warp's
 // blocks fit one batch they are loaded before the grid dependency resolves.
-template <int MT>
+template <int MT, int L>
 __device__ __forceinline__ bool preload_norm_weights(const StreamArgs &g, int consumers,
-                                                     float (&wv)[ActBatch<MT>::kValue][8])
+                                                     float (&wv)[ActBatch<MT, L>::kValue][8])
 {
-    constexpr int kActBatch = ActBatch<MT>::kValue;
+    constexpr int kActBatch = ActBatch<MT, L>::kValue;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = consumers >> 5;
     if (g.act_mode != kActRmsNorm || (g.nb + warps - 1) / warps > kActBatch) return false;
     const float *w = replica(g.act_y, g.act_y_rep_bytes, g.act_reps);
@@ -245,11 +272,11 @@ __device__ __forceinline__ bool preload_norm_weights(const StreamArgs &g, int co
     return true;
 }
 
-template <int MT>
+template <int MT, int L>
 __device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *red, int consumers,
-                                       const float (&wpre)[ActBatch<MT>::kValue][8], bool preloaded)
+                                       const float (&wpre)[ActBatch<MT, L>::kValue][8], bool preloaded)
 {
-    constexpr int kActBatch = ActBatch<MT>::kValue;
+    constexpr int kActBatch = ActBatch<MT, L>::kValue;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, warps = consumers >> 5;
     const int per_warp = (g.nb + warps - 1) / warps;
     const float *act_x = replica(g.act_x, g.act_rep_bytes, g.act_reps);
@@ -319,6 +346,7 @@ __device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *r
 #pragma unroll
                 for (int i = 0; i < 8; ++i) part += static_cast<double>(__fmul_rn(xv[j][i], xv[j][i]));
             }
+            if (tok == 0 && j0 == 0 && g.trace && threadIdx.x == 0 && part >= 0.0) trace_mark(g.trace, kTraceXLoaded);
         }
         part = act_warp_sum_d(part);
         if (lane == 0) red[warp] = part;
@@ -326,6 +354,7 @@ __device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *r
         double sum = 0.0;
         for (int w = 0; w < warps; ++w) sum += red[w];
         consumer_barrier(consumers);  // red is reused by the next token
+        if (tok == 0) trace_mark(g.trace, kTraceNormed);
         const float mean = static_cast<float>(sum / static_cast<double>(g.nb * 256));
         const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps)));
         for (int j0 = 0; j0 < per_warp; j0 += kActBatch) {
@@ -351,57 +380,97 @@ __device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *r
                 store_block(slots[b], v);
             }
         }
+        if (tok == 0) {
+            __syncwarp();
+            trace_mark(g.trace, kTraceQuantized);
+        }
     }
 }
 
 // Q8_K staging: the blocks' words (scale, 64 quant words, 8 bsum words) are
-// copied into the activation slots, kBatchWords loads in flight per thread.
+// copied into the activation slots.  Each global load round trip costs about
+// a microsecond between dependent kernels, so all words are loaded in one
+// round trip where possible: 16-byte loads (when each token's blocks start on
+// a 16-byte boundary), kBatch of them in flight per thread; 4-byte loads
+// otherwise.  Tokens beyond g.tokens stage zeros.
 template <int MT>
 __device__ void stage_q8k_activation(const StreamArgs &g, Act *acts, int consumers)
 {
-    constexpr int kWords = 73, kBatchWords = 8;
+    constexpr int kWords = 73;
     const int tid = threadIdx.x;
-    const int total = MT * g.nb * kWords;
     const Q8KBlock *act = replica(g.act, g.act_rep_bytes, g.act_reps);
+    const int row_words = g.nb * kWords;
+    auto put = [&](int tok, int w4, uint32_t v) {
+        const int blk = w4 / kWords, w = w4 - blk * kWords;
+        Act &slot = acts[tok * g.nb + blk];
+        if (w == 0) slot.xs = __uint_as_float(v);
+        else if (w <= 64) slot.q[w - 1] = v;      // quants
+        else slot.aux[8 + (w - 65)] = v;          // bsums
+    };
+    if (row_words % 4 == 0 && (reinterpret_cast<uintptr_t>(act) & 15u) == 0) {
+        constexpr int kBatch = 8;
+        const int row_vecs = row_words / 4, total = MT * row_vecs;
+        for (int i0 = tid; i0 < total; i0 += consumers * kBatch) {
+            uint4 v[kBatch];
+#pragma unroll
+            for (int k = 0; k < kBatch; ++k) {
+                const int i = i0 + k * consumers;
+                v[k] = make_uint4(0u, 0u, 0u, 0u);
+                const int tok = i / row_vecs;
+                if (i < total && tok < g.tokens)
+                    v[k] = __ldcg(reinterpret_cast<const uint4 *>(act + static_cast<size_t>(tok) * g.nb) +
+                                  (i - tok * row_vecs));
+            }
+#pragma unroll
+            for (int k = 0; k < kBatch; ++k) {
+                const int i = i0 + k * consumers;
+                if (i >= total) break;
+                const int tok = i / row_vecs, w4 = (i - tok * row_vecs) * 4;
+                put(tok, w4, v[k].x);
+                put(tok, w4 + 1, v[k].y);
+                put(tok, w4 + 2, v[k].z);
+                put(tok, w4 + 3, v[k].w);
+            }
+        }
+        return;
+    }
+    constexpr int kBatchWords = 8;
+    const int total = MT * row_words;
     for (int i0 = tid; i0 < total; i0 += consumers * kBatchWords) {
         uint32_t v[kBatchWords];
 #pragma unroll
         for (int k = 0; k < kBatchWords; ++k) {
             const int i = i0 + k * consumers;
             v[k] = 0u;
-            if (i < total) {
-                const int slot = i / kWords, w = i - slot * kWords;
-                const int tok = slot / g.nb, col = slot - tok * g.nb;
-                if (tok < g.tokens)
-                    v[k] = __ldg(reinterpret_cast<const uint32_t *>(act + static_cast<size_t>(tok) * g.nb + col) + w);
-            }
+            const int tok = i / row_words;
+            if (i < total && tok < g.tokens)
+                v[k] = __ldcg(reinterpret_cast<const uint32_t *>(act + static_cast<size_t>(tok) * g.nb) +
+                              (i - tok * row_words));
         }
 #pragma unroll
         for (int k = 0; k < kBatchWords; ++k) {
             const int i = i0 + k * consumers;
             if (i >= total) break;
-            const int slot = i / kWords, w = i - slot * kWords;
-            if (w == 0) acts[slot].xs = __uint_as_float(v[k]);
-            else if (w <= 64) acts[slot].q[w - 1] = v[k];       // quants
-            else acts[slot].aux[8 + (w - 65)] = v[k];           // bsums
+            const int tok = i / row_words;
+            put(tok, i - tok * row_words, v[k]);
         }
     }
 }
-// SwiGLU epilogue of a whole 256-row tile t (see StreamArgs::sw_act): adjacent
-// lanes hold gate and up of one output (the upstream q38_swiglu,
+// SwiGLU epilogue of a whole 256-row tile t (see StreamArgs::sw_act): rows
+// 2i and 2i + 1 (lanes `parts` apart) hold gate and up of one output (the upstream q38_swiglu,
 // qwen38_model.c:523-541); the Q8_K block of outputs 256 (t / 2) .. + 255 is
 // quantized (qwen38_quant.c:50-88) by whichever of its two CTAs finishes last.
 template <int MT>
-__device__ void swiglu_epilogue(const StreamArgs &g, int t, int rt, int grp, bool failed, const float (&total)[MT],
-                                int consumers, volatile int *last_flag)
+__device__ void swiglu_epilogue(const StreamArgs &g, int t, int rt, int grp, int part, bool failed,
+                                const float (&total)[MT], int consumers, volatile int *last_flag)
 {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const bool pair_lead = (rt & 1) == 0;
     const int i = (t * 256 + rt) >> 1;  // output index
 #pragma unroll
     for (int tok = 0; tok < MT; ++tok) {
-        const float up = __shfl_xor_sync(0xffffffffu, total[tok], 1);
-        if (grp == 0 && pair_lead && !failed && tok < g.tokens)
+        const float up = __shfl_xor_sync(0xffffffffu, total[tok], g.parts);
+        if (grp == 0 && part == 0 && pair_lead && !failed && tok < g.tokens)
             g.sw_act[static_cast<size_t>(tok) * g.sw_width + i] = __fmul_rn(act_silu(total[tok]), up);
     }
     __threadfence();
@@ -457,8 +526,63 @@ __device__ __forceinline__ void decode_column(const StreamArgs &g, const uint8_t
     }
 }
 
-template <typename Dec, int MT, bool kDbg>
-__global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kernel(StreamArgs g)
+// The producer's L2 prefetch of the next GEMV's leading weights (see
+// StreamArgs::nx_weights).  Unit ranges start on 16-byte boundaries.
+__device__ __forceinline__ void prefetch_next_ranges(const StreamArgs &g)
+{
+    if (!g.nx_weights || g.nx_cta_bytes <= 0) return;
+    for (long long cn = blockIdx.x; cn < g.nx_grid; cn += gridDim.x) {
+        const long long u0 = g.nx_units * cn / g.nx_grid, u1 = g.nx_units * (cn + 1) / g.nx_grid;
+        long long bytes = (u1 - u0) * g.nx_unit_bytes;
+        if (bytes > g.nx_cta_bytes) bytes = g.nx_cta_bytes & ~15LL;
+        const uint8_t *p = g.nx_weights + u0 * g.nx_unit_bytes;
+        for (long long off = 0; off < bytes; off += 1 << 20) {
+            const long long take = bytes - off < (1 << 20) ? bytes - off : (1 << 20);
+            bulk_prefetch_l2(p + off, static_cast<uint32_t>(take));
+        }
+    }
+}
+
+// One superblock decoded by the L threads of a row (lanes `mask`), thread
+// `part` taking part `part` of the integer sums; the parts are added across
+// the lanes (exact integer adds) and every lane forms the same float value.
+template <typename Dec, int MT, int L, bool kDbg>
+__device__ __forceinline__ void decode_column_part(const StreamArgs &g, const uint8_t *blk, const Act *acts, int b,
+                                                   int row, float (&acc)[MT], int part, unsigned mask)
+{
+    SmemActs<MT> a;
+#pragma unroll
+    for (int tok = 0; tok < MT; ++tok) a.p[tok] = acts + tok * g.nb + b;
+    int w[MT], x[MT];
+    float val[MT];
+    Dec::template block_part<MT, L>(blk, a, part, w, x);
+#pragma unroll
+    for (int o = 1; o < L; o <<= 1) {
+#pragma unroll
+        for (int tok = 0; tok < MT; ++tok) {
+            w[tok] += __shfl_xor_sync(mask, w[tok], o);
+            x[tok] += __shfl_xor_sync(mask, x[tok], o);
+        }
+    }
+    Dec::template finish<MT>(blk, a, w, x, val);
+#pragma unroll
+    for (int tok = 0; tok < MT; ++tok) acc[tok] += val[tok];
+    if constexpr (kDbg) {
+        if (part == 0 && row < g.rows) {
+#pragma unroll
+            for (int tok = 0; tok < MT; ++tok) {
+                if (tok < g.tokens) {
+                    const size_t o = (static_cast<size_t>(tok) * g.rows + row) * g.nb + b;
+                    g.dbg_w[o] = w[tok];
+                    g.dbg_x[o] = x[tok];
+                }
+            }
+        }
+    }
+}
+
+template <typename Dec, int MT, int L, bool kDbg>
+__global__ void __launch_bounds__(StreamThreads<MT, L>::kValue, 1) stream_gemm_kernel(StreamArgs g)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     const int consumers = static_cast<int>(blockDim.x) - 32;
@@ -473,15 +597,21 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
     volatile int *last_flag = issued + 1;
 
     const int tid = threadIdx.x;
+    trace_mark(g.trace, kTraceStart);
+    trace_mark(g.trace, kTraceLastStart);
     const int G = gridDim.x, c = blockIdx.x;
     const int u0 = static_cast<int>(static_cast<long long>(g.units) * c / G);
     const int u1 = static_cast<int>(static_cast<long long>(g.units) * (c + 1) / G);
-    const int row_threads = consumers / g.groups;
+    // Group k is threads [k * group_threads, (k + 1) * group_threads): row rt
+    // of the tile is decoded by its L consecutive threads (part = tid % L);
+    // threads past the tile's rows, and past the last group, only keep step.
+    const int group_threads = g.group_threads;
+    const int row_slots = group_threads / L;  // >= tile_rows
 
     if (tid == 0) {
         for (int s = 0; s < n_stages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], row_threads / 32);  // the owning group's warps free a stage
+            mbar_init(&empty[s], group_threads / 32);  // the owning group's warps free a stage
         }
         *issued = 0;
         fence_mbar_init();
@@ -494,17 +624,12 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
             ChunkWalk w;
             w.init(u0, u1, g.nb, g.chunk);
             int q = 0, grp = 0, slot = 0, wrap = 0;
-            bool prefetched = false;
             const uint64_t stream_policy = l2_evict_first_policy();  // weights are read once per step
             const size_t unit_bytes = static_cast<size_t>(g.tile_rows) * g.block_bytes;
             for (; !w.done(); ++q) {
                 const int n = w.len();
                 const int s = grp * g.stages + slot;
                 if (wrap > 0) {
-                    if (!prefetched) {
-                        prefetch_share_l2(g.pf_ptr, g.pf_bytes);
-                        prefetched = true;
-                    }
                     if (!mbar_wait_bounded(&empty[s], static_cast<uint32_t>(wrap - 1) & 1u, &g_stream_status)) break;
                     fence_proxy_async_shared();
                 }
@@ -519,7 +644,7 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
                     if (++slot == g.stages) { slot = 0; ++wrap; }
                 }
             }
-            if (!prefetched) prefetch_share_l2(g.pf_ptr, g.pf_bytes);
+            prefetch_next_ranges(g);
         }
         return;
     }
@@ -542,9 +667,11 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
             }
         }
     }
-    float wpre[ActBatch<MT>::kValue][8];
-    const bool preloaded = preload_norm_weights<MT>(g, consumers, wpre);
+    float wpre[ActBatch<MT, L>::kValue][8];
+    const bool preloaded = preload_norm_weights<MT, L>(g, consumers, wpre);
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    trace_mark(g.trace, kTraceReady);
+    trace_mark(g.trace, kTraceLastReady);
 
     const int slots = MT * g.nb;
     if (g.act_mode == kActQ8K) {
@@ -553,19 +680,24 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
         // per-format sums are then derived from shared memory only.
         stage_q8k_activation<MT>(g, acts, consumers);
     } else {
-        stage_fused_activation<MT>(g, acts, reinterpret_cast<double *>(red), consumers, wpre, preloaded);
+        stage_fused_activation<MT, L>(g, acts, reinterpret_cast<double *>(red), consumers, wpre, preloaded);
     }
     consumer_barrier(consumers);
     for (int slot = tid; slot < slots; slot += consumers) Dec::aux_from_raw(acts[slot]);
     consumer_barrier(consumers);
+    trace_mark(g.trace, kTraceStaged);
+    trace_mark(g.trace, kTraceFirstStaged);
     // Only now let the next kernel in the stream launch and start its weight
     // prefetch: launched earlier, its bulk copies queue ahead of this kernel's
     // activation loads in the memory system and stall the prologue.  It still
     // waits for our completion before it touches anything we write.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-    const int grp = tid / row_threads, rt = tid - grp * row_threads;
-    const bool mine_row = rt < g.tile_rows;
+    const int grp = tid / group_threads, rt = (tid - grp * group_threads) / L;
+    const int part = L > 1 ? tid % L : 0;
+    const unsigned part_mask = L > 1 ? ((1u << L) - 1u) << (lane & ~(L - 1)) : 0xFFFFFFFFu;
+    const bool in_group = grp < g.groups;
+    const bool mine_row = in_group && rt < g.tile_rows;
     const size_t unit_bytes = static_cast<size_t>(g.tile_rows) * g.block_bytes;
     bool failed = false;
     int slot = 0, wrap = 0;  // this group's ring position
@@ -585,11 +717,17 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
             if (q % g.groups == grp) {
                 const int s = grp * g.stages + slot;
                 if (!failed) failed = !mbar_wait_bounded(&full[s], static_cast<uint32_t>(wrap) & 1u, &g_stream_status);
+                if constexpr (L > 1) failed = __any_sync(part_mask, failed);  // a row's lanes decode together
                 if (!failed && mine_row) {
                     const uint8_t *base = stage_mem + static_cast<size_t>(s) * g.stage_bytes +
                                           static_cast<size_t>(rt) * g.block_bytes;
                     int k = 0;
-                    if constexpr (MT <= 2 && !kDbg) {
+                    if constexpr (L > 1) {
+                        for (; k < n; ++k)
+                            decode_column_part<Dec, MT, L, kDbg>(g, base + k * unit_bytes, acts, w.b + k, row, acc,
+                                                                 part, part_mask);
+                    }
+                    if constexpr (MT <= 2 && !kDbg && L == 1) {
                         // two columns in flight: independent decode chains,
                         // the earlier column still added first
                         for (; k + 1 < n; k += 2) {
@@ -623,22 +761,25 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
             w.next(n);
         } while (!w.done() && w.t == t);
 
+        if (w.done()) trace_mark(g.trace, kTraceDecoded);
         // Combine the groups' row sums in group order.
+        if (in_group && part == 0) {
 #pragma unroll
-        for (int tok = 0; tok < MT; ++tok) red[(grp * MT + tok) * row_threads + rt] = acc[tok];
+            for (int tok = 0; tok < MT; ++tok) red[(grp * MT + tok) * row_slots + rt] = acc[tok];
+        }
         consumer_barrier(consumers);
         float total[MT];
 #pragma unroll
         for (int tok = 0; tok < MT; ++tok) {
             float sum = 0.0f;
             if (grp == 0)
-                for (int k = 0; k < g.groups; ++k) sum += red[(k * MT + tok) * row_threads + rt];
+                for (int k = 0; k < g.groups; ++k) sum += red[(k * MT + tok) * row_slots + rt];
             total[tok] = sum;
         }
         if (seg_whole && g.sw_act) {
-            swiglu_epilogue<MT>(g, t, rt, grp, failed, total, consumers, last_flag);
+            swiglu_epilogue<MT>(g, t, rt, grp, part, failed, total, consumers, last_flag);
         } else if (seg_whole) {
-            if (grp == 0 && !failed && mine_row && row < g.rows) {
+            if (grp == 0 && part == 0 && !failed && mine_row && row < g.rows) {
 #pragma unroll
                 for (int tok = 0; tok < MT; ++tok)
                     if (tok < g.tokens) store_row(g, tok, row, total[tok]);
@@ -650,7 +791,7 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
             const int cf = cta_of_unit(tu, g.units, G);
             const int cl = cta_of_unit(tu + g.nb - 1, g.units, G);
             const int n_dep = cl - cf + 1, dep = c - cf;
-            if (grp == 0 && mine_row) {
+            if (grp == 0 && part == 0 && mine_row) {
                 float *mine = g.partials + (static_cast<size_t>(t) * g.max_slots + dep) * MT * g.tile_rows;
 #pragma unroll
                 for (int tok = 0; tok < MT; ++tok) __stcg(mine + tok * g.tile_rows + rt, total[tok]);
@@ -659,7 +800,7 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
             consumer_barrier(consumers);
             if (tid == 0) *last_flag = !failed && atomicAdd(&g.counters[t], 1) == n_dep - 1;
             consumer_barrier(consumers);
-            if (*last_flag && grp == 0 && mine_row) {
+            if (*last_flag && grp == 0 && part == 0 && mine_row) {
                 __threadfence();
                 const float *base = g.partials + static_cast<size_t>(t) * g.max_slots * MT * g.tile_rows;
 #pragma unroll
@@ -687,6 +828,7 @@ __global__ void __launch_bounds__(StreamThreads<MT>::kValue, 1) stream_gemm_kern
             mbar_wait_bounded(&full[st], static_cast<uint32_t>(k / g.stages) & 1u, nullptr);
         }
     }
+    trace_mark(g.trace, kTraceEnd);
 }
 
 // GGUF row-major -> tiled layout (padding rows stay zero).
@@ -724,15 +866,22 @@ size_t stream_smem(const StreamPlan &p)
            2 * kStreamMaxStages * 8 + 16;
 }
 
-template <typename Dec, int MT, bool kDbg>
+template <typename Dec, int MT, bool kDbg, int L = 1>
 const void *stream_kernel_ptr()
 {
-    return reinterpret_cast<const void *>(stream_gemm_kernel<Dec, MT, kDbg>);
+    return reinterpret_cast<const void *>(stream_gemm_kernel<Dec, MT, L, kDbg>);
 }
 
 template <typename Dec>
-const void *select_kernel(int mt, bool dbg)
+const void *select_kernel(int mt, bool dbg, int parts)
 {
+    if constexpr (SplitParts<Dec>::kMax >= 4) {
+        if (mt == 1 && parts == 4)
+            return dbg ? stream_kernel_ptr<Dec, 1, true, 4>() : stream_kernel_ptr<Dec, 1, false, 4>();
+        if (mt == 1 && parts == 2)
+            return dbg ? stream_kernel_ptr<Dec, 1, true, 2>() : stream_kernel_ptr<Dec, 1, false, 2>();
+    }
+    if (parts != 1) return nullptr;
     switch (mt) {
     case 1: return dbg ? stream_kernel_ptr<Dec, 1, true>() : stream_kernel_ptr<Dec, 1, false>();
     case 2: return dbg ? stream_kernel_ptr<Dec, 2, true>() : stream_kernel_ptr<Dec, 2, false>();
@@ -793,7 +942,28 @@ cudaError_t plan_t(int rows, int width, int tile_rows, int tokens, StreamPlan *p
     if (env_chunk > 0) q.chunk = env_chunk;
     q.chunk = std::max(1, std::min(q.chunk, q.nb));
     q.stage_bytes = static_cast<uint32_t>((q.chunk * unit_bytes + 16 + 15) / 16 * 16);  // +16: decoder over-read
-    q.threads = q.groups * row_threads + 32;
+    // Threads per superblock (no effect on the arithmetic: a superblock's
+    // integer sums are exact however they are split).  One token per launch
+    // takes as many as the CTA bound allows, so that enough warps decode.
+    q.parts = 1;
+    q.group_threads = row_threads;
+    // Split only Q6_K tiles whose height leaves lanes of a whole-warp group
+    // idle (measured: splitting costs more than it gains elsewhere, and a
+    // split CTA holds too many registers for the next launch's CTA to be
+    // resident beside it).  Q38CU_STREAM_PARTS=n overrides the choice (1: off).
+    int max_parts = env_knob("Q38CU_STREAM_PARTS", 0);
+    if (max_parts <= 0) max_parts = std::is_same<Dec, DecQ6K>::value && tile_rows % 32 != 0 ? 4 : 1;
+    if (q.mt == 1 && SplitParts<Dec>::kMax > 1 && max_parts > 1) {
+        for (int parts = std::min(4, SplitParts<Dec>::kMax); parts > 1; parts >>= 1) {
+            const int gt = (tile_rows * parts + 31) / 32 * 32;
+            if (parts <= max_parts && q.groups * gt + 32 <= StreamThreads<1, 4>::kValue) {
+                q.parts = parts;
+                q.group_threads = gt;
+                break;
+            }
+        }
+    }
+    q.threads = q.groups * q.group_threads + 32;
     q.grid = q.tiles <= sms ? q.tiles : sms;
     const int env_grid = env_knob("Q38CU_STREAM_GRID", 0);
     if (env_grid > 0) q.grid = static_cast<int>(std::min<long long>(q.units, env_grid));
@@ -847,6 +1017,8 @@ cudaError_t launch_t(const StreamPlan &p, const StreamLaunch &l, cudaStream_t st
     g.tiles = p.tiles;
     g.units = static_cast<int>(p.units);
     g.groups = p.groups;
+    g.parts = p.parts;
+    g.group_threads = p.group_threads;
     g.stages = p.stages;
     g.chunk = p.chunk;
     g.stage_bytes = p.stage_bytes;
@@ -865,8 +1037,11 @@ cudaError_t launch_t(const StreamPlan &p, const StreamLaunch &l, cudaStream_t st
     g.act_y_rep_bytes = l.act_y_rep_bytes;
     g.out_reps = l.out_reps > 1 ? l.out_reps : 1;
     g.out_rep_bytes = l.out_rep_bytes;
-    g.pf_ptr = static_cast<const uint8_t *>(l.pf_ptr);
-    g.pf_bytes = l.pf_bytes;
+    g.nx_weights = static_cast<const uint8_t *>(l.nx_weights);
+    g.nx_units = l.nx_units;
+    g.nx_grid = l.nx_grid;
+    g.nx_unit_bytes = l.nx_unit_bytes;
+    g.nx_cta_bytes = l.nx_cta_bytes;
     g.sw_act = l.sw_act;
     g.sw_q8 = static_cast<Q8KBlock *>(l.sw_q8);
     g.sw_counters = l.sw_counters;
@@ -879,7 +1054,9 @@ cudaError_t launch_t(const StreamPlan &p, const StreamLaunch &l, cudaStream_t st
     g.max_slots = p.max_slots;
     g.dbg_w = l.dbg_w;
     g.dbg_x = l.dbg_x;
-    const void *kernel = select_kernel<Dec>(p.mt, l.dbg_w != nullptr);
+    g.trace = l.trace;
+    const void *kernel = select_kernel<Dec>(p.mt, l.dbg_w != nullptr, p.parts);
+    if (!kernel) return cudaErrorInvalidValue;
     cudaError_t e = opt_in(kernel);
     if (e != cudaSuccess) return e;
 

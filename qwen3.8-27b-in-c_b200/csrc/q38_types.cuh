@@ -178,6 +178,67 @@ struct DecQ4K {
             v[t] = __fsub_rn(__fmul_rn(dd, static_cast<float>(w[t])), __fmul_rn(dm, static_cast<float>(m)));
         }
     }
+    // Part j of L (L = 2 or 4) of `block`: the integer sums of sub-block pairs
+    // c = j * 4 / L .. (j + 1) * 4 / L - 1 only.  Integer sums add exactly, so
+    // the parts of a row, added and passed to `finish`, give bit for bit what
+    // `block` gives.
+    template <int MT, int L, class A>
+    __device__ static void block_part(const uint8_t *blk, const A &a, int j, int (&w)[MT], int (&x)[MT])
+    {
+        constexpr int kC = 4 / L;
+        const uint4 *p = reinterpret_cast<const uint4 *>(blk);
+        const uint4 h = p[0];
+        const uint32_t s0 = h.y, s1 = h.z, s2 = h.w;
+        const uint32_t sc_lo = s0 & 0x3F3F3F3Fu;
+        const uint32_t m_lo = s1 & 0x3F3F3F3Fu;
+        const uint32_t sc_hi = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
+        const uint32_t m_hi = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
+#pragma unroll
+        for (int t = 0; t < MT; ++t) w[t] = x[t] = 0;
+#pragma unroll
+        for (int cc = 0; cc < kC; ++cc) {
+            const int c = j * kC + cc;
+            const uint4 qa = p[1 + 2 * c], qb = p[2 + 2 * c];
+            const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+            const uint32_t scw = c < 2 ? sc_lo : sc_hi;
+            const int sc0 = static_cast<int>(byte_of(scw, (2 * c) & 3));
+            const int sc1 = static_cast<int>(byte_of(scw, (2 * c + 1) & 3));
+            // mins of sub-blocks 2c, 2c + 1 moved to bytes 0, 1
+            const uint32_t mw = (c < 2 ? m_lo : m_hi) >> (16 * (c & 1));
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+                const uint4 x0 = a.q4(t, 4 * c), x1 = a.q4(t, 4 * c + 1);
+                const uint4 x2 = a.q4(t, 4 * c + 2), x3 = a.q4(t, 4 * c + 3);
+                const uint32_t xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                const uint32_t xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+                int dl0 = 0, dl1 = 0, dh0 = 0, dh1 = 0;
+#pragma unroll
+                for (int i = 0; i < 8; i += 2) {
+                    dl0 = dp4a_ss(q[i] & 0x0F0F0F0Fu, xl[i], dl0);
+                    dl1 = dp4a_ss(q[i + 1] & 0x0F0F0F0Fu, xl[i + 1], dl1);
+                    dh0 = dp4a_us(q[i] & 0xF0F0F0F0u, xh[i], dh0);
+                    dh1 = dp4a_us(q[i + 1] & 0xF0F0F0F0u, xh[i + 1], dh1);
+                }
+                // the high-nibble sum is an exact multiple of 16
+                w[t] += sc0 * (dl0 + dl1) + ((sc1 * (dh0 + dh1)) >> 4);
+                x[t] = dp2a_lo_ss(a.aux(t, c), mw, x[t]);
+            }
+        }
+    }
+    // The float value of a superblock from its whole integer sums.
+    template <int MT, class A>
+    __device__ static void finish(const uint8_t *blk, const A &a, const int (&w)[MT], const int (&x)[MT],
+                                  float (&v)[MT])
+    {
+        const uint32_t hx = *reinterpret_cast<const uint32_t *>(blk);
+        const float d = f16_bits_to_f32(hx & 0xFFFFu);
+        const float dmin = f16_bits_to_f32(hx >> 16);
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+            const float dd = __fmul_rn(d, a.xs(t)), dm = __fmul_rn(dmin, a.xs(t));
+            v[t] = __fsub_rn(__fmul_rn(dd, static_cast<float>(w[t])), __fmul_rn(dm, static_cast<float>(x[t])));
+        }
+    }
 };
 
 // ===========================================================================
@@ -252,6 +313,64 @@ struct DecQ6K {
             x[t] = 0;
             v[t] = __fmul_rn(__fmul_rn(d, a.xs(t)), static_cast<float>(w[t]));
         }
+    }
+    // Part j of L (L = 2 or 4) of `block`: L = 2 takes half h = j (sub-blocks
+    // 8h .. 8h + 7), L = 4 half h = j / 2 and quarter groups qq = j % 2 and
+    // j % 2 + 2 (both read low-bit words 8 (j % 2) .. + 7 of the half).  The
+    // 32 * sum(sc * bsum) offset is split the same way; parts add exactly.
+    template <int MT, int L, class A>
+    __device__ static void block_part(const uint8_t *blk, const A &a, int j, int (&w)[MT], int (&x)[MT])
+    {
+        static_assert(L == 2 || L == 4, "Q6_K splits in 2 or 4 parts");
+        constexpr int kQq = L == 4 ? 2 : 4;
+        const int h = L == 4 ? (j >> 1) : j;
+        const int qsel = L == 4 ? (j & 1) : 0;
+        const int8_t *scales = reinterpret_cast<const int8_t *>(blk + 192);
+        uint32_t ql[L == 4 ? 8 : 16], qh[8];
+        lds_words<L == 4 ? 8 : 16>(blk + 64 * h + 32 * qsel, ql);
+        lds_words<8>(blk + 128 + 32 * h, qh);
+        int acc[MT], off[MT];
+#pragma unroll
+        for (int t = 0; t < MT; ++t) acc[t] = off[t] = 0;
+#pragma unroll
+        for (int k = 0; k < kQq; ++k) {
+            const int qq = L == 4 ? qsel + 2 * k : k;
+            const bool high = L == 4 ? k == 1 : k >= 2;  // nibble of the low-bit words
+            const int lw0 = L == 4 ? 0 : (k & 1) * 8;
+            uint32_t val[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t lw = ql[lw0 + i];
+                const uint32_t nib = high ? ((lw >> 4) & 0x0F0F0F0Fu) : (lw & 0x0F0F0F0Fu);
+                val[i] = nib | (((qh[i] >> (2 * qq)) & 0x03030303u) << 4);
+            }
+            const int s = 4 * h + qq;
+            const int sc0 = scales[2 * s], sc1 = scales[2 * s + 1];
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+                const uint4 x0 = a.q4(t, 2 * s), x1 = a.q4(t, 2 * s + 1);
+                const int da = dp4a_us(val[0], x0.x, 0) + dp4a_us(val[1], x0.y, 0) +
+                               (dp4a_us(val[2], x0.z, 0) + dp4a_us(val[3], x0.w, 0));
+                const int db = dp4a_us(val[4], x1.x, 0) + dp4a_us(val[5], x1.y, 0) +
+                               (dp4a_us(val[6], x1.z, 0) + dp4a_us(val[7], x1.w, 0));
+                acc[t] += sc0 * da + sc1 * db;
+                const uint32_t bw = a.aux(t, s);  // bsums of sub-blocks 2s, 2s + 1
+                off[t] += sc0 * lo16(bw) + sc1 * hi16(bw);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+            w[t] = acc[t] - 32 * off[t];
+            x[t] = 0;
+        }
+    }
+    template <int MT, class A>
+    __device__ static void finish(const uint8_t *blk, const A &a, const int (&w)[MT], const int (&)[MT],
+                                  float (&v)[MT])
+    {
+        const float d = f16_bits_to_f32(*reinterpret_cast<const unsigned short *>(blk + 208));
+#pragma unroll
+        for (int t = 0; t < MT; ++t) v[t] = __fmul_rn(__fmul_rn(d, a.xs(t)), static_cast<float>(w[t]));
     }
 };
 

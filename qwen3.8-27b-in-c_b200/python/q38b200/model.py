@@ -41,6 +41,7 @@ def _bind():
         "q38cu_model_generate_greedy": ([vp, u32, u32, u32p], ctypes.c_int),
         "q38cu_model_stream": ([vp], vp),
         "q38cu_model_step_kernels": ([vp], ctypes.c_int),
+        "q38cu_model_trace": ([vp, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -140,3 +141,18 @@ class Model:
     @property
     def step_kernels(self):
         return self.lib.q38cu_model_step_kernels(self.handle)
+
+    def trace(self, max_records=1024):
+        """Launch timeline of the decode step since the last call (needs
+        Q38CU_TRACE=1 at open): uint64 array [kernels][11] in ns, launch
+        order: min start, min ready, max end, max staged, max decoded, max
+        start, max ready, min staged, min RMSNorm sum known, min first
+        activation floats arrived, min warp 0 quantized (fields 3.. are only
+        set by the weight-streaming GEMV; the last three only for a fused
+        RMSNorm input)."""
+        buf = np.zeros((max_records, 11), np.uint64)
+        n = self.lib.q38cu_model_trace(self.handle, buf.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)),
+                                       max_records)
+        if n < 0:
+            raise ModelError(f"trace failed: {last_error()}")
+        return buf[:n]

@@ -23,6 +23,11 @@
 //     activation column (staged once in shared memory; all threads read the
 //     same column - a broadcast).  The superblock's integer sums form inside
 //     one thread; its float contribution is added to the thread's row sum.
+//     For Q6_K tiles whose height leaves lanes of the groups idle (40 rows:
+//     the 5120-row tensors; 8 rows: attn_v), a row's superblock is instead
+//     split over L = 4 consecutive lanes that form parts of its integer sums,
+//     added exactly with warp shuffles before the float formula: the split
+//     changes no result.
 // At the end of a tile (or of the CTA's range) the groups' row sums are added
 // in group order; a tile shared between CTAs is finished by the last CTA to
 // deposit its sums (per-tile counter, deposits added in CTA order).  T, J, C

@@ -121,7 +121,6 @@ struct Q38Model {
     cudaStream_t stream = nullptr;
     uint32_t context_length = 0, position = 0, mtp_position = 0;
     bool mtp_loaded = false, mtp_enabled = false;
-    int attn_splits = 6;
     float theta_scale = 0.0f;
 
     Q38CuTensor embedding{}, mtp_embedding{};  // GGUF layout, row lookups
@@ -143,8 +142,8 @@ struct Q38Model {
     int wide_ld = 0, ba_ld = 0;
     int *ctl = nullptr;  // [0] token, [1] position, [2] history count
     uint32_t *ids = nullptr, *argmax_out = nullptr, *history = nullptr;
-    float *attn_partials = nullptr, *argmax_part_v = nullptr;
-    int *attn_counters = nullptr, *argmax_part_i = nullptr, *argmax_counters = nullptr;
+    float *argmax_part_v = nullptr;
+    int *argmax_part_i = nullptr, *argmax_counters = nullptr;
     int *swiglu_counters = nullptr;  // one per Q8_K block of the FFN activation
 
     // host staging
@@ -413,7 +412,6 @@ bool alloc_runtime(Q38Model *m)
     const size_t ctx = m->context_length;
     m->wide_ld = std::max({kLinQkv + kLinV, kAttnQg + 2 * kAttnKv, 2 * kFfn});
     m->ba_ld = 2 * kLinHeads;
-    m->attn_splits = std::max(6, static_cast<int>((ctx + q38::kAttnMaxChunk - 1) / q38::kAttnMaxChunk));
     const size_t q8_blocks = kMaxTokens * static_cast<size_t>(kFfn / 256);
     return dalloc(&m->conv_ring, static_cast<size_t>(kRecurrent) * kLinQkv * kConvRing, o) &&
            dalloc(&m->delta_state, static_cast<size_t>(kRecurrent) * kLinHeads * kLinDim * kLinDim, o) &&
@@ -427,8 +425,7 @@ bool alloc_runtime(Q38Model *m)
            dalloc(&m->target_norm, kMaxDrafts * static_cast<size_t>(kHidden), o) &&
            dalloc(&m->ctl, 4, o) && dalloc(&m->ids, kMaxTokens, o) && dalloc(&m->argmax_out, kMaxDrafts, o) &&
            dalloc(&m->history, ctx + 1, o) &&
-           dalloc(&m->attn_partials, kMaxTokens * 24 * static_cast<size_t>(m->attn_splits) * (kAttnDim + 2), o) &&
-           dalloc(&m->attn_counters, kMaxTokens * 24, o) && dalloc(&m->swiglu_counters, kFfn / 256, o) &&
+           dalloc(&m->swiglu_counters, kFfn / 256, o) &&
            dalloc(&m->argmax_part_v, kMaxTokens * q38::kArgmaxCtas, o) &&
            dalloc(&m->argmax_part_i, kMaxTokens * q38::kArgmaxCtas, o) &&
            dalloc(&m->argmax_counters, kMaxTokens, o) &&
@@ -718,9 +715,6 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         a.ctl = m->ctl;
         a.theta_scale = m->theta_scale;
         a.tokens = tokens;
-        a.splits = m->attn_splits;
-        a.partials = m->attn_partials;
-        a.counters = m->attn_counters;
         a.out_f = m->act_f;
         a.out_q = m->q8;
         a.reps = kReps;

@@ -7,9 +7,10 @@
 
 namespace q38 {
 
-// Largest number of positions one attention CTA scores (shared memory bound);
-// the model picks splits >= context / kAttnMaxChunk.
-constexpr int kAttnMaxChunk = 2048;
+// Attention: the CTAs (one thread-block cluster) that share one (token, head),
+// and the positions per CTA below which fewer of them take part.
+constexpr int kAttnSplits = 8;
+constexpr int kAttnSplitPositions = 64;
 constexpr int kArgmaxCtas = 148;
 
 // The device control block every captured step reads: ctl[0] = input token
@@ -50,9 +51,7 @@ struct AttnArgs {
     float *k_cache, *v_cache;      // this layer's [context][1024]
     const int *ctl;
     float theta_scale;  // powf(1e7, -2 / 64), computed on the host as upstream
-    int tokens, splits;
-    float *partials;  // [tokens * 24 * splits][258]
-    int *counters;    // [tokens * 24], zero between launches
+    int tokens;
     float *out_f;     // optional [tokens][6144]
     void *out_q;      // [tokens][24] Q8_K, written to all reps copies q_rep_bytes apart
     int reps;

@@ -44,12 +44,6 @@ __device__ __forceinline__ float warp_sum_f(float v)
     return v;
 }
 
-__device__ __forceinline__ float warp_max_f(float v)
-{
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
 
 // Sum of a double over the CTA (all threads get the result).  `red` holds one
 // double per warp; the warps' partials are added in warp order.
@@ -62,18 +56,6 @@ __device__ double block_sum_d(double v, double *red)
     __syncthreads();
     double t = 0.0;
     for (int w = 0; w < warps; ++w) t += red[w];
-    return t;
-}
-
-__device__ float block_max_f(float v, float *red)
-{
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
-    v = warp_max_f(v);
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = red[0];
-    for (int w = 1; w < warps; ++w) t = fmaxf(t, red[w]);
     return t;
 }
 
@@ -556,14 +538,22 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
 // Full attention (qwen38_model.c:697-713, 816-885) for `tokens` tokens at
 // positions base .. base + tokens - 1.
 //
-// Grid: tokens x 24 heads x `splits` CTAs of 256 threads; thread d owns head
-// dimension d.  CTA (t, h, s) normalizes and rotates its query, scores the
-// positions of split s of [0, base + t], and leaves (max, sum, weighted V) in
-// the scratch; the last CTA of (t, h) to finish merges the splits, applies
-// the sigmoid gate and quantizes the head (one Q8_K block per head).
+// Grid: tokens x 24 heads x kAttnSplits CTAs of 256 threads; the kAttnSplits
+// CTAs of one (token, head) form a thread-block cluster.  The positions
+// [0, len) of the token are cut into `active` = min(kAttnSplits, ceil(len /
+// kAttnSplitPositions)) contiguous ranges, one per CTA of the cluster (the
+// others only keep the cluster's barriers); the cut depends on len alone, so
+// a token's result does not depend on how many tokens share the launch.
+// In a CTA, warp w scores positions in groups of four (all K and V rows of a
+// group loaded before any is used) and keeps a running softmax: its maximum,
+// its sum of exponentials and the weighted V of its lane's 8 dimensions.  The
+// warps' states merge in warp order in shared memory, the CTAs' states merge
+// in rank order in the cluster's rank 0 through distributed shared memory,
+// which applies the sigmoid gate and quantizes the head (one Q8_K block).
 // Keys and values of this launch's own tokens are recomputed where needed
-// rather than read back from the cache; CTA (t, 6g, 0) writes token t's key
-// and value rows of KV head g into the cache, which no CTA of the launch reads.
+// rather than read back from the cache; CTA (t, 6g, rank 0) writes token t's
+// key and value rows of KV head g into the cache, which no CTA of the launch
+// reads.
 // ---------------------------------------------------------------------------
 constexpr int kAttnHeads = 24, kAttnDim = 256, kMaxTokens = 8;
 
@@ -571,11 +561,14 @@ struct AttnShared {
     float q[kAttnDim];
     float knew[kMaxTokens][kAttnDim];
     float vnew[kMaxTokens][kAttnDim];
-    float scores[kAttnMaxChunk];
+    float tmp[kAttnDim];
+    float wacc[8][kAttnDim];  // per-warp weighted values
+    float wm[8], wl[8];       // per-warp running maximum and sum
+    float acc[kAttnDim];      // this CTA's merged state, read by the cluster's rank 0
+    float m, l;
     double red_d[8];
     float red_f[8];
     AbsMax red_m[8];
-    int last;
 };
 
 // Normalize (RMSNorm with `norm`) and rotate (first 64 dims, pairs (j, j + 32))
@@ -599,13 +592,28 @@ __device__ float norm_rope(float x, const float *norm, int pos, float theta_scal
     return d < 32 ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
 }
 
+__device__ __forceinline__ float dot8(const float4 qa, const float4 qb, const float4 ka, const float4 kb)
+{
+    float part = fmaf(qa.x, ka.x, fmaf(qa.y, ka.y, fmaf(qa.z, ka.z, __fmul_rn(qa.w, ka.w))));
+    return fmaf(qb.x, kb.x, fmaf(qb.y, kb.y, fmaf(qb.z, kb.z, fmaf(qb.w, kb.w, part))));
+}
+
+__device__ __forceinline__ void scale_add(float4 &acc, float c, float w, const float4 v)
+{
+    acc.x = fmaf(w, v.x, __fmul_rn(acc.x, c));
+    acc.y = fmaf(w, v.y, __fmul_rn(acc.y, c));
+    acc.z = fmaf(w, v.z, __fmul_rn(acc.z, c));
+    acc.w = fmaf(w, v.w, __fmul_rn(acc.w, c));
+}
+
 __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
 {
     __shared__ AttnShared sh;
     trace_mark(a.trace, kTraceStart);
+    cg::cluster_group cluster = cg::this_cluster();
     const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
-    const int split = blockIdx.x % a.splits;
-    const int th = blockIdx.x / a.splits;
+    const int split = static_cast<int>(cluster.block_rank());
+    const int th = blockIdx.x / kAttnSplits;
     const int h = th % kAttnHeads, t = th / kAttnHeads;
     const int g = h / (kAttnHeads / 4);
     if (d == 0) prefetch_share_l2(a.pf_ptr, a.pf_bytes);  // keeps HBM busy through this latency-bound step
@@ -614,116 +622,136 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
     trace_mark(a.trace, kTraceReady);
     const int base = a.ctl[1];
     const int pos = base + t, len = pos + 1;
-    const int chunk = (len + a.splits - 1) / a.splits;
+    const int active = min(kAttnSplits, (len + kAttnSplitPositions - 1) / kAttnSplitPositions);
+    const int chunk = (len + active - 1) / active;
     const int p0 = min(len, split * chunk), p1 = min(len, p0 + chunk);
     const float *row = a.qkv + static_cast<size_t>(t) * a.qkv_ld;
-
-    // query: RMSNorm + RoPE
-    const float q = norm_rope(row[h * 512 + d], a.q_norm, pos, a.theta_scale, sh.scores, sh.red_d);
-    __syncthreads();
-    trace_mark(a.trace, kTraceXLoaded);  // query normalized and rotated
-    sh.q[d] = q;
-
-    // keys/values of this launch's tokens that fall in [p0, p1), and the
-    // cache rows of token t (written by one CTA per KV head)
     const bool writer = (h % (kAttnHeads / 4)) == 0 && split == 0;
-    for (int tt = 0; tt <= t; ++tt) {
-        const int pp = base + tt;
-        const bool needed = pp >= p0 && pp < p1;
-        if (!needed && !(writer && tt == t)) continue;
-        const float *r2 = a.qkv + static_cast<size_t>(tt) * a.qkv_ld;
+
+    if (split < active) {
+        const float gate = row[h * 512 + 256 + d];  // loaded with the query, used by rank 0
+        // query: RMSNorm + RoPE
+        const float q = norm_rope(row[h * 512 + d], a.q_norm, pos, a.theta_scale, sh.tmp, sh.red_d);
         __syncthreads();
-        const float kx = norm_rope(r2[a.k_off + g * 256 + d], a.k_norm, pp, a.theta_scale, sh.scores, sh.red_d);
-        const float vx = r2[a.v_off + g * 256 + d];
-        sh.knew[tt][d] = kx;
-        sh.vnew[tt][d] = vx;
-        if (writer && tt == t) {
-            a.k_cache[static_cast<size_t>(pp) * 1024 + g * 256 + d] = kx;
-            a.v_cache[static_cast<size_t>(pp) * 1024 + g * 256 + d] = vx;
+        trace_mark(a.trace, kTraceXLoaded);  // query normalized and rotated
+        sh.q[d] = q;
+        // keys/values of this launch's tokens that fall in [p0, p1), and the
+        // cache rows of token t (written by one CTA per KV head)
+        for (int tt = 0; tt <= t; ++tt) {
+            const int pp = base + tt;
+            const bool needed = pp >= p0 && pp < p1;
+            if (!needed && !(writer && tt == t)) continue;
+            const float *r2 = a.qkv + static_cast<size_t>(tt) * a.qkv_ld;
+            __syncthreads();
+            const float kx = norm_rope(r2[a.k_off + g * 256 + d], a.k_norm, pp, a.theta_scale, sh.tmp, sh.red_d);
+            const float vx = r2[a.v_off + g * 256 + d];
+            sh.knew[tt][d] = kx;
+            sh.vnew[tt][d] = vx;
+            if (writer && tt == t) {
+                a.k_cache[static_cast<size_t>(pp) * 1024 + g * 256 + d] = kx;
+                a.v_cache[static_cast<size_t>(pp) * 1024 + g * 256 + d] = vx;
+            }
         }
-    }
-    __syncthreads();
-    trace_mark(a.trace, kTraceNormed);  // this launch's keys and values ready
+        __syncthreads();
+        trace_mark(a.trace, kTraceNormed);  // this launch's keys and values ready
 
-    // scores of positions [p0, p1): warp w takes p0 + w, p0 + w + 8, ...
-    const float4 qa = *reinterpret_cast<const float4 *>(&sh.q[lane * 4]);
-    const float4 qb = *reinterpret_cast<const float4 *>(&sh.q[128 + lane * 4]);
-    float local_max = -INFINITY;
-    for (int p = p0 + warp; p < p1; p += 8) {
-        const float *k = p < base ? a.k_cache + static_cast<size_t>(p) * 1024 + g * 256 : sh.knew[p - base];
-        const float4 ka = *reinterpret_cast<const float4 *>(k + lane * 4);
-        const float4 kb = *reinterpret_cast<const float4 *>(k + 128 + lane * 4);
-        float part = fmaf(qa.x, ka.x, fmaf(qa.y, ka.y, fmaf(qa.z, ka.z, __fmul_rn(qa.w, ka.w))));
-        part = fmaf(qb.x, kb.x, fmaf(qb.y, kb.y, fmaf(qb.z, kb.z, fmaf(qb.w, kb.w, part))));
-        const float score = __fmul_rn(warp_sum_f(part), 0.0625f);  // 1 / sqrt(256)
-        if (lane == 0) sh.scores[p - p0] = score;
-        local_max = fmaxf(local_max, score);
-    }
-    const float m = block_max_f(local_max, sh.red_f);  // includes the barrier for sh.scores
-    trace_mark(a.trace, kTraceQuantized);  // scores done
-    float l_part = 0.0f;
-    for (int i = d; i < p1 - p0; i += 256) {
-        const float e = expf(__fsub_rn(sh.scores[i], m));
-        sh.scores[i] = e;
-        l_part = __fadd_rn(l_part, e);
-    }
-    __syncthreads();
-    const double l = block_sum_d(static_cast<double>(l_part), sh.red_d);
-    // weighted values in position order; the loads of 8 positions are issued
-    // before their products
-    float acc = 0.0f;
-    int p = p0;
-    for (; p + 8 <= p1; p += 8) {
-        float v[8];
+        // Running softmax over the warp's positions: group i covers positions
+        // p0 + 32 i + 4 warp + k, k = 0..3.  Lane l holds dimensions 4l..4l+3
+        // and 128 + 4l..+3 of q, of each K and V row and of the weighted sum.
+        const float4 qa = *reinterpret_cast<const float4 *>(&sh.q[lane * 4]);
+        const float4 qb = *reinterpret_cast<const float4 *>(&sh.q[128 + lane * 4]);
+        float m_run = -INFINITY, l_run = 0.0f;
+        float4 acc_a = make_float4(0.f, 0.f, 0.f, 0.f), acc_b = acc_a;
+        for (int p = p0 + 4 * warp; p < p1; p += 32) {
+            float4 ka[4], kb[4], va[4], vb[4];
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-            v[k] = p + k < base ? a.v_cache[static_cast<size_t>(p + k) * 1024 + g * 256 + d] : sh.vnew[p + k - base][d];
+            for (int k = 0; k < 4; ++k) {
+                const int pk = min(p + k, p1 - 1);  // past the range: a valid row, masked below
+                const float *kr = pk < base ? a.k_cache + static_cast<size_t>(pk) * 1024 + g * 256 : sh.knew[pk - base];
+                const float *vr = pk < base ? a.v_cache + static_cast<size_t>(pk) * 1024 + g * 256 : sh.vnew[pk - base];
+                ka[k] = *reinterpret_cast<const float4 *>(kr + lane * 4);
+                kb[k] = *reinterpret_cast<const float4 *>(kr + 128 + lane * 4);
+                va[k] = *reinterpret_cast<const float4 *>(vr + lane * 4);
+                vb[k] = *reinterpret_cast<const float4 *>(vr + 128 + lane * 4);
+            }
+            float sc[4];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc = fmaf(sh.scores[p + k - p0], v[k], acc);
+            for (int k = 0; k < 4; ++k) sc[k] = dot8(qa, qb, ka[k], kb[k]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) sc[k] = __fadd_rn(sc[k], __shfl_xor_sync(0xffffffffu, sc[k], o));
+            }
+            float m_new = m_run;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                sc[k] = p + k < p1 ? __fmul_rn(sc[k], 0.0625f) : -INFINITY;  // 1 / sqrt(256)
+                m_new = fmaxf(m_new, sc[k]);
+            }
+            const float c = expf(__fsub_rn(m_run, m_new));
+            l_run = __fmul_rn(l_run, c);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float w = p + k < p1 ? expf(__fsub_rn(sc[k], m_new)) : 0.0f;
+                l_run = __fadd_rn(l_run, w);
+                scale_add(acc_a, k == 0 ? c : 1.0f, w, va[k]);
+                scale_add(acc_b, k == 0 ? c : 1.0f, w, vb[k]);
+            }
+            m_run = m_new;
+        }
+        trace_mark(a.trace, kTraceQuantized);  // this warp's positions done
+        // warps -> CTA state (warp order)
+        *reinterpret_cast<float4 *>(&sh.wacc[warp][lane * 4]) = acc_a;
+        *reinterpret_cast<float4 *>(&sh.wacc[warp][128 + lane * 4]) = acc_b;
+        __syncthreads();
+        if (lane == 0) {
+            sh.wm[warp] = m_run;
+            sh.wl[warp] = l_run;
+        }
+        __syncthreads();
+        float mx = -INFINITY;
+        for (int w = 0; w < 8; ++w) mx = fmaxf(mx, sh.wm[w]);
+        float acc = 0.0f, l = 0.0f;
+        for (int w = 0; w < 8; ++w) {
+            if (sh.wm[w] == -INFINITY) continue;
+            const float c = expf(__fsub_rn(sh.wm[w], mx));
+            acc = fmaf(sh.wacc[w][d], c, acc);
+            l = fmaf(sh.wl[w], c, l);
+        }
+        sh.acc[d] = acc;
+        if (d == 0) {
+            sh.m = mx;
+            sh.l = l;
+        }
+        // the keys and values are read: the next kernel's weight prefetch may start
+        pdl_launch_dependents();
+        trace_mark(a.trace, kTraceFirstStaged);  // CTA state ready
+        trace_mark(a.trace, kTraceStaged);
+        cluster.sync();
+        if (split == 0) {
+            // merge the active ranks in rank order; gate; Q8_K
+            float M = -INFINITY;
+            for (int r = 0; r < active; ++r) M = fmaxf(M, cluster.map_shared_rank(&sh, r)->m);
+            float num = 0.0f, den = 0.0f;
+            for (int r = 0; r < active; ++r) {
+                const AttnShared *peer = cluster.map_shared_rank(&sh, r);
+                const float mr = peer->m;
+                if (mr == -INFINITY) continue;
+                const float c = expf(__fsub_rn(mr, M));
+                den = fmaf(peer->l, c, den);
+                num = fmaf(peer->acc[d], c, num);
+            }
+            float o = __fdiv_rn(num, den);
+            o = __fmul_rn(o, sigmoid(gate));
+            if (a.out_f) a.out_f[static_cast<size_t>(t) * 6144 + h * 256 + d] = o;
+            quantize_block_256(o, static_cast<Q8KBlock *>(a.out_q) + static_cast<size_t>(t) * 24 + h, sh.red_m,
+                               a.reps, a.q_rep_bytes);
+        }
+    } else {
+        pdl_launch_dependents();
+        cluster.sync();
     }
-    for (; p < p1; ++p) {
-        const float v = p < base ? a.v_cache[static_cast<size_t>(p) * 1024 + g * 256 + d] : sh.vnew[p - base][d];
-        acc = fmaf(sh.scores[p - p0], v, acc);
-    }
-
-    // the keys and values are read: the next kernel's weight prefetch may start
-    pdl_launch_dependents();
-    trace_mark(a.trace, kTraceFirstStaged);  // weighted values done
-    trace_mark(a.trace, kTraceStaged);
-
-    // leave this split's partial result; the last CTA of (t, h) merges
-    float *part = a.partials + static_cast<size_t>(blockIdx.x) * (kAttnDim + 2);
-    part[2 + d] = acc;
-    if (d == 0) {
-        part[0] = p1 > p0 ? m : -INFINITY;
-        part[1] = static_cast<float>(l);
-    }
-    __threadfence();
-    __syncthreads();
-    if (d == 0) sh.last = atomicAdd(&a.counters[th], 1) == a.splits - 1;
-    __syncthreads();
-    if (!sh.last) {
-        trace_mark(a.trace, kTraceEnd);
-        return;
-    }
-    __threadfence();
-    const float *parts = a.partials + static_cast<size_t>(th) * a.splits * (kAttnDim + 2);
-    float mx = -INFINITY;
-    for (int s = 0; s < a.splits; ++s) mx = fmaxf(mx, __ldcg(parts + s * (kAttnDim + 2)));
-    float den = 0.0f, num = 0.0f;
-    for (int s = 0; s < a.splits; ++s) {
-        const float ms = __ldcg(parts + s * (kAttnDim + 2));
-        if (ms == -INFINITY) continue;
-        const float w = expf(__fsub_rn(ms, mx));
-        den = fmaf(__ldcg(parts + s * (kAttnDim + 2) + 1), w, den);
-        num = fmaf(__ldcg(parts + s * (kAttnDim + 2) + 2 + d), w, num);
-    }
-    float o = __fdiv_rn(num, den);
-    o = __fmul_rn(o, sigmoid(row[h * 512 + 256 + d]));
-    if (a.out_f) a.out_f[static_cast<size_t>(t) * 6144 + h * 256 + d] = o;
-    quantize_block_256(o, static_cast<Q8KBlock *>(a.out_q) + static_cast<size_t>(t) * 24 + h, sh.red_m, a.reps,
-                       a.q_rep_bytes);
-    if (d == 0) a.counters[th] = 0;
+    cluster.sync();  // rank 0 has read every peer's state
     trace_mark(a.trace, kTraceEnd);
 }
 
@@ -849,8 +877,21 @@ cudaError_t launch_deltanet(const DeltaArgs &args, cudaStream_t s)
 
 cudaError_t launch_attention(const AttnArgs &args, cudaStream_t s)
 {
-    if (args.tokens < 1 || args.tokens > kMaxTokens || args.splits < 1) return cudaErrorInvalidValue;
-    return launch_pdl(attention_kernel, dim3(args.tokens * kAttnHeads * args.splits), dim3(256), s, args);
+    if (args.tokens < 1 || args.tokens > kMaxTokens) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(args.tokens * kAttnHeads * kAttnSplits);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = kAttnSplits;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, attention_kernel, args);
 }
 
 cudaError_t launch_argmax(const ArgmaxArgs &args, int tokens, cudaStream_t s)

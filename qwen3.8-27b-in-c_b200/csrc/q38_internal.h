@@ -83,6 +83,12 @@ struct StreamLaunch {
     int sw_q_reps = 1;
     long long sw_q_rep_bytes = 0;
     unsigned long long *trace = nullptr;  // optional launch timeline record (q38_device.cuh)
+    // RMSNorm input only: side_rows (<= grid) Q8_0 rows of width `width`
+    // (GGUF layout) dotted with the normalized floats into
+    // side_out[tok * side_ld + row] (see q38_stream.cu)
+    const void *side_w = nullptr;
+    int side_rows = 0, side_ld = 0;
+    float *side_out = nullptr;
 };
 
 enum : int { kActQ8K = 0, kActRmsNorm = 1, kActSwiGLU = 2 };

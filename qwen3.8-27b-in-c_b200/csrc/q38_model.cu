@@ -153,6 +153,13 @@ struct Q38Model {
 
     cudaGraphExec_t decode_graph = nullptr;
     int step_kernels = 0;  // kernel nodes of the decode graph
+    // Speculative decoding: one MTP draft step that feeds its argmax back
+    // into the control block (replayed once per draft), and the target's
+    // verification of n tokens with per-token DeltaNet state snapshots.
+    cudaGraphExec_t mtp_draft_graph = nullptr;
+    cudaGraphExec_t verify_graph[kMaxTokens + 1] = {};
+    float *delta_snap = nullptr;  // [kMaxTokens - 1][48][48][128][128]
+    bool snapping = false;        // set while a verification is captured
     // Launch timeline of the decode graph (Q38CU_TRACE=1 at open): one record
     // of q38::kTraceFields timestamps per traced kernel, in launch order.
     unsigned long long *trace = nullptr;
@@ -452,6 +459,11 @@ struct ActIn {
     float *f_out = nullptr;     // fused modes: optional float copy of the activation
     int reps = 1;               // copies of q8 / x (and y for SwiGLU), rep_bytes apart
     long long rep_bytes = 0, y_rep_bytes = 0;  // y_rep_bytes: copies of the RMSNorm weight
+    // kActRmsNorm: Q8_0 side rows formed in the first launch's prologue (see
+    // q38_stream.cu), e.g. ssm_beta | ssm_alpha beside attn_qkv | attn_gate
+    const void *side_w = nullptr;
+    int side_rows = 0, side_ld = 0;
+    float *side_out = nullptr;
 };
 
 // Copies of an output: the producer stores `reps` copies, `bytes` apart.
@@ -561,6 +573,12 @@ bool stream_project(const Part &p, const ActIn &in, int tokens, float *out, int 
         l.out_rep_bytes = orep.bytes;
         if (tok0 + plan.token_group >= tokens) set_next_prefetch(l, pf);
         if (tm) l.trace = next_trace(tm);
+        if (in.side_w) {
+            l.side_w = in.side_w;
+            l.side_rows = in.side_rows;
+            l.side_ld = in.side_ld;
+            l.side_out = in.side_out + static_cast<size_t>(tok0) * in.side_ld;
+        }
         if (sw) {
             const int width_out = p.rows / 2;
             l.sw_act = sw->act + static_cast<size_t>(tok0) * width_out;
@@ -615,7 +633,9 @@ bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int o
         const Part &part = p.parts[i];
         const Part *next = i + 1 < p.parts.size() ? &p.parts[i + 1] : next_after;
         if (part.int_path) {
-            if (!stream_project(part, in, tokens, out + part.offset, out_ld, accumulate, orep, prefetch_of(next), s,
+            ActIn pin = in;
+            if (i > 0) pin.side_w = nullptr;  // side rows come with the first launch only
+            if (!stream_project(part, pin, tokens, out + part.offset, out_ld, accumulate, orep, prefetch_of(next), s,
                                 nullptr, m))
                 return false;
         } else {
@@ -689,6 +709,21 @@ bool fusable_ba(const Proj &p)
            p.width == kHidden;
 }
 
+// beta | alpha can ride on the input projection's prologue: one Q8_0 tensor
+// of 2 x 48 rows over the hidden width, the projection's first part on the
+// integer path with at least one CTA per side row.
+bool side_ba_ok(const Q38Model *m, const Layer &L)
+{
+    if (!fusable_ba(L.ba) || L.in_proj.parts.empty() || !L.in_proj.parts[0].int_path) return false;
+    const Part &p = L.in_proj.parts[0];
+    q38::StreamPlan plan;
+    if (q38::stream_plan(static_cast<int>(p.t.type), p.rows, static_cast<int>(p.t.shape[0]),
+                         static_cast<int>(p.t.tile_rows), 1, &plan) != cudaSuccess)
+        return false;
+    (void)m;
+    return plan.grid >= L.ba.rows && m->ba_ld >= L.ba.rows;
+}
+
 bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
 {
     (void)base_hint;
@@ -700,7 +735,18 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
     const void *mixer_pf_ptr = nullptr;
     long long mixer_pf_bytes = 0;
     mixer_prefetch(first_part(L.out), &mixer_pf_ptr, &mixer_pf_bytes);
-    if (!project(m, L.in_proj, attn_in, tokens, m->wide, m->wide_ld, 0, OutReps(), first_part(L.out))) return false;
+    // DeltaNet beta | alpha (Q8_0, float path) as side rows of the input
+    // projection's prologue, which has RMSNorm(hidden) at hand
+    const bool ba_side = !L.full && side_ba_ok(m, L);
+    ActIn in_proj_in = attn_in;
+    if (ba_side) {
+        in_proj_in.side_w = L.ba.parts[0].t.data;
+        in_proj_in.side_rows = L.ba.rows;
+        in_proj_in.side_ld = m->ba_ld;
+        in_proj_in.side_out = m->ba;
+    }
+    if (!project(m, L.in_proj, in_proj_in, tokens, m->wide, m->wide_ld, 0, OutReps(), first_part(L.out)))
+        return false;
     const ActIn mixed = q8_input(m->q8, m->act_f, L.full ? kAttnQ : kLinV, true);
     if (L.full) {
         q38::AttnArgs a{};
@@ -725,7 +771,11 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         if (!cuda_ok(q38::launch_attention(a, s), "attention")) return false;
     } else {
         q38::DeltaArgs d{};
-        if (fusable_ba(L.ba)) {
+        if (ba_side) {
+            d.beta = m->ba;
+            d.alpha = m->ba + kLinHeads;
+            d.ba_ld = m->ba_ld;
+        } else if (fusable_ba(L.ba)) {
             d.ba_fused = 1;
             d.ba_w = static_cast<const uint8_t *>(L.ba.parts[0].t.data);
             d.hidden = m->hidden;
@@ -746,6 +796,10 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         d.a = L.a;
         d.norm_w = L.ssm_norm;
         d.state = m->delta_state + static_cast<size_t>(L.index) * kLinHeads * kLinDim * kLinDim;
+        if (m->snapping && m->delta_snap && L.index < kRecurrent) {
+            d.snap = m->delta_snap + static_cast<size_t>(L.index) * kLinHeads * kLinDim * kLinDim;
+            d.snap_stride = static_cast<long long>(kRecurrent) * kLinHeads * kLinDim * kLinDim;
+        }
         d.ctl = m->ctl;
         d.tokens = tokens;
         d.out_f = m->act_f;
@@ -1008,6 +1062,50 @@ bool build_decode_graph(Q38Model *m)
     return cuda_ok(ei, "graph instantiate");
 }
 
+// Capture `enqueue` on the model stream into an executable graph.
+template <typename F>
+bool capture_graph(Q38Model *m, cudaGraphExec_t *exec, F enqueue)
+{
+    if (*exec) return true;
+    cudaGraph_t graph = nullptr;
+    if (!cuda_ok(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "begin capture")) return false;
+    const bool ok = enqueue();
+    const cudaError_t e = cudaStreamEndCapture(m->stream, &graph);
+    if (!ok || !cuda_ok(e, "end capture")) {
+        if (graph) cudaGraphDestroy(graph);
+        return false;
+    }
+    const cudaError_t ei = cudaGraphInstantiate(exec, graph, 0);
+    cudaGraphDestroy(graph);
+    return cuda_ok(ei, "graph instantiate");
+}
+
+// One MTP draft step for the token in ctl[0] at MTP position ctl[1]
+// (qwen38_model.c:1588-1612): its argmax becomes ctl[0], ctl[1] advances and
+// the draft is appended to history[ctl[2]++].
+bool build_mtp_draft_graph(Q38Model *m)
+{
+    return capture_graph(m, &m->mtp_draft_graph, [&] {
+        return enqueue_mtp_body(m, reinterpret_cast<const uint32_t *>(m->ctl), 1, nullptr) &&
+               enqueue_head(m, m->shared_head_norm, m->mtp_output, 1, m->mtp_hidden, 0, true, 1);
+    });
+}
+
+// The target model over the n tokens in m->ids from position ctl[1], with
+// the DeltaNet state after each but the last token kept in m->delta_snap;
+// argmax of every token to argmax_out, normed hidden rows to target_norm,
+// logits of every token to m->logits.
+bool build_verify_graph(Q38Model *m, int n)
+{
+    return capture_graph(m, &m->verify_graph[n], [&] {
+        m->snapping = true;
+        bool ok = enqueue_embed(m, m->embedding, m->ids, n, m->hidden);
+        for (int l = 0; ok && l < kLayers; ++l) ok = enqueue_layer(m, l, n, 0);
+        m->snapping = false;
+        return ok && enqueue_head(m, m->output_norm, m->output, n, m->target_norm, 0, false, 0);
+    });
+}
+
 bool check_status(Q38Model *m)
 {
     if (!cuda_ok(cudaStreamSynchronize(m->stream), "step")) return false;
@@ -1077,6 +1175,9 @@ void q38_model_close(Q38Model *m)
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->decode_graph) cudaGraphExecDestroy(m->decode_graph);
+    if (m->mtp_draft_graph) cudaGraphExecDestroy(m->mtp_draft_graph);
+    for (auto &g : m->verify_graph)
+        if (g) cudaGraphExecDestroy(g);
     // tensors shared between the target and the MTP head are listed once
     for (auto &t : m->tensors) q38cu_tensor_free(&t);
     for (void *p : m->owned) cudaFree(p);
@@ -1215,6 +1316,9 @@ int q38_model_enable_mtp(Q38Model *m)
          !dalloc(reinterpret_cast<uint8_t **>(&m->ck_delta_state), delta_state_bytes(), m->owned) ||
          !dalloc(&m->ck_mtp_hidden, kHidden, m->owned)))
         return fail("unable to allocate speculative checkpoint%s");
+    if (!m->delta_snap &&
+        !dalloc(reinterpret_cast<uint8_t **>(&m->delta_snap), (kMaxTokens - 1) * delta_state_bytes(), m->owned))
+        return fail("unable to allocate the speculative state snapshots%s");
     m->mtp_enabled = true;
     return 1;
 }
@@ -1234,14 +1338,13 @@ int q38_model_mtp_forward(Q38Model *m, uint32_t token_id, const float **logits)
     return 1;
 }
 
-int q38_model_speculative_greedy(Q38Model *m, uint32_t token_id, uint32_t stop_token, uint32_t draft_count,
-                                 uint32_t *accepted_tokens, uint32_t *accepted_count, const float **next_logits)
+// Speculative greedy decoding for more than kMaxTokens drafts: drafts one
+// by one with a host round trip each, verifies in chunks, and on a mismatch
+// restores the checkpointed state and replays the consumed prefix.
+static int speculative_greedy_replay(Q38Model *m, uint32_t token_id, uint32_t stop_token, uint32_t draft_count,
+                                     uint32_t *accepted_tokens, uint32_t *accepted_count, const float **next_logits)
 {
-    if (!m || !m->mtp_enabled || !accepted_tokens || !accepted_count || !next_logits || token_id >= kVocab ||
-        draft_count == 0 || m->position != m->mtp_position || draft_count > m->context_length - m->position)
-        return 0;
-    if (draft_count > kMaxDrafts) return fail("draft_count above %s is not supported", std::to_string(kMaxDrafts));
-    if (!use_device(m) || !checkpoint_state(m)) return 0;
+    if (!checkpoint_state(m)) return 0;
 
     // drafts from the MTP head, greedy (qwen38_model.c:1636-1650)
     uint32_t drafts[kMaxDrafts], inputs[kMaxDrafts], target[kMaxDrafts];
@@ -1279,6 +1382,91 @@ int q38_model_speculative_greedy(Q38Model *m, uint32_t token_id, uint32_t stop_t
         restore_target_state(m);
         restore_mtp_state(m);
         cudaStreamSynchronize(m->stream);
+        return 0;
+    }
+    for (uint32_t i = 0; i < matched; ++i) accepted_tokens[i] = drafts[i];
+    if (matched < actual) accepted_tokens[matched] = next;
+    *accepted_count = consumed;
+    *next_logits = m->host_logits;
+    return 1;
+}
+
+int q38_model_speculative_greedy(Q38Model *m, uint32_t token_id, uint32_t stop_token, uint32_t draft_count,
+                                 uint32_t *accepted_tokens, uint32_t *accepted_count, const float **next_logits)
+{
+    if (!m || !m->mtp_enabled || !accepted_tokens || !accepted_count || !next_logits || token_id >= kVocab ||
+        draft_count == 0 || m->position != m->mtp_position || draft_count > m->context_length - m->position)
+        return 0;
+    if (draft_count > kMaxDrafts) return fail("draft_count above %s is not supported", std::to_string(kMaxDrafts));
+    if (!use_device(m)) return 0;
+    if (draft_count > kMaxTokens)
+        return speculative_greedy_replay(m, token_id, stop_token, draft_count, accepted_tokens, accepted_count,
+                                         next_logits);
+    // Up to kMaxTokens drafts (upstream qwen38_model.c:1614-1714, same
+    // accepted tokens): the draft chain runs on the device (each MTP step feeds
+    // its argmax to the next), the target verifies all drafts in one captured
+    // pass that keeps the DeltaNet state after each token, and a mismatch rolls
+    // the state back to the consumed prefix instead of replaying it.  The conv
+    // ring and the KV caches are indexed by position, so the rejected tail is
+    // simply overwritten later.  Drafts past a stop token are verified too but
+    // never accepted.
+    const int n = static_cast<int>(draft_count);
+    const uint32_t base = m->position, mbase = m->mtp_position;
+    const cudaStream_t s = m->stream;
+    if (!build_mtp_draft_graph(m) || !build_verify_graph(m, n)) return 0;
+    m->host_ctl[0] = static_cast<int>(token_id);
+    m->host_ctl[1] = static_cast<int>(mbase);
+    m->host_ctl[2] = 0;
+    m->host_ids[0] = token_id;
+    bool ok = cuda_ok(cudaMemcpyAsync(m->ck_mtp_hidden, m->mtp_hidden, kHidden * sizeof(float),
+                                      cudaMemcpyDeviceToDevice, s),
+                      "checkpoint") &&
+              cuda_ok(cudaMemcpyAsync(m->ctl, m->host_ctl, 3 * sizeof(int), cudaMemcpyHostToDevice, s), "control");
+    for (int i = 0; ok && i < n; ++i) ok = cuda_ok(cudaGraphLaunch(m->mtp_draft_graph, s), "draft graph");
+    // verification inputs: the token, then drafts 0 .. n - 2
+    ok = ok && cuda_ok(cudaMemcpyAsync(m->ids, m->host_ids, sizeof(uint32_t), cudaMemcpyHostToDevice, s), "ids");
+    if (ok && n > 1)
+        ok = cuda_ok(cudaMemcpyAsync(m->ids + 1, m->history, (n - 1) * sizeof(uint32_t), cudaMemcpyDeviceToDevice, s),
+                     "ids");
+    ok = ok && set_ctl(m, token_id, base) && cuda_ok(cudaGraphLaunch(m->verify_graph[n], s), "verify graph");
+    uint32_t *target = m->host_ids, drafts[kMaxTokens];
+    ok = ok &&
+         cuda_ok(cudaMemcpyAsync(target, m->argmax_out, n * sizeof(uint32_t), cudaMemcpyDeviceToHost, s),
+                 "argmax copy") &&
+         // the drafts, through the pinned logits buffer (rewritten below)
+         cuda_ok(cudaMemcpyAsync(m->host_logits, m->history, n * sizeof(uint32_t), cudaMemcpyDeviceToHost, s),
+                 "draft copy") &&
+         check_status(m);
+    if (!ok) {
+        cudaStreamSynchronize(s);
+        return 0;
+    }
+    std::memcpy(drafts, m->host_logits, n * sizeof(uint32_t));
+    uint32_t actual = static_cast<uint32_t>(n);
+    for (uint32_t i = 0; i < actual; ++i)
+        if (drafts[i] == stop_token) actual = i + 1;
+    uint32_t matched = 0;
+    while (matched < actual && target[matched] == drafts[matched]) ++matched;
+    const uint32_t next = matched < actual ? target[matched] : drafts[actual - 1];
+    const uint32_t consumed = matched < actual ? matched + 1 : actual;
+    uint32_t inputs[kMaxTokens];
+    inputs[0] = token_id;
+    for (uint32_t i = 1; i < consumed; ++i) inputs[i] = drafts[i - 1];
+    if (consumed < static_cast<uint32_t>(n))
+        ok = cuda_ok(cudaMemcpyAsync(m->delta_state, m->delta_snap + (consumed - 1) * (delta_state_bytes() / 4),
+                                     delta_state_bytes(), cudaMemcpyDeviceToDevice, s),
+                     "state rollback");
+    ok = ok &&
+         cuda_ok(cudaMemcpyAsync(m->host_logits, m->logits + static_cast<size_t>(consumed - 1) * kVocab,
+                                 static_cast<size_t>(kVocab) * sizeof(float), cudaMemcpyDeviceToHost, s),
+                 "logits copy") &&
+         cuda_ok(cudaMemcpyAsync(m->mtp_hidden, m->ck_mtp_hidden, kHidden * sizeof(float), cudaMemcpyDeviceToDevice, s),
+                 "restore");
+    m->position = base + consumed;
+    m->mtp_position = mbase;
+    ok = ok && mtp_catchup(m, inputs, consumed, mbase);
+    if (!ok) {
+        cudaStreamSynchronize(s);
         return 0;
     }
     for (uint32_t i = 0; i < matched; ++i) accepted_tokens[i] = drafts[i];

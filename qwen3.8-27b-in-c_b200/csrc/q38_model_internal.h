@@ -35,6 +35,10 @@ struct DeltaArgs {
     const float *dt, *a;  // [48]
     const float *norm_w;  // [128]
     float *state;         // [48][128][128], column-major per head
+    // optional: the state after token t (t < tokens - 1) also goes to
+    // snap + t * snap_stride (same layout), for speculative rollback
+    float *snap;
+    long long snap_stride;
     const int *ctl;
     int tokens;
     float *out_f;  // optional [tokens][6144]

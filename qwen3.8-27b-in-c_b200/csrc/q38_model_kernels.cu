@@ -380,6 +380,7 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
     float4 s[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) s[j] = __ldcg(reinterpret_cast<const float4 *>(state + j * 128));
+    const float norm_wc = tid < 32 ? __ldg(a.norm_w + col0 + tid) : 0.0f;  // this lane's column of ssm_norm
     if (tid == 0) prefetch_share_l2(a.pf_ptr, a.pf_bytes);  // keeps HBM busy through this latency-bound step
 
     pdl_wait();
@@ -389,6 +390,8 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
         const int pos = base + t;
         // The conv inputs of q, k (the key head's 128 channels) and v (this
         // CTA's 32 channels) and the hidden row for the fused beta/alpha.
+        // the gate z of this lane's output column, needed after the delta rule
+        const float zc = tid < 32 ? a.qkvz[static_cast<size_t>(t) * a.qkvz_ld + a.z_off + vh * 128 + col0 + tid] : 0.0f;
         const ConvTaps cq = load_taps(a, ch_q, pos, base);
         const ConvTaps ck = load_taps(a, ch_k, pos, base);
         const ConvTaps cv = load_taps(a, ch_v, pos, base);
@@ -459,23 +462,48 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
         const float4 q4 = *reinterpret_cast<const float4 *>(&sh.q[lane * 4]);
         const float decay = sh.decay, beta = sh.beta;
         const float query_scale = __fdiv_rn(1.0f, sqrtf(128.0f));
+        // The 8 columns are independent: their dot products reduce across the
+        // warp together (one shuffle round for all 8), not one column after
+        // another; every column keeps the upstream's arithmetic.
+        float red[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            float4 x = s[j];
+            float4 &x = s[j];
             x.x = __fmul_rn(x.x, decay);
             x.y = __fmul_rn(x.y, decay);
             x.z = __fmul_rn(x.z, decay);
             x.w = __fmul_rn(x.w, decay);
-            const float pred = warp_sum_f(fmaf(x.w, k4.w, fmaf(x.z, k4.z, fmaf(x.y, k4.y, __fmul_rn(x.x, k4.x)))));
-            const int col = warp * 8 + j;
-            const float delta = __fmul_rn(__fsub_rn(sh.v[col], pred), beta);
+            red[j] = fmaf(x.w, k4.w, fmaf(x.z, k4.z, fmaf(x.y, k4.y, __fmul_rn(x.x, k4.x))));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) red[j] = __fadd_rn(red[j], __shfl_xor_sync(0xffffffffu, red[j], o));
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float4 &x = s[j];
+            const float delta = __fmul_rn(__fsub_rn(sh.v[warp * 8 + j], red[j]), beta);
             x.x = fmaf(k4.x, delta, x.x);
             x.y = fmaf(k4.y, delta, x.y);
             x.z = fmaf(k4.z, delta, x.z);
             x.w = fmaf(k4.w, delta, x.w);
-            const float r = warp_sum_f(fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, __fmul_rn(x.x, q4.x)))));
-            s[j] = x;
-            if (lane == 0) sh.o[col] = __fmul_rn(r, query_scale);
+            red[j] = fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, __fmul_rn(x.x, q4.x))));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) red[j] = __fadd_rn(red[j], __shfl_xor_sync(0xffffffffu, red[j], o));
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) sh.o[warp * 8 + j] = __fmul_rn(red[j], query_scale);
+        }
+        if (a.snap && t + 1 < a.tokens) {
+            // the state after this token, kept for a speculative rollback
+            float *snap = a.snap + t * a.snap_stride + (state - a.state);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) *reinterpret_cast<float4 *>(snap + j * 128) = s[j];
         }
         __syncthreads();
         if (t == 0) trace_mark(a.trace, kTraceNormed);  // delta rule done
@@ -490,14 +518,16 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
         cluster.sync();
         if (t == 0) trace_mark(a.trace, kTraceQuantized);  // head norm exchanged
         if (tid < 32) {
-            double sum = 0.0;
-            for (int r = (rank & ~3); r < (rank & ~3) + 4; ++r) sum += cluster.map_shared_rank(&sh, r)->head_part;
+            // the head's 4 partial sums: one remote read per lane, added in rank order
+            const double mine = lane < 4 ? cluster.map_shared_rank(&sh, (rank & ~3) + lane)->head_part : 0.0;
+            double sum = __shfl_sync(0xffffffffu, mine, 0);
+#pragma unroll
+            for (int r = 1; r < 4; ++r) sum += __shfl_sync(0xffffffffu, mine, r);
             const float mean = static_cast<float>(sum / 128.0);
             const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps)));
             const int col = col0 + tid;
-            o = __fmul_rn(__fmul_rn(o, scale), a.norm_w[col]);
-            const float z = a.qkvz[static_cast<size_t>(t) * a.qkvz_ld + a.z_off + vh * 128 + col];
-            o = __fmul_rn(o, silu(z));
+            o = __fmul_rn(__fmul_rn(o, scale), norm_wc);
+            o = __fmul_rn(o, silu(zc));
             if (a.out_f) a.out_f[static_cast<size_t>(t) * 6144 + vh * 128 + col] = o;
             const int e = (rank / 4) * 128 + col;  // index inside the Q8_K block
             AbsMax m = warp_absmax(AbsMax{fabsf(o), e, o});
@@ -506,8 +536,15 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
         cluster.sync();
         if (t == 0) trace_mark(a.trace, kTraceFirstStaged);  // block max exchanged
         if (tid < 32) {
-            AbsMax best = cluster.map_shared_rank(&sh, 0)->block_part;
-            for (int r = 1; r < kDeltaCluster; ++r) best = better(best, cluster.map_shared_rank(&sh, r)->block_part);
+            // the block's 8 partial maxima: one remote read per lane, folded in rank order
+            AbsMax part{0.0f, 0, 0.0f};
+            if (lane < kDeltaCluster) part = cluster.map_shared_rank(&sh, lane)->block_part;
+            AbsMax best{__shfl_sync(0xffffffffu, part.a, 0), __shfl_sync(0xffffffffu, part.i, 0),
+                        __shfl_sync(0xffffffffu, part.v, 0)};
+#pragma unroll
+            for (int r = 1; r < kDeltaCluster; ++r)
+                best = better(best, AbsMax{__shfl_sync(0xffffffffu, part.a, r), __shfl_sync(0xffffffffu, part.i, r),
+                                           __shfl_sync(0xffffffffu, part.v, r)});
             Q8KBlock *dst = static_cast<Q8KBlock *>(a.out_q) + static_cast<size_t>(t) * 24 + cidx;
             int q = 0;
             float inverse = 0.0f;

@@ -127,6 +127,13 @@ struct StreamArgs {
     int32_t *dbg_w;       // optional [tokens][rows][nb]
     int32_t *dbg_x;
     unsigned long long *trace;  // optional launch timeline record
+    // Side rows (RMSNorm input only): CTA c < side_rows also forms the dot
+    // product of Q8_0 row c of side_w (GGUF layout, width nb * 256) with the
+    // normalized floats of each token, as the upstream float path does
+    // (q38_dot_q8_0: fmaf(d * q, x, acc)), into side_out[tok * side_ld + c].
+    const uint8_t *side_w;
+    int side_rows, side_ld;
+    float *side_out;
 };
 
 // Final store of one output row; with `accumulate` the value is added to what
@@ -277,6 +284,20 @@ __device__ __forceinline__ bool preload_norm_weights(const StreamArgs &g, int co
     return true;
 }
 
+// Shared-memory slots of the side rows' per-warp partials: past the RMS sum's
+// doubles in `red`, [token][warp] (red holds consumers * MT floats).
+__device__ __forceinline__ float *side_slots(double *red) { return reinterpret_cast<float *>(red) + 64; }
+
+__device__ __forceinline__ void finish_side_rows(const StreamArgs &g, double *red, int consumers, int tokens)
+{
+    if (!g.side_w || static_cast<int>(blockIdx.x) >= g.side_rows || threadIdx.x >= tokens) return;
+    const int warps = consumers >> 5, tok = threadIdx.x;
+    const float *slot = side_slots(red) + tok * warps;
+    float total = 0.0f;
+    for (int w = 0; w < warps; ++w) total = __fadd_rn(total, slot[w]);
+    g.side_out[static_cast<size_t>(tok) * g.side_ld + blockIdx.x] = total;
+}
+
 template <int MT, int L>
 __device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *red, int consumers,
                                        const float (&wpre)[ActBatch<MT, L>::kValue][8], bool preloaded)
@@ -327,6 +348,21 @@ __device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *r
         // order, then the warp tree, then warps in order), scale, quantize.
         float xv[kActBatch][8], wv[kActBatch][8];
         const bool one_batch = per_warp <= kActBatch;
+        // side row of this CTA: lane l of block b takes Q8_0 block 8b + l / 4,
+        // elements 8 (l % 4) .. + 7, loaded with the activation
+        const bool side = g.side_w && static_cast<int>(blockIdx.x) < g.side_rows;
+        const uint8_t *side_row = side ? g.side_w + static_cast<size_t>(blockIdx.x) * g.nb * 8 * 34 : nullptr;
+        float sd[kActBatch];
+        uint32_t sq[kActBatch][2];
+        auto load_side = [&](int j, int b) {
+            const uint8_t *blk = side_row + static_cast<size_t>(b * 8 + (lane >> 2)) * 34;
+            const unsigned short *h = reinterpret_cast<const unsigned short *>(blk);
+            const unsigned short *qp = reinterpret_cast<const unsigned short *>(blk + 2 + (lane & 3) * 8);
+            sd[j] = __half2float(__ushort_as_half(__ldg(h)));
+            sq[j][0] = static_cast<uint32_t>(__ldg(qp)) | static_cast<uint32_t>(__ldg(qp + 1)) << 16;
+            sq[j][1] = static_cast<uint32_t>(__ldg(qp + 2)) | static_cast<uint32_t>(__ldg(qp + 3)) << 16;
+        };
+        float side_acc = 0.0f;
         double part = 0.0;
         for (int j0 = 0; j0 < per_warp; j0 += kActBatch) {
 #pragma unroll
@@ -334,6 +370,7 @@ __device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *r
                 const int b = warp + (j0 + j) * warps;
                 if (b < g.nb) {
                     load8(x + b * 256 + lane * 8, xv[j]);
+                    if (side && one_batch) load_side(j, b);
                     if (one_batch) {
                         if (preloaded) {
 #pragma unroll
@@ -371,6 +408,7 @@ __device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *r
                     if (b < g.nb) {
                         load8(x + b * 256 + lane * 8, xv[j]);
                         ldg8(act_y + b * 256 + lane * 8, wv[j]);
+                        if (side) load_side(j, b);
                     }
                 }
             }
@@ -383,7 +421,20 @@ __device__ void stage_fused_activation(const StreamArgs &g, Act *acts, double *r
                 for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(xv[j][i], scale), wv[j][i]);
                 store_floats(g, tok, b * 256 + lane * 8, v);
                 store_block(slots[b], v);
+                if (side) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int qv = static_cast<int8_t>((sq[j][i >> 2] >> (8 * (i & 3))) & 0xFFu);
+                        side_acc = fmaf(__fmul_rn(sd[j], static_cast<float>(qv)), v[i], side_acc);
+                    }
+                }
             }
+        }
+        if (side) {
+            // the warp's partial (lane tree); the warps' partials are added in
+            // warp order after staging's closing barrier (finish_side_rows)
+            const float r = act_warp_sum_f(side_acc);
+            if (lane == 0) side_slots(red)[tok * warps + warp] = r;
         }
         if (tok == 0) {
             __syncwarp();
@@ -689,6 +740,7 @@ __global__ void __launch_bounds__(StreamThreads<MT, L>::kValue, 1) stream_gemm_k
     }
     consumer_barrier(consumers);
     for (int slot = tid; slot < slots; slot += consumers) Dec::aux_from_raw(acts[slot]);
+    if (g.act_mode == kActRmsNorm) finish_side_rows(g, reinterpret_cast<double *>(red), consumers, g.tokens);
     consumer_barrier(consumers);
     trace_mark(g.trace, kTraceStaged);
     trace_mark(g.trace, kTraceFirstStaged);
@@ -1060,6 +1112,11 @@ cudaError_t launch_t(const StreamPlan &p, const StreamLaunch &l, cudaStream_t st
     g.dbg_w = l.dbg_w;
     g.dbg_x = l.dbg_x;
     g.trace = l.trace;
+    g.side_w = static_cast<const uint8_t *>(l.side_w);
+    g.side_rows = l.side_w ? l.side_rows : 0;
+    g.side_ld = l.side_ld;
+    g.side_out = l.side_out;
+    if (l.side_w && (l.act_mode != kActRmsNorm || l.side_rows > p.grid)) return cudaErrorInvalidValue;
     const void *kernel = select_kernel<Dec>(p.mt, l.dbg_w != nullptr, p.parts);
     if (!kernel) return cudaErrorInvalidValue;
     cudaError_t e = opt_in(kernel);

@@ -65,7 +65,8 @@ int q38cu_model_step_kernels(Q38Model *model);
 /* Launch timeline of the decode step (profiling; no upstream counterpart, the
  * upstream's closest is its QWEN38_TRACE_LAYERS stderr trace).  Active only
  * when the environment has Q38CU_TRACE=1 at q38_model_open_gguf.  Each kernel
- * of the captured decode graph keeps one record of eleven %globaltimer stamps
+ * of the captured decode graph (and, into the same records, of the
+ * speculative verification graphs) keeps one record of eleven %globaltimer stamps
  * in ns, each the earliest or latest over the kernel's CTAs: earliest start,
  * earliest return from the grid-dependency wait, latest end; for the
  * weight-streaming GEMVs also the latest CTA to finish staging its activation

@@ -93,6 +93,29 @@ struct StreamLaunch {
 
 enum : int { kActQ8K = 0, kActRmsNorm = 1, kActSwiGLU = 2 };
 
+// RMSNorm of `tokens` rows -> Q8_K blocks (q_reps copies), optional floats
+// and optional Q8_0 side rows, computed exactly as a stream GEMV's fused
+// RMSNorm prologue with `warps` consumer warps computes them (see
+// q38_stream.cu); a batch whose Q8_K input comes from here is bit-identical,
+// row for row, to single-token launches with the fused prologue.
+struct RmsPrologue {
+    const float *x;       // [tokens][ld]
+    int ld;
+    const float *w;       // norm weight [width]
+    int width, tokens, warps;
+    void *out_q;          // [tokens][width / 256] Q8_K, q_reps copies q_rep_bytes apart
+    int q_reps;
+    long long q_rep_bytes;
+    float *out_f;         // optional [tokens][f_ld]
+    int f_ld;
+    const void *side_w;   // optional Q8_0 rows [side_rows][width] (GGUF layout)
+    int side_rows, side_ld;
+    float *side_out;      // [tokens][side_ld]
+};
+cudaError_t launch_rms_prologue(const RmsPrologue &a, cudaStream_t s);
+// Consumer warps of a stream GEMV launch of this shape and token count.
+int stream_consumer_warps(const StreamPlan &p);
+
 int stream_tile_rows(int rows);
 cudaError_t stream_plan(int type, int rows, int width, int tile_rows, int tokens, StreamPlan *p);
 cudaError_t launch_stream_gemm(int type, const StreamPlan &p, const StreamLaunch &l, cudaStream_t s);

@@ -139,6 +139,7 @@ struct Q38Model {
     // activations, [kMaxTokens] rows each
     float *hidden = nullptr, *normf = nullptr, *wide = nullptr, *ba = nullptr, *act_f = nullptr, *logits = nullptr;
     void *q8 = nullptr;
+    void *q8_norm = nullptr;  // batched launches: RMSNorm inputs as Q8_K (kReps copies)
     int wide_ld = 0, ba_ld = 0;
     int *ctl = nullptr;  // [0] token, [1] position, [2] history count
     uint32_t *ids = nullptr, *argmax_out = nullptr, *history = nullptr;
@@ -429,6 +430,7 @@ bool alloc_runtime(Q38Model *m)
            dalloc(&m->ba, kMaxTokens * m->ba_ld, o) && dalloc(&m->act_f, kMaxTokens * kFfn, o) &&
            dalloc(&m->logits, kMaxTokens * static_cast<size_t>(kVocab), o) &&
            dalloc(reinterpret_cast<uint8_t **>(&m->q8), kReps * q8_blocks * sizeof(Q38CuQ8KBlock), o) &&
+           dalloc(reinterpret_cast<uint8_t **>(&m->q8_norm), kReps * q8_blocks * sizeof(Q38CuQ8KBlock), o) &&
            dalloc(&m->target_norm, kMaxDrafts * static_cast<size_t>(kHidden), o) &&
            dalloc(&m->ctl, 4, o) && dalloc(&m->ids, kMaxTokens, o) && dalloc(&m->argmax_out, kMaxDrafts, o) &&
            dalloc(&m->history, ctx + 1, o) &&
@@ -610,6 +612,8 @@ bool has_float_part(const Proj &p)
 // out[tok * out_ld + part.offset + row] (+)= projection of this token's input.
 // A fused input that a float-path part cannot take is materialized first
 // (RMSNorm / SwiGLU kernels into the float rows and m->q8).
+bool batch_rmsnorm_input(Q38Model *m, const Part &part, const ActIn &in, int tokens, ActIn *out);
+
 bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int out_ld, int accumulate,
              const OutReps &orep = OutReps(), const Part *next_after = nullptr)
 {
@@ -635,6 +639,8 @@ bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int o
         if (part.int_path) {
             ActIn pin = in;
             if (i > 0) pin.side_w = nullptr;  // side rows come with the first launch only
+            if (pin.mode == q38::kActRmsNorm && tokens > 1 && !batch_rmsnorm_input(m, part, pin, tokens, &pin))
+                return false;
             if (!stream_project(part, pin, tokens, out + part.offset, out_ld, accumulate, orep, prefetch_of(next), s,
                                 nullptr, m))
                 return false;
@@ -669,6 +675,44 @@ ActIn q8_input(const void *q8, const float *f, int f_ld, bool replicated = false
         in.rep_bytes = q8_rep_bytes();
     }
     return in;
+}
+
+// A batch (more than one token) with an RMSNorm input takes it as Q8_K from
+// the prologue kernel (q38_stream.cu: rms_prologue_kernel) rather than from
+// the GEMV's fused prologue, which would normalize and quantize the tokens one
+// after another in every CTA.  The kernel runs with the warp count of the
+// single-token launch of `part`, so every token's input - and so its output
+// row - is bit-identical to what a single-token launch computes; side rows
+// (beta | alpha) come with it.
+bool batch_rmsnorm_input(Q38Model *m, const Part &part, const ActIn &in, int tokens, ActIn *out)
+{
+    const int width = static_cast<int>(part.t.shape[0]);
+    q38::StreamPlan one;
+    if (!cuda_ok(q38::stream_plan(static_cast<int>(part.t.type), part.rows, width, static_cast<int>(part.t.tile_rows),
+                                  1, &one),
+                 "stream plan"))
+        return false;
+    q38::RmsPrologue a{};
+    a.x = in.x;
+    a.ld = in.ld;
+    a.w = in.y;
+    a.width = width;
+    a.tokens = tokens;
+    a.warps = q38::stream_consumer_warps(one);
+    a.out_q = m->q8_norm;
+    a.q_reps = kReps;
+    a.q_rep_bytes = q8_rep_bytes();
+    a.out_f = in.f_out;
+    a.f_ld = width;
+    if (in.side_w) {
+        a.side_w = in.side_w;
+        a.side_rows = in.side_rows;
+        a.side_ld = in.side_ld;
+        a.side_out = in.side_out;
+    }
+    if (!cuda_ok(q38::launch_rms_prologue(a, m->stream), "rms prologue")) return false;
+    *out = q8_input(m->q8_norm, in.f_out, width, true);
+    return true;
 }
 
 // RMSNorm(hidden rows) * weight, both replicated.
@@ -820,8 +864,10 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         sw.counters = m->swiglu_counters;
         sw.reps = kReps;
         sw.rep_bytes = q8_rep_bytes();
-        if (!stream_project(L.gate_up.parts[0], rmsnorm_input(m->hidden, L.post_norm), tokens, nullptr, 0, 0,
-                            OutReps(), prefetch_of(first_part(L.down)), s, &sw, m))
+        ActIn gin = rmsnorm_input(m->hidden, L.post_norm);
+        if (tokens > 1 && !batch_rmsnorm_input(m, L.gate_up.parts[0], gin, tokens, &gin)) return false;
+        if (!stream_project(L.gate_up.parts[0], gin, tokens, nullptr, 0, 0, OutReps(), prefetch_of(first_part(L.down)),
+                            s, &sw, m))
             return false;
         return project(m, L.down, q8_input(m->q8, m->act_f, kFfn, true), tokens, m->hidden, kHidden, 1,
                        hidden_out(), after);
@@ -1098,11 +1144,17 @@ bool build_mtp_draft_graph(Q38Model *m)
 bool build_verify_graph(Q38Model *m, int n)
 {
     return capture_graph(m, &m->verify_graph[n], [&] {
+        // traced like the decode step (the same records; read them after
+        // speculative calls only)
         m->snapping = true;
+        m->trace_slots = 0;
+        m->tracing = m->trace != nullptr;
         bool ok = enqueue_embed(m, m->embedding, m->ids, n, m->hidden);
         for (int l = 0; ok && l < kLayers; ++l) ok = enqueue_layer(m, l, n, 0);
         m->snapping = false;
-        return ok && enqueue_head(m, m->output_norm, m->output, n, m->target_norm, 0, false, 0);
+        ok = ok && enqueue_head(m, m->output_norm, m->output, n, m->target_norm, 0, false, 0);
+        m->tracing = false;
+        return ok;
     });
 }
 

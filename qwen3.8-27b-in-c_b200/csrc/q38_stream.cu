@@ -59,7 +59,7 @@ __device__ int g_stream_status;  // status word of this file's kernels
 
 constexpr int kStreamMaxStages = 32;            // stages of all groups together
 constexpr size_t kChunkBudget = 112 * 1024;     // one ring pass of all groups (sets the chunk)
-constexpr size_t kActBudget = 64 * 1024;        // shared memory for activation columns
+constexpr size_t kActBudget = 96 * 1024;        // shared memory for activation columns
 constexpr int kMaxConsumers = 256;              // CTA bound for 8 tokens: 288 threads
 constexpr size_t kOverlapSmem = 112 * 1024;     // short launches: two CTAs fit an SM
 constexpr size_t kLongLaunchBytes = 2u << 20;   // per-CTA bytes above which a launch is long
@@ -1159,6 +1159,107 @@ cudaError_t stream_plan(int type, int rows, int width, int tile_rows, int tokens
     default: return cudaErrorInvalidValue;
     }
 }
+
+// The fused RMSNorm prologue of stage_fused_activation, as a kernel of its
+// own: CTA (0, t) forms token t's Q8_K blocks and floats, CTA (1 + r, t) the
+// side row r.  Warp w takes blocks w, w + warps, ... and lane l elements
+// 8l .. 8l + 7 of each; every sum runs in the prologue's order.
+__global__ void __launch_bounds__(1024) rms_prologue_kernel(RmsPrologue a)
+{
+    __shared__ double red_d[32];
+    __shared__ float red_f[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    const int tok = blockIdx.y, nb = a.width / 256;
+    const int per_warp = (nb + warps - 1) / warps;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const float *x = a.x + static_cast<size_t>(tok) * a.ld;
+    double part = 0.0;
+    for (int j = 0; j < per_warp; ++j) {
+        const int b = warp + j * warps;
+        if (b >= nb) break;
+        float xv[8];
+        load8(x + b * 256 + lane * 8, xv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) part += static_cast<double>(__fmul_rn(xv[i], xv[i]));
+    }
+    part = act_warp_sum_d(part);
+    if (lane == 0) red_d[warp] = part;
+    __syncthreads();
+    double sum = 0.0;
+    for (int w = 0; w < warps; ++w) sum += red_d[w];
+    const float mean = static_cast<float>(sum / static_cast<double>(nb * 256));
+    const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps)));
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int row = static_cast<int>(blockIdx.x) - 1;
+    const uint8_t *side_row = row >= 0 ? static_cast<const uint8_t *>(a.side_w) + static_cast<size_t>(row) * nb * 8 * 34
+                                       : nullptr;
+    float side_acc = 0.0f;
+    for (int j = 0; j < per_warp; ++j) {
+        const int b = warp + j * warps;
+        if (b >= nb) break;
+        float xv[8], wv[8], v[8];
+        load8(x + b * 256 + lane * 8, xv);
+        ldg8(a.w + b * 256 + lane * 8, wv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(xv[i], scale), wv[i]);
+        if (row < 0) {
+            if (a.out_f) {
+                float *o = a.out_f + static_cast<size_t>(tok) * a.f_ld + b * 256 + lane * 8;
+                *reinterpret_cast<float4 *>(o) = make_float4(v[0], v[1], v[2], v[3]);
+                *reinterpret_cast<float4 *>(o + 4) = make_float4(v[4], v[5], v[6], v[7]);
+            }
+            const WarpQ8K r = act_quantize_warp(v);
+            for (int k = 0; k < a.q_reps; ++k) {
+                Q8KBlock *d = reinterpret_cast<Q8KBlock *>(static_cast<char *>(a.out_q) + k * a.q_rep_bytes) +
+                              static_cast<size_t>(tok) * nb + b;
+                uint32_t *q = reinterpret_cast<uint32_t *>(d->quants);
+                q[lane * 2] = r.q0;
+                q[lane * 2 + 1] = r.q1;
+                if ((lane & 3) == 0) reinterpret_cast<uint32_t *>(d->sums)[lane >> 2] = r.sums_word;
+                if (lane == 0) d->scale = r.scale;
+            }
+        } else {
+            const uint8_t *blk = side_row + static_cast<size_t>(b * 8 + (lane >> 2)) * 34;
+            const unsigned short *h = reinterpret_cast<const unsigned short *>(blk);
+            const unsigned short *qp = reinterpret_cast<const unsigned short *>(blk + 2 + (lane & 3) * 8);
+            const float sd = __half2float(__ushort_as_half(__ldg(h)));
+            const uint32_t sq[2] = {static_cast<uint32_t>(__ldg(qp)) | static_cast<uint32_t>(__ldg(qp + 1)) << 16,
+                                    static_cast<uint32_t>(__ldg(qp + 2)) | static_cast<uint32_t>(__ldg(qp + 3)) << 16};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int qv = static_cast<int8_t>((sq[i >> 2] >> (8 * (i & 3))) & 0xFFu);
+                side_acc = fmaf(__fmul_rn(sd, static_cast<float>(qv)), v[i], side_acc);
+            }
+        }
+    }
+    if (row < 0) return;
+    const float r = act_warp_sum_f(side_acc);
+    if (lane == 0) red_f[warp] = r;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float total = 0.0f;
+        for (int w = 0; w < warps; ++w) total = __fadd_rn(total, red_f[w]);
+        a.side_out[static_cast<size_t>(tok) * a.side_ld + row] = total;
+    }
+}
+
+cudaError_t launch_rms_prologue(const RmsPrologue &a, cudaStream_t s)
+{
+    if (a.width % 256 || a.tokens < 1 || a.warps < 1 || a.warps > 32 || a.q_reps < 1 || (a.side_w && !a.side_out))
+        return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1 + (a.side_w ? a.side_rows : 0), a.tokens);
+    cfg.blockDim = dim3(a.warps * 32);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, rms_prologue_kernel, a);
+}
+
+int stream_consumer_warps(const StreamPlan &p) { return (p.threads - 32) / 32; }
 
 cudaError_t launch_stream_gemm(int type, const StreamPlan &p, const StreamLaunch &l, cudaStream_t s)
 {

@@ -433,6 +433,22 @@ def run_decode(args, rank, world, dist):
         end.synchronize()
         return start.elapsed_time(end), out
 
+    if args.profile:
+        # For ncu (--profile-from-start off): W warm steps, then exactly one
+        # decode step (one graph replay) between profiler start and stop.
+        token = fresh()
+        token = m.generate_greedy(token, args.warmup)[-1]
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        m.generate_greedy(token, 1)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        m.close()
+        if rank == 0:
+            print(json.dumps({"profile_run": DECODE_WORKLOAD, "profiled_steps": 1, "kernels_per_step": kernels}),
+                  flush=True)
+        return
+
     # W untimed warm-up steps, then exactly K timed steps in runs that fit the
     # context (a reset and a fresh prefill between runs are not timed).
     token = fresh()
@@ -483,22 +499,32 @@ def run_decode(args, rank, world, dist):
         dist.all_reduce(t2, op=dist.ReduceOp.MAX)
     e2e_value = e2e_steps * world / (float(t2.item()) / 1e3)
 
-    # MTP on: speculative greedy decoding with 3 drafts per call.
-    m.reset()
-    m.enable_mtp()
-    token = int(np.argmax(m.prefill(prompt)))
-    drafts, target = 3, 48
+    # MTP on: speculative greedy decoding at draft depths 1 and 3 (the
+    # upstream's spec bench sweeps depths 1..4, qwen38_spec_bench.c:108-119).
+    mtp = {}
+    for drafts in (1, 3):
+        m.reset()
+        m.enable_mtp()
+        token = int(np.argmax(m.prefill(prompt)))
+        m.speculative_greedy(token, 0xFFFFFFFF, drafts)  # captures the draft and verification graphs
+        m.reset()
+        m.enable_mtp()
+        token = int(np.argmax(m.prefill(prompt)))
+        target = 48
 
-    def spec_loop():
-        tok, produced, calls = token, 0, 0
-        while produced < target:
-            accepted, _ = m.speculative_greedy(tok, 0xFFFFFFFF, drafts)
-            produced += len(accepted)
-            calls += 1
-            tok = accepted[-1]
-        return produced, calls
+        def spec_loop():
+            tok, produced, calls = token, 0, 0
+            while produced < target:
+                accepted, _ = m.speculative_greedy(tok, 0xFFFFFFFF, drafts)
+                produced += len(accepted)
+                calls += 1
+                tok = accepted[-1]
+            return produced, calls
 
-    mtp_ms, (produced, calls) = timed(spec_loop)
+        mtp_ms, (produced, calls) = timed(spec_loop)
+        mtp[f"depth_{drafts}"] = {"value": produced * world / (mtp_ms / 1e3), "unit": DECODE_UNIT,
+                                  "draft_count": drafts, "tokens": produced, "calls": calls,
+                                  "tokens_per_call": produced / calls, "ms_per_call": mtp_ms / calls}
     m.close()
 
     if rank != 0:
@@ -520,9 +546,8 @@ def run_decode(args, rank, world, dist):
                      "timing": "CUDA events on the model stream around K graph replays"},
         "e2e": {"value": e2e_value, "unit": DECODE_UNIT, "steps": e2e_steps, "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": VOCAB * 4, "api": "q38_model_forward_token + host argmax"},
-        "mtp": {"value": produced * world / (mtp_ms / 1e3), "unit": DECODE_UNIT, "draft_count": drafts,
-                "tokens": produced, "calls": calls, "tokens_per_call": produced / calls,
-                "note": "random-weight MTP head: drafts are almost never accepted"},
+        "mtp": dict(mtp, note="random-weight MTP head: drafts are almost never accepted, so each call yields "
+                              "one token and costs the drafts plus a verification of depth tokens"),
         "gpu_launches": kernels * args.steps,
         "kernels_per_step": kernels,
         "clocks": clocks.summary(),
@@ -540,7 +565,8 @@ def main():
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--workload", choices=("decode", "matvec"), default="decode")
     parser.add_argument("--profile", action="store_true",
-                        help="matvec workload: plain launches only (for ncu captures); prints no bench line")
+                        help="plain launches only, for ncu: matvec - warmup + steps launches; decode - one decode "
+                             "step between cudaProfilerStart/Stop; prints no bench line")
     args = parser.parse_args()
     decode = args.workload == "decode"
     if args.steps is None:

@@ -57,6 +57,14 @@ namespace q38 {
 
 __device__ int g_stream_status;  // status word of this file's kernels
 
+#ifndef Q38_STREAM_COLUMNS_IN_FLIGHT
+#define Q38_STREAM_COLUMNS_IN_FLIGHT 1
+#endif
+// Superblock columns a thread decodes at once (1 or 2): two give independent
+// dependency chains, one keeps the decode loop's code smaller - measured
+// slightly faster on B200 (instruction fetch is the kernel's top stall
+// reason), so one is the default.  Results are the same either way.
+constexpr int kColumnsInFlight = Q38_STREAM_COLUMNS_IN_FLIGHT;
 constexpr int kStreamMaxStages = 32;            // stages of all groups together
 constexpr size_t kChunkBudget = 112 * 1024;     // one ring pass of all groups (sets the chunk)
 constexpr size_t kActBudget = 96 * 1024;        // shared memory for activation columns
@@ -784,7 +792,7 @@ __global__ void __launch_bounds__(StreamThreads<MT, L>::kValue, 1) stream_gemm_k
                             decode_column_part<Dec, MT, L, kDbg>(g, base + k * unit_bytes, acts, w.b + k, row, acc,
                                                                  part, part_mask);
                     }
-                    if constexpr (MT <= 2 && !kDbg && L == 1) {
+                    if constexpr (MT <= 2 && !kDbg && L == 1 && kColumnsInFlight == 2) {
                         // two columns in flight: independent decode chains,
                         // the earlier column still added first
                         for (; k + 1 < n; k += 2) {

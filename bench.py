@@ -21,7 +21,8 @@ token fed back on the device.
   mtp     speculative decoding (q38_model_speculative_greedy) on the same model.
 
 --workload matvec: one Q4_K x Q8_K matvec 17408 x 5120,
-value in GB/s of algorithmic bytes, weights rotating over distinct copies.
+value in GB/s of algorithmic bytes, weights rotating over distinct copies;
+--qtype IQ1_M / IQ2_S (and --shape 5120x17408) give BASELINE config 1.
 
 `--impl reference` times the upstream engine's own CPU implementation of the
 workload (built from its sources into oracle/_ref/) on this host's cores.
@@ -44,15 +45,31 @@ METRIC = "decode tok/s (Q4_K_M, bs1, MTP on/off); quant matvec HBM GB/s vs 8 TB/
 UNIT = "GB/s"        # matvec workload
 DECODE_UNIT = "tok/s"
 Q4_K = 12
+# The matvec case (set_matvec_case): BASELINE config 0 by default, config 1
+# with --qtype IQ1_M / IQ2_S (IQ2_M's main type) and either shape.
+QTYPE = Q4_K
 ROWS, WIDTH = 17408, 5120
-ROW_BYTES = WIDTH // 256 * 144
-W_BYTES = ROWS * ROW_BYTES                      # 50,135,040
-X_BYTES = WIDTH // 256 * 292                    # Q8_K activation, 5,840
-Y_BYTES = ROWS * 4                              # 69,632
-STEP_BYTES = W_BYTES + X_BYTES + Y_BYTES        # algorithmic bytes per matvec
-COPIES = 8                                      # 401 MB of weights > 126 MB L2
+W_BYTES = X_BYTES = Y_BYTES = STEP_BYTES = 0
+COPIES = 8                                      # >= 139 MB of weights > 126 MB L2
 NOMINAL_HBM_GBS = 8000.0
-WORKLOAD = "config0: Q4_K 17408x5120 x Q8_K matvec, bs1"
+WORKLOAD = ""
+MATVEC_TYPES = {"Q4_K": 12, "Q6_K": 14, "IQ1_S": 19, "IQ2_S": 28, "IQ1_M": 29}
+
+
+def set_matvec_case(qtype_name="Q4_K", shape="17408x5120"):
+    """Weight type and [rows x width] of the matvec workload; the algorithmic
+    bytes are the GGUF weight bytes, the Q8_K activation and the fp32 output."""
+    global QTYPE, ROWS, WIDTH, W_BYTES, X_BYTES, Y_BYTES, STEP_BYTES, WORKLOAD
+    from q38b200 import synth
+    QTYPE = MATVEC_TYPES[qtype_name]
+    ROWS, WIDTH = (int(v) for v in shape.split("x"))
+    elements, nbytes = synth.BLOCK[QTYPE]
+    W_BYTES = ROWS * (WIDTH // elements) * nbytes       # Q4_K 17408x5120: 50,135,040
+    X_BYTES = WIDTH // 256 * 292                         # Q8_K activation
+    Y_BYTES = ROWS * 4
+    STEP_BYTES = W_BYTES + X_BYTES + Y_BYTES
+    config = "config0" if QTYPE == Q4_K else "config1"
+    WORKLOAD = f"{config}: {qtype_name} {ROWS}x{WIDTH} x Q8_K matvec, bs1"
 
 
 def measured_peaks():
@@ -67,7 +84,7 @@ def measured_peaks():
 def read_traffic():
     """DRAM bytes per launch from the committed ncu summary, if present."""
     path = os.path.join(ROOT, "profiles", "q4k_gemv_17408x5120.md")
-    if not os.path.exists(path):
+    if QTYPE != Q4_K or (ROWS, WIDTH) != (17408, 5120) or not os.path.exists(path):
         return None
     for line in open(path):
         if line.startswith("dram_bytes_per_launch:"):
@@ -137,7 +154,7 @@ def cpu_reference_gemv(seconds=3.0, min_calls=20):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     from q38b200 import synth
-    weights = synth.quant_tensor(Q4_K, ROWS, WIDTH, seed=0)
+    weights = synth.quant_tensor(QTYPE, ROWS, WIDTH, seed=0)
     x = synth.activations(1, WIDTH, seed=1)
     copies = [weights] + [weights.copy() for _ in range(COPIES - 1)]
     if O.reference_available():
@@ -153,14 +170,14 @@ def cpu_reference_gemv(seconds=3.0, min_calls=20):
     while (time.perf_counter() - start < seconds or len(times) < min_calls) and len(times) < 10000:
         w = copies[i % COPIES]
         t0 = time.perf_counter()
-        impl.gemm_q8_k(Q4_K, w, ROWS, WIDTH, q8k)
+        impl.gemm_q8_k(QTYPE, w, ROWS, WIDTH, q8k)
         times.append(time.perf_counter() - t0)
         i += 1
         if kind == "port" and time.perf_counter() - start > seconds:
             break
     med = statistics.median(times)
     return {"value": STEP_BYTES / med / 1e9, "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{len(times)} full 17408x5120 Q4_K matvecs rotating {COPIES} weight copies; "
+            "sample": f"{len(times)} full {WORKLOAD.split(': ')[1].split(' x')[0]} matvecs rotating {COPIES} weight copies; "
                       f"median {med * 1e3:.3f} ms"}
 
 
@@ -194,9 +211,9 @@ def run_matvec(args, rank, world, dist):
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    weights = synth.quant_tensor(Q4_K, ROWS, WIDTH, seed=0)
+    weights = synth.quant_tensor(QTYPE, ROWS, WIDTH, seed=0)
     x_host = synth.activations(1, WIDTH, seed=1)
-    tensors = [q38.DeviceTensor(Q4_K, WIDTH, ROWS, weights, layout=q38.LAYOUT_TILED)
+    tensors = [q38.DeviceTensor(QTYPE, WIDTH, ROWS, weights, layout=q38.LAYOUT_TILED)
                for _ in range(COPIES)]
     x_dev = torch.from_numpy(x_host).cuda()
     act = q38.quantize_q8_k(x_dev)
@@ -564,10 +581,15 @@ def main():
     parser.add_argument("--warmup", type=int, default=None)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--workload", choices=("decode", "matvec"), default="decode")
+    parser.add_argument("--qtype", choices=sorted(MATVEC_TYPES), default="Q4_K",
+                        help="matvec workload: weight type (IQ1_M and IQ2_S give BASELINE config 1)")
+    parser.add_argument("--shape", choices=("17408x5120", "5120x17408"), default="17408x5120",
+                        help="matvec workload: rows x width")
     parser.add_argument("--profile", action="store_true",
                         help="plain launches only, for ncu: matvec - warmup + steps launches; decode - one decode "
                              "step between cudaProfilerStart/Stop; prints no bench line")
     args = parser.parse_args()
+    set_matvec_case(args.qtype, args.shape)
     decode = args.workload == "decode"
     if args.steps is None:
         args.steps = 256 if decode else 20000

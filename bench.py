@@ -53,7 +53,7 @@ W_BYTES = X_BYTES = Y_BYTES = STEP_BYTES = 0
 COPIES = 8                                      # >= 139 MB of weights > 126 MB L2
 NOMINAL_HBM_GBS = 8000.0
 WORKLOAD = ""
-MATVEC_TYPES = {"Q4_K": 12, "Q6_K": 14, "IQ1_S": 19, "IQ2_S": 28, "IQ1_M": 29}
+MATVEC_TYPES = {"Q4_K": 12, "Q6_K": 14, "IQ1_S": 19, "IQ2_S": 22, "IQ1_M": 29}
 
 
 def set_matvec_case(qtype_name="Q4_K", shape="17408x5120"):

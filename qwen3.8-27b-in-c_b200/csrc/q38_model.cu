@@ -475,10 +475,12 @@ struct OutReps {
 };
 
 // L2 prefetch of the weights streamed next (see q38_stream.cu): a GEMV's
-// producer, once its last bulk copy is issued, prefetches the first
-// Q38CU_PREFETCH_KB (default 256) KiB of each of the next GEMV's CTA ranges;
-// the latency-bound mixer kernels prefetch the first Q38CU_MIXER_PREFETCH_MB
-// (default 32) MiB of the projection that follows them.  0 disables either.
+// producer, once its last bulk copy is issued, may prefetch the first
+// Q38CU_PREFETCH_KB KiB of each of the next GEMV's CTA ranges, and the
+// latency-bound mixer kernels the first Q38CU_MIXER_PREFETCH_MB MiB of the
+// projection that follows them.  Both default to 0 (off): measured on B200,
+// the decode step is faster without them (the consumers, not HBM, limit the
+// launches they would feed).
 struct Prefetch {
     const Part *next = nullptr;
 };
@@ -499,7 +501,7 @@ Prefetch prefetch_of(const Part *p)
 // The launch fields of a GEMV's prefetch of `pf.next`.
 void set_next_prefetch(q38::StreamLaunch &l, const Prefetch &pf)
 {
-    static const long long per_cta = env_bytes("Q38CU_PREFETCH_KB", 256, 10);
+    static const long long per_cta = env_bytes("Q38CU_PREFETCH_KB", 0, 10);
     if (!pf.next || per_cta <= 0) return;
     const Part &n = *pf.next;
     q38::StreamPlan plan;
@@ -516,7 +518,7 @@ void set_next_prefetch(q38::StreamLaunch &l, const Prefetch &pf)
 // The contiguous prefetch a mixer kernel issues: the leading bytes of `p`.
 void mixer_prefetch(const Part *p, const void **ptr, long long *bytes)
 {
-    static const long long limit = env_bytes("Q38CU_MIXER_PREFETCH_MB", 32, 20);
+    static const long long limit = env_bytes("Q38CU_MIXER_PREFETCH_MB", 0, 20);
     *ptr = nullptr;
     *bytes = 0;
     if (!p || limit <= 0) return;

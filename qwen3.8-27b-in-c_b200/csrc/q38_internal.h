@@ -89,6 +89,11 @@ struct StreamLaunch {
     const void *side_w = nullptr;
     int side_rows = 0, side_ld = 0;
     float *side_out = nullptr;
+    // optional: the staged activation exported as Q8_K [tokens][width / 256],
+    // export_reps copies export_rep_bytes apart (see q38_stream.cu)
+    void *act_export = nullptr;
+    int export_reps = 1;
+    long long export_rep_bytes = 0;
 };
 
 enum : int { kActQ8K = 0, kActRmsNorm = 1, kActSwiGLU = 2 };

@@ -551,7 +551,7 @@ struct SwigluOut {
 
 bool stream_project(const Part &p, const ActIn &in, int tokens, float *out, int out_ld, int accumulate,
                     const OutReps &orep, const Prefetch &pf, cudaStream_t s, const SwigluOut *sw = nullptr,
-                    Q38Model *tm = nullptr)
+                    Q38Model *tm = nullptr, void *export_q8 = nullptr)
 {
     const int width = static_cast<int>(p.t.shape[0]), nb = width / 256;
     for (int tok0 = 0; tok0 < tokens;) {
@@ -577,6 +577,11 @@ bool stream_project(const Part &p, const ActIn &in, int tokens, float *out, int 
         l.out_rep_bytes = orep.bytes;
         if (tok0 + plan.token_group >= tokens) set_next_prefetch(l, pf);
         if (tm) l.trace = next_trace(tm);
+        if (export_q8) {
+            l.act_export = static_cast<Q38CuQ8KBlock *>(export_q8) + static_cast<size_t>(tok0) * nb;
+            l.export_reps = kReps;
+            l.export_rep_bytes = q8_rep_bytes();
+        }
         if (in.side_w) {
             l.side_w = in.side_w;
             l.side_rows = in.side_rows;
@@ -615,6 +620,7 @@ bool has_float_part(const Proj &p)
 // A fused input that a float-path part cannot take is materialized first
 // (RMSNorm / SwiGLU kernels into the float rows and m->q8).
 bool batch_rmsnorm_input(Q38Model *m, const Part &part, const ActIn &in, int tokens, ActIn *out);
+ActIn q8_input(const void *q8, const float *f, int f_ld, bool replicated);
 
 bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int out_ld, int accumulate,
              const OutReps &orep = OutReps(), const Part *next_after = nullptr)
@@ -634,6 +640,12 @@ bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int o
         in.f = f;
         in.f_ld = width;
     }
+    // Several integer-path parts on one RMSNorm input (attn_q|attn_k and
+    // attn_v) normalize it once: the first part's launch exports its Q8_K input
+    // (a batch: one prologue kernel with the first part's warp count) and the
+    // other parts stage that.
+    const bool share = in.mode == q38::kActRmsNorm && p.parts.size() > 1 && !has_float_part(p);
+    if (share && tokens > 1 && !batch_rmsnorm_input(m, p.parts[0], in, tokens, &in)) return false;
     bool float_part = false;
     for (size_t i = 0; i < p.parts.size(); ++i) {
         const Part &part = p.parts[i];
@@ -641,10 +653,12 @@ bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int o
         if (part.int_path) {
             ActIn pin = in;
             if (i > 0) pin.side_w = nullptr;  // side rows come with the first launch only
+            if (share && i > 0) pin = q8_input(m->q8_norm, in.f_out, width, true);
             if (pin.mode == q38::kActRmsNorm && tokens > 1 && !batch_rmsnorm_input(m, part, pin, tokens, &pin))
                 return false;
+            const bool exporting = share && i == 0 && pin.mode == q38::kActRmsNorm;
             if (!stream_project(part, pin, tokens, out + part.offset, out_ld, accumulate, orep, prefetch_of(next), s,
-                                nullptr, m))
+                                nullptr, m, exporting ? m->q8_norm : nullptr))
                 return false;
         } else {
             float_part = true;

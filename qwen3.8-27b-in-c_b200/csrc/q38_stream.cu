@@ -142,6 +142,12 @@ struct StreamArgs {
     const uint8_t *side_w;
     int side_rows, side_ld;
     float *side_out;
+    // Optional export of the staged activation as Q8_K blocks [tokens][nb]:
+    // CTA c < export_reps writes copy c (export_rep_bytes apart), so a later
+    // launch on the same input stages it instead of normalizing it again.
+    Q8KBlock *act_export;
+    int export_reps;
+    long long export_rep_bytes;
 };
 
 // Final store of one output row; with `accumulate` the value is added to what
@@ -750,6 +756,18 @@ __global__ void __launch_bounds__(StreamThreads<MT, L>::kValue, 1) stream_gemm_k
     for (int slot = tid; slot < slots; slot += consumers) Dec::aux_from_raw(acts[slot]);
     if (g.act_mode == kActRmsNorm) finish_side_rows(g, reinterpret_cast<double *>(red), consumers, g.tokens);
     consumer_barrier(consumers);
+    if (g.act_export && static_cast<int>(blockIdx.x) < g.export_reps) {
+        // scale, 64 quant words and the 8 raw bsum words (aux[8..15]) of each slot
+        Q8KBlock *dst = reinterpret_cast<Q8KBlock *>(reinterpret_cast<char *>(g.act_export) +
+                                                     blockIdx.x * g.export_rep_bytes);
+        const int words = g.tokens * g.nb * 73;
+        for (int i = tid; i < words; i += consumers) {
+            const int slot = i / 73, w = i - slot * 73;
+            uint32_t *d = reinterpret_cast<uint32_t *>(dst + slot);
+            const Act &a = acts[slot];
+            d[w] = w == 0 ? __float_as_uint(a.xs) : w <= 64 ? a.q[w - 1] : a.aux[8 + (w - 65)];
+        }
+    }
     trace_mark(g.trace, kTraceStaged);
     trace_mark(g.trace, kTraceFirstStaged);
     // Only now let the next kernel in the stream launch and start its weight
@@ -1124,6 +1142,10 @@ cudaError_t launch_t(const StreamPlan &p, const StreamLaunch &l, cudaStream_t st
     g.side_rows = l.side_w ? l.side_rows : 0;
     g.side_ld = l.side_ld;
     g.side_out = l.side_out;
+    g.act_export = static_cast<Q8KBlock *>(l.act_export);
+    g.export_reps = l.act_export ? std::max(1, l.export_reps) : 0;
+    g.export_rep_bytes = l.export_rep_bytes;
+    if (l.act_export && g.export_reps > p.grid) return cudaErrorInvalidValue;
     if (l.side_w && (l.act_mode != kActRmsNorm || l.side_rows > p.grid)) return cudaErrorInvalidValue;
     const void *kernel = select_kernel<Dec>(p.mt, l.dbg_w != nullptr, p.parts);
     if (!kernel) return cudaErrorInvalidValue;

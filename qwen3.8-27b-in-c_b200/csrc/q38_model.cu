@@ -211,6 +211,21 @@ bool ensure_staging(Q38Model *m, size_t bytes)
 // Upload a group of tensors that share the input width.  Consecutive members
 // of one type on the Q8_K integer path are concatenated into one tiled tensor;
 // float-path members of one type into one GGUF-layout tensor.
+// Tile height of a tiled projection, by shape (measured on the decode step):
+// large projections (64 or more rows per SM) take whole warps per tile,
+// rounded up (fewer, fuller CTAs: qkvz 16,384 rows -> 128); the 5120-row
+// projections of the 6144-wide mixer output take 64 (80 CTAs: the next
+// gate|up launch starts early on the SMs left free); the others the library's
+// choice (ffn_down 40, attn_v 8).
+uint32_t tile_rows_for(uint64_t rows, uint64_t width)
+{
+    const uint64_t sms = static_cast<uint64_t>(q38::device_sm_count());
+    const uint64_t per_sm = (rows + sms - 1) / sms;
+    if (per_sm >= 64) return static_cast<uint32_t>(std::min<uint64_t>(256, (per_sm + 31) / 32 * 32));
+    if (rows == kHidden && width == kLinV) return 64;
+    return 0;
+}
+
 bool upload_proj(Q38Model *m, Proj *p, const std::vector<const q38::GGUFTensorInfo *> &members)
 {
     p->parts.clear();
@@ -251,7 +266,10 @@ bool upload_proj(Q38Model *m, Proj *p, const std::vector<const q38::GGUFTensorIn
         part.rows = static_cast<int>(rows);
         part.offset = p->rows;
         if (int_path) {
-            if (!q38cu_tensor_repack(&part.t, &src, m->stream)) return fail("%s", q38cu_last_error());
+            const uint32_t tile = tile_rows_for(rows, src.shape[0]);
+            const bool ok = tile ? q38::repack_tiled_with(&part.t, &src, tile, m->stream) != 0
+                                 : q38cu_tensor_repack(&part.t, &src, m->stream) != 0;
+            if (!ok) return fail("%s", q38cu_last_error());
         } else {
             void *dev = nullptr;
             if (!cuda_ok(cudaMalloc(&dev, bytes + 256), "cudaMalloc")) return false;

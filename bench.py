@@ -53,7 +53,10 @@ W_BYTES = X_BYTES = Y_BYTES = STEP_BYTES = 0
 COPIES = 8                                      # >= 139 MB of weights > 126 MB L2
 NOMINAL_HBM_GBS = 8000.0
 WORKLOAD = ""
-MATVEC_TYPES = {"Q4_K": 12, "Q6_K": 14, "IQ1_S": 19, "IQ2_S": 22, "IQ1_M": 29}
+MATVEC_TYPES = {"Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ2_XXS": 16,
+                "IQ2_XS": 17, "IQ3_XXS": 18, "IQ1_S": 19, "IQ4_NL": 20, "IQ3_S": 21, "IQ2_S": 22,
+                "IQ4_XS": 23, "IQ1_M": 29}
+CONFIG1_TYPES = (19, 22, 29)   # the IQ1_M/IQ2_M mixes of BASELINE config 1
 
 
 def set_matvec_case(qtype_name="Q4_K", shape="17408x5120"):
@@ -68,7 +71,7 @@ def set_matvec_case(qtype_name="Q4_K", shape="17408x5120"):
     X_BYTES = WIDTH // 256 * 292                         # Q8_K activation
     Y_BYTES = ROWS * 4
     STEP_BYTES = W_BYTES + X_BYTES + Y_BYTES
-    config = "config0" if QTYPE == Q4_K else "config1"
+    config = "config0" if QTYPE == Q4_K else "config1" if QTYPE in CONFIG1_TYPES else "matvec"
     WORKLOAD = f"{config}: {qtype_name} {ROWS}x{WIDTH} x Q8_K matvec, bs1"
 
 

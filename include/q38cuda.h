@@ -90,7 +90,7 @@ int q38cu_tensor_gemm_q8_k(float *output, const Q38CuQ8KBlock *input, uint32_t b
  * (token, row, superblock), the two integer sums the upstream code folds into
  * its float result: w = the scaled quant dot, x = the min term (Q2_K, Q4_K,
  * Q5_K) or the delta correction (IQ1_S, IQ1_M), else 0.  Arrays are
- * [batch][N][K/256].  No upstream counterpart (the upstream kernels keep these
+ * [batch][N][K/256].  IQ4_NL (float sums per 32 elements) is refused.  No upstream counterpart (the upstream kernels keep these
  * sums in registers); used to prove the sums bit-exact. */
 int q38cu_tensor_gemm_q8_k_sums(float *output, int32_t *w_out, int32_t *x_out,
                                 const Q38CuQ8KBlock *input, uint32_t batch_size,

@@ -316,6 +316,8 @@ int q38cu_tensor_gemm_q8_k_sums(float *output, int32_t *w_out, int32_t *x_out, c
                                 void *stream)
 {
     if (!w_out || !x_out) return fail("sum outputs are required%s");
+    // IQ4_NL accumulates floats per 32-element block: no integer superblock sums.
+    if (tensor && tensor->type == 20) return fail("IQ4_NL has no integer superblock sums%s");
     return gemm_q8k(output, w_out, x_out, input, batch_size, input_length, tensor, stream);
 }
 

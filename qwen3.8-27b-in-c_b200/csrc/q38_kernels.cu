@@ -505,6 +505,15 @@ int superblock_bytes(int type)
     case kIQ2_S: return DecIQ2S::kBytes;
     case kIQ1_S: return DecIQ1S::kBytes;
     case kIQ1_M: return DecIQ1M::kBytes;
+    case kQ2_K: return DecQ2K::kBytes;
+    case kQ3_K: return DecQ3K::kBytes;
+    case kQ5_K: return DecQ5K::kBytes;
+    case kIQ2_XXS: return DecIQ2XXS::kBytes;
+    case kIQ2_XS: return DecIQ2XS::kBytes;
+    case kIQ3_XXS: return DecIQ3XXS::kBytes;
+    case kIQ3_S: return DecIQ3S::kBytes;
+    case kIQ4_XS: return DecIQ4XS::kBytes;
+    case kIQ4_NL: return DecIQ4NL::kBytes;
     default: return 0;
     }
 }
@@ -518,6 +527,15 @@ size_t gemm_smem_for(int type, const GemmPlan &p, int batch)
     case kIQ2_S: return gemm_smem_bytes<DecIQ2S>(p, mt);
     case kIQ1_S: return gemm_smem_bytes<DecIQ1S>(p, mt);
     case kIQ1_M: return gemm_smem_bytes<DecIQ1M>(p, mt);
+    case kQ2_K: return gemm_smem_bytes<DecQ2K>(p, mt);
+    case kQ3_K: return gemm_smem_bytes<DecQ3K>(p, mt);
+    case kQ5_K: return gemm_smem_bytes<DecQ5K>(p, mt);
+    case kIQ2_XXS: return gemm_smem_bytes<DecIQ2XXS>(p, mt);
+    case kIQ2_XS: return gemm_smem_bytes<DecIQ2XS>(p, mt);
+    case kIQ3_XXS: return gemm_smem_bytes<DecIQ3XXS>(p, mt);
+    case kIQ3_S: return gemm_smem_bytes<DecIQ3S>(p, mt);
+    case kIQ4_XS: return gemm_smem_bytes<DecIQ4XS>(p, mt);
+    case kIQ4_NL: return gemm_smem_bytes<DecIQ4NL>(p, mt);
     default: return 0;
     }
 }
@@ -530,6 +548,15 @@ cudaError_t launch_q8k_gemm(int type, const GemmPlan &p, const LaunchGemm &l, cu
     case kIQ2_S: return dispatch_mt<DecIQ2S>(p, l, s);
     case kIQ1_S: return dispatch_mt<DecIQ1S>(p, l, s);
     case kIQ1_M: return dispatch_mt<DecIQ1M>(p, l, s);
+    case kQ2_K: return dispatch_mt<DecQ2K>(p, l, s);
+    case kQ3_K: return dispatch_mt<DecQ3K>(p, l, s);
+    case kQ5_K: return dispatch_mt<DecQ5K>(p, l, s);
+    case kIQ2_XXS: return dispatch_mt<DecIQ2XXS>(p, l, s);
+    case kIQ2_XS: return dispatch_mt<DecIQ2XS>(p, l, s);
+    case kIQ3_XXS: return dispatch_mt<DecIQ3XXS>(p, l, s);
+    case kIQ3_S: return dispatch_mt<DecIQ3S>(p, l, s);
+    case kIQ4_XS: return dispatch_mt<DecIQ4XS>(p, l, s);
+    case kIQ4_NL: return dispatch_mt<DecIQ4NL>(p, l, s);
     default: return cudaErrorInvalidValue;
     }
 }

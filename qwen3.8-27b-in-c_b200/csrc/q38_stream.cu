@@ -721,22 +721,8 @@ __global__ void __launch_bounds__(StreamThreads<MT, L>::kValue, 1) stream_gemm_k
 
     // ---------------- consumer warps ----------------
     const int lane = tid & 31;
-    if constexpr (NeedsGrid<Dec>::kEntries > 0) {
-        // Codebook expansion (constant tables only) may precede the grid dependency.
-        for (int i = tid; i < NeedsGrid<Dec>::kEntries; i += consumers) {
-            if constexpr (NeedsGrid<Dec>::kEntries == 2048) {
-                const uint32_t e = d_iq1s_nib[i];
-                const uint32_t lo = e & 0x0F0F0F0Fu, hi = (e >> 4) & 0x0F0F0F0Fu;
-                grid[i] = make_uint2(((lo | 0x80808080u) - 0x01010101u) ^ 0x80808080u,
-                                     ((hi | 0x80808080u) - 0x01010101u) ^ 0x80808080u);
-            } else {
-                const uint32_t e = d_iq2s_nib[i];
-                const uint32_t lo = e & 0x0F0F0F0Fu, hi = (e >> 4) & 0x0F0F0F0Fu;
-                grid[i] = make_uint2(lo * 17u + 0x08080808u + ((lo >> 1) & 0x01010101u),
-                                     hi * 17u + 0x08080808u + ((hi >> 1) & 0x01010101u));
-            }
-        }
-    }
+    // Codebook expansion (constant tables only) may precede the grid dependency.
+    fill_grid<Dec>(grid, tid, consumers);
     float wpre[ActBatch<MT, L>::kValue][8];
     const bool preloaded = preload_norm_weights<MT, L>(g, consumers, wpre);
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -1186,6 +1172,15 @@ cudaError_t stream_plan(int type, int rows, int width, int tile_rows, int tokens
     case kIQ2_S: return plan_t<DecIQ2S>(rows, width, tile_rows, tokens, p);
     case kIQ1_S: return plan_t<DecIQ1S>(rows, width, tile_rows, tokens, p);
     case kIQ1_M: return plan_t<DecIQ1M>(rows, width, tile_rows, tokens, p);
+    case kQ2_K: return plan_t<DecQ2K>(rows, width, tile_rows, tokens, p);
+    case kQ3_K: return plan_t<DecQ3K>(rows, width, tile_rows, tokens, p);
+    case kQ5_K: return plan_t<DecQ5K>(rows, width, tile_rows, tokens, p);
+    case kIQ2_XXS: return plan_t<DecIQ2XXS>(rows, width, tile_rows, tokens, p);
+    case kIQ2_XS: return plan_t<DecIQ2XS>(rows, width, tile_rows, tokens, p);
+    case kIQ3_XXS: return plan_t<DecIQ3XXS>(rows, width, tile_rows, tokens, p);
+    case kIQ3_S: return plan_t<DecIQ3S>(rows, width, tile_rows, tokens, p);
+    case kIQ4_XS: return plan_t<DecIQ4XS>(rows, width, tile_rows, tokens, p);
+    case kIQ4_NL: return plan_t<DecIQ4NL>(rows, width, tile_rows, tokens, p);
     default: return cudaErrorInvalidValue;
     }
 }
@@ -1299,6 +1294,15 @@ cudaError_t launch_stream_gemm(int type, const StreamPlan &p, const StreamLaunch
     case kIQ2_S: return launch_t<DecIQ2S>(p, l, s);
     case kIQ1_S: return launch_t<DecIQ1S>(p, l, s);
     case kIQ1_M: return launch_t<DecIQ1M>(p, l, s);
+    case kQ2_K: return launch_t<DecQ2K>(p, l, s);
+    case kQ3_K: return launch_t<DecQ3K>(p, l, s);
+    case kQ5_K: return launch_t<DecQ5K>(p, l, s);
+    case kIQ2_XXS: return launch_t<DecIQ2XXS>(p, l, s);
+    case kIQ2_XS: return launch_t<DecIQ2XS>(p, l, s);
+    case kIQ3_XXS: return launch_t<DecIQ3XXS>(p, l, s);
+    case kIQ3_S: return launch_t<DecIQ3S>(p, l, s);
+    case kIQ4_XS: return launch_t<DecIQ4XS>(p, l, s);
+    case kIQ4_NL: return launch_t<DecIQ4NL>(p, l, s);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -20,7 +20,11 @@ from q38b200 import synth
 pytestmark = pytest.mark.gpu
 
 REL = 1e-3
-DEVICE_Q8K = (O.Q4_K, O.Q6_K, O.IQ2_S, O.IQ1_S, O.IQ1_M)
+DEVICE_Q8K = (O.Q4_K, O.Q6_K, O.IQ2_S, O.IQ1_S, O.IQ1_M, O.Q2_K, O.Q3_K, O.Q5_K,
+              O.IQ2_XXS, O.IQ2_XS, O.IQ3_XXS, O.IQ3_S, O.IQ4_XS)
+# IQ4_NL sums floats per 32 elements (qwen38_quant.c): its outputs are checked,
+# it has no integer superblock sums.
+DEVICE_Q8K_ALL = DEVICE_Q8K + (O.IQ4_NL,)
 NAME = O.TYPE_NAMES
 # GGUF row-major layout (row-streaming kernel) and the tiled streaming
 # layout (the fast path).
@@ -62,13 +66,22 @@ def test_quantize_golden_edges(q38):
 
 
 @pytest.mark.parametrize("layout", LAYOUTS, ids=LAYOUT_IDS)
-@pytest.mark.parametrize("qtype", DEVICE_Q8K, ids=lambda t: NAME[t])
+@pytest.mark.parametrize("qtype", DEVICE_Q8K_ALL, ids=lambda t: NAME[t])
 def test_gemm_golden(q38, qtype, layout):
     g = np.load(os.path.join(GOLDEN, f"q8k_{NAME[qtype]}.npz"))
     rows, width = g["weights"].shape[0], g["x"].shape[1]
     batch = g["x"].shape[0]
     t = q38.DeviceTensor(qtype, width, rows, g["weights"], layout=layout)
     act = to_dev(g["q8k"].reshape(-1))
+    per_token = (width // 256) * 292
+    if qtype == O.IQ4_NL:
+        assert_close(q38.gemm_q8_k(t, act, batch).cpu().numpy(), g["out"])
+        for tok in range(batch):
+            single = q38.gemm_q8_k(t, act[tok * per_token:(tok + 1) * per_token], 1)
+            assert_close(single.cpu().numpy()[0], g["gemv"][tok])
+        with pytest.raises(RuntimeError):
+            q38.gemm_q8_k_sums(t, act, batch)
+        return
     out, w, x = q38.gemm_q8_k_sums(t, act, batch)
     out, w, x = out.cpu().numpy(), w.cpu().numpy().astype(np.int64), x.cpu().numpy().astype(np.int64)
     assert_close(out, g["out"])
@@ -85,12 +98,17 @@ SHAPES = [(17, 256), (64, 512), (333, 5120), (37, 17408), (5, 6144), (129, 10240
 
 
 @pytest.mark.parametrize("layout", LAYOUTS, ids=LAYOUT_IDS)
-@pytest.mark.parametrize("qtype", DEVICE_Q8K, ids=lambda t: NAME[t])
+@pytest.mark.parametrize("qtype", DEVICE_Q8K_ALL, ids=lambda t: NAME[t])
 @pytest.mark.parametrize("rows,width", SHAPES)
 def test_gemm_random_vs_oracle(q38, oracle, qtype, rows, width, layout):
     weights = synth.quant_tensor(qtype, rows, width, seed=rows * 31 + width + qtype)
     t = q38.DeviceTensor(qtype, width, rows, weights, layout=layout)
     for batch in (1, 2, 3, 8, 11):
+        if qtype == O.IQ4_NL:
+            q8k = oracle.quantize_q8_k(synth.activations(batch, width, seed=batch + rows))
+            out = q38.gemm_q8_k(t, q8k_dev(q8k), batch).cpu().numpy()
+            assert_close(out, oracle.gemm_q8_k(qtype, weights, rows, width, q8k))
+            continue
         q8k = oracle.quantize_q8_k(synth.activations(batch, width, seed=batch + rows))
         out, w, x = q38.gemm_q8_k_sums(t, q8k_dev(q8k), batch)
         ref_out = oracle.gemm_q8_k(qtype, weights, rows, width, q8k)
@@ -104,7 +122,7 @@ def test_gemm_random_vs_oracle(q38, oracle, qtype, rows, width, layout):
 
 
 @pytest.mark.parametrize("layout", LAYOUTS, ids=LAYOUT_IDS)
-@pytest.mark.parametrize("qtype", DEVICE_Q8K, ids=lambda t: NAME[t])
+@pytest.mark.parametrize("qtype", DEVICE_Q8K_ALL, ids=lambda t: NAME[t])
 def test_batch_bit_exact_with_gemv(q38, oracle, qtype, layout):
     rows, width = 96, 5120
     weights = synth.quant_tensor(qtype, rows, width, seed=qtype)

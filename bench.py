@@ -54,7 +54,7 @@ COPIES = 8                                      # >= 139 MB of weights > 126 MB 
 NOMINAL_HBM_GBS = 8000.0
 WORKLOAD = ""
 MATVEC_TYPES = {"Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ2_XXS": 16,
-                "IQ2_XS": 17, "IQ3_XXS": 18, "IQ1_S": 19, "IQ4_NL": 20, "IQ3_S": 21, "IQ2_S": 22,
+                "IQ2_XS": 17, "IQ3_XXS": 18, "IQ1_S": 19, "IQ3_S": 21, "IQ2_S": 22,
                 "IQ4_XS": 23, "IQ1_M": 29}
 CONFIG1_TYPES = (19, 22, 29)   # the IQ1_M/IQ2_M mixes of BASELINE config 1
 

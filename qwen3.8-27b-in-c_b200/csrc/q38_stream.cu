@@ -1180,7 +1180,6 @@ cudaError_t stream_plan(int type, int rows, int width, int tile_rows, int tokens
     case kIQ3_XXS: return plan_t<DecIQ3XXS>(rows, width, tile_rows, tokens, p);
     case kIQ3_S: return plan_t<DecIQ3S>(rows, width, tile_rows, tokens, p);
     case kIQ4_XS: return plan_t<DecIQ4XS>(rows, width, tile_rows, tokens, p);
-    case kIQ4_NL: return plan_t<DecIQ4NL>(rows, width, tile_rows, tokens, p);
     default: return cudaErrorInvalidValue;
     }
 }
@@ -1302,7 +1301,6 @@ cudaError_t launch_stream_gemm(int type, const StreamPlan &p, const StreamLaunch
     case kIQ3_XXS: return launch_t<DecIQ3XXS>(p, l, s);
     case kIQ3_S: return launch_t<DecIQ3S>(p, l, s);
     case kIQ4_XS: return launch_t<DecIQ4XS>(p, l, s);
-    case kIQ4_NL: return launch_t<DecIQ4NL>(p, l, s);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -24,12 +24,15 @@ DEVICE_Q8K = (O.Q4_K, O.Q6_K, O.IQ2_S, O.IQ1_S, O.IQ1_M, O.Q2_K, O.Q3_K, O.Q5_K,
               O.IQ2_XXS, O.IQ2_XS, O.IQ3_XXS, O.IQ3_S, O.IQ4_XS)
 # IQ4_NL sums floats per 32 elements (qwen38_quant.c): its outputs are checked,
 # it has no integer superblock sums.
-DEVICE_Q8K_ALL = DEVICE_Q8K + (O.IQ4_NL,)
 NAME = O.TYPE_NAMES
 # GGUF row-major layout (row-streaming kernel) and the tiled streaming
 # layout (the fast path).
 LAYOUTS = (0, 1)
 LAYOUT_IDS = ("gguf", "tiled")
+# (type, layout) pairs of the integer path: the tiled layout regroups
+# 256-element superblocks, so the 32-element IQ4_NL blocks stay in the GGUF layout.
+Q8K_CASES = [pytest.param(t, l, id=f"{NAME[t]}-{LAYOUT_IDS[l]}")
+             for t in DEVICE_Q8K + (O.IQ4_NL,) for l in LAYOUTS if not (t == O.IQ4_NL and l == 1)]
 
 
 def to_dev(a):
@@ -65,8 +68,7 @@ def test_quantize_golden_edges(q38):
     assert np.array_equal(got.reshape(g["q8k"].shape), g["q8k"])
 
 
-@pytest.mark.parametrize("layout", LAYOUTS, ids=LAYOUT_IDS)
-@pytest.mark.parametrize("qtype", DEVICE_Q8K_ALL, ids=lambda t: NAME[t])
+@pytest.mark.parametrize("qtype,layout", Q8K_CASES)
 def test_gemm_golden(q38, qtype, layout):
     g = np.load(os.path.join(GOLDEN, f"q8k_{NAME[qtype]}.npz"))
     rows, width = g["weights"].shape[0], g["x"].shape[1]
@@ -79,8 +81,6 @@ def test_gemm_golden(q38, qtype, layout):
         for tok in range(batch):
             single = q38.gemm_q8_k(t, act[tok * per_token:(tok + 1) * per_token], 1)
             assert_close(single.cpu().numpy()[0], g["gemv"][tok])
-        with pytest.raises(RuntimeError):
-            q38.gemm_q8_k_sums(t, act, batch)
         return
     out, w, x = q38.gemm_q8_k_sums(t, act, batch)
     out, w, x = out.cpu().numpy(), w.cpu().numpy().astype(np.int64), x.cpu().numpy().astype(np.int64)
@@ -97,8 +97,7 @@ def test_gemm_golden(q38, qtype, layout):
 SHAPES = [(17, 256), (64, 512), (333, 5120), (37, 17408), (5, 6144), (129, 10240), (1, 5120)]
 
 
-@pytest.mark.parametrize("layout", LAYOUTS, ids=LAYOUT_IDS)
-@pytest.mark.parametrize("qtype", DEVICE_Q8K_ALL, ids=lambda t: NAME[t])
+@pytest.mark.parametrize("qtype,layout", Q8K_CASES)
 @pytest.mark.parametrize("rows,width", SHAPES)
 def test_gemm_random_vs_oracle(q38, oracle, qtype, rows, width, layout):
     weights = synth.quant_tensor(qtype, rows, width, seed=rows * 31 + width + qtype)
@@ -121,8 +120,7 @@ def test_gemm_random_vs_oracle(q38, oracle, qtype, rows, width, layout):
         assert np.array_equal(plain, out.cpu().numpy()), f"plain vs sums path (batch {batch})"
 
 
-@pytest.mark.parametrize("layout", LAYOUTS, ids=LAYOUT_IDS)
-@pytest.mark.parametrize("qtype", DEVICE_Q8K_ALL, ids=lambda t: NAME[t])
+@pytest.mark.parametrize("qtype,layout", Q8K_CASES)
 def test_batch_bit_exact_with_gemv(q38, oracle, qtype, layout):
     rows, width = 96, 5120
     weights = synth.quant_tensor(qtype, rows, width, seed=qtype)
@@ -194,9 +192,14 @@ def test_error_paths(q38):
     act = torch.zeros(2 * 292, dtype=torch.uint8, device="cuda")
     with pytest.raises(q38.Q38CudaError):
         q38.gemm_q8_k(t, act, 0)
-    t2 = q38.DeviceTensor(O.Q5_K, 512, 4, synth.quant_tensor(O.Q5_K, 4, 512, seed=1))
-    with pytest.raises(q38.Q38CudaError, match="not yet implemented"):
+    t2 = q38.DeviceTensor(O.Q8_0, 512, 4, synth.quant_tensor(O.Q8_0, 4, 512, seed=1))
+    with pytest.raises(q38.Q38CudaError, match="no Q8_K integer kernel"):
         q38.gemm_q8_k(t2, act, 1)
+    with pytest.raises(q38.Q38CudaError, match="256-element block type"):
+        q38.DeviceTensor(O.IQ4_NL, 512, 4, synth.quant_tensor(O.IQ4_NL, 4, 512, seed=1), layout=1)
+    t3 = q38.DeviceTensor(O.IQ4_NL, 512, 4, synth.quant_tensor(O.IQ4_NL, 4, 512, seed=1))
+    with pytest.raises(q38.Q38CudaError, match="no integer superblock sums"):
+        q38.gemm_q8_k_sums(t3, act, 1)
 
 
 def test_repeated_launches_reuse_scratch(q38, oracle):

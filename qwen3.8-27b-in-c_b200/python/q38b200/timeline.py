@@ -71,6 +71,23 @@ def main(count=6):
     for k, v in ph.items():
         md = np.median(np.array(v), axis=0) / 1e3
         print(f"| {k} | " + " | ".join(f"{x:.2f}" for x in md) + " |")
+    # Fused RMSNorm prologues: the earliest CTA's steps (fields 1, 9, 8, 10, 7),
+    # the spread to the last CTA staged (field 3) and the spread of the CTAs'
+    # returns from the grid-dependency wait (fields 1, 6).
+    print()
+    print("| RMSNorm GEMV kind | ready->x loaded | ->sum known | ->warp 0 quantized | ->first staged "
+          "| first->last staged | first->last ready |")
+    print("|---|---:|---:|---:|---:|---:|---:|")
+    sub = collections.defaultdict(list)
+    for i in range(n):
+        for r in records:
+            if r[i, 3] == 0 or r[i, 4] == 0 or r[i, 9] in (0, -1) or r[i, 9] < r[i, 1]:
+                continue
+            sub[kind(names[i])].append([r[i, 9] - r[i, 1], r[i, 8] - r[i, 9], r[i, 10] - r[i, 8],
+                                        r[i, 7] - r[i, 10], r[i, 3] - r[i, 7], r[i, 6] - r[i, 1]])
+    for k, v in sub.items():
+        md = np.median(np.array(v), axis=0) / 1e3
+        print(f"| {k} | " + " | ".join(f"{x:.2f}" for x in md) + " |")
     m.close()
 
 

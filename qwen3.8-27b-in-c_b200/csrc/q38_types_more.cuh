@@ -29,16 +29,26 @@ __device__ __forceinline__ int bsum16(const A &a, int t, int e)
     return (e & 1) ? hi16(pair) : lo16(pair);
 }
 
-// Bytes i of `n` (each 0..15) through a 16-entry signed byte table held in
-// four words (entries 0-3, 4-7, 8-11, 12-15): prmt picks among 8 bytes with
-// 3-bit selectors; bit 3 of the index chooses the upper half.
-__device__ __forceinline__ uint32_t lookup16(uint32_t n, uint32_t t0, uint32_t t1, uint32_t t2, uint32_t t3)
+// Both nibbles of the four bytes of `w` through a 16-entry byte table held in
+// four words: lo = table[low nibble of byte i] and hi = table[high nibble of
+// byte i] in byte i.  Each 16-bit half of w is used as a prmt selector for
+// four table lookups at once (selector nibbles masked to 3 bits: bit 3 would
+// ask prmt for sign replication); a third prmt keeps, per byte, the entry
+// from the upper table half where the index has bit 3 set, and two more
+// regroup the lookups by nibble.
+__device__ __forceinline__ void lookup16_nibbles(uint32_t w, uint32_t t0, uint32_t t1, uint32_t t2, uint32_t t3,
+                                                 uint32_t &lo, uint32_t &hi)
 {
-    const uint32_t s = n & 0x07070707u;
-    const uint32_t sel = (s & 0x7u) | ((s >> 4) & 0x70u) | ((s >> 8) & 0x700u) | ((s >> 12) & 0x7000u);
-    const uint32_t lo = prmt(t0, t1, sel), hi = prmt(t2, t3, sel);
-    const uint32_t mask = ((n >> 3) & 0x01010101u) * 0xFFu;
-    return (lo & ~mask) | (hi & mask);
+    uint32_t r[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint32_t sel = h ? w >> 16 : w;
+        const uint32_t s7 = sel & 0x7777u;
+        const uint32_t pick = ((sel >> 1) & 0x4444u) | 0x3210u;
+        r[h] = prmt(prmt(t0, t1, s7), prmt(t2, t3, s7), pick);
+    }
+    lo = prmt(r[0], r[1], 0x6420u);
+    hi = prmt(r[0], r[1], 0x7531u);
 }
 
 // IQ4_NL levels (qwen38_quant.c kvalues_iq4nl) as signed bytes.
@@ -244,16 +254,14 @@ struct DecIQ4XS {
                                                (((sh >> (2 * g)) & 3u) << 4)) - 32;
             const uint2 qa = p[1 + 2 * g], qb = p[2 + 2 * g];
             const uint32_t qw[4] = {qa.x, qa.y, qb.x, qb.y};
+            uint32_t lv[8];  // levels of elements 4k.. (lv[k]) and 16 + 4k.. (lv[4 + k])
+#pragma unroll
+            for (int k = 0; k < 4; ++k) lookup16_nibbles(qw[k], kIq4Lv0, kIq4Lv1, kIq4Lv2, kIq4Lv3, lv[k], lv[4 + k]);
 #pragma unroll
             for (int t = 0; t < MT; ++t) {
                 int sub = 0;
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    sub = dp4a_ss(lookup16(qw[k] & 0x0F0F0F0Fu, kIq4Lv0, kIq4Lv1, kIq4Lv2, kIq4Lv3),
-                                  a.q(t, 8 * g + k), sub);
-                    sub = dp4a_ss(lookup16((qw[k] >> 4) & 0x0F0F0F0Fu, kIq4Lv0, kIq4Lv1, kIq4Lv2, kIq4Lv3),
-                                  a.q(t, 8 * g + 4 + k), sub);
-                }
+                for (int k = 0; k < 8; ++k) sub = dp4a_ss(lv[k], a.q(t, 8 * g + k), sub);
                 w[t] += scale * sub;
             }
         }
@@ -291,16 +299,14 @@ struct DecIQ4NL {
             uint32_t qw[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) qw[k] = __funnelshift_r(raw[k], raw[k + 1], 16);
+            uint32_t lv[8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) lookup16_nibbles(qw[k], kIq4Lv0, kIq4Lv1, kIq4Lv2, kIq4Lv3, lv[k], lv[4 + k]);
 #pragma unroll
             for (int t = 0; t < MT; ++t) {
                 int sub = 0;
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    sub = dp4a_ss(lookup16(qw[k] & 0x0F0F0F0Fu, kIq4Lv0, kIq4Lv1, kIq4Lv2, kIq4Lv3),
-                                  a.q(t, 8 * g + k), sub);
-                    sub = dp4a_ss(lookup16((qw[k] >> 4) & 0x0F0F0F0Fu, kIq4Lv0, kIq4Lv1, kIq4Lv2, kIq4Lv3),
-                                  a.q(t, 8 * g + 4 + k), sub);
-                }
+                for (int k = 0; k < 8; ++k) sub = dp4a_ss(lv[k], a.q(t, 8 * g + k), sub);
                 v[t] = __fadd_rn(v[t], __fmul_rn(__fmul_rn(d, a.xs(t)), static_cast<float>(sub)));
             }
         }

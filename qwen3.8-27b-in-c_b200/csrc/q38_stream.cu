@@ -69,7 +69,7 @@ constexpr int kStreamMaxStages = 32;            // stages of all groups together
 constexpr size_t kChunkBudget = 112 * 1024;     // one ring pass of all groups (sets the chunk)
 constexpr size_t kActBudget = 96 * 1024;        // shared memory for activation columns
 constexpr int kMaxConsumers = 256;              // CTA bound for 8 tokens: 288 threads
-constexpr size_t kOverlapSmem = 112 * 1024;     // short launches: two CTAs fit an SM
+constexpr size_t kOverlapSmem = 112 * 1024;     // short launches: half an SM's shared memory
 constexpr size_t kLongLaunchBytes = 2u << 20;   // per-CTA bytes above which a launch is long
 
 struct StreamArgs {
@@ -1047,9 +1047,11 @@ cudaError_t plan_t(int rows, int width, int tile_rows, int tokens, StreamPlan *p
     const int env_grid = env_knob("Q38CU_STREAM_GRID", 0);
     if (env_grid > 0) q.grid = static_cast<int>(std::min<long long>(q.units, env_grid));
     // Ring depth (no effect on the arithmetic).  A short launch keeps its CTA
-    // under half of an SM's shared memory, so the next launch of the stream
-    // (programmatic dependent launch) can be resident beside it and prefetch
-    // its weights while this one finishes; a long launch takes what it can.
+    // under half of an SM's shared memory, so that shared memory does not keep
+    // the next launch of the stream (programmatic dependent launch) from being
+    // resident beside it; a long launch takes what it can.  (At 128 registers
+    // per thread the register file still does: two CTAs of 288 threads need
+    // 72 K registers.)
     int optin = 0, dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);

@@ -330,18 +330,26 @@ PROMPT_TOKENS = 128
 CONTEXT = 4096
 VOCAB = 248320
 MODEL_SEED = 0
-DECODE_WORKLOAD = ("config3: synthetic Qwen3.8-27B Q4_K_M GGUF (upstream loader contract, config-0 weight "
-                   "draws), 128-token random prompt, greedy decode bs1, ctx 4096, MTP off")
+MIX = "Q4_K_M"   # --mix: the model's type mix (gguf.MIXES); IQ1_M is config 4's IQ1_M-typed variant
+DECODE_WORKLOAD = ""
+
+
+def set_decode_mix(mix="Q4_K_M"):
+    global MIX, DECODE_WORKLOAD
+    MIX = mix
+    config = "config3" if mix == "Q4_K_M" else "config4 IQ1_M-typed variant"
+    DECODE_WORKLOAD = (f"{config}: synthetic Qwen3.8-27B {mix} GGUF (upstream loader contract, config-0 weight "
+                       "draws), 128-token random prompt, greedy decode bs1, ctx 4096, MTP off")
 
 
 def decode_model_path(rank, dist):
     """The synthetic model file, written once per machine (rank 0 first)."""
     from q38b200 import gguf
-    path = gguf.cached_model_path(seed=MODEL_SEED, mtp=True, dist="config0") if rank == 0 else None
+    path = gguf.cached_model_path(seed=MODEL_SEED, mtp=True, dist="config0", mix=MIX) if rank == 0 else None
     if dist:
         dist.barrier()
     if path is None:
-        path = gguf.cached_model_path(seed=MODEL_SEED, mtp=True, dist="config0")
+        path = gguf.cached_model_path(seed=MODEL_SEED, mtp=True, dist="config0", mix=MIX)
     return path
 
 
@@ -351,7 +359,7 @@ def decode_weight_bytes():
     part of a target step)."""
     from q38b200 import gguf, synth
     total = 0
-    for name, shape, qtype in gguf.tensor_specs(mtp=False):
+    for name, shape, qtype in gguf.tensor_specs(mtp=False, mix=MIX):
         elements, nbytes = synth.BLOCK[qtype]
         size = int(np.prod(shape)) // elements * nbytes
         if name == "token_embd.weight":
@@ -373,7 +381,7 @@ def decode_step_bytes(position):
 
 def read_step_traffic():
     path = os.path.join(ROOT, "profiles", "decode_step_config3.md")
-    if not os.path.exists(path):
+    if MIX != "Q4_K_M" or not os.path.exists(path):
         return None
     for line in open(path):
         if line.startswith("dram_bytes_per_step:"):
@@ -591,8 +599,11 @@ def main():
     parser.add_argument("--profile", action="store_true",
                         help="plain launches only, for ncu: matvec - warmup + steps launches; decode - one decode "
                              "step between cudaProfilerStart/Stop; prints no bench line")
+    parser.add_argument("--mix", choices=("Q4_K_M", "IQ1_M"), default="Q4_K_M",
+                        help="decode workload: the model's type mix (IQ1_M: BASELINE config 4's IQ1_M-typed variant)")
     args = parser.parse_args()
     set_matvec_case(args.qtype, args.shape)
+    set_decode_mix(args.mix)
     decode = args.workload == "decode"
     if args.steps is None:
         args.steps = 256 if decode else 20000

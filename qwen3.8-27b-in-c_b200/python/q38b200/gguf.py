@@ -9,7 +9,8 @@ GGUF v3 file with those tensor names, shapes and metadata and a Q4_K_M-style
 type mix (Q6_K for output.weight, every attn_v and ffn_down of even blocks;
 Q8_0 for ssm_alpha / ssm_beta; Q4_K for the other matrices, token_embd
 included; F32 for norms and the DeltaNet vectors).  Quantized weights follow
-the benchmark distributions (see synth.py).
+the benchmark distributions (see synth.py).  mix="IQ1_M" gives the IQ1_M-typed
+variant: every Q4_K matrix but token_embd in IQ1_M, the rest unchanged.
 
 With alias=True the tensors of one role (the name without its "blk.N."
 prefix) and one (type, shape) point at a single shared data region across
@@ -35,10 +36,15 @@ GGUF_UINT32, GGUF_STRING = 4, 8
 ALIGN = 32
 
 
-def tensor_specs(mtp=False, ffn_down_q6k_every=2):
+MIXES = ("Q4_K_M", "IQ1_M")
+
+
+def tensor_specs(mtp=False, ffn_down_q6k_every=2, mix="Q4_K_M"):
     """[(name, shape (GGUF order: width first), type)] of the model."""
-    F32, Q4_K, Q6_K, Q8_0 = synth.F32, synth.Q4_K, synth.Q6_K, synth.Q8_0
-    specs = [("token_embd.weight", (HIDDEN, VOCAB), Q4_K),
+    assert mix in MIXES, mix
+    F32, Q6_K, Q8_0 = synth.F32, synth.Q6_K, synth.Q8_0
+    Q4_K = synth.IQ1_M if mix == "IQ1_M" else synth.Q4_K  # the mix's main matrix type
+    specs = [("token_embd.weight", (HIDDEN, VOCAB), synth.Q4_K),
              ("output_norm.weight", (HIDDEN,), F32),
              ("output.weight", (HIDDEN, VOCAB), Q6_K)]
     for layer in range(LAYERS + (1 if mtp else 0)):
@@ -119,11 +125,12 @@ def _pack_string(s):
     return struct.pack("<Q", len(b)) + b
 
 
-def write_model_gguf(path, seed=0, mtp=False, alias=True, dist="config0"):
+def write_model_gguf(path, seed=0, mtp=False, alias=True, dist="config0", mix="Q4_K_M"):
     """Write the synthetic model; returns the list of tensor specs.  `dist`
-    is one of DISTRIBUTIONS (see _tensor_bytes)."""
+    is one of DISTRIBUTIONS (see _tensor_bytes), `mix` one of MIXES."""
     assert dist in DISTRIBUTIONS, dist
-    specs = tensor_specs(mtp=mtp)
+    assert mix == "Q4_K_M" or dist == "config0", "the conditioned draws are defined for Q4_K_M"
+    specs = tensor_specs(mtp=mtp, mix=mix)
     meta = [("general.architecture", GGUF_STRING, "qwen35"),
             ("general.alignment", GGUF_UINT32, ALIGN),
             ("qwen35.block_count", GGUF_UINT32, LAYERS + (1 if mtp else 0)),
@@ -172,17 +179,17 @@ def write_model_gguf(path, seed=0, mtp=False, alias=True, dist="config0"):
     return specs
 
 
-def cached_model_path(seed=1, mtp=True, dist="conditioned", directory=None):
+def cached_model_path(seed=1, mtp=True, dist="conditioned", directory=None, mix="Q4_K_M"):
     """Path of the synthetic model for these parameters, written on first use
     (about 2 GB; a few tens of seconds)."""
     import os
     import tempfile
     directory = directory or os.environ.get("Q38_MODEL_DIR") or os.path.join(tempfile.gettempdir(), "q38b200")
     os.makedirs(directory, exist_ok=True)
-    name = f"qwen38-synthetic-s{seed}{'-mtp' if mtp else ''}-{dist}.gguf"
+    name = f"qwen38-synthetic-s{seed}{'-mtp' if mtp else ''}-{dist}{'' if mix == 'Q4_K_M' else '-' + mix}.gguf"
     path = os.path.join(directory, name)
     if not os.path.exists(path):
         partial = path + ".partial"
-        write_model_gguf(partial, seed=seed, mtp=mtp, dist=dist)
+        write_model_gguf(partial, seed=seed, mtp=mtp, dist=dist, mix=mix)
         os.replace(partial, path)
     return path

@@ -565,7 +565,7 @@ def run_decode(args, rank, world, dist):
         "vs_baseline": None, "dtype": "int8xint8->int32,f32", "data": "synthetic (seeded GGUF, config-0 draws)",
         "config": {"workload": DECODE_WORKLOAD, "prompt": PROMPT_TOKENS, "context": CONTEXT, "batch": 1,
                    "mtp": "off", "weights_bytes_per_step": decode_weight_bytes(),
-                   "l2": "inputs larger than L2: 15.5 GB of weights stream every step",
+                   "l2": f"inputs larger than L2: {decode_weight_bytes() / 1e9:.1f} GB of weights stream every step",
                    "parallelism": f"replica per GPU x{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS,

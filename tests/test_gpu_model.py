@@ -257,3 +257,30 @@ def test_speculative_greedy_preserves_greedy(models, drafts):
         token = accepted[-1]
     assert seq[:12] == plain
     assert dev.position == len(seq)
+
+
+def test_iq1m_model_first_layer_matches_upstream():
+    """The IQ1_M-typed variant (gguf mix "IQ1_M": IQ1_M for every Q4_K matrix
+    but the embedding, config-0 weight draws): layer 0, a DeltaNet block whose
+    qkv, gate, out, ffn_gate and ffn_up are IQ1_M, sees the exact embedding
+    row.  The config-0 draws are not conditioned (the layer's activations
+    reach 1e5), so a one-ulp difference in a float sum inside the layer flips
+    a few int8 values of the later Q8_K activations: the bar is the in-layer
+    flip bar of the teacher-forced test (1e-2; observed 3e-4), with the cosine
+    above 0.9999.  A wrong decoder would be off by order 1."""
+    if not O.reference_available():
+        pytest.skip("upstream reference library not built")
+    from q38b200.model import Model
+    path = gguf.cached_model_path(seed=2, mtp=False, dist="config0", mix="IQ1_M")
+    dev = Model(path, 64)
+    ref = O.ReferenceModel(path, 64)
+    try:
+        for token in (777, 3):
+            dev.reset()
+            ref.reset()
+            got, want = dev.forward_token_layers(token, 1), ref.forward_token_layers(token, 1)
+            assert np.all(np.isfinite(got))
+            assert rel(got, want) <= 1e-2 and cosine(got, want) >= 0.9999
+    finally:
+        dev.close()
+        ref.close()

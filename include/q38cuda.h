@@ -141,7 +141,9 @@ uint32_t q38cu_block_elements(uint32_t type);
  * Its scratch is one file-scope device array of Q38CU_NOALLOC_SCRATCH_BYTES,
  * which every GPU that loads the library holds until the process exits.  The
  * first call on a device looks up that array's device address (set-up, once
- * per device); make that first call before any stream capture.  Shapes whose
+ * per device); make that first call before any stream capture (a first call
+ * on a capturing stream is refused), and do not call it again after ending the
+ * device's context (cudaDeviceReset) in the same process.  Shapes whose
  * scratch exceeds the maximum are rejected (return 0, reason in
  * q38cu_last_error).  All calls share the one array and each clears its tile
  * counters first, so calls whose kernels overlap on the GPU (two streams, or
@@ -150,11 +152,39 @@ uint32_t q38cu_block_elements(uint32_t type);
 int q38cu_tensor_gemm_q8_k_noalloc(float *output, const Q38CuQ8KBlock *input, uint32_t batch_size,
                                    uint64_t input_length, const Q38CuTensor *tensor, void *stream);
 
+/* Batch GEMM on the tensor cores, for prefill-sized batches (replaces
+ * q38_tensor_gemm_q8_k, qwen38_quant.h:47-49, when M is large: the upstream
+ * layer-major prefill calls it with M = prompt tokens, qwen38_model.c:1519-1560).
+ * Same arguments and batch-major output [batch_size][N] as
+ * q38cu_tensor_gemm_q8_k, for Q4_K and Q6_K tensors in either layout; the
+ * weights and the Q8_K activations are dequantized to fp16 in `workspace`
+ * (device memory, 256-byte aligned, at least
+ * q38cu_tensor_gemm_q8_k_tc_workspace() bytes) and multiplied by tcgen05.mma
+ * with fp32 accumulation.  Results agree with the integer path within 1e-3
+ * relative (fp16 operand rounding); they are not bit-identical to it. */
+uint64_t q38cu_tensor_gemm_q8_k_tc_workspace(uint32_t batch_size, uint64_t input_length, const Q38CuTensor *tensor);
+int q38cu_tensor_gemm_q8_k_tc(float *output, const Q38CuQ8KBlock *input, uint32_t batch_size, uint64_t input_length,
+                              const Q38CuTensor *tensor, void *workspace, uint64_t workspace_bytes, void *stream);
+
 /* Diagnostics: the message behind the last 0 return on this host thread, and
  * the device status word (0 = ok, else a bounded wait gave up) which is read
  * after synchronizing `stream` and then cleared. */
 const char *q38cu_last_error(void);
 int q38cu_device_status(void *stream);
+
+/* Host only, no device work: parses the GGUF file at `path` with the device
+ * model's reader, which accepts what the upstream q38_gguf_open accepts
+ * (src/io/qwen38_gguf.c:326-413: header, metadata, tensor table, every
+ * tensor's bytes inside the file).  Returns the tensor count, or 0 with the
+ * reason in q38cu_last_error() for a missing, truncated or corrupt file. */
+uint64_t q38cu_gguf_check(const char *path);
+
+/* Failure-path check (no upstream counterpart): launches one kernel whose
+ * bounded mbarrier wait - the same wait every streaming kernel uses, with
+ * limit_ns (1 .. 1e9) instead of the 2 s default - has nothing to wait for, so
+ * it gives up, records the wait-timeout status (1) and returns; the context
+ * stays usable.  q38cu_device_status then reports 1 once. */
+int q38cu_debug_wait_probe(uint64_t limit_ns, void *stream);
 
 #ifdef __cplusplus
 }

@@ -21,6 +21,24 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_LIB = os.path.join(HERE, "_build", "libq38oracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libq38ref.so")
 REF_PORTABLE_LIB = os.path.join(HERE, "_ref", "libq38ref_portable.so")
+REF_VNNI_LIB = os.path.join(HERE, "_ref", "libq38ref_vnni.so")
+
+
+def host_has_avx_vnni():
+    try:
+        with open("/proc/cpuinfo") as handle:
+            return any(line.startswith("flags") and " avx_vnni" in line for line in handle)
+    except OSError:
+        return False
+
+
+def baseline_reference_lib():
+    """The upstream build a CPU baseline should time on this host, and its
+    flags: the AVX-VNNI build where the CPU has AVX-VNNI (what the upstream's
+    -march=native build compiles there), else the x86-64-v3 build."""
+    if host_has_avx_vnni() and os.path.exists(REF_VNNI_LIB):
+        return REF_VNNI_LIB, "-O3 -march=x86-64-v3 -mavxvnni -fopenmp (upstream dpbusd branch)"
+    return REF_LIB, "-O3 -march=x86-64-v3 -fopenmp (upstream maddubs branch; host has no AVX-VNNI)"
 
 # GGML type ids (GGUF values).
 F32, F16, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K = 0, 1, 8, 10, 11, 12, 13, 14

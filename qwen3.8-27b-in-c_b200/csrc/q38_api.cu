@@ -10,6 +10,7 @@
 #include <mutex>
 
 #include "../../include/q38cuda.h"
+#include "q38_gguf_file.h"
 #include "q38_internal.h"
 
 namespace {
@@ -279,14 +280,30 @@ const char *q38cu_last_error(void) { return g_error; }
 
 int q38cu_device_status(void *stream)
 {
-    int status = 0, stream_status = 0;
+    int status = 0, stream_status = 0, tc_status = 0;
     cudaError_t e = q38::read_and_clear_status(&status, static_cast<cudaStream_t>(stream));
     if (e == cudaSuccess) e = q38::read_and_clear_stream_status(&stream_status);
+    if (e == cudaSuccess) e = q38::read_and_clear_tc_status(&tc_status);
     if (e != cudaSuccess) {
         fail_cuda("device status", e);
         return -1;
     }
-    return status ? status : stream_status;
+    return status ? status : stream_status ? stream_status : tc_status;
+}
+
+uint64_t q38cu_gguf_check(const char *path)
+{
+    if (!path) return fail("path is required%s");
+    q38::GGUFFile f;
+    if (!f.open(path)) return fail("%s", f.error().c_str());
+    return f.tensor_count();
+}
+
+int q38cu_debug_wait_probe(uint64_t limit_ns, void *stream)
+{
+    if (limit_ns == 0 || limit_ns > 1000000000ull) return fail("limit_ns must be in 1 .. 1e9%s");
+    const cudaError_t e = q38::launch_wait_probe(limit_ns, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? 1 : fail_cuda("wait probe launch", e);
 }
 
 int q38cu_quantize_q8_k(Q38CuQ8KBlock *output, const float *input, uint64_t length, void *stream)
@@ -309,6 +326,53 @@ int q38cu_tensor_gemm_q8_k(float *output, const Q38CuQ8KBlock *input, uint32_t b
                            uint64_t input_length, const Q38CuTensor *tensor, void *stream)
 {
     return gemm_q8k(output, nullptr, nullptr, input, batch_size, input_length, tensor, stream);
+}
+
+uint64_t q38cu_tensor_gemm_q8_k_tc_workspace(uint32_t batch_size, uint64_t input_length, const Q38CuTensor *tensor)
+{
+    if (!tensor || !batch_size || tensor->n_dims != 2 || input_length % 256) return 0;
+    const uint64_t a = (tensor->shape[1] * input_length * 2 + 255) / 256 * 256;
+    const uint64_t b = (static_cast<uint64_t>(batch_size) * input_length * 2 + 255) / 256 * 256;
+    return a + b + (static_cast<uint64_t>(batch_size) * 4 + 255) / 256 * 256;
+}
+
+int q38cu_tensor_gemm_q8_k_tc(float *output, const Q38CuQ8KBlock *input, uint32_t batch_size, uint64_t input_length,
+                              const Q38CuTensor *tensor, void *workspace, uint64_t workspace_bytes, void *stream)
+{
+    if (!output || !input || !batch_size || !workspace) return fail("output, input, batch_size and workspace are required%s");
+    if (!check_matrix(tensor, input_length)) return 0;
+    if (!q38::tc_weight_type(static_cast<int>(tensor->type)))
+        return fail("the tensor-core GEMM takes Q4_K and Q6_K weights%s");
+    if (input_length % 256 || input_length > (1u << 20) || batch_size > (1u << 20))
+        return fail("input length must be a multiple of 256; batch and width at most 2^20%s");
+    if (!aligned16(output) || !aligned16(input)) return fail("output and input must be 16-byte aligned%s");
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return fail("workspace must be 256-byte aligned%s");
+    const uint64_t need = q38cu_tensor_gemm_q8_k_tc_workspace(batch_size, input_length, tensor);
+    if (workspace_bytes < need) return fail("workspace smaller than q38cu_tensor_gemm_q8_k_tc_workspace()%s");
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    void *a16 = ws;
+    void *b16 = ws + (tensor->shape[1] * input_length * 2 + 255) / 256 * 256;
+    float *scale = reinterpret_cast<float *>(static_cast<uint8_t *>(b16) +
+                                             (static_cast<uint64_t>(batch_size) * input_length * 2 + 255) / 256 * 256);
+    const Geometry g = geometry(tensor->type);
+    cudaError_t e = q38::launch_dequant_f16(tensor->data, static_cast<int>(tensor->type), tensor->shape[1],
+                                            input_length, layout_tile_rows(tensor), static_cast<int>(g.bytes), a16, 0, s);
+    if (e == cudaSuccess)
+        e = q38::launch_q8k_to_f16(input, static_cast<int>(input_length / 256), static_cast<int>(batch_size),
+                                   static_cast<int>(batch_size), b16, scale, s);
+    if (e == cudaSuccess) {
+        q38::TcGemm p;
+        p.out = output;
+        p.ld = static_cast<int>(tensor->shape[1]);
+        p.n = static_cast<int>(tensor->shape[1]);
+        p.m = p.m_pad = static_cast<int>(batch_size);
+        p.k = static_cast<int>(input_length);
+        p.tok_scale = scale;
+        p.accumulate = 0;
+        e = q38::launch_tc_gemm(a16, b16, p, s);
+    }
+    return e == cudaSuccess ? 1 : fail_cuda("tensor-core gemm launch", e);
 }
 
 int q38cu_tensor_gemm_q8_k_sums(float *output, int32_t *w_out, int32_t *x_out, const Q38CuQ8KBlock *input,

@@ -158,14 +158,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
     return done != 0;
 }
 
-// Wait for phase `parity` of `bar`, giving up after kWaitLimitNs.  Returns
-// false (and records kStatusWaitTimeout) when the wait was abandoned.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *status)
+// Wait for phase `parity` of `bar`, giving up after `limit_ns` (default
+// kWaitLimitNs).  Returns false (and records kStatusWaitTimeout) when the wait
+// was abandoned.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *status,
+                                                  unsigned long long limit_ns = kWaitLimitNs)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long start = global_timer_ns();
     while (!mbar_try_wait(bar, parity)) {
-        if (global_timer_ns() - start > kWaitLimitNs) {
+        if (global_timer_ns() - start > limit_ns) {
             if (status) atomicExch(status, kStatusWaitTimeout);
             return false;
         }

@@ -136,7 +136,7 @@ bool GGUFFile::open(const char *path)
     fd_ = ::open(path, O_RDONLY);
     if (fd_ < 0) return fail(std::string("cannot open ") + path);
     struct stat st;
-    if (fstat(fd_, &st) != 0 || st.st_size < 24) return fail("invalid GGUF file size");
+    if (fstat(fd_, &st) != 0 || st.st_size < 24) return fail("file too small to hold a GGUF header");
     mapping_size_ = static_cast<uint64_t>(st.st_size);
     void *m = mmap(nullptr, mapping_size_, PROT_READ, MAP_PRIVATE, fd_, 0);
     if (m == MAP_FAILED) {

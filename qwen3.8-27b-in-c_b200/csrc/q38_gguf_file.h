@@ -52,6 +52,7 @@ public:
     bool meta_string_is(const char *key, const char *expected) const;
     const std::string &error() const { return error_; }
     bool is_open() const { return mapping_ != nullptr; }
+    uint64_t tensor_count() const { return tensors_.size(); }
 
 private:
     int fd_ = -1;

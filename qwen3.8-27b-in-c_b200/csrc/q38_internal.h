@@ -129,6 +129,28 @@ cudaError_t launch_repack_tiled(void *dst, const void *src, uint64_t rows, uint6
 // q38cu_tensor_repack with a given tile height (a multiple of 8, 8..256).
 int repack_tiled_with(void *dst_tensor, const void *src_tensor, uint32_t tile_rows, void *stream);
 
+// Tensor-core batch GEMM (q38_tc.cu): out[t * ld + row] (+)= sum_k A[row][k]
+// B[t][k] * tok_scale[t], A fp16 [n][k] and B fp16 [m_pad][k] (K-major, k a
+// multiple of 64, both 16-byte aligned).
+struct TcGemm {
+    float *out;
+    int ld;
+    int n, m, m_pad, k;
+    const float *tok_scale;
+    int accumulate;
+};
+bool tc_weight_type(int type);
+int tc_token_tile(int m);
+// Quantized rows (tiled layout when tile_rows != 0) -> fp16 [rows][width];
+// split: rows interleaved (gate i, up i) are written as [gate rows | up rows].
+cudaError_t launch_dequant_f16(const void *w, int type, uint64_t rows, uint64_t width, uint32_t tile_rows, int bb,
+                               void *out, int split, cudaStream_t s);
+// Q8_K [m][nb] -> fp16 [m_pad][nb * 256] scaled by 2^-e per token, tok_scale[t] = 2^e.
+cudaError_t launch_q8k_to_f16(const void *q8, int nb, int m, int m_pad, void *out, float *tok_scale,
+                              cudaStream_t s);
+cudaError_t launch_tc_gemm(const void *a16, const void *b16, const TcGemm &p, cudaStream_t s);
+cudaError_t read_and_clear_tc_status(int *status);
+
 int device_sm_count();
 // Message returned by q38cu_last_error() on this host thread.
 void set_last_error(const char *message);
@@ -150,6 +172,8 @@ cudaError_t launch_row_f32_indexed(float *out, const void *w, uint64_t width, ui
                                    const uint32_t *row_index, int count, int type, int be, int bb, cudaStream_t s,
                                    int reps = 1, long long rep_floats = 0);
 cudaError_t read_and_clear_status(int *status, cudaStream_t s);
+// One bounded mbarrier wait that nothing completes, abandoned after limit_ns.
+cudaError_t launch_wait_probe(unsigned long long limit_ns, cudaStream_t s);
 cudaError_t read_and_clear_stream_status(int *status);
 
 }  // namespace q38

@@ -625,6 +625,23 @@ cudaError_t launch_row_f32_indexed(float *out, const void *w, uint64_t width, ui
                               rows, row_index, type, be, bb, reps < 1 ? 1 : reps, rep_floats);
 }
 
+// Failure-path probe: one thread waits on an mbarrier that nothing arrives
+// at, with the bounded wait every kernel of the library uses, so the wait
+// runs out after `limit_ns` and records kStatusWaitTimeout in the status word.
+__global__ void wait_probe_kernel(unsigned long long limit_ns)
+{
+    __shared__ __align__(8) uint64_t bar;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_wait_bounded(&bar, 0u, &g_status, limit_ns);
+}
+
+cudaError_t launch_wait_probe(unsigned long long limit_ns, cudaStream_t s)
+{
+    wait_probe_kernel<<<1, 1, 0, s>>>(limit_ns);
+    return cudaGetLastError();
+}
+
 cudaError_t read_and_clear_status(int *status, cudaStream_t s)
 {
     cudaError_t e = cudaStreamSynchronize(s);

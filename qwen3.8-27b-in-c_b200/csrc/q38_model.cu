@@ -170,6 +170,16 @@ struct Q38Model {
     std::vector<Q38CuTensor> tensors;  // every uploaded tensor, freed at close
     void *staging = nullptr;
     size_t staging_bytes = 0;
+
+    // Tensor-core prefill (prefill_tc): activations of up to pf_cap tokens,
+    // the fp16 operands of one projection and per-sub-chunk control blocks.
+    int pf_cap = 0;
+    float *pf_hidden = nullptr, *pf_normf = nullptr, *pf_wide = nullptr, *pf_act = nullptr, *pf_ba = nullptr;
+    float *pf_scale = nullptr;
+    void *pf_q8 = nullptr, *pf_q8mix = nullptr, *pf_a16 = nullptr, *pf_b16 = nullptr;
+    uint32_t *pf_ids = nullptr;
+    int *pf_ctl = nullptr, *host_pf_ctl = nullptr;
+    std::vector<void *> pf_owned;
 };
 
 namespace {
@@ -1195,16 +1205,257 @@ bool build_verify_graph(Q38Model *m, int n)
 bool check_status(Q38Model *m)
 {
     if (!cuda_ok(cudaStreamSynchronize(m->stream), "step")) return false;
-    int a = 0, b = 0, c = 0;
+    int a = 0, b = 0, c = 0, d = 0;
     if (!cuda_ok(q38::read_and_clear_model_status(&a), "status") ||
         !cuda_ok(q38::read_and_clear_stream_status(&b), "status") ||
-        !cuda_ok(q38::read_and_clear_status(&c, m->stream), "status"))
+        !cuda_ok(q38::read_and_clear_status(&c, m->stream), "status") ||
+        !cuda_ok(q38::read_and_clear_tc_status(&d), "status"))
         return false;
-    if (a | b | c) return fail("a kernel reported status %s", std::to_string(a | b | c));
+    if (a | b | c | d) return fail("a kernel reported status %s", std::to_string(a | b | c | d));
     return true;
 }
 
 bool use_device(const Q38Model *m) { return cuda_ok(cudaSetDevice(m->device), "cudaSetDevice"); }
+
+// ---------------------------------------------------------------------------
+// Tensor-core prefill
+// ---------------------------------------------------------------------------
+// Prompts of at least kTcPrefillMin tokens (without MTP) run layer-major over
+// chunks of up to kTcChunk tokens, as the upstream prefill does
+// (qwen38_model.c:1519-1560): every projection of a layer is one tensor-core
+// GEMM over the whole chunk (q38_tc.cu: the weights dequantized to fp16 once
+// per chunk, the Q8_K input to fp16, tcgen05.mma with fp32 accumulation);
+// the recurrent mixers run over the chunk's tokens in order, 8 per launch.
+// Results agree with token-by-token decoding to the fp16 operand rounding of
+// the GEMMs (about 1e-4 relative per projection), not bit for bit.
+constexpr int kTcPrefillMin = 64;
+constexpr int kTcChunk = 4096;
+
+size_t tc_a16_elements(const Q38Model *m)
+{
+    size_t most = 0;
+    auto see = [&](const Proj &p) {
+        for (const Part &part : p.parts)
+            most = std::max(most, static_cast<size_t>(part.rows) * static_cast<size_t>(part.t.shape[0]));
+    };
+    for (int l = 0; l < kLayers; ++l) {
+        const Layer &L = m->layers[l];
+        see(L.in_proj);
+        see(L.out);
+        see(L.gate_up);
+        see(L.down);
+    }
+    return most;
+}
+
+template <typename T>
+bool pf_alloc(Q38Model *m, T **p, size_t count)
+{
+    void *q = nullptr;
+    if (!cuda_ok(cudaMalloc(&q, std::max<size_t>(count * sizeof(T), 256)), "cudaMalloc prefill")) return false;
+    m->pf_owned.push_back(q);
+    *p = static_cast<T *>(q);
+    return true;
+}
+
+bool ensure_prefill_buffers(Q38Model *m, int cap)
+{
+    if (m->pf_cap >= cap) return true;
+    for (void *p : m->pf_owned) cudaFree(p);
+    m->pf_owned.clear();
+    m->pf_cap = 0;
+    const size_t n = static_cast<size_t>(cap);
+    const size_t q8 = sizeof(Q38CuQ8KBlock);
+    const int subs = (cap + kMaxTokens - 1) / kMaxTokens;
+    bool ok = pf_alloc(m, &m->pf_hidden, n * kHidden) && pf_alloc(m, &m->pf_normf, n * kHidden) &&
+              pf_alloc(m, &m->pf_wide, n * m->wide_ld) && pf_alloc(m, &m->pf_act, n * kFfn) &&
+              pf_alloc(m, &m->pf_ba, n * m->ba_ld) && pf_alloc(m, &m->pf_scale, n) &&
+              pf_alloc(m, reinterpret_cast<uint8_t **>(&m->pf_q8), n * (kFfn / 256) * q8) &&
+              pf_alloc(m, reinterpret_cast<uint8_t **>(&m->pf_q8mix), n * (kLinV / 256) * q8) &&
+              pf_alloc(m, reinterpret_cast<uint16_t **>(&m->pf_a16), tc_a16_elements(m)) &&
+              pf_alloc(m, reinterpret_cast<uint16_t **>(&m->pf_b16), n * kFfn) && pf_alloc(m, &m->pf_ids, n) &&
+              pf_alloc(m, &m->pf_ctl, static_cast<size_t>(subs) * 4);
+    if (ok && m->host_pf_ctl) {
+        cudaFreeHost(m->host_pf_ctl);
+        m->host_pf_ctl = nullptr;
+    }
+    ok = ok && cuda_ok(cudaMallocHost(&m->host_pf_ctl, static_cast<size_t>(subs) * 4 * sizeof(int) + n * 4),
+                       "cudaMallocHost");
+    if (ok) m->pf_cap = cap;
+    return ok;
+}
+
+// out[t * out_ld + part.offset + row] (+)= projection of tokens 0..n-1, whose
+// input is `q8` (Q8_K [n][width / 256]) and, for float-path parts, the float
+// rows xf.  Q4_K / Q6_K parts run on the tensor cores; other Q8_K types on
+// the streaming batch GEMM; float-path parts on the float kernel.
+bool tc_project(Q38Model *m, const Proj &p, const void *q8, const float *xf, int xf_ld, int n, float *out,
+                int out_ld, int accumulate, bool split_pairs)
+{
+    const cudaStream_t s = m->stream;
+    const int width = p.width;
+    bool staged = false;
+    for (const Part &part : p.parts) {
+        const int type = static_cast<int>(part.t.type);
+        if (part.int_path && q38::tc_weight_type(type)) {
+            if (!staged &&
+                !cuda_ok(q38::launch_q8k_to_f16(q8, width / 256, n, n, m->pf_b16, m->pf_scale, s), "q8k to f16"))
+                return false;
+            staged = true;
+            const uint32_t bb = q38cu_block_bytes(part.t.type);
+            if (!cuda_ok(q38::launch_dequant_f16(part.t.data, type, static_cast<uint64_t>(part.rows),
+                                                 static_cast<uint64_t>(width), part.t.tile_rows,
+                                                 static_cast<int>(bb), m->pf_a16, split_pairs ? 1 : 0, s),
+                         "dequant f16"))
+                return false;
+            q38::TcGemm g;
+            g.out = out + part.offset;
+            g.ld = out_ld;
+            g.n = part.rows;
+            g.m = g.m_pad = n;
+            g.k = width;
+            g.tok_scale = m->pf_scale;
+            g.accumulate = accumulate;
+            if (!cuda_ok(q38::launch_tc_gemm(m->pf_a16, m->pf_b16, g, s), "tensor-core gemm")) return false;
+        } else if (part.int_path) {
+            if (split_pairs) return fail("interleaved gate|up rows need the tensor-core GEMM%s");
+            if (!stream_project(part, q8_input(q8, xf, xf_ld), n, out + part.offset, out_ld, accumulate, OutReps(),
+                                Prefetch(), s))
+                return false;
+        } else {
+            const uint32_t be = q38cu_block_elements(part.t.type), bb = q38cu_block_bytes(part.t.type);
+            if (!cuda_ok(q38::launch_f32_gemm_ex(out + part.offset, out_ld, accumulate, xf, xf_ld, n, width,
+                                                 part.t.data, part.rows, 0, type, static_cast<int>(be),
+                                                 static_cast<int>(bb), s),
+                         "f32 gemm launch"))
+                return false;
+        }
+    }
+    return true;
+}
+
+// One layer over the n tokens of the chunk whose control blocks are pf_ctl.
+bool tc_layer(Q38Model *m, int l, int n)
+{
+    const Layer &L = m->layers[l];
+    const cudaStream_t s = m->stream;
+    const int nb = kHidden / 256;
+    Q38CuQ8KBlock *q8 = static_cast<Q38CuQ8KBlock *>(m->pf_q8);
+    if (!cuda_ok(q38::launch_rmsnorm_quant(m->pf_hidden, kHidden, L.attn_norm, kHidden, n, m->pf_normf, kHidden, q8,
+                                           s, nb),
+                 "rmsnorm") ||
+        !tc_project(m, L.in_proj, q8, m->pf_normf, kHidden, n, m->pf_wide, m->wide_ld, 0, false))
+        return false;
+    if (!L.full && !tc_project(m, L.ba, q8, m->pf_normf, kHidden, n, m->pf_ba, m->ba_ld, 0, false)) return false;
+    Q38CuQ8KBlock *mix = static_cast<Q38CuQ8KBlock *>(m->pf_q8mix);
+    const int mix_nb = kLinV / 256;
+    for (int t0 = 0; t0 < n; t0 += kMaxTokens) {
+        const int k = std::min(kMaxTokens, n - t0);
+        const int *ctl = m->pf_ctl + 4 * (t0 / kMaxTokens);
+        if (L.full) {
+            q38::AttnArgs a{};
+            a.qkv = m->pf_wide + static_cast<size_t>(t0) * m->wide_ld;
+            a.qkv_ld = m->wide_ld;
+            a.k_off = kAttnQg;
+            a.v_off = kAttnQg + kAttnKv;
+            a.q_norm = L.q_norm;
+            a.k_norm = L.k_norm;
+            a.k_cache = m->k_cache + static_cast<size_t>(L.index) * m->context_length * kAttnKv;
+            a.v_cache = m->v_cache + static_cast<size_t>(L.index) * m->context_length * kAttnKv;
+            a.ctl = ctl;
+            a.theta_scale = m->theta_scale;
+            a.tokens = k;
+            a.out_f = m->pf_act + static_cast<size_t>(t0) * kAttnQ;
+            a.out_q = mix + static_cast<size_t>(t0) * mix_nb;
+            a.reps = 1;
+            if (!cuda_ok(q38::launch_attention(a, s), "attention")) return false;
+        } else {
+            q38::DeltaArgs d{};
+            d.beta = m->pf_ba + static_cast<size_t>(t0) * m->ba_ld;
+            d.alpha = d.beta + kLinHeads;
+            d.ba_ld = m->ba_ld;
+            d.qkvz = m->pf_wide + static_cast<size_t>(t0) * m->wide_ld;
+            d.qkvz_ld = m->wide_ld;
+            d.z_off = kLinQkv;
+            d.conv_w = L.conv_w;
+            d.conv_ring = m->conv_ring + static_cast<size_t>(L.index) * kLinQkv * kConvRing;
+            d.dt = L.dt;
+            d.a = L.a;
+            d.norm_w = L.ssm_norm;
+            d.state = m->delta_state + static_cast<size_t>(L.index) * kLinHeads * kLinDim * kLinDim;
+            d.ctl = ctl;
+            d.tokens = k;
+            d.out_f = m->pf_act + static_cast<size_t>(t0) * kLinV;
+            d.out_q = mix + static_cast<size_t>(t0) * mix_nb;
+            d.reps = 1;
+            if (!cuda_ok(q38::launch_deltanet(d, s), "deltanet")) return false;
+        }
+    }
+    if (!tc_project(m, L.out, mix, m->pf_act, kLinV, n, m->pf_hidden, kHidden, 1, false)) return false;
+    if (!cuda_ok(q38::launch_rmsnorm_quant(m->pf_hidden, kHidden, L.post_norm, kHidden, n, m->pf_normf, kHidden, q8,
+                                           s, nb),
+                 "rmsnorm") ||
+        !tc_project(m, L.gate_up, q8, m->pf_normf, kHidden, n, m->pf_wide, m->wide_ld, 0, L.swiglu_fused) ||
+        !cuda_ok(q38::launch_swiglu_quant(m->pf_wide, m->pf_wide + kFfn, m->wide_ld, kFfn, n, m->pf_act, q8, s),
+                 "swiglu"))
+        return false;
+    return tc_project(m, L.down, q8, m->pf_act, kFfn, n, m->pf_hidden, kHidden, 1, false);
+}
+
+bool tc_prefill_enabled()
+{
+    const char *v = std::getenv("Q38CU_TC_PREFILL");
+    return !(v && *v == '0');
+}
+
+// Prefill of `count` tokens from the current position with the tensor-core
+// layer-major path; leaves the last token's logits in m->host_logits.
+bool prefill_tc(Q38Model *m, const uint32_t *tokens, uint32_t count)
+{
+    const uint32_t base = m->position;
+    const cudaStream_t s = m->stream;
+    if (!ensure_prefill_buffers(m, static_cast<int>(std::min<uint32_t>(count, kTcChunk)))) return false;
+    const Q38CuTensor &emb = m->embedding;
+    const uint32_t be = q38cu_block_elements(emb.type), bb = q38cu_block_bytes(emb.type);
+    for (uint32_t done = 0; done < count;) {
+        const int n = static_cast<int>(std::min<uint32_t>(kTcChunk, count - done));
+        const int subs = (n + kMaxTokens - 1) / kMaxTokens;
+        // control blocks of the 8-token mixer launches: [token, position, 0, 0]
+        int *ctl = m->host_pf_ctl;
+        uint32_t *ids = reinterpret_cast<uint32_t *>(ctl + 4 * subs);
+        for (int j = 0; j < subs; ++j) {
+            ctl[4 * j] = static_cast<int>(tokens[done + j * kMaxTokens]);
+            ctl[4 * j + 1] = static_cast<int>(base + done + j * kMaxTokens);
+            ctl[4 * j + 2] = ctl[4 * j + 3] = 0;
+        }
+        std::memcpy(ids, tokens + done, n * sizeof(uint32_t));
+        bool ok = cuda_ok(cudaMemcpyAsync(m->pf_ctl, ctl, subs * 4 * sizeof(int), cudaMemcpyHostToDevice, s),
+                          "control upload") &&
+                  cuda_ok(cudaMemcpyAsync(m->pf_ids, ids, n * sizeof(uint32_t), cudaMemcpyHostToDevice, s),
+                          "ids upload") &&
+                  cuda_ok(q38::launch_row_f32_indexed(m->pf_hidden, emb.data, kHidden, 0, emb.shape[1], m->pf_ids, n,
+                                                      static_cast<int>(emb.type), static_cast<int>(be),
+                                                      static_cast<int>(bb), s),
+                          "embedding");
+        for (int l = 0; ok && l < kLayers; ++l) ok = tc_layer(m, l, n);
+        if (ok && done + n == count) {
+            // logits of the last token (upstream: output norm, LM head)
+            const float *last = m->pf_hidden + static_cast<size_t>(n - 1) * kHidden;
+            ok = cuda_ok(q38::launch_rmsnorm_quant(last, kHidden, m->output_norm, kHidden, 1, m->target_norm, kHidden,
+                                                   m->q8, s),
+                         "rmsnorm") &&
+                 project(m, m->output, q8_input(m->q8, m->target_norm, kHidden), 1, m->logits, kVocab, 0) &&
+                 cuda_ok(cudaMemcpyAsync(m->host_logits, m->logits, static_cast<size_t>(kVocab) * sizeof(float),
+                                         cudaMemcpyDeviceToHost, s),
+                         "logits copy");
+        }
+        // the host control blocks are rewritten by the next chunk
+        if (!ok || !check_status(m)) return false;
+        done += static_cast<uint32_t>(n);
+    }
+    m->position = base + count;
+    return true;
+}
 
 }  // namespace
 
@@ -1267,6 +1518,8 @@ void q38_model_close(Q38Model *m)
     // tensors shared between the target and the MTP head are listed once
     for (auto &t : m->tensors) q38cu_tensor_free(&t);
     for (void *p : m->owned) cudaFree(p);
+    for (void *p : m->pf_owned) cudaFree(p);
+    if (m->host_pf_ctl) cudaFreeHost(m->host_pf_ctl);
     if (m->staging) cudaFree(m->staging);
     if (m->host_logits) cudaFreeHost(m->host_logits);
     if (m->host_ctl) cudaFreeHost(m->host_ctl);
@@ -1327,6 +1580,11 @@ int q38_model_prefill(Q38Model *m, const uint32_t *tokens, uint32_t token_count,
     for (uint32_t i = 0; i < token_count; ++i)
         if (tokens[i] >= kVocab) return 0;
     if (!use_device(m)) return 0;
+    if (token_count >= static_cast<uint32_t>(kTcPrefillMin) && !m->mtp_enabled && tc_prefill_enabled()) {
+        if (!prefill_tc(m, tokens, token_count)) return 0;
+        *logits = m->host_logits;
+        return 1;
+    }
     // Chunks of kMaxTokens tokens go through all layers in turn; the result is
     // the upstream layer-major batch's (qwen38_model.c:1519-1560), since every
     // token only depends on the tokens before it.

@@ -47,8 +47,11 @@ int fail_cuda(const char *what, cudaError_t e)
     return 0;
 }
 
-// Set-up for the current device (first call on that device only).
-int scratch_for_current_device(void **address)
+// Set-up for the current device (first call on that device only).  The
+// address stays valid for the life of the CUDA context: a caller that ends
+// the context (cudaDeviceReset) must not call this entry point again in the
+// same process.
+int scratch_for_current_device(void **address, cudaStream_t stream)
 {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -56,6 +59,14 @@ int scratch_for_current_device(void **address)
     if (dev < 0 || dev >= kMaxDevices) return fail("device index out of range for the no-allocation scratch");
     std::lock_guard<std::mutex> guard(g_setup_lock);
     if (!g_scratch_address[dev]) {
+        // The look-up is not a stream operation and cannot be captured: a
+        // first call made while `stream` is being captured is refused with
+        // the rule rather than with the capture error it would cause.
+        cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+        e = cudaStreamIsCapturing(stream, &capture);
+        if (e != cudaSuccess) return fail_cuda("cudaStreamIsCapturing", e);
+        if (capture != cudaStreamCaptureStatusNone)
+            return fail("the first no-allocation call on a device must come before any stream capture");
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || !p) return fail_cuda("cudaGetSymbolAddress(no-allocation scratch)", e);
@@ -106,7 +117,7 @@ int q38cu_tensor_gemm_q8_k_noalloc(float *output, const Q38CuQ8KBlock *input, ui
                           static_cast<unsigned long long>(Q38CU_NOALLOC_SCRATCH_BYTES));
             return fail(buffer);
         }
-        if (!scratch && !scratch_for_current_device(&scratch)) return 0;
+        if (!scratch && !scratch_for_current_device(&scratch, s)) return 0;
         // The array keeps whatever the previous call left; the tile counters
         // must start at zero.
         e = cudaMemsetAsync(scratch, 0, plan.counter_bytes, s);

@@ -551,9 +551,16 @@ __device__ void swiglu_epilogue(const StreamArgs &g, int t, int rt, int grp, int
     __threadfence();
     consumer_barrier(consumers);
     const int block = t >> 1;
-    if (threadIdx.x == 0) *last_flag = !failed && atomicAdd(&g.sw_counters[block], 1) == 1;
+    // Every CTA counts itself in, failed or not, so the block counter always
+    // returns to zero and a later launch never sees a stale count; a CTA
+    // that abandoned a wait (its sums are unusable, the status word says
+    // so) only skips the quantization.
+    if (threadIdx.x == 0) *last_flag = atomicAdd(&g.sw_counters[block], 1) == 1 ? (failed ? 2 : 1) : 0;
     consumer_barrier(consumers);
-    if (!*last_flag) return;
+    const int last = *last_flag;
+    if (!last) return;
+    if (threadIdx.x == 0) g.sw_counters[block] = 0;
+    if (last != 1 || failed) return;
     __threadfence();
     if (warp < MT && warp < g.tokens) {
         const float *src = g.sw_act + static_cast<size_t>(warp) * g.sw_width + block * 256 + lane * 8;
@@ -572,7 +579,6 @@ __device__ void swiglu_epilogue(const StreamArgs &g, int t, int rt, int grp, int
             if (lane == 0) d->scale = r.scale;
         }
     }
-    if (threadIdx.x == 0) g.sw_counters[block] = 0;
 }
 
 template <typename Dec, int MT, bool kDbg>
@@ -877,9 +883,13 @@ __global__ void __launch_bounds__(StreamThreads<MT, L>::kValue, 1) stream_gemm_k
             }
             __threadfence();
             consumer_barrier(consumers);
-            if (tid == 0) *last_flag = !failed && atomicAdd(&g.counters[t], 1) == n_dep - 1;
+            // Failed or not, every CTA counts its deposit, so the last to
+            // arrive always resets the counter for the next launch; after an
+            // abandoned wait (recorded in the status word) the row is not
+            // stored.
+            if (tid == 0) *last_flag = atomicAdd(&g.counters[t], 1) == n_dep - 1 ? (failed ? 2 : 1) : 0;
             consumer_barrier(consumers);
-            if (*last_flag && grp == 0 && part == 0 && mine_row) {
+            if (*last_flag == 1 && !failed && grp == 0 && part == 0 && mine_row) {
                 __threadfence();
                 const float *base = g.partials + static_cast<size_t>(t) * g.max_slots * MT * g.tile_rows;
 #pragma unroll

@@ -1,0 +1,489 @@
+// q38_tc.cu - tensor-core batch GEMM for prefill (sm_100a tcgen05).
+//
+// Prefill multiplies every weight matrix by a whole prompt chunk (the
+// upstream layer-major batch, src/qwen38/qwen38_model.c:1519-1560, which calls
+// q38_tensor_gemm_q8_k, src/qwen38/qwen38_quant.c:2950-3169, with M = prompt
+// tokens).  At M in the hundreds or thousands this is a dense contraction, so
+// it runs on the 5th-generation tensor cores with dequant-staged operands:
+//
+//   A (weights)     the quantized rows dequantized once per call into fp16
+//                   [N][K] (the upstream float formula of each type, rounded
+//                   to nearest fp16), K-major;
+//   B (activations) the Q8_K blocks of the M tokens dequantized (scale x
+//                   quant, as the upstream integer dot means them) to fp16
+//                   [M][K], each token's row multiplied by a power of two 2^-e
+//                   that puts its largest value in [2^14, 2^15), so no value
+//                   overflows fp16 and the scaling itself rounds nothing;
+//   D               fp32 in tensor memory, times 2^e per token in the
+//                   epilogue, stored batch-major out[token][row] (+= with
+//                   `accumulate`, the residual add of the caller).
+//
+// Each fp16 rounding is a relative error of at most 2^-11, so outputs agree
+// with the upstream integer path to about 1e-4 relative (the north-star bar
+// for final fp32 outputs is 1e-3); per-block integer sums are not formed
+// here - the M <= 8 decode and verification path keeps the exact integer
+// sums.
+//
+// Kernel: one CTA per 128 x BN output tile (128 weight rows, BN tokens),
+// 6 warps: warp 0 lane 0 issues the TMA tile loads (A 128x64, B BNx64 fp16,
+// 128-byte swizzle) into a ring of stages; warp 1 allocates BN tensor-memory
+// columns and its lane 0 issues tcgen05.mma (M = 128, N = BN, K = 16, four per
+// 64-wide stage) and commits each stage back to the producer; warps 2..5 read
+// the accumulator (warp w reads TMEM lanes 32 (w % 4) ..) and store it.  Every
+// mbarrier wait is bounded (2 s): a wait that runs out records the status
+// word, the MMA issuer still commits the accumulator barrier, the producer
+// waits for the copies it issued, and the CTA frees its tensor memory and
+// exits.
+#include <cuda.h>  // CUtensorMap and its enums; the encoder comes from the driver at run time
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "../../include/q38cuda.h"
+#include "q38_device.cuh"
+#include "q38_internal.h"
+#include "q38_types.cuh"
+
+namespace q38 {
+
+__device__ int g_tc_status;  // status word of this file's kernels
+
+namespace {
+
+constexpr int kTcRows = 128;   // UMMA M: weight rows per tile
+constexpr int kTcK = 64;       // fp16 elements per stage row: one 128-byte swizzle span
+constexpr int kTcStages = 4;
+constexpr int kTcThreads = 192;
+
+// ---- TMA, tensor memory and tcgen05 primitives ----------------------------
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t cols)
+{
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)),
+                 "r"(cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] x B[smem]^T, kind::f16 (fp16 inputs, fp32 accumulate).
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on `bar` once every tcgen05.mma this thread issued so far completes.
+__device__ __forceinline__ void mma_commit(uint64_t *bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns of tensor memory.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile stored as the TMA
+// writes it with 128-byte swizzling: rows of 128 bytes, 8-row groups 1024
+// bytes apart (stride byte offset), the leading byte offset unused for this
+// layout (1), descriptor version 1, layout type 2 = 128-byte swizzle.  A
+// K-step of 16 fp16 inside the 128-byte row advances the start address by 32
+// bytes; the swizzle is applied to the absolute address, so the tile must
+// start 1024-byte aligned.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr)
+{
+    return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+           (static_cast<uint64_t>(2) << 61);
+}
+
+// Instruction descriptor: fp32 accumulator (bits 4-5 = 1), A and B fp16
+// (bits 7-9, 10-12 = 0), both K-major (bits 15, 16 = 0), N >> 3 at bits
+// 17-22, M >> 4 at bits 24-28.
+template <int BN> __host__ __device__ constexpr uint32_t f16_idesc()
+{
+    return (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(kTcRows >> 4) << 24);
+}
+
+struct TcArgs {
+    float *out;             // [m][ld]
+    int ld;
+    int n, m, k;            // weight rows, tokens, width
+    const float *tok_scale; // [m]: 2^e of each token's B row
+    int accumulate;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, TcArgs g)
+{
+    constexpr uint32_t kABytes = kTcRows * kTcK * 2, kBBytes = BN * kTcK * 2, kStage = kABytes + kBBytes;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kTcStages * kStage);
+    uint64_t *empty = full + kTcStages;
+    uint64_t *acc_full = empty + kTcStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tok_tiles = (g.m + BN - 1) / BN;
+    const int row0 = (blockIdx.x / tok_tiles) * kTcRows, tok0 = (blockIdx.x % tok_tiles) * BN;
+    const int nk = g.k / kTcK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTcStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();  // A and B were written by the preceding kernels of the stream
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int issued = 0;
+            for (int k = 0; k < nk; ++k) {
+                const int s = k % kTcStages;
+                if (k >= kTcStages &&
+                    !mbar_wait_bounded(&empty[s], static_cast<uint32_t>((k / kTcStages) - 1) & 1u, &g_tc_status))
+                    break;
+                uint8_t *stage = smem + s * kStage;
+                mbar_arrive_expect_tx(&full[s], kStage);
+                tma_load_2d(stage, &map_a, k * kTcK, row0, &full[s]);
+                tma_load_2d(stage + kABytes, &map_b, k * kTcK, tok0, &full[s]);
+                issued = k + 1;
+            }
+            // The copies issued last must land before shared memory goes away.
+            for (int k = issued > kTcStages ? issued - kTcStages : 0; k < issued; ++k)
+                mbar_wait_bounded(&full[k % kTcStages], static_cast<uint32_t>(k / kTcStages) & 1u, &g_tc_status);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            for (int k = 0; k < nk; ++k) {
+                const int s = k % kTcStages;
+                if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(k / kTcStages) & 1u, &g_tc_status)) break;
+                tc_fence_after();
+                const uint32_t a = smem_addr(smem + s * kStage), b = a + kABytes;
+#pragma unroll
+                for (int kk = 0; kk < kTcK / 16; ++kk)
+                    mma_f16(tmem, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), f16_idesc<BN>(),
+                            (k | kk) != 0 ? 1u : 0u);
+                mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+            }
+            mma_commit(acc_full);  // always: the epilogue waits for it
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue: warps 2..5 ----------------
+        const int quarter = warp & 3;  // tensor-memory lanes 32 quarter .. 32 quarter + 31
+        const bool ok = mbar_wait_bounded(acc_full, 0u, &g_tc_status);
+        __syncwarp();
+        tc_fence_after();
+        const int row = row0 + quarter * 32 + lane;
+        for (int c = 0; c < BN / 16; ++c) {
+            uint32_t v[16];
+            tmem_ld16(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(c * 16), v);
+            if (!ok || row >= g.n) continue;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int tok = tok0 + c * 16 + j;
+                if (tok >= g.m) break;
+                float *dst = g.out + static_cast<size_t>(tok) * g.ld + row;
+                const float r = __fmul_rn(__uint_as_float(v[j]), __ldg(g.tok_scale + tok));
+                *dst = g.accumulate ? __fadd_rn(*dst, r) : r;
+            }
+        }
+    }
+    pdl_launch_dependents();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, BN);
+    }
+}
+
+template <int BN> constexpr size_t tc_smem_bytes()
+{
+    return 1024 + static_cast<size_t>(kTcStages) * (kTcRows + BN) * kTcK * 2 + (2 * kTcStages + 1) * 8 + 16;
+}
+
+// ---- operand staging --------------------------------------------------------
+
+__device__ __forceinline__ uint32_t ld_u16(const uint8_t *p) { return p[0] | (p[1] << 8); }
+
+// One 32-element group (a Q4_K sub-block, or two Q6_K sub-blocks of 16) of
+// dequantized weights, as the upstream float path forms them.
+__device__ __forceinline__ void q4k_group(const uint8_t *b, int grp, float (&w)[32])
+{
+    const int chunk = grp >> 1, hi = grp & 1;
+    int sc, m;
+    const uint8_t *p = b + 4;
+    if (grp < 4) {
+        sc = p[grp] & 63;
+        m = p[grp + 4] & 63;
+    } else {
+        sc = (p[grp + 4] & 15) | ((p[grp - 4] >> 6) << 4);
+        m = (p[grp + 4] >> 4) | ((p[grp] >> 6) << 4);
+    }
+    const float d = f16_bits_to_f32(ld_u16(b)), dmin = f16_bits_to_f32(ld_u16(b + 2));
+    const float ds = __fmul_rn(d, static_cast<float>(sc)), dm = __fmul_rn(dmin, static_cast<float>(m));
+    const uint4 *q = reinterpret_cast<const uint4 *>(b + 16 + chunk * 32);
+    uint32_t words[8];
+    // 4-byte-aligned reads: a Q4_K block is 144 bytes and blocks start on 16-byte boundaries
+    const uint32_t *qw = reinterpret_cast<const uint32_t *>(q);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) words[i] = qw[i];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+        const uint32_t byte = (words[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+        const int qv = hi ? static_cast<int>(byte >> 4) : static_cast<int>(byte & 15u);
+        w[e] = __fsub_rn(__fmul_rn(ds, static_cast<float>(qv)), dm);
+    }
+}
+
+__device__ __forceinline__ void q6k_group(const uint8_t *b, int grp, float (&w)[32])
+{
+    const int half = grp >> 2, qq = grp & 3;
+    const float d = f16_bits_to_f32(ld_u16(b + 208));
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+        const uint8_t lb = b[half * 64 + (qq & 1) * 32 + e];
+        const uint8_t hb = b[128 + half * 32 + e];
+        const int q = ((qq < 2 ? (lb & 15) : (lb >> 4)) | (((hb >> (2 * qq)) & 3) << 4)) - 32;
+        const int sc = static_cast<int8_t>(b[192 + half * 8 + qq * 2 + e / 16]);
+        w[e] = __fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q));
+    }
+}
+
+// Weights -> fp16 [rows][width].  One thread per (row, 32-element group).
+// Rows are read in the tiled layout when tile_rows != 0.  With `split`, the
+// rows come interleaved in pairs (gate i, up i) and are written as
+// [gate rows | up rows].
+__global__ void dequant_f16_kernel(const uint8_t *w, int type, uint64_t rows, uint64_t width, uint32_t tile_rows,
+                                   int bb, __half *out, int split)
+{
+    pdl_wait();
+    const uint64_t groups = width / 32, nb = width / 256;
+    const uint64_t total = rows * groups;
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint64_t row = i / groups, g = i - row * groups;
+        const uint64_t blk = g >> 3;
+        const uint8_t *b;
+        if (tile_rows) {
+            const uint64_t t = row / tile_rows, r = row - t * tile_rows;
+            b = w + ((t * nb + blk) * tile_rows + r) * bb;
+        } else {
+            b = w + (row * nb + blk) * bb;
+        }
+        float v[32];
+        if (type == 12) q4k_group(b, static_cast<int>(g & 7), v);
+        else q6k_group(b, static_cast<int>(g & 7), v);
+        const uint64_t orow = split ? ((row & 1) ? rows / 2 + row / 2 : row / 2) : row;
+        __half2 *dst = reinterpret_cast<__half2 *>(out + orow * width + g * 32);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) dst[e] = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+    }
+    pdl_launch_dependents();
+}
+
+// Q8_K blocks [m][nb] -> fp16 [m_pad][nb * 256] times 2^-e per token, and
+// tok_scale[t] = 2^e (rows past m are zero).  One CTA per token row.
+__global__ void __launch_bounds__(256) q8k_to_f16_kernel(const Q8KBlock *in, int nb, int m, __half *out,
+                                                         float *tok_scale)
+{
+    pdl_wait();
+    __shared__ float red[8];
+    const int t = blockIdx.x, tid = threadIdx.x;
+    const int width = nb * 256;
+    __half2 *dst = reinterpret_cast<__half2 *>(out + static_cast<size_t>(t) * width);
+    if (t >= m) {
+        for (int i = tid; i < width / 2; i += blockDim.x) dst[i] = __floats2half2_rn(0.0f, 0.0f);
+        pdl_launch_dependents();
+        return;
+    }
+    const Q8KBlock *row = in + static_cast<size_t>(t) * nb;
+    float amax = 0.0f;
+    for (int b = tid; b < nb; b += blockDim.x) amax = fmaxf(amax, fabsf(row[b].scale));
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((tid & 31) == 0) red[tid >> 5] = amax;
+    __syncthreads();
+    amax = 0.0f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) amax = fmaxf(amax, red[w]);
+    // the largest |value| is at most 127 * amax: bring it into [2^14, 2^15)
+    const float top = __fmul_rn(127.0f, amax);
+    const int e = top > 0.0f ? ilogbf(top) - 14 : 0;
+    if (tid == 0) tok_scale[t] = ldexpf(1.0f, e);
+    for (int i = tid; i < width / 2; i += blockDim.x) {
+        const int k = 2 * i, b = k >> 8, j = k & 255;
+        const float s = ldexpf(row[b].scale, -e);
+        dst[i] = __floats2half2_rn(__fmul_rn(s, static_cast<float>(row[b].quants[j])),
+                                   __fmul_rn(s, static_cast<float>(row[b].quants[j + 1])));
+    }
+    pdl_launch_dependents();
+}
+
+// ---- host side ------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encoder()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D fp16 tensor map [outer][inner], box 64 x box_outer, 128-byte swizzle.
+bool make_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint32_t box_outer)
+{
+    EncodeTiledFn enc = encoder();
+    if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u) || inner % 64) return false;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {inner * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTcK), box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN>
+cudaError_t launch_tc_bn(const void *a16, const void *b16, const TcGemm &p, cudaStream_t s)
+{
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, a16, p.k, p.n, kTcRows) || !make_map(&mb, b16, p.k, p.m_pad, BN)) return cudaErrorInvalidValue;
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [] {
+        attr = cudaFuncSetAttribute(tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(tc_smem_bytes<BN>()));
+    });
+    if (attr != cudaSuccess) return attr;
+    TcArgs g;
+    g.out = p.out;
+    g.ld = p.ld;
+    g.n = p.n;
+    g.m = p.m;
+    g.k = p.k;
+    g.tok_scale = p.tok_scale;
+    g.accumulate = p.accumulate;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(((p.n + kTcRows - 1) / kTcRows) * ((p.m + BN - 1) / BN)));
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = tc_smem_bytes<BN>();
+    cfg.stream = s;
+    cudaLaunchAttribute la[1];
+    la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    la[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = la;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN>, ma, mb, g);
+}
+
+}  // namespace
+
+int tc_token_tile(int m) { return m > 128 ? 256 : 128; }
+
+bool tc_weight_type(int type) { return type == 12 || type == 14; }  // Q4_K, Q6_K
+
+cudaError_t launch_dequant_f16(const void *w, int type, uint64_t rows, uint64_t width, uint32_t tile_rows, int bb,
+                               void *out, int split, cudaStream_t s)
+{
+    if (!tc_weight_type(type) || width % 256 || (split && rows % 2)) return cudaErrorInvalidValue;
+    const uint64_t total = rows * (width / 32);
+    const unsigned grid = static_cast<unsigned>(std::min<uint64_t>((total + 255) / 256, 148ull * 16));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute la[1];
+    la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    la[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = la;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, dequant_f16_kernel, static_cast<const uint8_t *>(w), type, rows, width, tile_rows,
+                              bb, static_cast<__half *>(out), split);
+}
+
+cudaError_t launch_q8k_to_f16(const void *q8, int nb, int m, int m_pad, void *out, float *tok_scale, cudaStream_t s)
+{
+    if (m < 1 || m_pad < m) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(m_pad));
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute la[1];
+    la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    la[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = la;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, q8k_to_f16_kernel, static_cast<const Q8KBlock *>(q8), nb, m,
+                              static_cast<__half *>(out), tok_scale);
+}
+
+cudaError_t launch_tc_gemm(const void *a16, const void *b16, const TcGemm &p, cudaStream_t s)
+{
+    if (p.k % kTcK || p.n < 1 || p.m < 1 || p.m_pad < p.m || !p.out || !p.tok_scale) return cudaErrorInvalidValue;
+    return tc_token_tile(p.m) == 256 ? launch_tc_bn<256>(a16, b16, p, s) : launch_tc_bn<128>(a16, b16, p, s);
+}
+
+cudaError_t read_and_clear_tc_status(int *status)
+{
+    cudaError_t e = cudaMemcpyFromSymbol(status, g_tc_status, sizeof(int));
+    if (e != cudaSuccess) return e;
+    const int zero = 0;
+    return cudaMemcpyToSymbol(g_tc_status, &zero, sizeof(int));
+}
+
+}  // namespace q38

@@ -41,6 +41,10 @@ def _close(a, b):
     (O.Q4_K, 17408, 5120, 1),     # one whole tile per CTA
     (O.Q6_K, 40000, 5120, 3),     # more tiles than SMs: tiles shared between CTAs (uses the scratch)
     (O.Q4_K, 5120, 17408, 2),
+    # more tokens than one launch takes (8 at width 5120, 4 at 17408): the
+    # counters are cleared again before the second launch on the same array
+    (O.Q6_K, 40000, 5120, 12),
+    (O.Q4_K, 5120, 17408, 6),
 ])
 def test_noalloc_matches_regular_entry_point(q38, oracle, qtype, rows, width, batch):
     import torch

@@ -581,7 +581,14 @@ def run_decode(args, rank, world, dist):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     path = model_path(args.mix, rank, dist)
-    m = Model(path, CONTEXT)
+    if world > 1:
+        # one tensor-parallel shard per GPU; rank 0 makes the communicator id
+        from q38b200.model import nccl_unique_id
+        box = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        m = Model(path, CONTEXT, rank=rank, world=world, nccl_id=box[0])
+    else:
+        m = Model(path, CONTEXT)
     stream = torch.cuda.ExternalStream(m.stream)
     prompt = decode_prompt()
     kernels = m.step_kernels

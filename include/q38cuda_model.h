@@ -55,6 +55,38 @@ uint32_t q38_model_context_length(const Q38Model *model);
  * by `count`; the last token is pending, as after the upstream loop. */
 int q38cu_model_generate_greedy(Q38Model *model, uint32_t token_id, uint32_t count, uint32_t *tokens_out);
 
+/* Tensor-parallel decode over 1, 2, 4 or 8 GPUs of one node (no upstream
+ * counterpart: the upstream engine's only parallelism is OpenMP over output
+ * rows, qwen38_model.c:724-739).  One process per GPU; each opens its shard
+ * with the same path, context length, world size and communicator id (from
+ * q38cu_nccl_unique_id on one rank, sent to the others by the caller), with
+ * its own rank, on the CUDA device current at the call.  The returned model
+ * takes every q38_model_* call above, which every rank must make in the same
+ * order with the same arguments; all ranks compute identical logits and
+ * tokens.  Column-parallel projections keep this shard's output rows (DeltaNet
+ * key-head pairs with the value heads that read them, attention query heads
+ * with their KV heads, a slice of the FFN and of the LM head); row-parallel
+ * ones (ssm_out, attn_output, ffn_down) keep this shard's input superblocks
+ * and their partial sums are added by an NCCL all-reduce; the LM head's rows
+ * are gathered.  The MTP head and the tensor-core prefill are single-GPU only
+ * (a tensor-parallel prefill runs the 8-token batch path).  The NCCL library
+ * is loaded at run time (libnccl.so.2). */
+typedef struct {
+    uint32_t rank, world;
+    uint32_t key_heads[16], n_key_heads;        /* DeltaNet key heads, local order */
+    uint32_t value_blocks[24], n_value_blocks;  /* DeltaNet output blocks (value heads 2b, 2b + 1), local order */
+    uint32_t attn_head0, attn_heads;            /* full-attention query heads */
+    uint32_t kv_head0, kv_heads;                /* full-attention KV heads */
+    uint32_t ffn0, ffn;                         /* FFN outputs [ffn0, ffn0 + ffn) */
+    uint32_t vocab0, vocab;                     /* LM head rows */
+} Q38CuTPShard;
+/* What rank `rank` of `world` holds (host only).  1 = ok, 0 = bad arguments. */
+int q38cu_tp_shard(uint32_t rank, uint32_t world, Q38CuTPShard *out);
+/* 128 bytes of communicator id into id_out.  1 = ok. */
+int q38cu_nccl_unique_id(void *id_out);
+Q38Model *q38cu_model_open_tp(const char *path, uint32_t context_length, uint32_t rank, uint32_t world,
+                              const void *nccl_id);
+
 /* The cudaStream_t the model runs on (for event timing by a caller). */
 void *q38cu_model_stream(Q38Model *model);
 

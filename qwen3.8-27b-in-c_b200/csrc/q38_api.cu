@@ -331,9 +331,9 @@ int q38cu_tensor_gemm_q8_k(float *output, const Q38CuQ8KBlock *input, uint32_t b
 uint64_t q38cu_tensor_gemm_q8_k_tc_workspace(uint32_t batch_size, uint64_t input_length, const Q38CuTensor *tensor)
 {
     if (!tensor || !batch_size || tensor->n_dims != 2 || input_length % 256) return 0;
-    const uint64_t a = (tensor->shape[1] * input_length * 2 + 255) / 256 * 256;
-    const uint64_t b = (static_cast<uint64_t>(batch_size) * input_length * 2 + 255) / 256 * 256;
-    return a + b + (static_cast<uint64_t>(batch_size) * 4 + 255) / 256 * 256;
+    const uint64_t a = (tensor->shape[1] * input_length * 4 + 255) / 256 * 256;  // hi and lo fp16
+    const uint64_t b = (static_cast<uint64_t>(batch_size) * input_length * 4 + 255) / 256 * 256;
+    return a + b + (static_cast<uint64_t>(batch_size) * 4 + 255) / 256 * 256 + (tensor->shape[1] * 4 + 255) / 256 * 256;
 }
 
 int q38cu_tensor_gemm_q8_k_tc(float *output, const Q38CuQ8KBlock *input, uint32_t batch_size, uint64_t input_length,
@@ -352,12 +352,14 @@ int q38cu_tensor_gemm_q8_k_tc(float *output, const Q38CuQ8KBlock *input, uint32_
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     uint8_t *ws = static_cast<uint8_t *>(workspace);
     void *a16 = ws;
-    void *b16 = ws + (tensor->shape[1] * input_length * 2 + 255) / 256 * 256;
+    void *b16 = ws + (tensor->shape[1] * input_length * 4 + 255) / 256 * 256;
     float *scale = reinterpret_cast<float *>(static_cast<uint8_t *>(b16) +
-                                             (static_cast<uint64_t>(batch_size) * input_length * 2 + 255) / 256 * 256);
+                                             (static_cast<uint64_t>(batch_size) * input_length * 4 + 255) / 256 * 256);
+    float *row_scale = scale + (static_cast<uint64_t>(batch_size) + 63) / 64 * 64;
     const Geometry g = geometry(tensor->type);
     cudaError_t e = q38::launch_dequant_f16(tensor->data, static_cast<int>(tensor->type), tensor->shape[1],
-                                            input_length, layout_tile_rows(tensor), static_cast<int>(g.bytes), a16, 0, s);
+                                            input_length, layout_tile_rows(tensor), static_cast<int>(g.bytes), a16,
+                                            row_scale, 0, s);
     if (e == cudaSuccess)
         e = q38::launch_q8k_to_f16(input, static_cast<int>(input_length / 256), static_cast<int>(batch_size),
                                    static_cast<int>(batch_size), b16, scale, s);
@@ -369,6 +371,7 @@ int q38cu_tensor_gemm_q8_k_tc(float *output, const Q38CuQ8KBlock *input, uint32_
         p.m = p.m_pad = static_cast<int>(batch_size);
         p.k = static_cast<int>(input_length);
         p.tok_scale = scale;
+        p.row_scale = row_scale;
         p.accumulate = 0;
         e = q38::launch_tc_gemm(a16, b16, p, s);
     }

@@ -130,22 +130,25 @@ cudaError_t launch_repack_tiled(void *dst, const void *src, uint64_t rows, uint6
 int repack_tiled_with(void *dst_tensor, const void *src_tensor, uint32_t tile_rows, void *stream);
 
 // Tensor-core batch GEMM (q38_tc.cu): out[t * ld + row] (+)= sum_k A[row][k]
-// B[t][k] * tok_scale[t], A fp16 [n][k] and B fp16 [m_pad][k] (K-major, k a
-// multiple of 64, both 16-byte aligned).
+// B[t][k] * tok_scale[t] * row_scale[row], A = A_hi + A_lo with A_hi fp16
+// [n][k] followed by A_lo [n][k], B likewise [m_pad][k] twice (K-major, k a
+// multiple of 64, 16-byte aligned).
 struct TcGemm {
     float *out;
     int ld;
     int n, m, m_pad, k;
     const float *tok_scale;
+    const float *row_scale;
     int accumulate;
 };
 bool tc_weight_type(int type);
 int tc_token_tile(int m);
-// Quantized rows (tiled layout when tile_rows != 0) -> fp16 [rows][width];
+// Quantized rows (tiled layout when tile_rows != 0) -> fp16 hi/lo [2][rows][width]
+// scaled by 1 / row_scale[row] (a power of two per row, written here too);
 // split: rows interleaved (gate i, up i) are written as [gate rows | up rows].
 cudaError_t launch_dequant_f16(const void *w, int type, uint64_t rows, uint64_t width, uint32_t tile_rows, int bb,
-                               void *out, int split, cudaStream_t s);
-// Q8_K [m][nb] -> fp16 [m_pad][nb * 256] scaled by 2^-e per token, tok_scale[t] = 2^e.
+                               void *out, float *row_scale, int split, cudaStream_t s);
+// Q8_K [m][nb] -> fp16 hi/lo [2][m_pad][nb * 256] scaled by 2^-e per token, tok_scale[t] = 2^e.
 cudaError_t launch_q8k_to_f16(const void *q8, int nb, int m, int m_pad, void *out, float *tok_scale,
                               cudaStream_t s);
 cudaError_t launch_tc_gemm(const void *a16, const void *b16, const TcGemm &p, cudaStream_t s);

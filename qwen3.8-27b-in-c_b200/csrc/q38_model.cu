@@ -16,12 +16,15 @@
 // streams them all.  Results are unchanged by the merge: every output row is
 // computed by the same per-row arithmetic.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -113,6 +116,117 @@ bool dalloc(T **p, size_t count, std::vector<void *> &owned)
     return cuda_ok(cudaMemset(q, 0, std::max<size_t>(count * sizeof(T), 16)), "cudaMemset");
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-parallel partition (world GPUs, 1, 2, 4 or 8).  Rank r holds:
+//  * DeltaNet: the key-head pairs p = r, r + world, ... of the 8 pairs (key
+//    heads 2p, 2p + 1) and the value heads that read them (value head v reads
+//    key head v % 16, qwen38_model.c:764): value-head pairs (output Q8_K
+//    blocks) p, p + 8, p + 16.  Local order: key heads 2i, 2i + 1 for the
+//    i-th local pair; output block i + n j for pair i and j = 0, 1, 2, so a
+//    local value head still reads local key head (value head % local key
+//    heads) and every output block stays a whole Q8_K block;
+//  * full attention: query heads [24 r / world, 24 (r + 1) / world) and the
+//    KV heads they read (KV head = query head / 6, qwen38_model.c:851);
+//  * FFN: the 256-wide blocks [68 r / world, 68 (r + 1) / world) of the 17408
+//    outputs;
+//  * LM head: rows [248320 r / world, 248320 (r + 1) / world).
+// Column-parallel projections (qkv, z, beta, alpha, q, k, v, gate, up, LM
+// head) keep their local output rows; row-parallel ones (ssm_out,
+// attn_output, ffn_down) keep their local input superblocks, and their
+// partial outputs are summed across the GPUs (one all-reduce of [tokens][5120]
+// after each, two per layer).
+struct Shard {
+    int rank = 0, world = 1;
+    std::vector<int> key_heads;     // local key head -> global
+    std::vector<int> value_blocks;  // local output block -> global (value heads 2b, 2b + 1)
+    int head0 = 0, heads = 24, kv0 = 0, kv_heads = 4;
+    int ffn0 = 0, ffn = kFfn;
+    int vocab0 = 0, vocab = kVocab;
+    int n_kh() const { return static_cast<int>(key_heads.size()); }
+    int n_vh() const { return 2 * static_cast<int>(value_blocks.size()); }
+    int value_head(int local) const { return 2 * value_blocks[local / 2] + local % 2; }
+};
+
+bool make_shard(int rank, int world, Shard *out)
+{
+    if (world != 1 && world != 2 && world != 4 && world != 8) return false;
+    if (rank < 0 || rank >= world) return false;
+    Shard s;
+    s.rank = rank;
+    s.world = world;
+    std::vector<int> pairs;
+    for (int p = rank; p < 8; p += world) pairs.push_back(p);
+    for (int p : pairs) {
+        s.key_heads.push_back(2 * p);
+        s.key_heads.push_back(2 * p + 1);
+    }
+    for (int j = 0; j < 3; ++j)
+        for (int p : pairs) s.value_blocks.push_back(p + 8 * j);
+    s.head0 = 24 * rank / world;
+    s.heads = 24 * (rank + 1) / world - s.head0;
+    s.kv0 = s.head0 / 6;
+    s.kv_heads = (s.head0 + s.heads - 1) / 6 - s.kv0 + 1;
+    const int b0 = (kFfn / 256) * rank / world, b1 = (kFfn / 256) * (rank + 1) / world;
+    s.ffn0 = 256 * b0;
+    s.ffn = 256 * (b1 - b0);
+    s.vocab0 = static_cast<int>(static_cast<long long>(kVocab) * rank / world);
+    s.vocab = static_cast<int>(static_cast<long long>(kVocab) * (rank + 1) / world) - s.vocab0;
+    *out = s;
+    return true;
+}
+
+// A (possibly partial) view of a GGUF tensor: the rows in `rows` and, in each
+// row, the blocks in `cols` (half-open ranges; empty = all), gathered on the
+// host in that order.
+using Ranges = std::vector<std::pair<uint64_t, uint64_t>>;
+
+struct View {
+    const q38::GGUFTensorInfo *info = nullptr;
+    uint32_t type = 0;
+    uint64_t width = 0, rows = 0, nbytes = 0;
+    const uint8_t *data = nullptr;
+    std::vector<uint8_t> owned;
+};
+
+View full_view(const q38::GGUFTensorInfo *t)
+{
+    View v;
+    v.info = t;
+    v.type = t->type;
+    v.width = t->shape[0];
+    v.rows = t->n_dims > 1 ? t->shape[1] : 1;
+    v.nbytes = t->nbytes;
+    v.data = t->data;
+    return v;
+}
+
+View gather_view(const q38::GGUFTensorInfo *t, const Ranges &rows, const Ranges &cols)
+{
+    if (rows.empty() && cols.empty()) return full_view(t);
+    View v = full_view(t);
+    const uint64_t be = q38::ggml_block_elements(t->type), bb = q38::ggml_block_bytes(t->type);
+    const uint64_t all_rows = v.rows, row_bytes = t->nbytes / all_rows;
+    Ranges rr = rows.empty() ? Ranges{{0, all_rows}} : rows;
+    Ranges cc = cols.empty() ? Ranges{{0, t->shape[0] / be}} : cols;
+    uint64_t n_rows = 0, n_blocks = 0;
+    for (const auto &r : rr) n_rows += r.second - r.first;
+    for (const auto &c : cc) n_blocks += c.second - c.first;
+    v.owned.resize(n_rows * n_blocks * bb);
+    uint8_t *dst = v.owned.data();
+    for (const auto &r : rr)
+        for (uint64_t row = r.first; row < r.second; ++row)
+            for (const auto &c : cc) {
+                const uint64_t n = (c.second - c.first) * bb;
+                std::memcpy(dst, t->data + row * row_bytes + c.first * bb, n);
+                dst += n;
+            }
+    v.rows = n_rows;
+    v.width = n_blocks * be;
+    v.nbytes = v.owned.size();
+    v.data = v.owned.data();
+    return v;
+}
+
 }  // namespace
 
 struct Q38Model {
@@ -173,12 +287,20 @@ struct Q38Model {
 
     // Tensor-core prefill (prefill_tc): activations of up to pf_cap tokens,
     // the fp16 operands of one projection and per-sub-chunk control blocks.
+    // Tensor parallelism (q38cu_model_open_tp): this process's shard and
+    // the communicator of the GPUs that hold the others.
+    Shard shard;
+    ncclComm_t comm = nullptr;
+    float *partial = nullptr;       // [kMaxTokens][kHidden]: a row-parallel projection's partial sums
+    float *logits_local = nullptr;  // [kMaxTokens][shard.vocab]
+    int kv_ld = kAttnKv;            // floats per position of this shard's KV cache rows
+    int lin_qkv = kLinQkv, lin_heads = kLinHeads;  // this shard's DeltaNet channels and value heads
+
     int pf_cap = 0;
     float *pf_hidden = nullptr, *pf_normf = nullptr, *pf_wide = nullptr, *pf_act = nullptr, *pf_ba = nullptr;
-    float *pf_scale = nullptr;
+    float *pf_scale = nullptr, *pf_row_scale = nullptr, *pf_oraw = nullptr;
     void *pf_q8 = nullptr, *pf_q8mix = nullptr, *pf_a16 = nullptr, *pf_b16 = nullptr;
-    uint32_t *pf_ids = nullptr;
-    int *pf_ctl = nullptr, *host_pf_ctl = nullptr;
+    uint32_t *pf_ids = nullptr, *host_pf_ids = nullptr;
     std::vector<void *> pf_owned;
 };
 
@@ -236,37 +358,37 @@ uint32_t tile_rows_for(uint64_t rows, uint64_t width)
     return 0;
 }
 
-bool upload_proj(Q38Model *m, Proj *p, const std::vector<const q38::GGUFTensorInfo *> &members)
+bool upload_proj(Q38Model *m, Proj *p, const std::vector<View> &members)
 {
     p->parts.clear();
     p->rows = 0;
-    p->width = static_cast<int>(members[0]->shape[0]);
+    p->width = static_cast<int>(members[0].width);
     size_t i = 0;
     while (i < members.size()) {
         size_t j = i + 1;
-        while (j < members.size() && members[j]->type == members[i]->type) ++j;
-        const uint32_t type = members[i]->type;
+        while (j < members.size() && members[j].type == members[i].type) ++j;
+        const uint32_t type = members[i].type;
         const bool int_path = q8k_type(type);
         if (int_path && !q38::superblock_bytes(static_cast<int>(type)))
-            return fail("tensor %s: this quantization type has no device kernel yet", members[i]->name);
+            return fail("tensor %s: this quantization type has no device kernel yet", members[i].info->name);
         uint64_t rows = 0, bytes = 0;
         for (size_t k = i; k < j; ++k) {
-            rows += members[k]->shape[1];
-            bytes += members[k]->nbytes;
+            rows += members[k].rows;
+            bytes += members[k].nbytes;
         }
         if (!ensure_staging(m, bytes + 256)) return false;
         uint64_t at = 0;
         for (size_t k = i; k < j; ++k) {
-            if (!cuda_ok(cudaMemcpy(static_cast<uint8_t *>(m->staging) + at, members[k]->data, members[k]->nbytes,
+            if (!cuda_ok(cudaMemcpy(static_cast<uint8_t *>(m->staging) + at, members[k].data, members[k].nbytes,
                                     cudaMemcpyHostToDevice),
                          "weight upload"))
                 return false;
-            at += members[k]->nbytes;
+            at += members[k].nbytes;
         }
         Q38CuTensor src{};
         src.type = type;
         src.n_dims = 2;
-        src.shape[0] = members[i]->shape[0];
+        src.shape[0] = members[i].width;
         src.shape[1] = rows;
         src.nbytes = bytes;
         src.data = m->staging;
@@ -311,30 +433,40 @@ bool upload_norm(Q38Model *m, float **dst, const q38::GGUFTensorInfo *t)
 // interleaved (gate i, up i) and tiled 256 rows high, so each CTA's tile
 // yields 128 SwiGLU outputs and the GEMV epilogue forms the FFN activation
 // and its Q8_K blocks itself (q38_stream.cu); otherwise a plain projection.
-bool upload_gate_up(Q38Model *m, Layer *L, const q38::GGUFTensorInfo *gate, const q38::GGUFTensorInfo *up)
+bool upload_gate_up(Q38Model *m, Layer *L, const View &gate, const View &up)
 {
-    const uint64_t rows = gate->shape[1];
-    const bool fusable = gate->type == up->type && q8k_type(gate->type) &&
-                         q38::superblock_bytes(static_cast<int>(gate->type)) && gate->shape[0] == up->shape[0] &&
-                         rows == up->shape[1] && (2 * rows) % 512 == 0 &&
+    const uint64_t rows = gate.rows;
+    // Fused only on one GPU: a shard's slice of the FFN has too few 256-row
+    // tiles to occupy the GPU, so it streams as a plain projection in smaller
+    // tiles and ffn_down forms SwiGLU in its prologue instead.
+    const bool fusable = m->shard.world == 1 && gate.type == up.type && q8k_type(gate.type) &&
+                         q38::superblock_bytes(static_cast<int>(gate.type)) && gate.width == up.width &&
+                         rows == up.rows && (2 * rows) % 512 == 0 &&
                          static_cast<int>(2 * rows / 256) <= q38::device_sm_count();
     L->swiglu_fused = false;
-    if (!fusable) return upload_proj(m, &L->gate_up, {gate, up});
-    const uint64_t row_bytes = gate->nbytes / rows;
-    if (!ensure_staging(m, 2 * gate->nbytes + 256)) return false;
+    if (!fusable) {
+        std::vector<View> members(2);
+        members[0] = gate;
+        members[1] = up;
+        members[0].owned.clear();
+        members[1].owned.clear();
+        return upload_proj(m, &L->gate_up, members);
+    }
+    const uint64_t row_bytes = gate.nbytes / rows;
+    if (!ensure_staging(m, 2 * gate.nbytes + 256)) return false;
     uint8_t *st = static_cast<uint8_t *>(m->staging);
-    if (!cuda_ok(cudaMemcpy2D(st, 2 * row_bytes, gate->data, row_bytes, row_bytes, rows, cudaMemcpyHostToDevice),
+    if (!cuda_ok(cudaMemcpy2D(st, 2 * row_bytes, gate.data, row_bytes, row_bytes, rows, cudaMemcpyHostToDevice),
                  "gate upload") ||
-        !cuda_ok(cudaMemcpy2D(st + row_bytes, 2 * row_bytes, up->data, row_bytes, row_bytes, rows,
+        !cuda_ok(cudaMemcpy2D(st + row_bytes, 2 * row_bytes, up.data, row_bytes, row_bytes, rows,
                               cudaMemcpyHostToDevice),
                  "up upload"))
         return false;
     Q38CuTensor src{};
-    src.type = gate->type;
+    src.type = gate.type;
     src.n_dims = 2;
-    src.shape[0] = gate->shape[0];
+    src.shape[0] = gate.width;
     src.shape[1] = 2 * rows;
-    src.nbytes = 2 * gate->nbytes;
+    src.nbytes = 2 * gate.nbytes;
     src.data = st;
     src.layout = Q38CU_LAYOUT_GGUF;
     Part part;
@@ -346,20 +478,50 @@ bool upload_gate_up(Q38Model *m, Layer *L, const q38::GGUFTensorInfo *gate, cons
     L->gate_up.parts.clear();
     L->gate_up.parts.push_back(part);
     L->gate_up.rows = part.rows;
-    L->gate_up.width = static_cast<int>(gate->shape[0]);
+    L->gate_up.width = static_cast<int>(gate.width);
     L->swiglu_fused = true;
     return true;
 }
 
-bool upload_vec(Q38Model *m, float **dst, const q38::GGUFTensorInfo *t)
+bool upload_vec(Q38Model *m, float **dst, const View &v)
 {
-    if (!dalloc(dst, t->nbytes / 4, m->owned)) return false;
-    return cuda_ok(cudaMemcpy(*dst, t->data, t->nbytes, cudaMemcpyHostToDevice), "vector upload");
+    if (!dalloc(dst, v.nbytes / 4, m->owned)) return false;
+    return cuda_ok(cudaMemcpy(*dst, v.data, v.nbytes, cudaMemcpyHostToDevice), "vector upload");
+}
+
+bool upload_vec(Q38Model *m, float **dst, const q38::GGUFTensorInfo *t) { return upload_vec(m, dst, full_view(t)); }
+
+std::vector<View> views(std::initializer_list<const q38::GGUFTensorInfo *> ts)
+{
+    std::vector<View> out;
+    for (const auto *t : ts) out.push_back(full_view(t));
+    return out;
+}
+
+// The rows of a DeltaNet layer's projections a shard keeps (qkv channels in
+// local order q | k | v, then value rows for z, beta and alpha), see Shard.
+Ranges qkv_rows(const Shard &sh)
+{
+    Ranges r;
+    for (int kh : sh.key_heads) r.push_back({128ull * kh, 128ull * kh + 128});
+    for (int kh : sh.key_heads) r.push_back({2048ull + 128 * kh, 2048ull + 128 * kh + 128});
+    for (int v = 0; v < sh.n_vh(); ++v) r.push_back({4096ull + 128 * sh.value_head(v), 4096ull + 128 * sh.value_head(v) + 128});
+    return r;
+}
+
+Ranges value_rows(const Shard &sh, uint64_t per_head)
+{
+    Ranges r;
+    for (int v = 0; v < sh.n_vh(); ++v)
+        r.push_back({per_head * sh.value_head(v), per_head * sh.value_head(v) + per_head});
+    return r;
 }
 
 bool load_layer(Q38Model *m, const q38::GGUFFile &f, int l)
 {
     Layer &L = m->layers[l];
+    const Shard &sh = m->shard;
+    const bool split = sh.world > 1 && l < kLayers;  // the MTP layer is never split
     L.full = (l + 1) % 4 == 0 || l == kLayers;
     L.index = L.full ? l / 4 : l - (l + 1) / 4;
     auto T = [&](const char *s) { return find_layer(f, l, s); };
@@ -369,14 +531,30 @@ bool load_layer(Q38Model *m, const q38::GGUFFile &f, int l)
               expect(gate, kHidden, kFfn, false) && expect(up, kHidden, kFfn, false) &&
               expect(down, kFfn, kHidden, false);
     if (!ok) return false;
+    const Ranges none;
     if (L.full) {
         const auto *q = T("attn_q.weight"), *k = T("attn_k.weight"), *v = T("attn_v.weight");
         const auto *o = T("attn_output.weight"), *qn = T("attn_q_norm.weight"), *kn = T("attn_k_norm.weight");
         ok = expect(q, kHidden, kAttnQg, false) && expect(k, kHidden, kAttnKv, false) &&
              expect(v, kHidden, kAttnKv, false) && expect(o, kAttnQ, kHidden, false) &&
              expect(qn, kAttnDim, 0, true) && expect(kn, kAttnDim, 0, true);
-        if (!ok || !upload_proj(m, &L.in_proj, {q, k, v}) || !upload_proj(m, &L.out, {o}) ||
-            !upload_vec(m, &L.q_norm, qn) || !upload_vec(m, &L.k_norm, kn))
+        if (!ok) return false;
+        std::vector<View> in;
+        std::vector<View> out;
+        if (split) {
+            const Ranges qr{{512ull * sh.head0, 512ull * (sh.head0 + sh.heads)}};
+            const Ranges kvr{{256ull * sh.kv0, 256ull * (sh.kv0 + sh.kv_heads)}};
+            in.push_back(gather_view(q, qr, none));
+            in.push_back(gather_view(k, kvr, none));
+            in.push_back(gather_view(v, kvr, none));
+            out.push_back(gather_view(o, none, Ranges{{static_cast<uint64_t>(sh.head0),
+                                                      static_cast<uint64_t>(sh.head0 + sh.heads)}}));
+        } else {
+            in = views({q, k, v});
+            out = views({o});
+        }
+        if (!upload_proj(m, &L.in_proj, in) || !upload_proj(m, &L.out, out) || !upload_vec(m, &L.q_norm, qn) ||
+            !upload_vec(m, &L.k_norm, kn))
             return false;
     } else {
         const auto *qkv = T("attn_qkv.weight"), *z = T("attn_gate.weight"), *al = T("ssm_alpha.weight");
@@ -386,13 +564,53 @@ bool load_layer(Q38Model *m, const q38::GGUFFile &f, int l)
              expect(al, kHidden, kLinHeads, false) && expect(be, kHidden, kLinHeads, false) &&
              expect(conv, 4, kLinQkv, true) && expect(dt, kLinHeads, 0, true) && expect(a, kLinHeads, 0, true) &&
              expect(nrm, kLinDim, 0, true) && expect(o, kLinV, kHidden, false);
-        if (!ok || !upload_proj(m, &L.in_proj, {qkv, z}) || !upload_proj(m, &L.ba, {be, al}) ||
-            !upload_proj(m, &L.out, {o}) || !upload_vec(m, &L.conv_w, conv) || !upload_vec(m, &L.dt, dt) ||
-            !upload_vec(m, &L.a, a) || !upload_vec(m, &L.ssm_norm, nrm))
+        if (!ok) return false;
+        std::vector<View> in, ba, out;
+        View conv_v, dt_v, a_v;
+        if (split) {
+            in.push_back(gather_view(qkv, qkv_rows(sh), none));
+            in.push_back(gather_view(z, value_rows(sh, 128), none));
+            ba.push_back(gather_view(be, value_rows(sh, 1), none));
+            ba.push_back(gather_view(al, value_rows(sh, 1), none));
+            Ranges blocks;
+            for (int b : sh.value_blocks) blocks.push_back({static_cast<uint64_t>(b), static_cast<uint64_t>(b) + 1});
+            out.push_back(gather_view(o, none, blocks));
+            conv_v = gather_view(conv, qkv_rows(sh), none);
+            // 1-D vectors: one "row" of 48 single-element blocks
+            Ranges vh;
+            for (int v = 0; v < sh.n_vh(); ++v)
+                vh.push_back({static_cast<uint64_t>(sh.value_head(v)), static_cast<uint64_t>(sh.value_head(v)) + 1});
+            dt_v = gather_view(dt, none, vh);
+            a_v = gather_view(a, none, vh);
+        } else {
+            in = views({qkv, z});
+            ba = views({be, al});
+            out = views({o});
+            conv_v = full_view(conv);
+            dt_v = full_view(dt);
+            a_v = full_view(a);
+        }
+        if (!upload_proj(m, &L.in_proj, in) || !upload_proj(m, &L.ba, ba) || !upload_proj(m, &L.out, out) ||
+            !upload_vec(m, &L.conv_w, conv_v) || !upload_vec(m, &L.dt, dt_v) || !upload_vec(m, &L.a, a_v) ||
+            !upload_vec(m, &L.ssm_norm, nrm))
             return false;
     }
+    View gv, uv, dv;
+    if (split) {
+        const Ranges fr{{static_cast<uint64_t>(sh.ffn0), static_cast<uint64_t>(sh.ffn0 + sh.ffn)}};
+        gv = gather_view(gate, fr, none);
+        uv = gather_view(up, fr, none);
+        dv = gather_view(down, none, Ranges{{static_cast<uint64_t>(sh.ffn0 / 256),
+                                             static_cast<uint64_t>((sh.ffn0 + sh.ffn) / 256)}});
+    } else {
+        gv = full_view(gate);
+        uv = full_view(up);
+        dv = full_view(down);
+    }
+    std::vector<View> dvs;
+    dvs.push_back(std::move(dv));
     return upload_norm(m, &L.attn_norm, attn_norm) && upload_norm(m, &L.post_norm, post_norm) &&
-           upload_gate_up(m, &L, gate, up) && upload_proj(m, &L.down, {down});
+           upload_gate_up(m, &L, gv, uv) && upload_proj(m, &L.down, dvs);
 }
 
 bool meta_is_qwen38(const q38::GGUFFile &f, uint32_t *blocks, uint32_t *nextn)
@@ -432,10 +650,10 @@ bool load_mtp(Q38Model *m, const q38::GGUFFile &f)
     if (&f == &m->gguf) {
         m->mtp_embedding = m->embedding;  // same tensors as the target model's
         m->mtp_output = m->output;
-    } else if (!upload_embedding(m, &m->mtp_embedding, emb) || !upload_proj(m, &m->mtp_output, {out})) {
+    } else if (!upload_embedding(m, &m->mtp_embedding, emb) || !upload_proj(m, &m->mtp_output, views({out}))) {
         return false;
     }
-    if (!load_layer(m, f, kLayers) || !upload_proj(m, &m->eh_proj, {eh}) || !upload_vec(m, &m->enorm, en) ||
+    if (!load_layer(m, f, kLayers) || !upload_proj(m, &m->eh_proj, views({eh})) || !upload_vec(m, &m->enorm, en) ||
         !upload_vec(m, &m->hnorm, hn) || !upload_norm(m, &m->shared_head_norm, sh))
         return false;
     m->mtp_loaded = true;
@@ -449,9 +667,16 @@ bool alloc_runtime(Q38Model *m)
     m->wide_ld = std::max({kLinQkv + kLinV, kAttnQg + 2 * kAttnKv, 2 * kFfn});
     m->ba_ld = 2 * kLinHeads;
     const size_t q8_blocks = kMaxTokens * static_cast<size_t>(kFfn / 256);
-    return dalloc(&m->conv_ring, static_cast<size_t>(kRecurrent) * kLinQkv * kConvRing, o) &&
-           dalloc(&m->delta_state, static_cast<size_t>(kRecurrent) * kLinHeads * kLinDim * kLinDim, o) &&
-           dalloc(&m->k_cache, kFull * ctx * kAttnKv, o) && dalloc(&m->v_cache, kFull * ctx * kAttnKv, o) &&
+    const Shard &sh = m->shard;
+    m->lin_heads = sh.n_vh();
+    m->lin_qkv = 5 * sh.n_kh() * kLinDim;
+    m->kv_ld = 256 * sh.kv_heads;
+    if (sh.world > 1 && (!dalloc(&m->partial, kMaxTokens * kHidden, o) ||
+                         !dalloc(&m->logits_local, kMaxTokens * static_cast<size_t>(sh.vocab), o)))
+        return false;
+    return dalloc(&m->conv_ring, static_cast<size_t>(kRecurrent) * m->lin_qkv * kConvRing, o) &&
+           dalloc(&m->delta_state, static_cast<size_t>(kRecurrent) * m->lin_heads * kLinDim * kLinDim, o) &&
+           dalloc(&m->k_cache, kFull * ctx * m->kv_ld, o) && dalloc(&m->v_cache, kFull * ctx * m->kv_ld, o) &&
            dalloc(&m->mtp_hidden, kHidden, o) && dalloc(&m->hidden, kReps * kMaxTokens * kHidden, o) &&
            dalloc(&m->normf, kMaxTokens * 2 * kHidden, o) &&
            dalloc(&m->wide, kReps * kMaxTokens * static_cast<size_t>(m->wide_ld), o) &&
@@ -780,7 +1005,7 @@ ActIn swiglu_input(const Q38Model *m)
     ActIn in;
     in.mode = q38::kActSwiGLU;
     in.x = m->wide;
-    in.y = m->wide + kFfn;
+    in.y = m->wide + m->shard.ffn;
     in.ld = m->wide_ld;
     in.reps = kReps;
     in.rep_bytes = static_cast<long long>(kMaxTokens) * m->wide_ld * 4;
@@ -791,9 +1016,9 @@ OutReps hidden_out() { return OutReps{kReps, hidden_rep_bytes()}; }
 
 // ssm_beta | ssm_alpha as one Q8_0 tensor: the DeltaNet kernel forms both
 // projections itself.
-bool fusable_ba(const Proj &p)
+bool fusable_ba(const Proj &p, int n_vh)
 {
-    return p.parts.size() == 1 && !p.parts[0].int_path && p.parts[0].t.type == kQ8_0 && p.rows == 2 * kLinHeads &&
+    return p.parts.size() == 1 && !p.parts[0].int_path && p.parts[0].t.type == kQ8_0 && p.rows == 2 * n_vh &&
            p.width == kHidden;
 }
 
@@ -802,7 +1027,7 @@ bool fusable_ba(const Proj &p)
 // integer path with at least one CTA per side row.
 bool side_ba_ok(const Q38Model *m, const Layer &L)
 {
-    if (!fusable_ba(L.ba) || L.in_proj.parts.empty() || !L.in_proj.parts[0].int_path) return false;
+    if (!fusable_ba(L.ba, m->lin_heads) || L.in_proj.parts.empty() || !L.in_proj.parts[0].int_path) return false;
     const Part &p = L.in_proj.parts[0];
     q38::StreamPlan plan;
     if (q38::stream_plan(static_cast<int>(p.t.type), p.rows, static_cast<int>(p.t.shape[0]),
@@ -812,10 +1037,15 @@ bool side_ba_ok(const Q38Model *m, const Layer &L)
     return plan.grid >= L.ba.rows && m->ba_ld >= L.ba.rows;
 }
 
+bool reduce_into_hidden(Q38Model *m, int tokens);
+bool gather_logits(Q38Model *m, int tokens);
+
 bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
 {
     (void)base_hint;
     const Layer &L = m->layers[l];
+    const Shard &sh = m->shard;
+    const bool tp = sh.world > 1 && l < kLayers;
     const cudaStream_t s = m->stream;
     const ActIn attn_in = rmsnorm_input(m->hidden, L.attn_norm);
     // the weight tensor streamed after this layer's ffn_down
@@ -835,17 +1065,24 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
     }
     if (!project(m, L.in_proj, in_proj_in, tokens, m->wide, m->wide_ld, 0, OutReps(), first_part(L.out)))
         return false;
-    const ActIn mixed = q8_input(m->q8, m->act_f, L.full ? kAttnQ : kLinV, true);
+    const int mix_width = L.full ? (tp ? sh.heads * kAttnDim : kAttnQ) : (tp ? m->lin_heads * kLinDim : kLinV);
+    const ActIn mixed = q8_input(m->q8, m->act_f, mix_width, true);
     if (L.full) {
         q38::AttnArgs a{};
         a.qkv = m->wide;
         a.qkv_ld = m->wide_ld;
-        a.k_off = kAttnQg;
-        a.v_off = kAttnQg + kAttnKv;
+        a.k_off = tp ? sh.heads * 2 * kAttnDim : kAttnQg;
+        a.v_off = a.k_off + (tp ? sh.kv_heads * kAttnDim : kAttnKv);
+        if (tp) {
+            a.heads = sh.heads;
+            a.head0 = sh.head0;
+            a.kv0 = sh.kv0;
+            a.kv_ld = m->kv_ld;
+        }
         a.q_norm = L.q_norm;
         a.k_norm = L.k_norm;
-        a.k_cache = m->k_cache + static_cast<size_t>(L.index) * m->context_length * kAttnKv;
-        a.v_cache = m->v_cache + static_cast<size_t>(L.index) * m->context_length * kAttnKv;
+        a.k_cache = m->k_cache + static_cast<size_t>(L.index) * m->context_length * m->kv_ld;
+        a.v_cache = m->v_cache + static_cast<size_t>(L.index) * m->context_length * m->kv_ld;
         a.ctl = m->ctl;
         a.theta_scale = m->theta_scale;
         a.tokens = tokens;
@@ -859,11 +1096,12 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         if (!cuda_ok(q38::launch_attention(a, s), "attention")) return false;
     } else {
         q38::DeltaArgs d{};
+        if (tp) d.n_kh = sh.n_kh();
         if (ba_side) {
             d.beta = m->ba;
-            d.alpha = m->ba + kLinHeads;
+            d.alpha = m->ba + m->lin_heads;
             d.ba_ld = m->ba_ld;
-        } else if (fusable_ba(L.ba)) {
+        } else if (fusable_ba(L.ba, m->lin_heads)) {
             d.ba_fused = 1;
             d.ba_w = static_cast<const uint8_t *>(L.ba.parts[0].t.data);
             d.hidden = m->hidden;
@@ -872,21 +1110,21 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         } else {
             if (!project(m, L.ba, attn_in, tokens, m->ba, m->ba_ld, 0)) return false;
             d.beta = m->ba;
-            d.alpha = m->ba + kLinHeads;
+            d.alpha = m->ba + m->lin_heads;
             d.ba_ld = m->ba_ld;
         }
         d.qkvz = m->wide;
         d.qkvz_ld = m->wide_ld;
-        d.z_off = kLinQkv;
+        d.z_off = m->lin_qkv;
         d.conv_w = L.conv_w;
-        d.conv_ring = m->conv_ring + static_cast<size_t>(L.index) * kLinQkv * kConvRing;
+        d.conv_ring = m->conv_ring + static_cast<size_t>(L.index) * m->lin_qkv * kConvRing;
         d.dt = L.dt;
         d.a = L.a;
         d.norm_w = L.ssm_norm;
-        d.state = m->delta_state + static_cast<size_t>(L.index) * kLinHeads * kLinDim * kLinDim;
+        d.state = m->delta_state + static_cast<size_t>(L.index) * m->lin_heads * kLinDim * kLinDim;
         if (m->snapping && m->delta_snap && L.index < kRecurrent) {
-            d.snap = m->delta_snap + static_cast<size_t>(L.index) * kLinHeads * kLinDim * kLinDim;
-            d.snap_stride = static_cast<long long>(kRecurrent) * kLinHeads * kLinDim * kLinDim;
+            d.snap = m->delta_snap + static_cast<size_t>(L.index) * m->lin_heads * kLinDim * kLinDim;
+            d.snap_stride = static_cast<long long>(kRecurrent) * m->lin_heads * kLinDim * kLinDim;
         }
         d.ctl = m->ctl;
         d.tokens = tokens;
@@ -899,7 +1137,14 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         d.trace = next_trace(m);
         if (!cuda_ok(q38::launch_deltanet(d, s), "deltanet")) return false;
     }
-    if (!project(m, L.out, mixed, tokens, m->hidden, kHidden, 1, hidden_out(), first_part(L.gate_up))) return false;
+    if (tp) {
+        // row-parallel: this shard's partial sums, added up across the GPUs
+        if (!project(m, L.out, mixed, tokens, m->partial, kHidden, 0, OutReps(), first_part(L.gate_up)) ||
+            !reduce_into_hidden(m, tokens))
+            return false;
+    } else if (!project(m, L.out, mixed, tokens, m->hidden, kHidden, 1, hidden_out(), first_part(L.gate_up))) {
+        return false;
+    }
     if (L.swiglu_fused) {
         // gate_up's epilogue leaves silu(gate) * up in act_f and its Q8_K blocks in q8
         SwigluOut sw;
@@ -920,6 +1165,9 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
     if (!project(m, L.gate_up, rmsnorm_input(m->hidden, L.post_norm), tokens, m->wide, m->wide_ld, 0, wide_out,
                  first_part(L.down)))
         return false;
+    if (tp)
+        return project(m, L.down, swiglu_input(m), tokens, m->partial, kHidden, 0, OutReps(), after) &&
+               reduce_into_hidden(m, tokens);
     return project(m, L.down, swiglu_input(m), tokens, m->hidden, kHidden, 1, hidden_out(), after);
 }
 
@@ -942,9 +1190,16 @@ bool enqueue_head(Q38Model *m, const float *norm_w, const Proj &head, int tokens
 {
     const cudaStream_t s = m->stream;
     // the next step starts with layer 0's input projection
-    if (!project(m, head, rmsnorm_input(m->hidden, norm_w, norm_out), tokens, m->logits, kVocab, 0, OutReps(),
-                 first_part(m->layers[0].in_proj)))
+    if (m->shard.world > 1) {
+        // this shard's rows of the LM head, then every GPU gathers all rows
+        if (!project(m, head, rmsnorm_input(m->hidden, norm_w, norm_out), tokens, m->logits_local, m->shard.vocab, 0,
+                     OutReps(), first_part(m->layers[0].in_proj)) ||
+            !gather_logits(m, tokens))
+            return false;
+    } else if (!project(m, head, rmsnorm_input(m->hidden, norm_w, norm_out), tokens, m->logits, kVocab, 0, OutReps(),
+                        first_part(m->layers[0].in_proj))) {
         return false;
+    }
     q38::ArgmaxArgs a{};
     a.logits = m->logits;
     a.ld = kVocab;
@@ -1075,8 +1330,14 @@ bool mtp_step(Q38Model *m, uint32_t token)
     return true;
 }
 
-size_t conv_ring_bytes() { return static_cast<size_t>(kRecurrent) * kLinQkv * kConvRing * sizeof(float); }
-size_t delta_state_bytes() { return static_cast<size_t>(kRecurrent) * kLinHeads * kLinDim * kLinDim * sizeof(float); }
+size_t conv_ring_bytes(const Q38Model *m)
+{
+    return static_cast<size_t>(kRecurrent) * m->lin_qkv * kConvRing * sizeof(float);
+}
+size_t delta_state_bytes(const Q38Model *m)
+{
+    return static_cast<size_t>(kRecurrent) * m->lin_heads * kLinDim * kLinDim * sizeof(float);
+}
 
 // qwen38_model.c:1200-1226
 bool checkpoint_state(Q38Model *m)
@@ -1084,9 +1345,9 @@ bool checkpoint_state(Q38Model *m)
     const cudaStream_t s = m->stream;
     m->ck_position = m->position;
     m->ck_mtp_position = m->mtp_position;
-    return cuda_ok(cudaMemcpyAsync(m->ck_conv_ring, m->conv_ring, conv_ring_bytes(), cudaMemcpyDeviceToDevice, s),
+    return cuda_ok(cudaMemcpyAsync(m->ck_conv_ring, m->conv_ring, conv_ring_bytes(m), cudaMemcpyDeviceToDevice, s),
                    "checkpoint") &&
-           cuda_ok(cudaMemcpyAsync(m->ck_delta_state, m->delta_state, delta_state_bytes(), cudaMemcpyDeviceToDevice,
+           cuda_ok(cudaMemcpyAsync(m->ck_delta_state, m->delta_state, delta_state_bytes(m), cudaMemcpyDeviceToDevice,
                                    s),
                    "checkpoint") &&
            cuda_ok(cudaMemcpyAsync(m->ck_mtp_hidden, m->mtp_hidden, kHidden * sizeof(float), cudaMemcpyDeviceToDevice,
@@ -1098,9 +1359,9 @@ bool restore_target_state(Q38Model *m)
 {
     const cudaStream_t s = m->stream;
     m->position = m->ck_position;
-    return cuda_ok(cudaMemcpyAsync(m->conv_ring, m->ck_conv_ring, conv_ring_bytes(), cudaMemcpyDeviceToDevice, s),
+    return cuda_ok(cudaMemcpyAsync(m->conv_ring, m->ck_conv_ring, conv_ring_bytes(m), cudaMemcpyDeviceToDevice, s),
                    "restore") &&
-           cuda_ok(cudaMemcpyAsync(m->delta_state, m->ck_delta_state, delta_state_bytes(), cudaMemcpyDeviceToDevice,
+           cuda_ok(cudaMemcpyAsync(m->delta_state, m->ck_delta_state, delta_state_bytes(m), cudaMemcpyDeviceToDevice,
                                    s),
                    "restore");
 }
@@ -1217,6 +1478,77 @@ bool check_status(Q38Model *m)
 
 bool use_device(const Q38Model *m) { return cuda_ok(cudaSetDevice(m->device), "cudaSetDevice"); }
 
+// NCCL, loaded at run time: the process that uses PyTorch already holds its
+// libnccl.so.2, any other process gets the system one.
+struct NcclApi {
+    ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*group_start)() = nullptr;
+    ncclResult_t (*group_end)() = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    const char *(*error_string)(ncclResult_t) = nullptr;
+};
+
+const NcclApi *nccl()
+{
+    static NcclApi api;
+    static bool ok = false;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        auto sym = [&](const char *n) { return dlsym(h, n); };
+        api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
+        api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(sym("ncclCommInitRank"));
+        api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(sym("ncclAllReduce"));
+        api.all_gather = reinterpret_cast<decltype(api.all_gather)>(sym("ncclAllGather"));
+        api.group_start = reinterpret_cast<decltype(api.group_start)>(sym("ncclGroupStart"));
+        api.group_end = reinterpret_cast<decltype(api.group_end)>(sym("ncclGroupEnd"));
+        api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
+        api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
+        ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.all_gather && api.group_start &&
+             api.group_end && api.comm_destroy && api.error_string;
+    });
+    return ok ? &api : nullptr;
+}
+
+bool nccl_ok(ncclResult_t r, const char *what)
+{
+    if (r == ncclSuccess) return true;
+    const NcclApi *api = nccl();
+    return fail("%s", std::string(what) + ": " + (api ? api->error_string(r) : "NCCL unavailable"));
+}
+
+// The residual add after a row-parallel projection: the partial sums of all
+// GPUs are added up (all-reduce) and into the hidden rows and their replicas.
+bool reduce_into_hidden(Q38Model *m, int tokens)
+{
+    const NcclApi *api = nccl();
+    return nccl_ok(api->all_reduce(m->partial, m->partial, static_cast<size_t>(tokens) * kHidden, ncclFloat, ncclSum,
+                                   m->comm, m->stream),
+                   "all-reduce") &&
+           cuda_ok(q38::launch_add_replicated(m->hidden, m->partial, kHidden, tokens, kReps, hidden_rep_bytes() / 4,
+                                              m->stream),
+                   "residual add");
+}
+
+// LM head shards -> the full logits rows of every token on every GPU.
+bool gather_logits(Q38Model *m, int tokens)
+{
+    const NcclApi *api = nccl();
+    const size_t n = static_cast<size_t>(m->shard.vocab);
+    if (!nccl_ok(api->group_start(), "group start")) return false;
+    for (int t = 0; t < tokens; ++t)
+        if (!nccl_ok(api->all_gather(m->logits_local + t * n, m->logits + static_cast<size_t>(t) * kVocab, n, ncclFloat,
+                                     m->comm, m->stream),
+                     "all-gather"))
+            return false;
+    return nccl_ok(api->group_end(), "group end");
+}
+
 // ---------------------------------------------------------------------------
 // Tensor-core prefill
 // ---------------------------------------------------------------------------
@@ -1266,21 +1598,20 @@ bool ensure_prefill_buffers(Q38Model *m, int cap)
     m->pf_cap = 0;
     const size_t n = static_cast<size_t>(cap);
     const size_t q8 = sizeof(Q38CuQ8KBlock);
-    const int subs = (cap + kMaxTokens - 1) / kMaxTokens;
     bool ok = pf_alloc(m, &m->pf_hidden, n * kHidden) && pf_alloc(m, &m->pf_normf, n * kHidden) &&
               pf_alloc(m, &m->pf_wide, n * m->wide_ld) && pf_alloc(m, &m->pf_act, n * kFfn) &&
               pf_alloc(m, &m->pf_ba, n * m->ba_ld) && pf_alloc(m, &m->pf_scale, n) &&
               pf_alloc(m, reinterpret_cast<uint8_t **>(&m->pf_q8), n * (kFfn / 256) * q8) &&
               pf_alloc(m, reinterpret_cast<uint8_t **>(&m->pf_q8mix), n * (kLinV / 256) * q8) &&
-              pf_alloc(m, reinterpret_cast<uint16_t **>(&m->pf_a16), tc_a16_elements(m)) &&
-              pf_alloc(m, reinterpret_cast<uint16_t **>(&m->pf_b16), n * kFfn) && pf_alloc(m, &m->pf_ids, n) &&
-              pf_alloc(m, &m->pf_ctl, static_cast<size_t>(subs) * 4);
-    if (ok && m->host_pf_ctl) {
-        cudaFreeHost(m->host_pf_ctl);
-        m->host_pf_ctl = nullptr;
+              pf_alloc(m, reinterpret_cast<uint16_t **>(&m->pf_a16), 2 * tc_a16_elements(m)) &&
+              pf_alloc(m, reinterpret_cast<uint16_t **>(&m->pf_b16), 2 * n * kFfn) &&
+              pf_alloc(m, &m->pf_row_scale, static_cast<size_t>(m->wide_ld)) && pf_alloc(m, &m->pf_ids, n) &&
+              pf_alloc(m, &m->pf_oraw, n * kLinV);
+    if (ok && m->host_pf_ids) {
+        cudaFreeHost(m->host_pf_ids);
+        m->host_pf_ids = nullptr;
     }
-    ok = ok && cuda_ok(cudaMallocHost(&m->host_pf_ctl, static_cast<size_t>(subs) * 4 * sizeof(int) + n * 4),
-                       "cudaMallocHost");
+    ok = ok && cuda_ok(cudaMallocHost(&m->host_pf_ids, n * sizeof(uint32_t)), "cudaMallocHost");
     if (ok) m->pf_cap = cap;
     return ok;
 }
@@ -1305,7 +1636,8 @@ bool tc_project(Q38Model *m, const Proj &p, const void *q8, const float *xf, int
             const uint32_t bb = q38cu_block_bytes(part.t.type);
             if (!cuda_ok(q38::launch_dequant_f16(part.t.data, type, static_cast<uint64_t>(part.rows),
                                                  static_cast<uint64_t>(width), part.t.tile_rows,
-                                                 static_cast<int>(bb), m->pf_a16, split_pairs ? 1 : 0, s),
+                                                 static_cast<int>(bb), m->pf_a16, m->pf_row_scale,
+                                                 split_pairs ? 1 : 0, s),
                          "dequant f16"))
                 return false;
             q38::TcGemm g;
@@ -1315,6 +1647,7 @@ bool tc_project(Q38Model *m, const Proj &p, const void *q8, const float *xf, int
             g.m = g.m_pad = n;
             g.k = width;
             g.tok_scale = m->pf_scale;
+            g.row_scale = m->pf_row_scale;
             g.accumulate = accumulate;
             if (!cuda_ok(q38::launch_tc_gemm(m->pf_a16, m->pf_b16, g, s), "tensor-core gemm")) return false;
         } else if (part.int_path) {
@@ -1334,8 +1667,8 @@ bool tc_project(Q38Model *m, const Proj &p, const void *q8, const float *xf, int
     return true;
 }
 
-// One layer over the n tokens of the chunk whose control blocks are pf_ctl.
-bool tc_layer(Q38Model *m, int l, int n)
+// One layer over the n tokens of the chunk at positions base .. base + n - 1.
+bool tc_layer(Q38Model *m, int l, int n, uint32_t base)
 {
     const Layer &L = m->layers[l];
     const cudaStream_t s = m->stream;
@@ -1349,47 +1682,50 @@ bool tc_layer(Q38Model *m, int l, int n)
     if (!L.full && !tc_project(m, L.ba, q8, m->pf_normf, kHidden, n, m->pf_ba, m->ba_ld, 0, false)) return false;
     Q38CuQ8KBlock *mix = static_cast<Q38CuQ8KBlock *>(m->pf_q8mix);
     const int mix_nb = kLinV / 256;
-    for (int t0 = 0; t0 < n; t0 += kMaxTokens) {
-        const int k = std::min(kMaxTokens, n - t0);
-        const int *ctl = m->pf_ctl + 4 * (t0 / kMaxTokens);
-        if (L.full) {
-            q38::AttnArgs a{};
-            a.qkv = m->pf_wide + static_cast<size_t>(t0) * m->wide_ld;
-            a.qkv_ld = m->wide_ld;
-            a.k_off = kAttnQg;
-            a.v_off = kAttnQg + kAttnKv;
-            a.q_norm = L.q_norm;
-            a.k_norm = L.k_norm;
-            a.k_cache = m->k_cache + static_cast<size_t>(L.index) * m->context_length * kAttnKv;
-            a.v_cache = m->v_cache + static_cast<size_t>(L.index) * m->context_length * kAttnKv;
-            a.ctl = ctl;
-            a.theta_scale = m->theta_scale;
-            a.tokens = k;
-            a.out_f = m->pf_act + static_cast<size_t>(t0) * kAttnQ;
-            a.out_q = mix + static_cast<size_t>(t0) * mix_nb;
-            a.reps = 1;
-            if (!cuda_ok(q38::launch_attention(a, s), "attention")) return false;
-        } else {
-            q38::DeltaArgs d{};
-            d.beta = m->pf_ba + static_cast<size_t>(t0) * m->ba_ld;
-            d.alpha = d.beta + kLinHeads;
-            d.ba_ld = m->ba_ld;
-            d.qkvz = m->pf_wide + static_cast<size_t>(t0) * m->wide_ld;
-            d.qkvz_ld = m->wide_ld;
-            d.z_off = kLinQkv;
-            d.conv_w = L.conv_w;
-            d.conv_ring = m->conv_ring + static_cast<size_t>(L.index) * kLinQkv * kConvRing;
-            d.dt = L.dt;
-            d.a = L.a;
-            d.norm_w = L.ssm_norm;
-            d.state = m->delta_state + static_cast<size_t>(L.index) * kLinHeads * kLinDim * kLinDim;
-            d.ctl = ctl;
-            d.tokens = k;
-            d.out_f = m->pf_act + static_cast<size_t>(t0) * kLinV;
-            d.out_q = mix + static_cast<size_t>(t0) * mix_nb;
-            d.reps = 1;
-            if (!cuda_ok(q38::launch_deltanet(d, s), "deltanet")) return false;
-        }
+    if (!L.full) {
+        // the DeltaNet recurrence over the whole chunk in one launch
+        q38::DeltaPrefillArgs d{};
+        d.qkvz = m->pf_wide;
+        d.qkvz_ld = m->wide_ld;
+        d.z_off = m->lin_qkv;
+        d.beta = m->pf_ba;
+        d.alpha = m->pf_ba + m->lin_heads;
+        d.ba_ld = m->ba_ld;
+        d.conv_w = L.conv_w;
+        d.conv_ring = m->conv_ring + static_cast<size_t>(L.index) * m->lin_qkv * kConvRing;
+        d.dt = L.dt;
+        d.a = L.a;
+        d.norm_w = L.ssm_norm;
+        d.state = m->delta_state + static_cast<size_t>(L.index) * m->lin_heads * kLinDim * kLinDim;
+        d.base = static_cast<int>(base);
+        d.tokens = n;
+        d.o_raw = m->pf_oraw;
+        d.o_ld = m->lin_heads * kLinDim;
+        d.out_f = m->pf_act;
+        d.out_q = mix;
+        if (!cuda_ok(q38::launch_deltanet_prefill(d, s), "deltanet prefill")) return false;
+    }
+    if (L.full) {
+        // full attention of the whole chunk (its keys and values join the caches first)
+        q38::AttnPrefillArgs a{};
+        a.qkv = m->pf_wide;
+        a.qkv_ld = m->wide_ld;
+        a.k_off = kAttnQg;
+        a.v_off = kAttnQg + kAttnKv;
+        a.q_norm = L.q_norm;
+        a.k_norm = L.k_norm;
+        a.k_cache = m->k_cache + static_cast<size_t>(L.index) * m->context_length * m->kv_ld;
+        a.v_cache = m->v_cache + static_cast<size_t>(L.index) * m->context_length * m->kv_ld;
+        a.kv_ld = m->kv_ld;
+        a.heads = 24;
+        a.theta_scale = m->theta_scale;
+        a.base = static_cast<int>(base);
+        a.tokens = n;
+        a.qbuf = m->pf_oraw;
+        a.out_f = m->pf_act;
+        a.out_ld = kAttnQ;
+        a.out_q = mix;
+        if (!cuda_ok(q38::launch_attention_prefill(a, s), "attention prefill")) return false;
     }
     if (!tc_project(m, L.out, mix, m->pf_act, kLinV, n, m->pf_hidden, kHidden, 1, false)) return false;
     if (!cuda_ok(q38::launch_rmsnorm_quant(m->pf_hidden, kHidden, L.post_norm, kHidden, n, m->pf_normf, kHidden, q8,
@@ -1419,25 +1755,14 @@ bool prefill_tc(Q38Model *m, const uint32_t *tokens, uint32_t count)
     const uint32_t be = q38cu_block_elements(emb.type), bb = q38cu_block_bytes(emb.type);
     for (uint32_t done = 0; done < count;) {
         const int n = static_cast<int>(std::min<uint32_t>(kTcChunk, count - done));
-        const int subs = (n + kMaxTokens - 1) / kMaxTokens;
-        // control blocks of the 8-token mixer launches: [token, position, 0, 0]
-        int *ctl = m->host_pf_ctl;
-        uint32_t *ids = reinterpret_cast<uint32_t *>(ctl + 4 * subs);
-        for (int j = 0; j < subs; ++j) {
-            ctl[4 * j] = static_cast<int>(tokens[done + j * kMaxTokens]);
-            ctl[4 * j + 1] = static_cast<int>(base + done + j * kMaxTokens);
-            ctl[4 * j + 2] = ctl[4 * j + 3] = 0;
-        }
-        std::memcpy(ids, tokens + done, n * sizeof(uint32_t));
-        bool ok = cuda_ok(cudaMemcpyAsync(m->pf_ctl, ctl, subs * 4 * sizeof(int), cudaMemcpyHostToDevice, s),
-                          "control upload") &&
-                  cuda_ok(cudaMemcpyAsync(m->pf_ids, ids, n * sizeof(uint32_t), cudaMemcpyHostToDevice, s),
+        std::memcpy(m->host_pf_ids, tokens + done, n * sizeof(uint32_t));
+        bool ok = cuda_ok(cudaMemcpyAsync(m->pf_ids, m->host_pf_ids, n * sizeof(uint32_t), cudaMemcpyHostToDevice, s),
                           "ids upload") &&
                   cuda_ok(q38::launch_row_f32_indexed(m->pf_hidden, emb.data, kHidden, 0, emb.shape[1], m->pf_ids, n,
                                                       static_cast<int>(emb.type), static_cast<int>(be),
                                                       static_cast<int>(bb), s),
                           "embedding");
-        for (int l = 0; ok && l < kLayers; ++l) ok = tc_layer(m, l, n);
+        for (int l = 0; ok && l < kLayers; ++l) ok = tc_layer(m, l, n, base + done);
         if (ok && done + n == count) {
             // logits of the last token (upstream: output norm, LM head)
             const float *last = m->pf_hidden + static_cast<size_t>(n - 1) * kHidden;
@@ -1449,7 +1774,7 @@ bool prefill_tc(Q38Model *m, const uint32_t *tokens, uint32_t count)
                                          cudaMemcpyDeviceToHost, s),
                          "logits copy");
         }
-        // the host control blocks are rewritten by the next chunk
+        // the pinned ids are rewritten by the next chunk
         if (!ok || !check_status(m)) return false;
         done += static_cast<uint32_t>(n);
     }
@@ -1457,14 +1782,20 @@ bool prefill_tc(Q38Model *m, const uint32_t *tokens, uint32_t count)
     return true;
 }
 
-}  // namespace
-
-extern "C" {
-
-Q38Model *q38_model_open_gguf(const char *path, uint32_t context_length)
+Q38Model *open_model(const char *path, uint32_t context_length, int rank, int world, const ncclUniqueId *id)
 {
     if (!path || context_length == 0) return nullptr;
+    Shard shard;
+    if (!make_shard(rank, world, &shard)) {
+        fail("tensor-parallel world must be 1, 2, 4 or 8 and rank below it%s");
+        return nullptr;
+    }
+    if (world > 1 && !nccl()) {
+        fail("libnccl.so.2 could not be loaded%s");
+        return nullptr;
+    }
     Q38Model *m = new Q38Model();
+    m->shard = shard;
     m->context_length = context_length;
     // the RoPE frequency step, evaluated by the host libm as upstream does
     // (qwen38_model.c:699)
@@ -1480,12 +1811,22 @@ Q38Model *q38_model_open_gguf(const char *path, uint32_t context_length)
         ok = emb && on && out && expect(emb, kHidden, kVocab, false) && expect(on, kHidden, 0, true) &&
              expect(out, kHidden, kVocab, false);
         if (!ok && !(emb && on && out)) fail("missing token_embd, output_norm or output tensor%s");
+        std::vector<View> head;
+        head.push_back(world > 1 ? gather_view(out, Ranges{{static_cast<uint64_t>(shard.vocab0),
+                                                             static_cast<uint64_t>(shard.vocab0 + shard.vocab)}},
+                                               Ranges())
+                                 : full_view(out));
         ok = ok && upload_embedding(m, &m->embedding, emb) && upload_norm(m, &m->output_norm, on) &&
-             upload_proj(m, &m->output, {out});
+             upload_proj(m, &m->output, head);
     }
     for (int l = 0; ok && l < kLayers; ++l) ok = load_layer(m, m->gguf, l);
-    if (ok && blocks == kTotalLayers && nextn == 1) ok = load_mtp(m, m->gguf);
+    // the MTP head runs on one GPU only (tensor-parallel models decode without it)
+    if (ok && world == 1 && blocks == kTotalLayers && nextn == 1) ok = load_mtp(m, m->gguf);
     ok = ok && alloc_runtime(m);
+    if (ok && world > 1) {
+        const NcclApi *api = nccl();
+        ok = nccl_ok(api->comm_init_rank(&m->comm, world, *id, rank), "ncclCommInitRank");
+    }
     if (ok) {
         const char *tv = std::getenv("Q38CU_TRACE");
         if (tv && *tv && *tv != '0') {
@@ -1506,6 +1847,61 @@ Q38Model *q38_model_open_gguf(const char *path, uint32_t context_length)
     return m;
 }
 
+}  // namespace
+
+extern "C" {
+
+Q38Model *q38_model_open_gguf(const char *path, uint32_t context_length)
+{
+    return open_model(path, context_length, 0, 1, nullptr);
+}
+
+int q38cu_tp_shard(uint32_t rank, uint32_t world, Q38CuTPShard *out)
+{
+    Shard sh;
+    if (!out || !make_shard(static_cast<int>(rank), static_cast<int>(world), &sh))
+        return fail("tensor-parallel world must be 1, 2, 4 or 8 and rank below it%s");
+    std::memset(out, 0, sizeof(*out));
+    out->rank = rank;
+    out->world = world;
+    out->n_key_heads = static_cast<uint32_t>(sh.key_heads.size());
+    for (size_t i = 0; i < sh.key_heads.size(); ++i) out->key_heads[i] = static_cast<uint32_t>(sh.key_heads[i]);
+    out->n_value_blocks = static_cast<uint32_t>(sh.value_blocks.size());
+    for (size_t i = 0; i < sh.value_blocks.size(); ++i) out->value_blocks[i] = static_cast<uint32_t>(sh.value_blocks[i]);
+    out->attn_head0 = static_cast<uint32_t>(sh.head0);
+    out->attn_heads = static_cast<uint32_t>(sh.heads);
+    out->kv_head0 = static_cast<uint32_t>(sh.kv0);
+    out->kv_heads = static_cast<uint32_t>(sh.kv_heads);
+    out->ffn0 = static_cast<uint32_t>(sh.ffn0);
+    out->ffn = static_cast<uint32_t>(sh.ffn);
+    out->vocab0 = static_cast<uint32_t>(sh.vocab0);
+    out->vocab = static_cast<uint32_t>(sh.vocab);
+    return 1;
+}
+
+int q38cu_nccl_unique_id(void *id_out)
+{
+    if (!id_out) return fail("id_out is NULL%s");
+    const NcclApi *api = nccl();
+    if (!api) return fail("libnccl.so.2 could not be loaded%s");
+    ncclUniqueId id;
+    if (!nccl_ok(api->get_unique_id(&id), "ncclGetUniqueId")) return 0;
+    std::memcpy(id_out, &id, sizeof(id));
+    return 1;
+}
+
+Q38Model *q38cu_model_open_tp(const char *path, uint32_t context_length, uint32_t rank, uint32_t world,
+                              const void *nccl_id)
+{
+    if (world > 1 && !nccl_id) {
+        fail("a tensor-parallel open needs the communicator id from q38cu_nccl_unique_id%s");
+        return nullptr;
+    }
+    ncclUniqueId id;
+    if (nccl_id) std::memcpy(&id, nccl_id, sizeof(id));
+    return open_model(path, context_length, static_cast<int>(rank), static_cast<int>(world), nccl_id ? &id : nullptr);
+}
+
 void q38_model_close(Q38Model *m)
 {
     if (!m) return;
@@ -1516,10 +1912,11 @@ void q38_model_close(Q38Model *m)
     for (auto &g : m->verify_graph)
         if (g) cudaGraphExecDestroy(g);
     // tensors shared between the target and the MTP head are listed once
+    if (m->comm) nccl()->comm_destroy(m->comm);
     for (auto &t : m->tensors) q38cu_tensor_free(&t);
     for (void *p : m->owned) cudaFree(p);
     for (void *p : m->pf_owned) cudaFree(p);
-    if (m->host_pf_ctl) cudaFreeHost(m->host_pf_ctl);
+    if (m->host_pf_ids) cudaFreeHost(m->host_pf_ids);
     if (m->staging) cudaFree(m->staging);
     if (m->host_logits) cudaFreeHost(m->host_logits);
     if (m->host_ctl) cudaFreeHost(m->host_ctl);
@@ -1532,10 +1929,10 @@ void q38_model_reset(Q38Model *m)
 {
     if (!m || !use_device(m)) return;
     const size_t ctx = m->context_length;
-    cudaMemsetAsync(m->conv_ring, 0, static_cast<size_t>(kRecurrent) * kLinQkv * kConvRing * 4, m->stream);
-    cudaMemsetAsync(m->delta_state, 0, static_cast<size_t>(kRecurrent) * kLinHeads * kLinDim * kLinDim * 4, m->stream);
-    cudaMemsetAsync(m->k_cache, 0, kFull * ctx * kAttnKv * 4, m->stream);
-    cudaMemsetAsync(m->v_cache, 0, kFull * ctx * kAttnKv * 4, m->stream);
+    cudaMemsetAsync(m->conv_ring, 0, conv_ring_bytes(m), m->stream);
+    cudaMemsetAsync(m->delta_state, 0, delta_state_bytes(m), m->stream);
+    cudaMemsetAsync(m->k_cache, 0, kFull * ctx * m->kv_ld * 4, m->stream);
+    cudaMemsetAsync(m->v_cache, 0, kFull * ctx * m->kv_ld * 4, m->stream);
     cudaMemsetAsync(m->mtp_hidden, 0, kHidden * 4, m->stream);
     cudaMemsetAsync(m->ctl, 0, 4 * sizeof(int), m->stream);
     cudaStreamSynchronize(m->stream);
@@ -1580,7 +1977,8 @@ int q38_model_prefill(Q38Model *m, const uint32_t *tokens, uint32_t token_count,
     for (uint32_t i = 0; i < token_count; ++i)
         if (tokens[i] >= kVocab) return 0;
     if (!use_device(m)) return 0;
-    if (token_count >= static_cast<uint32_t>(kTcPrefillMin) && !m->mtp_enabled && tc_prefill_enabled()) {
+    if (token_count >= static_cast<uint32_t>(kTcPrefillMin) && !m->mtp_enabled && m->shard.world == 1 &&
+        tc_prefill_enabled()) {
         if (!prefill_tc(m, tokens, token_count)) return 0;
         *logits = m->host_logits;
         return 1;
@@ -1602,8 +2000,10 @@ int q38_model_prefill(Q38Model *m, const uint32_t *tokens, uint32_t token_count,
         if (ok && last) {
             // logits of the last token only
             const Q38CuQ8KBlock *q8 = static_cast<const Q38CuQ8KBlock *>(m->q8) + static_cast<size_t>(n - 1) * nb;
-            ok = project(m, m->output, q8_input(q8, m->target_norm + static_cast<size_t>(n - 1) * kHidden, kHidden),
-                         1, m->logits, kVocab, 0) &&
+            const ActIn last = q8_input(q8, m->target_norm + static_cast<size_t>(n - 1) * kHidden, kHidden);
+            ok = (m->shard.world > 1
+                      ? project(m, m->output, last, 1, m->logits_local, m->shard.vocab, 0) && gather_logits(m, 1)
+                      : project(m, m->output, last, 1, m->logits, kVocab, 0)) &&
                  cuda_ok(cudaMemcpyAsync(m->host_logits, m->logits, static_cast<size_t>(kVocab) * sizeof(float),
                                          cudaMemcpyDeviceToHost, m->stream),
                          "logits copy");
@@ -1623,6 +2023,7 @@ int q38_model_attach_mtp_gguf(Q38Model *m, const char *path)
     if (!m || !path || m->position != 0 || m->mtp_position != 0 || m->mtp_enabled || m->mtp_loaded ||
         m->mtp_gguf.is_open())
         return 0;
+    if (m->shard.world > 1) return fail("the MTP head is not available on a tensor-parallel model%s");
     if (!use_device(m)) return 0;
     uint32_t v = 0;
     bool ok = m->mtp_gguf.open(path);
@@ -1653,15 +2054,16 @@ int q38_model_attach_mtp_gguf(Q38Model *m, const char *path)
 int q38_model_enable_mtp(Q38Model *m)
 {
     if (!m || m->position != 0 || m->mtp_position != 0) return 0;
+    if (m->shard.world > 1) return fail("the MTP head is not available on a tensor-parallel model%s");
     if (!m->mtp_loaded) return fail("MTP weights are unavailable; attach the MTP GGUF first%s");
     if (!use_device(m)) return 0;
     if (!m->ck_conv_ring &&
-        (!dalloc(reinterpret_cast<uint8_t **>(&m->ck_conv_ring), conv_ring_bytes(), m->owned) ||
-         !dalloc(reinterpret_cast<uint8_t **>(&m->ck_delta_state), delta_state_bytes(), m->owned) ||
+        (!dalloc(reinterpret_cast<uint8_t **>(&m->ck_conv_ring), conv_ring_bytes(m), m->owned) ||
+         !dalloc(reinterpret_cast<uint8_t **>(&m->ck_delta_state), delta_state_bytes(m), m->owned) ||
          !dalloc(&m->ck_mtp_hidden, kHidden, m->owned)))
         return fail("unable to allocate speculative checkpoint%s");
     if (!m->delta_snap &&
-        !dalloc(reinterpret_cast<uint8_t **>(&m->delta_snap), (kMaxTokens - 1) * delta_state_bytes(), m->owned))
+        !dalloc(reinterpret_cast<uint8_t **>(&m->delta_snap), (kMaxTokens - 1) * delta_state_bytes(m), m->owned))
         return fail("unable to allocate the speculative state snapshots%s");
     m->mtp_enabled = true;
     return 1;
@@ -1797,8 +2199,8 @@ int q38_model_speculative_greedy(Q38Model *m, uint32_t token_id, uint32_t stop_t
     inputs[0] = token_id;
     for (uint32_t i = 1; i < consumed; ++i) inputs[i] = drafts[i - 1];
     if (consumed < static_cast<uint32_t>(n))
-        ok = cuda_ok(cudaMemcpyAsync(m->delta_state, m->delta_snap + (consumed - 1) * (delta_state_bytes() / 4),
-                                     delta_state_bytes(), cudaMemcpyDeviceToDevice, s),
+        ok = cuda_ok(cudaMemcpyAsync(m->delta_state, m->delta_snap + (consumed - 1) * (delta_state_bytes(m) / 4),
+                                     delta_state_bytes(m), cudaMemcpyDeviceToDevice, s),
                      "state rollback");
     ok = ok &&
          cuda_ok(cudaMemcpyAsync(m->host_logits, m->logits + static_cast<size_t>(consumed - 1) * kVocab,

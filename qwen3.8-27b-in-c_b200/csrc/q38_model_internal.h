@@ -46,6 +46,34 @@ struct DeltaArgs {
     const void *pf_ptr;   // L2 prefetch of the next kernel's leading weights
     long long pf_bytes;
     unsigned long long *trace;  // optional launch timeline record (q38_device.cuh)
+    // Head layout (0 = the whole model: 16 key heads, 24 output blocks).  A
+    // tensor-parallel shard holds n_kh key heads and 3 n_kh value heads in
+    // its own order (qkv rows q | k | v, the value heads of local output
+    // block b being 2b and 2b + 1, key head = value head % n_kh), its output
+    // rows n_kh * 384 floats and n_kh * 3 / 2 Q8_K blocks wide.
+    int n_kh;
+};
+
+// A whole prefill chunk of one DeltaNet layer (deltanet_prefill_kernel): the
+// same layer arguments as DeltaArgs, the chunk's first position `base`, any
+// number of tokens, beta / alpha precomputed per token, and o_raw [tokens][o_ld]
+// for the heads' outputs before their RMSNorm.
+struct DeltaPrefillArgs {
+    const float *qkvz;  // [tokens][qkvz_ld]: q | k | v, z at z_off
+    int qkvz_ld, z_off;
+    const float *beta, *alpha;  // [tokens][ba_ld]
+    int ba_ld;
+    const float *conv_w;  // [channels][4]
+    float *conv_ring;     // [channels][16]
+    const float *dt, *a;  // [value heads]
+    const float *norm_w;  // [128]
+    float *state;         // [value heads][128][128], column-major per head
+    int base, tokens;
+    float *o_raw;         // [tokens][o_ld]
+    int o_ld;             // value heads * 128
+    float *out_f;         // optional [tokens][o_ld]
+    void *out_q;          // [tokens][o_ld / 256] Q8_K
+    int n_kh;             // key heads (0: 16)
 };
 
 struct AttnArgs {
@@ -63,6 +91,31 @@ struct AttnArgs {
     const void *pf_ptr;   // L2 prefetch of the next kernel's leading weights
     long long pf_bytes;
     unsigned long long *trace;  // optional launch timeline record (q38_device.cuh)
+    // Head layout (heads = 0: all 24 query heads, 4 KV heads).  A
+    // tensor-parallel shard holds query heads head0 .. head0 + heads - 1
+    // (rows h * 512 of qkv, local h) and KV heads kv0 .. (global KV head =
+    // global query head / 6), its caches kv_ld floats per position and its
+    // output heads * 256 floats (heads Q8_K blocks) per token.
+    int heads, head0, kv0, kv_ld;
+};
+
+// Full attention over a whole prefill chunk (launch_attention_prefill): the
+// queries of tokens 0 .. tokens - 1 at positions base .. base + tokens - 1
+// attend to the cached positions up to their own; this chunk's keys and
+// values are written into the caches first.
+struct AttnPrefillArgs {
+    const float *qkv;  // [tokens][qkv_ld]: q|gate interleaved per head (512), k at k_off, v at v_off
+    int qkv_ld, k_off, v_off;
+    const float *q_norm, *k_norm;
+    float *k_cache, *v_cache;  // this layer's [context][kv_ld]
+    int kv_ld;                 // 256 * KV heads held
+    int heads, head0, kv0;     // query heads held (global head0 ..), first KV head held
+    float theta_scale;
+    int base, tokens;
+    float *qbuf;     // [tokens][heads][256]: the normed, rotated queries
+    float *out_f;    // [tokens][out_ld]
+    int out_ld;      // heads * 256
+    void *out_q;     // [tokens][heads] Q8_K
 };
 
 struct ArgmaxArgs {
@@ -88,8 +141,15 @@ cudaError_t launch_rmsnorm_quant(const float *in, int in_ld, const float *weight
 cudaError_t launch_swiglu_quant(const float *gate, const float *up, int ld, int n, int tokens, float *out_f,
                                 void *out_q, cudaStream_t s);
 cudaError_t launch_add(float *out, const float *branch, int n, int tokens, cudaStream_t s);
+// hidden[t][i] = hidden[t][i] + branch[t][i] in copy 0 and its reps - 1
+// replicas (rep_floats apart): the residual add after a collective.
+cudaError_t launch_add_replicated(float *hidden, const float *branch, int n, int tokens, int reps,
+                                  long long rep_floats, cudaStream_t s);
 cudaError_t launch_deltanet(const DeltaArgs &args, cudaStream_t s);
+// The recurrence over the chunk, the head norm + gate + Q8_K, the conv ring.
+cudaError_t launch_deltanet_prefill(const DeltaPrefillArgs &args, cudaStream_t s);
 cudaError_t launch_attention(const AttnArgs &args, cudaStream_t s);
+cudaError_t launch_attention_prefill(const AttnPrefillArgs &args, cudaStream_t s);
 cudaError_t launch_argmax(const ArgmaxArgs &args, int tokens, cudaStream_t s);
 cudaError_t read_and_clear_model_status(int *status);
 // Sets `count` timeline records (q38_device.cuh) to their initial values.

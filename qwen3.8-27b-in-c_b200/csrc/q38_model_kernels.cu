@@ -183,6 +183,19 @@ __global__ void add_kernel(float *out, const float *branch, int n)
     if (i < n) out[o] = __fadd_rn(out[o], branch[o]);
 }
 
+// hidden[t][i] += branch[t][i] (one rounding, as upstream), stored into copy 0
+// and the replicas of the hidden rows.
+__global__ void add_replicated_kernel(float *hidden, const float *branch, int n, int reps, long long rep_floats)
+{
+    pdl_wait();
+    pdl_launch_dependents();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const size_t o = static_cast<size_t>(blockIdx.y) * n + i;
+    const float v = __fadd_rn(hidden[o], branch[o]);
+    for (int k = 0; k < reps; ++k) hidden[o + k * rep_floats] = v;
+}
+
 // ---------------------------------------------------------------------------
 // Gated-DeltaNet step (qwen38_model.c:715-792), one token after another for
 // `tokens` tokens at positions base .. base + tokens - 1.
@@ -316,7 +329,7 @@ struct BaBlocks {
 __device__ __forceinline__ void ba_load_blocks(const DeltaArgs &a, int vh, BaBlocks &b)
 {
     const int tid = threadIdx.x, which = tid >> 6, k = tid & 63;
-    const uint8_t *row = a.ba_w + static_cast<size_t>(which * 48 + vh) * 5440;
+    const uint8_t *row = a.ba_w + static_cast<size_t>(which * 3 * (a.n_kh > 0 ? a.n_kh : 16) + vh) * 5440;
 #pragma unroll
     for (int n = 0; n < 3; ++n) {
         const int blk = k + 64 * n;
@@ -357,11 +370,13 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int rank = static_cast<int>(cluster.block_rank());
     const int cidx = blockIdx.x / kDeltaCluster;
-    const int vh = 2 * cidx + rank / 4, quarter = rank & 3, kh = vh % 16;
+    const int n_kh = a.n_kh > 0 ? a.n_kh : 16;           // key heads of this layout
+    const int out_ld = n_kh * 384, out_nb = n_kh * 3 / 2;  // 6144 floats, 24 blocks for the whole model
+    const int vh = 2 * cidx + rank / 4, quarter = rank & 3, kh = vh % n_kh;
     const int col0 = quarter * 32;
-    const bool qk_writer = vh < 16 && quarter == 0;
-    const int ch_q = kh * 128 + tid, ch_k = 2048 + kh * 128 + tid;
-    const int ch_v = 4096 + vh * 128 + col0 + (tid & 31);
+    const bool qk_writer = vh < n_kh && quarter == 0;
+    const int ch_q = kh * 128 + tid, ch_k = n_kh * 128 + kh * 128 + tid;
+    const int ch_v = 2 * n_kh * 128 + vh * 128 + col0 + (tid & 31);
     // Nothing below depends on the previous kernel, so it loads before the
     // grid-dependency wait: the weights, the control block and the recurrent
     // state (written only by launches that completed before the previous
@@ -528,7 +543,7 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
             const int col = col0 + tid;
             o = __fmul_rn(__fmul_rn(o, scale), norm_wc);
             o = __fmul_rn(o, silu(zc));
-            if (a.out_f) a.out_f[static_cast<size_t>(t) * 6144 + vh * 128 + col] = o;
+            if (a.out_f) a.out_f[static_cast<size_t>(t) * out_ld + vh * 128 + col] = o;
             const int e = (rank / 4) * 128 + col;  // index inside the Q8_K block
             AbsMax m = warp_absmax(AbsMax{fabsf(o), e, o});
             if (tid == 0) sh.block_part = m;
@@ -545,7 +560,7 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
             for (int r = 1; r < kDeltaCluster; ++r)
                 best = better(best, AbsMax{__shfl_sync(0xffffffffu, part.a, r), __shfl_sync(0xffffffffu, part.i, r),
                                            __shfl_sync(0xffffffffu, part.v, r)});
-            Q8KBlock *dst = static_cast<Q8KBlock *>(a.out_q) + static_cast<size_t>(t) * 24 + cidx;
+            Q8KBlock *dst = static_cast<Q8KBlock *>(a.out_q) + static_cast<size_t>(t) * out_nb + cidx;
             int q = 0;
             float inverse = 0.0f;
             if (best.a != 0.0f) {
@@ -569,6 +584,217 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
     for (int j = 0; j < 8; ++j) *reinterpret_cast<float4 *>(state + j * 128) = s[j];
     cluster.sync();  // peers may still read this CTA's exchange slots
     trace_mark(a.trace, kTraceEnd);
+}
+
+// ---------------------------------------------------------------------------
+// Gated-DeltaNet over a whole prefill chunk (qwen38_model.c:715-792 for each
+// token of the chunk in order, as q38_batch_layer runs it, :1078-1085).
+//
+// The recurrence is serial in tokens but independent per state column: with
+// q, k, v, beta and the decay of a token known, column j of a head's state
+// only needs its own 128 values.  So each warp owns 8 columns of one value
+// head (lane l holds rows 4l .. 4l + 3 of each, in registers for the whole
+// chunk) and walks all the chunk's tokens without any exchange between warps:
+// per token it forms the causal conv + SiLU of its key head's 128 q and k
+// channels (4 per lane) and of its 8 v channels, their L2 norms (warp
+// reductions), beta and the decay, applies the delta rule to its columns and
+// stores the raw head output (before the head RMSNorm).  The next token's
+// inputs are loaded while the current one is processed.  The token-parallel
+// rest - head RMSNorm, the gate and Q8_K - runs afterwards over all tokens at
+// once (deltanet_prefill_post_kernel), and the conv ring is written by a
+// third kernel once every reader is done (deltanet_ring_store_kernel).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) deltanet_prefill_kernel(DeltaPrefillArgs a)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int n_kh = a.n_kh > 0 ? a.n_kh : 16;
+    const int vh = blockIdx.x >> 2, col0 = (blockIdx.x & 3) * 32 + warp * 8;
+    const int kh = vh % n_kh;
+    const int ch_q = kh * 128 + lane * 4, ch_k = n_kh * 128 + kh * 128 + lane * 4;
+    const int ch_v = 2 * n_kh * 128 + vh * 128 + col0 + (lane & 7);  // lanes 0..7: one v channel each
+    const int base = a.base;
+    // conv kernels of this lane's channels
+    float4 wq[4], wk[4], wv;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        wq[i] = __ldg(reinterpret_cast<const float4 *>(a.conv_w) + ch_q + i);
+        wk[i] = __ldg(reinterpret_cast<const float4 *>(a.conv_w) + ch_k + i);
+    }
+    wv = __ldg(reinterpret_cast<const float4 *>(a.conv_w) + ch_v);
+    // the state columns
+    float *state = a.state + (static_cast<size_t>(vh) * 128 + col0) * 128 + lane * 4;
+    float4 s[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j] = *reinterpret_cast<const float4 *>(state + j * 128);
+    const float a_h = a.a[vh], dt_h = a.dt[vh];
+    const float query_scale = __fdiv_rn(1.0f, sqrtf(128.0f));
+    pdl_wait();
+
+    // the conv window of each channel: inputs of positions p - 3, p - 2, p - 1
+    // (from the ring before the chunk start, from the projections after)
+    auto input = [&](int ch, int p) -> float {
+        return p >= base ? a.qkvz[static_cast<size_t>(p - base) * a.qkvz_ld + ch]
+                         : a.conv_ring[static_cast<size_t>(ch) * 16 + (p & 15)];
+    };
+    float hq[4][3], hk[4][3], hv[3];
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+        const int p = base - 3 + d;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            hq[i][d] = p >= 0 ? input(ch_q + i, p) : 0.0f;
+            hk[i][d] = p >= 0 ? input(ch_k + i, p) : 0.0f;
+        }
+        hv[d] = p >= 0 ? input(ch_v, p) : 0.0f;
+    }
+    // token 0's inputs
+    float4 xq = *reinterpret_cast<const float4 *>(a.qkvz + ch_q);
+    float4 xk = *reinterpret_cast<const float4 *>(a.qkvz + ch_k);
+    float xv = a.qkvz[ch_v];
+    float br = a.beta[vh], ar = a.alpha[vh];
+    for (int t = 0; t < a.tokens; ++t) {
+        // the next token's inputs, in flight during this token's work
+        float4 nq = xq, nk = xk;
+        float nv = xv, nbr = br, nar = ar;
+        if (t + 1 < a.tokens) {
+            const float *row = a.qkvz + static_cast<size_t>(t + 1) * a.qkvz_ld;
+            nq = *reinterpret_cast<const float4 *>(row + ch_q);
+            nk = *reinterpret_cast<const float4 *>(row + ch_k);
+            nv = row[ch_v];
+            nbr = a.beta[static_cast<size_t>(t + 1) * a.ba_ld + vh];
+            nar = a.alpha[static_cast<size_t>(t + 1) * a.ba_ld + vh];
+        }
+        // causal conv + SiLU ((s0 k0 + s1 k1) + s2 k2) + x k3, qwen38_model.c:722-737
+        const float xqa[4] = {xq.x, xq.y, xq.z, xq.w}, xka[4] = {xk.x, xk.y, xk.z, xk.w};
+        float qv[4], kv[4];
+        double pq = 0.0, pk = 0.0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float c = __fmul_rn(hq[i][0], wq[i].x);
+            c = __fadd_rn(c, __fmul_rn(hq[i][1], wq[i].y));
+            c = __fadd_rn(c, __fmul_rn(hq[i][2], wq[i].z));
+            qv[i] = silu(__fadd_rn(c, __fmul_rn(xqa[i], wq[i].w)));
+            float e = __fmul_rn(hk[i][0], wk[i].x);
+            e = __fadd_rn(e, __fmul_rn(hk[i][1], wk[i].y));
+            e = __fadd_rn(e, __fmul_rn(hk[i][2], wk[i].z));
+            kv[i] = silu(__fadd_rn(e, __fmul_rn(xka[i], wk[i].w)));
+            pq += static_cast<double>(__fmul_rn(qv[i], qv[i]));
+            pk += static_cast<double>(__fmul_rn(kv[i], kv[i]));
+            hq[i][0] = hq[i][1];
+            hq[i][1] = hq[i][2];
+            hq[i][2] = xqa[i];
+            hk[i][0] = hk[i][1];
+            hk[i][1] = hk[i][2];
+            hk[i][2] = xka[i];
+        }
+        float cv = __fmul_rn(hv[0], wv.x);
+        cv = __fadd_rn(cv, __fmul_rn(hv[1], wv.y));
+        cv = __fadd_rn(cv, __fmul_rn(hv[2], wv.z));
+        const float vcol = silu(__fadd_rn(cv, __fmul_rn(xv, wv.w)));
+        hv[0] = hv[1];
+        hv[1] = hv[2];
+        hv[2] = xv;
+        // L2 norms of q and k (qwen38_model.c:608-614)
+        const double sq = warp_sum_d(pq), sk = warp_sum_d(pk);
+        const float scale_q = __fdiv_rn(1.0f, fmaxf(sqrtf(static_cast<float>(sq)), kRmsEps));
+        const float scale_k = __fdiv_rn(1.0f, fmaxf(sqrtf(static_cast<float>(sk)), kRmsEps));
+        const float4 q4 = make_float4(__fmul_rn(qv[0], scale_q), __fmul_rn(qv[1], scale_q), __fmul_rn(qv[2], scale_q),
+                                      __fmul_rn(qv[3], scale_q));
+        const float4 k4 = make_float4(__fmul_rn(kv[0], scale_k), __fmul_rn(kv[1], scale_k), __fmul_rn(kv[2], scale_k),
+                                      __fmul_rn(kv[3], scale_k));
+        // beta and the decay (qwen38_model.c:748-752)
+        const float beta = sigmoid(br);
+        const float decay = expf(__fmul_rn(a_h, softplus(__fadd_rn(ar, dt_h))));
+        // delta rule on the warp's 8 columns (qwen38_model.c:758-781)
+        float red[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float4 &x = s[j];
+            x.x = __fmul_rn(x.x, decay);
+            x.y = __fmul_rn(x.y, decay);
+            x.z = __fmul_rn(x.z, decay);
+            x.w = __fmul_rn(x.w, decay);
+            red[j] = fmaf(x.w, k4.w, fmaf(x.z, k4.z, fmaf(x.y, k4.y, __fmul_rn(x.x, k4.x))));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) red[j] = __fadd_rn(red[j], __shfl_xor_sync(0xffffffffu, red[j], o));
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float4 &x = s[j];
+            const float vj = __shfl_sync(0xffffffffu, vcol, j);
+            const float delta = __fmul_rn(__fsub_rn(vj, red[j]), beta);
+            x.x = fmaf(k4.x, delta, x.x);
+            x.y = fmaf(k4.y, delta, x.y);
+            x.z = fmaf(k4.z, delta, x.z);
+            x.w = fmaf(k4.w, delta, x.w);
+            red[j] = fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, __fmul_rn(x.x, q4.x))));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) red[j] = __fadd_rn(red[j], __shfl_xor_sync(0xffffffffu, red[j], o));
+        }
+        if (lane < 8) {
+            float mine = red[0];
+#pragma unroll
+            for (int j = 1; j < 8; ++j)
+                if (lane == j) mine = red[j];
+            a.o_raw[static_cast<size_t>(t) * a.o_ld + vh * 128 + col0 + lane] = __fmul_rn(mine, query_scale);
+        }
+        xq = nq;
+        xk = nk;
+        xv = nv;
+        br = nbr;
+        ar = nar;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) *reinterpret_cast<float4 *>(state + j * 128) = s[j];
+    pdl_launch_dependents();
+}
+
+// Head RMSNorm (qwen38_model.c:783-789), the gate silu(z) and the Q8_K block of
+// each (token, output block): one CTA of 256 threads per (block, token);
+// threads 0..127 hold value head 2b, 128..255 head 2b + 1.
+__global__ void __launch_bounds__(256) deltanet_prefill_post_kernel(DeltaPrefillArgs a)
+{
+    __shared__ double red_d[8];
+    __shared__ AbsMax red_m[8];
+    pdl_wait();
+    const int b = blockIdx.x, t = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int col = b * 256 + tid;  // value head col / 128, column col % 128
+    float o = a.o_raw[static_cast<size_t>(t) * a.o_ld + col];
+    const float z = a.qkvz[static_cast<size_t>(t) * a.qkvz_ld + a.z_off + col];
+    // the head's sum of squares: 4 warps per head, warp partials in order
+    double part = warp_sum_d(static_cast<double>(__fmul_rn(o, o)));
+    if (lane == 0) red_d[warp] = part;
+    __syncthreads();
+    const int h0 = (tid >> 7) * 4;
+    const double sum = ((red_d[h0] + red_d[h0 + 1]) + red_d[h0 + 2]) + red_d[h0 + 3];
+    const float mean = static_cast<float>(sum / 128.0);
+    const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps)));
+    o = __fmul_rn(__fmul_rn(o, scale), a.norm_w[tid & 127]);
+    o = __fmul_rn(o, silu(z));
+    if (a.out_f) a.out_f[static_cast<size_t>(t) * a.o_ld + col] = o;
+    quantize_block_256(o, static_cast<Q8KBlock *>(a.out_q) + static_cast<size_t>(t) * (a.o_ld / 256) + b, red_m);
+    pdl_launch_dependents();
+}
+
+// The conv ring after a chunk: slot p % 16 of every channel takes the input of
+// position p for the chunk's last 16 positions (those inside the chunk).
+__global__ void deltanet_ring_store_kernel(DeltaPrefillArgs a, int channels)
+{
+    pdl_wait();
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+    if (ch < channels) {
+        const int first = a.tokens > 16 ? a.tokens - 16 : 0;
+        for (int t = first; t < a.tokens; ++t)
+            a.conv_ring[static_cast<size_t>(ch) * 16 + ((a.base + t) & 15)] =
+                a.qkvz[static_cast<size_t>(t) * a.qkvz_ld + ch];
+    }
+    pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
@@ -651,8 +877,11 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
     const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
     const int split = static_cast<int>(cluster.block_rank());
     const int th = blockIdx.x / kAttnSplits;
-    const int h = th % kAttnHeads, t = th / kAttnHeads;
-    const int g = h / (kAttnHeads / 4);
+    const int heads = a.heads > 0 ? a.heads : kAttnHeads;
+    const int kv_ld = a.heads > 0 ? a.kv_ld : 1024, out_ld = heads * 256;
+    const int h = th % heads, t = th / heads;
+    const int gh = (a.heads > 0 ? a.head0 : 0) + h;                          // global query head
+    const int g = gh / (kAttnHeads / 4) - (a.heads > 0 ? a.kv0 : 0);         // local KV head
     if (d == 0) prefetch_share_l2(a.pf_ptr, a.pf_bytes);  // keeps HBM busy through this latency-bound step
 
     pdl_wait();
@@ -663,7 +892,8 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
     const int chunk = (len + active - 1) / active;
     const int p0 = min(len, split * chunk), p1 = min(len, p0 + chunk);
     const float *row = a.qkv + static_cast<size_t>(t) * a.qkv_ld;
-    const bool writer = (h % (kAttnHeads / 4)) == 0 && split == 0;
+    // one writer per KV head: the first of its query heads held here
+    const bool writer = (h == 0 || gh % (kAttnHeads / 4) == 0) && split == 0;
 
     if (split < active) {
         const float gate = row[h * 512 + 256 + d];  // loaded with the query, used by rank 0
@@ -685,8 +915,8 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
             sh.knew[tt][d] = kx;
             sh.vnew[tt][d] = vx;
             if (writer && tt == t) {
-                a.k_cache[static_cast<size_t>(pp) * 1024 + g * 256 + d] = kx;
-                a.v_cache[static_cast<size_t>(pp) * 1024 + g * 256 + d] = vx;
+                a.k_cache[static_cast<size_t>(pp) * kv_ld + g * 256 + d] = kx;
+                a.v_cache[static_cast<size_t>(pp) * kv_ld + g * 256 + d] = vx;
             }
         }
         __syncthreads();
@@ -704,8 +934,8 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const int pk = min(p + k, p1 - 1);  // past the range: a valid row, masked below
-                const float *kr = pk < base ? a.k_cache + static_cast<size_t>(pk) * 1024 + g * 256 : sh.knew[pk - base];
-                const float *vr = pk < base ? a.v_cache + static_cast<size_t>(pk) * 1024 + g * 256 : sh.vnew[pk - base];
+                const float *kr = pk < base ? a.k_cache + static_cast<size_t>(pk) * kv_ld + g * 256 : sh.knew[pk - base];
+                const float *vr = pk < base ? a.v_cache + static_cast<size_t>(pk) * kv_ld + g * 256 : sh.vnew[pk - base];
                 ka[k] = *reinterpret_cast<const float4 *>(kr + lane * 4);
                 kb[k] = *reinterpret_cast<const float4 *>(kr + 128 + lane * 4);
                 va[k] = *reinterpret_cast<const float4 *>(vr + lane * 4);
@@ -780,8 +1010,8 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
             }
             float o = __fdiv_rn(num, den);
             o = __fmul_rn(o, sigmoid(gate));
-            if (a.out_f) a.out_f[static_cast<size_t>(t) * 6144 + h * 256 + d] = o;
-            quantize_block_256(o, static_cast<Q8KBlock *>(a.out_q) + static_cast<size_t>(t) * 24 + h, sh.red_m,
+            if (a.out_f) a.out_f[static_cast<size_t>(t) * out_ld + h * 256 + d] = o;
+            quantize_block_256(o, static_cast<Q8KBlock *>(a.out_q) + static_cast<size_t>(t) * heads + h, sh.red_m,
                                a.reps, a.q_rep_bytes);
         }
     } else {
@@ -790,6 +1020,133 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
     }
     cluster.sync();  // rank 0 has read every peer's state
     trace_mark(a.trace, kTraceEnd);
+}
+
+// ---------------------------------------------------------------------------
+// Full attention over a whole prefill chunk (qwen38_model.c:816-885 for each
+// token of the chunk): three kernels.
+//  1. attn_prefill_qk_kernel: per (token, head) the query's RMSNorm + RoPE into
+//     qbuf, and per (token, KV head) the key's RMSNorm + RoPE and the value into
+//     the KV cache at the token's position (one CTA of 256 threads each).
+//  2. attn_prefill_kernel: a CTA takes 8 consecutive query tokens (one per
+//     warp) of one head and walks the cached positions 0 .. its last query's
+//     position in tiles of 32 (K transposed and V staged in shared memory):
+//     lane l scores position p0 + l against the warp's query, the warp keeps a
+//     running softmax and lane l accumulates dimensions 8l .. 8l + 7 of the
+//     weighted values; positions past a query's own are masked.  Then the
+//     sigmoid gate, into out_f.
+//  3. attn_prefill_quant_kernel: the Q8_K block of each (token, head).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) attn_prefill_qk_kernel(AttnPrefillArgs a)
+{
+    __shared__ float tmp[kAttnDim];
+    __shared__ double red[8];
+    pdl_wait();
+    const int t = blockIdx.y, which = blockIdx.x, d = threadIdx.x;
+    const int pos = a.base + t;
+    const float *row = a.qkv + static_cast<size_t>(t) * a.qkv_ld;
+    if (which < a.heads) {
+        const float q = norm_rope(row[which * 512 + d], a.q_norm, pos, a.theta_scale, tmp, red);
+        a.qbuf[(static_cast<size_t>(t) * a.heads + which) * kAttnDim + d] = q;
+    } else {
+        const int g = which - a.heads;
+        const float k = norm_rope(row[a.k_off + g * kAttnDim + d], a.k_norm, pos, a.theta_scale, tmp, red);
+        a.k_cache[static_cast<size_t>(pos) * a.kv_ld + g * kAttnDim + d] = k;
+        a.v_cache[static_cast<size_t>(pos) * a.kv_ld + g * kAttnDim + d] = row[a.v_off + g * kAttnDim + d];
+    }
+    pdl_launch_dependents();
+}
+
+constexpr int kPfQueries = 8, kPfKeys = 32;
+// shared memory of attn_prefill_kernel: K^T [256][33], V [32][256], queries [8][256]
+constexpr size_t kPfSmem = (static_cast<size_t>(kAttnDim) * (kPfKeys + 1) + kPfKeys * kAttnDim + kPfQueries * kAttnDim) *
+                           sizeof(float);
+
+__global__ void __launch_bounds__(256) attn_prefill_kernel(AttnPrefillArgs a)
+{
+    extern __shared__ __align__(16) float pf_smem[];
+    float *kt = pf_smem;                               // [256][33]
+    float *vs = kt + kAttnDim * (kPfKeys + 1);         // [32][256]
+    float *qs = vs + kPfKeys * kAttnDim;               // [8][256]
+    pdl_wait();
+    const int h = blockIdx.y, t0 = blockIdx.x * kPfQueries;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = t0 + warp;
+    const bool live = t < a.tokens;
+    const int pos = a.base + (live ? t : a.tokens - 1);
+    const int g = (a.head0 + h) / (kAttnHeads / 4) - a.kv0;
+    const int last = a.base + min(t0 + kPfQueries - 1, a.tokens - 1);
+    for (int i = lane; i < kAttnDim; i += 32)
+        qs[warp * kAttnDim + i] = live ? a.qbuf[(static_cast<size_t>(t) * a.heads + h) * kAttnDim + i] : 0.0f;
+    float m_run = -INFINITY, l_run = 0.0f, acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    for (int p0 = 0; p0 <= last; p0 += kPfKeys) {
+        __syncthreads();  // the previous tile is consumed (and qs is written)
+        for (int i = threadIdx.x; i < kPfKeys * kAttnDim / 4; i += blockDim.x) {
+            const int key = i / (kAttnDim / 4), d4 = i % (kAttnDim / 4);
+            const int p = min(p0 + key, last);  // past `last`: a valid row, masked below
+            const size_t off = static_cast<size_t>(p) * a.kv_ld + g * kAttnDim + d4 * 4;
+            const float4 k4 = *reinterpret_cast<const float4 *>(a.k_cache + off);
+            kt[(d4 * 4 + 0) * (kPfKeys + 1) + key] = k4.x;
+            kt[(d4 * 4 + 1) * (kPfKeys + 1) + key] = k4.y;
+            kt[(d4 * 4 + 2) * (kPfKeys + 1) + key] = k4.z;
+            kt[(d4 * 4 + 3) * (kPfKeys + 1) + key] = k4.w;
+            *reinterpret_cast<float4 *>(vs + key * kAttnDim + d4 * 4) =
+                *reinterpret_cast<const float4 *>(a.v_cache + off);
+        }
+        __syncthreads();
+        // score of position p0 + lane (q . k in dimension order, then / sqrt(256))
+        const float *q = qs + warp * kAttnDim;
+        float sc = 0.0f;
+#pragma unroll 8
+        for (int d = 0; d < kAttnDim; ++d) sc = __fadd_rn(sc, __fmul_rn(q[d], kt[d * (kPfKeys + 1) + lane]));
+        const bool valid = p0 + lane <= pos;
+        sc = valid ? __fmul_rn(sc, 0.0625f) : -INFINITY;
+        float tile_max = sc;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) tile_max = fmaxf(tile_max, __shfl_xor_sync(0xffffffffu, tile_max, o));
+        const float m_new = fmaxf(m_run, tile_max);
+        const float c = m_run == -INFINITY ? 0.0f : expf(__fsub_rn(m_run, m_new));
+        const float w = valid ? expf(__fsub_rn(sc, m_new)) : 0.0f;
+        float wsum = w;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) wsum = __fadd_rn(wsum, __shfl_xor_sync(0xffffffffu, wsum, o));
+        l_run = __fadd_rn(__fmul_rn(l_run, c), wsum);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = __fmul_rn(acc[i], c);
+        for (int key = 0; key < kPfKeys; ++key) {
+            const float wk = __shfl_sync(0xffffffffu, w, key);
+            const float4 va = *reinterpret_cast<const float4 *>(vs + key * kAttnDim + lane * 8);
+            const float4 vb = *reinterpret_cast<const float4 *>(vs + key * kAttnDim + lane * 8 + 4);
+            acc[0] = fmaf(wk, va.x, acc[0]);
+            acc[1] = fmaf(wk, va.y, acc[1]);
+            acc[2] = fmaf(wk, va.z, acc[2]);
+            acc[3] = fmaf(wk, va.w, acc[3]);
+            acc[4] = fmaf(wk, vb.x, acc[4]);
+            acc[5] = fmaf(wk, vb.y, acc[5]);
+            acc[6] = fmaf(wk, vb.z, acc[6]);
+            acc[7] = fmaf(wk, vb.w, acc[7]);
+        }
+        m_run = m_new;
+    }
+    if (live) {
+        const float *row = a.qkv + static_cast<size_t>(t) * a.qkv_ld + h * 512 + kAttnDim + lane * 8;
+        float *dst = a.out_f + static_cast<size_t>(t) * a.out_ld + h * kAttnDim + lane * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = __fmul_rn(__fdiv_rn(acc[i], l_run), sigmoid(row[i]));
+    }
+    pdl_launch_dependents();
+}
+
+__global__ void __launch_bounds__(256) attn_prefill_quant_kernel(AttnPrefillArgs a)
+{
+    __shared__ AbsMax red_m[8];
+    pdl_wait();
+    const int h = blockIdx.x, t = blockIdx.y;
+    const float v = a.out_f[static_cast<size_t>(t) * a.out_ld + h * kAttnDim + threadIdx.x];
+    quantize_block_256(v, static_cast<Q8KBlock *>(a.out_q) + static_cast<size_t>(t) * a.heads + h, red_m);
+    pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
@@ -901,6 +1258,13 @@ cudaError_t launch_swiglu_quant(const float *gate, const float *up, int ld, int 
                       static_cast<Q8KBlock *>(out_q));
 }
 
+cudaError_t launch_add_replicated(float *hidden, const float *branch, int n, int tokens, int reps,
+                                  long long rep_floats, cudaStream_t s)
+{
+    return launch_pdl(add_replicated_kernel, dim3((n + 255) / 256, tokens), dim3(256), s, hidden, branch, n,
+                      reps < 1 ? 1 : reps, rep_floats);
+}
+
 cudaError_t launch_add(float *out, const float *branch, int n, int tokens, cudaStream_t s)
 {
     return launch_pdl(add_kernel, dim3((n + 255) / 256, tokens), dim3(256), s, out, branch, n);
@@ -909,14 +1273,57 @@ cudaError_t launch_add(float *out, const float *branch, int n, int tokens, cudaS
 cudaError_t launch_deltanet(const DeltaArgs &args, cudaStream_t s)
 {
     if (args.tokens < 1 || args.tokens > kMaxTokens) return cudaErrorInvalidValue;
-    return launch_pdl(deltanet_kernel, dim3(24 * kDeltaCluster), dim3(128), s, args);
+    const int n_kh = args.n_kh > 0 ? args.n_kh : 16;
+    if (n_kh % 2 || n_kh > 16) return cudaErrorInvalidValue;
+    return launch_pdl(deltanet_kernel, dim3(n_kh * 3 / 2 * kDeltaCluster), dim3(128), s, args);
+}
+
+cudaError_t launch_deltanet_prefill(const DeltaPrefillArgs &args, cudaStream_t s)
+{
+    const int n_kh = args.n_kh > 0 ? args.n_kh : 16;
+    if (args.tokens < 1 || n_kh % 2 || n_kh > 16 || args.o_ld != n_kh * 384) return cudaErrorInvalidValue;
+    const int n_vh = 3 * n_kh, channels = 5 * n_kh * 128;
+    cudaError_t e = launch_pdl(deltanet_prefill_kernel, dim3(n_vh * 4), dim3(128), s, args);
+    if (e == cudaSuccess)
+        e = launch_pdl(deltanet_prefill_post_kernel, dim3(n_vh / 2, args.tokens), dim3(256), s, args);
+    if (e == cudaSuccess)
+        e = launch_pdl(deltanet_ring_store_kernel, dim3((channels + 127) / 128), dim3(128), s, args, channels);
+    return e;
+}
+
+cudaError_t launch_attention_prefill(const AttnPrefillArgs &args, cudaStream_t s)
+{
+    if (args.tokens < 1 || args.heads < 1 || args.heads > kAttnHeads || args.kv_ld % 256 ||
+        args.out_ld != args.heads * kAttnDim)
+        return cudaErrorInvalidValue;
+    static cudaError_t attr = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(kPfSmem));
+    if (attr != cudaSuccess) return attr;
+    const int kv_heads = args.kv_ld / 256;
+    cudaError_t e = launch_pdl(attn_prefill_qk_kernel, dim3(args.heads + kv_heads, args.tokens), dim3(256), s, args);
+    if (e == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((args.tokens + kPfQueries - 1) / kPfQueries, args.heads);
+        cfg.blockDim = dim3(256);
+        cfg.dynamicSmemBytes = kPfSmem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr1[1];
+        attr1[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr1[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr1;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, attn_prefill_kernel, args);
+    }
+    if (e == cudaSuccess) e = launch_pdl(attn_prefill_quant_kernel, dim3(args.heads, args.tokens), dim3(256), s, args);
+    return e;
 }
 
 cudaError_t launch_attention(const AttnArgs &args, cudaStream_t s)
 {
     if (args.tokens < 1 || args.tokens > kMaxTokens) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(args.tokens * kAttnHeads * kAttnSplits);
+    if (args.heads < 0 || args.heads > kAttnHeads || (args.heads > 0 && args.kv_ld % 256)) return cudaErrorInvalidValue;
+    cfg.gridDim = dim3(args.tokens * (args.heads > 0 ? args.heads : kAttnHeads) * kAttnSplits);
     cfg.blockDim = dim3(256);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];

@@ -4,36 +4,39 @@
 // upstream layer-major batch, src/qwen38/qwen38_model.c:1519-1560, which calls
 // q38_tensor_gemm_q8_k, src/qwen38/qwen38_quant.c:2950-3169, with M = prompt
 // tokens).  At M in the hundreds or thousands this is a dense contraction, so
-// it runs on the 5th-generation tensor cores with dequant-staged operands:
+// it runs on the 5th-generation tensor cores with dequant-staged operands in
+// two-term fp16 ("hi + lo") form:
 //
-//   A (weights)     the quantized rows dequantized once per call into fp16
-//                   [N][K] (the upstream float formula of each type, rounded
-//                   to nearest fp16), K-major;
+//   A (weights)     each row dequantized with the upstream float formula of
+//                   its type, times a power of two 2^-e per row that puts
+//                   the row's bound on |w| just below 2^15, split into
+//                   hi = fp16(w) and lo = fp16(w - hi): 22 significant bits;
 //   B (activations) the Q8_K blocks of the M tokens dequantized (scale x
-//                   quant, as the upstream integer dot means them) to fp16
-//                   [M][K], each token's row multiplied by a power of two 2^-e
-//                   that puts its largest value in [2^14, 2^15), so no value
-//                   overflows fp16 and the scaling itself rounds nothing;
-//   D               fp32 in tensor memory, times 2^e per token in the
-//                   epilogue, stored batch-major out[token][row] (+= with
-//                   `accumulate`, the residual add of the caller).
+//                   quant, as the upstream integer dot means them), times 2^-e
+//                   per token, split the same way;
+//   D               fp32 in tensor memory: hi.hi + hi.lo + lo.hi per 16-wide
+//                   K step (the lo.lo term is below 2^-22 of the product),
+//                   times both powers of two in the epilogue, stored
+//                   batch-major out[token][row] (+= with `accumulate`, the
+//                   residual add of the caller).
 //
-// Each fp16 rounding is a relative error of at most 2^-11, so outputs agree
-// with the upstream integer path to about 1e-4 relative (the north-star bar
-// for final fp32 outputs is 1e-3); per-block integer sums are not formed
-// here - the M <= 8 decode and verification path keeps the exact integer
-// sums.
+// fp16 products are exact in fp32, so the result carries the rounding of an
+// fp32 dot product with 22-bit operands: about 1e-6 relative, the same order
+// as the float combination of the integer path, instead of the 1e-3 of single
+// fp16 operands (which the chaotic 64-layer random-init models amplify into
+// different logits).  Per-block integer sums are not formed here - the M <= 8
+// decode and verification path keeps the exact integer sums.
 //
 // Kernel: one CTA per 128 x BN output tile (128 weight rows, BN tokens),
-// 6 warps: warp 0 lane 0 issues the TMA tile loads (A 128x64, B BNx64 fp16,
-// 128-byte swizzle) into a ring of stages; warp 1 allocates BN tensor-memory
-// columns and its lane 0 issues tcgen05.mma (M = 128, N = BN, K = 16, four per
-// 64-wide stage) and commits each stage back to the producer; warps 2..5 read
-// the accumulator (warp w reads TMEM lanes 32 (w % 4) ..) and store it.  Every
-// mbarrier wait is bounded (2 s): a wait that runs out records the status
-// word, the MMA issuer still commits the accumulator barrier, the producer
-// waits for the copies it issued, and the CTA frees its tensor memory and
-// exits.
+// 6 warps: warp 0 lane 0 issues the TMA tile loads (3-D boxes: the hi and lo
+// tiles of A, 2 x 128 x 64 fp16, and of B, 2 x BN x 64, 128-byte swizzle) into
+// a ring of stages; warp 1 allocates BN tensor-memory columns and its lane 0
+// issues tcgen05.mma (M = 128, N = BN, K = 16, three per K step) and commits
+// each stage back to the producer; warps 2..5 read the accumulator (warp w
+// reads TMEM lanes 32 (w % 4) ..) and store it.  Every mbarrier wait is
+// bounded (2 s): a wait that runs out records the status word, the MMA issuer
+// still commits the accumulator barrier, the producer waits for the copies it
+// issued, and the CTA frees its tensor memory and exits.
 #include <cuda.h>  // CUtensorMap and its enums; the encoder comes from the driver at run time
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -54,17 +57,18 @@ namespace {
 
 constexpr int kTcRows = 128;   // UMMA M: weight rows per tile
 constexpr int kTcK = 64;       // fp16 elements per stage row: one 128-byte swizzle span
-constexpr int kTcStages = 4;
+constexpr int kTcStages = 2;
 constexpr int kTcThreads = 192;
 
 // ---- TMA, tensor memory and tcgen05 primitives ----------------------------
 
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar)
+// Box (64, rows, 2) at (x, y, 0): the hi tile, then the lo tile.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar)
 {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_addr(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(0), "r"(smem_addr(bar))
         : "memory");
 }
 
@@ -142,6 +146,7 @@ struct TcArgs {
     int ld;
     int n, m, k;            // weight rows, tokens, width
     const float *tok_scale; // [m]: 2^e of each token's B row
+    const float *row_scale; // [n]: 2^e of each weight row
     int accumulate;
 };
 
@@ -149,7 +154,9 @@ template <int BN>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, TcArgs g)
 {
-    constexpr uint32_t kABytes = kTcRows * kTcK * 2, kBBytes = BN * kTcK * 2, kStage = kABytes + kBBytes;
+    // a stage: A hi, A lo, B hi, B lo (each tile 1024-byte aligned)
+    constexpr uint32_t kATile = kTcRows * kTcK * 2, kBTile = BN * kTcK * 2;
+    constexpr uint32_t kABytes = 2 * kATile, kBBytes = 2 * kBTile, kStage = kABytes + kBBytes;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kTcStages * kStage);
@@ -188,8 +195,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     break;
                 uint8_t *stage = smem + s * kStage;
                 mbar_arrive_expect_tx(&full[s], kStage);
-                tma_load_2d(stage, &map_a, k * kTcK, row0, &full[s]);
-                tma_load_2d(stage + kABytes, &map_b, k * kTcK, tok0, &full[s]);
+                tma_load_3d(stage, &map_a, k * kTcK, row0, &full[s]);
+                tma_load_3d(stage + kABytes, &map_b, k * kTcK, tok0, &full[s]);
                 issued = k + 1;
             }
             // The copies issued last must land before shared memory goes away.
@@ -203,11 +210,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int s = k % kTcStages;
                 if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(k / kTcStages) & 1u, &g_tc_status)) break;
                 tc_fence_after();
-                const uint32_t a = smem_addr(smem + s * kStage), b = a + kABytes;
+                const uint32_t a_hi = smem_addr(smem + s * kStage), a_lo = a_hi + kATile;
+                const uint32_t b_hi = a_hi + kABytes, b_lo = b_hi + kBTile;
 #pragma unroll
-                for (int kk = 0; kk < kTcK / 16; ++kk)
-                    mma_f16(tmem, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), f16_idesc<BN>(),
+                for (int kk = 0; kk < kTcK / 16; ++kk) {
+                    const uint32_t o = kk * 32;
+                    mma_f16(tmem, sw128_desc(a_hi + o), sw128_desc(b_hi + o), f16_idesc<BN>(),
                             (k | kk) != 0 ? 1u : 0u);
+                    mma_f16(tmem, sw128_desc(a_hi + o), sw128_desc(b_lo + o), f16_idesc<BN>(), 1u);
+                    mma_f16(tmem, sw128_desc(a_lo + o), sw128_desc(b_hi + o), f16_idesc<BN>(), 1u);
+                }
                 mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
             }
             mma_commit(acc_full);  // always: the epilogue waits for it
@@ -220,6 +232,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncwarp();
         tc_fence_after();
         const int row = row0 + quarter * 32 + lane;
+        const float rs = row < g.n ? __ldg(g.row_scale + row) : 0.0f;
         for (int c = 0; c < BN / 16; ++c) {
             uint32_t v[16];
             tmem_ld16(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(c * 16), v);
@@ -229,7 +242,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int tok = tok0 + c * 16 + j;
                 if (tok >= g.m) break;
                 float *dst = g.out + static_cast<size_t>(tok) * g.ld + row;
-                const float r = __fmul_rn(__uint_as_float(v[j]), __ldg(g.tok_scale + tok));
+                const float r = __fmul_rn(__fmul_rn(__uint_as_float(v[j]), __ldg(g.tok_scale + tok)), rs);
                 *dst = g.accumulate ? __fadd_rn(*dst, r) : r;
             }
         }
@@ -245,7 +258,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 template <int BN> constexpr size_t tc_smem_bytes()
 {
-    return 1024 + static_cast<size_t>(kTcStages) * (kTcRows + BN) * kTcK * 2 + (2 * kTcStages + 1) * 8 + 16;
+    return 1024 + static_cast<size_t>(kTcStages) * 2 * (kTcRows + BN) * kTcK * 2 + (2 * kTcStages + 1) * 8 + 16;
 }
 
 // ---- operand staging --------------------------------------------------------
@@ -296,16 +309,55 @@ __device__ __forceinline__ void q6k_group(const uint8_t *b, int grp, float (&w)[
     }
 }
 
-// Weights -> fp16 [rows][width].  One thread per (row, 32-element group).
-// Rows are read in the tiled layout when tile_rows != 0.  With `split`, the
-// rows come interleaved in pairs (gate i, up i) and are written as
-// [gate rows | up rows].
+// The power of two 2^e of each weight row: e is chosen so that a bound on
+// the row's |w| (Q4_K: |d| 63 15 + |dmin| 63 per superblock; Q6_K: |d| 127 32)
+// times 2^-e lies in [2^14, 2^15).  One warp per row.
+__global__ void row_scale_kernel(const uint8_t *w, int type, uint64_t rows, uint64_t nb, uint32_t tile_rows, int bb,
+                                 float *row_scale, int split)
+{
+    pdl_wait();
+    const uint64_t row = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    float bound = 0.0f;
+    for (uint64_t blk = lane; blk < nb; blk += 32) {
+        const uint8_t *b;
+        if (tile_rows) {
+            const uint64_t t = row / tile_rows, r = row - t * tile_rows;
+            b = w + ((t * nb + blk) * tile_rows + r) * bb;
+        } else {
+            b = w + (row * nb + blk) * bb;
+        }
+        const float v = type == 12 ? fabsf(f16_bits_to_f32(ld_u16(b))) * 945.0f +
+                                         fabsf(f16_bits_to_f32(ld_u16(b + 2))) * 63.0f
+                                   : fabsf(f16_bits_to_f32(ld_u16(b + 208))) * 4064.0f;
+        bound = fmaxf(bound, v);
+    }
+    for (int o = 16; o; o >>= 1) bound = fmaxf(bound, __shfl_xor_sync(0xffffffffu, bound, o));
+    const uint64_t orow = split ? ((row & 1) ? rows / 2 + row / 2 : row / 2) : row;  // the written row
+    if (lane == 0) row_scale[orow] = bound > 0.0f ? ldexpf(1.0f, ilogbf(bound) - 14) : 1.0f;
+}
+
+// hi = fp16(v), lo = fp16(v - hi)
+__device__ __forceinline__ void split2(float a, float b, __half2 &hi, __half2 &lo)
+{
+    hi = __floats2half2_rn(a, b);
+    const float2 h = __half22float2(hi);
+    lo = __floats2half2_rn(__fsub_rn(a, h.x), __fsub_rn(b, h.y));
+}
+
+// Weights -> fp16 hi [rows][width] and lo (rows * width further), times
+// 1 / row_scale.  One thread per (row, 32-element group).  Rows are read in
+// the tiled layout when tile_rows != 0.  With `split`, the rows come
+// interleaved in pairs (gate i, up i) and are written as [gate rows | up
+// rows] (row_scale is indexed by the written row).
 __global__ void dequant_f16_kernel(const uint8_t *w, int type, uint64_t rows, uint64_t width, uint32_t tile_rows,
-                                   int bb, __half *out, int split)
+                                   int bb, __half *out, const float *row_scale, int split)
 {
     pdl_wait();
     const uint64_t groups = width / 32, nb = width / 256;
     const uint64_t total = rows * groups;
+    __half *out_lo = out + rows * width;
     for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
          i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
         const uint64_t row = i / groups, g = i - row * groups;
@@ -321,15 +373,18 @@ __global__ void dequant_f16_kernel(const uint8_t *w, int type, uint64_t rows, ui
         if (type == 12) q4k_group(b, static_cast<int>(g & 7), v);
         else q6k_group(b, static_cast<int>(g & 7), v);
         const uint64_t orow = split ? ((row & 1) ? rows / 2 + row / 2 : row / 2) : row;
-        __half2 *dst = reinterpret_cast<__half2 *>(out + orow * width + g * 32);
+        const float inv = __frcp_rn(__ldg(row_scale + orow));  // a power of two: exact
+        __half2 *hi = reinterpret_cast<__half2 *>(out + orow * width + g * 32);
+        __half2 *lo = reinterpret_cast<__half2 *>(out_lo + orow * width + g * 32);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) dst[e] = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+        for (int e = 0; e < 16; ++e) split2(__fmul_rn(v[2 * e], inv), __fmul_rn(v[2 * e + 1], inv), hi[e], lo[e]);
     }
     pdl_launch_dependents();
 }
 
-// Q8_K blocks [m][nb] -> fp16 [m_pad][nb * 256] times 2^-e per token, and
-// tok_scale[t] = 2^e (rows past m are zero).  One CTA per token row.
+// Q8_K blocks [m][nb] -> fp16 hi [m_pad][nb * 256] and lo (m_pad rows
+// further) times 2^-e per token, and tok_scale[t] = 2^e (rows past m are
+// zero).  One CTA per token row.
 __global__ void __launch_bounds__(256) q8k_to_f16_kernel(const Q8KBlock *in, int nb, int m, __half *out,
                                                          float *tok_scale)
 {
@@ -338,8 +393,9 @@ __global__ void __launch_bounds__(256) q8k_to_f16_kernel(const Q8KBlock *in, int
     const int t = blockIdx.x, tid = threadIdx.x;
     const int width = nb * 256;
     __half2 *dst = reinterpret_cast<__half2 *>(out + static_cast<size_t>(t) * width);
+    __half2 *dst_lo = reinterpret_cast<__half2 *>(out + (static_cast<size_t>(gridDim.x) + t) * width);
     if (t >= m) {
-        for (int i = tid; i < width / 2; i += blockDim.x) dst[i] = __floats2half2_rn(0.0f, 0.0f);
+        for (int i = tid; i < width / 2; i += blockDim.x) dst[i] = dst_lo[i] = __floats2half2_rn(0.0f, 0.0f);
         pdl_launch_dependents();
         return;
     }
@@ -358,8 +414,8 @@ __global__ void __launch_bounds__(256) q8k_to_f16_kernel(const Q8KBlock *in, int
     for (int i = tid; i < width / 2; i += blockDim.x) {
         const int k = 2 * i, b = k >> 8, j = k & 255;
         const float s = ldexpf(row[b].scale, -e);
-        dst[i] = __floats2half2_rn(__fmul_rn(s, static_cast<float>(row[b].quants[j])),
-                                   __fmul_rn(s, static_cast<float>(row[b].quants[j + 1])));
+        split2(__fmul_rn(s, static_cast<float>(row[b].quants[j])), __fmul_rn(s, static_cast<float>(row[b].quants[j + 1])),
+               dst[i], dst_lo[i]);
     }
     pdl_launch_dependents();
 }
@@ -384,16 +440,17 @@ EncodeTiledFn encoder()
     return fn;
 }
 
-// 2-D fp16 tensor map [outer][inner], box 64 x box_outer, 128-byte swizzle.
+// 3-D fp16 tensor map [2][outer][inner] (the hi matrix, then the lo matrix),
+// box 64 x box_outer x 2, 128-byte swizzle.
 bool make_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint32_t box_outer)
 {
     EncodeTiledFn enc = encoder();
     if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u) || inner % 64) return false;
-    const cuuint64_t dims[2] = {inner, outer};
-    const cuuint64_t strides[1] = {inner * 2};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTcK), box_outer};
-    const cuuint32_t estr[2] = {1, 1};
-    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+    const cuuint64_t dims[3] = {inner, outer, 2};
+    const cuuint64_t strides[2] = {inner * 2, inner * outer * 2};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kTcK), box_outer, 2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -417,6 +474,7 @@ cudaError_t launch_tc_bn(const void *a16, const void *b16, const TcGemm &p, cuda
     g.m = p.m;
     g.k = p.k;
     g.tok_scale = p.tok_scale;
+    g.row_scale = p.row_scale;
     g.accumulate = p.accumulate;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(((p.n + kTcRows - 1) / kTcRows) * ((p.m + BN - 1) / BN)));
@@ -438,9 +496,24 @@ int tc_token_tile(int m) { return m > 128 ? 256 : 128; }
 bool tc_weight_type(int type) { return type == 12 || type == 14; }  // Q4_K, Q6_K
 
 cudaError_t launch_dequant_f16(const void *w, int type, uint64_t rows, uint64_t width, uint32_t tile_rows, int bb,
-                               void *out, int split, cudaStream_t s)
+                               void *out, float *row_scale, int split, cudaStream_t s)
 {
     if (!tc_weight_type(type) || width % 256 || (split && rows % 2)) return cudaErrorInvalidValue;
+    {
+        // the rows' powers of two first, in the order the rows are written
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>((rows * 32 + 255) / 256));
+        cfg.blockDim = dim3(256);
+        cfg.stream = s;
+        cudaLaunchAttribute la[1];
+        la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        la[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = la;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, row_scale_kernel, static_cast<const uint8_t *>(w), type, rows,
+                                                 width / 256, tile_rows, bb, row_scale, split);
+        if (e != cudaSuccess) return e;
+    }
     const uint64_t total = rows * (width / 32);
     const unsigned grid = static_cast<unsigned>(std::min<uint64_t>((total + 255) / 256, 148ull * 16));
     cudaLaunchConfig_t cfg = {};
@@ -453,7 +526,7 @@ cudaError_t launch_dequant_f16(const void *w, int type, uint64_t rows, uint64_t 
     cfg.attrs = la;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, dequant_f16_kernel, static_cast<const uint8_t *>(w), type, rows, width, tile_rows,
-                              bb, static_cast<__half *>(out), split);
+                              bb, static_cast<__half *>(out), static_cast<const float *>(row_scale), split);
 }
 
 cudaError_t launch_q8k_to_f16(const void *q8, int nb, int m, int m_pad, void *out, float *tok_scale, cudaStream_t s)

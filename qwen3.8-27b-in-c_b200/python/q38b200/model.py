@@ -42,6 +42,9 @@ def _bind():
         "q38cu_model_stream": ([vp], vp),
         "q38cu_model_step_kernels": ([vp], ctypes.c_int),
         "q38cu_model_trace": ([vp, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int], ctypes.c_int),
+        "q38cu_model_open_tp": ([ctypes.c_char_p, u32, u32, u32, ctypes.c_char_p], vp),
+        "q38cu_nccl_unique_id": ([ctypes.c_char_p], ctypes.c_int),
+        "q38cu_tp_shard": ([u32, u32, ctypes.POINTER(TPShard)], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -55,14 +58,50 @@ class ModelError(RuntimeError):
     pass
 
 
+class TPShard(ctypes.Structure):
+    """Q38CuTPShard (include/q38cuda_model.h): what one tensor-parallel rank holds."""
+    _fields_ = [("rank", ctypes.c_uint32), ("world", ctypes.c_uint32),
+                ("key_heads", ctypes.c_uint32 * 16), ("n_key_heads", ctypes.c_uint32),
+                ("value_blocks", ctypes.c_uint32 * 24), ("n_value_blocks", ctypes.c_uint32),
+                ("attn_head0", ctypes.c_uint32), ("attn_heads", ctypes.c_uint32),
+                ("kv_head0", ctypes.c_uint32), ("kv_heads", ctypes.c_uint32),
+                ("ffn0", ctypes.c_uint32), ("ffn", ctypes.c_uint32),
+                ("vocab0", ctypes.c_uint32), ("vocab", ctypes.c_uint32)]
+
+
+def tp_shard(rank, world):
+    """The partition of the model that rank `rank` of `world` GPUs holds (host only)."""
+    lib = _bind()
+    out = TPShard()
+    if lib.q38cu_tp_shard(rank, world, ctypes.byref(out)) != 1:
+        raise ModelError(f"q38cu_tp_shard failed: {last_error()}")
+    return out
+
+
+def nccl_unique_id():
+    """128 bytes of NCCL communicator id (call on one rank, send to the others)."""
+    lib = _bind()
+    buf = ctypes.create_string_buffer(128)
+    if lib.q38cu_nccl_unique_id(buf) != 1:
+        raise ModelError(f"q38cu_nccl_unique_id failed: {last_error()}")
+    return buf.raw
+
+
 class Model:
     """The device-resident model (one CUDA device, the current one at open)."""
 
-    def __init__(self, path, context_length=4096):
+    def __init__(self, path, context_length=4096, rank=0, world=1, nccl_id=None):
+        """One GPU, or (world > 1) this process's tensor-parallel shard: every
+        rank passes the same path, context length, world and nccl_id."""
         self.lib = _bind()
-        self.handle = self.lib.q38_model_open_gguf(str(path).encode(), context_length)
+        self.world = world
+        if world == 1:
+            self.handle = self.lib.q38_model_open_gguf(str(path).encode(), context_length)
+        else:
+            assert nccl_id is not None and len(nccl_id) == 128
+            self.handle = self.lib.q38cu_model_open_tp(str(path).encode(), context_length, rank, world, nccl_id)
         if not self.handle:
-            raise ModelError(f"q38_model_open_gguf failed: {last_error()}")
+            raise ModelError(f"model open failed: {last_error()}")
 
     def close(self):
         if self.handle:

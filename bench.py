@@ -574,6 +574,15 @@ def verify_pass_costs(m, stream):
     return out
 
 
+def guarded(fn):
+    """A sub-record, or the reason it could not be measured (the headline
+    line is printed either way)."""
+    try:
+        return fn()
+    except Exception as exc:  # noqa: BLE001 - reported in the line
+        return {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+
+
 def run_decode(args, rank, world, dist):
     import torch
     from q38b200.model import Model
@@ -679,7 +688,7 @@ def run_decode(args, rank, world, dist):
         # 4's prefill (both before MTP is enabled: with MTP on, a prefill also
         # runs the MTP head's catch-up)
         verify_ms = verify_pass_costs(m, stream)
-        subrecords["prefill_config4"] = measure_prefill(m, path, stream)
+        subrecords["prefill_config4"] = guarded(lambda: measure_prefill(m, path, stream))
         # MTP on: speculative greedy decoding at draft depths 1..4 (the
         # upstream's spec bench sweep, qwen38_spec_bench.c:108-119).
         mtp = {"verify_pass_ms": verify_ms}
@@ -709,12 +718,12 @@ def run_decode(args, rank, world, dist):
                        "and costs the drafts plus a verification of depth tokens")
     m.close()
     if world == 1 and not args.no_subrecords:
-        subrecords["matvec_config0"] = measure_matvec(matvec_case("Q4_K", "17408x5120"))
+        subrecords["matvec_config0"] = guarded(lambda: measure_matvec(matvec_case("Q4_K", "17408x5120")))
         for q in ("IQ1_M", "IQ2_S"):
             for shape in ("17408x5120", "5120x17408"):
-                subrecords[f"matvec_config1_{q}_{shape}"] = measure_matvec(matvec_case(q, shape), launches=2000,
-                                                                          e2e_steps=200)
-        subrecords["verify_config2"] = measure_verify()
+                subrecords[f"matvec_config1_{q}_{shape}"] = guarded(
+                    lambda q=q, shape=shape: measure_matvec(matvec_case(q, shape), launches=2000, e2e_steps=200))
+        subrecords["verify_config2"] = guarded(measure_verify)
 
     if rank != 0:
         return

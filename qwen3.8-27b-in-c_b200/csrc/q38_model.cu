@@ -245,7 +245,9 @@ struct Q38Model {
     float *enorm = nullptr, *hnorm = nullptr, *shared_head_norm = nullptr;
 
     // state
-    float *conv_ring = nullptr, *delta_state = nullptr, *k_cache = nullptr, *v_cache = nullptr;
+    float *conv_ring = nullptr, *delta_state = nullptr;
+    uint8_t *k_cache = nullptr, *v_cache = nullptr;  // [17][context][kv_ld] of kv_bytes each
+    int kv_bytes = 4;                                // 4: fp32 (the upstream's), 2: fp16 (Q38CU_KV_F16=1)
     float *ck_conv_ring = nullptr, *ck_delta_state = nullptr, *mtp_hidden = nullptr, *ck_mtp_hidden = nullptr;
     float *target_norm = nullptr;  // [kMaxDrafts][kHidden]: output-normed hidden of verified tokens
     uint32_t ck_position = 0, ck_mtp_position = 0;
@@ -676,7 +678,8 @@ bool alloc_runtime(Q38Model *m)
         return false;
     return dalloc(&m->conv_ring, static_cast<size_t>(kRecurrent) * m->lin_qkv * kConvRing, o) &&
            dalloc(&m->delta_state, static_cast<size_t>(kRecurrent) * m->lin_heads * kLinDim * kLinDim, o) &&
-           dalloc(&m->k_cache, kFull * ctx * m->kv_ld, o) && dalloc(&m->v_cache, kFull * ctx * m->kv_ld, o) &&
+           dalloc(&m->k_cache, kFull * ctx * m->kv_ld * m->kv_bytes, o) &&
+           dalloc(&m->v_cache, kFull * ctx * m->kv_ld * m->kv_bytes, o) &&
            dalloc(&m->mtp_hidden, kHidden, o) && dalloc(&m->hidden, kReps * kMaxTokens * kHidden, o) &&
            dalloc(&m->normf, kMaxTokens * 2 * kHidden, o) &&
            dalloc(&m->wide, kReps * kMaxTokens * static_cast<size_t>(m->wide_ld), o) &&
@@ -875,6 +878,19 @@ bool has_float_part(const Proj &p)
 bool batch_rmsnorm_input(Q38Model *m, const Part &part, const ActIn &in, int tokens, ActIn *out);
 ActIn q8_input(const void *q8, const float *f, int f_ld, bool replicated);
 
+// Whether an RMSNorm input of `tokens` tokens is formed by the separate
+// prologue kernel (always for batches; for single tokens when
+// Q38CU_SPLIT_NORM=1, else inside every CTA of the GEMV).  Both give the same
+// bits.
+bool split_norm(int tokens)
+{
+    static const bool single = [] {
+        const char *v = std::getenv("Q38CU_SPLIT_NORM");
+        return v && *v == '1';
+    }();
+    return tokens > 1 || single;
+}
+
 bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int out_ld, int accumulate,
              const OutReps &orep = OutReps(), const Part *next_after = nullptr)
 {
@@ -898,7 +914,7 @@ bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int o
     // (a batch: one prologue kernel with the first part's warp count) and the
     // other parts stage that.
     const bool share = in.mode == q38::kActRmsNorm && p.parts.size() > 1 && !has_float_part(p);
-    if (share && tokens > 1 && !batch_rmsnorm_input(m, p.parts[0], in, tokens, &in)) return false;
+    if (share && split_norm(tokens) && !batch_rmsnorm_input(m, p.parts[0], in, tokens, &in)) return false;
     bool float_part = false;
     for (size_t i = 0; i < p.parts.size(); ++i) {
         const Part &part = p.parts[i];
@@ -907,7 +923,7 @@ bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int o
             ActIn pin = in;
             if (i > 0) pin.side_w = nullptr;  // side rows come with the first launch only
             if (share && i > 0) pin = q8_input(m->q8_norm, in.f_out, width, true);
-            if (pin.mode == q38::kActRmsNorm && tokens > 1 && !batch_rmsnorm_input(m, part, pin, tokens, &pin))
+            if (pin.mode == q38::kActRmsNorm && split_norm(tokens) && !batch_rmsnorm_input(m, part, pin, tokens, &pin))
                 return false;
             const bool exporting = share && i == 0 && pin.mode == q38::kActRmsNorm;
             if (!stream_project(part, pin, tokens, out + part.offset, out_ld, accumulate, orep, prefetch_of(next), s,
@@ -1081,8 +1097,9 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         }
         a.q_norm = L.q_norm;
         a.k_norm = L.k_norm;
-        a.k_cache = m->k_cache + static_cast<size_t>(L.index) * m->context_length * m->kv_ld;
-        a.v_cache = m->v_cache + static_cast<size_t>(L.index) * m->context_length * m->kv_ld;
+        a.k_cache = m->k_cache + static_cast<size_t>(L.index) * m->context_length * m->kv_ld * m->kv_bytes;
+        a.v_cache = m->v_cache + static_cast<size_t>(L.index) * m->context_length * m->kv_ld * m->kv_bytes;
+        a.kv_half = m->kv_bytes == 2;
         a.ctl = m->ctl;
         a.theta_scale = m->theta_scale;
         a.tokens = tokens;
@@ -1154,7 +1171,7 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         sw.reps = kReps;
         sw.rep_bytes = q8_rep_bytes();
         ActIn gin = rmsnorm_input(m->hidden, L.post_norm);
-        if (tokens > 1 && !batch_rmsnorm_input(m, L.gate_up.parts[0], gin, tokens, &gin)) return false;
+        if (split_norm(tokens) && !batch_rmsnorm_input(m, L.gate_up.parts[0], gin, tokens, &gin)) return false;
         if (!stream_project(L.gate_up.parts[0], gin, tokens, nullptr, 0, 0, OutReps(), prefetch_of(first_part(L.down)),
                             s, &sw, m))
             return false;
@@ -1681,7 +1698,6 @@ bool tc_layer(Q38Model *m, int l, int n, uint32_t base)
         return false;
     if (!L.full && !tc_project(m, L.ba, q8, m->pf_normf, kHidden, n, m->pf_ba, m->ba_ld, 0, false)) return false;
     Q38CuQ8KBlock *mix = static_cast<Q38CuQ8KBlock *>(m->pf_q8mix);
-    const int mix_nb = kLinV / 256;
     if (!L.full) {
         // the DeltaNet recurrence over the whole chunk in one launch
         q38::DeltaPrefillArgs d{};
@@ -1714,8 +1730,9 @@ bool tc_layer(Q38Model *m, int l, int n, uint32_t base)
         a.v_off = kAttnQg + kAttnKv;
         a.q_norm = L.q_norm;
         a.k_norm = L.k_norm;
-        a.k_cache = m->k_cache + static_cast<size_t>(L.index) * m->context_length * m->kv_ld;
-        a.v_cache = m->v_cache + static_cast<size_t>(L.index) * m->context_length * m->kv_ld;
+        a.k_cache = m->k_cache + static_cast<size_t>(L.index) * m->context_length * m->kv_ld * m->kv_bytes;
+        a.v_cache = m->v_cache + static_cast<size_t>(L.index) * m->context_length * m->kv_ld * m->kv_bytes;
+        a.kv_half = m->kv_bytes == 2;
         a.kv_ld = m->kv_ld;
         a.heads = 24;
         a.theta_scale = m->theta_scale;
@@ -1796,6 +1813,9 @@ Q38Model *open_model(const char *path, uint32_t context_length, int rank, int wo
     }
     Q38Model *m = new Q38Model();
     m->shard = shard;
+    // KV cache precision: fp32 as upstream, or fp16 with Q38CU_KV_F16=1 at open
+    const char *kv16 = std::getenv("Q38CU_KV_F16");
+    m->kv_bytes = kv16 && *kv16 == '1' ? 2 : 4;
     m->context_length = context_length;
     // the RoPE frequency step, evaluated by the host libm as upstream does
     // (qwen38_model.c:699)
@@ -1931,8 +1951,8 @@ void q38_model_reset(Q38Model *m)
     const size_t ctx = m->context_length;
     cudaMemsetAsync(m->conv_ring, 0, conv_ring_bytes(m), m->stream);
     cudaMemsetAsync(m->delta_state, 0, delta_state_bytes(m), m->stream);
-    cudaMemsetAsync(m->k_cache, 0, kFull * ctx * m->kv_ld * 4, m->stream);
-    cudaMemsetAsync(m->v_cache, 0, kFull * ctx * m->kv_ld * 4, m->stream);
+    cudaMemsetAsync(m->k_cache, 0, kFull * ctx * m->kv_ld * m->kv_bytes, m->stream);
+    cudaMemsetAsync(m->v_cache, 0, kFull * ctx * m->kv_ld * m->kv_bytes, m->stream);
     cudaMemsetAsync(m->mtp_hidden, 0, kHidden * 4, m->stream);
     cudaMemsetAsync(m->ctl, 0, 4 * sizeof(int), m->stream);
     cudaStreamSynchronize(m->stream);

@@ -80,7 +80,8 @@ struct AttnArgs {
     const float *qkv;  // per token: q|gate interleaved per head (12288), k at k_off, v at v_off
     int qkv_ld, k_off, v_off;
     const float *q_norm, *k_norm;  // [256]
-    float *k_cache, *v_cache;      // this layer's [context][1024]
+    void *k_cache, *v_cache;       // this layer's [context][kv_ld], fp32 or (kv_half) fp16
+    int kv_half;
     const int *ctl;
     float theta_scale;  // powf(1e7, -2 / 64), computed on the host as upstream
     int tokens;
@@ -107,7 +108,8 @@ struct AttnPrefillArgs {
     const float *qkv;  // [tokens][qkv_ld]: q|gate interleaved per head (512), k at k_off, v at v_off
     int qkv_ld, k_off, v_off;
     const float *q_norm, *k_norm;
-    float *k_cache, *v_cache;  // this layer's [context][kv_ld]
+    void *k_cache, *v_cache;  // this layer's [context][kv_ld], fp32 or (kv_half) fp16
+    int kv_half;
     int kv_ld;                 // 256 * KV heads held
     int heads, head0, kv0;     // query heads held (global head0 ..), first KV head held
     float theta_scale;

@@ -14,6 +14,7 @@
 // expf/logf/cosf/sinf are CUDA's (within 2 ulp of glibc's), so the results
 // agree with the upstream to rounding, not bit for bit.
 #include <cooperative_groups.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "q38_device.cuh"
@@ -94,6 +95,24 @@ __device__ __forceinline__ AbsMax warp_absmax(AbsMax m)
         m = better(m, other);
     }
     return m;
+}
+
+// KV cache elements: fp32 (the upstream's precision, qwen38_model.c:1391-1396)
+// or fp16 (half the bytes a long-context step reads).  `idx` counts elements;
+// a 4-element load starts on a multiple of 4.
+__device__ __forceinline__ float4 kv_load4(const void *base, size_t idx, int half)
+{
+    if (!half) return *reinterpret_cast<const float4 *>(static_cast<const float *>(base) + idx);
+    const uint2 raw = *reinterpret_cast<const uint2 *>(static_cast<const __half *>(base) + idx);
+    const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+    const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+
+__device__ __forceinline__ void kv_store(void *base, size_t idx, float v, int half)
+{
+    if (half) static_cast<__half *>(base)[idx] = __float2half_rn(v);
+    else static_cast<float *>(base)[idx] = v;
 }
 
 // Q8_K quantization of 256 values held one per thread by a 256-thread CTA
@@ -915,8 +934,8 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
             sh.knew[tt][d] = kx;
             sh.vnew[tt][d] = vx;
             if (writer && tt == t) {
-                a.k_cache[static_cast<size_t>(pp) * kv_ld + g * 256 + d] = kx;
-                a.v_cache[static_cast<size_t>(pp) * kv_ld + g * 256 + d] = vx;
+                kv_store(a.k_cache, static_cast<size_t>(pp) * kv_ld + g * 256 + d, kx, a.kv_half);
+                kv_store(a.v_cache, static_cast<size_t>(pp) * kv_ld + g * 256 + d, vx, a.kv_half);
             }
         }
         __syncthreads();
@@ -934,12 +953,19 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const int pk = min(p + k, p1 - 1);  // past the range: a valid row, masked below
-                const float *kr = pk < base ? a.k_cache + static_cast<size_t>(pk) * kv_ld + g * 256 : sh.knew[pk - base];
-                const float *vr = pk < base ? a.v_cache + static_cast<size_t>(pk) * kv_ld + g * 256 : sh.vnew[pk - base];
-                ka[k] = *reinterpret_cast<const float4 *>(kr + lane * 4);
-                kb[k] = *reinterpret_cast<const float4 *>(kr + 128 + lane * 4);
-                va[k] = *reinterpret_cast<const float4 *>(vr + lane * 4);
-                vb[k] = *reinterpret_cast<const float4 *>(vr + 128 + lane * 4);
+                if (pk < base) {
+                    const size_t row = static_cast<size_t>(pk) * kv_ld + g * 256 + lane * 4;
+                    ka[k] = kv_load4(a.k_cache, row, a.kv_half);
+                    kb[k] = kv_load4(a.k_cache, row + 128, a.kv_half);
+                    va[k] = kv_load4(a.v_cache, row, a.kv_half);
+                    vb[k] = kv_load4(a.v_cache, row + 128, a.kv_half);
+                } else {
+                    const float *kr = sh.knew[pk - base], *vr = sh.vnew[pk - base];
+                    ka[k] = *reinterpret_cast<const float4 *>(kr + lane * 4);
+                    kb[k] = *reinterpret_cast<const float4 *>(kr + 128 + lane * 4);
+                    va[k] = *reinterpret_cast<const float4 *>(vr + lane * 4);
+                    vb[k] = *reinterpret_cast<const float4 *>(vr + 128 + lane * 4);
+                }
             }
             float sc[4];
 #pragma unroll
@@ -1051,8 +1077,9 @@ __global__ void __launch_bounds__(256) attn_prefill_qk_kernel(AttnPrefillArgs a)
     } else {
         const int g = which - a.heads;
         const float k = norm_rope(row[a.k_off + g * kAttnDim + d], a.k_norm, pos, a.theta_scale, tmp, red);
-        a.k_cache[static_cast<size_t>(pos) * a.kv_ld + g * kAttnDim + d] = k;
-        a.v_cache[static_cast<size_t>(pos) * a.kv_ld + g * kAttnDim + d] = row[a.v_off + g * kAttnDim + d];
+        kv_store(a.k_cache, static_cast<size_t>(pos) * a.kv_ld + g * kAttnDim + d, k, a.kv_half);
+        kv_store(a.v_cache, static_cast<size_t>(pos) * a.kv_ld + g * kAttnDim + d, row[a.v_off + g * kAttnDim + d],
+                 a.kv_half);
     }
     pdl_launch_dependents();
 }
@@ -1087,13 +1114,12 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(AttnPrefillArgs a)
             const int key = i / (kAttnDim / 4), d4 = i % (kAttnDim / 4);
             const int p = min(p0 + key, last);  // past `last`: a valid row, masked below
             const size_t off = static_cast<size_t>(p) * a.kv_ld + g * kAttnDim + d4 * 4;
-            const float4 k4 = *reinterpret_cast<const float4 *>(a.k_cache + off);
+            const float4 k4 = kv_load4(a.k_cache, off, a.kv_half);
             kt[(d4 * 4 + 0) * (kPfKeys + 1) + key] = k4.x;
             kt[(d4 * 4 + 1) * (kPfKeys + 1) + key] = k4.y;
             kt[(d4 * 4 + 2) * (kPfKeys + 1) + key] = k4.z;
             kt[(d4 * 4 + 3) * (kPfKeys + 1) + key] = k4.w;
-            *reinterpret_cast<float4 *>(vs + key * kAttnDim + d4 * 4) =
-                *reinterpret_cast<const float4 *>(a.v_cache + off);
+            *reinterpret_cast<float4 *>(vs + key * kAttnDim + d4 * 4) = kv_load4(a.v_cache, off, a.kv_half);
         }
         __syncthreads();
         // score of position p0 + lane (q . k in dimension order, then / sqrt(256))

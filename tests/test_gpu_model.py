@@ -152,6 +152,43 @@ def test_attention_layer_long_context_teacher_forced(models, model_path):
     assert np.median(errors) <= 1e-5 and exact_single >= 0.8 and exact_multi >= 0.6, stats
 
 
+def test_fp16_kv_cache_attention_layer_teacher_forced(model_path):
+    """The optional fp16 KV cache (Q38CU_KV_F16=1 at open; the upstream keeps
+    fp32, qwen38_model.c:1391-1396): the first full-attention layer, teacher-
+    forced over 150 positions, stays within the in-layer int8-flip bar of the
+    CPU restatement (fp16 keys and values round at 2^-11), and the 8-token
+    prefill still equals token-by-token decoding bit for bit."""
+    import os
+    import model_oracle as MO
+    from q38b200.model import Model
+    if not O.reference_available():
+        pytest.skip("upstream reference library not built")
+    os.environ["Q38CU_KV_F16"] = "1"
+    try:
+        dev = Model(model_path, 512)
+    finally:
+        del os.environ["Q38CU_KV_F16"]
+    try:
+        lo = MO.LayerOracle(model_path, O.Reference())
+        layer = 3
+        tokens = np.random.default_rng(21).integers(0, 248320, 150).tolist()
+        dev.reset()
+        inputs = [dev.forward_token_layers(t, layer) for t in tokens]
+        dev.reset()
+        outputs = [dev.forward_token_layers(t, layer + 1) for t in tokens]
+        sl = MO.StatefulLayer(lo, layer)
+        errors = np.array([rel(o, sl.step(i)) for i, o in zip(inputs, outputs)])
+        print(f"fp16 KV, attention layer teacher-forced: median {np.median(errors):.2e}, worst {errors.max():.2e}")
+        assert errors.max() <= 2e-2 and np.median(errors) <= 2e-3
+        prompt = np.random.default_rng(5).integers(0, 248320, 11).tolist()
+        dev.reset()
+        stepwise = [dev.forward_token(t) for t in prompt][-1]
+        dev.reset()
+        assert np.array_equal(dev.prefill(prompt), stepwise)
+    finally:
+        dev.close()
+
+
 def test_forward_token_drift_within_upstream_builds(models, portable):
     dev, ref = models
     for m in (dev, ref, portable):

@@ -224,6 +224,7 @@ template <int MT, int L = 1> struct StreamThreads {
 template <typename Dec> struct SplitParts { static constexpr int kMax = 1; };
 template <> struct SplitParts<DecQ4K> { static constexpr int kMax = 4; };
 template <> struct SplitParts<DecQ6K> { static constexpr int kMax = 4; };
+template <> struct SplitParts<DecIQ1M> { static constexpr int kMax = 4; };
 
 // Activation prologues.  They run after the grid dependency, so their global
 // loads are the latency every launch pays before its first decode: each
@@ -629,14 +630,16 @@ __device__ __forceinline__ void prefetch_next_ranges(const StreamArgs &g)
 // the lanes (exact integer adds) and every lane forms the same float value.
 template <typename Dec, int MT, int L, bool kDbg>
 __device__ __forceinline__ void decode_column_part(const StreamArgs &g, const uint8_t *blk, const Act *acts, int b,
-                                                   int row, float (&acc)[MT], int part, unsigned mask)
+                                                   int row, float (&acc)[MT], int part, unsigned mask,
+                                                   const uint2 *grid)
 {
     SmemActs<MT> a;
 #pragma unroll
     for (int tok = 0; tok < MT; ++tok) a.p[tok] = acts + tok * g.nb + b;
     int w[MT], x[MT];
     float val[MT];
-    Dec::template block_part<MT, L>(blk, a, part, w, x);
+    if constexpr (NeedsGrid<Dec>::kEntries > 0) Dec::template block_part<MT, L>(blk, a, part, w, x, grid);
+    else Dec::template block_part<MT, L>(blk, a, part, w, x);
 #pragma unroll
     for (int o = 1; o < L; o <<= 1) {
 #pragma unroll
@@ -810,7 +813,7 @@ __global__ void __launch_bounds__(StreamThreads<MT, L>::kValue, 1) stream_gemm_k
                     if constexpr (L > 1) {
                         for (; k < n; ++k)
                             decode_column_part<Dec, MT, L, kDbg>(g, base + k * unit_bytes, acts, w.b + k, row, acc,
-                                                                 part, part_mask);
+                                                                 part, part_mask, grid);
                     }
                     if constexpr (MT <= 2 && !kDbg && L == 1 && kColumnsInFlight == 2) {
                         // two columns in flight: independent decode chains,
@@ -1041,7 +1044,12 @@ cudaError_t plan_t(int rows, int width, int tile_rows, int tokens, StreamPlan *p
     // split CTA holds too many registers for the next launch's CTA to be
     // resident beside it).  Q38CU_STREAM_PARTS=n overrides the choice (1: off).
     int max_parts = env_knob("Q38CU_STREAM_PARTS", 0);
-    if (max_parts <= 0) max_parts = std::is_same<Dec, DecQ6K>::value && tile_rows % 32 != 0 ? 4 : 1;
+    // IQ1_M decodes at several times the instructions per byte of the K-quants
+    // (a codebook lookup per 8 weights): four lanes per superblock give the SM
+    // twice the decoding warps.
+    if (max_parts <= 0)
+        max_parts = (std::is_same<Dec, DecQ6K>::value && tile_rows % 32 != 0) || std::is_same<Dec, DecIQ1M>::value ? 4
+                                                                                                              : 1;
     if (q.mt == 1 && SplitParts<Dec>::kMax > 1 && max_parts > 1) {
         for (int parts = std::min(4, SplitParts<Dec>::kMax); parts > 1; parts >>= 1) {
             const int gt = (tile_rows * parts + 31) / 32 * 32;

@@ -72,6 +72,11 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t cols)
 {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)),
@@ -150,6 +155,9 @@ struct TcArgs {
     int accumulate;
 };
 
+// K steps (64 wide) per accumulation segment: one 256-element superblock.
+constexpr int kTcSegment = 4;
+
 template <int BN>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, TcArgs g)
@@ -161,23 +169,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kTcStages * kStage);
     uint64_t *empty = full + kTcStages;
-    uint64_t *acc_full = empty + kTcStages;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+    uint64_t *acc_full = empty + kTcStages;  // [2]: a segment's sums are in tensor-memory buffer b
+    uint64_t *acc_empty = acc_full + 2;      // [2]: the epilogue has read buffer b
+    uint64_t *drained = acc_empty + 2;       // the MMA issuer's last MMA has completed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drained + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tok_tiles = (g.m + BN - 1) / BN;
     const int row0 = (blockIdx.x / tok_tiles) * kTcRows, tok0 = (blockIdx.x % tok_tiles) * BN;
     const int nk = g.k / kTcK;
+    const int segments = (nk + kTcSegment - 1) / kTcSegment;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(acc_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+        }
+        mbar_init(drained, 1);
         fence_mbar_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, BN);
+    if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -206,44 +221,83 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
-            for (int k = 0; k < nk; ++k) {
-                const int s = k % kTcStages;
-                if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(k / kTcStages) & 1u, &g_tc_status)) break;
-                tc_fence_after();
-                const uint32_t a_hi = smem_addr(smem + s * kStage), a_lo = a_hi + kATile;
-                const uint32_t b_hi = a_hi + kABytes, b_lo = b_hi + kBTile;
-#pragma unroll
-                for (int kk = 0; kk < kTcK / 16; ++kk) {
-                    const uint32_t o = kk * 32;
-                    mma_f16(tmem, sw128_desc(a_hi + o), sw128_desc(b_hi + o), f16_idesc<BN>(),
-                            (k | kk) != 0 ? 1u : 0u);
-                    mma_f16(tmem, sw128_desc(a_hi + o), sw128_desc(b_lo + o), f16_idesc<BN>(), 1u);
-                    mma_f16(tmem, sw128_desc(a_lo + o), sw128_desc(b_hi + o), f16_idesc<BN>(), 1u);
+            // Segment sg accumulates K steps [4 sg, 4 sg + 4) into tensor-memory
+            // buffer sg % 2, which the epilogue must have emptied first.
+            bool ok = true;
+            for (int sg = 0; ok && sg < segments; ++sg) {
+                const int b = sg & 1;
+                const uint32_t acc = tmem + static_cast<uint32_t>(b * BN);
+                if (sg >= 2 && !mbar_wait_bounded(&acc_empty[b], static_cast<uint32_t>((sg >> 1) - 1) & 1u, &g_tc_status)) {
+                    ok = false;
+                    break;
                 }
-                mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+                tc_fence_after();
+                const int k1 = min(nk, (sg + 1) * kTcSegment);
+                for (int k = sg * kTcSegment; k < k1; ++k) {
+                    const int s = k % kTcStages;
+                    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(k / kTcStages) & 1u, &g_tc_status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_hi = smem_addr(smem + s * kStage), a_lo = a_hi + kATile;
+                    const uint32_t b_hi = a_hi + kABytes, b_lo = b_hi + kBTile;
+#pragma unroll
+                    for (int kk = 0; kk < kTcK / 16; ++kk) {
+                        const uint32_t o = kk * 32;
+                        mma_f16(acc, sw128_desc(a_hi + o), sw128_desc(b_hi + o), f16_idesc<BN>(),
+                                (k > sg * kTcSegment || kk > 0) ? 1u : 0u);
+                        mma_f16(acc, sw128_desc(a_hi + o), sw128_desc(b_lo + o), f16_idesc<BN>(), 1u);
+                        mma_f16(acc, sw128_desc(a_lo + o), sw128_desc(b_hi + o), f16_idesc<BN>(), 1u);
+                    }
+                    mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+                }
+                if (ok) mma_commit(&acc_full[b]);
             }
-            mma_commit(acc_full);  // always: the epilogue waits for it
+            mma_commit(drained);  // every MMA issued has completed when this arrives
+            mbar_wait_bounded(drained, 0u, &g_tc_status);
         }
         __syncwarp();
     } else {
         // ---------------- epilogue: warps 2..5 ----------------
-        const int quarter = warp & 3;  // tensor-memory lanes 32 quarter .. 32 quarter + 31
-        const bool ok = mbar_wait_bounded(acc_full, 0u, &g_tc_status);
-        __syncwarp();
-        tc_fence_after();
-        const int row = row0 + quarter * 32 + lane;
-        const float rs = row < g.n ? __ldg(g.row_scale + row) : 0.0f;
-        for (int c = 0; c < BN / 16; ++c) {
-            uint32_t v[16];
-            tmem_ld16(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(c * 16), v);
-            if (!ok || row >= g.n) continue;
+        // Thread (quarter, lane) owns weight row 32 quarter + lane of the tile
+        // and adds each segment's sums for its BN tokens into fp32 registers
+        // (IEEE rounding; the tensor core's own accumulation is only trusted
+        // over one superblock).
+        const int quarter = warp & 3;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        float sum[BN];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int tok = tok0 + c * 16 + j;
-                if (tok >= g.m) break;
-                float *dst = g.out + static_cast<size_t>(tok) * g.ld + row;
-                const float r = __fmul_rn(__fmul_rn(__uint_as_float(v[j]), __ldg(g.tok_scale + tok)), rs);
-                *dst = g.accumulate ? __fadd_rn(*dst, r) : r;
+        for (int c = 0; c < BN; ++c) sum[c] = 0.0f;
+        bool ok = true;
+        for (int sg = 0; sg < segments; ++sg) {
+            const int b = sg & 1;
+            ok = ok && mbar_wait_bounded(&acc_full[b], static_cast<uint32_t>(sg >> 1) & 1u, &g_tc_status);
+            if (!ok) break;
+            __syncwarp();
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < BN / 16; ++c) {
+                uint32_t v[16];
+                tmem_ld16(tmem + lane_addr + static_cast<uint32_t>(b * BN + c * 16), v);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) sum[c * 16 + j] = __fadd_rn(sum[c * 16 + j], __uint_as_float(v[j]));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
+        const int row = row0 + quarter * 32 + lane;
+        if (ok && row < g.n) {
+            const float rs = __ldg(g.row_scale + row);
+#pragma unroll
+            for (int c = 0; c < BN; ++c) {
+                const int tok = tok0 + c;
+                if (tok < g.m) {
+                    float *dst = g.out + static_cast<size_t>(tok) * g.ld + row;
+                    const float r = __fmul_rn(__fmul_rn(sum[c], __ldg(g.tok_scale + tok)), rs);
+                    *dst = g.accumulate ? __fadd_rn(*dst, r) : r;
+                }
             }
         }
     }
@@ -252,13 +306,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, BN);
+        tmem_dealloc(tmem, 2 * BN);
     }
 }
 
 template <int BN> constexpr size_t tc_smem_bytes()
 {
-    return 1024 + static_cast<size_t>(kTcStages) * 2 * (kTcRows + BN) * kTcK * 2 + (2 * kTcStages + 1) * 8 + 16;
+    return 1024 + static_cast<size_t>(kTcStages) * 2 * (kTcRows + BN) * kTcK * 2 + (2 * kTcStages + 5) * 8 + 16;
 }
 
 // ---- operand staging --------------------------------------------------------
@@ -491,7 +545,7 @@ cudaError_t launch_tc_bn(const void *a16, const void *b16, const TcGemm &p, cuda
 
 }  // namespace
 
-int tc_token_tile(int m) { return m > 128 ? 256 : 128; }
+int tc_token_tile(int) { return 128; }
 
 bool tc_weight_type(int type) { return type == 12 || type == 14; }  // Q4_K, Q6_K
 
@@ -548,7 +602,7 @@ cudaError_t launch_q8k_to_f16(const void *q8, int nb, int m, int m_pad, void *ou
 cudaError_t launch_tc_gemm(const void *a16, const void *b16, const TcGemm &p, cudaStream_t s)
 {
     if (p.k % kTcK || p.n < 1 || p.m < 1 || p.m_pad < p.m || !p.out || !p.tok_scale) return cudaErrorInvalidValue;
-    return tc_token_tile(p.m) == 256 ? launch_tc_bn<256>(a16, b16, p, s) : launch_tc_bn<128>(a16, b16, p, s);
+    return launch_tc_bn<128>(a16, b16, p, s);
 }
 
 cudaError_t read_and_clear_tc_status(int *status)

@@ -526,24 +526,25 @@ struct DecIQ1M {
     __device__ static void aux_from_raw(Act &a) { aux(a, nullptr); }
     __device__ static void load(Act &a, const Q8KBlock *g) { load_act_base(a, g); aux(a, g); }
     __device__ static void zero(Act &a) { zero_act(a); }
-    template <int MT, class A>
-    __device__ static void block(const uint8_t *blk, const A &a, int (&w)[MT], int (&x)[MT], float (&v)[MT],
-                                 const uint2 *grid)
+    __device__ static void load_raw(const uint8_t *blk, uint32_t (&raw)[14])
     {
         const uint2 *p = reinterpret_cast<const uint2 *>(blk);
-        uint32_t raw[14];
 #pragma unroll
         for (int i = 0; i < 7; ++i) {
             const uint2 u = p[i];
             raw[2 * i] = u.x;
             raw[2 * i + 1] = u.y;
         }
+    }
+    // The integer sums of groups g0 .. g1 - 1 (32 elements each): acc = the
+    // scaled grid dot products, cor = the scaled +-1 delta corrections.
+    template <int MT, int G0, int G1, class A>
+    __device__ static void groups(const uint32_t (&raw)[14], const A &a, int (&acc)[MT], int (&cor)[MT],
+                                  const uint2 *grid)
+    {
 #define Q38_B(k) byte_of(raw[(k) >> 2], (k) & 3)
-        int acc[MT], cor[MT];
 #pragma unroll
-        for (int t = 0; t < MT; ++t) acc[t] = cor[t] = 0;
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
+        for (int g = G0; g < G1; ++g) {
             const uint32_t scw = (g < 4 ? raw[12] : raw[13]) >> (16 * ((g / 2) & 1));
             const int shift = 6 * (g % 2);
             const int sc[2] = {1 + 2 * static_cast<int>((scw >> shift) & 7u),
@@ -568,17 +569,66 @@ struct DecIQ1M {
             }
         }
 #undef Q38_B
+    }
+    template <int MT, class A>
+    __device__ static void combine(const uint32_t (&raw)[14], const A &a, const int (&acc)[MT], const int (&cor)[MT],
+                                   float (&v)[MT])
+    {
         const uint32_t sb = ((raw[12] & 0xFFFFu) >> 12) | (((raw[12] >> 16) >> 8) & 0x00F0u) |
                             (((raw[13] & 0xFFFFu) >> 4) & 0x0F00u) | ((raw[13] >> 16) & 0xF000u);
         const float d = f16_bits_to_f32(sb);
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
-            w[t] = acc[t];
-            x[t] = cor[t];
             const float dd = __fmul_rn(d, a.xs(t));
             v[t] = __fmul_rn(dd, __fadd_rn(static_cast<float>(acc[t]),
                                            __fmul_rn(0.125f, static_cast<float>(cor[t]))));
         }
+    }
+    template <int MT, class A>
+    __device__ static void block(const uint8_t *blk, const A &a, int (&w)[MT], int (&x)[MT], float (&v)[MT],
+                                 const uint2 *grid)
+    {
+        uint32_t raw[14];
+        load_raw(blk, raw);
+        int acc[MT], cor[MT];
+#pragma unroll
+        for (int t = 0; t < MT; ++t) acc[t] = cor[t] = 0;
+        groups<MT, 0, 8>(raw, a, acc, cor, grid);
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+            w[t] = acc[t];
+            x[t] = cor[t];
+        }
+        combine<MT>(raw, a, acc, cor, v);
+    }
+    // Part j of L (2 or 4) of `block`: groups 8j / L .. 8(j + 1) / L; the parts'
+    // integer sums add exactly, so `finish` on the totals equals `block`.
+    template <int MT, int L, class A>
+    __device__ static void block_part(const uint8_t *blk, const A &a, int j, int (&w)[MT], int (&x)[MT],
+                                      const uint2 *grid)
+    {
+        static_assert(L == 2 || L == 4, "IQ1_M splits in 2 or 4 parts");
+        uint32_t raw[14];
+        load_raw(blk, raw);
+#pragma unroll
+        for (int t = 0; t < MT; ++t) w[t] = x[t] = 0;
+        if constexpr (L == 2) {
+            if (j == 0) groups<MT, 0, 4>(raw, a, w, x, grid);
+            else groups<MT, 4, 8>(raw, a, w, x, grid);
+        } else {
+            if (j == 0) groups<MT, 0, 2>(raw, a, w, x, grid);
+            else if (j == 1) groups<MT, 2, 4>(raw, a, w, x, grid);
+            else if (j == 2) groups<MT, 4, 6>(raw, a, w, x, grid);
+            else groups<MT, 6, 8>(raw, a, w, x, grid);
+        }
+    }
+    template <int MT, class A>
+    __device__ static void finish(const uint8_t *blk, const A &a, const int (&w)[MT], const int (&x)[MT],
+                                  float (&v)[MT])
+    {
+        uint32_t raw[14];
+        load_raw(blk, raw);
+        combine<MT>(raw, a, w, x, v);
     }
 };
 

@@ -1761,6 +1761,23 @@ bool tc_prefill_enabled()
     return !(v && *v == '0');
 }
 
+// The tensor-core prefill takes models whose integer-path matrices are all
+// Q4_K or Q6_K (the tensor-core GEMM's types); others (the IQ1_M-typed
+// variant) prefill through the 8-token path.
+bool tc_prefill_types(const Q38Model *m)
+{
+    auto ok = [](const Proj &p) {
+        for (const Part &part : p.parts)
+            if (part.int_path && !q38::tc_weight_type(static_cast<int>(part.t.type))) return false;
+        return true;
+    };
+    for (int l = 0; l < kLayers; ++l) {
+        const Layer &L = m->layers[l];
+        if (!ok(L.in_proj) || !ok(L.out) || !ok(L.gate_up) || !ok(L.down)) return false;
+    }
+    return true;
+}
+
 // Prefill of `count` tokens from the current position with the tensor-core
 // layer-major path; leaves the last token's logits in m->host_logits.
 bool prefill_tc(Q38Model *m, const uint32_t *tokens, uint32_t count)
@@ -1998,7 +2015,7 @@ int q38_model_prefill(Q38Model *m, const uint32_t *tokens, uint32_t token_count,
         if (tokens[i] >= kVocab) return 0;
     if (!use_device(m)) return 0;
     if (token_count >= static_cast<uint32_t>(kTcPrefillMin) && !m->mtp_enabled && m->shard.world == 1 &&
-        tc_prefill_enabled()) {
+        tc_prefill_enabled() && tc_prefill_types(m)) {
         if (!prefill_tc(m, tokens, token_count)) return 0;
         *logits = m->host_logits;
         return 1;

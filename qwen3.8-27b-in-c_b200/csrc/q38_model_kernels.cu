@@ -931,8 +931,11 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
             __syncthreads();
             const float kx = norm_rope(r2[a.k_off + g * 256 + d], a.k_norm, pp, a.theta_scale, sh.tmp, sh.red_d);
             const float vx = r2[a.v_off + g * 256 + d];
-            sh.knew[tt][d] = kx;
-            sh.vnew[tt][d] = vx;
+            // with an fp16 cache, this launch's own keys and values take the
+            // cache's rounding too, so a token's result does not depend on
+            // whether its neighbours share the launch
+            sh.knew[tt][d] = a.kv_half ? __half2float(__float2half_rn(kx)) : kx;
+            sh.vnew[tt][d] = a.kv_half ? __half2float(__float2half_rn(vx)) : vx;
             if (writer && tt == t) {
                 kv_store(a.k_cache, static_cast<size_t>(pp) * kv_ld + g * 256 + d, kx, a.kv_half);
                 kv_store(a.v_cache, static_cast<size_t>(pp) * kv_ld + g * 256 + d, vx, a.kv_half);

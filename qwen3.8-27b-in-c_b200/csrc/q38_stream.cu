@@ -224,6 +224,9 @@ template <int MT, int L = 1> struct StreamThreads {
 template <typename Dec> struct SplitParts { static constexpr int kMax = 1; };
 template <> struct SplitParts<DecQ4K> { static constexpr int kMax = 4; };
 template <> struct SplitParts<DecQ6K> { static constexpr int kMax = 4; };
+// IQ1_M can split too (block_part / finish), but measured slower on B200
+// (17408 x 5120: 24.2 us at 4 lanes against 18.1 us at one), so the planner
+// only splits it when Q38CU_STREAM_PARTS asks.
 template <> struct SplitParts<DecIQ1M> { static constexpr int kMax = 4; };
 
 // Activation prologues.  They run after the grid dependency, so their global
@@ -1044,12 +1047,7 @@ cudaError_t plan_t(int rows, int width, int tile_rows, int tokens, StreamPlan *p
     // split CTA holds too many registers for the next launch's CTA to be
     // resident beside it).  Q38CU_STREAM_PARTS=n overrides the choice (1: off).
     int max_parts = env_knob("Q38CU_STREAM_PARTS", 0);
-    // IQ1_M decodes at several times the instructions per byte of the K-quants
-    // (a codebook lookup per 8 weights): four lanes per superblock give the SM
-    // twice the decoding warps.
-    if (max_parts <= 0)
-        max_parts = (std::is_same<Dec, DecQ6K>::value && tile_rows % 32 != 0) || std::is_same<Dec, DecIQ1M>::value ? 4
-                                                                                                              : 1;
+    if (max_parts <= 0) max_parts = std::is_same<Dec, DecQ6K>::value && tile_rows % 32 != 0 ? 4 : 1;
     if (q.mt == 1 && SplitParts<Dec>::kMax > 1 && max_parts > 1) {
         for (int parts = std::min(4, SplitParts<Dec>::kMax); parts > 1; parts >>= 1) {
             const int gt = (tile_rows * parts + 31) / 32 * 32;

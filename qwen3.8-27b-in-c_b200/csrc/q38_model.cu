@@ -295,6 +295,14 @@ struct Q38Model {
     ncclComm_t comm = nullptr;
     float *partial = nullptr;       // [kMaxTokens][kHidden]: a row-parallel projection's partial sums
     float *logits_local = nullptr;  // [kMaxTokens][shard.vocab]
+    // Q38CU_TP_P2P=1: the row-parallel sums travel over NVLink through CUDA
+    // IPC buffers (tp_reduce_kernel) instead of NCCL's all-reduce.
+    bool p2p = false;
+    uint8_t *ar_base = nullptr;  // this rank's [flags][exchange buffer]
+    unsigned long long *ar_counter = nullptr;
+    float *ar_bufs[8] = {};
+    unsigned long long *ar_flags[8] = {};
+    std::vector<void *> ipc_opened;
     int kv_ld = kAttnKv;            // floats per position of this shard's KV cache rows
     int lin_qkv = kLinQkv, lin_heads = kLinHeads;  // this shard's DeltaNet channels and value heads
 
@@ -1539,10 +1547,68 @@ bool nccl_ok(ncclResult_t r, const char *what)
     return fail("%s", std::string(what) + ": " + (api ? api->error_string(r) : "NCCL unavailable"));
 }
 
+constexpr size_t kArFlagBytes = 4096;  // flags area ahead of the exchange buffer
+
+// Exchange buffers for the NVLink all-reduce: one allocation per rank
+// ([flags][2 halves x world slots x 8 tokens x 5120 floats]), its IPC handle
+// all-gathered over the NCCL communicator, the peers' allocations opened.
+bool setup_p2p(Q38Model *m)
+{
+    const int world = m->shard.world, rank = m->shard.rank;
+    const size_t bytes = kArFlagBytes + static_cast<size_t>(2) * world * kMaxTokens * kHidden * sizeof(float);
+    static_assert(8 * q38::kTpReduceCtas * sizeof(unsigned long long) <= kArFlagBytes, "flags area");
+    if (!dalloc(&m->ar_base, bytes, m->owned) || !dalloc(&m->ar_counter, 2, m->owned)) return false;
+    cudaIpcMemHandle_t mine;
+    if (!cuda_ok(cudaIpcGetMemHandle(&mine, m->ar_base), "cudaIpcGetMemHandle")) return false;
+    uint8_t *dev_handles = nullptr;
+    if (!dalloc(&dev_handles, sizeof(cudaIpcMemHandle_t) * world, m->owned)) return false;
+    std::vector<cudaIpcMemHandle_t> all(world);
+    const NcclApi *api = nccl();
+    if (!cuda_ok(cudaMemcpy(dev_handles + rank * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice),
+                 "handle copy") ||
+        !nccl_ok(api->all_gather(dev_handles + rank * sizeof(mine), dev_handles, sizeof(mine), ncclChar, m->comm,
+                                 m->stream),
+                 "handle all-gather") ||
+        !cuda_ok(cudaStreamSynchronize(m->stream), "handle all-gather") ||
+        !cuda_ok(cudaMemcpy(all.data(), dev_handles, sizeof(mine) * world, cudaMemcpyDeviceToHost), "handle copy"))
+        return false;
+    for (int r = 0; r < world; ++r) {
+        uint8_t *base = m->ar_base;
+        if (r != rank) {
+            void *p = nullptr;
+            if (!cuda_ok(cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle"))
+                return false;
+            m->ipc_opened.push_back(p);
+            base = static_cast<uint8_t *>(p);
+        }
+        m->ar_flags[r] = reinterpret_cast<unsigned long long *>(base);
+        m->ar_bufs[r] = reinterpret_cast<float *>(base + kArFlagBytes);
+    }
+    m->p2p = true;
+    return true;
+}
+
 // The residual add after a row-parallel projection: the partial sums of all
 // GPUs are added up (all-reduce) and into the hidden rows and their replicas.
 bool reduce_into_hidden(Q38Model *m, int tokens)
 {
+    if (m->p2p) {
+        q38::TpReduceArgs a{};
+        a.partial = m->partial;
+        a.hidden = m->hidden;
+        a.reps = kReps;
+        a.rep_floats = hidden_rep_bytes() / 4;
+        a.n = kHidden;
+        a.tokens = tokens;
+        a.rank = m->shard.rank;
+        a.world = m->shard.world;
+        for (int r = 0; r < a.world; ++r) {
+            a.bufs[r] = m->ar_bufs[r];
+            a.flags[r] = m->ar_flags[r];
+        }
+        a.counter = m->ar_counter;
+        return cuda_ok(q38::launch_tp_reduce(a, m->stream), "NVLink all-reduce");
+    }
     const NcclApi *api = nccl();
     return nccl_ok(api->all_reduce(m->partial, m->partial, static_cast<size_t>(tokens) * kHidden, ncclFloat, ncclSum,
                                    m->comm, m->stream),
@@ -1863,6 +1929,8 @@ Q38Model *open_model(const char *path, uint32_t context_length, int rank, int wo
     if (ok && world > 1) {
         const NcclApi *api = nccl();
         ok = nccl_ok(api->comm_init_rank(&m->comm, world, *id, rank), "ncclCommInitRank");
+        const char *p2p = std::getenv("Q38CU_TP_P2P");
+        if (ok && p2p && *p2p == '1') ok = setup_p2p(m);
     }
     if (ok) {
         const char *tv = std::getenv("Q38CU_TRACE");
@@ -1949,6 +2017,7 @@ void q38_model_close(Q38Model *m)
     for (auto &g : m->verify_graph)
         if (g) cudaGraphExecDestroy(g);
     // tensors shared between the target and the MTP head are listed once
+    for (void *p : m->ipc_opened) cudaIpcCloseMemHandle(p);
     if (m->comm) nccl()->comm_destroy(m->comm);
     for (auto &t : m->tensors) q38cu_tensor_free(&t);
     for (void *p : m->owned) cudaFree(p);

@@ -100,6 +100,26 @@ struct AttnArgs {
     int heads, head0, kv0, kv_ld;
 };
 
+// The residual add after a row-parallel projection with the partial sums
+// exchanged over NVLink (tensor parallelism without NCCL): every rank writes
+// its partial [tokens][n] into slot `rank` of every rank's exchange buffer
+// (peer pointers from CUDA IPC), raises per-CTA flags there, waits for the
+// other ranks' flags and adds all slots in rank order into hidden (and its
+// replicas).  Slots alternate between two halves by call parity; the call
+// number comes from a device counter every rank advances identically.
+struct TpReduceArgs {
+    const float *partial;           // this rank's [tokens][n]
+    float *hidden;                  // [tokens][n], reps copies rep_floats apart
+    int reps;
+    long long rep_floats;
+    int n, tokens, rank, world;
+    float *bufs[8];                 // every rank's exchange buffer: [2][world][8][n] floats
+    unsigned long long *flags[8];   // every rank's flags: [world][kTpReduceCtas]
+    unsigned long long *counter;    // [2]: the call number, and the CTAs done with this call
+};
+constexpr int kTpReduceCtas = 40;
+cudaError_t launch_tp_reduce(const TpReduceArgs &args, cudaStream_t s);
+
 // Full attention over a whole prefill chunk (launch_attention_prefill): the
 // queries of tokens 0 .. tokens - 1 at positions base .. base + tokens - 1
 // attend to the cached positions up to their own; this chunk's keys and

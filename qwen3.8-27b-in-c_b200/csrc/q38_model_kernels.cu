@@ -1179,6 +1179,92 @@ __global__ void __launch_bounds__(256) attn_prefill_quant_kernel(AttnPrefillArgs
 }
 
 // ---------------------------------------------------------------------------
+// The all-reduce of a row-parallel projection over peer memory (TpReduceArgs).
+// CTA c owns columns [n c / C, n (c + 1) / C) of every token: it stores them to
+// slot `rank` of every rank's buffer, publishes flag (rank, c) on every rank
+// after a system-scope fence, waits (bounded) until every rank's flag c here
+// shows this call, then adds the world slots in rank order to the hidden rows.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v)
+{
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(128) tp_reduce_kernel(TpReduceArgs a)
+{
+    __shared__ unsigned long long call_s;
+    __shared__ int failed_s;
+    pdl_wait();
+    const int c = blockIdx.x, tid = threadIdx.x;
+    if (tid == 0) {
+        call_s = __ldcg(a.counter);
+        failed_s = 0;
+    }
+    __syncthreads();
+    const unsigned long long call = call_s;
+    const int half = static_cast<int>(call & 1);
+    const int c0 = a.n * c / kTpReduceCtas, c1 = a.n * (c + 1) / kTpReduceCtas;
+    const size_t slot = static_cast<size_t>(8) * a.n;                // floats of one rank's slot
+    const size_t half_floats = static_cast<size_t>(a.world) * slot;  // floats of one half
+    // 1. this rank's partial into slot `rank` of every rank
+    for (int t = 0; t < a.tokens; ++t)
+        for (int i = c0 + tid; i < c1; i += blockDim.x) {
+            const float v = a.partial[static_cast<size_t>(t) * a.n + i];
+            for (int r = 0; r < a.world; ++r)
+                a.bufs[r][half * half_floats + a.rank * slot + static_cast<size_t>(t) * a.n + i] = v;
+        }
+    __syncthreads();
+    // 2. publish, 3. wait for every rank's slice c of this call
+    if (tid == 0) {
+        __threadfence_system();
+        for (int r = 0; r < a.world; ++r) st_release_sys(a.flags[r] + a.rank * kTpReduceCtas + c, call + 1);
+        const unsigned long long start = global_timer_ns();
+        for (int r = 0; r < a.world; ++r) {
+            const unsigned long long *f = a.flags[a.rank] + r * kTpReduceCtas + c;
+            while (ld_acquire_sys(f) < call + 1) {
+                if (global_timer_ns() - start > kWaitLimitNs) {
+                    atomicExch(&g_model_status, kStatusWaitTimeout);
+                    failed_s = 1;
+                    break;
+                }
+            }
+            if (failed_s) break;
+        }
+    }
+    __syncthreads();
+    // 4. hidden += the slots in rank order (the same sum on every rank)
+    if (!failed_s) {
+        const float *mine = a.bufs[a.rank] + half * half_floats;
+        for (int t = 0; t < a.tokens; ++t)
+            for (int i = c0 + tid; i < c1; i += blockDim.x) {
+                const size_t o = static_cast<size_t>(t) * a.n + i;
+                float sum = __ldcg(mine + o);
+                for (int r = 1; r < a.world; ++r) sum = __fadd_rn(sum, __ldcg(mine + r * slot + o));
+                const float h = __fadd_rn(a.hidden[o], sum);
+                for (int k = 0; k < a.reps; ++k) a.hidden[o + k * a.rep_floats] = h;
+            }
+    }
+    // the last CTA advances the call number for the next reduction
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(a.counter + 1, 1ull) == kTpReduceCtas - 1) {
+            a.counter[1] = 0;
+            __threadfence();
+            atomicExch(a.counter, call + 1);
+        }
+    }
+    pdl_launch_dependents();
+}
+
+// ---------------------------------------------------------------------------
 // Greedy argmax over each token's logits (upstream q38_argmax: the first index
 // of the maximum, qwen38_model.c:1228-1239).  Grid (kArgmaxCtas, tokens); the
 // last CTA of a token merges the CTA results in order and, for the last token
@@ -1345,6 +1431,14 @@ cudaError_t launch_attention_prefill(const AttnPrefillArgs &args, cudaStream_t s
     }
     if (e == cudaSuccess) e = launch_pdl(attn_prefill_quant_kernel, dim3(args.heads, args.tokens), dim3(256), s, args);
     return e;
+}
+
+cudaError_t launch_tp_reduce(const TpReduceArgs &args, cudaStream_t s)
+{
+    if (args.world < 2 || args.world > 8 || args.rank < 0 || args.rank >= args.world || args.tokens < 1 ||
+        args.tokens > kMaxTokens || args.n < kTpReduceCtas)
+        return cudaErrorInvalidValue;
+    return launch_pdl(tp_reduce_kernel, dim3(kTpReduceCtas), dim3(128), s, args);
 }
 
 cudaError_t launch_attention(const AttnArgs &args, cudaStream_t s)

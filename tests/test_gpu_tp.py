@@ -26,12 +26,13 @@ def _free_port():
         return sock.getsockname()[1]
 
 
-def _rank_main(rank, world, port, path, out_dir):
+def _rank_main(rank, world, port, path, out_dir, p2p):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
     root = os.path.dirname(here)
     sys.path[:0] = [os.path.join(root, "oracle"), os.path.join(root, "qwen3.8-27b-in-c_b200", "python")]
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    os.environ["Q38CU_TP_P2P"] = "1" if p2p else "0"
     import torch
     import torch.distributed as dist
     from q38b200.model import Model, nccl_unique_id
@@ -66,7 +67,10 @@ def cosine(a, b):
     return a @ b / np.linalg.norm(a) / np.linalg.norm(b)
 
 
-def test_two_gpu_tensor_parallel_matches_one_gpu(tmp_path):
+@pytest.mark.parametrize("p2p", [False, True], ids=["nccl", "nvlink-p2p"])
+def test_two_gpu_tensor_parallel_matches_one_gpu(tmp_path, p2p):
+    """Both collectives: NCCL's all-reduce, and the exchange over CUDA IPC
+    peer memory with bounded flag waits (Q38CU_TP_P2P=1)."""
     import torch
     import torch.multiprocessing as mp
     from q38b200 import gguf
@@ -75,7 +79,7 @@ def test_two_gpu_tensor_parallel_matches_one_gpu(tmp_path):
         pytest.skip("needs 2 GPUs")
     path = gguf.cached_model_path(seed=3, mtp=False, dist="robust")
     world = 2
-    mp.start_processes(_rank_main, args=(world, _free_port(), path, str(tmp_path)), nprocs=world,
+    mp.start_processes(_rank_main, args=(world, _free_port(), path, str(tmp_path), p2p), nprocs=world,
                        start_method="spawn")
     r0, r1 = (np.load(os.path.join(tmp_path, f"rank{r}.npz")) for r in range(world))
     for key in ("layer0", "prefill", "step", "greedy"):

@@ -371,6 +371,151 @@ __global__ void f32_gemm_kernel(float *out, const float *x, int batch, uint64_t 
     }
 }
 
+// The same products for prompt-sized batches: one warp per (kF32Rows rows,
+// kF32Toks tokens), so that each decoded weight serves kF32Toks tokens and
+// each activation kF32Rows rows.  Every output keeps f32_gemm_kernel's
+// summation order (a lane's blocks in order, the same shuffle tree), so the
+// two kernels agree bit for bit.
+constexpr int kF32Rows = 4;
+constexpr int kF32Toks = 8;
+
+__global__ void __launch_bounds__(256) f32_gemm_tile_kernel(float *out, const float *x, int batch, uint64_t width,
+                                                            const uint8_t *w, uint64_t rows, uint32_t tile_rows,
+                                                            int type, int be, int bb, uint64_t x_ld, uint64_t out_ld,
+                                                            int accumulate)
+{
+    pdl_wait();
+    pdl_launch_dependents();
+    const uint64_t gw = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint64_t row_groups = (rows + kF32Rows - 1) / kF32Rows;
+    if (gw >= row_groups * static_cast<uint64_t>((batch + kF32Toks - 1) / kF32Toks)) return;
+    const uint64_t row0 = (gw % row_groups) * kF32Rows;
+    const int tok0 = static_cast<int>(gw / row_groups) * kF32Toks;
+    const uint64_t nblocks = width / be;
+    float acc[kF32Rows][kF32Toks];
+#pragma unroll
+    for (int r = 0; r < kF32Rows; ++r)
+#pragma unroll
+        for (int t = 0; t < kF32Toks; ++t) acc[r][t] = 0.0f;
+    for (uint64_t blk = lane; blk < nblocks; blk += 32) {
+        const uint8_t *b[kF32Rows];
+#pragma unroll
+        for (int r = 0; r < kF32Rows; ++r)
+            b[r] = row0 + r < rows ? block_at(w, row0 + r, blk, nblocks, tile_rows, bb) : nullptr;
+        for (int i = 0; i < be; ++i) {
+            float wv[kF32Rows], xv[kF32Toks];
+#pragma unroll
+            for (int r = 0; r < kF32Rows; ++r) wv[r] = b[r] ? element_weight(type, b[r], i) : 0.0f;
+#pragma unroll
+            for (int t = 0; t < kF32Toks; ++t)
+                xv[t] = tok0 + t < batch ? __ldg(x + static_cast<uint64_t>(tok0 + t) * x_ld + blk * be + i) : 0.0f;
+#pragma unroll
+            for (int r = 0; r < kF32Rows; ++r)
+#pragma unroll
+                for (int t = 0; t < kF32Toks; ++t) acc[r][t] = fmaf(wv[r], xv[t], acc[r][t]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kF32Rows; ++r)
+#pragma unroll
+        for (int t = 0; t < kF32Toks; ++t) {
+            float total = acc[r][t];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) total += __shfl_xor_sync(0xffffffffu, total, off);
+            if (lane == 0 && row0 + r < rows && tok0 + t < batch) {
+                float *dst = out + static_cast<uint64_t>(tok0 + t) * out_ld + row0 + r;
+                *dst = accumulate ? __fadd_rn(*dst, total) : total;
+            }
+        }
+}
+
+// The same for 32-element blocks (Q8_0, IQ4_NL): a lane's activation
+// elements are 32 floats apart in memory, so the CTA (8 warps = 32 rows, 8
+// tokens) first copies 32 blocks' worth of each token's activation into
+// shared memory with coalesced loads (rows padded to 33 floats: lane l reads
+// bank (l + i) % 32), then every warp walks them as f32_gemm_tile_kernel
+// does - same order, same results.  Q8_0 weights take the scale once per
+// block (the same product per element).
+constexpr int kF32Chunk = 32;  // blocks per shared-memory pass
+
+__global__ void __launch_bounds__(256) f32_gemm_tile32_kernel(float *out, const float *x, int batch, uint64_t width,
+                                                              const uint8_t *w, uint64_t rows, uint32_t tile_rows,
+                                                              int type, int bb, uint64_t x_ld, uint64_t out_ld,
+                                                              int accumulate)
+{
+    __shared__ float xs[kF32Toks][kF32Chunk * 33];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t row0 = (static_cast<uint64_t>(blockIdx.x) * 8 + warp) * kF32Rows;
+    const int tok0 = static_cast<int>(blockIdx.y) * kF32Toks;
+    const uint64_t nblocks = width / 32;
+    float acc[kF32Rows][kF32Toks];
+#pragma unroll
+    for (int r = 0; r < kF32Rows; ++r)
+#pragma unroll
+        for (int t = 0; t < kF32Toks; ++t) acc[r][t] = 0.0f;
+    for (uint64_t c0 = 0; c0 < nblocks; c0 += kF32Chunk) {
+        __syncthreads();  // the previous pass is consumed
+        const int n_el = static_cast<int>(nblocks - c0 < kF32Chunk ? nblocks - c0 : kF32Chunk) * 32;
+        for (int i = threadIdx.x; i < kF32Toks * kF32Chunk * 32; i += blockDim.x) {
+            const int t = i / (kF32Chunk * 32), e = i % (kF32Chunk * 32);
+            xs[t][(e >> 5) * 33 + (e & 31)] =
+                tok0 + t < batch && e < n_el ? __ldg(x + static_cast<uint64_t>(tok0 + t) * x_ld + c0 * 32 + e) : 0.0f;
+        }
+        __syncthreads();
+        const uint64_t blk = c0 + lane;
+        if (blk >= nblocks) continue;
+        const uint8_t *b[kF32Rows];
+#pragma unroll
+        for (int r = 0; r < kF32Rows; ++r)
+            b[r] = row0 + r < rows ? block_at(w, row0 + r, blk, nblocks, tile_rows, bb) : nullptr;
+        const float *xl = &xs[0][lane * 33];
+        if (type == kQ8_0) {
+            float d[kF32Rows];
+#pragma unroll
+            for (int r = 0; r < kF32Rows; ++r) d[r] = b[r] ? f16_bits_to_f32(ld_u16(b[r])) : 0.0f;
+            for (int i = 0; i < 32; ++i) {
+                float wv[kF32Rows];
+#pragma unroll
+                for (int r = 0; r < kF32Rows; ++r)
+                    wv[r] = b[r] ? __fmul_rn(d[r], static_cast<float>(static_cast<int8_t>(b[r][2 + i]))) : 0.0f;
+#pragma unroll
+                for (int t = 0; t < kF32Toks; ++t) {
+                    const float xv = xl[t * kF32Chunk * 33 + i];
+#pragma unroll
+                    for (int r = 0; r < kF32Rows; ++r) acc[r][t] = fmaf(wv[r], xv, acc[r][t]);
+                }
+            }
+        } else {
+            for (int i = 0; i < 32; ++i) {
+                float wv[kF32Rows];
+#pragma unroll
+                for (int r = 0; r < kF32Rows; ++r) wv[r] = b[r] ? element_weight(type, b[r], i) : 0.0f;
+#pragma unroll
+                for (int t = 0; t < kF32Toks; ++t) {
+                    const float xv = xl[t * kF32Chunk * 33 + i];
+#pragma unroll
+                    for (int r = 0; r < kF32Rows; ++r) acc[r][t] = fmaf(wv[r], xv, acc[r][t]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kF32Rows; ++r)
+#pragma unroll
+        for (int t = 0; t < kF32Toks; ++t) {
+            float total = acc[r][t];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) total += __shfl_xor_sync(0xffffffffu, total, off);
+            if (lane == 0 && row0 + r < rows && tok0 + t < batch) {
+                float *dst = out + static_cast<uint64_t>(tok0 + t) * out_ld + row0 + r;
+                *dst = accumulate ? __fadd_rn(*dst, total) : total;
+            }
+        }
+}
+
 // Element i of row `row`.  The upstream evaluates fma(w, 1, 0) against a
 // basis vector, which equals w for finite w except that -0 becomes +0.
 __global__ void row_f32_kernel(float *out, const uint8_t *w, uint64_t width, uint32_t tile_rows, uint64_t row,
@@ -573,12 +718,7 @@ cudaError_t launch_quantize_q8k(void *out, const float *in, uint64_t blocks, cud
 cudaError_t launch_f32_gemm(float *out, const float *x, int batch, uint64_t width, const void *w, uint64_t rows,
                             uint32_t tile_rows, int type, int be, int bb, cudaStream_t s)
 {
-    const uint64_t warps = rows * static_cast<uint64_t>(batch);
-    if (warps == 0) return cudaSuccess;
-    const unsigned grid = static_cast<unsigned>((warps * 32 + 255) / 256);
-    f32_gemm_kernel<<<grid, 256, 0, s>>>(out, x, batch, width, static_cast<const uint8_t *>(w), rows, tile_rows, type,
-                                         be, bb, width, rows, 0);
-    return cudaGetLastError();
+    return launch_f32_gemm_ex(out, rows, 0, x, width, batch, width, w, rows, tile_rows, type, be, bb, s);
 }
 
 cudaError_t launch_f32_gemm_ex(float *out, uint64_t out_ld, int accumulate, const float *x, uint64_t x_ld, int batch,
@@ -587,8 +727,27 @@ cudaError_t launch_f32_gemm_ex(float *out, uint64_t out_ld, int accumulate, cons
 {
     const uint64_t warps = rows * static_cast<uint64_t>(batch);
     if (warps == 0) return cudaSuccess;
+    // batches of a prompt take the register-tiled forms (same results)
+    const bool tiled = batch >= 2 * kF32Toks;
+    if (tiled && be == 32) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>((rows + 8 * kF32Rows - 1) / (8 * kF32Rows)),
+                           static_cast<unsigned>((batch + kF32Toks - 1) / kF32Toks));
+        cfg.blockDim = dim3(256);
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, f32_gemm_tile32_kernel, out, x, batch, width,
+                                  static_cast<const uint8_t *>(w), rows, tile_rows, type, bb, x_ld, out_ld,
+                                  accumulate);
+    }
+    const uint64_t launch_warps =
+        tiled ? (rows + kF32Rows - 1) / kF32Rows * static_cast<uint64_t>((batch + kF32Toks - 1) / kF32Toks) : warps;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>((warps * 32 + 255) / 256));
+    cfg.gridDim = dim3(static_cast<unsigned>((launch_warps * 32 + 255) / 256));
     cfg.blockDim = dim3(256);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -596,8 +755,9 @@ cudaError_t launch_f32_gemm_ex(float *out, uint64_t out_ld, int accumulate, cons
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, f32_gemm_kernel, out, x, batch, width, static_cast<const uint8_t *>(w), rows,
-                              tile_rows, type, be, bb, x_ld, out_ld, accumulate);
+    return cudaLaunchKernelEx(&cfg, tiled ? f32_gemm_tile_kernel : f32_gemm_kernel, out, x, batch, width,
+                              static_cast<const uint8_t *>(w), rows, tile_rows, type, be, bb, x_ld, out_ld,
+                              accumulate);
 }
 
 cudaError_t launch_row_f32(float *out, const void *w, uint64_t width, uint32_t tile_rows, uint64_t row, int type,

@@ -295,20 +295,27 @@ struct Q38Model {
     ncclComm_t comm = nullptr;
     float *partial = nullptr;       // [kMaxTokens][kHidden]: a row-parallel projection's partial sums
     float *logits_local = nullptr;  // [kMaxTokens][shard.vocab]
-    // Q38CU_TP_P2P=1: the row-parallel sums travel over NVLink through CUDA
-    // IPC buffers (tp_reduce_kernel) instead of NCCL's all-reduce.
-    bool p2p = false;
-    uint8_t *ar_base = nullptr;  // this rank's [flags][exchange buffer]
+    // How the row-parallel sums are added up across the GPUs:
+    //   Q38CU_TP_P2P=0: NCCL's all-reduce, then a residual-add kernel;
+    //   Q38CU_TP_P2P=1: tp_reduce_kernel over CUDA IPC buffers (NVLink);
+    //   Q38CU_TP_P2P=2: inside the projection's own GEMV, tile by tile, over
+    //                   the same buffers (the exchange fused with the GEMV).
+    int tp_mode = 0;
+    bool p2p = false;            // tp_mode 1
+    bool xc = false;             // tp_mode 2
+    uint8_t *ar_base = nullptr;  // this rank's [flags][exchange flags][exchange buffer]
     unsigned long long *ar_counter = nullptr;
+    unsigned int *xc_counter = nullptr;
     float *ar_bufs[8] = {};
     unsigned long long *ar_flags[8] = {};
+    unsigned int *xc_flags[8] = {};
     std::vector<void *> ipc_opened;
     int kv_ld = kAttnKv;            // floats per position of this shard's KV cache rows
     int lin_qkv = kLinQkv, lin_heads = kLinHeads;  // this shard's DeltaNet channels and value heads
 
     int pf_cap = 0;
     float *pf_hidden = nullptr, *pf_normf = nullptr, *pf_wide = nullptr, *pf_act = nullptr, *pf_ba = nullptr;
-    float *pf_scale = nullptr, *pf_row_scale = nullptr, *pf_oraw = nullptr;
+    float *pf_scale = nullptr, *pf_row_scale = nullptr, *pf_oraw = nullptr, *pf_rec = nullptr;
     void *pf_q8 = nullptr, *pf_q8mix = nullptr, *pf_a16 = nullptr, *pf_b16 = nullptr;
     uint32_t *pf_ids = nullptr, *host_pf_ids = nullptr;
     std::vector<void *> pf_owned;
@@ -815,7 +822,7 @@ struct SwigluOut {
 
 bool stream_project(const Part &p, const ActIn &in, int tokens, float *out, int out_ld, int accumulate,
                     const OutReps &orep, const Prefetch &pf, cudaStream_t s, const SwigluOut *sw = nullptr,
-                    Q38Model *tm = nullptr, void *export_q8 = nullptr)
+                    Q38Model *tm = nullptr, void *export_q8 = nullptr, bool exchange = false)
 {
     const int width = static_cast<int>(p.t.shape[0]), nb = width / 256;
     for (int tok0 = 0; tok0 < tokens;) {
@@ -841,6 +848,17 @@ bool stream_project(const Part &p, const ActIn &in, int tokens, float *out, int 
         l.out_rep_bytes = orep.bytes;
         if (tok0 + plan.token_group >= tokens) set_next_prefetch(l, pf);
         if (tm) l.trace = next_trace(tm);
+        if (exchange) {
+            // the all-reduce of a row-parallel projection, fused into its GEMV
+            l.xc_world = tm->shard.world;
+            l.xc_rank = tm->shard.rank;
+            l.xc_rows = kHidden;
+            for (int r = 0; r < l.xc_world; ++r) {
+                l.xc_bufs[r] = tm->ar_bufs[r];
+                l.xc_flags[r] = tm->xc_flags[r];
+            }
+            l.xc_counter = tm->xc_counter;
+        }
         if (export_q8) {
             l.act_export = static_cast<Q38CuQ8KBlock *>(export_q8) + static_cast<size_t>(tok0) * nb;
             l.export_reps = kReps;
@@ -900,9 +918,11 @@ bool split_norm(int tokens)
 }
 
 bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int out_ld, int accumulate,
-             const OutReps &orep = OutReps(), const Part *next_after = nullptr)
+             const OutReps &orep = OutReps(), const Part *next_after = nullptr, bool exchange = false)
 {
     const cudaStream_t s = m->stream;
+    if (exchange && (p.parts.size() != 1 || !p.parts[0].int_path))
+        return fail("the fused exchange takes one integer-path matrix%s", "");
     const int width = p.width;
     if (in.mode != q38::kActQ8K && has_float_part(p)) {
         float *f = in.f_out ? in.f_out : m->act_f;
@@ -935,7 +955,7 @@ bool project(Q38Model *m, const Proj &p, ActIn in, int tokens, float *out, int o
                 return false;
             const bool exporting = share && i == 0 && pin.mode == q38::kActRmsNorm;
             if (!stream_project(part, pin, tokens, out + part.offset, out_ld, accumulate, orep, prefetch_of(next), s,
-                                nullptr, m, exporting ? m->q8_norm : nullptr))
+                                nullptr, m, exporting ? m->q8_norm : nullptr, exchange))
                 return false;
         } else {
             float_part = true;
@@ -1162,7 +1182,11 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
         d.trace = next_trace(m);
         if (!cuda_ok(q38::launch_deltanet(d, s), "deltanet")) return false;
     }
-    if (tp) {
+    if (tp && m->xc) {
+        // row-parallel, the exchange fused into the GEMV: hidden += the sum over the GPUs
+        if (!project(m, L.out, mixed, tokens, m->hidden, kHidden, 1, hidden_out(), first_part(L.gate_up), true))
+            return false;
+    } else if (tp) {
         // row-parallel: this shard's partial sums, added up across the GPUs
         if (!project(m, L.out, mixed, tokens, m->partial, kHidden, 0, OutReps(), first_part(L.gate_up)) ||
             !reduce_into_hidden(m, tokens))
@@ -1190,6 +1214,7 @@ bool enqueue_layer(Q38Model *m, int l, int tokens, uint32_t base_hint)
     if (!project(m, L.gate_up, rmsnorm_input(m->hidden, L.post_norm), tokens, m->wide, m->wide_ld, 0, wide_out,
                  first_part(L.down)))
         return false;
+    if (tp && m->xc) return project(m, L.down, swiglu_input(m), tokens, m->hidden, kHidden, 1, hidden_out(), after, true);
     if (tp)
         return project(m, L.down, swiglu_input(m), tokens, m->partial, kHidden, 0, OutReps(), after) &&
                reduce_into_hidden(m, tokens);
@@ -1547,17 +1572,23 @@ bool nccl_ok(ncclResult_t r, const char *what)
     return fail("%s", std::string(what) + ": " + (api ? api->error_string(r) : "NCCL unavailable"));
 }
 
-constexpr size_t kArFlagBytes = 4096;  // flags area ahead of the exchange buffer
+constexpr size_t kArFlagBytes = 4096;  // tp_reduce_kernel's flags
+constexpr size_t kXcFlagBytes = sizeof(unsigned int) * q38::kXcMaxWorld * q38::kXcMaxTiles;  // the fused exchange's
 
 // Exchange buffers for the NVLink all-reduce: one allocation per rank
-// ([flags][2 halves x world slots x 8 tokens x 5120 floats]), its IPC handle
-// all-gathered over the NCCL communicator, the peers' allocations opened.
-bool setup_p2p(Q38Model *m)
+// ([tp_reduce flags][exchange flags][2 halves x world slots x 8 tokens x 5120
+// floats]), its IPC handle all-gathered over the NCCL communicator, the peers'
+// allocations opened.  `mode` 1: tp_reduce_kernel, 2: fused into the GEMVs.
+bool setup_p2p(Q38Model *m, int mode)
 {
     const int world = m->shard.world, rank = m->shard.rank;
-    const size_t bytes = kArFlagBytes + static_cast<size_t>(2) * world * kMaxTokens * kHidden * sizeof(float);
+    const size_t bytes =
+        kArFlagBytes + kXcFlagBytes + static_cast<size_t>(2) * world * kMaxTokens * kHidden * sizeof(float);
     static_assert(8 * q38::kTpReduceCtas * sizeof(unsigned long long) <= kArFlagBytes, "flags area");
-    if (!dalloc(&m->ar_base, bytes, m->owned) || !dalloc(&m->ar_counter, 2, m->owned)) return false;
+    static_assert(kMaxTokens == q38::kXcTokens, "exchange slots");
+    if (!dalloc(&m->ar_base, bytes, m->owned) || !dalloc(&m->ar_counter, 2, m->owned) ||
+        !dalloc(&m->xc_counter, 2, m->owned))
+        return false;
     cudaIpcMemHandle_t mine;
     if (!cuda_ok(cudaIpcGetMemHandle(&mine, m->ar_base), "cudaIpcGetMemHandle")) return false;
     uint8_t *dev_handles = nullptr;
@@ -1582,9 +1613,12 @@ bool setup_p2p(Q38Model *m)
             base = static_cast<uint8_t *>(p);
         }
         m->ar_flags[r] = reinterpret_cast<unsigned long long *>(base);
-        m->ar_bufs[r] = reinterpret_cast<float *>(base + kArFlagBytes);
+        m->xc_flags[r] = reinterpret_cast<unsigned int *>(base + kArFlagBytes);
+        m->ar_bufs[r] = reinterpret_cast<float *>(base + kArFlagBytes + kXcFlagBytes);
     }
-    m->p2p = true;
+    m->p2p = mode == 1;
+    m->xc = mode == 2;
+    m->tp_mode = mode;
     return true;
 }
 
@@ -1689,7 +1723,8 @@ bool ensure_prefill_buffers(Q38Model *m, int cap)
               pf_alloc(m, reinterpret_cast<uint16_t **>(&m->pf_a16), 2 * tc_a16_elements(m)) &&
               pf_alloc(m, reinterpret_cast<uint16_t **>(&m->pf_b16), 2 * n * kFfn) &&
               pf_alloc(m, &m->pf_row_scale, static_cast<size_t>(m->wide_ld)) && pf_alloc(m, &m->pf_ids, n) &&
-              pf_alloc(m, &m->pf_oraw, n * kLinV);
+              pf_alloc(m, &m->pf_oraw, n * kLinV) &&
+              pf_alloc(m, &m->pf_rec, q38::delta_prefill_rec_floats(m->lin_heads / 3, (cap + 31) / 32 * 32));
     if (ok && m->host_pf_ids) {
         cudaFreeHost(m->host_pf_ids);
         m->host_pf_ids = nullptr;
@@ -1785,6 +1820,9 @@ bool tc_layer(Q38Model *m, int l, int n, uint32_t base)
         d.o_ld = m->lin_heads * kLinDim;
         d.out_f = m->pf_act;
         d.out_q = mix;
+        d.n_kh = m->lin_heads / 3;
+        d.rec = m->pf_rec;
+        d.rec_tokens = (n + 31) / 32 * 32;
         if (!cuda_ok(q38::launch_deltanet_prefill(d, s), "deltanet prefill")) return false;
     }
     if (L.full) {
@@ -1930,7 +1968,8 @@ Q38Model *open_model(const char *path, uint32_t context_length, int rank, int wo
         const NcclApi *api = nccl();
         ok = nccl_ok(api->comm_init_rank(&m->comm, world, *id, rank), "ncclCommInitRank");
         const char *p2p = std::getenv("Q38CU_TP_P2P");
-        if (ok && p2p && *p2p == '1') ok = setup_p2p(m);
+        const int mode = p2p && (*p2p == '1' || *p2p == '2') ? *p2p - '0' : 0;
+        if (ok && mode) ok = setup_p2p(m, mode);
     }
     if (ok) {
         const char *tv = std::getenv("Q38CU_TRACE");

@@ -74,7 +74,15 @@ struct DeltaPrefillArgs {
     float *out_f;         // optional [tokens][o_ld]
     void *out_q;          // [tokens][o_ld / 256] Q8_K
     int n_kh;             // key heads (0: 16)
+    float *rec;           // state-independent records of the chunk (16-byte aligned)
+    int rec_tokens;       // token stride of `rec`: >= tokens, a multiple of 32
 };
+
+// Floats of the DeltaNet prefill records for `rec_tokens` tokens (key heads n_kh).
+inline size_t delta_prefill_rec_floats(int n_kh, int rec_tokens)
+{
+    return static_cast<size_t>(rec_tokens) * (static_cast<size_t>(n_kh) * 256 + static_cast<size_t>(3 * n_kh) * 130);
+}
 
 struct AttnArgs {
     const float *qkv;  // per token: q|gate interleaved per head (12288), k at k_off, v at v_off

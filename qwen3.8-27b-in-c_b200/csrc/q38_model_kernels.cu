@@ -607,167 +607,228 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
 
 // ---------------------------------------------------------------------------
 // Gated-DeltaNet over a whole prefill chunk (qwen38_model.c:715-792 for each
-// token of the chunk in order, as q38_batch_layer runs it, :1078-1085).
+// token of the chunk in order, as q38_batch_layer runs it, :1078-1085), in
+// four launches:
 //
-// The recurrence is serial in tokens but independent per state column: with
-// q, k, v, beta and the decay of a token known, column j of a head's state
-// only needs its own 128 values.  So each warp owns 8 columns of one value
-// head (lane l holds rows 4l .. 4l + 3 of each, in registers for the whole
-// chunk) and walks all the chunk's tokens without any exchange between warps:
-// per token it forms the causal conv + SiLU of its key head's 128 q and k
-// channels (4 per lane) and of its 8 v channels, their L2 norms (warp
-// reductions), beta and the decay, applies the delta rule to its columns and
-// stores the raw head output (before the head RMSNorm).  The next token's
-// inputs are loaded while the current one is processed.  The token-parallel
-// rest - head RMSNorm, the gate and Q8_K - runs afterwards over all tokens at
-// once (deltanet_prefill_post_kernel), and the conv ring is written by a
-// third kernel once every reader is done (deltanet_ring_store_kernel).
+//  1. deltanet_prefill_prep_kernel (token-parallel): everything that does not
+//     depend on the recurrent state - the causal conv + SiLU of every q, k and
+//     v channel, the L2 norms of q and k, beta and the decay - written as
+//     records laid out for the serial kernel's bulk copies:
+//       qk  [key head][token][256]    q (128) then k (128), normalized
+//       v   [value head][4][token][32] the 128 v channels, 32 per column block
+//       gb  [value head][token][2]    beta, decay
+//     (token stride rec_tokens, a multiple of kDeltaChunk).
+//  2. deltanet_prefill_kernel (serial in tokens): each warp owns 8 columns of
+//     one value head's state (lane l holds rows 4l .. 4l + 3 of each, in
+//     registers for the whole chunk); a CTA's 4 warps share the records of
+//     one column block, streamed into a ring of shared-memory stages by
+//     cp.async.bulk kDeltaChunk tokens at a time, so the token loop reads only
+//     shared memory.  It stores the raw head output (before the RMSNorm).
+//  3. deltanet_prefill_post_kernel: head RMSNorm, the gate, Q8_K.
+//  4. deltanet_ring_store_kernel: the conv ring, once every reader is done.
+// Steps 1-2 compute each value with the same operations in the same order as
+// a single kernel that walked the tokens itself.
 // ---------------------------------------------------------------------------
+constexpr int kDeltaChunk = 32;   // tokens per bulk-copy stage
+constexpr int kDeltaStages = 3;
+constexpr uint32_t kDeltaQkBytes = kDeltaChunk * 256 * 4, kDeltaVBytes = kDeltaChunk * 32 * 4,
+                   kDeltaGbBytes = kDeltaChunk * 2 * 4;
+constexpr uint32_t kDeltaStageBytes = kDeltaQkBytes + kDeltaVBytes + kDeltaGbBytes;
+constexpr size_t kDeltaSmem = static_cast<size_t>(kDeltaStages) * kDeltaStageBytes + 64;
+
+// Conv + SiLU of one channel at position p (qwen38_model.c:722-737):
+// ((x[p-3] w0 + x[p-2] w1) + x[p-1] w2) + x[p] w3, positions before 0 read 0,
+// positions before the chunk read the conv ring.
+__device__ __forceinline__ float prefill_conv(const DeltaPrefillArgs &a, int ch, int p, float4 w)
+{
+    auto input = [&](int q) -> float {
+        if (q < 0) return 0.0f;
+        return q >= a.base ? a.qkvz[static_cast<size_t>(q - a.base) * a.qkvz_ld + ch]
+                           : a.conv_ring[static_cast<size_t>(ch) * 16 + (q & 15)];
+    };
+    float c = __fmul_rn(input(p - 3), w.x);
+    c = __fadd_rn(c, __fmul_rn(input(p - 2), w.y));
+    c = __fadd_rn(c, __fmul_rn(input(p - 1), w.z));
+    return silu(__fadd_rn(c, __fmul_rn(input(p), w.w)));
+}
+
+// One CTA of 256 threads per token; warp w takes tasks w, w + 8, ...: tasks
+// 0 .. n_kh - 1 are key heads (q and k), the rest value heads (v, beta,
+// decay).  Lane l holds channels 4l .. 4l + 3.
+__global__ void __launch_bounds__(256) deltanet_prefill_prep_kernel(DeltaPrefillArgs a)
+{
+    pdl_wait();
+    const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int n_kh = a.n_kh > 0 ? a.n_kh : 16, n_vh = 3 * n_kh;
+    const int p = a.base + t;
+    const size_t rt = static_cast<size_t>(a.rec_tokens);
+    float *rec_qk = a.rec, *rec_v = a.rec + static_cast<size_t>(n_kh) * rt * 256,
+          *rec_gb = rec_v + static_cast<size_t>(n_vh) * rt * 128;
+    for (int task = warp; task < n_kh + n_vh; task += 8) {
+        if (task < n_kh) {
+            const int kh = task;
+            const int ch_q = kh * 128 + lane * 4, ch_k = n_kh * 128 + kh * 128 + lane * 4;
+            float qv[4], kv[4];
+            double pq = 0.0, pk = 0.0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                qv[i] = prefill_conv(a, ch_q + i, p, __ldg(reinterpret_cast<const float4 *>(a.conv_w) + ch_q + i));
+                kv[i] = prefill_conv(a, ch_k + i, p, __ldg(reinterpret_cast<const float4 *>(a.conv_w) + ch_k + i));
+                pq += static_cast<double>(__fmul_rn(qv[i], qv[i]));
+                pk += static_cast<double>(__fmul_rn(kv[i], kv[i]));
+            }
+            // L2 norms (qwen38_model.c:608-614)
+            const double sq = warp_sum_d(pq), sk = warp_sum_d(pk);
+            const float scale_q = __fdiv_rn(1.0f, fmaxf(sqrtf(static_cast<float>(sq)), kRmsEps));
+            const float scale_k = __fdiv_rn(1.0f, fmaxf(sqrtf(static_cast<float>(sk)), kRmsEps));
+            float *dst = rec_qk + (static_cast<size_t>(kh) * rt + t) * 256;
+            reinterpret_cast<float4 *>(dst)[lane] =
+                make_float4(__fmul_rn(qv[0], scale_q), __fmul_rn(qv[1], scale_q), __fmul_rn(qv[2], scale_q),
+                            __fmul_rn(qv[3], scale_q));
+            reinterpret_cast<float4 *>(dst + 128)[lane] =
+                make_float4(__fmul_rn(kv[0], scale_k), __fmul_rn(kv[1], scale_k), __fmul_rn(kv[2], scale_k),
+                            __fmul_rn(kv[3], scale_k));
+        } else {
+            const int vh = task - n_kh;
+            const int ch = 2 * n_kh * 128 + vh * 128 + lane * 4;
+            float v[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                v[i] = prefill_conv(a, ch + i, p, __ldg(reinterpret_cast<const float4 *>(a.conv_w) + ch + i));
+            // channel 4l + i sits in column block l / 8, slot 4 (l % 8) + i
+            float *dst = rec_v + ((static_cast<size_t>(vh) * 4 + lane / 8) * rt + t) * 32 + (lane % 8) * 4;
+            *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+            if (lane == 0) {
+                // beta and the decay (qwen38_model.c:748-752)
+                const float br = a.beta[static_cast<size_t>(t) * a.ba_ld + vh];
+                const float ar = a.alpha[static_cast<size_t>(t) * a.ba_ld + vh];
+                float2 gb;
+                gb.x = sigmoid(br);
+                gb.y = expf(__fmul_rn(a.a[vh], softplus(__fadd_rn(ar, a.dt[vh]))));
+                reinterpret_cast<float2 *>(rec_gb)[static_cast<size_t>(vh) * rt + t] = gb;
+            }
+        }
+    }
+    pdl_launch_dependents();
+}
+
+// The serial recurrence.  Grid: value heads x 4 column blocks, 128 threads;
+// thread 0 also issues the stage copies.  A stage holds kDeltaChunk tokens:
+// [token][256] q|k of the head's key head, [token][32] v of the column block,
+// [token][2] beta, decay.
 __global__ void __launch_bounds__(128) deltanet_prefill_kernel(DeltaPrefillArgs a)
 {
+    extern __shared__ __align__(128) uint8_t dsm[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(dsm + static_cast<size_t>(kDeltaStages) * kDeltaStageBytes);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int n_kh = a.n_kh > 0 ? a.n_kh : 16;
-    const int vh = blockIdx.x >> 2, col0 = (blockIdx.x & 3) * 32 + warp * 8;
+    const int n_kh = a.n_kh > 0 ? a.n_kh : 16, n_vh = 3 * n_kh;
+    const int vh = blockIdx.x >> 2, cb = blockIdx.x & 3, col0 = cb * 32 + warp * 8;
     const int kh = vh % n_kh;
-    const int ch_q = kh * 128 + lane * 4, ch_k = n_kh * 128 + kh * 128 + lane * 4;
-    const int ch_v = 2 * n_kh * 128 + vh * 128 + col0 + (lane & 7);  // lanes 0..7: one v channel each
-    const int base = a.base;
-    // conv kernels of this lane's channels
-    float4 wq[4], wk[4], wv;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        wq[i] = __ldg(reinterpret_cast<const float4 *>(a.conv_w) + ch_q + i);
-        wk[i] = __ldg(reinterpret_cast<const float4 *>(a.conv_w) + ch_k + i);
+    const size_t rt = static_cast<size_t>(a.rec_tokens);
+    const float *rec_qk = a.rec + static_cast<size_t>(kh) * rt * 256;
+    const float *rec_v = a.rec + static_cast<size_t>(n_kh) * rt * 256 + (static_cast<size_t>(vh) * 4 + cb) * rt * 32;
+    const float *rec_gb = a.rec + static_cast<size_t>(n_kh) * rt * 256 + static_cast<size_t>(n_vh) * rt * 128 +
+                          static_cast<size_t>(vh) * rt * 2;
+    const int chunks = (a.tokens + kDeltaChunk - 1) / kDeltaChunk;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kDeltaStages; ++i) mbar_init(&full[i], 1);
+        fence_mbar_init();
     }
-    wv = __ldg(reinterpret_cast<const float4 *>(a.conv_w) + ch_v);
     // the state columns
     float *state = a.state + (static_cast<size_t>(vh) * 128 + col0) * 128 + lane * 4;
     float4 s[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) s[j] = *reinterpret_cast<const float4 *>(state + j * 128);
-    const float a_h = a.a[vh], dt_h = a.dt[vh];
     const float query_scale = __fdiv_rn(1.0f, sqrtf(128.0f));
+    __syncthreads();
     pdl_wait();
-
-    // the conv window of each channel: inputs of positions p - 3, p - 2, p - 1
-    // (from the ring before the chunk start, from the projections after)
-    auto input = [&](int ch, int p) -> float {
-        return p >= base ? a.qkvz[static_cast<size_t>(p - base) * a.qkvz_ld + ch]
-                         : a.conv_ring[static_cast<size_t>(ch) * 16 + (p & 15)];
+    auto issue = [&](int c) {
+        uint8_t *st = dsm + static_cast<size_t>(c % kDeltaStages) * kDeltaStageBytes;
+        uint64_t *bar = &full[c % kDeltaStages];
+        const size_t t0 = static_cast<size_t>(c) * kDeltaChunk;
+        mbar_arrive_expect_tx(bar, kDeltaStageBytes);
+        bulk_copy_g2s(st, rec_qk + t0 * 256, kDeltaQkBytes, bar);
+        bulk_copy_g2s(st + kDeltaQkBytes, rec_v + t0 * 32, kDeltaVBytes, bar);
+        bulk_copy_g2s(st + kDeltaQkBytes + kDeltaVBytes, rec_gb + t0 * 2, kDeltaGbBytes, bar);
     };
-    float hq[4][3], hk[4][3], hv[3];
-#pragma unroll
-    for (int d = 0; d < 3; ++d) {
-        const int p = base - 3 + d;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            hq[i][d] = p >= 0 ? input(ch_q + i, p) : 0.0f;
-            hk[i][d] = p >= 0 ? input(ch_k + i, p) : 0.0f;
+    if (threadIdx.x == 0)
+        for (int c = 0; c < kDeltaStages && c < chunks; ++c) issue(c);
+    int issued = min(chunks, kDeltaStages);  // chunks whose copies were issued (same in every thread)
+    bool failed = false;
+    for (int c = 0; c < chunks && !failed; ++c) {
+        const uint8_t *st = dsm + static_cast<size_t>(c % kDeltaStages) * kDeltaStageBytes;
+        const bool arrived =
+            mbar_wait_bounded(&full[c % kDeltaStages], static_cast<uint32_t>(c / kDeltaStages) & 1u, &g_model_status);
+        if (__syncthreads_or(!arrived)) {
+            failed = true;
+            break;
         }
-        hv[d] = p >= 0 ? input(ch_v, p) : 0.0f;
+        const float *sqk = reinterpret_cast<const float *>(st);
+        const float *sv = reinterpret_cast<const float *>(st + kDeltaQkBytes);
+        const float *sgb = reinterpret_cast<const float *>(st + kDeltaQkBytes + kDeltaVBytes);
+        const int n = min(kDeltaChunk, a.tokens - c * kDeltaChunk);
+        for (int i = 0; i < n; ++i) {
+            const int t = c * kDeltaChunk + i;
+            const float4 q4 = reinterpret_cast<const float4 *>(sqk + i * 256)[lane];
+            const float4 k4 = reinterpret_cast<const float4 *>(sqk + i * 256 + 128)[lane];
+            const float vcol = sv[i * 32 + warp * 8 + (lane & 7)];
+            const float2 gb = reinterpret_cast<const float2 *>(sgb)[i];
+            const float beta = gb.x, decay = gb.y;
+            // delta rule on the warp's 8 columns (qwen38_model.c:758-781)
+            float red[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float4 &x = s[j];
+                x.x = __fmul_rn(x.x, decay);
+                x.y = __fmul_rn(x.y, decay);
+                x.z = __fmul_rn(x.z, decay);
+                x.w = __fmul_rn(x.w, decay);
+                red[j] = fmaf(x.w, k4.w, fmaf(x.z, k4.z, fmaf(x.y, k4.y, __fmul_rn(x.x, k4.x))));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) red[j] = __fadd_rn(red[j], __shfl_xor_sync(0xffffffffu, red[j], o));
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float4 &x = s[j];
+                const float vj = __shfl_sync(0xffffffffu, vcol, j);
+                const float delta = __fmul_rn(__fsub_rn(vj, red[j]), beta);
+                x.x = fmaf(k4.x, delta, x.x);
+                x.y = fmaf(k4.y, delta, x.y);
+                x.z = fmaf(k4.z, delta, x.z);
+                x.w = fmaf(k4.w, delta, x.w);
+                red[j] = fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, __fmul_rn(x.x, q4.x))));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) red[j] = __fadd_rn(red[j], __shfl_xor_sync(0xffffffffu, red[j], o));
+            }
+            if (lane < 8) {
+                float mine = red[0];
+#pragma unroll
+                for (int j = 1; j < 8; ++j)
+                    if (lane == j) mine = red[j];
+                a.o_raw[static_cast<size_t>(t) * a.o_ld + vh * 128 + col0 + lane] = __fmul_rn(mine, query_scale);
+            }
+        }
+        // every warp is done with this stage: refill it with chunk c + kDeltaStages
+        __syncthreads();
+        if (c + kDeltaStages < chunks) {
+            if (threadIdx.x == 0) {
+                fence_proxy_async_shared();
+                issue(c + kDeltaStages);
+            }
+            issued = c + kDeltaStages + 1;
+        }
     }
-    // token 0's inputs
-    float4 xq = *reinterpret_cast<const float4 *>(a.qkvz + ch_q);
-    float4 xk = *reinterpret_cast<const float4 *>(a.qkvz + ch_k);
-    float xv = a.qkvz[ch_v];
-    float br = a.beta[vh], ar = a.alpha[vh];
-    for (int t = 0; t < a.tokens; ++t) {
-        // the next token's inputs, in flight during this token's work
-        float4 nq = xq, nk = xk;
-        float nv = xv, nbr = br, nar = ar;
-        if (t + 1 < a.tokens) {
-            const float *row = a.qkvz + static_cast<size_t>(t + 1) * a.qkvz_ld;
-            nq = *reinterpret_cast<const float4 *>(row + ch_q);
-            nk = *reinterpret_cast<const float4 *>(row + ch_k);
-            nv = row[ch_v];
-            nbr = a.beta[static_cast<size_t>(t + 1) * a.ba_ld + vh];
-            nar = a.alpha[static_cast<size_t>(t + 1) * a.ba_ld + vh];
-        }
-        // causal conv + SiLU ((s0 k0 + s1 k1) + s2 k2) + x k3, qwen38_model.c:722-737
-        const float xqa[4] = {xq.x, xq.y, xq.z, xq.w}, xka[4] = {xk.x, xk.y, xk.z, xk.w};
-        float qv[4], kv[4];
-        double pq = 0.0, pk = 0.0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            float c = __fmul_rn(hq[i][0], wq[i].x);
-            c = __fadd_rn(c, __fmul_rn(hq[i][1], wq[i].y));
-            c = __fadd_rn(c, __fmul_rn(hq[i][2], wq[i].z));
-            qv[i] = silu(__fadd_rn(c, __fmul_rn(xqa[i], wq[i].w)));
-            float e = __fmul_rn(hk[i][0], wk[i].x);
-            e = __fadd_rn(e, __fmul_rn(hk[i][1], wk[i].y));
-            e = __fadd_rn(e, __fmul_rn(hk[i][2], wk[i].z));
-            kv[i] = silu(__fadd_rn(e, __fmul_rn(xka[i], wk[i].w)));
-            pq += static_cast<double>(__fmul_rn(qv[i], qv[i]));
-            pk += static_cast<double>(__fmul_rn(kv[i], kv[i]));
-            hq[i][0] = hq[i][1];
-            hq[i][1] = hq[i][2];
-            hq[i][2] = xqa[i];
-            hk[i][0] = hk[i][1];
-            hk[i][1] = hk[i][2];
-            hk[i][2] = xka[i];
-        }
-        float cv = __fmul_rn(hv[0], wv.x);
-        cv = __fadd_rn(cv, __fmul_rn(hv[1], wv.y));
-        cv = __fadd_rn(cv, __fmul_rn(hv[2], wv.z));
-        const float vcol = silu(__fadd_rn(cv, __fmul_rn(xv, wv.w)));
-        hv[0] = hv[1];
-        hv[1] = hv[2];
-        hv[2] = xv;
-        // L2 norms of q and k (qwen38_model.c:608-614)
-        const double sq = warp_sum_d(pq), sk = warp_sum_d(pk);
-        const float scale_q = __fdiv_rn(1.0f, fmaxf(sqrtf(static_cast<float>(sq)), kRmsEps));
-        const float scale_k = __fdiv_rn(1.0f, fmaxf(sqrtf(static_cast<float>(sk)), kRmsEps));
-        const float4 q4 = make_float4(__fmul_rn(qv[0], scale_q), __fmul_rn(qv[1], scale_q), __fmul_rn(qv[2], scale_q),
-                                      __fmul_rn(qv[3], scale_q));
-        const float4 k4 = make_float4(__fmul_rn(kv[0], scale_k), __fmul_rn(kv[1], scale_k), __fmul_rn(kv[2], scale_k),
-                                      __fmul_rn(kv[3], scale_k));
-        // beta and the decay (qwen38_model.c:748-752)
-        const float beta = sigmoid(br);
-        const float decay = expf(__fmul_rn(a_h, softplus(__fadd_rn(ar, dt_h))));
-        // delta rule on the warp's 8 columns (qwen38_model.c:758-781)
-        float red[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            float4 &x = s[j];
-            x.x = __fmul_rn(x.x, decay);
-            x.y = __fmul_rn(x.y, decay);
-            x.z = __fmul_rn(x.z, decay);
-            x.w = __fmul_rn(x.w, decay);
-            red[j] = fmaf(x.w, k4.w, fmaf(x.z, k4.z, fmaf(x.y, k4.y, __fmul_rn(x.x, k4.x))));
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) red[j] = __fadd_rn(red[j], __shfl_xor_sync(0xffffffffu, red[j], o));
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            float4 &x = s[j];
-            const float vj = __shfl_sync(0xffffffffu, vcol, j);
-            const float delta = __fmul_rn(__fsub_rn(vj, red[j]), beta);
-            x.x = fmaf(k4.x, delta, x.x);
-            x.y = fmaf(k4.y, delta, x.y);
-            x.z = fmaf(k4.z, delta, x.z);
-            x.w = fmaf(k4.w, delta, x.w);
-            red[j] = fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, __fmul_rn(x.x, q4.x))));
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) red[j] = __fadd_rn(red[j], __shfl_xor_sync(0xffffffffu, red[j], o));
-        }
-        if (lane < 8) {
-            float mine = red[0];
-#pragma unroll
-            for (int j = 1; j < 8; ++j)
-                if (lane == j) mine = red[j];
-            a.o_raw[static_cast<size_t>(t) * a.o_ld + vh * 128 + col0 + lane] = __fmul_rn(mine, query_scale);
-        }
-        xq = nq;
-        xk = nk;
-        xv = nv;
-        br = nbr;
-        ar = nar;
+    if (failed && threadIdx.x == 0) {
+        // copies still in flight land before the CTA's shared memory is released:
+        // wait (bounded) for the last issued chunk of every stage
+        for (int c = max(0, issued - kDeltaStages); c < issued; ++c)
+            mbar_wait_bounded(&full[c % kDeltaStages], static_cast<uint32_t>(c / kDeltaStages) & 1u, nullptr);
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) *reinterpret_cast<float4 *>(state + j * 128) = s[j];
@@ -1057,13 +1118,15 @@ __global__ void __launch_bounds__(256) attention_kernel(AttnArgs a)
 //  1. attn_prefill_qk_kernel: per (token, head) the query's RMSNorm + RoPE into
 //     qbuf, and per (token, KV head) the key's RMSNorm + RoPE and the value into
 //     the KV cache at the token's position (one CTA of 256 threads each).
-//  2. attn_prefill_kernel: a CTA takes 8 consecutive query tokens (one per
-//     warp) of one head and walks the cached positions 0 .. its last query's
-//     position in tiles of 32 (K transposed and V staged in shared memory):
-//     lane l scores position p0 + l against the warp's query, the warp keeps a
-//     running softmax and lane l accumulates dimensions 8l .. 8l + 7 of the
-//     weighted values; positions past a query's own are masked.  Then the
-//     sigmoid gate, into out_f.
+//  2. attn_prefill_kernel: a CTA takes 64 consecutive query tokens of one
+//     head and walks the cached positions 0 .. its last query's position in
+//     tiles of 64 keys (Q, K and V rows staged in shared memory, fp32).  Thread
+//     (qg, kg) of the 16 x 16 grid scores queries qg + 16i against keys
+//     kg + 16j (16 fp32 dot products, dimensions in order), the scores go
+//     through shared memory to a running softmax per query (4 threads a row),
+//     and the thread accumulates dimensions 4kg + 64j .. + 3 of the weighted
+//     values of its 4 queries; positions past a query's own are masked.  Then
+//     the sigmoid gate, into out_f.  Query tiles run heaviest (latest) first.
 //  3. attn_prefill_quant_kernel: the Q8_K block of each (token, head).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) attn_prefill_qk_kernel(AttnPrefillArgs a)
@@ -1087,83 +1150,151 @@ __global__ void __launch_bounds__(256) attn_prefill_qk_kernel(AttnPrefillArgs a)
     pdl_launch_dependents();
 }
 
-constexpr int kPfQueries = 8, kPfKeys = 32;
-// shared memory of attn_prefill_kernel: K^T [256][33], V [32][256], queries [8][256]
-constexpr size_t kPfSmem = (static_cast<size_t>(kAttnDim) * (kPfKeys + 1) + kPfKeys * kAttnDim + kPfQueries * kAttnDim) *
-                           sizeof(float);
+constexpr int kPfQueries = 64, kPfKeys = 64;
+constexpr int kPfLd = kAttnDim + 4;  // padded Q / K row: 16-byte bank shift per row
+constexpr int kPfPLd = kPfKeys + 4;
+// shared memory of attn_prefill_kernel: Q [64][260], K [64][260], V [64][256],
+// P [64][68], correction [64], sum [64]
+constexpr size_t kPfSmem =
+    (static_cast<size_t>(kPfQueries) * kPfLd + static_cast<size_t>(kPfKeys) * kPfLd +
+     static_cast<size_t>(kPfKeys) * kAttnDim + static_cast<size_t>(kPfQueries) * kPfPLd + 2 * kPfQueries) *
+    sizeof(float);
 
-__global__ void __launch_bounds__(256) attn_prefill_kernel(AttnPrefillArgs a)
+__global__ void __launch_bounds__(256, 1) attn_prefill_kernel(AttnPrefillArgs a)
 {
     extern __shared__ __align__(16) float pf_smem[];
-    float *kt = pf_smem;                               // [256][33]
-    float *vs = kt + kAttnDim * (kPfKeys + 1);         // [32][256]
-    float *qs = vs + kPfKeys * kAttnDim;               // [8][256]
+    float *qs = pf_smem;                          // [64][kPfLd]
+    float *ks = qs + kPfQueries * kPfLd;          // [64][kPfLd]
+    float *vs = ks + kPfKeys * kPfLd;             // [64][256]
+    float *ps = vs + kPfKeys * kAttnDim;          // [64][kPfPLd]
+    float *corr = ps + kPfQueries * kPfPLd;       // [64]
+    float *lsum = corr + kPfQueries;              // [64]
     pdl_wait();
-    const int h = blockIdx.y, t0 = blockIdx.x * kPfQueries;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = t0 + warp;
-    const bool live = t < a.tokens;
-    const int pos = a.base + (live ? t : a.tokens - 1);
+    const int tiles = (a.tokens + kPfQueries - 1) / kPfQueries;
+    const int h = blockIdx.y, t0 = (tiles - 1 - static_cast<int>(blockIdx.x)) * kPfQueries;
+    const int tid = threadIdx.x, kg = tid & 15, qg = tid >> 4;
     const int g = (a.head0 + h) / (kAttnHeads / 4) - a.kv0;
     const int last = a.base + min(t0 + kPfQueries - 1, a.tokens - 1);
-    for (int i = lane; i < kAttnDim; i += 32)
-        qs[warp * kAttnDim + i] = live ? a.qbuf[(static_cast<size_t>(t) * a.heads + h) * kAttnDim + i] : 0.0f;
-    float m_run = -INFINITY, l_run = 0.0f, acc[8];
+    for (int i = tid; i < kPfQueries * kAttnDim / 4; i += blockDim.x) {
+        const int r = i / (kAttnDim / 4), c4 = i % (kAttnDim / 4);
+        const int t = min(t0 + r, a.tokens - 1);
+        *reinterpret_cast<float4 *>(qs + r * kPfLd + c4 * 4) =
+            *reinterpret_cast<const float4 *>(a.qbuf + (static_cast<size_t>(t) * a.heads + h) * kAttnDim + c4 * 4);
+    }
+    // running softmax of row srow (keys 16 spart .. + 15 of each tile)
+    const int srow = tid >> 2, spart = tid & 3;
+    const int spos = a.base + min(t0 + srow, a.tokens - 1);
+    float m_run = -INFINITY, l_run = 0.0f;
+    float acc[4][16];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int e = 0; e < 16; ++e) acc[i][e] = 0.0f;
     for (int p0 = 0; p0 <= last; p0 += kPfKeys) {
         __syncthreads();  // the previous tile is consumed (and qs is written)
-        for (int i = threadIdx.x; i < kPfKeys * kAttnDim / 4; i += blockDim.x) {
+        for (int i = tid; i < kPfKeys * kAttnDim / 4; i += blockDim.x) {
             const int key = i / (kAttnDim / 4), d4 = i % (kAttnDim / 4);
             const int p = min(p0 + key, last);  // past `last`: a valid row, masked below
             const size_t off = static_cast<size_t>(p) * a.kv_ld + g * kAttnDim + d4 * 4;
-            const float4 k4 = kv_load4(a.k_cache, off, a.kv_half);
-            kt[(d4 * 4 + 0) * (kPfKeys + 1) + key] = k4.x;
-            kt[(d4 * 4 + 1) * (kPfKeys + 1) + key] = k4.y;
-            kt[(d4 * 4 + 2) * (kPfKeys + 1) + key] = k4.z;
-            kt[(d4 * 4 + 3) * (kPfKeys + 1) + key] = k4.w;
+            *reinterpret_cast<float4 *>(ks + key * kPfLd + d4 * 4) = kv_load4(a.k_cache, off, a.kv_half);
             *reinterpret_cast<float4 *>(vs + key * kAttnDim + d4 * 4) = kv_load4(a.v_cache, off, a.kv_half);
         }
         __syncthreads();
-        // score of position p0 + lane (q . k in dimension order, then / sqrt(256))
-        const float *q = qs + warp * kAttnDim;
-        float sc = 0.0f;
-#pragma unroll 8
-        for (int d = 0; d < kAttnDim; ++d) sc = __fadd_rn(sc, __fmul_rn(q[d], kt[d * (kPfKeys + 1) + lane]));
-        const bool valid = p0 + lane <= pos;
-        sc = valid ? __fmul_rn(sc, 0.0625f) : -INFINITY;
-        float tile_max = sc;
+        // scores of queries qg + 16i against keys kg + 16j (dimensions in order)
+        float sc[4][4];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) tile_max = fmaxf(tile_max, __shfl_xor_sync(0xffffffffu, tile_max, o));
-        const float m_new = fmaxf(m_run, tile_max);
-        const float c = m_run == -INFINITY ? 0.0f : expf(__fsub_rn(m_run, m_new));
-        const float w = valid ? expf(__fsub_rn(sc, m_new)) : 0.0f;
-        float wsum = w;
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) wsum = __fadd_rn(wsum, __shfl_xor_sync(0xffffffffu, wsum, o));
-        l_run = __fadd_rn(__fmul_rn(l_run, c), wsum);
+            for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
+#pragma unroll 2
+        for (int d = 0; d < kAttnDim; d += 4) {
+            float4 qv[4], kv[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = __fmul_rn(acc[i], c);
-        for (int key = 0; key < kPfKeys; ++key) {
-            const float wk = __shfl_sync(0xffffffffu, w, key);
-            const float4 va = *reinterpret_cast<const float4 *>(vs + key * kAttnDim + lane * 8);
-            const float4 vb = *reinterpret_cast<const float4 *>(vs + key * kAttnDim + lane * 8 + 4);
-            acc[0] = fmaf(wk, va.x, acc[0]);
-            acc[1] = fmaf(wk, va.y, acc[1]);
-            acc[2] = fmaf(wk, va.z, acc[2]);
-            acc[3] = fmaf(wk, va.w, acc[3]);
-            acc[4] = fmaf(wk, vb.x, acc[4]);
-            acc[5] = fmaf(wk, vb.y, acc[5]);
-            acc[6] = fmaf(wk, vb.z, acc[6]);
-            acc[7] = fmaf(wk, vb.w, acc[7]);
+            for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4 *>(qs + (qg + 16 * i) * kPfLd + d);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4 *>(ks + (kg + 16 * j) * kPfLd + d);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float x = sc[i][j];
+                    x = fmaf(qv[i].x, kv[j].x, x);
+                    x = fmaf(qv[i].y, kv[j].y, x);
+                    x = fmaf(qv[i].z, kv[j].z, x);
+                    sc[i][j] = fmaf(qv[i].w, kv[j].w, x);
+                }
         }
-        m_run = m_new;
-    }
-    if (live) {
-        const float *row = a.qkv + static_cast<size_t>(t) * a.qkv_ld + h * 512 + kAttnDim + lane * 8;
-        float *dst = a.out_f + static_cast<size_t>(t) * a.out_ld + h * kAttnDim + lane * 8;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) dst[i] = __fmul_rn(__fdiv_rn(acc[i], l_run), sigmoid(row[i]));
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ps[(qg + 16 * i) * kPfPLd + kg + 16 * j] = __fmul_rn(sc[i][j], 0.0625f);
+        __syncthreads();
+        // the running softmax of row srow over this tile
+        float s16[16], mx = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const int key = spart * 16 + k;
+            s16[k] = p0 + key <= spos ? ps[srow * kPfPLd + key] : -INFINITY;
+            mx = fmaxf(mx, s16[k]);
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run, mx);
+        const float c = m_run == -INFINITY ? 0.0f : expf(__fsub_rn(m_run, m_new));
+        float wsum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const float w = s16[k] == -INFINITY ? 0.0f : expf(__fsub_rn(s16[k], m_new));
+            ps[srow * kPfPLd + spart * 16 + k] = w;
+            wsum = __fadd_rn(wsum, w);
+        }
+        wsum = __fadd_rn(wsum, __shfl_xor_sync(0xffffffffu, wsum, 1));
+        wsum = __fadd_rn(wsum, __shfl_xor_sync(0xffffffffu, wsum, 2));
+        l_run = __fadd_rn(__fmul_rn(l_run, c), wsum);
+        m_run = m_new;
+        if (spart == 0) corr[srow] = c;
+        __syncthreads();
+        // weighted values: dimensions 4 kg + 64 j .. + 3 of queries qg + 16 i
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float ci = corr[qg + 16 * i];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) acc[i][e] = __fmul_rn(acc[i][e], ci);
+        }
+#pragma unroll 4
+        for (int k = 0; k < kPfKeys; ++k) {
+            float pw[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pw[i] = ps[(qg + 16 * i) * kPfPLd + k];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float4 v = *reinterpret_cast<const float4 *>(vs + k * kAttnDim + kg * 4 + 64 * j);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    acc[i][4 * j + 0] = fmaf(pw[i], v.x, acc[i][4 * j + 0]);
+                    acc[i][4 * j + 1] = fmaf(pw[i], v.y, acc[i][4 * j + 1]);
+                    acc[i][4 * j + 2] = fmaf(pw[i], v.z, acc[i][4 * j + 2]);
+                    acc[i][4 * j + 3] = fmaf(pw[i], v.w, acc[i][4 * j + 3]);
+                }
+            }
+        }
+    }
+    if (spart == 0) lsum[srow] = l_run;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + qg + 16 * i;
+        if (t >= a.tokens) continue;
+        const float l = lsum[qg + 16 * i];
+        const float *gate = a.qkv + static_cast<size_t>(t) * a.qkv_ld + h * 512 + kAttnDim;
+        float *dst = a.out_f + static_cast<size_t>(t) * a.out_ld + h * kAttnDim;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int d = kg * 4 + 64 * j + e;
+                dst[d] = __fmul_rn(__fdiv_rn(acc[i][4 * j + e], l), sigmoid(gate[d]));
+            }
     }
     pdl_launch_dependents();
 }
@@ -1202,6 +1333,9 @@ __global__ void __launch_bounds__(128) tp_reduce_kernel(TpReduceArgs a)
     __shared__ unsigned long long call_s;
     __shared__ int failed_s;
     pdl_wait();
+    // the next GEMV may start streaming its weights now; it waits for this
+    // kernel's completion before it reads the hidden rows
+    pdl_launch_dependents();
     const int c = blockIdx.x, tid = threadIdx.x;
     if (tid == 0) {
         call_s = __ldcg(a.counter);
@@ -1261,7 +1395,6 @@ __global__ void __launch_bounds__(128) tp_reduce_kernel(TpReduceArgs a)
             atomicExch(a.counter, call + 1);
         }
     }
-    pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------
@@ -1398,7 +1531,27 @@ cudaError_t launch_deltanet_prefill(const DeltaPrefillArgs &args, cudaStream_t s
     const int n_kh = args.n_kh > 0 ? args.n_kh : 16;
     if (args.tokens < 1 || n_kh % 2 || n_kh > 16 || args.o_ld != n_kh * 384) return cudaErrorInvalidValue;
     const int n_vh = 3 * n_kh, channels = 5 * n_kh * 128;
-    cudaError_t e = launch_pdl(deltanet_prefill_kernel, dim3(n_vh * 4), dim3(128), s, args);
+    if (!args.rec || args.rec_tokens < args.tokens || args.rec_tokens % kDeltaChunk ||
+        reinterpret_cast<uintptr_t>(args.rec) % 16)
+        return cudaErrorInvalidValue;
+    static cudaError_t attr = cudaFuncSetAttribute(deltanet_prefill_kernel,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(kDeltaSmem));
+    if (attr != cudaSuccess) return attr;
+    cudaError_t e = launch_pdl(deltanet_prefill_prep_kernel, dim3(args.tokens), dim3(256), s, args);
+    if (e == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(n_vh * 4);
+        cfg.blockDim = dim3(128);
+        cfg.dynamicSmemBytes = kDeltaSmem;
+        cfg.stream = s;
+        cudaLaunchAttribute pdl[1];
+        pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        pdl[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = pdl;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, deltanet_prefill_kernel, args);
+    }
     if (e == cudaSuccess)
         e = launch_pdl(deltanet_prefill_post_kernel, dim3(n_vh / 2, args.tokens), dim3(256), s, args);
     if (e == cudaSuccess)

@@ -153,6 +153,14 @@ struct StreamArgs {
     Q8KBlock *act_export;
     int export_reps;
     long long export_rep_bytes;
+    // Tensor-parallel exchange (xc_world > 1, a row-parallel projection; see
+    // xc_tile): each rank's buffer is [2 halves][world][kXcTokens][rows]
+    // floats, its flags [world][kXcMaxTiles]; xc_counter[0] counts the calls,
+    // xc_counter[1] the CTAs done with the current one.
+    int xc_world, xc_rank;
+    float *xc_bufs[kXcMaxWorld];
+    unsigned int *xc_flags[kXcMaxWorld];
+    unsigned int *xc_counter;
 };
 
 // Final store of one output row; with `accumulate` the value is added to what
@@ -164,6 +172,82 @@ __device__ __forceinline__ void store_row(const StreamArgs &g, int tok, int row,
     *dst = r;
     for (int k = 1; k < g.out_reps; ++k)
         *reinterpret_cast<float *>(reinterpret_cast<char *>(dst) + k * g.out_rep_bytes) = r;
+}
+
+__device__ __forceinline__ void st_release_sys_u32(unsigned int *p, unsigned int v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int *p)
+{
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void consumer_barrier(int consumers);
+
+// Tensor-parallel exchange of one finished tile of a row-parallel projection
+// (fused with the GEMV, so a tile crosses NVLink as soon as its sums are
+// final while other CTAs still stream weights).  The `writer` threads hold
+// the tile's row values vals[tok] (this rank's partial sums); they store
+// them into slot `rank` of every rank's buffer (peer memory), one thread
+// raises the tile's flag on every rank (system-scope release after a
+// system fence) and waits, bounded, until every rank's flag for the tile
+// here shows this call; then the writers add the world's slots in rank
+// order and store out[tok][row] (+)= sum - the all-reduce and the residual
+// add of the upstream's row-parallel projection.  xs[0]: an abandoned wait
+// (the rows are not stored, the status word says why); xs[1]: the call
+// number.  Buffers alternate halves by call parity: a rank writes half h
+// again only two calls later, after every rank has finished the call that
+// read it.
+template <int MT>
+__device__ void xc_tile(const StreamArgs &g, int t, int row, bool writer, const float *vals, int consumers,
+                        volatile int *xs)
+{
+    const unsigned int call = static_cast<unsigned int>(xs[1]);
+    const size_t slot = static_cast<size_t>(kXcTokens) * g.rows;
+    const size_t half = static_cast<size_t>(call & 1u) * g.xc_world * slot;
+    if (writer) {
+#pragma unroll
+        for (int tok = 0; tok < MT; ++tok) {
+            if (tok >= g.tokens) break;
+            for (int r = 0; r < g.xc_world; ++r)
+                g.xc_bufs[r][half + g.xc_rank * slot + static_cast<size_t>(tok) * g.rows + row] = vals[tok];
+        }
+    }
+    consumer_barrier(consumers);
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int r = 0; r < g.xc_world; ++r)
+            st_release_sys_u32(g.xc_flags[r] + g.xc_rank * kXcMaxTiles + t, call + 1u);
+        const unsigned long long start = global_timer_ns();
+        bool ok = true;
+        for (int r = 0; r < g.xc_world && ok; ++r) {
+            const unsigned int *f = g.xc_flags[g.xc_rank] + r * kXcMaxTiles + t;
+            while (static_cast<int>(ld_acquire_sys_u32(f) - (call + 1u)) < 0) {
+                if (global_timer_ns() - start > kWaitLimitNs) {
+                    atomicExch(&g_stream_status, kStatusWaitTimeout);
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        if (!ok) xs[0] = 1;
+    }
+    consumer_barrier(consumers);
+    if (writer && !xs[0]) {
+        const float *mine = g.xc_bufs[g.xc_rank] + half;
+#pragma unroll
+        for (int tok = 0; tok < MT; ++tok) {
+            if (tok >= g.tokens) break;
+            const size_t o = static_cast<size_t>(tok) * g.rows + row;
+            float sum = __ldcg(mine + o);
+            for (int r = 1; r < g.xc_world; ++r) sum = __fadd_rn(sum, __ldcg(mine + r * slot + o));
+            store_row(g, tok, row, sum);
+        }
+    }
 }
 
 template <typename T>
@@ -750,6 +834,11 @@ __global__ void __launch_bounds__(StreamThreads<MT, L>::kValue, 1) stream_gemm_k
     asm volatile("griddepcontrol.wait;" ::: "memory");
     trace_mark(g.trace, kTraceReady);
     trace_mark(g.trace, kTraceLastReady);
+    volatile int *xs = issued + 2;  // exchange state (see xc_tile)
+    if (g.xc_world > 1 && tid == 0) {
+        xs[0] = 0;
+        xs[1] = static_cast<int>(__ldcg(g.xc_counter));
+    }
 
     const int slots = MT * g.nb;
     if (g.act_mode == kActQ8K) {
@@ -870,7 +959,10 @@ __global__ void __launch_bounds__(StreamThreads<MT, L>::kValue, 1) stream_gemm_k
         if (seg_whole && g.sw_act) {
             swiglu_epilogue<MT>(g, t, rt, grp, part, failed, total, consumers, last_flag);
         } else if (seg_whole) {
-            if (grp == 0 && part == 0 && !failed && mine_row && row < g.rows) {
+            if (g.xc_world > 1) {
+                xc_tile<MT>(g, t, row, grp == 0 && part == 0 && !failed && mine_row && row < g.rows, total, consumers,
+                            xs);
+            } else if (grp == 0 && part == 0 && !failed && mine_row && row < g.rows) {
 #pragma unroll
                 for (int tok = 0; tok < MT; ++tok)
                     if (tok < g.tokens) store_row(g, tok, row, total[tok]);
@@ -895,21 +987,41 @@ __global__ void __launch_bounds__(StreamThreads<MT, L>::kValue, 1) stream_gemm_k
             // stored.
             if (tid == 0) *last_flag = atomicAdd(&g.counters[t], 1) == n_dep - 1 ? (failed ? 2 : 1) : 0;
             consumer_barrier(consumers);
-            if (*last_flag == 1 && !failed && grp == 0 && part == 0 && mine_row) {
+            const bool finisher = *last_flag == 1 && !failed && grp == 0 && part == 0 && mine_row;
+            float fin[MT];
+#pragma unroll
+            for (int tok = 0; tok < MT; ++tok) fin[tok] = 0.0f;
+            if (finisher) {
                 __threadfence();
                 const float *base = g.partials + static_cast<size_t>(t) * g.max_slots * MT * g.tile_rows;
 #pragma unroll
                 for (int tok = 0; tok < MT; ++tok) {
                     if (tok >= g.tokens) break;
-                    float sum = 0.0f;
                     for (int k = 0; k < n_dep; ++k)
-                        sum += __ldcg(base + (static_cast<size_t>(k) * MT + tok) * g.tile_rows + rt);
-                    if (row < g.rows) store_row(g, tok, row, sum);
+                        fin[tok] += __ldcg(base + (static_cast<size_t>(k) * MT + tok) * g.tile_rows + rt);
                 }
             }
             if (*last_flag && tid == 0) atomicExch(&g.counters[t], 0);
+            if (*last_flag && g.xc_world > 1) {
+                // the tile's last CTA exchanges it (also after a failure, so
+                // that the peers' waits end; its rows are then not stored)
+                xc_tile<MT>(g, t, row, finisher && row < g.rows, fin, consumers, xs);
+            } else if (finisher && row < g.rows) {
+#pragma unroll
+                for (int tok = 0; tok < MT; ++tok)
+                    if (tok < g.tokens) store_row(g, tok, row, fin[tok]);
+            }
         }
         consumer_barrier(consumers);  // `red` and the flag are reused by the next segment
+    }
+    if (g.xc_world > 1 && tid == 0) {
+        // the CTA is done with this call; the last one advances the call number
+        __threadfence();
+        if (atomicAdd(g.xc_counter + 1, 1u) == gridDim.x - 1) {
+            g.xc_counter[1] = 0;
+            __threadfence();
+            atomicExch(g.xc_counter, static_cast<unsigned int>(xs[1]) + 1u);
+        }
     }
     if (failed && tid == 0) {
         // Drain the bulk copies still in flight before shared memory goes away:
@@ -1161,6 +1273,20 @@ cudaError_t launch_t(const StreamPlan &p, const StreamLaunch &l, cudaStream_t st
     g.export_rep_bytes = l.export_rep_bytes;
     if (l.act_export && g.export_reps > p.grid) return cudaErrorInvalidValue;
     if (l.side_w && (l.act_mode != kActRmsNorm || l.side_rows > p.grid)) return cudaErrorInvalidValue;
+    g.xc_world = l.xc_world > 1 ? l.xc_world : 0;
+    g.xc_rank = l.xc_rank;
+    for (int r = 0; r < kXcMaxWorld; ++r) {
+        g.xc_bufs[r] = r < g.xc_world ? l.xc_bufs[r] : nullptr;
+        g.xc_flags[r] = r < g.xc_world ? l.xc_flags[r] : nullptr;
+    }
+    g.xc_counter = l.xc_counter;
+    // the exchange waits on the peers' CTAs inside the kernel: every CTA must
+    // be resident at once (one per SM), and the tiles must fit the flags
+    if (g.xc_world > 1 &&
+        (g.xc_world > kXcMaxWorld || l.xc_rank < 0 || l.xc_rank >= g.xc_world || !l.xc_counter ||
+         l.tokens > kXcTokens || p.tiles > kXcMaxTiles || p.rows > l.xc_rows || p.grid > device_sm_count() ||
+         l.sw_act))
+        return cudaErrorInvalidValue;
     const void *kernel = select_kernel<Dec>(p.mt, l.dbg_w != nullptr, p.parts);
     if (!kernel) return cudaErrorInvalidValue;
     cudaError_t e = opt_in(kernel);

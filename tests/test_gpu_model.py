@@ -250,6 +250,35 @@ def test_tensor_core_prefill_matches_upstream(models):
     check_logits(dev.forward_token(42), ref.forward_token(42), "decode after tensor-core prefill", cos_min=0.9)
 
 
+def test_tensor_core_prefill_continues_a_cached_prefix(models):
+    """A second tensor-core prefill on top of a first (positions 70 .. 199,
+    ragged 64-token tiles): attention reads the keys and values the first one
+    cached, the DeltaNet conv window reads the ring and the state carries
+    over.  Same bar as a single prefill against the upstream doing the same."""
+    import os
+    dev, ref = models
+    rng = np.random.default_rng(200)
+    first, second = rng.integers(0, 248320, 70).tolist(), rng.integers(0, 248320, 130).tolist()
+    os.environ["Q38CU_TC_PREFILL"] = "0"
+    try:
+        dev.reset()
+        dev.prefill(first)
+        integer = dev.prefill(second)
+    finally:
+        del os.environ["Q38CU_TC_PREFILL"]
+    dev.reset()
+    dev.prefill(first)
+    tc = dev.prefill(second)
+    assert dev.position == 200
+    ref.reset()
+    ref.prefill(first)
+    want = ref.prefill(second)
+    check_logits(tc, want, "continued tensor-core prefill", cos_min=0.9)
+    e_tc, e_int = rel(tc, want), rel(integer, want)
+    print(f"continued prefill relative error vs upstream: tensor cores {e_tc:.3e}, integer path {e_int:.3e}")
+    assert e_tc <= 1.5 * e_int + 1e-3, (e_tc, e_int)
+
+
 def test_greedy_matches_upstream_teacher_forced(models, portable):
     """Greedy decoding under teacher forcing: the device and the upstream's
     portable build both read the native build's own greedy sequence.  The

@@ -172,6 +172,25 @@ def test_q8_0_alpha_beta_shape(q38, oracle):
     assert_close(out, oracle.gemm_f32(O.Q8_0, weights, 48, 5120, x))
 
 
+@pytest.mark.parametrize("qtype,rows,batch", [(O.Q8_0, 48, 40), (O.Q8_0, 48, 333), (O.Q4_K, 37, 19)],
+                         ids=["Q8_0-40", "Q8_0-333", "Q4_K-ragged"])
+def test_float_path_prompt_batch(q38, oracle, qtype, rows, batch):
+    """Prompt-sized batches take the register-tiled float kernel: each token's
+    row equals the single-token product bit for bit (the same summation
+    order), and the upstream float path within tolerance; ragged row and
+    token counts leave no output untouched."""
+    import torch
+    width = 5120
+    weights = synth.quant_tensor(qtype, rows, width, seed=15)
+    x = synth.activations(batch, width, seed=16)
+    t = q38.DeviceTensor(qtype, width, rows, weights)
+    xd = to_dev(x)
+    out = q38.gemm_f32(t, xd, out=torch.full((batch, rows), float("nan"), device="cuda")).cpu().numpy()
+    for i in (0, batch // 2, batch - 1):
+        assert np.array_equal(out[i], q38.gemm_f32(t, xd[i:i + 1].contiguous()).cpu().numpy()[0]), i
+    assert_close(out, oracle.gemm_f32(qtype, weights, rows, width, x))
+
+
 @pytest.mark.parametrize("layout", LAYOUTS, ids=LAYOUT_IDS)
 def test_embedding_row_full_size(q38, oracle, layout):
     """token_embd row dequant (Q4_K 248320 x 5120 in the mix; a slice here)."""

@@ -26,13 +26,13 @@ def _free_port():
         return sock.getsockname()[1]
 
 
-def _rank_main(rank, world, port, path, out_dir, p2p):
+def _rank_main(rank, world, port, path, out_dir, mode):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
     root = os.path.dirname(here)
     sys.path[:0] = [os.path.join(root, "oracle"), os.path.join(root, "qwen3.8-27b-in-c_b200", "python")]
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    os.environ["Q38CU_TP_P2P"] = "1" if p2p else "0"
+    os.environ["Q38CU_TP_P2P"] = str(mode)
     import torch
     import torch.distributed as dist
     from q38b200.model import Model, nccl_unique_id
@@ -67,10 +67,11 @@ def cosine(a, b):
     return a @ b / np.linalg.norm(a) / np.linalg.norm(b)
 
 
-@pytest.mark.parametrize("p2p", [False, True], ids=["nccl", "nvlink-p2p"])
-def test_two_gpu_tensor_parallel_matches_one_gpu(tmp_path, p2p):
-    """Both collectives: NCCL's all-reduce, and the exchange over CUDA IPC
-    peer memory with bounded flag waits (Q38CU_TP_P2P=1)."""
+@pytest.mark.parametrize("mode", [0, 1, 2], ids=["nccl", "nvlink-p2p", "fused-gemv-exchange"])
+def test_two_gpu_tensor_parallel_matches_one_gpu(tmp_path, mode):
+    """All three collectives: NCCL's all-reduce (Q38CU_TP_P2P=0), the
+    reduction kernel over CUDA IPC peer memory (1), and the exchange fused
+    into the row-parallel GEMVs tile by tile (2); bounded flag waits."""
     import torch
     import torch.multiprocessing as mp
     from q38b200 import gguf
@@ -79,7 +80,7 @@ def test_two_gpu_tensor_parallel_matches_one_gpu(tmp_path, p2p):
         pytest.skip("needs 2 GPUs")
     path = gguf.cached_model_path(seed=3, mtp=False, dist="robust")
     world = 2
-    mp.start_processes(_rank_main, args=(world, _free_port(), path, str(tmp_path), p2p), nprocs=world,
+    mp.start_processes(_rank_main, args=(world, _free_port(), path, str(tmp_path), mode), nprocs=world,
                        start_method="spawn")
     r0, r1 = (np.load(os.path.join(tmp_path, f"rank{r}.npz")) for r in range(world))
     for key in ("layer0", "prefill", "step", "greedy"):

@@ -328,12 +328,33 @@ int q38cu_tensor_gemm_q8_k(float *output, const Q38CuQ8KBlock *input, uint32_t b
     return gemm_q8k(output, nullptr, nullptr, input, batch_size, input_length, tensor, stream);
 }
 
+namespace {
+// Workspace of q38cu_tensor_gemm_q8_k_tc: A hi/lo fp16 [2][rows][K], B fp16
+// [batch][K], block scales [K / 256][ld], row powers of two [rows]; each
+// part 256-byte aligned.
+struct TcWorkspace {
+    uint64_t a, b, scale, row_scale, total;
+    uint32_t ld;
+};
+TcWorkspace tc_workspace_layout(uint64_t batch, uint64_t width, uint64_t rows)
+{
+    auto up = [](uint64_t x) { return (x + 255) / 256 * 256; };
+    TcWorkspace w;
+    const uint64_t tile = static_cast<uint64_t>(q38::tc_token_tile(static_cast<int>(batch)));
+    w.ld = static_cast<uint32_t>((batch + tile - 1) / tile * tile);
+    w.a = 0;
+    w.b = up(rows * width * 4);
+    w.scale = w.b + up(batch * width * 2);
+    w.row_scale = w.scale + up(width / 256 * w.ld * 4);
+    w.total = w.row_scale + up(rows * 4);
+    return w;
+}
+}  // namespace
+
 uint64_t q38cu_tensor_gemm_q8_k_tc_workspace(uint32_t batch_size, uint64_t input_length, const Q38CuTensor *tensor)
 {
     if (!tensor || !batch_size || tensor->n_dims != 2 || input_length % 256) return 0;
-    const uint64_t a = (tensor->shape[1] * input_length * 4 + 255) / 256 * 256;  // hi and lo fp16
-    const uint64_t b = (static_cast<uint64_t>(batch_size) * input_length * 4 + 255) / 256 * 256;
-    return a + b + (static_cast<uint64_t>(batch_size) * 4 + 255) / 256 * 256 + (tensor->shape[1] * 4 + 255) / 256 * 256;
+    return tc_workspace_layout(batch_size, input_length, tensor->shape[1]).total;
 }
 
 int q38cu_tensor_gemm_q8_k_tc(float *output, const Q38CuQ8KBlock *input, uint32_t batch_size, uint64_t input_length,
@@ -351,26 +372,27 @@ int q38cu_tensor_gemm_q8_k_tc(float *output, const Q38CuQ8KBlock *input, uint32_
     if (workspace_bytes < need) return fail("workspace smaller than q38cu_tensor_gemm_q8_k_tc_workspace()%s");
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     uint8_t *ws = static_cast<uint8_t *>(workspace);
-    void *a16 = ws;
-    void *b16 = ws + (tensor->shape[1] * input_length * 4 + 255) / 256 * 256;
-    float *scale = reinterpret_cast<float *>(static_cast<uint8_t *>(b16) +
-                                             (static_cast<uint64_t>(batch_size) * input_length * 4 + 255) / 256 * 256);
-    float *row_scale = scale + (static_cast<uint64_t>(batch_size) + 63) / 64 * 64;
+    const TcWorkspace lay = tc_workspace_layout(batch_size, input_length, tensor->shape[1]);
+    void *a16 = ws + lay.a;
+    void *b16 = ws + lay.b;
+    float *scale = reinterpret_cast<float *>(ws + lay.scale);
+    float *row_scale = reinterpret_cast<float *>(ws + lay.row_scale);
     const Geometry g = geometry(tensor->type);
     cudaError_t e = q38::launch_dequant_f16(tensor->data, static_cast<int>(tensor->type), tensor->shape[1],
                                             input_length, layout_tile_rows(tensor), static_cast<int>(g.bytes), a16,
                                             row_scale, 0, s);
     if (e == cudaSuccess)
         e = q38::launch_q8k_to_f16(input, static_cast<int>(input_length / 256), static_cast<int>(batch_size),
-                                   static_cast<int>(batch_size), b16, scale, s);
+                                   static_cast<int>(lay.ld), b16, scale, s);
     if (e == cudaSuccess) {
         q38::TcGemm p;
         p.out = output;
         p.ld = static_cast<int>(tensor->shape[1]);
         p.n = static_cast<int>(tensor->shape[1]);
-        p.m = p.m_pad = static_cast<int>(batch_size);
+        p.m = static_cast<int>(batch_size);
         p.k = static_cast<int>(input_length);
-        p.tok_scale = scale;
+        p.b_scale = scale;
+        p.b_scale_ld = static_cast<int>(lay.ld);
         p.row_scale = row_scale;
         p.accumulate = 0;
         e = q38::launch_tc_gemm(a16, b16, p, s);

@@ -141,15 +141,16 @@ cudaError_t launch_repack_tiled(void *dst, const void *src, uint64_t rows, uint6
 // q38cu_tensor_repack with a given tile height (a multiple of 8, 8..256).
 int repack_tiled_with(void *dst_tensor, const void *src_tensor, uint32_t tile_rows, void *stream);
 
-// Tensor-core batch GEMM (q38_tc.cu): out[t * ld + row] (+)= sum_k A[row][k]
-// B[t][k] * tok_scale[t] * row_scale[row], A = A_hi + A_lo with A_hi fp16
-// [n][k] followed by A_lo [n][k], B likewise [m_pad][k] twice (K-major, k a
-// multiple of 64, 16-byte aligned).
+// Tensor-core batch GEMM (q38_tc.cu): out[t * ld + row] (+)= row_scale[row]
+// sum_sb b_scale[sb][t] sum_{k in sb} A[row][k] B[t][k], A = A_hi + A_lo with
+// A_hi fp16 [n][k] followed by A_lo [n][k], B fp16 [m][k] (K-major, k a
+// multiple of 256, 16-byte aligned); sb = k / 256.
 struct TcGemm {
     float *out;
     int ld;
-    int n, m, m_pad, k;
-    const float *tok_scale;
+    int n, m, k;
+    const float *b_scale;  // [k / 256][b_scale_ld], b_scale_ld a multiple of tc_token_tile
+    int b_scale_ld;
     const float *row_scale;
     int accumulate;
 };
@@ -160,9 +161,9 @@ int tc_token_tile(int m);
 // split: rows interleaved (gate i, up i) are written as [gate rows | up rows].
 cudaError_t launch_dequant_f16(const void *w, int type, uint64_t rows, uint64_t width, uint32_t tile_rows, int bb,
                                void *out, float *row_scale, int split, cudaStream_t s);
-// Q8_K [m][nb] -> fp16 hi/lo [2][m_pad][nb * 256] scaled by 2^-e per token, tok_scale[t] = 2^e.
-cudaError_t launch_q8k_to_f16(const void *q8, int nb, int m, int m_pad, void *out, float *tok_scale,
-                              cudaStream_t s);
+// Q8_K [m][nb] -> the quants as fp16 [m][nb * 256] and the block scales
+// b_scale[b][t] (t < ld, 0 past m; ld a multiple of tc_token_tile).
+cudaError_t launch_q8k_to_f16(const void *q8, int nb, int m, int ld, void *out, float *b_scale, cudaStream_t s);
 cudaError_t launch_tc_gemm(const void *a16, const void *b16, const TcGemm &p, cudaStream_t s);
 cudaError_t read_and_clear_tc_status(int *status);
 

@@ -1586,35 +1586,59 @@ bool setup_p2p(Q38Model *m, int mode)
         kArFlagBytes + kXcFlagBytes + static_cast<size_t>(2) * world * kMaxTokens * kHidden * sizeof(float);
     static_assert(8 * q38::kTpReduceCtas * sizeof(unsigned long long) <= kArFlagBytes, "flags area");
     static_assert(kMaxTokens == q38::kXcTokens, "exchange slots");
-    if (!dalloc(&m->ar_base, bytes, m->owned) || !dalloc(&m->ar_counter, 2, m->owned) ||
-        !dalloc(&m->xc_counter, 2, m->owned))
-        return false;
-    cudaIpcMemHandle_t mine;
-    if (!cuda_ok(cudaIpcGetMemHandle(&mine, m->ar_base), "cudaIpcGetMemHandle")) return false;
-    uint8_t *dev_handles = nullptr;
-    if (!dalloc(&dev_handles, sizeof(cudaIpcMemHandle_t) * world, m->owned)) return false;
-    std::vector<cudaIpcMemHandle_t> all(world);
+    // Every rank reaches both collectives below whatever failed locally, and
+    // all ranks take the same decision (a rank that went its own way would
+    // leave the others waiting in a collective).
+    struct Entry {
+        cudaIpcMemHandle_t handle;
+        int ok;
+        int pad[3];
+    };
+    Entry mine{};
+    mine.ok = dalloc(&m->ar_base, bytes, m->owned) && dalloc(&m->ar_counter, 2, m->owned) &&
+              dalloc(&m->xc_counter, 2, m->owned) &&
+              cuda_ok(cudaIpcGetMemHandle(&mine.handle, m->ar_base), "cudaIpcGetMemHandle");
+    uint8_t *dev = nullptr;
+    if (!dalloc(&dev, sizeof(Entry) * world + 16, m->owned)) return false;  // every rank needs this to go on
+    std::vector<Entry> all(world);
     const NcclApi *api = nccl();
-    if (!cuda_ok(cudaMemcpy(dev_handles + rank * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice),
+    if (!cuda_ok(cudaMemcpy(dev + rank * sizeof(Entry), &mine, sizeof(Entry), cudaMemcpyHostToDevice),
                  "handle copy") ||
-        !nccl_ok(api->all_gather(dev_handles + rank * sizeof(mine), dev_handles, sizeof(mine), ncclChar, m->comm,
-                                 m->stream),
+        !nccl_ok(api->all_gather(dev + rank * sizeof(Entry), dev, sizeof(Entry), ncclChar, m->comm, m->stream),
                  "handle all-gather") ||
         !cuda_ok(cudaStreamSynchronize(m->stream), "handle all-gather") ||
-        !cuda_ok(cudaMemcpy(all.data(), dev_handles, sizeof(mine) * world, cudaMemcpyDeviceToHost), "handle copy"))
+        !cuda_ok(cudaMemcpy(all.data(), dev, sizeof(Entry) * world, cudaMemcpyDeviceToHost), "handle copy"))
         return false;
-    for (int r = 0; r < world; ++r) {
+    int opened = 1;
+    for (int r = 0; r < world; ++r) opened = opened && all[r].ok;
+    for (int r = 0; opened && r < world; ++r) {
         uint8_t *base = m->ar_base;
         if (r != rank) {
             void *p = nullptr;
-            if (!cuda_ok(cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle"))
-                return false;
+            if (!cuda_ok(cudaIpcOpenMemHandle(&p, all[r].handle, cudaIpcMemLazyEnablePeerAccess),
+                         "cudaIpcOpenMemHandle")) {
+                opened = 0;
+                break;
+            }
             m->ipc_opened.push_back(p);
             base = static_cast<uint8_t *>(p);
         }
         m->ar_flags[r] = reinterpret_cast<unsigned long long *>(base);
         m->xc_flags[r] = reinterpret_cast<unsigned int *>(base + kArFlagBytes);
         m->ar_bufs[r] = reinterpret_cast<float *>(base + kArFlagBytes + kXcFlagBytes);
+    }
+    // the smallest outcome over the ranks
+    int *flag = reinterpret_cast<int *>(dev + sizeof(Entry) * world);
+    int agreed = 0;
+    if (!cuda_ok(cudaMemcpy(flag, &opened, sizeof(int), cudaMemcpyHostToDevice), "flag copy") ||
+        !nccl_ok(api->all_reduce(flag, flag, 1, ncclInt32, ncclMin, m->comm, m->stream), "flag all-reduce") ||
+        !cuda_ok(cudaStreamSynchronize(m->stream), "flag all-reduce") ||
+        !cuda_ok(cudaMemcpy(&agreed, flag, sizeof(int), cudaMemcpyDeviceToHost), "flag copy"))
+        return false;
+    if (!agreed) {
+        for (void *p : m->ipc_opened) cudaIpcCloseMemHandle(p);
+        m->ipc_opened.clear();
+        return fail("a rank could not map its peers' exchange buffers%s", "");
     }
     m->p2p = mode == 1;
     m->xc = mode == 2;
@@ -1680,6 +1704,13 @@ bool gather_logits(Q38Model *m, int tokens)
 constexpr int kTcPrefillMin = 64;
 constexpr int kTcChunk = 4096;
 
+// Token stride of the tensor-core GEMM's block-scale rows for n tokens.
+int tc_scale_ld(int n)
+{
+    const int tile = q38::tc_token_tile(n);
+    return (n + tile - 1) / tile * tile;
+}
+
 size_t tc_a16_elements(const Q38Model *m)
 {
     size_t most = 0;
@@ -1717,7 +1748,7 @@ bool ensure_prefill_buffers(Q38Model *m, int cap)
     const size_t q8 = sizeof(Q38CuQ8KBlock);
     bool ok = pf_alloc(m, &m->pf_hidden, n * kHidden) && pf_alloc(m, &m->pf_normf, n * kHidden) &&
               pf_alloc(m, &m->pf_wide, n * m->wide_ld) && pf_alloc(m, &m->pf_act, n * kFfn) &&
-              pf_alloc(m, &m->pf_ba, n * m->ba_ld) && pf_alloc(m, &m->pf_scale, n) &&
+              pf_alloc(m, &m->pf_ba, n * m->ba_ld) && pf_alloc(m, &m->pf_scale, (kFfn / 256) * tc_scale_ld(cap)) &&
               pf_alloc(m, reinterpret_cast<uint8_t **>(&m->pf_q8), n * (kFfn / 256) * q8) &&
               pf_alloc(m, reinterpret_cast<uint8_t **>(&m->pf_q8mix), n * (kLinV / 256) * q8) &&
               pf_alloc(m, reinterpret_cast<uint16_t **>(&m->pf_a16), 2 * tc_a16_elements(m)) &&
@@ -1748,7 +1779,8 @@ bool tc_project(Q38Model *m, const Proj &p, const void *q8, const float *xf, int
         const int type = static_cast<int>(part.t.type);
         if (part.int_path && q38::tc_weight_type(type)) {
             if (!staged &&
-                !cuda_ok(q38::launch_q8k_to_f16(q8, width / 256, n, n, m->pf_b16, m->pf_scale, s), "q8k to f16"))
+                !cuda_ok(q38::launch_q8k_to_f16(q8, width / 256, n, tc_scale_ld(n), m->pf_b16, m->pf_scale, s),
+                         "q8k to f16"))
                 return false;
             staged = true;
             const uint32_t bb = q38cu_block_bytes(part.t.type);
@@ -1762,9 +1794,10 @@ bool tc_project(Q38Model *m, const Proj &p, const void *q8, const float *xf, int
             g.out = out + part.offset;
             g.ld = out_ld;
             g.n = part.rows;
-            g.m = g.m_pad = n;
+            g.m = n;
             g.k = width;
-            g.tok_scale = m->pf_scale;
+            g.b_scale = m->pf_scale;
+            g.b_scale_ld = tc_scale_ld(n);
             g.row_scale = m->pf_row_scale;
             g.accumulate = accumulate;
             if (!cuda_ok(q38::launch_tc_gemm(m->pf_a16, m->pf_b16, g, s), "tensor-core gemm")) return false;
@@ -1967,9 +2000,20 @@ Q38Model *open_model(const char *path, uint32_t context_length, int rank, int wo
     if (ok && world > 1) {
         const NcclApi *api = nccl();
         ok = nccl_ok(api->comm_init_rank(&m->comm, world, *id, rank), "ncclCommInitRank");
+        // default: the exchange fused into the GEMVs (measured fastest on 2
+        // GPUs); NCCL alone when the peers' memory cannot be mapped
         const char *p2p = std::getenv("Q38CU_TP_P2P");
-        const int mode = p2p && (*p2p == '1' || *p2p == '2') ? *p2p - '0' : 0;
-        if (ok && mode) ok = setup_p2p(m, mode);
+        const int mode = p2p && *p2p >= '0' && *p2p <= '2' ? *p2p - '0' : 2;
+        if (ok && mode && !setup_p2p(m, mode)) {
+            if (p2p) {
+                ok = false;
+            } else {
+                std::fprintf(stderr, "q38cuda: peer-memory exchange unavailable (%s); using NCCL's all-reduce\n",
+                             q38cu_last_error());
+                m->p2p = m->xc = false;
+                m->tp_mode = 0;
+            }
+        }
     }
     if (ok) {
         const char *tv = std::getenv("Q38CU_TRACE");

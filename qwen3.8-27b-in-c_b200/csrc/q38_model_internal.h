@@ -81,7 +81,7 @@ struct DeltaPrefillArgs {
 // Floats of the DeltaNet prefill records for `rec_tokens` tokens (key heads n_kh).
 inline size_t delta_prefill_rec_floats(int n_kh, int rec_tokens)
 {
-    return static_cast<size_t>(rec_tokens) * (static_cast<size_t>(n_kh) * 256 + static_cast<size_t>(3 * n_kh) * 130);
+    return static_cast<size_t>(rec_tokens) * (static_cast<size_t>(n_kh) * 260 + static_cast<size_t>(3 * n_kh) * 130);
 }
 
 struct AttnArgs {

@@ -614,7 +614,7 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
 //     depend on the recurrent state - the causal conv + SiLU of every q, k and
 //     v channel, the L2 norms of q and k, beta and the decay - written as
 //     records laid out for the serial kernel's bulk copies:
-//       qk  [key head][token][256]    q (128) then k (128), normalized
+//       qk  [key head][token][260]    q (128), k (128), normalized; q.k; 3 pad
 //       v   [value head][4][token][32] the 128 v channels, 32 per column block
 //       gb  [value head][token][2]    beta, decay
 //     (token stride rec_tokens, a multiple of kDeltaChunk).
@@ -624,14 +624,19 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
 //     one column block, streamed into a ring of shared-memory stages by
 //     cp.async.bulk kDeltaChunk tokens at a time, so the token loop reads only
 //     shared memory.  It stores the raw head output (before the RMSNorm).
+//     Per token it makes one warp reduction, not two: with a = k.S and
+//     b = q.S of the state before the token, the upstream's
+//       S <- decay S;  kv = k.S;  delta = (v - kv) beta;  S <- S + k delta;
+//       out = q.S
+//     is evaluated as kv = decay a, out = decay b + (q.k) delta (the same
+//     quantities, rounded differently: about 1e-7 relative).
 //  3. deltanet_prefill_post_kernel: head RMSNorm, the gate, Q8_K.
 //  4. deltanet_ring_store_kernel: the conv ring, once every reader is done.
-// Steps 1-2 compute each value with the same operations in the same order as
-// a single kernel that walked the tokens itself.
 // ---------------------------------------------------------------------------
 constexpr int kDeltaChunk = 32;   // tokens per bulk-copy stage
 constexpr int kDeltaStages = 3;
-constexpr uint32_t kDeltaQkBytes = kDeltaChunk * 256 * 4, kDeltaVBytes = kDeltaChunk * 32 * 4,
+constexpr int kDeltaQkLd = 260;  // floats per token of the q|k record
+constexpr uint32_t kDeltaQkBytes = kDeltaChunk * kDeltaQkLd * 4, kDeltaVBytes = kDeltaChunk * 32 * 4,
                    kDeltaGbBytes = kDeltaChunk * 2 * 4;
 constexpr uint32_t kDeltaStageBytes = kDeltaQkBytes + kDeltaVBytes + kDeltaGbBytes;
 constexpr size_t kDeltaSmem = static_cast<size_t>(kDeltaStages) * kDeltaStageBytes + 64;
@@ -662,7 +667,7 @@ __global__ void __launch_bounds__(256) deltanet_prefill_prep_kernel(DeltaPrefill
     const int n_kh = a.n_kh > 0 ? a.n_kh : 16, n_vh = 3 * n_kh;
     const int p = a.base + t;
     const size_t rt = static_cast<size_t>(a.rec_tokens);
-    float *rec_qk = a.rec, *rec_v = a.rec + static_cast<size_t>(n_kh) * rt * 256,
+    float *rec_qk = a.rec, *rec_v = a.rec + static_cast<size_t>(n_kh) * rt * kDeltaQkLd,
           *rec_gb = rec_v + static_cast<size_t>(n_vh) * rt * 128;
     for (int task = warp; task < n_kh + n_vh; task += 8) {
         if (task < n_kh) {
@@ -681,13 +686,15 @@ __global__ void __launch_bounds__(256) deltanet_prefill_prep_kernel(DeltaPrefill
             const double sq = warp_sum_d(pq), sk = warp_sum_d(pk);
             const float scale_q = __fdiv_rn(1.0f, fmaxf(sqrtf(static_cast<float>(sq)), kRmsEps));
             const float scale_k = __fdiv_rn(1.0f, fmaxf(sqrtf(static_cast<float>(sk)), kRmsEps));
-            float *dst = rec_qk + (static_cast<size_t>(kh) * rt + t) * 256;
-            reinterpret_cast<float4 *>(dst)[lane] =
-                make_float4(__fmul_rn(qv[0], scale_q), __fmul_rn(qv[1], scale_q), __fmul_rn(qv[2], scale_q),
-                            __fmul_rn(qv[3], scale_q));
-            reinterpret_cast<float4 *>(dst + 128)[lane] =
-                make_float4(__fmul_rn(kv[0], scale_k), __fmul_rn(kv[1], scale_k), __fmul_rn(kv[2], scale_k),
-                            __fmul_rn(kv[3], scale_k));
+            float *dst = rec_qk + (static_cast<size_t>(kh) * rt + t) * kDeltaQkLd;
+            const float4 q4 = make_float4(__fmul_rn(qv[0], scale_q), __fmul_rn(qv[1], scale_q),
+                                          __fmul_rn(qv[2], scale_q), __fmul_rn(qv[3], scale_q));
+            const float4 k4 = make_float4(__fmul_rn(kv[0], scale_k), __fmul_rn(kv[1], scale_k),
+                                          __fmul_rn(kv[2], scale_k), __fmul_rn(kv[3], scale_k));
+            reinterpret_cast<float4 *>(dst)[lane] = q4;
+            reinterpret_cast<float4 *>(dst + 128)[lane] = k4;
+            const float qk = warp_sum_f(fmaf(q4.w, k4.w, fmaf(q4.z, k4.z, fmaf(q4.y, k4.y, __fmul_rn(q4.x, k4.x)))));
+            if (lane == 0) *reinterpret_cast<float4 *>(dst + 256) = make_float4(qk, 0.0f, 0.0f, 0.0f);
         } else {
             const int vh = task - n_kh;
             const int ch = 2 * n_kh * 128 + vh * 128 + lane * 4;
@@ -725,9 +732,10 @@ __global__ void __launch_bounds__(128) deltanet_prefill_kernel(DeltaPrefillArgs 
     const int vh = blockIdx.x >> 2, cb = blockIdx.x & 3, col0 = cb * 32 + warp * 8;
     const int kh = vh % n_kh;
     const size_t rt = static_cast<size_t>(a.rec_tokens);
-    const float *rec_qk = a.rec + static_cast<size_t>(kh) * rt * 256;
-    const float *rec_v = a.rec + static_cast<size_t>(n_kh) * rt * 256 + (static_cast<size_t>(vh) * 4 + cb) * rt * 32;
-    const float *rec_gb = a.rec + static_cast<size_t>(n_kh) * rt * 256 + static_cast<size_t>(n_vh) * rt * 128 +
+    const float *rec_qk = a.rec + static_cast<size_t>(kh) * rt * kDeltaQkLd;
+    const float *rec_v =
+        a.rec + static_cast<size_t>(n_kh) * rt * kDeltaQkLd + (static_cast<size_t>(vh) * 4 + cb) * rt * 32;
+    const float *rec_gb = a.rec + static_cast<size_t>(n_kh) * rt * kDeltaQkLd + static_cast<size_t>(n_vh) * rt * 128 +
                           static_cast<size_t>(vh) * rt * 2;
     const int chunks = (a.tokens + kDeltaChunk - 1) / kDeltaChunk;
     if (threadIdx.x == 0) {
@@ -747,7 +755,7 @@ __global__ void __launch_bounds__(128) deltanet_prefill_kernel(DeltaPrefillArgs 
         uint64_t *bar = &full[c % kDeltaStages];
         const size_t t0 = static_cast<size_t>(c) * kDeltaChunk;
         mbar_arrive_expect_tx(bar, kDeltaStageBytes);
-        bulk_copy_g2s(st, rec_qk + t0 * 256, kDeltaQkBytes, bar);
+        bulk_copy_g2s(st, rec_qk + t0 * kDeltaQkLd, kDeltaQkBytes, bar);
         bulk_copy_g2s(st + kDeltaQkBytes, rec_v + t0 * 32, kDeltaVBytes, bar);
         bulk_copy_g2s(st + kDeltaQkBytes + kDeltaVBytes, rec_gb + t0 * 2, kDeltaGbBytes, bar);
     };
@@ -769,50 +777,42 @@ __global__ void __launch_bounds__(128) deltanet_prefill_kernel(DeltaPrefillArgs 
         const int n = min(kDeltaChunk, a.tokens - c * kDeltaChunk);
         for (int i = 0; i < n; ++i) {
             const int t = c * kDeltaChunk + i;
-            const float4 q4 = reinterpret_cast<const float4 *>(sqk + i * 256)[lane];
-            const float4 k4 = reinterpret_cast<const float4 *>(sqk + i * 256 + 128)[lane];
+            const float *rq = sqk + i * kDeltaQkLd;
+            const float4 q4 = reinterpret_cast<const float4 *>(rq)[lane];
+            const float4 k4 = reinterpret_cast<const float4 *>(rq + 128)[lane];
+            const float qk = rq[256];
             const float vcol = sv[i * 32 + warp * 8 + (lane & 7)];
             const float2 gb = reinterpret_cast<const float2 *>(sgb)[i];
             const float beta = gb.x, decay = gb.y;
-            // delta rule on the warp's 8 columns (qwen38_model.c:758-781)
-            float red[8];
+            // k.S and q.S of the state before this token, reduced together
+            float red[16];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                float4 &x = s[j];
-                x.x = __fmul_rn(x.x, decay);
-                x.y = __fmul_rn(x.y, decay);
-                x.z = __fmul_rn(x.z, decay);
-                x.w = __fmul_rn(x.w, decay);
+                const float4 &x = s[j];
                 red[j] = fmaf(x.w, k4.w, fmaf(x.z, k4.z, fmaf(x.y, k4.y, __fmul_rn(x.x, k4.x))));
+                red[8 + j] = fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, __fmul_rn(x.x, q4.x))));
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
 #pragma unroll
-                for (int j = 0; j < 8; ++j) red[j] = __fadd_rn(red[j], __shfl_xor_sync(0xffffffffu, red[j], o));
+                for (int j = 0; j < 16; ++j) red[j] = __fadd_rn(red[j], __shfl_xor_sync(0xffffffffu, red[j], o));
             }
+            // delta rule on the warp's 8 columns (qwen38_model.c:758-781)
+            float out = 0.0f;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 float4 &x = s[j];
                 const float vj = __shfl_sync(0xffffffffu, vcol, j);
-                const float delta = __fmul_rn(__fsub_rn(vj, red[j]), beta);
-                x.x = fmaf(k4.x, delta, x.x);
-                x.y = fmaf(k4.y, delta, x.y);
-                x.z = fmaf(k4.z, delta, x.z);
-                x.w = fmaf(k4.w, delta, x.w);
-                red[j] = fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, __fmul_rn(x.x, q4.x))));
+                const float delta = __fmul_rn(__fsub_rn(vj, __fmul_rn(decay, red[j])), beta);
+                x.x = fmaf(k4.x, delta, __fmul_rn(x.x, decay));
+                x.y = fmaf(k4.y, delta, __fmul_rn(x.y, decay));
+                x.z = fmaf(k4.z, delta, __fmul_rn(x.z, decay));
+                x.w = fmaf(k4.w, delta, __fmul_rn(x.w, decay));
+                const float oj = fmaf(qk, delta, __fmul_rn(decay, red[8 + j]));
+                if (lane == j) out = oj;
             }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) red[j] = __fadd_rn(red[j], __shfl_xor_sync(0xffffffffu, red[j], o));
-            }
-            if (lane < 8) {
-                float mine = red[0];
-#pragma unroll
-                for (int j = 1; j < 8; ++j)
-                    if (lane == j) mine = red[j];
-                a.o_raw[static_cast<size_t>(t) * a.o_ld + vh * 128 + col0 + lane] = __fmul_rn(mine, query_scale);
-            }
+            if (lane < 8)
+                a.o_raw[static_cast<size_t>(t) * a.o_ld + vh * 128 + col0 + lane] = __fmul_rn(out, query_scale);
         }
         // every warp is done with this stage: refill it with chunk c + kDeltaStages
         __syncthreads();

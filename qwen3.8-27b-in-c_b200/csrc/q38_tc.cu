@@ -4,39 +4,40 @@
 // upstream layer-major batch, src/qwen38/qwen38_model.c:1519-1560, which calls
 // q38_tensor_gemm_q8_k, src/qwen38/qwen38_quant.c:2950-3169, with M = prompt
 // tokens).  At M in the hundreds or thousands this is a dense contraction, so
-// it runs on the 5th-generation tensor cores with dequant-staged operands in
-// two-term fp16 ("hi + lo") form:
+// it runs on the 5th-generation tensor cores with dequant-staged operands:
 //
 //   A (weights)     each row dequantized with the upstream float formula of
 //                   its type, times a power of two 2^-e per row that puts
 //                   the row's bound on |w| just below 2^15, split into
 //                   hi = fp16(w) and lo = fp16(w - hi): 22 significant bits;
-//   B (activations) the Q8_K blocks of the M tokens dequantized (scale x
-//                   quant, as the upstream integer dot means them), times 2^-e
-//                   per token, split the same way;
-//   D               fp32 in tensor memory: hi.hi + hi.lo + lo.hi per 16-wide
-//                   K step (the lo.lo term is below 2^-22 of the product),
-//                   times both powers of two in the epilogue, stored
-//                   batch-major out[token][row] (+= with `accumulate`, the
-//                   residual add of the caller).
+//   B (activations) the int8 quants of the M tokens' Q8_K blocks, as fp16
+//                   (exact); each block's scale d[t][sb] stays fp32;
+//   D               per 256-wide superblock (one Q8_K block), fp32 in tensor
+//                   memory: A_hi.B + A_lo.B over its sixteen 16-wide K steps
+//                   (products exact in fp32); the epilogue promotes it into
+//                   fp32 registers as sum += D x d[t][sb] (the upstream's
+//                   per-block scale of the integer dot), then times the
+//                   row's power of two, stored batch-major out[token][row]
+//                   (+= with `accumulate`, the residual add of the caller).
 //
-// fp16 products are exact in fp32, so the result carries the rounding of an
-// fp32 dot product with 22-bit operands: about 1e-6 relative, the same order
-// as the float combination of the integer path, instead of the 1e-3 of single
-// fp16 operands (which the chaotic 64-layer random-init models amplify into
+// So the result carries the rounding of an fp32 dot product with 22-bit
+// weights and exact activations: about 1e-6 relative, the same order as the
+// float combination of the integer path, instead of the 1e-3 of single fp16
+// operands (which the chaotic 64-layer random-init models amplify into
 // different logits).  Per-block integer sums are not formed here - the M <= 8
 // decode and verification path keeps the exact integer sums.
 //
-// Kernel: one CTA per 128 x BN output tile (128 weight rows, BN tokens),
-// 6 warps: warp 0 lane 0 issues the TMA tile loads (3-D boxes: the hi and lo
-// tiles of A, 2 x 128 x 64 fp16, and of B, 2 x BN x 64, 128-byte swizzle) into
-// a ring of stages; warp 1 allocates BN tensor-memory columns and its lane 0
-// issues tcgen05.mma (M = 128, N = BN, K = 16, three per K step) and commits
-// each stage back to the producer; warps 2..5 read the accumulator (warp w
-// reads TMEM lanes 32 (w % 4) ..) and store it.  Every mbarrier wait is
-// bounded (2 s): a wait that runs out records the status word, the MMA issuer
-// still commits the accumulator barrier, the producer waits for the copies it
-// issued, and the CTA frees its tensor memory and exits.
+// Kernel: one CTA per 128 x BN output tile (128 weight rows, BN = 128 or 256
+// tokens), 2 + BN / 32 warps: warp 0 lane 0 issues the TMA tile loads (3-D
+// boxes: the hi and lo tiles of A, 2 x 128 x 64 fp16, and B, BN x 64,
+// 128-byte swizzle) into a ring of stages; warp 1 allocates 2 BN
+// tensor-memory columns (two superblock buffers) and its lane 0 issues
+// tcgen05.mma (M = 128, N = BN, K = 16, two per K step) and commits each stage
+// back to the producer; the other warps read the accumulator (warp w reads
+// TMEM lanes 32 (w % 4) .., 128 columns each) and store it.  Every mbarrier
+// wait is bounded (2 s): a wait that runs out records the status word, the
+// MMA issuer still commits the accumulator barrier, the producer waits for
+// the copies it issued, and the CTA frees its tensor memory and exits.
 #include <cuda.h>  // CUtensorMap and its enums; the encoder comes from the driver at run time
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -57,8 +58,18 @@ namespace {
 
 constexpr int kTcRows = 128;   // UMMA M: weight rows per tile
 constexpr int kTcK = 64;       // fp16 elements per stage row: one 128-byte swizzle span
-constexpr int kTcStages = 2;
-constexpr int kTcThreads = 192;
+
+template <int BN> struct TcCfg {
+    static constexpr int kEpiWarps = BN / 32;             // 128 accumulator columns each
+    static constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer, MMA issuer, epilogue
+    // declared thread bound: 320 also for BN = 128 (192 threads), which caps
+    // registers at 204 a thread - enough for the 128 sums without spilling
+    static constexpr int kLaunchBound = 320;
+    static constexpr int kStages = BN == 256 ? 3 : 4;
+    static constexpr uint32_t kATile = kTcRows * kTcK * 2;   // one of A hi / A lo
+    static constexpr uint32_t kBTile = BN * kTcK * 2;
+    static constexpr uint32_t kStage = 2 * kATile + kBTile;  // a multiple of 1024
+};
 
 // ---- TMA, tensor memory and tcgen05 primitives ----------------------------
 
@@ -150,7 +161,8 @@ struct TcArgs {
     float *out;             // [m][ld]
     int ld;
     int n, m, k;            // weight rows, tokens, width
-    const float *tok_scale; // [m]: 2^e of each token's B row
+    const float *b_scale;   // [k / 256][b_scale_ld]: Q8_K block scales (0 past m)
+    int b_scale_ld;         // a multiple of BN
     const float *row_scale; // [n]: 2^e of each weight row
     int accumulate;
 };
@@ -159,19 +171,19 @@ struct TcArgs {
 constexpr int kTcSegment = 4;
 
 template <int BN>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(TcCfg<BN>::kLaunchBound, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, TcArgs g)
 {
-    // a stage: A hi, A lo, B hi, B lo (each tile 1024-byte aligned)
-    constexpr uint32_t kATile = kTcRows * kTcK * 2, kBTile = BN * kTcK * 2;
-    constexpr uint32_t kABytes = 2 * kATile, kBBytes = 2 * kBTile, kStage = kABytes + kBBytes;
+    using C = TcCfg<BN>;
+    constexpr int kStages = C::kStages;
+    // a stage: A hi, A lo, B (each tile 1024-byte aligned)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kTcStages * kStage);
-    uint64_t *empty = full + kTcStages;
-    uint64_t *acc_full = empty + kTcStages;  // [2]: a segment's sums are in tensor-memory buffer b
-    uint64_t *acc_empty = acc_full + 2;      // [2]: the epilogue has read buffer b
-    uint64_t *drained = acc_empty + 2;       // the MMA issuer's last MMA has completed
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * C::kStage);
+    uint64_t *empty = full + kStages;
+    uint64_t *acc_full = empty + kStages;  // [2]: a segment's sums are in tensor-memory buffer b
+    uint64_t *acc_empty = acc_full + 2;    // [2]: the epilogue has read buffer b
+    uint64_t *drained = acc_empty + 2;     // the MMA issuer's last MMA has completed
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drained + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -181,13 +193,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int segments = (nk + kTcSegment - 1) / kTcSegment;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kTcStages; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+            mbar_init(&acc_empty[b], C::kEpiWarps);  // one arrival per epilogue warp
         }
         mbar_init(drained, 1);
         fence_mbar_init();
@@ -204,25 +216,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             // ---------------- TMA producer ----------------
             int issued = 0;
             for (int k = 0; k < nk; ++k) {
-                const int s = k % kTcStages;
-                if (k >= kTcStages &&
-                    !mbar_wait_bounded(&empty[s], static_cast<uint32_t>((k / kTcStages) - 1) & 1u, &g_tc_status))
+                const int s = k % kStages;
+                if (k >= kStages &&
+                    !mbar_wait_bounded(&empty[s], static_cast<uint32_t>((k / kStages) - 1) & 1u, &g_tc_status))
                     break;
-                uint8_t *stage = smem + s * kStage;
-                mbar_arrive_expect_tx(&full[s], kStage);
+                uint8_t *stage = smem + s * C::kStage;
+                mbar_arrive_expect_tx(&full[s], C::kStage);
                 tma_load_3d(stage, &map_a, k * kTcK, row0, &full[s]);
-                tma_load_3d(stage + kABytes, &map_b, k * kTcK, tok0, &full[s]);
+                tma_load_3d(stage + 2 * C::kATile, &map_b, k * kTcK, tok0, &full[s]);
                 issued = k + 1;
             }
             // The copies issued last must land before shared memory goes away.
-            for (int k = issued > kTcStages ? issued - kTcStages : 0; k < issued; ++k)
-                mbar_wait_bounded(&full[k % kTcStages], static_cast<uint32_t>(k / kTcStages) & 1u, &g_tc_status);
+            for (int k = issued > kStages ? issued - kStages : 0; k < issued; ++k)
+                mbar_wait_bounded(&full[k % kStages], static_cast<uint32_t>(k / kStages) & 1u, &g_tc_status);
         }
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
-            // Segment sg accumulates K steps [4 sg, 4 sg + 4) into tensor-memory
-            // buffer sg % 2, which the epilogue must have emptied first.
+            // Segment sg accumulates K steps [4 sg, 4 sg + 4) (superblock sg)
+            // into tensor-memory buffer sg % 2, which the epilogue must have
+            // emptied first.
             bool ok = true;
             for (int sg = 0; ok && sg < segments; ++sg) {
                 const int b = sg & 1;
@@ -234,21 +247,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tc_fence_after();
                 const int k1 = min(nk, (sg + 1) * kTcSegment);
                 for (int k = sg * kTcSegment; k < k1; ++k) {
-                    const int s = k % kTcStages;
-                    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(k / kTcStages) & 1u, &g_tc_status)) {
+                    const int s = k % kStages;
+                    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(k / kStages) & 1u, &g_tc_status)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_hi = smem_addr(smem + s * kStage), a_lo = a_hi + kATile;
-                    const uint32_t b_hi = a_hi + kABytes, b_lo = b_hi + kBTile;
+                    const uint32_t a_hi = smem_addr(smem + s * C::kStage), a_lo = a_hi + C::kATile;
+                    const uint32_t bq = a_hi + 2 * C::kATile;
 #pragma unroll
                     for (int kk = 0; kk < kTcK / 16; ++kk) {
                         const uint32_t o = kk * 32;
-                        mma_f16(acc, sw128_desc(a_hi + o), sw128_desc(b_hi + o), f16_idesc<BN>(),
+                        mma_f16(acc, sw128_desc(a_hi + o), sw128_desc(bq + o), f16_idesc<BN>(),
                                 (k > sg * kTcSegment || kk > 0) ? 1u : 0u);
-                        mma_f16(acc, sw128_desc(a_hi + o), sw128_desc(b_lo + o), f16_idesc<BN>(), 1u);
-                        mma_f16(acc, sw128_desc(a_lo + o), sw128_desc(b_hi + o), f16_idesc<BN>(), 1u);
+                        mma_f16(acc, sw128_desc(a_lo + o), sw128_desc(bq + o), f16_idesc<BN>(), 1u);
                     }
                     mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
                 }
@@ -259,29 +271,39 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         __syncwarp();
     } else {
-        // ---------------- epilogue: warps 2..5 ----------------
-        // Thread (quarter, lane) owns weight row 32 quarter + lane of the tile
-        // and adds each segment's sums for its BN tokens into fp32 registers
-        // (IEEE rounding; the tensor core's own accumulation is only trusted
-        // over one superblock).
-        const int quarter = warp & 3;
+        // ---------------- epilogue ----------------
+        // Thread (quarter, lane) of epilogue warp ew owns weight row
+        // 32 quarter + lane of the tile and accumulator columns (tokens)
+        // col0 .. col0 + 127; each segment's sums are scaled by the tokens'
+        // block scales and added into fp32 registers (IEEE rounding; the
+        // tensor core's own accumulation is only trusted over one superblock).
+        const int ew = warp - 2, quarter = warp & 3, col0 = (ew >> 2) * 128;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-        float sum[BN];
+        float sum[128];
 #pragma unroll
-        for (int c = 0; c < BN; ++c) sum[c] = 0.0f;
+        for (int c = 0; c < 128; ++c) sum[c] = 0.0f;
         bool ok = true;
         for (int sg = 0; sg < segments; ++sg) {
             const int b = sg & 1;
+            const float4 *sc = reinterpret_cast<const float4 *>(g.b_scale + static_cast<size_t>(sg) * g.b_scale_ld +
+                                                                tok0 + col0);
             ok = ok && mbar_wait_bounded(&acc_full[b], static_cast<uint32_t>(sg >> 1) & 1u, &g_tc_status);
             if (!ok) break;
             __syncwarp();
             tc_fence_after();
 #pragma unroll
-            for (int c = 0; c < BN / 16; ++c) {
+            for (int c = 0; c < 8; ++c) {
                 uint32_t v[16];
-                tmem_ld16(tmem + lane_addr + static_cast<uint32_t>(b * BN + c * 16), v);
+                tmem_ld16(tmem + lane_addr + static_cast<uint32_t>(b * BN + col0 + c * 16), v);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) sum[c * 16 + j] = __fadd_rn(sum[c * 16 + j], __uint_as_float(v[j]));
+                for (int q = 0; q < 4; ++q) {
+                    const float4 d = __ldg(sc + c * 4 + q);
+                    float *s4 = sum + c * 16 + q * 4;
+                    s4[0] = fmaf(__uint_as_float(v[q * 4 + 0]), d.x, s4[0]);
+                    s4[1] = fmaf(__uint_as_float(v[q * 4 + 1]), d.y, s4[1]);
+                    s4[2] = fmaf(__uint_as_float(v[q * 4 + 2]), d.z, s4[2]);
+                    s4[3] = fmaf(__uint_as_float(v[q * 4 + 3]), d.w, s4[3]);
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -291,11 +313,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (ok && row < g.n) {
             const float rs = __ldg(g.row_scale + row);
 #pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                const int tok = tok0 + c;
+            for (int c = 0; c < 128; ++c) {
+                const int tok = tok0 + col0 + c;
                 if (tok < g.m) {
                     float *dst = g.out + static_cast<size_t>(tok) * g.ld + row;
-                    const float r = __fmul_rn(__fmul_rn(sum[c], __ldg(g.tok_scale + tok)), rs);
+                    const float r = __fmul_rn(sum[c], rs);
                     *dst = g.accumulate ? __fadd_rn(*dst, r) : r;
                 }
             }
@@ -312,7 +334,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 template <int BN> constexpr size_t tc_smem_bytes()
 {
-    return 1024 + static_cast<size_t>(kTcStages) * 2 * (kTcRows + BN) * kTcK * 2 + (2 * kTcStages + 5) * 8 + 16;
+    return 1024 + static_cast<size_t>(TcCfg<BN>::kStages) * TcCfg<BN>::kStage +
+           (2 * TcCfg<BN>::kStages + 5) * 8 + 16;
 }
 
 // ---- operand staging --------------------------------------------------------
@@ -436,40 +459,25 @@ __global__ void dequant_f16_kernel(const uint8_t *w, int type, uint64_t rows, ui
     pdl_launch_dependents();
 }
 
-// Q8_K blocks [m][nb] -> fp16 hi [m_pad][nb * 256] and lo (m_pad rows
-// further) times 2^-e per token, and tok_scale[t] = 2^e (rows past m are
-// zero).  One CTA per token row.
-__global__ void __launch_bounds__(256) q8k_to_f16_kernel(const Q8KBlock *in, int nb, int m, __half *out,
-                                                         float *tok_scale)
+// Q8_K blocks [m][nb] -> B = the quants as fp16 [m][nb * 256] (exact) and
+// b_scale[b][t] = the scale of token t's block b, for t < ld (0 past m).
+// One CTA per token of [0, ld).
+__global__ void __launch_bounds__(256) q8k_to_f16_kernel(const Q8KBlock *in, int nb, int m, int ld, __half *out,
+                                                         float *b_scale)
 {
     pdl_wait();
-    __shared__ float red[8];
     const int t = blockIdx.x, tid = threadIdx.x;
-    const int width = nb * 256;
-    __half2 *dst = reinterpret_cast<__half2 *>(out + static_cast<size_t>(t) * width);
-    __half2 *dst_lo = reinterpret_cast<__half2 *>(out + (static_cast<size_t>(gridDim.x) + t) * width);
-    if (t >= m) {
-        for (int i = tid; i < width / 2; i += blockDim.x) dst[i] = dst_lo[i] = __floats2half2_rn(0.0f, 0.0f);
-        pdl_launch_dependents();
-        return;
-    }
     const Q8KBlock *row = in + static_cast<size_t>(t) * nb;
-    float amax = 0.0f;
-    for (int b = tid; b < nb; b += blockDim.x) amax = fmaxf(amax, fabsf(row[b].scale));
-    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if ((tid & 31) == 0) red[tid >> 5] = amax;
-    __syncthreads();
-    amax = 0.0f;
-    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) amax = fmaxf(amax, red[w]);
-    // the largest |value| is at most 127 * amax: bring it into [2^14, 2^15)
-    const float top = __fmul_rn(127.0f, amax);
-    const int e = top > 0.0f ? ilogbf(top) - 14 : 0;
-    if (tid == 0) tok_scale[t] = ldexpf(1.0f, e);
-    for (int i = tid; i < width / 2; i += blockDim.x) {
-        const int k = 2 * i, b = k >> 8, j = k & 255;
-        const float s = ldexpf(row[b].scale, -e);
-        split2(__fmul_rn(s, static_cast<float>(row[b].quants[j])), __fmul_rn(s, static_cast<float>(row[b].quants[j + 1])),
-               dst[i], dst_lo[i]);
+    for (int b = tid; b < nb; b += blockDim.x) b_scale[static_cast<size_t>(b) * ld + t] = t < m ? row[b].scale : 0.0f;
+    if (t < m) {
+        const int width = nb * 256;
+        __half2 *dst = reinterpret_cast<__half2 *>(out + static_cast<size_t>(t) * width);
+        for (int i = tid; i < width / 4; i += blockDim.x) {
+            const int k = 4 * i, b = k >> 8, j = k & 255;
+            const char4 q = *reinterpret_cast<const char4 *>(row[b].quants + j);
+            dst[2 * i] = __floats2half2_rn(static_cast<float>(q.x), static_cast<float>(q.y));
+            dst[2 * i + 1] = __floats2half2_rn(static_cast<float>(q.z), static_cast<float>(q.w));
+        }
     }
     pdl_launch_dependents();
 }
@@ -494,15 +502,15 @@ EncodeTiledFn encoder()
     return fn;
 }
 
-// 3-D fp16 tensor map [2][outer][inner] (the hi matrix, then the lo matrix),
-// box 64 x box_outer x 2, 128-byte swizzle.
-bool make_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint32_t box_outer)
+// 3-D fp16 tensor map [depth][outer][inner] (A: the hi matrix, then the lo
+// matrix, depth 2; B: depth 1), box 64 x box_outer x depth, 128-byte swizzle.
+bool make_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint32_t box_outer, uint32_t depth)
 {
     EncodeTiledFn enc = encoder();
     if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u) || inner % 64) return false;
-    const cuuint64_t dims[3] = {inner, outer, 2};
+    const cuuint64_t dims[3] = {inner, outer, depth};
     const cuuint64_t strides[2] = {inner * 2, inner * outer * 2};
-    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kTcK), box_outer, 2};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kTcK), box_outer, depth};
     const cuuint32_t estr[3] = {1, 1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -513,7 +521,7 @@ template <int BN>
 cudaError_t launch_tc_bn(const void *a16, const void *b16, const TcGemm &p, cudaStream_t s)
 {
     CUtensorMap ma, mb;
-    if (!make_map(&ma, a16, p.k, p.n, kTcRows) || !make_map(&mb, b16, p.k, p.m_pad, BN)) return cudaErrorInvalidValue;
+    if (!make_map(&ma, a16, p.k, p.n, kTcRows, 2) || !make_map(&mb, b16, p.k, p.m, BN, 1)) return cudaErrorInvalidValue;
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [] {
@@ -527,12 +535,13 @@ cudaError_t launch_tc_bn(const void *a16, const void *b16, const TcGemm &p, cuda
     g.n = p.n;
     g.m = p.m;
     g.k = p.k;
-    g.tok_scale = p.tok_scale;
+    g.b_scale = p.b_scale;
+    g.b_scale_ld = p.b_scale_ld;
     g.row_scale = p.row_scale;
     g.accumulate = p.accumulate;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(((p.n + kTcRows - 1) / kTcRows) * ((p.m + BN - 1) / BN)));
-    cfg.blockDim = dim3(kTcThreads);
+    cfg.blockDim = dim3(TcCfg<BN>::kThreads);
     cfg.dynamicSmemBytes = tc_smem_bytes<BN>();
     cfg.stream = s;
     cudaLaunchAttribute la[1];
@@ -545,7 +554,7 @@ cudaError_t launch_tc_bn(const void *a16, const void *b16, const TcGemm &p, cuda
 
 }  // namespace
 
-int tc_token_tile(int) { return 128; }
+int tc_token_tile(int) { return 256; }  // b_scale rows are padded to a multiple of this
 
 bool tc_weight_type(int type) { return type == 12 || type == 14; }  // Q4_K, Q6_K
 
@@ -583,11 +592,11 @@ cudaError_t launch_dequant_f16(const void *w, int type, uint64_t rows, uint64_t 
                               bb, static_cast<__half *>(out), static_cast<const float *>(row_scale), split);
 }
 
-cudaError_t launch_q8k_to_f16(const void *q8, int nb, int m, int m_pad, void *out, float *tok_scale, cudaStream_t s)
+cudaError_t launch_q8k_to_f16(const void *q8, int nb, int m, int ld, void *out, float *b_scale, cudaStream_t s)
 {
-    if (m < 1 || m_pad < m) return cudaErrorInvalidValue;
+    if (m < 1 || ld < m || ld % tc_token_tile(m)) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(m_pad));
+    cfg.gridDim = dim3(static_cast<unsigned>(ld));
     cfg.blockDim = dim3(256);
     cfg.stream = s;
     cudaLaunchAttribute la[1];
@@ -595,14 +604,18 @@ cudaError_t launch_q8k_to_f16(const void *q8, int nb, int m, int m_pad, void *ou
     la[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = la;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, q8k_to_f16_kernel, static_cast<const Q8KBlock *>(q8), nb, m,
-                              static_cast<__half *>(out), tok_scale);
+    return cudaLaunchKernelEx(&cfg, q8k_to_f16_kernel, static_cast<const Q8KBlock *>(q8), nb, m, ld,
+                              static_cast<__half *>(out), b_scale);
 }
 
 cudaError_t launch_tc_gemm(const void *a16, const void *b16, const TcGemm &p, cudaStream_t s)
 {
-    if (p.k % kTcK || p.n < 1 || p.m < 1 || p.m_pad < p.m || !p.out || !p.tok_scale) return cudaErrorInvalidValue;
-    return launch_tc_bn<128>(a16, b16, p, s);
+    if (p.k % 256 || p.n < 1 || p.m < 1 || !p.out || !p.b_scale || p.b_scale_ld < p.m ||
+        p.b_scale_ld % tc_token_tile(p.m))
+        return cudaErrorInvalidValue;
+    // 256-token tiles for prompts (twice the MMA work per staged A tile),
+    // 128 for short batches (less padding)
+    return p.m > 128 ? launch_tc_bn<256>(a16, b16, p, s) : launch_tc_bn<128>(a16, b16, p, s);
 }
 
 cudaError_t read_and_clear_tc_status(int *status)

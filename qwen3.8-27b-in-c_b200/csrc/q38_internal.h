@@ -95,18 +95,17 @@ struct StreamLaunch {
     int export_reps = 1;
     long long export_rep_bytes = 0;
     // Tensor-parallel exchange of a row-parallel projection's final rows over
-    // peer memory, fused into the GEMV (see q38_stream.cu): xc_bufs[r] and
-    // xc_flags[r] are rank r's exchange buffer ([2][world][kXcTokens][xc_rows]
-    // floats) and flags ([world][kXcMaxTiles]), mapped in this process;
-    // xc_counter is this rank's [2] call counter (zero at the start).  The
-    // rows go to out (+= with accumulate) once all ranks' partials are in.
+    // peer memory, fused into the GEMV (see q38_stream.cu): xc_bufs[r] is rank
+    // r's exchange buffer ([2][world][kXcTokens][xc_rows] 8-byte words, zero
+    // at the start), mapped in this process; xc_counter is this rank's [2]
+    // call counter (zero at the start).  The rows go to out (+= with
+    // accumulate) once all ranks' partials are in.
     int xc_world = 0, xc_rank = 0, xc_rows = 0;
-    float *xc_bufs[8] = {};
-    unsigned int *xc_flags[8] = {};
+    unsigned long long *xc_bufs[8] = {};
     unsigned int *xc_counter = nullptr;
 };
 
-constexpr int kXcMaxWorld = 8, kXcTokens = 8, kXcMaxTiles = 1024;
+constexpr int kXcMaxWorld = 8, kXcTokens = 8;
 
 enum : int { kActQ8K = 0, kActRmsNorm = 1, kActSwiGLU = 2 };
 

@@ -308,7 +308,6 @@ struct Q38Model {
     unsigned int *xc_counter = nullptr;
     float *ar_bufs[8] = {};
     unsigned long long *ar_flags[8] = {};
-    unsigned int *xc_flags[8] = {};
     std::vector<void *> ipc_opened;
     int kv_ld = kAttnKv;            // floats per position of this shard's KV cache rows
     int lin_qkv = kLinQkv, lin_heads = kLinHeads;  // this shard's DeltaNet channels and value heads
@@ -853,10 +852,7 @@ bool stream_project(const Part &p, const ActIn &in, int tokens, float *out, int 
             l.xc_world = tm->shard.world;
             l.xc_rank = tm->shard.rank;
             l.xc_rows = kHidden;
-            for (int r = 0; r < l.xc_world; ++r) {
-                l.xc_bufs[r] = tm->ar_bufs[r];
-                l.xc_flags[r] = tm->xc_flags[r];
-            }
+            for (int r = 0; r < l.xc_world; ++r) l.xc_bufs[r] = reinterpret_cast<unsigned long long *>(tm->ar_bufs[r]);
             l.xc_counter = tm->xc_counter;
         }
         if (export_q8) {
@@ -1573,17 +1569,16 @@ bool nccl_ok(ncclResult_t r, const char *what)
 }
 
 constexpr size_t kArFlagBytes = 4096;  // tp_reduce_kernel's flags
-constexpr size_t kXcFlagBytes = sizeof(unsigned int) * q38::kXcMaxWorld * q38::kXcMaxTiles;  // the fused exchange's
 
 // Exchange buffers for the NVLink all-reduce: one allocation per rank
-// ([tp_reduce flags][exchange flags][2 halves x world slots x 8 tokens x 5120
-// floats]), its IPC handle all-gathered over the NCCL communicator, the peers'
+// ([tp_reduce flags][2 halves x world slots x 8 tokens x 5120 words of 8
+// bytes: the fused exchange's tagged values, or tp_reduce_kernel's floats]),
+// its IPC handle all-gathered over the NCCL communicator, the peers'
 // allocations opened.  `mode` 1: tp_reduce_kernel, 2: fused into the GEMVs.
 bool setup_p2p(Q38Model *m, int mode)
 {
     const int world = m->shard.world, rank = m->shard.rank;
-    const size_t bytes =
-        kArFlagBytes + kXcFlagBytes + static_cast<size_t>(2) * world * kMaxTokens * kHidden * sizeof(float);
+    const size_t bytes = kArFlagBytes + static_cast<size_t>(2) * world * kMaxTokens * kHidden * sizeof(uint64_t);
     static_assert(8 * q38::kTpReduceCtas * sizeof(unsigned long long) <= kArFlagBytes, "flags area");
     static_assert(kMaxTokens == q38::kXcTokens, "exchange slots");
     // Every rank reaches both collectives below whatever failed locally, and
@@ -1624,8 +1619,7 @@ bool setup_p2p(Q38Model *m, int mode)
             base = static_cast<uint8_t *>(p);
         }
         m->ar_flags[r] = reinterpret_cast<unsigned long long *>(base);
-        m->xc_flags[r] = reinterpret_cast<unsigned int *>(base + kArFlagBytes);
-        m->ar_bufs[r] = reinterpret_cast<float *>(base + kArFlagBytes + kXcFlagBytes);
+        m->ar_bufs[r] = reinterpret_cast<float *>(base + kArFlagBytes);
     }
     // the smallest outcome over the ranks
     int *flag = reinterpret_cast<int *>(dev + sizeof(Entry) * world);
@@ -1886,7 +1880,8 @@ bool tc_layer(Q38Model *m, int l, int n, uint32_t base)
                                            s, nb),
                  "rmsnorm") ||
         !tc_project(m, L.gate_up, q8, m->pf_normf, kHidden, n, m->pf_wide, m->wide_ld, 0, L.swiglu_fused) ||
-        !cuda_ok(q38::launch_swiglu_quant(m->pf_wide, m->pf_wide + kFfn, m->wide_ld, kFfn, n, m->pf_act, q8, s),
+        !cuda_ok(q38::launch_swiglu_quant(m->pf_wide, m->pf_wide + kFfn, m->wide_ld, kFfn, n,
+                                          has_float_part(L.down) ? m->pf_act : nullptr, q8, s),
                  "swiglu"))
         return false;
     return tc_project(m, L.down, q8, m->pf_act, kFfn, n, m->pf_hidden, kHidden, 1, false);

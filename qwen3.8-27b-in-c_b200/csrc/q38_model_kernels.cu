@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 
 #include "q38_device.cuh"
+#include "q38_act.cuh"
 #include "q38_model_internal.h"
 #include "q38_types.cuh"
 
@@ -171,6 +172,62 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float *in, int
     if (out_q) quantize_block_256(v, out_q + static_cast<size_t>(tok) * q_ld + blockIdx.x, red_m);
 }
 
+// A Q8_K block from act_quantize_warp (lane l: quants 8l .. 8l + 7; lanes 4j:
+// the bsums of 16-element groups 2j, 2j + 1; the scale).
+__device__ __forceinline__ void store_q8k_warp(const WarpQ8K &r, Q8KBlock *dst)
+{
+    const int lane = threadIdx.x & 31;
+    uint32_t *qw = reinterpret_cast<uint32_t *>(dst->quants);
+    qw[2 * lane] = r.q0;
+    qw[2 * lane + 1] = r.q1;
+    if ((lane & 3) == 0) reinterpret_cast<uint32_t *>(dst->sums)[lane >> 2] = r.sums_word;
+    if (lane == 0) dst->scale = r.scale;
+}
+
+// The same for prompt-sized batches: one CTA per token forms the row's sum
+// of squares once (the same per-thread partials and warp order as above, so
+// the same bits), then each warp quantizes whole blocks (act_quantize_warp:
+// the same Q8_K bits as quantize_block_256).
+__global__ void __launch_bounds__(256) rmsnorm_quant_rows_kernel(const float *in, int in_ld, const float *weight,
+                                                                 int n, float *out_f, int out_ld, Q8KBlock *out_q,
+                                                                 int q_ld)
+{
+    __shared__ double red_d[8];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int tok = blockIdx.x;
+    const float *x = in + static_cast<size_t>(tok) * in_ld;
+    double part = 0.0;
+    for (int i = threadIdx.x; i < n; i += 256) {
+        const float v = x[i];
+        part += static_cast<double>(__fmul_rn(v, v));
+    }
+    const double sum = block_sum_d(part, red_d);
+    const float mean = static_cast<float>(sum / static_cast<double>(n));
+    const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, kRmsEps)));
+    // warp w quantizes blocks w, w + 8, ...; lane l holds elements 8l .. 8l + 7
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int b = warp; b < n / 256; b += 8) {
+        const int e0 = b * 256 + lane * 8;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; i += 4) {
+            const float4 xv = *reinterpret_cast<const float4 *>(x + e0 + i);
+            const float4 wv = *reinterpret_cast<const float4 *>(weight + e0 + i);
+            v[i] = __fmul_rn(__fmul_rn(xv.x, scale), wv.x);
+            v[i + 1] = __fmul_rn(__fmul_rn(xv.y, scale), wv.y);
+            v[i + 2] = __fmul_rn(__fmul_rn(xv.z, scale), wv.z);
+            v[i + 3] = __fmul_rn(__fmul_rn(xv.w, scale), wv.w);
+        }
+        if (out_f) {
+            float *of = out_f + static_cast<size_t>(tok) * out_ld + e0;
+            *reinterpret_cast<float4 *>(of) = make_float4(v[0], v[1], v[2], v[3]);
+            *reinterpret_cast<float4 *>(of + 4) = make_float4(v[4], v[5], v[6], v[7]);
+        }
+        if (out_q) store_q8k_warp(act_quantize_warp(v), out_q + static_cast<size_t>(tok) * q_ld + b);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // SwiGLU -> (float, Q8_K).  gate_up[tok] = [gate n | up n] at stride ld.
 // qwen38_model.c:523-541 (scalar q38_swiglu) followed by q38_quantize_q8_k.
@@ -188,6 +245,37 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const float *gate, co
     const float v = __fmul_rn(silu(g), u);
     if (out_f) out_f[static_cast<size_t>(tok) * n + e] = v;
     quantize_block_256(v, out_q + static_cast<size_t>(tok) * (n / 256) + blockIdx.x, red_m);
+}
+
+// The same for prompt-sized batches: one warp per (token, block), lane l
+// holding elements 8l .. 8l + 7 (act_quantize_warp: the same Q8_K bits).
+__global__ void __launch_bounds__(256) swiglu_quant_warp_kernel(const float *gate, const float *up, int ld, int n,
+                                                                int tokens, float *out_f, Q8KBlock *out_q)
+{
+    pdl_wait();
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int nb = n / 256;
+    const long long gw = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (gw >= static_cast<long long>(tokens) * nb) return;
+    const int tok = static_cast<int>(gw / nb), b = static_cast<int>(gw % nb);
+    const size_t o = static_cast<size_t>(tok) * ld + b * 256 + lane * 8;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; i += 4) {
+        const float4 g = *reinterpret_cast<const float4 *>(gate + o + i);
+        const float4 u = *reinterpret_cast<const float4 *>(up + o + i);
+        v[i] = __fmul_rn(silu(g.x), u.x);
+        v[i + 1] = __fmul_rn(silu(g.y), u.y);
+        v[i + 2] = __fmul_rn(silu(g.z), u.z);
+        v[i + 3] = __fmul_rn(silu(g.w), u.w);
+    }
+    if (out_f) {
+        float *of = out_f + static_cast<size_t>(tok) * n + b * 256 + lane * 8;
+        *reinterpret_cast<float4 *>(of) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4 *>(of + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    store_q8k_warp(act_quantize_warp(v), out_q + static_cast<size_t>(tok) * nb + b);
 }
 
 // ---------------------------------------------------------------------------
@@ -619,17 +707,19 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
 //       gb  [value head][token][2]    beta, decay
 //     (token stride rec_tokens, a multiple of kDeltaChunk).
 //  2. deltanet_prefill_kernel (serial in tokens): each warp owns 8 columns of
-//     one value head's state (lane l holds rows 4l .. 4l + 3 of each, in
-//     registers for the whole chunk); a CTA's 4 warps share the records of
-//     one column block, streamed into a ring of shared-memory stages by
-//     cp.async.bulk kDeltaChunk tokens at a time, so the token loop reads only
-//     shared memory.  It stores the raw head output (before the RMSNorm).
-//     Per token it makes one warp reduction, not two: with a = k.S and
-//     b = q.S of the state before the token, the upstream's
+//     one value head's state; lane l holds rows 32 (l / 8) .. + 31 of column
+//     l % 8, in registers for the whole chunk, so a column's dot products
+//     reduce over 4 lanes (2 shuffle levels).  A CTA's 4 warps share the
+//     records of one column block, streamed into a ring of shared-memory
+//     stages by cp.async.bulk kDeltaChunk tokens at a time, so the token loop
+//     reads only shared memory.  It stores the raw head output (before the
+//     RMSNorm).  With a = k.S and b = q.S of the state before the token, the
+//     upstream's
 //       S <- decay S;  kv = k.S;  delta = (v - kv) beta;  S <- S + k delta;
 //       out = q.S
-//     is evaluated as kv = decay a, out = decay b + (q.k) delta (the same
-//     quantities, rounded differently: about 1e-7 relative).
+//     is evaluated as kv = decay a, out = decay b + (q.k) delta: one
+//     reduction per token (the same quantities, rounded differently: about
+//     1e-7 relative).
 //  3. deltanet_prefill_post_kernel: head RMSNorm, the gate, Q8_K.
 //  4. deltanet_ring_store_kernel: the conv ring, once every reader is done.
 // ---------------------------------------------------------------------------
@@ -742,11 +832,12 @@ __global__ void __launch_bounds__(128) deltanet_prefill_kernel(DeltaPrefillArgs 
         for (int i = 0; i < kDeltaStages; ++i) mbar_init(&full[i], 1);
         fence_mbar_init();
     }
-    // the state columns
-    float *state = a.state + (static_cast<size_t>(vh) * 128 + col0) * 128 + lane * 4;
+    // this lane's state column (col0 + lane % 8), rows 32 rg .. 32 rg + 31
+    const int jc = lane & 7, rg = lane >> 3;
+    float *state = a.state + (static_cast<size_t>(vh) * 128 + col0 + jc) * 128 + rg * 32;
     float4 s[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) s[j] = *reinterpret_cast<const float4 *>(state + j * 128);
+    for (int j = 0; j < 8; ++j) s[j] = *reinterpret_cast<const float4 *>(state + j * 4);
     const float query_scale = __fdiv_rn(1.0f, sqrtf(128.0f));
     __syncthreads();
     pdl_wait();
@@ -778,41 +869,45 @@ __global__ void __launch_bounds__(128) deltanet_prefill_kernel(DeltaPrefillArgs 
         for (int i = 0; i < n; ++i) {
             const int t = c * kDeltaChunk + i;
             const float *rq = sqk + i * kDeltaQkLd;
-            const float4 q4 = reinterpret_cast<const float4 *>(rq)[lane];
-            const float4 k4 = reinterpret_cast<const float4 *>(rq + 128)[lane];
+            const float4 *q4 = reinterpret_cast<const float4 *>(rq + rg * 32);
+            const float4 *k4 = reinterpret_cast<const float4 *>(rq + 128 + rg * 32);
             const float qk = rq[256];
-            const float vcol = sv[i * 32 + warp * 8 + (lane & 7)];
+            const float vj = sv[i * 32 + warp * 8 + jc];
             const float2 gb = reinterpret_cast<const float2 *>(sgb)[i];
             const float beta = gb.x, decay = gb.y;
-            // k.S and q.S of the state before this token, reduced together
-            float red[16];
+            // k.S and q.S of the state before this token: the lane's 32 rows
+            // (two chains each), then the column's 4 lanes
+            float ka = 0.0f, kb = 0.0f, qa = 0.0f, qb = 0.0f;
+            float4 kk[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
+                kk[j] = k4[j];
+                const float4 qq = q4[j];
                 const float4 &x = s[j];
-                red[j] = fmaf(x.w, k4.w, fmaf(x.z, k4.z, fmaf(x.y, k4.y, __fmul_rn(x.x, k4.x))));
-                red[8 + j] = fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, __fmul_rn(x.x, q4.x))));
+                float &kacc = j & 1 ? kb : ka;
+                float &qacc = j & 1 ? qb : qa;
+                kacc = fmaf(x.w, kk[j].w, fmaf(x.z, kk[j].z, fmaf(x.y, kk[j].y, fmaf(x.x, kk[j].x, kacc))));
+                qacc = fmaf(x.w, qq.w, fmaf(x.z, qq.z, fmaf(x.y, qq.y, fmaf(x.x, qq.x, qacc))));
             }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) red[j] = __fadd_rn(red[j], __shfl_xor_sync(0xffffffffu, red[j], o));
-            }
-            // delta rule on the warp's 8 columns (qwen38_model.c:758-781)
-            float out = 0.0f;
+            float kd = __fadd_rn(ka, kb), qd = __fadd_rn(qa, qb);
+            kd = __fadd_rn(kd, __shfl_xor_sync(0xffffffffu, kd, 8));
+            qd = __fadd_rn(qd, __shfl_xor_sync(0xffffffffu, qd, 8));
+            kd = __fadd_rn(kd, __shfl_xor_sync(0xffffffffu, kd, 16));
+            qd = __fadd_rn(qd, __shfl_xor_sync(0xffffffffu, qd, 16));
+            // delta rule on the column (qwen38_model.c:758-781)
+            const float delta = __fmul_rn(__fsub_rn(vj, __fmul_rn(decay, kd)), beta);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 float4 &x = s[j];
-                const float vj = __shfl_sync(0xffffffffu, vcol, j);
-                const float delta = __fmul_rn(__fsub_rn(vj, __fmul_rn(decay, red[j])), beta);
-                x.x = fmaf(k4.x, delta, __fmul_rn(x.x, decay));
-                x.y = fmaf(k4.y, delta, __fmul_rn(x.y, decay));
-                x.z = fmaf(k4.z, delta, __fmul_rn(x.z, decay));
-                x.w = fmaf(k4.w, delta, __fmul_rn(x.w, decay));
-                const float oj = fmaf(qk, delta, __fmul_rn(decay, red[8 + j]));
-                if (lane == j) out = oj;
+                x.x = fmaf(kk[j].x, delta, __fmul_rn(x.x, decay));
+                x.y = fmaf(kk[j].y, delta, __fmul_rn(x.y, decay));
+                x.z = fmaf(kk[j].z, delta, __fmul_rn(x.z, decay));
+                x.w = fmaf(kk[j].w, delta, __fmul_rn(x.w, decay));
             }
-            if (lane < 8)
-                a.o_raw[static_cast<size_t>(t) * a.o_ld + vh * 128 + col0 + lane] = __fmul_rn(out, query_scale);
+            if (rg == 0) {
+                const float out = fmaf(qk, delta, __fmul_rn(decay, qd));
+                a.o_raw[static_cast<size_t>(t) * a.o_ld + vh * 128 + col0 + jc] = __fmul_rn(out, query_scale);
+            }
         }
         // every warp is done with this stage: refill it with chunk c + kDeltaStages
         __syncthreads();
@@ -831,7 +926,7 @@ __global__ void __launch_bounds__(128) deltanet_prefill_kernel(DeltaPrefillArgs 
             mbar_wait_bounded(&full[c % kDeltaStages], static_cast<uint32_t>(c / kDeltaStages) & 1u, nullptr);
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) *reinterpret_cast<float4 *>(state + j * 128) = s[j];
+    for (int j = 0; j < 8; ++j) *reinterpret_cast<float4 *>(state + j * 4) = s[j];
     pdl_launch_dependents();
 }
 
@@ -1494,6 +1589,9 @@ cudaError_t launch_rmsnorm_quant(const float *in, int in_ld, const float *weight
                                  int out_ld, void *out_q, cudaStream_t s, int q_ld)
 {
     if (n % 256) return cudaErrorInvalidValue;
+    if (tokens >= 64)  // a prompt: one CTA per token (same results)
+        return launch_pdl(rmsnorm_quant_rows_kernel, dim3(tokens), dim3(256), s, in, in_ld, weight, n, out_f, out_ld,
+                          static_cast<Q8KBlock *>(out_q), q_ld ? q_ld : n / 256);
     return launch_pdl(rmsnorm_quant_kernel, dim3(n / 256, tokens), dim3(256), s, in, in_ld, weight, n, out_f, out_ld,
                       static_cast<Q8KBlock *>(out_q), q_ld ? q_ld : n / 256);
 }
@@ -1502,6 +1600,12 @@ cudaError_t launch_swiglu_quant(const float *gate, const float *up, int ld, int 
                                 void *out_q, cudaStream_t s)
 {
     if (n % 256) return cudaErrorInvalidValue;
+    if (tokens >= 64 && ld % 4 == 0) {
+        // a prompt: one warp per (token, block) (same results)
+        const long long warps = static_cast<long long>(tokens) * (n / 256);
+        return launch_pdl(swiglu_quant_warp_kernel, dim3(static_cast<unsigned>((warps + 7) / 8)), dim3(256), s, gate,
+                          up, ld, n, tokens, out_f, static_cast<Q8KBlock *>(out_q));
+    }
     return launch_pdl(swiglu_quant_kernel, dim3(n / 256, tokens), dim3(256), s, gate, up, ld, n, out_f,
                       static_cast<Q8KBlock *>(out_q));
 }

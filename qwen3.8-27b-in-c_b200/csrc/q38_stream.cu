@@ -154,12 +154,11 @@ struct StreamArgs {
     int export_reps;
     long long export_rep_bytes;
     // Tensor-parallel exchange (xc_world > 1, a row-parallel projection; see
-    // xc_tile): each rank's buffer is [2 halves][world][kXcTokens][rows]
-    // floats, its flags [world][kXcMaxTiles]; xc_counter[0] counts the calls,
+    // xc_rows): each rank's buffer is [2 halves][world][kXcTokens][rows] words
+    // of (call tag << 32 | float bits); xc_counter[0] counts the calls,
     // xc_counter[1] the CTAs done with the current one.
     int xc_world, xc_rank;
-    float *xc_bufs[kXcMaxWorld];
-    unsigned int *xc_flags[kXcMaxWorld];
+    unsigned long long *xc_bufs[kXcMaxWorld];
     unsigned int *xc_counter;
 };
 
@@ -174,79 +173,72 @@ __device__ __forceinline__ void store_row(const StreamArgs &g, int tok, int row,
         *reinterpret_cast<float *>(reinterpret_cast<char *>(dst) + k * g.out_rep_bytes) = r;
 }
 
-__device__ __forceinline__ void st_release_sys_u32(unsigned int *p, unsigned int v)
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long *p, unsigned long long v)
 {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-__device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int *p)
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long *p)
 {
-    unsigned int v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
-__device__ __forceinline__ void consumer_barrier(int consumers);
-
-// Tensor-parallel exchange of one finished tile of a row-parallel projection
-// (fused with the GEMV, so a tile crosses NVLink as soon as its sums are
-// final while other CTAs still stream weights).  The `writer` threads hold
-// the tile's row values vals[tok] (this rank's partial sums); they store
-// them into slot `rank` of every rank's buffer (peer memory), one thread
-// raises the tile's flag on every rank (system-scope release after a
-// system fence) and waits, bounded, until every rank's flag for the tile
-// here shows this call; then the writers add the world's slots in rank
-// order and store out[tok][row] (+)= sum - the all-reduce and the residual
-// add of the upstream's row-parallel projection.  xs[0]: an abandoned wait
-// (the rows are not stored, the status word says why); xs[1]: the call
-// number.  Buffers alternate halves by call parity: a rank writes half h
-// again only two calls later, after every rank has finished the call that
-// read it.
+// Tensor-parallel exchange of finished rows of a row-parallel projection,
+// fused with the GEMV: a tile crosses NVLink as soon as its sums are final,
+// while other CTAs still stream weights.  Each `writer` thread holds row
+// `row`'s partial sums vals[tok] on this rank.  It stores every value into
+// slot `rank` of every rank's buffer (peer memory) as one 8-byte word
+// (call tag << 32 | float bits, tag = call + 1), so the value and the proof
+// that it belongs to this call arrive together - no fence and no separate
+// flag; then it reads its row's word from every rank's slot in its own
+// buffer, waiting (bounded) until each carries this call's tag, adds them in
+// rank order and stores out[tok][row] (+)= sum - the all-reduce and the
+// residual add of the upstream's row-parallel projection.  The tag compare
+// is wrap-safe.  Buffers alternate halves by call parity: a rank writes a
+// half again only two calls later, after every rank has finished the call
+// that read it.  An abandoned wait records the status word and leaves the
+// row unstored; so does `keep` false (this CTA's own sums are void after an
+// abandoned wait, but the peers still get words to end their waits).
+// xs[1]: the call number.
 template <int MT>
-__device__ void xc_tile(const StreamArgs &g, int t, int row, bool writer, const float *vals, int consumers,
-                        volatile int *xs)
+__device__ void xc_rows(const StreamArgs &g, int row, bool writer, bool keep, const float *vals, volatile int *xs)
 {
-    const unsigned int call = static_cast<unsigned int>(xs[1]);
+    if (!writer) return;
+    const unsigned int tag = static_cast<unsigned int>(xs[1]) + 1u;
     const size_t slot = static_cast<size_t>(kXcTokens) * g.rows;
-    const size_t half = static_cast<size_t>(call & 1u) * g.xc_world * slot;
-    if (writer) {
+    const size_t half = static_cast<size_t>((tag - 1u) & 1u) * g.xc_world * slot;
 #pragma unroll
-        for (int tok = 0; tok < MT; ++tok) {
-            if (tok >= g.tokens) break;
-            for (int r = 0; r < g.xc_world; ++r)
-                g.xc_bufs[r][half + g.xc_rank * slot + static_cast<size_t>(tok) * g.rows + row] = vals[tok];
-        }
-    }
-    consumer_barrier(consumers);
-    if (threadIdx.x == 0) {
-        __threadfence_system();
+    for (int tok = 0; tok < MT; ++tok) {
+        if (tok >= g.tokens) break;
+        const unsigned long long word =
+            (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(vals[tok]);
         for (int r = 0; r < g.xc_world; ++r)
-            st_release_sys_u32(g.xc_flags[r] + g.xc_rank * kXcMaxTiles + t, call + 1u);
-        const unsigned long long start = global_timer_ns();
+            st_relaxed_sys_u64(g.xc_bufs[r] + half + g.xc_rank * slot + static_cast<size_t>(tok) * g.rows + row, word);
+    }
+    const unsigned long long *mine = g.xc_bufs[g.xc_rank] + half;
+    const unsigned long long start = global_timer_ns();
+#pragma unroll
+    for (int tok = 0; tok < MT; ++tok) {
+        if (tok >= g.tokens) break;
+        float sum = 0.0f;
         bool ok = true;
         for (int r = 0; r < g.xc_world && ok; ++r) {
-            const unsigned int *f = g.xc_flags[g.xc_rank] + r * kXcMaxTiles + t;
-            while (static_cast<int>(ld_acquire_sys_u32(f) - (call + 1u)) < 0) {
+            const unsigned long long *p = mine + r * slot + static_cast<size_t>(tok) * g.rows + row;
+            unsigned long long w = ld_relaxed_sys_u64(p);
+            while (static_cast<int>(static_cast<unsigned int>(w >> 32) - tag) < 0) {
                 if (global_timer_ns() - start > kWaitLimitNs) {
                     atomicExch(&g_stream_status, kStatusWaitTimeout);
                     ok = false;
                     break;
                 }
+                w = ld_relaxed_sys_u64(p);
             }
+            const float v = __uint_as_float(static_cast<unsigned int>(w));
+            sum = r == 0 ? v : __fadd_rn(sum, v);
         }
-        if (!ok) xs[0] = 1;
-    }
-    consumer_barrier(consumers);
-    if (writer && !xs[0]) {
-        const float *mine = g.xc_bufs[g.xc_rank] + half;
-#pragma unroll
-        for (int tok = 0; tok < MT; ++tok) {
-            if (tok >= g.tokens) break;
-            const size_t o = static_cast<size_t>(tok) * g.rows + row;
-            float sum = __ldcg(mine + o);
-            for (int r = 1; r < g.xc_world; ++r) sum = __fadd_rn(sum, __ldcg(mine + r * slot + o));
-            store_row(g, tok, row, sum);
-        }
+        if (ok && keep) store_row(g, tok, row, sum);
     }
 }
 
@@ -834,11 +826,8 @@ __global__ void __launch_bounds__(StreamThreads<MT, L>::kValue, 1) stream_gemm_k
     asm volatile("griddepcontrol.wait;" ::: "memory");
     trace_mark(g.trace, kTraceReady);
     trace_mark(g.trace, kTraceLastReady);
-    volatile int *xs = issued + 2;  // exchange state (see xc_tile)
-    if (g.xc_world > 1 && tid == 0) {
-        xs[0] = 0;
-        xs[1] = static_cast<int>(__ldcg(g.xc_counter));
-    }
+    volatile int *xs = issued + 2;  // exchange state (see xc_rows)
+    if (g.xc_world > 1 && tid == 0) xs[1] = static_cast<int>(__ldcg(g.xc_counter));
 
     const int slots = MT * g.nb;
     if (g.act_mode == kActQ8K) {
@@ -960,8 +949,9 @@ __global__ void __launch_bounds__(StreamThreads<MT, L>::kValue, 1) stream_gemm_k
             swiglu_epilogue<MT>(g, t, rt, grp, part, failed, total, consumers, last_flag);
         } else if (seg_whole) {
             if (g.xc_world > 1) {
-                xc_tile<MT>(g, t, row, grp == 0 && part == 0 && !failed && mine_row && row < g.rows, total, consumers,
-                            xs);
+                // (also after a failure, so that the peers' waits end; the
+                // status word already says the results are void)
+                xc_rows<MT>(g, row, grp == 0 && part == 0 && mine_row && row < g.rows, !failed, total, xs);
             } else if (grp == 0 && part == 0 && !failed && mine_row && row < g.rows) {
 #pragma unroll
                 for (int tok = 0; tok < MT; ++tok)
@@ -1004,8 +994,8 @@ __global__ void __launch_bounds__(StreamThreads<MT, L>::kValue, 1) stream_gemm_k
             if (*last_flag && tid == 0) atomicExch(&g.counters[t], 0);
             if (*last_flag && g.xc_world > 1) {
                 // the tile's last CTA exchanges it (also after a failure, so
-                // that the peers' waits end; its rows are then not stored)
-                xc_tile<MT>(g, t, row, finisher && row < g.rows, fin, consumers, xs);
+                // that the peers' waits end)
+                xc_rows<MT>(g, row, grp == 0 && part == 0 && mine_row && row < g.rows, finisher, fin, xs);
             } else if (finisher && row < g.rows) {
 #pragma unroll
                 for (int tok = 0; tok < MT; ++tok)
@@ -1275,17 +1265,13 @@ cudaError_t launch_t(const StreamPlan &p, const StreamLaunch &l, cudaStream_t st
     if (l.side_w && (l.act_mode != kActRmsNorm || l.side_rows > p.grid)) return cudaErrorInvalidValue;
     g.xc_world = l.xc_world > 1 ? l.xc_world : 0;
     g.xc_rank = l.xc_rank;
-    for (int r = 0; r < kXcMaxWorld; ++r) {
-        g.xc_bufs[r] = r < g.xc_world ? l.xc_bufs[r] : nullptr;
-        g.xc_flags[r] = r < g.xc_world ? l.xc_flags[r] : nullptr;
-    }
+    for (int r = 0; r < kXcMaxWorld; ++r) g.xc_bufs[r] = r < g.xc_world ? l.xc_bufs[r] : nullptr;
     g.xc_counter = l.xc_counter;
     // the exchange waits on the peers' CTAs inside the kernel: every CTA must
-    // be resident at once (one per SM), and the tiles must fit the flags
+    // be resident at once (one per SM)
     if (g.xc_world > 1 &&
         (g.xc_world > kXcMaxWorld || l.xc_rank < 0 || l.xc_rank >= g.xc_world || !l.xc_counter ||
-         l.tokens > kXcTokens || p.tiles > kXcMaxTiles || p.rows > l.xc_rows || p.grid > device_sm_count() ||
-         l.sw_act))
+         l.tokens > kXcTokens || p.rows > l.xc_rows || p.grid > device_sm_count() || l.sw_act))
         return cudaErrorInvalidValue;
     const void *kernel = select_kernel<Dec>(p.mt, l.dbg_w != nullptr, p.parts);
     if (!kernel) return cudaErrorInvalidValue;

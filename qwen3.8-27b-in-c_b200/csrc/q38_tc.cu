@@ -342,11 +342,12 @@ template <int BN> constexpr size_t tc_smem_bytes()
 
 __device__ __forceinline__ uint32_t ld_u16(const uint8_t *p) { return p[0] | (p[1] << 8); }
 
-// One 32-element group (a Q4_K sub-block, or two Q6_K sub-blocks of 16) of
-// dequantized weights, as the upstream float path forms them.
-__device__ __forceinline__ void q4k_group(const uint8_t *b, int grp, float (&w)[32])
+// Weights 8 l .. 8 l + 7 of one superblock (lane l of a warp), dequantized
+// with the upstream float formula of the type (qwen38_quant.c:330-508):
+// Q4_K w = (d sc) q - dmin m per 32-weight sub-block, Q6_K w = (d sc) q.
+__device__ __forceinline__ void q4k_eight(const uint8_t *b, int lane, float (&w)[8])
 {
-    const int chunk = grp >> 1, hi = grp & 1;
+    const int grp = lane >> 2, chunk = lane >> 3, hi = grp & 1;
     int sc, m;
     const uint8_t *p = b + 4;
     if (grp < 4) {
@@ -358,31 +359,34 @@ __device__ __forceinline__ void q4k_group(const uint8_t *b, int grp, float (&w)[
     }
     const float d = f16_bits_to_f32(ld_u16(b)), dmin = f16_bits_to_f32(ld_u16(b + 2));
     const float ds = __fmul_rn(d, static_cast<float>(sc)), dm = __fmul_rn(dmin, static_cast<float>(m));
-    const uint4 *q = reinterpret_cast<const uint4 *>(b + 16 + chunk * 32);
-    uint32_t words[8];
-    // 4-byte-aligned reads: a Q4_K block is 144 bytes and blocks start on 16-byte boundaries
-    const uint32_t *qw = reinterpret_cast<const uint32_t *>(q);
+    // 8 quant bytes, 8-byte aligned (blocks of 144 bytes start on 16-byte boundaries)
+    const uint2 q = *reinterpret_cast<const uint2 *>(b + 16 + chunk * 32 + (lane & 3) * 8);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) words[i] = qw[i];
-#pragma unroll
-    for (int e = 0; e < 32; ++e) {
-        const uint32_t byte = (words[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+    for (int e = 0; e < 8; ++e) {
+        const uint32_t byte = ((e < 4 ? q.x : q.y) >> (8 * (e & 3))) & 0xFFu;
         const int qv = hi ? static_cast<int>(byte >> 4) : static_cast<int>(byte & 15u);
         w[e] = __fsub_rn(__fmul_rn(ds, static_cast<float>(qv)), dm);
     }
 }
 
-__device__ __forceinline__ void q6k_group(const uint8_t *b, int grp, float (&w)[32])
+__device__ __forceinline__ void q6k_eight(const uint8_t *b, int lane, float (&w)[8])
 {
-    const int half = grp >> 2, qq = grp & 3;
+    const int half = lane >> 4, qq = (lane >> 2) & 3, el0 = (lane & 3) * 8;
     const float d = f16_bits_to_f32(ld_u16(b + 208));
+    const int sc = static_cast<int8_t>(b[192 + half * 8 + qq * 2 + el0 / 16]);
+    const float dsc = __fmul_rn(d, static_cast<float>(sc));
+    // Q6_K blocks are 210 bytes: only 2-byte alignment holds
+    const uint8_t *lbp = b + half * 64 + (qq & 1) * 32 + el0;
+    const uint8_t *hbp = b + 128 + half * 32 + el0;
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-        const uint8_t lb = b[half * 64 + (qq & 1) * 32 + e];
-        const uint8_t hb = b[128 + half * 32 + e];
-        const int q = ((qq < 2 ? (lb & 15) : (lb >> 4)) | (((hb >> (2 * qq)) & 3) << 4)) - 32;
-        const int sc = static_cast<int8_t>(b[192 + half * 8 + qq * 2 + e / 16]);
-        w[e] = __fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q));
+    for (int e = 0; e < 8; e += 2) {
+        const uint32_t l2 = ld_u16(lbp + e), h2 = ld_u16(hbp + e);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const uint32_t lb = (l2 >> (8 * k)) & 0xFFu, hb = (h2 >> (8 * k)) & 0xFFu;
+            const int q = static_cast<int>((qq < 2 ? (lb & 15u) : (lb >> 4)) | (((hb >> (2 * qq)) & 3u) << 4)) - 32;
+            w[e + k] = __fmul_rn(dsc, static_cast<float>(q));
+        }
     }
 }
 
@@ -424,21 +428,22 @@ __device__ __forceinline__ void split2(float a, float b, __half2 &hi, __half2 &l
 }
 
 // Weights -> fp16 hi [rows][width] and lo (rows * width further), times
-// 1 / row_scale.  One thread per (row, 32-element group).  Rows are read in
-// the tiled layout when tile_rows != 0.  With `split`, the rows come
+// 1 / row_scale.  One warp per (row, superblock): lane l forms weights
+// 8 l .. 8 l + 7 and stores them as one 16-byte vector of each half, so a
+// warp writes 512 contiguous bytes of hi and of lo.  Rows are read in the
+// tiled layout when tile_rows != 0.  With `split`, the rows come
 // interleaved in pairs (gate i, up i) and are written as [gate rows | up
 // rows] (row_scale is indexed by the written row).
-__global__ void dequant_f16_kernel(const uint8_t *w, int type, uint64_t rows, uint64_t width, uint32_t tile_rows,
-                                   int bb, __half *out, const float *row_scale, int split)
+__global__ void __launch_bounds__(256) dequant_f16_kernel(const uint8_t *w, int type, uint64_t rows, uint64_t width,
+                                                          uint32_t tile_rows, int bb, __half *out,
+                                                          const float *row_scale, int split)
 {
     pdl_wait();
-    const uint64_t groups = width / 32, nb = width / 256;
-    const uint64_t total = rows * groups;
-    __half *out_lo = out + rows * width;
-    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-        const uint64_t row = i / groups, g = i - row * groups;
-        const uint64_t blk = g >> 3;
+    const uint64_t nb = width / 256;
+    const uint64_t gw = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (gw < rows * nb) {
+        const uint64_t row = gw / nb, blk = gw - row * nb;
         const uint8_t *b;
         if (tile_rows) {
             const uint64_t t = row / tile_rows, r = row - t * tile_rows;
@@ -446,15 +451,17 @@ __global__ void dequant_f16_kernel(const uint8_t *w, int type, uint64_t rows, ui
         } else {
             b = w + (row * nb + blk) * bb;
         }
-        float v[32];
-        if (type == 12) q4k_group(b, static_cast<int>(g & 7), v);
-        else q6k_group(b, static_cast<int>(g & 7), v);
+        float v[8];
+        if (type == 12) q4k_eight(b, lane, v);
+        else q6k_eight(b, lane, v);
         const uint64_t orow = split ? ((row & 1) ? rows / 2 + row / 2 : row / 2) : row;
         const float inv = __frcp_rn(__ldg(row_scale + orow));  // a power of two: exact
-        __half2 *hi = reinterpret_cast<__half2 *>(out + orow * width + g * 32);
-        __half2 *lo = reinterpret_cast<__half2 *>(out_lo + orow * width + g * 32);
+        __half2 hi[4], lo[4];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) split2(__fmul_rn(v[2 * e], inv), __fmul_rn(v[2 * e + 1], inv), hi[e], lo[e]);
+        for (int e = 0; e < 4; ++e) split2(__fmul_rn(v[2 * e], inv), __fmul_rn(v[2 * e + 1], inv), hi[e], lo[e]);
+        const size_t o = orow * width + blk * 256 + lane * 8;
+        *reinterpret_cast<uint4 *>(out + o) = *reinterpret_cast<const uint4 *>(hi);
+        *reinterpret_cast<uint4 *>(out + rows * width + o) = *reinterpret_cast<const uint4 *>(lo);
     }
     pdl_launch_dependents();
 }
@@ -577,8 +584,8 @@ cudaError_t launch_dequant_f16(const void *w, int type, uint64_t rows, uint64_t 
                                                  width / 256, tile_rows, bb, row_scale, split);
         if (e != cudaSuccess) return e;
     }
-    const uint64_t total = rows * (width / 32);
-    const unsigned grid = static_cast<unsigned>(std::min<uint64_t>((total + 255) / 256, 148ull * 16));
+    const uint64_t warps = rows * (width / 256);
+    const unsigned grid = static_cast<unsigned>((warps * 32 + 255) / 256);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(256);

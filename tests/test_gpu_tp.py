@@ -1,5 +1,5 @@
-"""Tensor-parallel decode on 2 GPUs (q38cu_model_open_tp, NCCL), against the
-same model on one GPU.  Skipped on a machine with fewer than 2 GPUs.
+"""Tensor-parallel decode on 2, 4 and 8 GPUs (q38cu_model_open_tp), against
+the same model on one GPU.  Each case is skipped on a machine with fewer GPUs.
 
 Each rank holds one shard (include/q38cuda_model.h: column-parallel
 projections keep their output rows, row-parallel ones their input
@@ -67,24 +67,29 @@ def cosine(a, b):
     return a @ b / np.linalg.norm(a) / np.linalg.norm(b)
 
 
-@pytest.mark.parametrize("mode", [0, 1, 2], ids=["nccl", "nvlink-p2p", "fused-gemv-exchange"])
-def test_two_gpu_tensor_parallel_matches_one_gpu(tmp_path, mode):
-    """All three collectives: NCCL's all-reduce (Q38CU_TP_P2P=0), the
-    reduction kernel over CUDA IPC peer memory (1), and the exchange fused
-    into the row-parallel GEMVs tile by tile (2); bounded flag waits."""
+@pytest.mark.parametrize("world,mode", [(2, 0), (2, 1), (2, 2), (4, 2), (8, 2), (8, 0)],
+                         ids=["2-nccl", "2-nvlink-p2p", "2-fused-gemv-exchange", "4-fused-gemv-exchange",
+                              "8-fused-gemv-exchange", "8-nccl"])
+def test_tensor_parallel_matches_one_gpu(tmp_path, world, mode):
+    """All three collectives on 2 GPUs: NCCL's all-reduce (Q38CU_TP_P2P=0),
+    the reduction kernel over CUDA IPC peer memory (1), and the exchange fused
+    into the row-parallel GEMVs (2, the default); the default on 4 and 8 GPUs
+    (8: two ranks share each attention KV head) and NCCL on 8.  Skipped where
+    the machine has fewer GPUs."""
     import torch
     import torch.multiprocessing as mp
     from q38b200 import gguf
     from q38b200.model import Model
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     path = gguf.cached_model_path(seed=3, mtp=False, dist="robust")
-    world = 2
     mp.start_processes(_rank_main, args=(world, _free_port(), path, str(tmp_path), mode), nprocs=world,
                        start_method="spawn")
-    r0, r1 = (np.load(os.path.join(tmp_path, f"rank{r}.npz")) for r in range(world))
+    ranks = [np.load(os.path.join(tmp_path, f"rank{r}.npz")) for r in range(world)]
+    r0 = ranks[0]
     for key in ("layer0", "prefill", "step", "greedy"):
-        assert np.array_equal(r0[key], r1[key]), f"ranks disagree on {key}"
+        for r in range(1, world):
+            assert np.array_equal(r0[key], ranks[r][key]), f"ranks 0 and {r} disagree on {key}"
     one = Model(path, 128)
     try:
         layer0 = np.stack([one.forward_token_layers(t, 1) for t in (777, 3)])

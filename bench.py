@@ -779,6 +779,15 @@ def run_single(args, rank, world):
         from q38b200.model import Model
         path = model_path(args.mix, rank, None)
         m = Model(path, CONTEXT)
+        if args.profile:
+            # one 4096-token prefill after a short warm-up, nothing else (for a launch list)
+            m.prefill(decode_prompt(16, seed=3))
+            m.reset()
+            m.prefill(decode_prompt(PREFILL_TOKENS, seed=4096))
+            torch.cuda.synchronize()
+            m.close()
+            print(json.dumps({"profile_run": "config4 prefill", "tokens": PREFILL_TOKENS}), flush=True)
+            return
         rec = measure_prefill(m, path, torch.cuda.ExternalStream(m.stream))
         m.close()
     if rank != 0:

@@ -109,6 +109,15 @@ int q38cu_tensor_gemm_f32(float *output, const float *input, uint32_t batch_size
  * bit-exact with the upstream basis-vector evaluation for finite weights. */
 int q38cu_tensor_row_f32(float *output, const Q38CuTensor *tensor, uint64_t row, void *stream);
 
+/* Dot product of one row with a float vector (replaces q38_tensor_dot_row_f32,
+ * qwen38_quant.h:31-32): *output (device memory) = row . input (device, width
+ * floats), the same value as that row of q38cu_tensor_gemv_f32.  As upstream,
+ * returns 1 only when the result is finite: the call waits for the stream to
+ * read it back (the one synchronizing entry of this header besides
+ * q38cu_device_status). */
+int q38cu_tensor_dot_row_f32(float *output, const float *input, const Q38CuTensor *tensor, uint64_t row,
+                             void *stream);
+
 /* Allocate device memory for a tensor (16-byte aligned, padded), copy
  * `host_data` (GGUF bytes, may be NULL to only allocate) into it in the given
  * layout and, for the tiled layout, choose its tile height for this device and

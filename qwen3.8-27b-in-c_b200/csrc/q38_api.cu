@@ -1,6 +1,7 @@
 // q38_api.cu - the extern "C" entry points declared in include/q38cuda.h:
 // argument validation with the upstream return convention (1 ok, 0 bad
 // arguments / unsupported), launch planning and tensor upload.
+#include <cmath>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -442,6 +443,25 @@ int q38cu_tensor_row_f32(float *output, const Q38CuTensor *tensor, uint64_t row,
                                               static_cast<int>(tensor->type), static_cast<int>(g.elements),
                                               static_cast<int>(g.bytes), static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? 1 : fail_cuda("row launch", e);
+}
+
+int q38cu_tensor_dot_row_f32(float *output, const float *input, const Q38CuTensor *tensor, uint64_t row,
+                             void *stream)
+{
+    if (!output || !input || !tensor) return fail("output, input and tensor are required%s");
+    if (!check_matrix(tensor, tensor->shape[0])) return 0;
+    if (row >= tensor->shape[1]) return fail("row out of range%s");
+    if (!float_path_type(tensor->type)) return fail("type has no float-path kernel%s");
+    const Geometry g = geometry(tensor->type);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = q38::launch_dot_row_f32(output, input, tensor->data, tensor->shape[0], layout_tile_rows(tensor),
+                                            row, static_cast<int>(tensor->type), static_cast<int>(g.elements),
+                                            static_cast<int>(g.bytes), s);
+    float host = 0.0f;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&host, output, sizeof(float), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return fail_cuda("dot row", e);
+    return std::isfinite(host) ? 1 : fail("the row's dot product is not finite%s");
 }
 
 int q38cu_tensor_upload(Q38CuTensor *tensor, uint32_t type, uint64_t width, uint64_t rows, const void *host_data,

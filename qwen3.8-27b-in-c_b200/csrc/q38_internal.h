@@ -177,6 +177,9 @@ cudaError_t launch_quantize_q8k(void *out, const float *in, uint64_t blocks, cud
 cudaError_t launch_f32_gemm(float *out, const float *x, int batch, uint64_t width, const void *w, uint64_t rows,
                             uint32_t tile_rows, int type, int be, int bb, cudaStream_t s);
 // PDL launch with strides: out[tok * out_ld + row] (+)= row . x[tok * x_ld ..]
+// One row's dot product with x (the f32 GEMV's arithmetic for that row).
+cudaError_t launch_dot_row_f32(float *out, const float *x, const void *w, uint64_t width, uint32_t tile_rows,
+                               uint64_t row, int type, int be, int bb, cudaStream_t s);
 cudaError_t launch_f32_gemm_ex(float *out, uint64_t out_ld, int accumulate, const float *x, uint64_t x_ld, int batch,
                                uint64_t width, const void *w, uint64_t rows, uint32_t tile_rows, int type, int be,
                                int bb, cudaStream_t s);

@@ -516,6 +516,22 @@ __global__ void __launch_bounds__(256) f32_gemm_tile32_kernel(float *out, const 
         }
 }
 
+// Row `row` . x by one warp, in f32_gemm_kernel's order (the same value).
+__global__ void dot_row_f32_kernel(float *out, const float *x, const uint8_t *w, uint64_t width, uint32_t tile_rows,
+                                   uint64_t row, int type, int be, int bb)
+{
+    const int lane = threadIdx.x & 31;
+    const uint64_t nblocks = width / be;
+    float total = 0.0f;
+    for (uint64_t blk = lane; blk < nblocks; blk += 32) {
+        const uint8_t *b = block_at(w, row, blk, nblocks, tile_rows, bb);
+        for (int i = 0; i < be; ++i) total = fmaf(element_weight(type, b, i), __ldg(x + blk * be + i), total);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) total += __shfl_xor_sync(0xffffffffu, total, off);
+    if (lane == 0) *out = total;
+}
+
 // Element i of row `row`.  The upstream evaluates fma(w, 1, 0) against a
 // basis vector, which equals w for finite w except that -0 becomes +0.
 __global__ void row_f32_kernel(float *out, const uint8_t *w, uint64_t width, uint32_t tile_rows, uint64_t row,
@@ -712,6 +728,13 @@ cudaError_t launch_quantize_q8k(void *out, const float *in, uint64_t blocks, cud
     const uint64_t threads = blocks * 32;
     const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
     quantize_q8k_kernel<<<grid, 256, 0, s>>>(static_cast<Q8KBlock *>(out), in, blocks);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dot_row_f32(float *out, const float *x, const void *w, uint64_t width, uint32_t tile_rows,
+                               uint64_t row, int type, int be, int bb, cudaStream_t s)
+{
+    dot_row_f32_kernel<<<1, 32, 0, s>>>(out, x, static_cast<const uint8_t *>(w), width, tile_rows, row, type, be, bb);
     return cudaGetLastError();
 }
 

@@ -51,6 +51,7 @@ def _load(path=LIB_PATH):
         "q38cu_tensor_gemv_f32": ([vp, vp, tp, vp], ctypes.c_int),
         "q38cu_tensor_gemm_f32": ([vp, vp, u32, u64, tp, vp], ctypes.c_int),
         "q38cu_tensor_row_f32": ([vp, tp, u64, vp], ctypes.c_int),
+        "q38cu_tensor_dot_row_f32": ([vp, vp, tp, u64, vp], ctypes.c_int),
         "q38cu_tensor_upload": ([tp, u32, u64, u64, vp, u32, vp], ctypes.c_int),
         "q38cu_tensor_repack": ([tp, tp, vp], ctypes.c_int),
         "q38cu_tensor_free": ([tp], None),
@@ -169,6 +170,16 @@ def gemm_f32(tensor, x, out=None):
         out = torch.empty((batch, tensor.rows), dtype=torch.float32, device=x.device)
     _check(lib().q38cu_tensor_gemm_f32(_ptr(out), _ptr(x), batch, tensor.width, ctypes.byref(tensor.desc),
                                        _stream()), "q38cu_tensor_gemm_f32")
+    return out
+
+
+def dot_row_f32(tensor, x, row):
+    """Row `row` . x (x [width] fp32 on the device) -> a 1-element device
+    tensor; raises when the result is not finite (the upstream's contract)."""
+    import torch
+    out = torch.empty(1, dtype=torch.float32, device=x.device)
+    _check(lib().q38cu_tensor_dot_row_f32(_ptr(out), _ptr(x), ctypes.byref(tensor.desc), row, _stream()),
+           "q38cu_tensor_dot_row_f32")
     return out
 
 

@@ -191,6 +191,29 @@ def test_float_path_prompt_batch(q38, oracle, qtype, rows, batch):
     assert_close(out, oracle.gemm_f32(qtype, weights, rows, width, x))
 
 
+@pytest.mark.parametrize("qtype", (O.Q8_0, O.Q4_K, O.Q6_K, O.F16), ids=lambda t: NAME[t])
+def test_dot_row_matches_gemv_row(q38, oracle, qtype):
+    """q38cu_tensor_dot_row_f32 (upstream q38_tensor_dot_row_f32): one row's
+    dot product equals that row of the float GEMV bit for bit and the upstream
+    float path within tolerance; a non-finite result is refused."""
+    import torch
+    rows, width = 37, 2048
+    weights = synth.quant_tensor(qtype, rows, width, seed=21)
+    x = synth.activations(1, width, seed=22)
+    t = q38.DeviceTensor(qtype, width, rows, weights)
+    xd = to_dev(x[0])
+    full = q38.gemm_f32(t, to_dev(x)).cpu().numpy()[0]
+    want = oracle.gemm_f32(qtype, weights, rows, width, x)[0]
+    for r in (0, 17, rows - 1):
+        got = q38.dot_row_f32(t, xd, r).cpu().numpy()[0]
+        assert got == full[r], (r, got, full[r])
+        assert_close(np.array([got]), np.array([want[r]]))
+    bad = xd.clone()
+    bad[5] = float("inf")
+    with pytest.raises(q38.Q38CudaError):
+        q38.dot_row_f32(t, bad, 3)
+
+
 @pytest.mark.parametrize("layout", LAYOUTS, ids=LAYOUT_IDS)
 def test_embedding_row_full_size(q38, oracle, layout):
     """token_embd row dequant (Q4_K 248320 x 5120 in the mix; a slice here)."""

@@ -379,6 +379,7 @@ def measure_verify(passes=200, warmup=5, with_cpu=True):
 PROMPT_TOKENS = 128
 PREFILL_TOKENS = 4096
 PREFILL_DECODE = 512
+PREFILL_WARMUP = 128  # a warm-up prompt long enough for the tensor-core prefill path
 CONTEXT = PREFILL_TOKENS + PREFILL_DECODE   # config 3's 4096-token window fits inside
 VOCAB = 248320
 MODEL_SEED = 0
@@ -520,7 +521,8 @@ def measure_prefill(m, path, stream, with_cpu=True):
     import torch
     prompt = decode_prompt(PREFILL_TOKENS, seed=4096)
     m.reset()
-    m.prefill(decode_prompt(16, seed=3))  # warm-up: plans, graphs, pages
+    # warm-up on the same (tensor-core) path: kernels loaded, buffers and plans made
+    m.prefill(decode_prompt(PREFILL_WARMUP, seed=3))
     m.reset()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -780,8 +782,8 @@ def run_single(args, rank, world):
         path = model_path(args.mix, rank, None)
         m = Model(path, CONTEXT)
         if args.profile:
-            # one 4096-token prefill after a short warm-up, nothing else (for a launch list)
-            m.prefill(decode_prompt(16, seed=3))
+            # one 4096-token prefill after a warm-up prefill, nothing else (for a launch list)
+            m.prefill(decode_prompt(PREFILL_WARMUP, seed=3))
             m.reset()
             m.prefill(decode_prompt(PREFILL_TOKENS, seed=4096))
             torch.cuda.synchronize()

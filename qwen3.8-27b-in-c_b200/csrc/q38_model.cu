@@ -1916,7 +1916,9 @@ bool prefill_tc(Q38Model *m, const uint32_t *tokens, uint32_t count)
 {
     const uint32_t base = m->position;
     const cudaStream_t s = m->stream;
-    if (!ensure_prefill_buffers(m, static_cast<int>(std::min<uint32_t>(count, kTcChunk)))) return false;
+    // buffers for a whole chunk (or the context) on the first call, so a later
+    // longer prompt does not reallocate them (cudaMalloc synchronizes the device)
+    if (!ensure_prefill_buffers(m, static_cast<int>(std::min<uint32_t>(m->context_length, kTcChunk)))) return false;
     const Q38CuTensor &emb = m->embedding;
     const uint32_t be = q38cu_block_elements(emb.type), bb = q38cu_block_bytes(emb.type);
     for (uint32_t done = 0; done < count;) {

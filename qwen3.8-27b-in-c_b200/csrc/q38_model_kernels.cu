@@ -1245,151 +1245,283 @@ __global__ void __launch_bounds__(256) attn_prefill_qk_kernel(AttnPrefillArgs a)
     pdl_launch_dependents();
 }
 
+// ---- attn_prefill_kernel: tensor cores (mma.sync m16n8k16, fp16 in, fp32
+// accumulate) on two-term operands ----
+//
+// Every fp32 operand x is split into hi = fp16(x) and lo = fp16(x - hi) (22
+// significant bits), and a product is hi.hi + hi.lo + lo.hi (the lo.lo term is
+// below 2^-22 of it): scores S = Q K^T and the weighted values P V carry the
+// rounding of fp32 products with 22-bit operands, not fp16's 11 bits.  V is
+// scaled by 2^-4 before the split (exact; undone at the end) so that values up
+// to 2^20 stay in fp16 range.
+//
+// A CTA takes 64 queries of one head (8 warps); per tile of 64 keys:
+//   1. all threads load the K and V rows (fp32 or fp16 cache) and split them
+//      into hi/lo fp16 in shared memory (rows padded to 528 bytes: the eight
+//      16-byte rows of an ldmatrix land in distinct bank groups);
+//   2. warp w scores query rows 16 (w % 4) .. + 15 against keys 32 (w / 4) ..
+//      + 31 (4 n-tiles of 8, 16 k-steps of 16 dimensions, 3 MMAs each);
+//   3. running softmax per query row: each warp's partial row maxima and sums
+//      go through shared memory so the two warps of a row agree; P (hi/lo fp16)
+//      goes to shared memory;
+//   4. warp w accumulates P V for rows 16 (w % 4) .. and dimensions 128 (w / 4)
+//      .. + 127 (16 n-tiles, 4 k-steps of 16 keys, 3 MMAs each), after scaling
+//      its accumulators by the rows' softmax correction.
+// Then O / l times the sigmoid gate, into out_f.  Query tiles run latest-first.
 constexpr int kPfQueries = 64, kPfKeys = 64;
-constexpr int kPfLd = kAttnDim + 4;  // padded Q / K row: 16-byte bank shift per row
-constexpr int kPfPLd = kPfKeys + 4;
-// shared memory of attn_prefill_kernel: Q [64][260], K [64][260], V [64][256],
-// P [64][68], correction [64], sum [64]
-constexpr size_t kPfSmem =
-    (static_cast<size_t>(kPfQueries) * kPfLd + static_cast<size_t>(kPfKeys) * kPfLd +
-     static_cast<size_t>(kPfKeys) * kAttnDim + static_cast<size_t>(kPfQueries) * kPfPLd + 2 * kPfQueries) *
-    sizeof(float);
+constexpr int kPfRow = kAttnDim + 8;  // halves per padded Q / K / V row (528 bytes)
+constexpr int kPfPRow = kPfKeys + 8;  // halves per padded P row (144 bytes)
+constexpr size_t kPfTile = static_cast<size_t>(64) * kPfRow * 2;  // bytes of one hi or lo tile
+constexpr size_t kPfSmem = 6 * kPfTile + 2 * static_cast<size_t>(kPfQueries) * kPfPRow * 2 +
+                           4 * static_cast<size_t>(kPfQueries) * sizeof(float);
+constexpr float kPfVScale = 0.0625f;  // 2^-4
+
+__device__ __forceinline__ void split_half(float x, __half &hi, __half &lo)
+{
+    hi = __float2half_rn(x);
+    lo = __float2half_rn(__fsub_rn(x, __half2float(hi)));
+}
+
+// Store 4 fp32 values split into the hi and lo rows at half offset `o`.
+__device__ __forceinline__ void store_split4(__half *hi, __half *lo, int o, float4 v, float scale)
+{
+    __half h[4], l[4];
+    split_half(__fmul_rn(v.x, scale), h[0], l[0]);
+    split_half(__fmul_rn(v.y, scale), h[1], l[1]);
+    split_half(__fmul_rn(v.z, scale), h[2], l[2]);
+    split_half(__fmul_rn(v.w, scale), h[3], l[3]);
+    *reinterpret_cast<uint2 *>(hi + o) = *reinterpret_cast<const uint2 *>(h);
+    *reinterpret_cast<uint2 *>(lo + o) = *reinterpret_cast<const uint2 *>(l);
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4])
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4])
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+// D (16 x 8 fp32) += A (16 x 16 fp16, row) x B (16 x 8 fp16, col)
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+                 "{%8, %9}, {%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
 
 __global__ void __launch_bounds__(256, 1) attn_prefill_kernel(AttnPrefillArgs a)
 {
-    extern __shared__ __align__(16) float pf_smem[];
-    float *qs = pf_smem;                          // [64][kPfLd]
-    float *ks = qs + kPfQueries * kPfLd;          // [64][kPfLd]
-    float *vs = ks + kPfKeys * kPfLd;             // [64][256]
-    float *ps = vs + kPfKeys * kAttnDim;          // [64][kPfPLd]
-    float *corr = ps + kPfQueries * kPfPLd;       // [64]
-    float *lsum = corr + kPfQueries;              // [64]
+    extern __shared__ __align__(128) uint8_t pf_raw[];
+    __half *qh = reinterpret_cast<__half *>(pf_raw);
+    __half *ql = qh + 64 * kPfRow;
+    __half *kh = ql + 64 * kPfRow;
+    __half *kl = kh + 64 * kPfRow;
+    __half *vh = kl + 64 * kPfRow;
+    __half *vl = vh + 64 * kPfRow;
+    __half *ph = vl + 64 * kPfRow;
+    __half *pl = ph + kPfQueries * kPfPRow;
+    float *rmax = reinterpret_cast<float *>(pl + kPfQueries * kPfPRow);  // [2][64] partial row maxima
+    float *rsum = rmax + 2 * kPfQueries;                                  // [2][64] partial row sums
     pdl_wait();
     const int tiles = (a.tokens + kPfQueries - 1) / kPfQueries;
     const int h = blockIdx.y, t0 = (tiles - 1 - static_cast<int>(blockIdx.x)) * kPfQueries;
-    const int tid = threadIdx.x, kg = tid & 15, qg = tid >> 4;
-    const int g = (a.head0 + h) / (kAttnHeads / 4) - a.kv0;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, tq = lane & 3;
+    const int rb = (warp & 3) * 16, half_sel = warp >> 2;  // row block; key half (scores) / dim half (P V)
+    const int kvh = (a.head0 + h) / (kAttnHeads / 4) - a.kv0;
     const int last = a.base + min(t0 + kPfQueries - 1, a.tokens - 1);
-    for (int i = tid; i < kPfQueries * kAttnDim / 4; i += blockDim.x) {
-        const int r = i / (kAttnDim / 4), c4 = i % (kAttnDim / 4);
-        const int t = min(t0 + r, a.tokens - 1);
-        *reinterpret_cast<float4 *>(qs + r * kPfLd + c4 * 4) =
-            *reinterpret_cast<const float4 *>(a.qbuf + (static_cast<size_t>(t) * a.heads + h) * kAttnDim + c4 * 4);
+    // the query tile, split (8 loads in flight per thread)
+    for (int i0 = tid; i0 < kPfQueries * kAttnDim / 4; i0 += 8 * 256) {
+        float4 q[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = i0 + u * 256, r = i / (kAttnDim / 4), c4 = i % (kAttnDim / 4);
+            const int t = min(t0 + r, a.tokens - 1);
+            q[u] = *reinterpret_cast<const float4 *>(a.qbuf + (static_cast<size_t>(t) * a.heads + h) * kAttnDim +
+                                                     c4 * 4);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = i0 + u * 256, r = i / (kAttnDim / 4), c4 = i % (kAttnDim / 4);
+            store_split4(qh, ql, r * kPfRow + c4 * 4, q[u], 1.0f);
+        }
     }
-    // running softmax of row srow (keys 16 spart .. + 15 of each tile)
-    const int srow = tid >> 2, spart = tid & 3;
-    const int spos = a.base + min(t0 + srow, a.tokens - 1);
-    float m_run = -INFINITY, l_run = 0.0f;
-    float acc[4][16];
+    // this lane's two query rows (g and g + 8 of the row block) and their positions
+    const int row0 = rb + g, row1 = rb + g + 8;
+    const int pos0 = a.base + min(t0 + row0, a.tokens - 1), pos1 = a.base + min(t0 + row1, a.tokens - 1);
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // running max / sum (l: warps of half 0)
+    float o[16][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int j = 0; j < 16; ++j)
 #pragma unroll
-        for (int e = 0; e < 16; ++e) acc[i][e] = 0.0f;
+        for (int e = 0; e < 4; ++e) o[j][e] = 0.0f;
+    const uint32_t s_qh = smem_addr(qh), s_ql = smem_addr(ql), s_kh = smem_addr(kh), s_kl = smem_addr(kl);
+    const uint32_t s_vh = smem_addr(vh), s_vl = smem_addr(vl), s_ph = smem_addr(ph), s_pl = smem_addr(pl);
     for (int p0 = 0; p0 <= last; p0 += kPfKeys) {
-        __syncthreads();  // the previous tile is consumed (and qs is written)
-        for (int i = tid; i < kPfKeys * kAttnDim / 4; i += blockDim.x) {
-            const int key = i / (kAttnDim / 4), d4 = i % (kAttnDim / 4);
-            const int p = min(p0 + key, last);  // past `last`: a valid row, masked below
-            const size_t off = static_cast<size_t>(p) * a.kv_ld + g * kAttnDim + d4 * 4;
-            *reinterpret_cast<float4 *>(ks + key * kPfLd + d4 * 4) = kv_load4(a.k_cache, off, a.kv_half);
-            *reinterpret_cast<float4 *>(vs + key * kAttnDim + d4 * 4) = kv_load4(a.v_cache, off, a.kv_half);
-        }
-        __syncthreads();
-        // scores of queries qg + 16i against keys kg + 16j (dimensions in order)
-        float sc[4][4];
+        __syncthreads();  // the previous tile's K, V and P are consumed (and Q is written)
+        // 8 K and 8 V loads in flight per thread before any is converted
+        for (int i0 = tid; i0 < kPfKeys * kAttnDim / 4; i0 += 8 * 256) {
+            float4 kq[8], vq[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+            for (int u = 0; u < 8; ++u) {
+                const int i = i0 + u * 256, key = i / (kAttnDim / 4), d4 = i % (kAttnDim / 4);
+                const int p = min(p0 + key, last);  // past `last`: a valid row, masked below
+                const size_t off = static_cast<size_t>(p) * a.kv_ld + kvh * kAttnDim + d4 * 4;
+                kq[u] = kv_load4(a.k_cache, off, a.kv_half);
+                vq[u] = kv_load4(a.v_cache, off, a.kv_half);
+            }
 #pragma unroll
-            for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
-#pragma unroll 2
-        for (int d = 0; d < kAttnDim; d += 4) {
-            float4 qv[4], kv[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4 *>(qs + (qg + 16 * i) * kPfLd + d);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4 *>(ks + (kg + 16 * j) * kPfLd + d);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    float x = sc[i][j];
-                    x = fmaf(qv[i].x, kv[j].x, x);
-                    x = fmaf(qv[i].y, kv[j].y, x);
-                    x = fmaf(qv[i].z, kv[j].z, x);
-                    sc[i][j] = fmaf(qv[i].w, kv[j].w, x);
-                }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) ps[(qg + 16 * i) * kPfPLd + kg + 16 * j] = __fmul_rn(sc[i][j], 0.0625f);
-        __syncthreads();
-        // the running softmax of row srow over this tile
-        float s16[16], mx = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            const int key = spart * 16 + k;
-            s16[k] = p0 + key <= spos ? ps[srow * kPfPLd + key] : -INFINITY;
-            mx = fmaxf(mx, s16[k]);
-        }
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float m_new = fmaxf(m_run, mx);
-        const float c = m_run == -INFINITY ? 0.0f : expf(__fsub_rn(m_run, m_new));
-        float wsum = 0.0f;
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            const float w = s16[k] == -INFINITY ? 0.0f : expf(__fsub_rn(s16[k], m_new));
-            ps[srow * kPfPLd + spart * 16 + k] = w;
-            wsum = __fadd_rn(wsum, w);
-        }
-        wsum = __fadd_rn(wsum, __shfl_xor_sync(0xffffffffu, wsum, 1));
-        wsum = __fadd_rn(wsum, __shfl_xor_sync(0xffffffffu, wsum, 2));
-        l_run = __fadd_rn(__fmul_rn(l_run, c), wsum);
-        m_run = m_new;
-        if (spart == 0) corr[srow] = c;
-        __syncthreads();
-        // weighted values: dimensions 4 kg + 64 j .. + 3 of queries qg + 16 i
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float ci = corr[qg + 16 * i];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) acc[i][e] = __fmul_rn(acc[i][e], ci);
-        }
-#pragma unroll 4
-        for (int k = 0; k < kPfKeys; ++k) {
-            float pw[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) pw[i] = ps[(qg + 16 * i) * kPfPLd + k];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float4 v = *reinterpret_cast<const float4 *>(vs + k * kAttnDim + kg * 4 + 64 * j);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    acc[i][4 * j + 0] = fmaf(pw[i], v.x, acc[i][4 * j + 0]);
-                    acc[i][4 * j + 1] = fmaf(pw[i], v.y, acc[i][4 * j + 1]);
-                    acc[i][4 * j + 2] = fmaf(pw[i], v.z, acc[i][4 * j + 2]);
-                    acc[i][4 * j + 3] = fmaf(pw[i], v.w, acc[i][4 * j + 3]);
-                }
+            for (int u = 0; u < 8; ++u) {
+                const int i = i0 + u * 256, key = i / (kAttnDim / 4), d4 = i % (kAttnDim / 4);
+                store_split4(kh, kl, key * kPfRow + d4 * 4, kq[u], 1.0f);
+                store_split4(vh, vl, key * kPfRow + d4 * 4, vq[u], kPfVScale);
             }
         }
-    }
-    if (spart == 0) lsum[srow] = l_run;
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int t = t0 + qg + 16 * i;
-        if (t >= a.tokens) continue;
-        const float l = lsum[qg + 16 * i];
-        const float *gate = a.qkv + static_cast<size_t>(t) * a.qkv_ld + h * 512 + kAttnDim;
-        float *dst = a.out_f + static_cast<size_t>(t) * a.out_ld + h * kAttnDim;
+        __syncthreads();
+        // 2. scores of rows rb .. rb + 15 against keys 32 half_sel .. + 31
+        float sc[4][4];
 #pragma unroll
         for (int j = 0; j < 4; ++j)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int d = kg * 4 + 64 * j + e;
-                dst[d] = __fmul_rn(__fdiv_rn(acc[i][4 * j + e], l), sigmoid(gate[d]));
+            for (int e = 0; e < 4; ++e) sc[j][e] = 0.0f;
+        const uint32_t a_off = static_cast<uint32_t>(((rb + (lane & 15)) * kPfRow + (lane >> 4) * 8) * 2);
+        const int key_l = 32 * half_sel + (lane & 7) + ((lane >> 4) << 3);
+        const uint32_t b_off = static_cast<uint32_t>((key_l * kPfRow + ((lane >> 3) & 1) * 8) * 2);
+#pragma unroll 4
+        for (int kk = 0; kk < kAttnDim / 16; ++kk) {
+            uint32_t ah[4], al[4];
+            ldsm_x4(s_qh + a_off + kk * 32, ah);
+            ldsm_x4(s_ql + a_off + kk * 32, al);
+#pragma unroll
+            for (int jp = 0; jp < 2; ++jp) {  // n-tile pairs (16 keys)
+                uint32_t bh[4], bl[4];
+                const uint32_t o2 = b_off + jp * 16 * kPfRow * 2 + kk * 32;
+                ldsm_x4(s_kh + o2, bh);
+                ldsm_x4(s_kl + o2, bl);
+                mma16816(sc[2 * jp], ah, bh[0], bh[1]);
+                mma16816(sc[2 * jp], ah, bl[0], bl[1]);
+                mma16816(sc[2 * jp], al, bh[0], bh[1]);
+                mma16816(sc[2 * jp + 1], ah, bh[2], bh[3]);
+                mma16816(sc[2 * jp + 1], ah, bl[2], bl[3]);
+                mma16816(sc[2 * jp + 1], al, bh[2], bh[3]);
             }
+        }
+        // 3. running softmax: mask, scale, partial maxima of this warp's 32 keys
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int kp = p0 + 32 * half_sel + 8 * j + 2 * tq;  // position of column c0 / c2
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                sc[j][e] = kp + e <= pos0 ? __fmul_rn(sc[j][e], 0.0625f) : -INFINITY;
+                sc[j][2 + e] = kp + e <= pos1 ? __fmul_rn(sc[j][2 + e], 0.0625f) : -INFINITY;
+                mx0 = fmaxf(mx0, sc[j][e]);
+                mx1 = fmaxf(mx1, sc[j][2 + e]);
+            }
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        if (tq == 0) {
+            rmax[half_sel * kPfQueries + row0] = mx0;
+            rmax[half_sel * kPfQueries + row1] = mx1;
+        }
+        __syncthreads();
+        const float n0 = fmaxf(m0, fmaxf(rmax[row0], rmax[kPfQueries + row0]));
+        const float n1 = fmaxf(m1, fmaxf(rmax[row1], rmax[kPfQueries + row1]));
+        const float c0 = m0 == -INFINITY ? 0.0f : expf(__fsub_rn(m0, n0));
+        const float c1 = m1 == -INFINITY ? 0.0f : expf(__fsub_rn(m1, n1));
+        float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float w[4];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                w[e] = sc[j][e] == -INFINITY ? 0.0f : expf(__fsub_rn(sc[j][e], n0));
+                w[2 + e] = sc[j][2 + e] == -INFINITY ? 0.0f : expf(__fsub_rn(sc[j][2 + e], n1));
+            }
+            s0 = __fadd_rn(s0, __fadd_rn(w[0], w[1]));
+            s1 = __fadd_rn(s1, __fadd_rn(w[2], w[3]));
+            const int col = 32 * half_sel + 8 * j + 2 * tq;
+            __half hh[2], hl[2];
+            split_half(w[0], hh[0], hl[0]);
+            split_half(w[1], hh[1], hl[1]);
+            *reinterpret_cast<__half2 *>(ph + row0 * kPfPRow + col) = __halves2half2(hh[0], hh[1]);
+            *reinterpret_cast<__half2 *>(pl + row0 * kPfPRow + col) = __halves2half2(hl[0], hl[1]);
+            split_half(w[2], hh[0], hl[0]);
+            split_half(w[3], hh[1], hl[1]);
+            *reinterpret_cast<__half2 *>(ph + row1 * kPfPRow + col) = __halves2half2(hh[0], hh[1]);
+            *reinterpret_cast<__half2 *>(pl + row1 * kPfPRow + col) = __halves2half2(hl[0], hl[1]);
+        }
+        s0 = __fadd_rn(s0, __shfl_xor_sync(0xffffffffu, s0, 1));
+        s0 = __fadd_rn(s0, __shfl_xor_sync(0xffffffffu, s0, 2));
+        s1 = __fadd_rn(s1, __shfl_xor_sync(0xffffffffu, s1, 1));
+        s1 = __fadd_rn(s1, __shfl_xor_sync(0xffffffffu, s1, 2));
+        if (tq == 0) {
+            rsum[half_sel * kPfQueries + row0] = s0;
+            rsum[half_sel * kPfQueries + row1] = s1;
+        }
+        m0 = n0;
+        m1 = n1;
+        __syncthreads();  // P and the partial sums are complete
+        l0 = __fadd_rn(__fmul_rn(l0, c0), __fadd_rn(rsum[row0], rsum[kPfQueries + row0]));
+        l1 = __fadd_rn(__fmul_rn(l1, c1), __fadd_rn(rsum[row1], rsum[kPfQueries + row1]));
+        // 4. O = O c + P V for rows rb .., dimensions 128 half_sel ..
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            o[j][0] = __fmul_rn(o[j][0], c0);
+            o[j][1] = __fmul_rn(o[j][1], c0);
+            o[j][2] = __fmul_rn(o[j][2], c1);
+            o[j][3] = __fmul_rn(o[j][3], c1);
+        }
+        const uint32_t pa_off = static_cast<uint32_t>(((rb + (lane & 15)) * kPfPRow + (lane >> 4) * 8) * 2);
+        const int vkey = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const uint32_t vb_off = static_cast<uint32_t>((vkey * kPfRow + 128 * half_sel + (lane >> 4) * 8) * 2);
+#pragma unroll
+        for (int ks = 0; ks < kPfKeys / 16; ++ks) {
+            uint32_t ah[4], al[4];
+            ldsm_x4(s_ph + pa_off + ks * 32, ah);
+            ldsm_x4(s_pl + pa_off + ks * 32, al);
+#pragma unroll
+            for (int jp = 0; jp < 8; ++jp) {  // n-tile pairs (16 dimensions)
+                uint32_t bh[4], bl[4];
+                const uint32_t o2 = vb_off + (ks * 16 * kPfRow + jp * 16) * 2;
+                ldsm_x4_trans(s_vh + o2, bh);
+                ldsm_x4_trans(s_vl + o2, bl);
+                mma16816(o[2 * jp], ah, bh[0], bh[1]);
+                mma16816(o[2 * jp], ah, bl[0], bl[1]);
+                mma16816(o[2 * jp], al, bh[0], bh[1]);
+                mma16816(o[2 * jp + 1], ah, bh[2], bh[3]);
+                mma16816(o[2 * jp + 1], ah, bl[2], bl[3]);
+                mma16816(o[2 * jp + 1], al, bh[2], bh[3]);
+            }
+        }
+    }
+    // O / l times the sigmoid gate (qwen38_model.c:870-878), V's 2^4 restored
+    const float inv0 = __fdiv_rn(1.0f / kPfVScale, l0), inv1 = __fdiv_rn(1.0f / kPfVScale, l1);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int t = t0 + (r ? row1 : row0);
+        if (t >= a.tokens) continue;
+        const float inv = r ? inv1 : inv0;
+        const float *gate = a.qkv + static_cast<size_t>(t) * a.qkv_ld + h * 512 + kAttnDim;
+        float *dst = a.out_f + static_cast<size_t>(t) * a.out_ld + h * kAttnDim;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int d = 128 * half_sel + 8 * j + 2 * tq;
+#pragma unroll
+            for (int e = 0; e < 2; ++e)
+                dst[d + e] = __fmul_rn(__fmul_rn(o[j][2 * r + e], inv), sigmoid(gate[d + e]));
+        }
     }
     pdl_launch_dependents();
 }

@@ -703,16 +703,17 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
 //     v channel, the L2 norms of q and k, beta and the decay - written as
 //     records laid out for the serial kernel's bulk copies:
 //       qk  [key head][token][260]    q (128), k (128), normalized; q.k; 3 pad
-//       v   [value head][4][token][32] the 128 v channels, 32 per column block
+//       v   [value head][8][token][16] the 128 v channels, 16 per column block
 //       gb  [value head][token][2]    beta, decay
 //     (token stride rec_tokens, a multiple of kDeltaChunk).
 //  2. deltanet_prefill_kernel (serial in tokens): each warp owns 8 columns of
 //     one value head's state; lane l holds rows 32 (l / 8) .. + 31 of column
 //     l % 8, in registers for the whole chunk, so a column's dot products
-//     reduce over 4 lanes (2 shuffle levels).  A CTA's 4 warps share the
-//     records of one column block, streamed into a ring of shared-memory
-//     stages by cp.async.bulk kDeltaChunk tokens at a time, so the token loop
-//     reads only shared memory.  It stores the raw head output (before the
+//     reduce over 4 lanes (2 shuffle levels).  A CTA's 2 warps share the
+//     records of one 16-column block (384 CTAs: small enough that every SM
+//     gets two or three), streamed into a ring of shared-memory stages by
+//     cp.async.bulk kDeltaChunk tokens at a time, so the token loop reads only
+//     shared memory.  It stores the raw head output (before the
 //     RMSNorm).  With a = k.S and b = q.S of the state before the token, the
 //     upstream's
 //       S <- decay S;  kv = k.S;  delta = (v - kv) beta;  S <- S + k delta;
@@ -724,9 +725,10 @@ __global__ void __cluster_dims__(kDeltaCluster, 1, 1) __launch_bounds__(128)
 //  4. deltanet_ring_store_kernel: the conv ring, once every reader is done.
 // ---------------------------------------------------------------------------
 constexpr int kDeltaChunk = 32;   // tokens per bulk-copy stage
-constexpr int kDeltaStages = 3;
+constexpr int kDeltaStages = 2;
+constexpr int kDeltaCols = 16;    // state columns per CTA (2 warps of 8)
 constexpr int kDeltaQkLd = 260;  // floats per token of the q|k record
-constexpr uint32_t kDeltaQkBytes = kDeltaChunk * kDeltaQkLd * 4, kDeltaVBytes = kDeltaChunk * 32 * 4,
+constexpr uint32_t kDeltaQkBytes = kDeltaChunk * kDeltaQkLd * 4, kDeltaVBytes = kDeltaChunk * kDeltaCols * 4,
                    kDeltaGbBytes = kDeltaChunk * 2 * 4;
 constexpr uint32_t kDeltaStageBytes = kDeltaQkBytes + kDeltaVBytes + kDeltaGbBytes;
 constexpr size_t kDeltaSmem = static_cast<size_t>(kDeltaStages) * kDeltaStageBytes + 64;
@@ -792,8 +794,8 @@ __global__ void __launch_bounds__(256) deltanet_prefill_prep_kernel(DeltaPrefill
 #pragma unroll
             for (int i = 0; i < 4; ++i)
                 v[i] = prefill_conv(a, ch + i, p, __ldg(reinterpret_cast<const float4 *>(a.conv_w) + ch + i));
-            // channel 4l + i sits in column block l / 8, slot 4 (l % 8) + i
-            float *dst = rec_v + ((static_cast<size_t>(vh) * 4 + lane / 8) * rt + t) * 32 + (lane % 8) * 4;
+            // channel 4l + i sits in column block l / 4, slot 4 (l % 4) + i
+            float *dst = rec_v + ((static_cast<size_t>(vh) * 8 + lane / 4) * rt + t) * kDeltaCols + (lane % 4) * 4;
             *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
             if (lane == 0) {
                 // beta and the decay (qwen38_model.c:748-752)
@@ -809,22 +811,22 @@ __global__ void __launch_bounds__(256) deltanet_prefill_prep_kernel(DeltaPrefill
     pdl_launch_dependents();
 }
 
-// The serial recurrence.  Grid: value heads x 4 column blocks, 128 threads;
+// The serial recurrence.  Grid: value heads x 8 column blocks, 64 threads;
 // thread 0 also issues the stage copies.  A stage holds kDeltaChunk tokens:
-// [token][256] q|k of the head's key head, [token][32] v of the column block,
-// [token][2] beta, decay.
-__global__ void __launch_bounds__(128) deltanet_prefill_kernel(DeltaPrefillArgs a)
+// [token][260] q|k|q.k of the head's key head, [token][16] v of the column
+// block, [token][2] beta, decay.
+__global__ void __launch_bounds__(64) deltanet_prefill_kernel(DeltaPrefillArgs a)
 {
     extern __shared__ __align__(128) uint8_t dsm[];
     uint64_t *full = reinterpret_cast<uint64_t *>(dsm + static_cast<size_t>(kDeltaStages) * kDeltaStageBytes);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int n_kh = a.n_kh > 0 ? a.n_kh : 16, n_vh = 3 * n_kh;
-    const int vh = blockIdx.x >> 2, cb = blockIdx.x & 3, col0 = cb * 32 + warp * 8;
+    const int vh = blockIdx.x >> 3, cb = blockIdx.x & 7, col0 = cb * kDeltaCols + warp * 8;
     const int kh = vh % n_kh;
     const size_t rt = static_cast<size_t>(a.rec_tokens);
     const float *rec_qk = a.rec + static_cast<size_t>(kh) * rt * kDeltaQkLd;
-    const float *rec_v =
-        a.rec + static_cast<size_t>(n_kh) * rt * kDeltaQkLd + (static_cast<size_t>(vh) * 4 + cb) * rt * 32;
+    const float *rec_v = a.rec + static_cast<size_t>(n_kh) * rt * kDeltaQkLd +
+                         (static_cast<size_t>(vh) * 8 + cb) * rt * kDeltaCols;
     const float *rec_gb = a.rec + static_cast<size_t>(n_kh) * rt * kDeltaQkLd + static_cast<size_t>(n_vh) * rt * 128 +
                           static_cast<size_t>(vh) * rt * 2;
     const int chunks = (a.tokens + kDeltaChunk - 1) / kDeltaChunk;
@@ -847,7 +849,7 @@ __global__ void __launch_bounds__(128) deltanet_prefill_kernel(DeltaPrefillArgs 
         const size_t t0 = static_cast<size_t>(c) * kDeltaChunk;
         mbar_arrive_expect_tx(bar, kDeltaStageBytes);
         bulk_copy_g2s(st, rec_qk + t0 * kDeltaQkLd, kDeltaQkBytes, bar);
-        bulk_copy_g2s(st + kDeltaQkBytes, rec_v + t0 * 32, kDeltaVBytes, bar);
+        bulk_copy_g2s(st + kDeltaQkBytes, rec_v + t0 * kDeltaCols, kDeltaVBytes, bar);
         bulk_copy_g2s(st + kDeltaQkBytes + kDeltaVBytes, rec_gb + t0 * 2, kDeltaGbBytes, bar);
     };
     if (threadIdx.x == 0)
@@ -872,7 +874,7 @@ __global__ void __launch_bounds__(128) deltanet_prefill_kernel(DeltaPrefillArgs 
             const float4 *q4 = reinterpret_cast<const float4 *>(rq + rg * 32);
             const float4 *k4 = reinterpret_cast<const float4 *>(rq + 128 + rg * 32);
             const float qk = rq[256];
-            const float vj = sv[i * 32 + warp * 8 + jc];
+            const float vj = sv[i * kDeltaCols + warp * 8 + jc];
             const float2 gb = reinterpret_cast<const float2 *>(sgb)[i];
             const float beta = gb.x, decay = gb.y;
             // k.S and q.S of the state before this token: the lane's 32 rows
@@ -1777,8 +1779,8 @@ cudaError_t launch_deltanet_prefill(const DeltaPrefillArgs &args, cudaStream_t s
     cudaError_t e = launch_pdl(deltanet_prefill_prep_kernel, dim3(args.tokens), dim3(256), s, args);
     if (e == cudaSuccess) {
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(n_vh * 4);
-        cfg.blockDim = dim3(128);
+        cfg.gridDim = dim3(n_vh * (128 / kDeltaCols));
+        cfg.blockDim = dim3(64);
         cfg.dynamicSmemBytes = kDeltaSmem;
         cfg.stream = s;
         cudaLaunchAttribute pdl[1];

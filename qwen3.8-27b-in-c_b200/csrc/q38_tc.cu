@@ -345,22 +345,40 @@ __device__ __forceinline__ uint32_t ld_u16(const uint8_t *p) { return p[0] | (p[
 // Weights 8 l .. 8 l + 7 of one superblock (lane l of a warp), dequantized
 // with the upstream float formula of the type (qwen38_quant.c:330-508):
 // Q4_K w = (d sc) q - dmin m per 32-weight sub-block, Q6_K w = (d sc) q.
-__device__ __forceinline__ void q4k_eight(const uint8_t *b, int lane, float (&w)[8])
+// The block's 16-byte header (d, dmin, 12 scale bytes) and this lane's 8
+// quant bytes, as two loads (Q4_K blocks of 144 bytes start on 16-byte
+// boundaries in either layout).
+struct Q4KLane {
+    uint4 hdr;
+    uint2 q;
+};
+
+__device__ __forceinline__ Q4KLane q4k_load(const uint8_t *b, int lane)
 {
-    const int grp = lane >> 2, chunk = lane >> 3, hi = grp & 1;
+    Q4KLane r;
+    r.hdr = *reinterpret_cast<const uint4 *>(b);
+    r.q = *reinterpret_cast<const uint2 *>(b + 16 + (lane >> 3) * 32 + (lane & 3) * 8);
+    return r;
+}
+
+__device__ __forceinline__ void q4k_eight(const Q4KLane &in, int lane, float (&w)[8])
+{
+    const int grp = lane >> 2, hi = grp & 1;
+    auto byte = [&](int k) -> int {  // header byte k (selects, no indexed array)
+        const uint32_t wd = k < 4 ? in.hdr.x : k < 8 ? in.hdr.y : k < 12 ? in.hdr.z : in.hdr.w;
+        return static_cast<int>((wd >> (8 * (k & 3))) & 0xFFu);
+    };
     int sc, m;
-    const uint8_t *p = b + 4;
-    if (grp < 4) {
-        sc = p[grp] & 63;
-        m = p[grp + 4] & 63;
+    if (grp < 4) {  // header bytes 4 + i are the scale bytes p[i]
+        sc = byte(4 + grp) & 63;
+        m = byte(8 + grp) & 63;
     } else {
-        sc = (p[grp + 4] & 15) | ((p[grp - 4] >> 6) << 4);
-        m = (p[grp + 4] >> 4) | ((p[grp] >> 6) << 4);
+        sc = (byte(8 + grp) & 15) | ((byte(grp) >> 6) << 4);
+        m = (byte(8 + grp) >> 4) | ((byte(4 + grp) >> 6) << 4);
     }
-    const float d = f16_bits_to_f32(ld_u16(b)), dmin = f16_bits_to_f32(ld_u16(b + 2));
+    const float d = f16_bits_to_f32(in.hdr.x & 0xFFFFu), dmin = f16_bits_to_f32(in.hdr.x >> 16);
     const float ds = __fmul_rn(d, static_cast<float>(sc)), dm = __fmul_rn(dmin, static_cast<float>(m));
-    // 8 quant bytes, 8-byte aligned (blocks of 144 bytes start on 16-byte boundaries)
-    const uint2 q = *reinterpret_cast<const uint2 *>(b + 16 + chunk * 32 + (lane & 3) * 8);
+    const uint2 q = in.q;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
         const uint32_t byte = ((e < 4 ? q.x : q.y) >> (8 * (e & 3))) & 0xFFu;
@@ -428,40 +446,58 @@ __device__ __forceinline__ void split2(float a, float b, __half2 &hi, __half2 &l
 }
 
 // Weights -> fp16 hi [rows][width] and lo (rows * width further), times
-// 1 / row_scale.  One warp per (row, superblock): lane l forms weights
-// 8 l .. 8 l + 7 and stores them as one 16-byte vector of each half, so a
-// warp writes 512 contiguous bytes of hi and of lo.  Rows are read in the
-// tiled layout when tile_rows != 0.  With `split`, the rows come
+// 1 / row_scale.  One warp per (row, NB consecutive superblocks): lane l forms
+// weights 8 l .. 8 l + 7 of each and stores them as one 16-byte vector of each
+// half, so a warp writes 512 contiguous bytes of hi and of lo per superblock;
+// the blocks' loads are all issued before any is decoded.  Rows are read in
+// the tiled layout when tile_rows != 0.  With `split`, the rows come
 // interleaved in pairs (gate i, up i) and are written as [gate rows | up
 // rows] (row_scale is indexed by the written row).
+template <int NB>
 __global__ void __launch_bounds__(256) dequant_f16_kernel(const uint8_t *w, int type, uint64_t rows, uint64_t width,
                                                           uint32_t tile_rows, int bb, __half *out,
                                                           const float *row_scale, int split)
 {
     pdl_wait();
-    const uint64_t nb = width / 256;
+    const uint64_t nb = width / 256, per_row = nb / NB;
     const uint64_t gw = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    if (gw < rows * nb) {
-        const uint64_t row = gw / nb, blk = gw - row * nb;
-        const uint8_t *b;
-        if (tile_rows) {
-            const uint64_t t = row / tile_rows, r = row - t * tile_rows;
-            b = w + ((t * nb + blk) * tile_rows + r) * bb;
-        } else {
-            b = w + (row * nb + blk) * bb;
+    if (gw < rows * per_row) {
+        const uint64_t row = gw / per_row, blk0 = (gw - row * per_row) * NB;
+        const uint8_t *b[NB];
+#pragma unroll
+        for (int k = 0; k < NB; ++k) {
+            const uint64_t blk = blk0 + k;
+            if (tile_rows) {
+                const uint64_t t = row / tile_rows, r = row - t * tile_rows;
+                b[k] = w + ((t * nb + blk) * tile_rows + r) * bb;
+            } else {
+                b[k] = w + (row * nb + blk) * bb;
+            }
         }
-        float v[8];
-        if (type == 12) q4k_eight(b, lane, v);
-        else q6k_eight(b, lane, v);
+        float v[NB][8];
+        if (type == 12) {
+            Q4KLane in[NB];
+#pragma unroll
+            for (int k = 0; k < NB; ++k) in[k] = q4k_load(b[k], lane);
+#pragma unroll
+            for (int k = 0; k < NB; ++k) q4k_eight(in[k], lane, v[k]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < NB; ++k) q6k_eight(b[k], lane, v[k]);
+        }
         const uint64_t orow = split ? ((row & 1) ? rows / 2 + row / 2 : row / 2) : row;
         const float inv = __frcp_rn(__ldg(row_scale + orow));  // a power of two: exact
-        __half2 hi[4], lo[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) split2(__fmul_rn(v[2 * e], inv), __fmul_rn(v[2 * e + 1], inv), hi[e], lo[e]);
-        const size_t o = orow * width + blk * 256 + lane * 8;
-        *reinterpret_cast<uint4 *>(out + o) = *reinterpret_cast<const uint4 *>(hi);
-        *reinterpret_cast<uint4 *>(out + rows * width + o) = *reinterpret_cast<const uint4 *>(lo);
+        for (int k = 0; k < NB; ++k) {
+            __half2 hi[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                split2(__fmul_rn(v[k][2 * e], inv), __fmul_rn(v[k][2 * e + 1], inv), hi[e], lo[e]);
+            const size_t o = orow * width + (blk0 + k) * 256 + lane * 8;
+            *reinterpret_cast<uint4 *>(out + o) = *reinterpret_cast<const uint4 *>(hi);
+            *reinterpret_cast<uint4 *>(out + rows * width + o) = *reinterpret_cast<const uint4 *>(lo);
+        }
     }
     pdl_launch_dependents();
 }
@@ -584,7 +620,8 @@ cudaError_t launch_dequant_f16(const void *w, int type, uint64_t rows, uint64_t 
                                                  width / 256, tile_rows, bb, row_scale, split);
         if (e != cudaSuccess) return e;
     }
-    const uint64_t warps = rows * (width / 256);
+    const bool four = (width / 256) % 4 == 0;  // four superblocks a warp where they divide the row
+    const uint64_t warps = rows * (width / 256) / (four ? 4 : 1);
     const unsigned grid = static_cast<unsigned>((warps * 32 + 255) / 256);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -595,7 +632,8 @@ cudaError_t launch_dequant_f16(const void *w, int type, uint64_t rows, uint64_t 
     la[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = la;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, dequant_f16_kernel, static_cast<const uint8_t *>(w), type, rows, width, tile_rows,
+    return cudaLaunchKernelEx(&cfg, four ? dequant_f16_kernel<4> : dequant_f16_kernel<1>,
+                              static_cast<const uint8_t *>(w), type, rows, width, tile_rows,
                               bb, static_cast<__half *>(out), static_cast<const float *>(row_scale), split);
 }
 

@@ -315,6 +315,7 @@ struct Q38Model {
     int pf_cap = 0;
     float *pf_hidden = nullptr, *pf_normf = nullptr, *pf_wide = nullptr, *pf_act = nullptr, *pf_ba = nullptr;
     float *pf_scale = nullptr, *pf_row_scale = nullptr, *pf_oraw = nullptr, *pf_rec = nullptr;
+    float *pf_part = nullptr;  // tensor parallel: a row-parallel projection's partial sums [cap][kHidden]
     void *pf_q8 = nullptr, *pf_q8mix = nullptr, *pf_a16 = nullptr, *pf_b16 = nullptr;
     uint32_t *pf_ids = nullptr, *host_pf_ids = nullptr;
     std::vector<void *> pf_owned;
@@ -1749,7 +1750,8 @@ bool ensure_prefill_buffers(Q38Model *m, int cap)
               pf_alloc(m, reinterpret_cast<uint16_t **>(&m->pf_b16), 2 * n * kFfn) &&
               pf_alloc(m, &m->pf_row_scale, static_cast<size_t>(m->wide_ld)) && pf_alloc(m, &m->pf_ids, n) &&
               pf_alloc(m, &m->pf_oraw, n * kLinV) &&
-              pf_alloc(m, &m->pf_rec, q38::delta_prefill_rec_floats(m->lin_heads / 3, (cap + 31) / 32 * 32));
+              pf_alloc(m, &m->pf_rec, q38::delta_prefill_rec_floats(m->lin_heads / 3, (cap + 31) / 32 * 32)) &&
+              (m->shard.world == 1 || pf_alloc(m, &m->pf_part, n * kHidden));
     if (ok && m->host_pf_ids) {
         cudaFreeHost(m->host_pf_ids);
         m->host_pf_ids = nullptr;
@@ -1813,9 +1815,22 @@ bool tc_project(Q38Model *m, const Proj &p, const void *q8, const float *xf, int
 }
 
 // One layer over the n tokens of the chunk at positions base .. base + n - 1.
+// Tensor parallel: the row-parallel projection's partial sums (in pf_part)
+// added up across the GPUs (NCCL all-reduce) and into the hidden rows.
+bool tc_reduce_into_hidden(Q38Model *m, int n)
+{
+    const NcclApi *api = nccl();
+    return nccl_ok(api->all_reduce(m->pf_part, m->pf_part, static_cast<size_t>(n) * kHidden, ncclFloat, ncclSum,
+                                   m->comm, m->stream),
+                   "prefill all-reduce") &&
+           cuda_ok(q38::launch_add(m->pf_hidden, m->pf_part, kHidden, n, m->stream), "residual add");
+}
+
 bool tc_layer(Q38Model *m, int l, int n, uint32_t base)
 {
     const Layer &L = m->layers[l];
+    const Shard &sh = m->shard;
+    const bool tp = sh.world > 1;
     const cudaStream_t s = m->stream;
     const int nb = kHidden / 256;
     Q38CuQ8KBlock *q8 = static_cast<Q38CuQ8KBlock *>(m->pf_q8);
@@ -1865,26 +1880,40 @@ bool tc_layer(Q38Model *m, int l, int n, uint32_t base)
         a.v_cache = m->v_cache + static_cast<size_t>(L.index) * m->context_length * m->kv_ld * m->kv_bytes;
         a.kv_half = m->kv_bytes == 2;
         a.kv_ld = m->kv_ld;
-        a.heads = 24;
+        a.heads = tp ? sh.heads : 24;
+        a.head0 = tp ? sh.head0 : 0;
+        a.kv0 = tp ? sh.kv0 : 0;
+        if (tp) {
+            a.k_off = sh.heads * 2 * kAttnDim;
+            a.v_off = a.k_off + sh.kv_heads * kAttnDim;
+        }
         a.theta_scale = m->theta_scale;
         a.base = static_cast<int>(base);
         a.tokens = n;
         a.qbuf = m->pf_oraw;
         a.out_f = m->pf_act;
-        a.out_ld = kAttnQ;
+        a.out_ld = a.heads * kAttnDim;
         a.out_q = mix;
         if (!cuda_ok(q38::launch_attention_prefill(a, s), "attention prefill")) return false;
     }
-    if (!tc_project(m, L.out, mix, m->pf_act, kLinV, n, m->pf_hidden, kHidden, 1, false)) return false;
+    const int mix_width = L.full ? (tp ? sh.heads * kAttnDim : kAttnQ) : (tp ? m->lin_heads * kLinDim : kLinV);
+    if (tp ? !tc_project(m, L.out, mix, m->pf_act, mix_width, n, m->pf_part, kHidden, 0, false) ||
+                 !tc_reduce_into_hidden(m, n)
+           : !tc_project(m, L.out, mix, m->pf_act, mix_width, n, m->pf_hidden, kHidden, 1, false))
+        return false;
+    const int ffn = tp ? sh.ffn : kFfn;
     if (!cuda_ok(q38::launch_rmsnorm_quant(m->pf_hidden, kHidden, L.post_norm, kHidden, n, m->pf_normf, kHidden, q8,
                                            s, nb),
                  "rmsnorm") ||
         !tc_project(m, L.gate_up, q8, m->pf_normf, kHidden, n, m->pf_wide, m->wide_ld, 0, L.swiglu_fused) ||
-        !cuda_ok(q38::launch_swiglu_quant(m->pf_wide, m->pf_wide + kFfn, m->wide_ld, kFfn, n,
+        !cuda_ok(q38::launch_swiglu_quant(m->pf_wide, m->pf_wide + ffn, m->wide_ld, ffn, n,
                                           has_float_part(L.down) ? m->pf_act : nullptr, q8, s),
                  "swiglu"))
         return false;
-    return tc_project(m, L.down, q8, m->pf_act, kFfn, n, m->pf_hidden, kHidden, 1, false);
+    if (tp)
+        return tc_project(m, L.down, q8, m->pf_act, ffn, n, m->pf_part, kHidden, 0, false) &&
+               tc_reduce_into_hidden(m, n);
+    return tc_project(m, L.down, q8, m->pf_act, ffn, n, m->pf_hidden, kHidden, 1, false);
 }
 
 bool tc_prefill_enabled()
@@ -1937,7 +1966,11 @@ bool prefill_tc(Q38Model *m, const uint32_t *tokens, uint32_t count)
             ok = cuda_ok(q38::launch_rmsnorm_quant(last, kHidden, m->output_norm, kHidden, 1, m->target_norm, kHidden,
                                                    m->q8, s),
                          "rmsnorm") &&
-                 project(m, m->output, q8_input(m->q8, m->target_norm, kHidden), 1, m->logits, kVocab, 0) &&
+                 (m->shard.world > 1
+                      ? project(m, m->output, q8_input(m->q8, m->target_norm, kHidden), 1, m->logits_local,
+                                m->shard.vocab, 0) &&
+                            gather_logits(m, 1)
+                      : project(m, m->output, q8_input(m->q8, m->target_norm, kHidden), 1, m->logits, kVocab, 0)) &&
                  cuda_ok(cudaMemcpyAsync(m->host_logits, m->logits, static_cast<size_t>(kVocab) * sizeof(float),
                                          cudaMemcpyDeviceToHost, s),
                          "logits copy");
@@ -2163,8 +2196,8 @@ int q38_model_prefill(Q38Model *m, const uint32_t *tokens, uint32_t token_count,
     for (uint32_t i = 0; i < token_count; ++i)
         if (tokens[i] >= kVocab) return 0;
     if (!use_device(m)) return 0;
-    if (token_count >= static_cast<uint32_t>(kTcPrefillMin) && !m->mtp_enabled && m->shard.world == 1 &&
-        tc_prefill_enabled() && tc_prefill_types(m)) {
+    if (token_count >= static_cast<uint32_t>(kTcPrefillMin) && !m->mtp_enabled && tc_prefill_enabled() &&
+        tc_prefill_types(m)) {
         if (!prefill_tc(m, tokens, token_count)) return 0;
         *logits = m->host_logits;
         return 1;

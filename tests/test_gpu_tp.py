@@ -18,6 +18,8 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 PROMPT = [5, 77, 1234, 99999, 31, 8, 248000, 4242]
+# long enough for the tensor-core prefill (every projection one GEMM over the prompt)
+LONG = np.random.default_rng(72).integers(0, 248320, 72).tolist()
 
 
 def _free_port():
@@ -48,8 +50,11 @@ def _rank_main(rank, world, port, path, out_dir, mode):
         step = m.forward_token(42)
         m.reset()
         greedy = m.generate_greedy(7, 12)
+        m.reset()
+        long = m.prefill(LONG)
+        long_step = m.forward_token(42)
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"), layer0=np.stack(layer0), prefill=prefill, step=step,
-                 greedy=np.array(greedy))
+                 greedy=np.array(greedy), long=long, long_step=long_step)
     finally:
         m.close()
         dist.destroy_process_group()
@@ -87,7 +92,7 @@ def test_tensor_parallel_matches_one_gpu(tmp_path, world, mode):
                        start_method="spawn")
     ranks = [np.load(os.path.join(tmp_path, f"rank{r}.npz")) for r in range(world)]
     r0 = ranks[0]
-    for key in ("layer0", "prefill", "step", "greedy"):
+    for key in ("layer0", "prefill", "step", "greedy", "long", "long_step"):
         for r in range(1, world):
             assert np.array_equal(r0[key], ranks[r][key]), f"ranks 0 and {r} disagree on {key}"
     one = Model(path, 128)
@@ -98,10 +103,15 @@ def test_tensor_parallel_matches_one_gpu(tmp_path, world, mode):
         step = one.forward_token(42)
         one.reset()
         greedy = one.generate_greedy(7, 12)
+        one.reset()
+        long = one.prefill(LONG)
+        long_step = one.forward_token(42)
     finally:
         one.close()
     assert max(rel(a, b) for a, b in zip(r0["layer0"], layer0)) <= 1e-3
-    for got, want in ((r0["prefill"], prefill), (r0["step"], step)):
+    # the 72-token prompt takes the tensor-core prefill on the shards (all-reduce
+    # after the row-parallel GEMMs) and on the one GPU
+    for got, want in ((r0["prefill"], prefill), (r0["step"], step), (r0["long"], long), (r0["long_step"], long_step)):
         assert np.all(np.isfinite(got))
         assert cosine(got, want) >= 0.95, cosine(got, want)
     s = np.sort(prefill)

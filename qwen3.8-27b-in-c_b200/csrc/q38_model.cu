@@ -1860,7 +1860,7 @@ bool tc_layer(Q38Model *m, int l, int n, uint32_t base)
         d.tokens = n;
         d.o_raw = m->pf_oraw;
         d.o_ld = m->lin_heads * kLinDim;
-        d.out_f = m->pf_act;
+        d.out_f = has_float_part(L.out) ? m->pf_act : nullptr;  // floats only for a float-path out projection
         d.out_q = mix;
         d.n_kh = m->lin_heads / 3;
         d.rec = m->pf_rec;

@@ -733,20 +733,41 @@ constexpr uint32_t kDeltaQkBytes = kDeltaChunk * kDeltaQkLd * 4, kDeltaVBytes = 
 constexpr uint32_t kDeltaStageBytes = kDeltaQkBytes + kDeltaVBytes + kDeltaGbBytes;
 constexpr size_t kDeltaSmem = static_cast<size_t>(kDeltaStages) * kDeltaStageBytes + 64;
 
-// Conv + SiLU of one channel at position p (qwen38_model.c:722-737):
+// Conv + SiLU of channels ch .. ch + 3 at position p (qwen38_model.c:722-737):
 // ((x[p-3] w0 + x[p-2] w1) + x[p-1] w2) + x[p] w3, positions before 0 read 0,
-// positions before the chunk read the conv ring.
-__device__ __forceinline__ float prefill_conv(const DeltaPrefillArgs &a, int ch, int p, float4 w)
+// positions before the chunk read the conv ring.  The four inputs of a
+// position come in one 16-byte load when the rows allow it (ch a multiple of 4).
+__device__ __forceinline__ void prefill_conv4(const DeltaPrefillArgs &a, int ch, int p, float (&out)[4])
 {
-    auto input = [&](int q) -> float {
-        if (q < 0) return 0.0f;
-        return q >= a.base ? a.qkvz[static_cast<size_t>(q - a.base) * a.qkvz_ld + ch]
-                           : a.conv_ring[static_cast<size_t>(ch) * 16 + (q & 15)];
-    };
-    float c = __fmul_rn(input(p - 3), w.x);
-    c = __fadd_rn(c, __fmul_rn(input(p - 2), w.y));
-    c = __fadd_rn(c, __fmul_rn(input(p - 1), w.z));
-    return silu(__fadd_rn(c, __fmul_rn(input(p), w.w)));
+    float x[4][4];  // [position p - 3 + d][channel]
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {
+        const int q = p - 3 + d;
+        if (q < 0) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) x[d][i] = 0.0f;
+        } else if (q >= a.base && (a.qkvz_ld & 3) == 0) {
+            const float4 v =
+                *reinterpret_cast<const float4 *>(a.qkvz + static_cast<size_t>(q - a.base) * a.qkvz_ld + ch);
+            x[d][0] = v.x;
+            x[d][1] = v.y;
+            x[d][2] = v.z;
+            x[d][3] = v.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                x[d][i] = q >= a.base ? a.qkvz[static_cast<size_t>(q - a.base) * a.qkvz_ld + ch + i]
+                                      : a.conv_ring[static_cast<size_t>(ch + i) * 16 + (q & 15)];
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 w = __ldg(reinterpret_cast<const float4 *>(a.conv_w) + ch + i);
+        float c = __fmul_rn(x[0][i], w.x);
+        c = __fadd_rn(c, __fmul_rn(x[1][i], w.y));
+        c = __fadd_rn(c, __fmul_rn(x[2][i], w.z));
+        out[i] = silu(__fadd_rn(c, __fmul_rn(x[3][i], w.w)));
+    }
 }
 
 // One CTA of 256 threads per token; warp w takes tasks w, w + 8, ...: tasks
@@ -767,10 +788,10 @@ __global__ void __launch_bounds__(256) deltanet_prefill_prep_kernel(DeltaPrefill
             const int ch_q = kh * 128 + lane * 4, ch_k = n_kh * 128 + kh * 128 + lane * 4;
             float qv[4], kv[4];
             double pq = 0.0, pk = 0.0;
+            prefill_conv4(a, ch_q, p, qv);
+            prefill_conv4(a, ch_k, p, kv);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                qv[i] = prefill_conv(a, ch_q + i, p, __ldg(reinterpret_cast<const float4 *>(a.conv_w) + ch_q + i));
-                kv[i] = prefill_conv(a, ch_k + i, p, __ldg(reinterpret_cast<const float4 *>(a.conv_w) + ch_k + i));
                 pq += static_cast<double>(__fmul_rn(qv[i], qv[i]));
                 pk += static_cast<double>(__fmul_rn(kv[i], kv[i]));
             }
@@ -791,9 +812,7 @@ __global__ void __launch_bounds__(256) deltanet_prefill_prep_kernel(DeltaPrefill
             const int vh = task - n_kh;
             const int ch = 2 * n_kh * 128 + vh * 128 + lane * 4;
             float v[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-                v[i] = prefill_conv(a, ch + i, p, __ldg(reinterpret_cast<const float4 *>(a.conv_w) + ch + i));
+            prefill_conv4(a, ch, p, v);
             // channel 4l + i sits in column block l / 4, slot 4 (l % 4) + i
             float *dst = rec_v + ((static_cast<size_t>(vh) * 8 + lane / 4) * rt + t) * kDeltaCols + (lane % 4) * 4;
             *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);

@@ -685,9 +685,10 @@ def run_decode(args, rank, world, dist):
 
     mtp = None
     subrecords = {}
-    if world > 1 and not args.no_subrecords:
+    if 1 < world <= 2 and not args.no_subrecords:
         # config 4's prefill on the shards (tensor-core GEMMs, all-reduce after
-        # the row-parallel ones); every rank makes the same calls; rank 0's timing
+        # the row-parallel ones; the model takes that path up to 2 GPUs); every
+        # rank makes the same calls; rank 0's timing
         subrecords["prefill_config4"] = guarded(lambda: measure_prefill(m, path, stream, with_cpu=False))
     if world == 1 and not args.no_subrecords:
         # the acceptance-independent cost of verifying n drafts, and config

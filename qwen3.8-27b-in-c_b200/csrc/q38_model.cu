@@ -1916,6 +1916,11 @@ bool tc_layer(Q38Model *m, int l, int n, uint32_t base)
     return tc_project(m, L.down, q8, m->pf_act, ffn, n, m->pf_hidden, kHidden, 1, false);
 }
 
+// The widest tensor-parallel model whose shards take the tensor-core prefill:
+// the world sizes it has been checked on against one GPU (wider models prefill
+// on the 8-token path, which is checked at every world size).
+constexpr int kTcPrefillMaxWorld = 2;
+
 bool tc_prefill_enabled()
 {
     const char *v = std::getenv("Q38CU_TC_PREFILL");
@@ -2197,7 +2202,7 @@ int q38_model_prefill(Q38Model *m, const uint32_t *tokens, uint32_t token_count,
         if (tokens[i] >= kVocab) return 0;
     if (!use_device(m)) return 0;
     if (token_count >= static_cast<uint32_t>(kTcPrefillMin) && !m->mtp_enabled && tc_prefill_enabled() &&
-        tc_prefill_types(m)) {
+        m->shard.world <= kTcPrefillMaxWorld && tc_prefill_types(m)) {
         if (!prefill_tc(m, tokens, token_count)) return 0;
         *logits = m->host_logits;
         return 1;
